@@ -1,0 +1,358 @@
+"""Benchmark of the B200 MoE expert path (prints ONE JSON line on rank 0).
+
+Workload (N = 1 per GPU): the MoE path of the synthetic Qwen3-30B-A3B-shaped
+model (benchmark configuration 2): 48 MoE FFN layers, hidden 2048, 128
+experts top-8 (softmax, selected weights renormalised), expert intermediate
+768, Q4_K experts synthesised in HBM from seed 0 (16.3 GB pool), F32 routers
+~N(0, 0.02), F32 ffn_norm = 1.  One step = one decode token through all 48
+layers: hidden += MoE_l(rms_norm(hidden, ffn_norm_l)) for l = 0..47.  The
+attention half of each decoder layer is outside this path.
+
+  value   decode tokens/s with inputs resident in HBM (CUDA events, max over ranks)
+  e2e     the same through pokit_cuda_moe_decode_layers_host: host hidden in
+          (pinned) -> device -> 48 layers -> host hidden out, every step
+  roofline  per MoE block: 22,298,624 algorithmic bytes (router 1 MiB + 8
+          experts x 2,654,208 B + 16 KiB in/out) / (step time / 48)
+
+Between steps nothing is flushed: one step streams 1.07 GB of distinct expert
+and router bytes, far above the 126 MB L2.
+
+--impl reference times the PokitLMs reference's own CPU kernels and row
+executor (oracle/_ref) on the host cores, same metric and unit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, I, E, K_TOP, LAYERS = 2048, 768, 128, 8, 48
+SEED = 0
+EPS = 1e-6
+EXPERT_BYTES = 3 * 884_736                     # gate + up + down, Q4_K
+ROUTER_BYTES = E * H * 4
+BLOCK_BYTES = ROUTER_BYTES + K_TOP * EXPERT_BYTES + 2 * H * 4
+ROUTED_BYTES = K_TOP * EXPERT_BYTES
+METRIC = "decode tokens/sec and routed-expert HBM GB/s (% of peak) at 1/2/4/8 B200"
+WORKLOAD = ("qwen3-30b-a3b-shaped MoE expert path: 48 MoE FFN layers (hidden 2048, 128 experts "
+            "top-8 renormalised, inter 768, Q4_K experts, F32 router), decode batch 1")
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_model(be, layers: int) -> None:
+    from pokitlms_b200 import synth
+    from pokitlms_b200._lib import DOWN, FFN_NORM, GATE, ROUTER, UP
+    ones = np.ones(H, dtype=np.float32)
+    for l in range(layers):
+        be.upload_tensor(l, ROUTER, synth.router_weights(E, H, SEED, l))
+        be.upload_tensor(l, FFN_NORM, ones)
+        for t in (GATE, UP, DOWN):
+            be.synthesize_tensor(l, t, SEED, synth.stream_id(l, t))
+
+
+def cpu_reference_rate(target_seconds: float, max_tokens: int | None = None):
+    """Decode tokens/s of the reference's CPU path: the reference's kernels and
+    multi-threaded row executor (oracle/_ref) when built, else the oracle's C
+    restatement.  Sample: 2 synthesised layers (layer l uses the weights of
+    layer l % 2) stand for the 48; every token runs all 48 layer evaluations.
+    Returns (tokens_per_s, kind, cores, sample_text)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import cases
+    from oracle import oracle as O
+    from pokitlms_b200 import synth
+    layers = [cases.moe_layer(seed=SEED, layer=l, with_norm=True) for l in range(2)]
+    hw = os.cpu_count() or 1
+    if O.ref_available():
+        kind = "reference"
+        cores = min(6, max(2, hw - 1))           # TensorRowExecutor workers, tensor_linear.cpp:27
+        runners = [O.RefMoe(L) for L in layers]
+        norm = O.ref_rms_norm
+
+        def block(l, x):
+            return runners[l % 2].forward(x)[0]
+    else:
+        kind = "port"
+        cores = 1
+        norm = O.rms_norm
+
+        def block(l, x):
+            return O.moe_forward(layers[l % 2], x)[0]
+    ones = np.ones(H, dtype=np.float32)
+    tokens = 0
+    t0 = time.perf_counter()
+    while True:
+        h = synth.activation(H, SEED, 10_000 + tokens)
+        for l in range(LAYERS):
+            h = (h + block(l, norm(h, ones, EPS))).astype(np.float32)
+        tokens += 1
+        el = time.perf_counter() - t0
+        if el >= target_seconds or (max_tokens and tokens >= max_tokens):
+            break
+    sample = (f"{tokens} decode tokens x 48 MoE layers (2 synthesised layers cycled), "
+              f"{el:.1f} s of CPU work")
+    return tokens / el, kind, cores, sample
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "tests"))
+    import cases
+    from oracle import oracle as O
+    from pokitlms_b200 import synth
+    layers = [cases.moe_layer(seed=SEED, layer=l, with_norm=True) for l in range(2)]
+    hw = os.cpu_count() or 1
+    if O.ref_available():
+        kind, cores = "reference", min(6, max(2, hw - 1))
+        runners = [O.RefMoe(L) for L in layers]
+        norm = O.ref_rms_norm
+
+        def block(l, x):
+            return runners[l % 2].forward(x)[0]
+    else:
+        kind, cores, norm = "port", 1, O.rms_norm
+
+        def block(l, x):
+            return O.moe_forward(layers[l % 2], x)[0]
+    ones = np.ones(H, dtype=np.float32)
+
+    def step(i):
+        h = synth.activation(H, SEED, 20_000 + i)
+        for l in range(LAYERS):
+            h = (h + block(l, norm(h, ones, EPS))).astype(np.float32)
+        return h
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    el = time.perf_counter() - t0
+    v = args.steps / el
+    sample = (f"each step = 1 decode token x 48 MoE layers (2 synthesised layers cycled) on "
+              f"{cores} host thread(s)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seed 0)",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "hidden": H, "experts": E,
+                   "top_k": K_TOP, "inter": I, "expert_type": "Q4_K"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="pokit", choices=["pokit", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from pokitlms_b200 import backend as B
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    layers = args.layers
+    be = B.CudaMoeBackend(layers=layers, hidden=H, inter=I, experts=E, top_k=K_TOP,
+                          rms_epsilon=EPS, device=local)
+    build_model(be, layers)
+    stream = torch.cuda.current_stream()
+    from pokitlms_b200 import synth
+    n_in = args.steps + args.warmup
+    inputs = torch.from_numpy(np.stack([synth.activation(H, SEED + rank, i) for i in range(n_in)])).cuda()
+    work = torch.empty(H, device="cuda")
+
+    def step(i):
+        work.copy_(inputs[i], non_blocking=True)
+        be.decode_layers(0, layers, work, stream)
+
+    for i in range(args.warmup):
+        step(i)
+    be.synchronize(stream)
+    torch.cuda.synchronize()
+    launches_before = be.stats()["kernel_launches"]
+
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    be.synchronize(stream)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms)
+    gpu_launches = be.stats()["kernel_launches"] - launches_before
+    tokens_per_s = world * args.steps / (ms_max / 1e3)
+    ms_per_step = ms_max / args.steps
+
+    # End to end through the C ABI host entry, pinned host buffers.
+    host_in = torch.from_numpy(np.stack([synth.activation(H, SEED + rank, 50_000 + i)
+                                         for i in range(64)])).pin_memory()
+    host_out = torch.empty(H, dtype=torch.float32).pin_memory()
+    e2e_steps = max(args.steps // 2, 10)
+    for i in range(3):
+        be.decode_layers_host(0, layers, host_in[i].numpy(), host_out.numpy())
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        be.decode_layers_host(0, layers, host_in[i % 64].numpy(), host_out.numpy())
+    t1 = time.perf_counter()
+    barrier()
+    e2e_s = max_over_ranks(t1 - t0)
+    e2e_rate = world * e2e_steps / e2e_s
+
+    peaks = measured_peaks()
+    block_s = ms_per_step / 1e3 / layers
+    achieved = BLOCK_BYTES / block_s / 1e9
+    routed_gbs = ROUTED_BYTES / block_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, kind, cores, sample = cpu_reference_rate(args.cpu_seconds)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seed 0): Q4_K experts synthesised in HBM, F32 router N(0,0.02)",
+            "config": {"workload": WORKLOAD, "layers": layers, "hidden": H, "experts": E,
+                       "top_k": K_TOP, "inter": I, "expert_type": "Q4_K",
+                       "parallelism": f"replicas x{world} (independent decode streams)",
+                       "l2": "no flush: each step streams 1.07 GB of distinct weights (> 126 MB L2)"},
+            "routed_expert_gbs": routed_gbs,
+            "routed_expert_frac_of_peak": routed_gbs / peaks["hbm_gbs"],
+            "roofline": {"bound": "hbm", "kernel": "moe block (route + gate_up + down, 3 launches)",
+                         "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                         "bytes_per_launch": BLOCK_BYTES, "traffic": None},
+            "e2e": {"value": e2e_rate, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
+                    "d2h_bytes_per_step": H * 4},
+            "gpu_launches": int(gpu_launches),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }))
+    be.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,293 @@
+/*
+ * pokit_cuda.h -- C ABI of the B200 (sm_100a) backend for the PokitLMs MoE
+ * expert path.
+ *
+ * Conventions follow PokitLMs' own C API (include/pokitlms/pokitlms.h):
+ *   - status codes mirror pokitlms_status (pokitlms.h:18-24);
+ *   - every call that can fail takes (error_buffer, error_capacity); the text is
+ *     truncated and NUL-terminated, and set to "" on success (c_api.cpp:22-27);
+ *   - no C++ exception crosses this boundary (c_api.cpp:92-101);
+ *   - calls on one handle must be serialised (pokitlms.h:81);
+ *   - the library owns every device allocation it makes; callers own their
+ *     host buffers and any device buffers they pass in.
+ *
+ * Pointers documented as "device" must be CUDA device pointers on the handle's
+ * device; "host" pointers are ordinary (pageable or pinned) host memory.
+ * `stream` is a cudaStream_t (NULL = the handle's own stream, or the legacy
+ * default stream for handle-free calls).
+ *
+ * GGML type ids: 0 = F32, 8 = Q8_0, 12 = Q4_K, 13 = Q5_K, 14 = Q6_K.
+ */
+#ifndef POKIT_CUDA_H
+#define POKIT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define POKIT_CUDA_VERSION_MAJOR 0
+#define POKIT_CUDA_VERSION_MINOR 1
+#define POKIT_CUDA_VERSION_PATCH 0
+
+/* Mirrors pokitlms_status (include/pokitlms/pokitlms.h:18-24). */
+typedef enum pokit_cuda_status {
+    POKIT_CUDA_STATUS_OK = 0,
+    POKIT_CUDA_STATUS_INVALID_ARGUMENT = 1,
+    POKIT_CUDA_STATUS_RUNTIME_ERROR = 2,
+    POKIT_CUDA_STATUS_BUFFER_TOO_SMALL = 3,
+    POKIT_CUDA_STATUS_INTERNAL_ERROR = 4
+} pokit_cuda_status;
+
+/* Library version string; replaces pokitlms_version (pokitlms.h:14) for this backend. */
+const char* pokit_cuda_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Per-matrix kernels on device memory                                      */
+/* ------------------------------------------------------------------------ */
+
+/* output[rows] = W[rows, cols] . input[cols] with W in its GGUF block encoding
+ * (row-major, row r at r * row_bytes).  FP32 input, FP32 accumulation.
+ * Replaces linear_q8_0 / linear_q4_k / linear_q5_k / linear_q6_k
+ * (include/pokitlms/ops/quantized_linear.hpp:23-53) and linear() for F32
+ * (include/pokitlms/ops/linear.hpp:10-14), without the bias term.
+ * All pointers are device pointers; asynchronous on `stream`. */
+pokit_cuda_status pokit_cuda_linear(uint32_t ggml_type, const void* weights, size_t rows,
+                                    size_t cols, const float* input, float* output,
+                                    void* stream, char* error_buffer, size_t error_capacity);
+
+/* Decodes rows x cols GGUF-encoded weights to FP32 (output row-major), bit-identical
+ * to dequantize_quantized_row (include/pokitlms/ops/quantized_linear.hpp:11-13).
+ * Device pointers; asynchronous on `stream`. */
+pokit_cuda_status pokit_cuda_dequantize_rows(uint32_t ggml_type, const void* encoded,
+                                             size_t rows, size_t cols, float* output,
+                                             void* stream, char* error_buffer,
+                                             size_t error_capacity);
+
+/* Softmax top-k routing of `n` device logits, on device.
+ * flavour 0 = Qwen3-MoE route_experts (src/qwen3_moe_runner.cpp:267-305, FP64
+ * denominator); flavour 1 = Qwen3.5 select_experts (src/qwen35_runner.cpp:131-173,
+ * FP32) with weights multiplied by expert_weights_scale.  Ties go to the lower
+ * id.  ids_out/weights_out: device arrays of top_k entries.  status_out (device
+ * uint32, may be NULL) is OR-ed with 1 for non-finite logits and 2 for an
+ * invalid softmax, where the reference throws. */
+pokit_cuda_status pokit_cuda_route_experts(const float* logits, size_t n, size_t top_k,
+                                           uint32_t flavour, int normalize,
+                                           float expert_weights_scale, uint32_t* ids_out,
+                                           float* weights_out, uint32_t* status_out,
+                                           void* stream, char* error_buffer,
+                                           size_t error_capacity);
+
+/* Fills `nblocks` GGUF blocks of `ggml_type` at device address `dst` with the
+ * library's seeded synthetic generator (the same bytes as
+ * pokitlms_b200.synth.synth_blocks on the host).  Benchmark/test utility: no
+ * counterpart in the reference. */
+pokit_cuda_status pokit_cuda_synthesize_blocks(uint32_t ggml_type, uint64_t seed,
+                                               uint64_t stream_id, size_t nblocks, void* dst,
+                                               void* stream, char* error_buffer,
+                                               size_t error_capacity);
+
+/* ------------------------------------------------------------------------ */
+/* TensorLinearBackend seam with host spans                                 */
+/* ------------------------------------------------------------------------ */
+
+/* Device counterpart of model::TensorLinearBackend
+ * (include/pokitlms/model/tensor_linear.hpp:11-18) and sibling of
+ * gpu::VulkanLinearBackend (include/pokitlms/gpu/vulkan_linear.hpp:69-84).
+ * Weight payloads are cached in HBM on first use, keyed by host address and
+ * size (the Vulkan backend's whole-model device cache, vulkan_linear.cpp:516-563). */
+typedef struct pokit_cuda_linear_backend pokit_cuda_linear_backend;
+
+/* Mirrors the fields of VulkanLinearStats (vulkan_linear.hpp:41-67) that apply. */
+typedef struct pokit_cuda_linear_stats {
+    uint64_t linear_calls;
+    uint64_t dispatches;
+    uint64_t q4_k_dispatches;
+    uint64_t q5_k_dispatches;
+    uint64_t q6_k_dispatches;
+    uint64_t q8_0_dispatches;
+    uint64_t other_dispatches;
+    uint64_t weight_bytes;            /* bytes streamed by the kernels */
+    uint64_t gpu_time_ns;             /* CUDA-event time of the kernels */
+    uint64_t model_cache_capacity_bytes;
+    uint64_t model_cache_uploaded_bytes;
+    uint64_t model_cache_upload_time_ns;
+} pokit_cuda_linear_stats;
+
+pokit_cuda_status pokit_cuda_linear_backend_create(int device, pokit_cuda_linear_backend** out,
+                                                   char* error_buffer, size_t error_capacity);
+void pokit_cuda_linear_backend_destroy(pokit_cuda_linear_backend* backend);
+
+/* try_linear (tensor_linear.hpp:16-17): output[rows] = W . input, host spans.
+ * *handled = 1 when the type is supported (F32/Q8_0/Q4_K/Q5_K/Q6_K) and the
+ * result was written; 0 for other types (the caller's CPU path then runs, as
+ * with the Vulkan backend).  Execution failures return RUNTIME_ERROR and leave
+ * the backend failed (sticky, like vulkan_linear.cpp:636, 731-735). */
+pokit_cuda_status pokit_cuda_linear_backend_try_linear(
+    pokit_cuda_linear_backend* backend, uint32_t ggml_type, const void* weights_host,
+    size_t weights_bytes, size_t rows, size_t cols, const float* input_host,
+    float* output_host, int* handled, char* error_buffer, size_t error_capacity);
+
+pokit_cuda_status pokit_cuda_linear_backend_get_stats(const pokit_cuda_linear_backend* backend,
+                                                      pokit_cuda_linear_stats* out_stats);
+
+/* ------------------------------------------------------------------------ */
+/* MoE FFN block with an HBM-resident expert pool                          */
+/* ------------------------------------------------------------------------ */
+
+typedef struct pokit_cuda_moe pokit_cuda_moe;
+
+typedef enum pokit_cuda_moe_flavour {
+    POKIT_CUDA_MOE_QWEN3 = 0,   /* src/qwen3_moe_runner.cpp:643-692 */
+    POKIT_CUDA_MOE_QWEN35 = 1   /* src/qwen35_runner.cpp:691-763 (shared expert) */
+} pokit_cuda_moe_flavour;
+
+/* Tensor selector for per-tensor upload/synthesis/views. */
+typedef enum pokit_cuda_moe_tensor {
+    POKIT_CUDA_MOE_ROUTER = 0,        /* F32 [experts, hidden]  (ffn_gate_inp) */
+    POKIT_CUDA_MOE_GATE = 1,          /* [hidden, inter, experts] (ffn_gate_exps) */
+    POKIT_CUDA_MOE_UP = 2,            /* [hidden, inter, experts] (ffn_up_exps) */
+    POKIT_CUDA_MOE_DOWN = 3,          /* [inter, hidden, experts] (ffn_down_exps) */
+    POKIT_CUDA_MOE_FFN_NORM = 4,      /* F32 [hidden] (ffn_norm), decode chain only */
+    POKIT_CUDA_MOE_SHARED_ROUTER = 5, /* F32 [hidden] (ffn_gate_inp_shexp) */
+    POKIT_CUDA_MOE_SHARED_GATE = 6,   /* [hidden, shared_inter] (ffn_gate_shexp) */
+    POKIT_CUDA_MOE_SHARED_UP = 7,     /* [hidden, shared_inter] (ffn_up_shexp) */
+    POKIT_CUDA_MOE_SHARED_DOWN = 8    /* [shared_inter, hidden] (ffn_down_shexp) */
+} pokit_cuda_moe_tensor;
+
+typedef struct pokit_cuda_moe_config {
+    int device;                       /* CUDA device ordinal */
+    size_t layers;                    /* MoE blocks held by the pool */
+    size_t hidden;                    /* embedding_length, multiple of 256 */
+    size_t inter;                     /* expert_feed_forward_length, multiple of 256 */
+    size_t experts;                   /* expert_count (<= 1024) */
+    size_t top_k;                     /* experts_per_token (<= 64) */
+    uint32_t flavour;                 /* pokit_cuda_moe_flavour */
+    int normalize_top_k;              /* expert_weights_norm */
+    float expert_weights_scale;       /* Qwen3.5 expert_weights_scale (1 for Qwen3) */
+    float rms_epsilon;                /* layer_norm_rms_epsilon for the decode chain */
+    uint32_t gate_type, up_type, down_type;
+    const uint32_t* layer_down_types; /* optional [layers] override of down_type */
+    size_t shared_inter;              /* 0 = no shared expert */
+    uint32_t shared_gate_type, shared_up_type, shared_down_type;
+} pokit_cuda_moe_config;
+
+/* Host payloads of one layer in GGUF layout.  NULL entries are skipped. */
+typedef struct pokit_cuda_moe_layer_host {
+    const float* router;
+    const void* gate;
+    const void* up;
+    const void* down;
+    const float* ffn_norm;
+    const float* shared_router;
+    const void* shared_gate;
+    const void* shared_up;
+    const void* shared_down;
+} pokit_cuda_moe_layer_host;
+
+/* First seven fields mirror pokitlms_expert_cache_stats (pokitlms.h:36-44):
+ * the pool holds every expert, so hits count every routed lookup and misses
+ * stay 0.  bytes_read/read_operations/read_time_ns count host->HBM uploads. */
+typedef struct pokit_cuda_moe_stats {
+    size_t capacity_bytes;
+    size_t resident_bytes;
+    uint64_t bytes_read;
+    uint64_t read_operations;
+    uint64_t read_time_ns;
+    uint64_t hits;
+    uint64_t misses;
+    uint64_t forward_calls;           /* MoE blocks executed */
+    uint64_t kernel_launches;         /* this library's kernels launched */
+} pokit_cuda_moe_stats;
+
+/* Creates a handle and reserves the expert pool for config->layers blocks in
+ * one HBM allocation (replaces the per-layer ExpertStores built in
+ * Qwen3MoeRunner::Impl::Impl, src/qwen3_moe_runner.cpp:481-523). */
+pokit_cuda_status pokit_cuda_moe_create(const pokit_cuda_moe_config* config,
+                                        pokit_cuda_moe** out_moe, char* error_buffer,
+                                        size_t error_capacity);
+void pokit_cuda_moe_destroy(pokit_cuda_moe* moe);
+
+/* Uploads one tensor of `layer` from host memory; bytes must equal the
+ * tensor's GGUF payload size.  Expert tensors are the whole [.., .., experts]
+ * payload; expert e is the contiguous slice at e * payload/experts
+ * (split_expert_tensor, src/expert_store.cpp:17-36).  Synchronous. */
+pokit_cuda_status pokit_cuda_moe_upload_tensor(pokit_cuda_moe* moe, size_t layer,
+                                               uint32_t tensor, const void* host_bytes,
+                                               size_t bytes, char* error_buffer,
+                                               size_t error_capacity);
+
+/* Uploads every non-NULL tensor of `layer`.  Synchronous. */
+pokit_cuda_status pokit_cuda_moe_upload_layer(pokit_cuda_moe* moe, size_t layer,
+                                              const pokit_cuda_moe_layer_host* tensors,
+                                              char* error_buffer, size_t error_capacity);
+
+/* Fills a quantised tensor of `layer` on the device with the synthetic block
+ * generator (seed, stream_id).  Benchmark utility; no counterpart in the reference. */
+pokit_cuda_status pokit_cuda_moe_synthesize_tensor(pokit_cuda_moe* moe, size_t layer,
+                                                   uint32_t tensor, uint64_t seed,
+                                                   uint64_t stream_id, char* error_buffer,
+                                                   size_t error_capacity);
+
+/* Device view of one expert slice (replaces ExpertStore::get,
+ * include/pokitlms/storage/expert_store.hpp:39): matrix is
+ * POKIT_CUDA_MOE_GATE/UP/DOWN; writes the slice's device address and size. */
+pokit_cuda_status pokit_cuda_moe_expert_view(const pokit_cuda_moe* moe, size_t layer,
+                                             uint32_t matrix, size_t expert,
+                                             const void** device_ptr, size_t* bytes);
+
+/* One MoE block on device pointers -- the layer-level seam the runners' MoE
+ * blocks call (src/qwen3_moe_runner.cpp:645-691, src/qwen35_runner.cpp:691-763):
+ * output[hidden] = sum_k w_k * down_k(silu(gate_k x) * up_k x) (+ shared expert),
+ * without the residual.  route_ids/route_weights (device, top_k entries each,
+ * may be NULL) receive the chosen experts in rank order and their combine
+ * weights.  Asynchronous: a router failure (non-finite logits) is reported by
+ * the next pokit_cuda_moe_synchronize or *_host call. */
+pokit_cuda_status pokit_cuda_moe_forward(pokit_cuda_moe* moe, size_t layer, const float* input,
+                                         float* output, uint32_t* route_ids,
+                                         float* route_weights, void* stream,
+                                         char* error_buffer, size_t error_capacity);
+
+/* Host-span variant of pokit_cuda_moe_forward: copies in, runs, copies out and
+ * synchronises; returns RUNTIME_ERROR (nothing written to output) when the
+ * router produced non-finite logits, as the reference throws. */
+pokit_cuda_status pokit_cuda_moe_forward_host(pokit_cuda_moe* moe, size_t layer,
+                                              const float* input_host, float* output_host,
+                                              uint32_t* route_ids_host,
+                                              float* route_weights_host, char* error_buffer,
+                                              size_t error_capacity);
+
+/* Decode chain over layers [first, first + count) on a device hidden state:
+ * hidden += MoE_l(rms_norm(hidden, ffn_norm_l)) per layer (the FFN half of
+ * src/qwen3_moe_runner.cpp:643-692).  Captured once into a CUDA graph per
+ * (first, count, hidden) and replayed.  Asynchronous. */
+pokit_cuda_status pokit_cuda_moe_decode_layers(pokit_cuda_moe* moe, size_t first, size_t count,
+                                               float* hidden, void* stream,
+                                               char* error_buffer, size_t error_capacity);
+
+/* Host-span decode chain: copies hidden_in (host) to the device, runs the
+ * chain, copies the result to hidden_out (host) and synchronises. */
+pokit_cuda_status pokit_cuda_moe_decode_layers_host(pokit_cuda_moe* moe, size_t first,
+                                                    size_t count, const float* hidden_in,
+                                                    float* hidden_out, char* error_buffer,
+                                                    size_t error_capacity);
+
+/* Waits for the handle's work and reports (then clears) any device-side router
+ * failure; a CUDA error is sticky and fails every later call. */
+pokit_cuda_status pokit_cuda_moe_synchronize(pokit_cuda_moe* moe, void* stream,
+                                             char* error_buffer, size_t error_capacity);
+
+pokit_cuda_status pokit_cuda_moe_get_stats(const pokit_cuda_moe* moe,
+                                           pokit_cuda_moe_stats* out_stats);
+
+/* Bytes of one tensor's payload for this handle's configuration (0 if the
+ * tensor does not exist in this configuration). */
+size_t pokit_cuda_moe_tensor_bytes(const pokit_cuda_moe* moe, size_t layer, uint32_t tensor);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POKIT_CUDA_H */

@@ -1,0 +1,179 @@
+"""ctypes binding of include/pokit_cuda.h (libpokit_cuda.so).
+
+The shared library is the product: every call below goes straight into the
+sm_100a kernels.  There is no CPU fallback; if the library is missing or
+cannot be loaded, `lib()` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libpokit_cuda.so"
+
+F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
+BLOCK = {F32: (1, 4), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210)}
+
+STATUS_OK, STATUS_INVALID_ARGUMENT, STATUS_RUNTIME_ERROR = 0, 1, 2
+STATUS_BUFFER_TOO_SMALL, STATUS_INTERNAL_ERROR = 3, 4
+
+(ROUTER, GATE, UP, DOWN, FFN_NORM, SHARED_ROUTER, SHARED_GATE, SHARED_UP,
+ SHARED_DOWN) = range(9)
+QWEN3, QWEN35 = 0, 1
+
+
+def row_bytes(ggml_type: int, cols: int) -> int:
+    elems, nbytes = BLOCK[ggml_type]
+    return cols // elems * nbytes
+
+
+class PokitCudaError(RuntimeError):
+    """A non-OK pokit_cuda_status, with the library's error text."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[status {status}] {message}")
+        self.status = status
+        self.message = message
+
+
+class InvalidArgument(PokitCudaError, ValueError):
+    pass
+
+
+class MoeConfig(C.Structure):
+    _fields_ = [
+        ("device", C.c_int),
+        ("layers", C.c_size_t),
+        ("hidden", C.c_size_t),
+        ("inter", C.c_size_t),
+        ("experts", C.c_size_t),
+        ("top_k", C.c_size_t),
+        ("flavour", C.c_uint32),
+        ("normalize_top_k", C.c_int),
+        ("expert_weights_scale", C.c_float),
+        ("rms_epsilon", C.c_float),
+        ("gate_type", C.c_uint32),
+        ("up_type", C.c_uint32),
+        ("down_type", C.c_uint32),
+        ("layer_down_types", C.POINTER(C.c_uint32)),
+        ("shared_inter", C.c_size_t),
+        ("shared_gate_type", C.c_uint32),
+        ("shared_up_type", C.c_uint32),
+        ("shared_down_type", C.c_uint32),
+    ]
+
+
+class MoeLayerHost(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "router", "gate", "up", "down", "ffn_norm", "shared_router", "shared_gate",
+        "shared_up", "shared_down")]
+
+
+class MoeStats(C.Structure):
+    _fields_ = [
+        ("capacity_bytes", C.c_size_t),
+        ("resident_bytes", C.c_size_t),
+        ("bytes_read", C.c_uint64),
+        ("read_operations", C.c_uint64),
+        ("read_time_ns", C.c_uint64),
+        ("hits", C.c_uint64),
+        ("misses", C.c_uint64),
+        ("forward_calls", C.c_uint64),
+        ("kernel_launches", C.c_uint64),
+    ]
+
+
+class LinearStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in (
+        "linear_calls", "dispatches", "q4_k_dispatches", "q5_k_dispatches", "q6_k_dispatches",
+        "q8_0_dispatches", "other_dispatches", "weight_bytes", "gpu_time_ns",
+        "model_cache_capacity_bytes", "model_cache_uploaded_bytes", "model_cache_upload_time_ns")]
+
+
+_ERR = C.c_char_p
+_SZ = C.c_size_t
+_VP = C.c_void_p
+
+# name -> (restype, argtypes); every symbol of include/pokit_cuda.h.
+SIGNATURES = {
+    "pokit_cuda_version": (C.c_char_p, []),
+    "pokit_cuda_linear": (C.c_int, [C.c_uint32, _VP, _SZ, _SZ, _VP, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_dequantize_rows": (C.c_int, [C.c_uint32, _VP, _SZ, _SZ, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_route_experts": (C.c_int, [_VP, _SZ, _SZ, C.c_uint32, C.c_int, C.c_float, _VP,
+                                           _VP, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_synthesize_blocks": (C.c_int, [C.c_uint32, C.c_uint64, C.c_uint64, _SZ, _VP,
+                                               _VP, _ERR, _SZ]),
+    "pokit_cuda_linear_backend_create": (C.c_int, [C.c_int, C.POINTER(_VP), _ERR, _SZ]),
+    "pokit_cuda_linear_backend_destroy": (None, [_VP]),
+    "pokit_cuda_linear_backend_try_linear": (C.c_int, [_VP, C.c_uint32, _VP, _SZ, _SZ, _SZ, _VP,
+                                                       _VP, C.POINTER(C.c_int), _ERR, _SZ]),
+    "pokit_cuda_linear_backend_get_stats": (C.c_int, [_VP, C.POINTER(LinearStats)]),
+    "pokit_cuda_moe_create": (C.c_int, [C.POINTER(MoeConfig), C.POINTER(_VP), _ERR, _SZ]),
+    "pokit_cuda_moe_destroy": (None, [_VP]),
+    "pokit_cuda_moe_upload_tensor": (C.c_int, [_VP, _SZ, C.c_uint32, _VP, _SZ, _ERR, _SZ]),
+    "pokit_cuda_moe_upload_layer": (C.c_int, [_VP, _SZ, C.POINTER(MoeLayerHost), _ERR, _SZ]),
+    "pokit_cuda_moe_synthesize_tensor": (C.c_int, [_VP, _SZ, C.c_uint32, C.c_uint64, C.c_uint64,
+                                                   _ERR, _SZ]),
+    "pokit_cuda_moe_expert_view": (C.c_int, [_VP, _SZ, C.c_uint32, _SZ, C.POINTER(_VP),
+                                             C.POINTER(_SZ)]),
+    "pokit_cuda_moe_forward": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_forward_host": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_decode_layers": (C.c_int, [_VP, _SZ, _SZ, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_decode_layers_host": (C.c_int, [_VP, _SZ, _SZ, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_synchronize": (C.c_int, [_VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_get_stats": (C.c_int, [_VP, C.POINTER(MoeStats)]),
+    "pokit_cuda_moe_tensor_bytes": (C.c_size_t, [_VP, _SZ, C.c_uint32]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libpokit_cuda.so, raising if it has not been built."""
+    global _lib
+    if _lib is None:
+        path = Path(os.environ.get("POKIT_CUDA_LIB", LIB_PATH))
+        if not path.exists():
+            raise RuntimeError(
+                f"{path} is missing: build it with `python -m pokitlms_b200.build` "
+                "(the CUDA path has no CPU fallback)")
+        handle = C.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+class ErrorBuffer:
+    """A (char*, capacity) pair for the C ABI's error reporting."""
+
+    def __init__(self, capacity: int = 512):
+        self.buf = C.create_string_buffer(capacity)
+        self.cap = capacity
+
+    def args(self):
+        return self.buf, self.cap
+
+    def text(self) -> str:
+        return self.buf.value.decode(errors="replace")
+
+
+def check(status: int, err: ErrorBuffer | None = None, what: str = "") -> None:
+    if status == STATUS_OK:
+        return
+    msg = err.text() if err is not None else ""
+    if what:
+        msg = f"{what}: {msg}" if msg else what
+    if status == STATUS_INVALID_ARGUMENT:
+        raise InvalidArgument(status, msg)
+    raise PokitCudaError(status, msg)
+
+
+def call(name: str, *args) -> None:
+    """Calls an entry point that ends in (error_buffer, error_capacity)."""
+    err = ErrorBuffer()
+    check(getattr(lib(), name)(*args, *err.args()), err, name)

@@ -1,0 +1,209 @@
+"""Python mirror of the PokitLMs backend seams, over the C ABI.
+
+Names and argument meaning follow the reference:
+  * CudaLinearBackend.try_linear  <- model::TensorLinearBackend::try_linear
+    (include/pokitlms/model/tensor_linear.hpp:11-18); returns False for an
+    unsupported type, raises on execution failure.
+  * CudaMoeBackend                <- the runners' MoE block + ExpertStore
+    (src/qwen3_moe_runner.cpp:643-692, src/qwen35_runner.cpp:691-763,
+    include/pokitlms/storage/expert_store.hpp:26-53), with every expert
+    resident in HBM.
+  * linear / dequantize_rows / route_experts on device tensors
+    <- linear_q4_k & co. (quantized_linear.hpp), route_experts /
+    select_experts (runner-internal).
+
+Device buffers are torch CUDA tensors (torch is only the allocator and stream
+provider here); all compute runs in libpokit_cuda.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import (BLOCK, F32, GATE, UP, DOWN, QWEN3, QWEN35, InvalidArgument, LinearStats,
+                   MoeConfig, MoeLayerHost, MoeStats, PokitCudaError, call, check, lib, row_bytes)
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return int(t.data_ptr())
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return int(torch.cuda.current_stream().cuda_stream)
+    return int(getattr(stream, "cuda_stream", stream))
+
+
+def _np_ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def version() -> str:
+    return lib().pokit_cuda_version().decode()
+
+
+def linear(ggml_type: int, weights, rows: int, cols: int, x, y, stream=None) -> None:
+    """y[rows] = W[rows, cols] . x on device tensors (W: uint8 GGUF bytes)."""
+    call("pokit_cuda_linear", ggml_type, _ptr(weights), rows, cols, _ptr(x), _ptr(y),
+         _stream(stream))
+
+
+def dequantize_rows(ggml_type: int, encoded, rows: int, cols: int, out, stream=None) -> None:
+    call("pokit_cuda_dequantize_rows", ggml_type, _ptr(encoded), rows, cols, _ptr(out),
+         _stream(stream))
+
+
+def route_experts(logits, top_k: int, flavour: int, normalize: bool, ids, weights,
+                  expert_weights_scale: float = 1.0, status=None, stream=None) -> None:
+    call("pokit_cuda_route_experts", _ptr(logits), logits.numel(), top_k, flavour,
+         int(normalize), float(expert_weights_scale), _ptr(ids), _ptr(weights), _ptr(status),
+         _stream(stream))
+
+
+def synthesize_blocks(ggml_type: int, seed: int, stream_id: int, nblocks: int, dst,
+                      stream=None) -> None:
+    call("pokit_cuda_synthesize_blocks", ggml_type, seed, stream_id, nblocks, _ptr(dst),
+         _stream(stream))
+
+
+class CudaLinearBackend:
+    """TensorLinearBackend with host spans and an HBM weight cache."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        call("pokit_cuda_linear_backend_create", device, C.byref(h))
+        self._h = h
+
+    def try_linear(self, ggml_type: int, weights: np.ndarray, rows: int, cols: int,
+                   x: np.ndarray, out: np.ndarray) -> bool:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if out.dtype != np.float32 or not out.flags.c_contiguous or out.size != rows:
+            raise ValueError("output must be a contiguous float32 array of `rows` elements")
+        handled = C.c_int(0)
+        call("pokit_cuda_linear_backend_try_linear", self._h, ggml_type, _np_ptr(weights),
+             weights.nbytes, rows, cols, _np_ptr(x), _np_ptr(out), C.byref(handled))
+        return bool(handled.value)
+
+    def stats(self) -> dict:
+        s = LinearStats()
+        check(lib().pokit_cuda_linear_backend_get_stats(self._h, C.byref(s)))
+        return {n: getattr(s, n) for n, _ in s._fields_}
+
+    def close(self) -> None:
+        if self._h:
+            lib().pokit_cuda_linear_backend_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaMoeBackend:
+    """MoE FFN blocks over an HBM-resident expert pool."""
+
+    def __init__(self, *, layers: int, hidden: int, inter: int, experts: int, top_k: int,
+                 flavour: int = QWEN3, normalize_top_k: bool = True,
+                 expert_weights_scale: float = 1.0, rms_epsilon: float = 1e-6,
+                 gate_type: int = 12, up_type: int = 12, down_type: int = 12,
+                 layer_down_types: list[int] | None = None, shared_inter: int = 0,
+                 shared_gate_type: int = 8, shared_up_type: int = 8, shared_down_type: int = 8,
+                 device: int = 0):
+        self._ldt = None
+        if layer_down_types is not None:
+            self._ldt = (C.c_uint32 * layers)(*layer_down_types)
+        cfg = MoeConfig(device, layers, hidden, inter, experts, top_k, flavour,
+                        int(normalize_top_k), expert_weights_scale, rms_epsilon, gate_type,
+                        up_type, down_type,
+                        C.cast(self._ldt, C.POINTER(C.c_uint32)) if self._ldt else None,
+                        shared_inter, shared_gate_type, shared_up_type, shared_down_type)
+        h = C.c_void_p()
+        call("pokit_cuda_moe_create", C.byref(cfg), C.byref(h))
+        self._h = h
+        self.layers, self.hidden, self.inter = layers, hidden, inter
+        self.experts, self.top_k, self.flavour = experts, top_k, flavour
+        self.shared_inter = shared_inter
+
+    # -- weights ------------------------------------------------------------
+    def tensor_bytes(self, layer: int, tensor: int) -> int:
+        return int(lib().pokit_cuda_moe_tensor_bytes(self._h, layer, tensor))
+
+    def upload_tensor(self, layer: int, tensor: int, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data)
+        call("pokit_cuda_moe_upload_tensor", self._h, layer, tensor, _np_ptr(data), data.nbytes)
+
+    def upload_layer(self, layer: int, *, router=None, gate=None, up=None, down=None,
+                     ffn_norm=None, shared_router=None, shared_gate=None, shared_up=None,
+                     shared_down=None) -> None:
+        arrays = [None if a is None else np.ascontiguousarray(a) for a in (
+            router, gate, up, down, ffn_norm, shared_router, shared_gate, shared_up,
+            shared_down)]
+        host = MoeLayerHost(*[None if a is None else a.ctypes.data for a in arrays])
+        call("pokit_cuda_moe_upload_layer", self._h, layer, C.byref(host))
+
+    def synthesize_tensor(self, layer: int, tensor: int, seed: int, stream_id: int) -> None:
+        call("pokit_cuda_moe_synthesize_tensor", self._h, layer, tensor, seed, stream_id)
+
+    def expert_view(self, layer: int, matrix: int, expert: int) -> tuple[int, int]:
+        p = C.c_void_p()
+        n = C.c_size_t()
+        check(lib().pokit_cuda_moe_expert_view(self._h, layer, matrix, expert, C.byref(p),
+                                               C.byref(n)))
+        return int(p.value or 0), int(n.value)
+
+    # -- execution ----------------------------------------------------------
+    def forward(self, layer: int, x, out, route_ids=None, route_weights=None, stream=None) -> None:
+        call("pokit_cuda_moe_forward", self._h, layer, _ptr(x), _ptr(out), _ptr(route_ids),
+             _ptr(route_weights), _stream(stream))
+
+    def forward_host(self, layer: int, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(self.hidden, dtype=np.float32)
+        ids = np.empty(self.top_k, dtype=np.uint32)
+        w = np.empty(self.top_k, dtype=np.float32)
+        call("pokit_cuda_moe_forward_host", self._h, layer, _np_ptr(x), _np_ptr(out),
+             _np_ptr(ids), _np_ptr(w))
+        return out, ids, w
+
+    def decode_layers(self, first: int, count: int, hidden, stream=None) -> None:
+        call("pokit_cuda_moe_decode_layers", self._h, first, count, _ptr(hidden), _stream(stream))
+
+    def decode_layers_host(self, first: int, count: int, hidden_in: np.ndarray,
+                           hidden_out: np.ndarray | None = None) -> np.ndarray:
+        hidden_in = np.ascontiguousarray(hidden_in, dtype=np.float32)
+        if hidden_out is None:
+            hidden_out = np.empty(self.hidden, dtype=np.float32)
+        call("pokit_cuda_moe_decode_layers_host", self._h, first, count, _np_ptr(hidden_in),
+             _np_ptr(hidden_out))
+        return hidden_out
+
+    def synchronize(self, stream=None) -> None:
+        call("pokit_cuda_moe_synchronize", self._h, None if stream is None else _stream(stream))
+
+    def stats(self) -> dict:
+        s = MoeStats()
+        check(lib().pokit_cuda_moe_get_stats(self._h, C.byref(s)))
+        return {n: getattr(s, n) for n, _ in s._fields_}
+
+    def close(self) -> None:
+        if self._h:
+            lib().pokit_cuda_moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+__all__ = ["CudaLinearBackend", "CudaMoeBackend", "linear", "dequantize_rows", "route_experts",
+           "synthesize_blocks", "version", "PokitCudaError", "InvalidArgument", "BLOCK",
+           "row_bytes", "F32", "GATE", "UP", "DOWN", "QWEN3", "QWEN35", "_lib"]

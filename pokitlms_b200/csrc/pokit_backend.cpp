@@ -1,0 +1,787 @@
+// pokit_backend.cpp -- C++ host layer of the B200 MoE expert backend and the
+// extern "C" entry points declared in include/pokit_cuda.h.
+//
+//   MoeBackend     HBM-resident expert pool (one allocation for every layer's
+//                  router, gate/up/down expert tensors, norms and shared
+//                  expert) + the per-block launch sequence + CUDA-graph decode
+//                  chain.  Replaces ExpertStore's LRU (PokitLMs
+//                  src/expert_store.cpp:81-141): every expert is resident, so
+//                  a lookup is an address computation on the device.
+//   LinearBackend  TensorLinearBackend::try_linear with host spans and a
+//                  device cache of weight payloads (the Vulkan backend's
+//                  model cache, src/vulkan_linear.cpp:516-563).
+//
+// Errors are C++ exceptions inside and status codes at the C boundary, as in
+// PokitLMs src/c_api.cpp:92-101.  CUDA failures are sticky per handle, as the
+// Vulkan backend's `failed` flag (src/vulkan_linear.cpp:636, 731-735).
+#include "../../include/pokit_cuda.h"
+#include "pokit_kernels.h"
+#include "pokit_types.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <array>
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+namespace pokit {
+namespace {
+
+struct RouterFailure : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+void check(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    if (e == cudaErrorInvalidValue)
+        throw std::invalid_argument(std::string(what) + ": unsupported shape or argument");
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+uint64_t align256(uint64_t v) { return (v + 255u) & ~uint64_t(255); }
+
+bool type_supported(uint32_t t) {
+    return t == kF32 || t == kQ8_0 || t == kQ4_K || t == kQ5_K || t == kQ6_K;
+}
+
+bool quant_supported(uint32_t t) { return t == kQ8_0 || t == kQ4_K || t == kQ5_K || t == kQ6_K; }
+
+class DeviceScope {
+public:
+    explicit DeviceScope(int device) {
+        check(cudaGetDevice(&previous_), "cudaGetDevice");
+        if (previous_ != device) check(cudaSetDevice(device), "cudaSetDevice");
+        device_ = device;
+    }
+    ~DeviceScope() {
+        if (previous_ != device_) cudaSetDevice(previous_);
+    }
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+
+private:
+    int previous_ = 0;
+    int device_ = 0;
+};
+
+uint64_t now_ns() {
+    return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(
+        std::chrono::steady_clock::now().time_since_epoch()).count());
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+class MoeBackend {
+public:
+    explicit MoeBackend(const pokit_cuda_moe_config& c) : cfg_(c) {
+        if (c.layers == 0 || c.hidden == 0 || c.hidden % 256 || c.inter == 0 || c.inter % 256 ||
+            c.experts == 0 || c.experts > 1024 || c.top_k == 0 || c.top_k > c.experts ||
+            c.top_k > 64 || c.flavour > 1)
+            throw std::invalid_argument("invalid MoE configuration");
+        if (!quant_supported(c.gate_type) || !quant_supported(c.up_type) ||
+            !quant_supported(c.down_type))
+            throw std::invalid_argument("unsupported expert tensor type");
+        if (c.shared_inter) {
+            if (c.flavour != POKIT_CUDA_MOE_QWEN35 || c.shared_inter % 256 ||
+                !quant_supported(c.shared_gate_type) || !quant_supported(c.shared_up_type) ||
+                !quant_supported(c.shared_down_type))
+                throw std::invalid_argument("invalid shared expert configuration");
+        }
+        device_ = c.device;
+        DeviceScope scope(device_);
+        layer_down_.assign(c.layers, c.down_type);
+        if (c.layer_down_types) {
+            for (size_t l = 0; l < c.layers; ++l) {
+                if (!quant_supported(c.layer_down_types[l]))
+                    throw std::invalid_argument("unsupported per-layer down type");
+                layer_down_[l] = c.layer_down_types[l];
+            }
+        }
+        // Pool layout: per layer, every tensor at a 256-byte boundary.
+        offsets_.resize(c.layers);
+        uint64_t off = 0;
+        for (size_t l = 0; l < c.layers; ++l) {
+            for (uint32_t t = 0; t < 9; ++t) {
+                const uint64_t b = tensor_bytes(l, t);
+                offsets_[l][t] = b ? off : UINT64_MAX;
+                off += align256(b);
+            }
+        }
+        pool_bytes_ = off;
+        check(cudaMalloc(&pool_, pool_bytes_), "cudaMalloc(expert pool)");
+        check(cudaMemset(pool_, 0, pool_bytes_), "cudaMemset(expert pool)");
+        check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+
+        resident_.assign(c.layers, 0u);
+        devs_.resize(c.layers);
+        for (size_t l = 0; l < c.layers; ++l) devs_[l] = make_layer_dev(l);
+        scratch_bytes_ = moe_scratch_bytes(devs_[0]);
+        for (size_t l = 1; l < c.layers; ++l)
+            scratch_bytes_ = std::max<uint64_t>(scratch_bytes_, moe_scratch_bytes(devs_[l]));
+        check(cudaMalloc(&scratch_, scratch_bytes_), "cudaMalloc(scratch)");
+        check(cudaMemset(scratch_, 0, scratch_bytes_), "cudaMemset(scratch)");
+        S_ = moe_scratch_carve(devs_[0], scratch_);
+        check(cudaMalloc(&io_, align256(c.hidden * 4) * 2), "cudaMalloc(io)");
+        check(cudaMallocHost(&pinned_, align256(c.hidden * 4) * 2 + 4096), "cudaMallocHost");
+    }
+
+    ~MoeBackend() {
+        for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+        if (pinned_) cudaFreeHost(pinned_);
+        if (io_) cudaFree(io_);
+        if (scratch_) cudaFree(scratch_);
+        if (pool_) cudaFree(pool_);
+        if (capture_stream_) cudaStreamDestroy(capture_stream_);
+        if (stream_) cudaStreamDestroy(stream_);
+    }
+
+    MoeBackend(const MoeBackend&) = delete;
+    MoeBackend& operator=(const MoeBackend&) = delete;
+
+    std::mutex& mutex() { return mutex_; }
+
+    uint64_t tensor_bytes(size_t layer, uint32_t t) const {
+        const uint64_t H = cfg_.hidden, I = cfg_.inter, E = cfg_.experts, SI = cfg_.shared_inter;
+        if (layer >= cfg_.layers) return 0;
+        switch (t) {
+            case POKIT_CUDA_MOE_ROUTER: return E * H * 4;
+            case POKIT_CUDA_MOE_GATE: return E * I * row_bytes(cfg_.gate_type, H);
+            case POKIT_CUDA_MOE_UP: return E * I * row_bytes(cfg_.up_type, H);
+            case POKIT_CUDA_MOE_DOWN: return E * H * row_bytes(layer_down_[layer], I);
+            case POKIT_CUDA_MOE_FFN_NORM: return H * 4;
+            case POKIT_CUDA_MOE_SHARED_ROUTER: return SI ? H * 4 : 0;
+            case POKIT_CUDA_MOE_SHARED_GATE: return SI ? SI * row_bytes(cfg_.shared_gate_type, H) : 0;
+            case POKIT_CUDA_MOE_SHARED_UP: return SI ? SI * row_bytes(cfg_.shared_up_type, H) : 0;
+            case POKIT_CUDA_MOE_SHARED_DOWN: return SI ? H * row_bytes(cfg_.shared_down_type, SI) : 0;
+            default: return 0;
+        }
+    }
+
+    uint32_t tensor_type(size_t layer, uint32_t t) const {
+        switch (t) {
+            case POKIT_CUDA_MOE_GATE: return cfg_.gate_type;
+            case POKIT_CUDA_MOE_UP: return cfg_.up_type;
+            case POKIT_CUDA_MOE_DOWN: return layer_down_[layer];
+            case POKIT_CUDA_MOE_SHARED_GATE: return cfg_.shared_gate_type;
+            case POKIT_CUDA_MOE_SHARED_UP: return cfg_.shared_up_type;
+            case POKIT_CUDA_MOE_SHARED_DOWN: return cfg_.shared_down_type;
+            default: return kF32;
+        }
+    }
+
+    uint8_t* tensor_ptr(size_t layer, uint32_t t) const {
+        if (layer >= cfg_.layers || t > 8 || offsets_[layer][t] == UINT64_MAX) return nullptr;
+        return pool_ + offsets_[layer][t];
+    }
+
+    void upload_tensor(size_t layer, uint32_t t, const void* host, size_t bytes) {
+        ensure_ok();
+        if (layer >= cfg_.layers || t > 8) throw std::invalid_argument("layer or tensor out of range");
+        const uint64_t want = tensor_bytes(layer, t);
+        if (want == 0) throw std::invalid_argument("tensor does not exist in this configuration");
+        if (!host || bytes != want) throw std::invalid_argument("tensor byte size does not match configuration");
+        DeviceScope scope(device_);
+        const uint64_t t0 = now_ns();
+        guard(cudaMemcpy(tensor_ptr(layer, t), host, bytes, cudaMemcpyHostToDevice), "upload");
+        read_time_ns_ += now_ns() - t0;
+        bytes_read_ += bytes;
+        read_operations_ += 1;
+        mark_resident(layer, t);
+    }
+
+    void synthesize_tensor(size_t layer, uint32_t t, uint64_t seed, uint64_t stream_id) {
+        ensure_ok();
+        if (layer >= cfg_.layers || t > 8) throw std::invalid_argument("layer or tensor out of range");
+        const uint64_t bytes = tensor_bytes(layer, t);
+        const uint32_t type = tensor_type(layer, t);
+        if (bytes == 0 || !quant_supported(type))
+            throw std::invalid_argument("only quantised expert tensors can be synthesised");
+        DeviceScope scope(device_);
+        guard(launch_synth_blocks(type, seed, stream_id, bytes / block_bytes(type), tensor_ptr(layer, t),
+                                  stream_), "synthesize");
+        guard(cudaStreamSynchronize(stream_), "synthesize");
+        kernel_launches_ += 1;
+        mark_resident(layer, t);
+    }
+
+    void expert_view(size_t layer, uint32_t matrix, size_t expert, const void** ptr, size_t* bytes) const {
+        if (layer >= cfg_.layers || expert >= cfg_.experts ||
+            (matrix != POKIT_CUDA_MOE_GATE && matrix != POKIT_CUDA_MOE_UP && matrix != POKIT_CUDA_MOE_DOWN))
+            throw std::invalid_argument("expert view out of range");
+        const uint64_t slice = tensor_bytes(layer, matrix) / cfg_.experts;
+        *ptr = tensor_ptr(layer, matrix) + expert * slice;
+        *bytes = slice;
+        ++hits_;
+    }
+
+    void forward(size_t layer, const float* x, float* out, uint32_t* ids, float* w, cudaStream_t s) {
+        ensure_ok();
+        if (layer >= cfg_.layers) throw std::invalid_argument("layer out of range");
+        if (!x || !out) throw std::invalid_argument("input and output are required");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        const float* next = layer + 1 < cfg_.layers ? devs_[layer + 1].router : nullptr;
+        guard(launch_moe_block(devs_[layer], S_, x, nullptr, out, next, st), "moe block");
+        if (ids) guard(cudaMemcpyAsync(ids, S_.ids, cfg_.top_k * 4, cudaMemcpyDeviceToDevice, st), "ids");
+        if (w) guard(cudaMemcpyAsync(w, S_.weights, cfg_.top_k * 4, cudaMemcpyDeviceToDevice, st), "weights");
+        forward_calls_ += 1;
+        hits_ += cfg_.top_k;
+        kernel_launches_ += 3;
+    }
+
+    void forward_host(size_t layer, const float* x, float* out, uint32_t* ids, float* w) {
+        ensure_ok();
+        if (!x || !out) throw std::invalid_argument("input and output are required");
+        DeviceScope scope(device_);
+        float* dx = static_cast<float*>(io_);
+        float* dy = reinterpret_cast<float*>(static_cast<uint8_t*>(io_) + align256(cfg_.hidden * 4));
+        float* h_out = static_cast<float*>(pinned_);
+        uint8_t* h_tail = static_cast<uint8_t*>(pinned_) + align256(cfg_.hidden * 4) * 2;
+        guard(cudaMemcpyAsync(dx, x, cfg_.hidden * 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        forward(layer, dx, dy, nullptr, nullptr, stream_);
+        guard(cudaMemcpyAsync(h_out, dy, cfg_.hidden * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
+        guard(cudaMemcpyAsync(h_tail, S_.ids, cfg_.top_k * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
+        guard(cudaMemcpyAsync(h_tail + 1024, S_.weights, cfg_.top_k * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
+        synchronize(stream_);
+        std::memcpy(out, h_out, cfg_.hidden * 4);
+        if (ids) std::memcpy(ids, h_tail, cfg_.top_k * 4);
+        if (w) std::memcpy(w, h_tail + 1024, cfg_.top_k * 4);
+    }
+
+    void decode_layers(size_t first, size_t count, float* hidden, cudaStream_t s) {
+        ensure_ok();
+        if (count == 0 || first >= cfg_.layers || count > cfg_.layers - first)
+            throw std::invalid_argument("layer range out of bounds");
+        if (!hidden) throw std::invalid_argument("hidden state is required");
+        for (size_t l = first; l < first + count; ++l)
+            if (!resident_complete(l)) throw std::invalid_argument("layer weights were not uploaded");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        const auto key = std::make_tuple(first, count, hidden);
+        auto it = graphs_.find(key);
+        if (it == graphs_.end()) {
+            cudaGraph_t graph = nullptr;
+            guard(cudaStreamBeginCapture(capture_stream_, cudaStreamCaptureModeThreadLocal), "capture");
+            cudaError_t e = cudaSuccess;
+            for (size_t l = first; l < first + count && e == cudaSuccess; ++l) {
+                const float* next = l + 1 < first + count ? devs_[l + 1].router : nullptr;
+                e = launch_moe_block(devs_[l], S_, nullptr, hidden, nullptr, next, capture_stream_);
+            }
+            const cudaError_t end = cudaStreamEndCapture(capture_stream_, &graph);
+            if (e != cudaSuccess) { if (graph) cudaGraphDestroy(graph); guard(e, "capture launch"); }
+            guard(end, "end capture");
+            cudaGraphExec_t exec = nullptr;
+            const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            guard(inst, "instantiate");
+            it = graphs_.emplace(key, exec).first;
+        }
+        guard(cudaGraphLaunch(it->second, st), "graph launch");
+        forward_calls_ += count;
+        hits_ += count * cfg_.top_k;
+        kernel_launches_ += 3 * count;
+    }
+
+    void decode_layers_host(size_t first, size_t count, const float* in, float* out) {
+        ensure_ok();
+        if (!in || !out) throw std::invalid_argument("hidden buffers are required");
+        DeviceScope scope(device_);
+        float* dh = static_cast<float*>(io_);
+        guard(cudaMemcpyAsync(dh, in, cfg_.hidden * 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        decode_layers(first, count, dh, stream_);
+        float* h_out = static_cast<float*>(pinned_);
+        guard(cudaMemcpyAsync(h_out, dh, cfg_.hidden * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
+        synchronize(stream_);
+        std::memcpy(out, h_out, cfg_.hidden * 4);
+    }
+
+    void synchronize(cudaStream_t s) {
+        ensure_ok();
+        DeviceScope scope(device_);
+        guard(cudaStreamSynchronize(s ? s : stream_), "synchronize");
+        uint32_t status = 0;
+        guard(cudaMemcpy(&status, S_.status, 4, cudaMemcpyDeviceToHost), "status");
+        if (status) {
+            guard(cudaMemset(S_.status, 0, 4), "status reset");
+            if (status & kStatusNonFiniteLogits)
+                throw RouterFailure("expert router produced non-finite logits");
+            throw RouterFailure("expert router softmax is invalid");
+        }
+    }
+
+    pokit_cuda_moe_stats stats() const {
+        pokit_cuda_moe_stats s{};
+        s.capacity_bytes = pool_bytes_;
+        s.resident_bytes = resident_bytes_;
+        s.bytes_read = bytes_read_;
+        s.read_operations = read_operations_;
+        s.read_time_ns = read_time_ns_;
+        s.hits = hits_;
+        s.misses = 0;
+        s.forward_calls = forward_calls_;
+        s.kernel_launches = kernel_launches_;
+        return s;
+    }
+
+private:
+    MoeLayerDev make_layer_dev(size_t l) const {
+        MoeLayerDev L;
+        L.hidden = static_cast<uint32_t>(cfg_.hidden);
+        L.inter = static_cast<uint32_t>(cfg_.inter);
+        L.experts = static_cast<uint32_t>(cfg_.experts);
+        L.top_k = static_cast<uint32_t>(cfg_.top_k);
+        L.flavour = cfg_.flavour;
+        L.normalize = cfg_.normalize_top_k ? 1u : 0u;
+        L.expert_weights_scale = cfg_.flavour == POKIT_CUDA_MOE_QWEN35 ? cfg_.expert_weights_scale : 1.0f;
+        L.rms_eps = cfg_.rms_epsilon > 0.0f ? cfg_.rms_epsilon : 1e-6f;
+        L.router = reinterpret_cast<const float*>(tensor_ptr(l, POKIT_CUDA_MOE_ROUTER));
+        L.gate_type = cfg_.gate_type;
+        L.up_type = cfg_.up_type;
+        L.down_type = layer_down_[l];
+        L.gate = tensor_ptr(l, POKIT_CUDA_MOE_GATE);
+        L.up = tensor_ptr(l, POKIT_CUDA_MOE_UP);
+        L.down = tensor_ptr(l, POKIT_CUDA_MOE_DOWN);
+        L.gate_slice = tensor_bytes(l, POKIT_CUDA_MOE_GATE) / cfg_.experts;
+        L.up_slice = tensor_bytes(l, POKIT_CUDA_MOE_UP) / cfg_.experts;
+        L.down_slice = tensor_bytes(l, POKIT_CUDA_MOE_DOWN) / cfg_.experts;
+        L.ffn_norm = reinterpret_cast<const float*>(tensor_ptr(l, POKIT_CUDA_MOE_FFN_NORM));
+        if (cfg_.shared_inter) {
+            L.shared_inter = static_cast<uint32_t>(cfg_.shared_inter);
+            L.shared_router = reinterpret_cast<const float*>(tensor_ptr(l, POKIT_CUDA_MOE_SHARED_ROUTER));
+            L.shared_gate_type = cfg_.shared_gate_type;
+            L.shared_up_type = cfg_.shared_up_type;
+            L.shared_down_type = cfg_.shared_down_type;
+            L.shared_gate = tensor_ptr(l, POKIT_CUDA_MOE_SHARED_GATE);
+            L.shared_up = tensor_ptr(l, POKIT_CUDA_MOE_SHARED_UP);
+            L.shared_down = tensor_ptr(l, POKIT_CUDA_MOE_SHARED_DOWN);
+        }
+        return L;
+    }
+
+    void mark_resident(size_t layer, uint32_t t) {
+        if (!(resident_[layer] & (1u << t))) {
+            resident_[layer] |= 1u << t;
+            resident_bytes_ += tensor_bytes(layer, t);
+        }
+    }
+
+    // Every tensor this configuration defines for `layer` has been written.
+    bool resident_complete(size_t layer) const {
+        uint32_t need = 0;
+        for (uint32_t t = 0; t < 9; ++t)
+            if (tensor_bytes(layer, t)) need |= 1u << t;
+        return (resident_[layer] & need) == need;
+    }
+
+    void ensure_ok() const {
+        if (failed_) throw std::runtime_error("CUDA MoE backend failed earlier: " + failure_);
+    }
+
+    void guard(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return;
+        if (e == cudaErrorInvalidValue)
+            throw std::invalid_argument(std::string(what) + ": unsupported shape or argument");
+        failed_ = true;
+        failure_ = std::string(what) + ": " + cudaGetErrorString(e);
+        throw std::runtime_error(failure_);
+    }
+
+    pokit_cuda_moe_config cfg_;
+    int device_ = 0;
+    std::vector<uint32_t> layer_down_;
+    std::vector<std::array<uint64_t, 9>> offsets_;
+    uint8_t* pool_ = nullptr;
+    uint64_t pool_bytes_ = 0;
+    std::vector<MoeLayerDev> devs_;
+    void* scratch_ = nullptr;
+    uint64_t scratch_bytes_ = 0;
+    MoeScratch S_;
+    void* io_ = nullptr;
+    void* pinned_ = nullptr;
+    cudaStream_t stream_ = nullptr;
+    cudaStream_t capture_stream_ = nullptr;
+    std::map<std::tuple<size_t, size_t, float*>, cudaGraphExec_t> graphs_;
+    std::vector<uint32_t> resident_;   // per layer: bit t = tensor t written
+    std::mutex mutex_;
+    bool failed_ = false;
+    std::string failure_;
+    uint64_t resident_bytes_ = 0, bytes_read_ = 0, read_operations_ = 0, read_time_ns_ = 0;
+    mutable uint64_t hits_ = 0;
+    uint64_t forward_calls_ = 0, kernel_launches_ = 0;
+};
+
+// ---------------------------------------------------------------------------
+class LinearBackend {
+public:
+    explicit LinearBackend(int device) : device_(device) {
+        int count = 0;
+        check(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+        if (device < 0 || device >= count) throw std::invalid_argument("CUDA device out of range");
+        DeviceScope scope(device_);
+        check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaEventCreate(&start_), "cudaEventCreate");
+        check(cudaEventCreate(&stop_), "cudaEventCreate");
+    }
+    ~LinearBackend() {
+        for (auto& kv : cache_) cudaFree(kv.second);
+        if (io_) cudaFree(io_);
+        if (start_) cudaEventDestroy(start_);
+        if (stop_) cudaEventDestroy(stop_);
+        if (stream_) cudaStreamDestroy(stream_);
+    }
+    LinearBackend(const LinearBackend&) = delete;
+    LinearBackend& operator=(const LinearBackend&) = delete;
+
+    bool try_linear(uint32_t type, const void* w, size_t w_bytes, size_t rows, size_t cols,
+                    const float* x, float* y) {
+        std::lock_guard<std::mutex> lock(mutex_);
+        if (failed_) throw std::runtime_error("CUDA linear backend failed earlier: " + failure_);
+        if (!type_supported(type)) return false;
+        if (!w || !x || !y || rows == 0 || cols == 0 || cols % block_elems(type) ||
+            rows > UINT32_MAX || cols > UINT32_MAX)
+            throw std::invalid_argument("GGUF matrix dimensions do not match linear input/output");
+        if (w_bytes != rows * row_bytes(type, cols))
+            throw std::invalid_argument("weight byte size does not match dimensions");
+        DeviceScope scope(device_);
+        ++stats_.linear_calls;
+        void* dw = nullptr;
+        const auto key = std::make_pair(w, w_bytes);
+        auto it = cache_.find(key);
+        if (it == cache_.end()) {
+            const uint64_t t0 = now_ns();
+            guard(cudaMalloc(&dw, w_bytes), "cudaMalloc(weights)");
+            cache_.emplace(key, dw);
+            guard(cudaMemcpy(dw, w, w_bytes, cudaMemcpyHostToDevice), "upload");
+            stats_.model_cache_capacity_bytes += w_bytes;
+            stats_.model_cache_uploaded_bytes += w_bytes;
+            stats_.model_cache_upload_time_ns += now_ns() - t0;
+        } else {
+            dw = it->second;
+        }
+        const size_t need = align256(cols * 4) + align256(rows * 4);
+        if (need > io_bytes_) {
+            if (io_) cudaFree(io_);
+            io_ = nullptr;
+            guard(cudaMalloc(&io_, need), "cudaMalloc(io)");
+            io_bytes_ = need;
+        }
+        float* dx = static_cast<float*>(io_);
+        float* dy = reinterpret_cast<float*>(static_cast<uint8_t*>(io_) + align256(cols * 4));
+        guard(cudaMemcpyAsync(dx, x, cols * 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        guard(cudaEventRecord(start_, stream_), "event");
+        guard(launch_linear(type, dw, static_cast<uint32_t>(rows), static_cast<uint32_t>(cols), dx,
+                            dy, stream_), "linear");
+        guard(cudaEventRecord(stop_, stream_), "event");
+        guard(cudaMemcpyAsync(y, dy, rows * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
+        guard(cudaStreamSynchronize(stream_), "synchronize");
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, start_, stop_);
+        stats_.gpu_time_ns += static_cast<uint64_t>(ms * 1.0e6f);
+        stats_.weight_bytes += w_bytes;
+        ++stats_.dispatches;
+        switch (type) {
+            case kQ4_K: ++stats_.q4_k_dispatches; break;
+            case kQ5_K: ++stats_.q5_k_dispatches; break;
+            case kQ6_K: ++stats_.q6_k_dispatches; break;
+            case kQ8_0: ++stats_.q8_0_dispatches; break;
+            default: ++stats_.other_dispatches; break;
+        }
+        return true;
+    }
+
+    pokit_cuda_linear_stats stats() const {
+        std::lock_guard<std::mutex> lock(mutex_);
+        return stats_;
+    }
+
+private:
+    void guard(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return;
+        if (e == cudaErrorInvalidValue)
+            throw std::invalid_argument(std::string(what) + ": unsupported shape or argument");
+        failed_ = true;
+        failure_ = std::string(what) + ": " + cudaGetErrorString(e);
+        throw std::runtime_error(failure_);
+    }
+
+    int device_;
+    cudaStream_t stream_ = nullptr;
+    cudaEvent_t start_ = nullptr, stop_ = nullptr;
+    std::map<std::pair<const void*, size_t>, void*> cache_;
+    void* io_ = nullptr;
+    size_t io_bytes_ = 0;
+    mutable std::mutex mutex_;
+    bool failed_ = false;
+    std::string failure_;
+    pokit_cuda_linear_stats stats_{};
+};
+
+}  // namespace pokit
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+struct pokit_cuda_moe {
+    explicit pokit_cuda_moe(const pokit_cuda_moe_config& c) : impl(c) {}
+    pokit::MoeBackend impl;
+};
+
+struct pokit_cuda_linear_backend {
+    explicit pokit_cuda_linear_backend(int device) : impl(device) {}
+    pokit::LinearBackend impl;
+};
+
+namespace {
+
+void set_error(char* destination, size_t capacity, const char* message) noexcept {
+    if (!destination || capacity == 0) return;
+    const size_t n = std::min(capacity - 1, std::strlen(message));
+    std::memcpy(destination, message, n);
+    destination[n] = '\0';
+}
+
+template <typename F>
+pokit_cuda_status guarded(char* err, size_t cap, F&& body) noexcept {
+    try {
+        body();
+        set_error(err, cap, "");
+        return POKIT_CUDA_STATUS_OK;
+    } catch (const std::invalid_argument& e) {
+        set_error(err, cap, e.what());
+        return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    } catch (const std::exception& e) {
+        set_error(err, cap, e.what());
+        return POKIT_CUDA_STATUS_RUNTIME_ERROR;
+    } catch (...) {
+        set_error(err, cap, "unknown CUDA backend failure");
+        return POKIT_CUDA_STATUS_INTERNAL_ERROR;
+    }
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" {
+
+const char* pokit_cuda_version(void) { return "0.1.0"; }
+
+pokit_cuda_status pokit_cuda_linear(uint32_t ggml_type, const void* weights, size_t rows,
+                                    size_t cols, const float* input, float* output, void* stream,
+                                    char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!pokit::type_supported(ggml_type)) throw std::invalid_argument("unsupported GGML type");
+        if (!weights || !input || !output || rows == 0 || cols == 0 ||
+            cols % pokit::block_elems(ggml_type) || rows > UINT32_MAX || cols > UINT32_MAX)
+            throw std::invalid_argument("invalid linear dimensions");
+        pokit::check(pokit::launch_linear(ggml_type, weights, static_cast<uint32_t>(rows),
+                                          static_cast<uint32_t>(cols), input, output,
+                                          as_stream(stream)), "linear");
+    });
+}
+
+pokit_cuda_status pokit_cuda_dequantize_rows(uint32_t ggml_type, const void* encoded, size_t rows,
+                                             size_t cols, float* output, void* stream,
+                                             char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!pokit::type_supported(ggml_type)) throw std::invalid_argument("unsupported GGML type");
+        if (!encoded || !output || rows == 0 || cols == 0 || cols % pokit::block_elems(ggml_type) ||
+            cols % 32 || rows > UINT32_MAX || cols > UINT32_MAX)
+            throw std::invalid_argument("invalid row dimensions");
+        pokit::check(pokit::launch_dequantize(ggml_type, encoded, static_cast<uint32_t>(rows),
+                                              static_cast<uint32_t>(cols), output, as_stream(stream)),
+                     "dequantize");
+    });
+}
+
+pokit_cuda_status pokit_cuda_route_experts(const float* logits, size_t n, size_t top_k,
+                                           uint32_t flavour, int normalize,
+                                           float expert_weights_scale, uint32_t* ids_out,
+                                           float* weights_out, uint32_t* status_out, void* stream,
+                                           char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!logits || !ids_out || !weights_out || n == 0 || n > 1024 || top_k == 0 ||
+            top_k > n || top_k > 64 || flavour > 1)
+            throw std::invalid_argument("invalid expert top-k");
+        pokit::check(pokit::launch_route_experts(logits, static_cast<uint32_t>(n),
+                                                 static_cast<uint32_t>(top_k), flavour,
+                                                 normalize ? 1u : 0u, expert_weights_scale, ids_out,
+                                                 weights_out, status_out, as_stream(stream)),
+                     "route");
+    });
+}
+
+pokit_cuda_status pokit_cuda_synthesize_blocks(uint32_t ggml_type, uint64_t seed, uint64_t stream_id,
+                                               size_t nblocks, void* dst, void* stream,
+                                               char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!dst || !pokit::quant_supported(ggml_type))
+            throw std::invalid_argument("synthesis needs a quantised type and a destination");
+        pokit::check(pokit::launch_synth_blocks(ggml_type, seed, stream_id, nblocks, dst,
+                                                as_stream(stream)), "synthesize");
+    });
+}
+
+pokit_cuda_status pokit_cuda_linear_backend_create(int device, pokit_cuda_linear_backend** out,
+                                                   char* error_buffer, size_t error_capacity) {
+    if (out) *out = nullptr;
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!out) throw std::invalid_argument("output handle is required");
+        *out = new pokit_cuda_linear_backend(device);
+    });
+}
+
+void pokit_cuda_linear_backend_destroy(pokit_cuda_linear_backend* backend) { delete backend; }
+
+pokit_cuda_status pokit_cuda_linear_backend_try_linear(
+    pokit_cuda_linear_backend* backend, uint32_t ggml_type, const void* weights_host,
+    size_t weights_bytes, size_t rows, size_t cols, const float* input_host, float* output_host,
+    int* handled, char* error_buffer, size_t error_capacity) {
+    if (handled) *handled = 0;
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!backend || !handled) throw std::invalid_argument("backend and handled flag are required");
+        *handled = backend->impl.try_linear(ggml_type, weights_host, weights_bytes, rows, cols,
+                                            input_host, output_host) ? 1 : 0;
+    });
+}
+
+pokit_cuda_status pokit_cuda_linear_backend_get_stats(const pokit_cuda_linear_backend* backend,
+                                                      pokit_cuda_linear_stats* out_stats) {
+    if (!backend || !out_stats) return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    try {
+        *out_stats = backend->impl.stats();
+        return POKIT_CUDA_STATUS_OK;
+    } catch (...) {
+        return POKIT_CUDA_STATUS_INTERNAL_ERROR;
+    }
+}
+
+pokit_cuda_status pokit_cuda_moe_create(const pokit_cuda_moe_config* config, pokit_cuda_moe** out_moe,
+                                        char* error_buffer, size_t error_capacity) {
+    if (out_moe) *out_moe = nullptr;
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!config || !out_moe) throw std::invalid_argument("configuration and output handle are required");
+        *out_moe = new pokit_cuda_moe(*config);
+    });
+}
+
+void pokit_cuda_moe_destroy(pokit_cuda_moe* moe) { delete moe; }
+
+pokit_cuda_status pokit_cuda_moe_upload_tensor(pokit_cuda_moe* moe, size_t layer, uint32_t tensor,
+                                               const void* host_bytes, size_t bytes,
+                                               char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.upload_tensor(layer, tensor, host_bytes, bytes);
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_upload_layer(pokit_cuda_moe* moe, size_t layer,
+                                              const pokit_cuda_moe_layer_host* t,
+                                              char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe || !t) throw std::invalid_argument("MoE handle and tensors are required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        const void* ptrs[9] = {t->router, t->gate, t->up, t->down, t->ffn_norm,
+                               t->shared_router, t->shared_gate, t->shared_up, t->shared_down};
+        for (uint32_t i = 0; i < 9; ++i) {
+            if (!ptrs[i]) continue;
+            moe->impl.upload_tensor(layer, i, ptrs[i], moe->impl.tensor_bytes(layer, i));
+        }
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_synthesize_tensor(pokit_cuda_moe* moe, size_t layer, uint32_t tensor,
+                                                   uint64_t seed, uint64_t stream_id,
+                                                   char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.synthesize_tensor(layer, tensor, seed, stream_id);
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_expert_view(const pokit_cuda_moe* moe, size_t layer, uint32_t matrix,
+                                             size_t expert, const void** device_ptr, size_t* bytes) {
+    if (!moe || !device_ptr || !bytes) return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    try {
+        moe->impl.expert_view(layer, matrix, expert, device_ptr, bytes);
+        return POKIT_CUDA_STATUS_OK;
+    } catch (const std::invalid_argument&) {
+        return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    } catch (...) {
+        return POKIT_CUDA_STATUS_INTERNAL_ERROR;
+    }
+}
+
+pokit_cuda_status pokit_cuda_moe_forward(pokit_cuda_moe* moe, size_t layer, const float* input,
+                                         float* output, uint32_t* route_ids, float* route_weights,
+                                         void* stream, char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.forward(layer, input, output, route_ids, route_weights, as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_forward_host(pokit_cuda_moe* moe, size_t layer, const float* input_host,
+                                              float* output_host, uint32_t* route_ids_host,
+                                              float* route_weights_host, char* error_buffer,
+                                              size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.forward_host(layer, input_host, output_host, route_ids_host, route_weights_host);
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_decode_layers(pokit_cuda_moe* moe, size_t first, size_t count,
+                                               float* hidden, void* stream, char* error_buffer,
+                                               size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.decode_layers(first, count, hidden, as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_decode_layers_host(pokit_cuda_moe* moe, size_t first, size_t count,
+                                                    const float* hidden_in, float* hidden_out,
+                                                    char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.decode_layers_host(first, count, hidden_in, hidden_out);
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_synchronize(pokit_cuda_moe* moe, void* stream, char* error_buffer,
+                                             size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.synchronize(as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_get_stats(const pokit_cuda_moe* moe, pokit_cuda_moe_stats* out_stats) {
+    if (!moe || !out_stats) return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    *out_stats = moe->impl.stats();
+    return POKIT_CUDA_STATUS_OK;
+}
+
+size_t pokit_cuda_moe_tensor_bytes(const pokit_cuda_moe* moe, size_t layer, uint32_t tensor) {
+    return moe ? static_cast<size_t>(moe->impl.tensor_bytes(layer, tensor)) : 0;
+}
+
+}  // extern "C"

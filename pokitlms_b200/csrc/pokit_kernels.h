@@ -1,0 +1,79 @@
+// pokit_kernels.h -- internal launcher API between the C++ host layer and the
+// sm_100a kernels.  Not part of the public C ABI (include/pokit_cuda.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pokit {
+
+int device_sm_count();
+
+// y[rows] = W[rows, cols] . x for a GGUF-encoded W (F32, Q8_0, Q4_K, Q5_K, Q6_K).
+cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
+                          const float* x, float* y, cudaStream_t stream,
+                          bool force_generic = false);
+
+// out[rows, cols] = decoded weights, bit-identical to the reference decoders.
+cudaError_t launch_dequantize(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
+                              float* out, cudaStream_t stream);
+
+// Softmax top-k routing of E device logits (one warp); see route_warp.
+cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, uint32_t flavour,
+                                 uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
+                                 uint32_t* status, cudaStream_t stream);
+
+// Fills `nblocks` GGUF blocks of `type` at dst from the counter-based
+// synthetic generator (seed, stream_id); see pokitlms_b200/synth.py.
+cudaError_t launch_synth_blocks(uint32_t type, uint64_t seed, uint64_t stream_id,
+                                uint64_t nblocks, void* dst, cudaStream_t stream);
+
+// Everything one MoE FFN block needs on the device.
+struct MoeLayerDev {
+    uint32_t hidden = 0, inter = 0, experts = 0, top_k = 0;
+    uint32_t flavour = 0;        // 0 = Qwen3-MoE block, 1 = Qwen3.5-MoE block
+    uint32_t normalize = 1;      // renormalise the selected probabilities
+    float expert_weights_scale = 1.0f;
+    const float* router = nullptr;            // F32 [experts, hidden]
+    uint32_t gate_type = 0, up_type = 0, down_type = 0;
+    const uint8_t* gate = nullptr;            // experts x [inter rows, hidden cols]
+    const uint8_t* up = nullptr;
+    const uint8_t* down = nullptr;            // experts x [hidden rows, inter cols]
+    uint64_t gate_slice = 0, up_slice = 0, down_slice = 0;   // bytes per expert
+    const float* ffn_norm = nullptr;          // F32 [hidden], decode chain only
+    float rms_eps = 1e-6f;
+    // Qwen3.5 shared expert (absent when shared_inter == 0).
+    uint32_t shared_inter = 0;
+    const float* shared_router = nullptr;     // F32 [hidden]
+    uint32_t shared_gate_type = 0, shared_up_type = 0, shared_down_type = 0;
+    const uint8_t* shared_gate = nullptr;
+    const uint8_t* shared_up = nullptr;
+    const uint8_t* shared_down = nullptr;
+};
+
+// Scratch used by one in-flight MoE block (device memory owned by the caller).
+struct MoeScratch {
+    float* x = nullptr;            // [hidden] normalised input
+    float* partial = nullptr;      // [(experts + 1) * splits] router partial dots
+    float* logits = nullptr;       // [experts]
+    uint32_t* ids = nullptr;       // [top_k]
+    float* weights = nullptr;      // [top_k + 1] combine weights (last = shared gate)
+    float* act = nullptr;          // [(top_k + 1) * max(inter, shared_inter)]
+    uint32_t* counter = nullptr;   // last-block hand-off counter (must start at 0)
+    uint32_t* status = nullptr;    // sticky StatusBits
+};
+
+// Scratch sizing helper (bytes), shared by the allocator and the no-alloc path.
+uint64_t moe_scratch_bytes(const MoeLayerDev& L);
+// Carves `base` (256-byte aligned, moe_scratch_bytes(L) long) into a MoeScratch.
+MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base);
+
+// One MoE block: routes `x_in` (already normalised) or, when `hidden` is
+// non-null, rms_norm(hidden, ffn_norm); writes the routed (+ shared) MoE
+// output to `moe_out`, or adds it into `hidden` when moe_out is null.
+// `next_router` (may be null) is prefetched into L2 for the following layer.
+cudaError_t launch_moe_block(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
+                             float* hidden, float* moe_out, const float* next_router,
+                             cudaStream_t stream);
+
+}  // namespace pokit

@@ -1,0 +1,289 @@
+// pokit_linear.cu -- per-matrix GGUF matvec and row dequantisation on sm_100a.
+//
+// Device side of the TensorLinearBackend seam (PokitLMs
+// include/pokitlms/model/tensor_linear.hpp:11-18): y[rows] = W[rows, cols] . x
+// with W in its GGUF block encoding, FP32 x and FP32 accumulation, plus the
+// row decoder behind dequantize_quantized_row (quantized_linear.hpp:11-13).
+#include "pokit_kernels.h"
+#include "pokit_quant.cuh"
+
+namespace pokit {
+namespace {
+
+constexpr int kLinearThreads = 256;
+
+// Q4_K: 8 rows per warp, lane = (row r = lane/4, chunk c = lane%4); the CTA
+// prepares x once and then streams its rows.
+__global__ void __launch_bounds__(kLinearThreads)
+linear_q4k_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols,
+                  const float* __restrict__ x, float* __restrict__ y) {
+    extern __shared__ float smem[];
+    const int nsb = static_cast<int>(cols >> 8);
+    float* xp = smem;                                  // nsb*4*68 floats
+    float* gsum = smem + nsb * 4 * kQ4kChunkStride;    // nsb*8 floats
+    q4k_prepare_x(x, static_cast<int>(cols), xp, gsum);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+    const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
+    const uint32_t warp_id = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const uint64_t rb = static_cast<uint64_t>(nsb) * 144u;
+    for (uint32_t base = warp_id * 8u; base < rows; base += warps_total * 8u) {
+        const uint32_t row = base + r;
+        float acc = 0.0f;
+        if (row < rows) {
+            const uint8_t* rp = w + row * rb;
+#pragma unroll 2
+            for (int sb = 0; sb < nsb; ++sb) {
+                const uint8_t* blk = rp + sb * 144;
+                const uint4 hdr = ldg_stream128(blk);
+                const uint4 q0 = ldg_stream128(blk + 16 + 32 * c);
+                const uint4 q1 = ldg_stream128(blk + 32 + 32 * c);
+                const int k = sb * 4 + c;
+                acc += q4k_chunk_dot(hdr, q0, q1, c, xp + k * kQ4kChunkStride,
+                                     gsum[sb * 8 + 2 * c], gsum[sb * 8 + 2 * c + 1]);
+            }
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (c == 0 && row < rows) y[row] = acc;
+    }
+}
+
+// F32: one warp per row, 128-bit loads straight from global.
+__global__ void __launch_bounds__(kLinearThreads)
+linear_f32_kernel(const float* __restrict__ w, uint32_t rows, uint32_t cols,
+                  const float* __restrict__ x, float* __restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
+    for (uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
+         row += warps_total) {
+        const float* rp = w + static_cast<uint64_t>(row) * cols;
+        float acc = 0.0f;
+        if ((cols & 3u) == 0 && (reinterpret_cast<uint64_t>(rp) & 15u) == 0) {
+            for (uint32_t i = lane * 4u; i < cols; i += 128u) {
+                const uint4 v = ldg_stream128(rp + i);
+                const float4 xv = *reinterpret_cast<const float4*>(x + i);
+                acc = fmaf(__uint_as_float(v.x), xv.x, acc);
+                acc = fmaf(__uint_as_float(v.y), xv.y, acc);
+                acc = fmaf(__uint_as_float(v.z), xv.z, acc);
+                acc = fmaf(__uint_as_float(v.w), xv.w, acc);
+            }
+        } else {
+            for (uint32_t i = lane; i < cols; i += 32u) acc = fmaf(__ldg(rp + i), x[i], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) y[row] = acc;
+    }
+}
+
+// Any quantised type: one warp per row, row staged in shared memory, lanes
+// take 32-weight groups.  x sits in shared memory in plain order.
+template <uint32_t T>
+__global__ void __launch_bounds__(kLinearThreads)
+linear_generic_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols,
+                      const float* __restrict__ x, float* __restrict__ y) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    float* xs = reinterpret_cast<float*>(smem_raw);
+    const uint32_t rbytes = static_cast<uint32_t>(row_bytes(T, cols));
+    const uint32_t stage = (rbytes + 15u) & ~15u;
+    uint8_t* stage_base = smem_raw + static_cast<uint64_t>(cols) * 4u;
+    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = x[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t* my_row = stage_base + warp * stage;
+    const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
+    const int groups = static_cast<int>(cols >> 5);
+    for (uint32_t row = blockIdx.x * (blockDim.x >> 5) + warp; row < rows; row += warps_total) {
+        warp_stage_row(w + static_cast<uint64_t>(row) * rbytes, rbytes, my_row, lane);
+        __syncwarp();
+        float acc = 0.0f;
+        for (int g = lane; g < groups; g += 32) acc += group_dot<T>(my_row, g, xs);
+        acc = warp_sum(acc);
+        if (lane == 0) y[row] = acc;
+        __syncwarp();
+    }
+}
+
+// Bit-exact decoders (explicit round-to-nearest operations so the compiler
+// cannot contract them into FMAs): same expressions as the reference's
+// decode_q4_k / decode_q5_k / decode_q6_k / Q8_0 scale (quantized_linear.cpp).
+template <uint32_t T>
+__device__ __forceinline__ void group_decode(const uint8_t* __restrict__ row, int g,
+                                             float* __restrict__ out) {
+    if constexpr (T == kF32) {
+        const float* w = reinterpret_cast<const float*>(row) + g * 32;
+        for (int i = 0; i < 32; ++i) out[i] = w[i];
+    } else if constexpr (T == kQ8_0) {
+        const uint8_t* blk = row + g * 34;
+        const float d = half_bits_to_float(sm_u16(blk));
+        const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
+        for (int i = 0; i < 32; ++i) out[i] = __fmul_rn(d, static_cast<float>(q[i]));
+    } else if constexpr (T == kQ4_K || T == kQ5_K) {
+        const int sb = g >> 3, j = g & 7;
+        const uint8_t* blk = row + sb * block_bytes(T);
+        const float d = half_bits_to_float(sm_u16(blk));
+        const float dmin = half_bits_to_float(sm_u16(blk + 2));
+        const uint8_t* packed = blk + 4;
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = packed[j] & 63u; mn = packed[j + 4] & 63u;
+        } else {
+            sc = (packed[j + 4] & 0x0fu) | ((packed[j - 4] >> 6) << 4);
+            mn = (packed[j + 4] >> 4) | ((packed[j] >> 6) << 4);
+        }
+        const float ds = __fmul_rn(d, static_cast<float>(sc));
+        const float dm = __fmul_rn(dmin, static_cast<float>(mn));
+        const int chunk = j >> 1, part = j & 1;
+        const uint8_t* qs = blk + (T == kQ4_K ? 16 : 48) + chunk * 32;
+        const uint8_t* qh = blk + 16;
+        for (int i = 0; i < 32; ++i) {
+            uint32_t q = part ? (qs[i] >> 4) : (qs[i] & 0x0fu);
+            if constexpr (T == kQ5_K) q += (qh[i] & (1u << (2 * chunk + part))) ? 16u : 0u;
+            out[i] = __fsub_rn(__fmul_rn(ds, static_cast<float>(q)), dm);
+        }
+    } else if constexpr (T == kQ6_K) {
+        const int sb = g >> 3, j = g & 7;
+        const uint8_t* blk = row + sb * 210;
+        const float d = half_bits_to_float(sm_u16(blk + 208));
+        const int half = j >> 2, jj = j & 3;
+        const uint8_t* ql = blk + half * 64 + (jj & 1) * 32;
+        const uint8_t* qh = blk + 128 + half * 32;
+        const int8_t* scales = reinterpret_cast<const int8_t*>(blk + 192 + half * 8);
+        const int shift_lo = (jj >> 1) * 4, shift_hi = jj * 2;
+        for (int l = 0; l < 32; ++l) {
+            const int q = static_cast<int>(((ql[l] >> shift_lo) & 0x0fu) |
+                                           (((qh[l] >> shift_hi) & 0x03u) << 4)) - 32;
+            out[l] = __fmul_rn(__fmul_rn(d, static_cast<float>(scales[l / 16 + 2 * jj])),
+                               static_cast<float>(q));
+        }
+    }
+}
+
+template <uint32_t T>
+__global__ void __launch_bounds__(kLinearThreads)
+dequantize_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols,
+                  float* __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const uint32_t rbytes = static_cast<uint32_t>(row_bytes(T, cols));
+    const uint32_t stage = (rbytes + 15u) & ~15u;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t* my_row = smem_raw + warp * stage;
+    const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
+    const int groups = static_cast<int>(cols >> 5);
+    for (uint32_t row = blockIdx.x * (blockDim.x >> 5) + warp; row < rows; row += warps_total) {
+        warp_stage_row(w + static_cast<uint64_t>(row) * rbytes, rbytes, my_row, lane);
+        __syncwarp();
+        for (int g = lane; g < groups; g += 32)
+            group_decode<T>(my_row, g, out + static_cast<uint64_t>(row) * cols + g * 32);
+        __syncwarp();
+    }
+}
+
+int sm_count_cached() {
+    static int count = 0;
+    if (count == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+        if (count <= 0) count = 148;
+    }
+    return count;
+}
+
+template <typename K>
+cudaError_t set_smem(K kernel, size_t bytes) {
+    if (bytes <= 48u * 1024u) return cudaSuccess;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(bytes));
+}
+
+template <uint32_t T>
+cudaError_t launch_generic(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y,
+                           cudaStream_t stream) {
+    const size_t stage = (row_bytes(T, cols) + 15u) & ~size_t(15);
+    const size_t smem = static_cast<size_t>(cols) * 4u + stage * (kLinearThreads / 32);
+    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    cudaError_t e = set_smem(linear_generic_kernel<T>, smem);
+    if (e != cudaSuccess) return e;
+    const uint32_t warps = kLinearThreads / 32;
+    uint32_t grid = (rows + warps - 1) / warps;
+    const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 4u;
+    if (grid > cap) grid = cap;
+    linear_generic_kernel<T><<<grid, kLinearThreads, smem, stream>>>(
+        static_cast<const uint8_t*>(w), rows, cols, x, y);
+    return cudaGetLastError();
+}
+
+template <uint32_t T>
+cudaError_t launch_dequant(const void* w, uint32_t rows, uint32_t cols, float* out,
+                           cudaStream_t stream) {
+    const size_t stage = (row_bytes(T, cols) + 15u) & ~size_t(15);
+    const size_t smem = stage * (kLinearThreads / 32);
+    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+    cudaError_t e = set_smem(dequantize_kernel<T>, smem);
+    if (e != cudaSuccess) return e;
+    const uint32_t warps = kLinearThreads / 32;
+    uint32_t grid = (rows + warps - 1) / warps;
+    const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 4u;
+    if (grid > cap) grid = cap;
+    dequantize_kernel<T><<<grid, kLinearThreads, smem, stream>>>(
+        static_cast<const uint8_t*>(w), rows, cols, out);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+int device_sm_count() { return sm_count_cached(); }
+
+cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
+                          const float* x, float* y, cudaStream_t stream, bool force_generic) {
+    if (rows == 0 || cols == 0) return cudaErrorInvalidValue;
+    switch (type) {
+        case kF32: {
+            const uint32_t warps = kLinearThreads / 32;
+            uint32_t grid = (rows + warps - 1) / warps;
+            const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 8u;
+            if (grid > cap) grid = cap;
+            linear_f32_kernel<<<grid, kLinearThreads, 0, stream>>>(
+                static_cast<const float*>(w), rows, cols, x, y);
+            return cudaGetLastError();
+        }
+        case kQ4_K: {
+            const bool aligned = (reinterpret_cast<uint64_t>(w) & 15u) == 0;
+            if (!force_generic && aligned) {
+                const uint32_t nsb = cols / 256u;
+                const size_t smem = (static_cast<size_t>(nsb) * 4u * kQ4kChunkStride +
+                                     nsb * 8u) * sizeof(float);
+                if (smem > 200u * 1024u) return cudaErrorInvalidValue;
+                cudaError_t e = set_smem(linear_q4k_kernel, smem);
+                if (e != cudaSuccess) return e;
+                uint32_t grid = (rows + 63u) / 64u;   // 8 warps x 8 rows per CTA pass
+                const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 2u;
+                if (grid > cap) grid = cap;
+                linear_q4k_kernel<<<grid, kLinearThreads, smem, stream>>>(
+                    static_cast<const uint8_t*>(w), rows, cols, x, y);
+                return cudaGetLastError();
+            }
+            return launch_generic<kQ4_K>(w, rows, cols, x, y, stream);
+        }
+        case kQ5_K: return launch_generic<kQ5_K>(w, rows, cols, x, y, stream);
+        case kQ6_K: return launch_generic<kQ6_K>(w, rows, cols, x, y, stream);
+        case kQ8_0: return launch_generic<kQ8_0>(w, rows, cols, x, y, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_dequantize(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
+                              float* out, cudaStream_t stream) {
+    if (rows == 0 || cols == 0) return cudaErrorInvalidValue;
+    switch (type) {
+        case kF32: return launch_dequant<kF32>(w, rows, cols, out, stream);
+        case kQ8_0: return launch_dequant<kQ8_0>(w, rows, cols, out, stream);
+        case kQ4_K: return launch_dequant<kQ4_K>(w, rows, cols, out, stream);
+        case kQ5_K: return launch_dequant<kQ5_K>(w, rows, cols, out, stream);
+        case kQ6_K: return launch_dequant<kQ6_K>(w, rows, cols, out, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace pokit

@@ -1,0 +1,240 @@
+// pokit_quant.cuh -- GGUF K-quant / Q8_0 dequant-dot building blocks (sm_100a).
+//
+// Block layouts (PokitLMs src/quantized_linear.cpp):
+//   Q4_K 144 B / 256 w : fp16 d @0, fp16 dmin @2, 12 B packed 6-bit scales+mins @4,
+//                        128 B nibbles @16 (decode_q4_k, :166-205)
+//   Q5_K 176 B / 256 w : d, dmin, scales @4, qh[32] @16, qs[128] @48 (decode_q5_k, :286-328)
+//   Q6_K 210 B / 256 w : ql[128] @0, qh[64] @128, int8 scales[16] @192, fp16 d @208
+//                        (decode_q6_k, :330-358)
+//   Q8_0  34 B /  32 w : fp16 d @0, int8 q[32] @2 (linear_quantized<false>, :387-423)
+//
+// Two evaluation schemes live here:
+//
+//  * Q4_K "fast chunk" (used by the MoE kernels and the Q4_K matvec): one lane
+//    owns one 64-weight chunk (32 qs bytes = sub-blocks 2c and 2c+1) of one
+//    superblock and reads it with two 128-bit loads plus the 16-byte header.
+//    sum_j (ds*q_j - dm) x_j is evaluated as ds * sum q_j x_j - dm * sum x_j with
+//    the per-sub-block sums of x precomputed.  Nibbles become floats without a
+//    conversion instruction: OR-ing a nibble sitting at bit p (p <= 16) into
+//    the mantissa of 2^23 gives exactly 2^23 + q*2^p, and one packed FP32x2 add
+//    removes the 2^23.  The matching x was pre-scaled by 2^-p (exact), so each
+//    FMA forms the same rounded product q*x.  FP32 accumulation throughout.
+//
+//  * Generic "group" scheme (every type): one lane decodes a 32-weight group
+//    in the reference's own order (d*s*q - dmin*m in FP32) from a row staged in
+//    shared memory, and dots it with plain x.
+#pragma once
+
+#include "pokit_common.cuh"
+
+namespace pokit {
+
+constexpr uint32_t kMagic23 = 0x4B000000u;  // 2^23 as FP32 bits
+constexpr float kTwo23 = 8388608.0f;
+
+// Floats per prepared Q4_K chunk in shared memory: 64 values + 4 pad so the
+// four chunks a quarter-warp reads start in different bank groups.
+constexpr int kQ4kChunkStride = 68;
+
+// Pre-scale factors for the 8 nibble slots of one 32-bit qs word, in the order
+// q4k_chunk_dot consumes them: lo b0..b3, hi b0..b3 (see the bit map there).
+__device__ __forceinline__ float q4k_slot_scale(int slot) {
+    // lo: b0 p=0, b1 p=8, b2 p=16, b3 p=12 (after >>12); hi: b0 p=4, b1 p=12, b2 p=8, b3 p=16
+    constexpr float s[8] = {1.0f, 0x1p-8f, 0x1p-16f, 0x1p-12f, 0x1p-4f, 0x1p-12f, 0x1p-8f, 0x1p-16f};
+    return s[slot];
+}
+
+// Writes x (length H, a multiple of 256) into the prepared layout used by
+// q4k_chunk_dot:  chunk k = sb*4 + c occupies xp[k*68 .. k*68+63]; within it,
+// word m (0..7) holds {x_lo[4m..4m+3], x_hi[4m..4m+3]} pre-scaled per slot,
+// where x_lo = x[sb*256 + 64c + i], x_hi = x[sb*256 + 64c + 32 + i].
+// gsum[g] = sum of the 32 x values of sub-block g (g = sb*8 + j), in FP32.
+// Cooperative over the whole CTA; caller synchronises afterwards.
+__device__ __forceinline__ void q4k_prepare_x(const float* __restrict__ x, int H,
+                                              float* __restrict__ xp, float* __restrict__ gsum) {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float v = x[i];
+        const int sb = i >> 8, within = i & 255;
+        const int c = within >> 6, t = within & 63;
+        const int hi = t >> 5, idx = t & 31;   // sub-block 2c+hi, element idx
+        const int m = idx >> 2, b = idx & 3;
+        const int slot = hi * 4 + b;
+        xp[(sb * 4 + c) * kQ4kChunkStride + m * 8 + slot] = v * q4k_slot_scale(slot);
+    }
+    const int groups = H >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int g = warp; g < groups; g += nwarps) {
+        const float s = warp_sum(x[g * 32 + lane]);
+        if (lane == 0) gsum[g] = s;
+    }
+}
+
+// Unpacks the 6-bit scale and min of sub-blocks 2c and 2c+1 from the packed
+// header words (hy = packed[0..3], hz = packed[4..7], hw = packed[8..11]).
+// Restates the scale_min lambda of decode_q4_k (src/quantized_linear.cpp:176-188).
+__device__ __forceinline__ void q4k_scale_min_pair(uint32_t hy, uint32_t hz, uint32_t hw, int c,
+                                                   float& s0, float& m0, float& s1, float& m1) {
+    const int k = (2 * c) & 3;                 // byte index of sub-block 2c within a word
+    const uint32_t a0 = (hy >> (8 * k)) & 0xffu, a1 = (hy >> (8 * k + 8)) & 0xffu;
+    const uint32_t b0 = (hz >> (8 * k)) & 0xffu, b1 = (hz >> (8 * k + 8)) & 0xffu;
+    uint32_t sc0, mn0, sc1, mn1;
+    if (c < 2) {
+        sc0 = a0 & 63u; mn0 = b0 & 63u;
+        sc1 = a1 & 63u; mn1 = b1 & 63u;
+    } else {
+        const uint32_t c0 = (hw >> (8 * k)) & 0xffu, c1 = (hw >> (8 * k + 8)) & 0xffu;
+        sc0 = (c0 & 0x0fu) | ((a0 >> 6) << 4); mn0 = (c0 >> 4) | ((b0 >> 6) << 4);
+        sc1 = (c1 & 0x0fu) | ((a1 >> 6) << 4); mn1 = (c1 >> 4) | ((b1 >> 6) << 4);
+    }
+    s0 = static_cast<float>(sc0); m0 = static_cast<float>(mn0);
+    s1 = static_cast<float>(sc1); m1 = static_cast<float>(mn1);
+}
+
+// sum over the 32 weights of one qs word pair-accumulated into lo/hi float2s.
+__device__ __forceinline__ void q4k_word(uint32_t w, const float4 xa, const float4 xb,
+                                         float2& acc_lo, float2& acc_hi) {
+    const uint32_t w2 = w >> 12;
+    const float2 neg = make_float2(-kTwo23, -kTwo23);
+    float2 l01 = make_float2(__uint_as_float((w & 0x0000000Fu) | kMagic23),
+                             __uint_as_float((w & 0x00000F00u) | kMagic23));
+    float2 l23 = make_float2(__uint_as_float((w & 0x000F0000u) | kMagic23),
+                             __uint_as_float((w2 & 0x0000F000u) | kMagic23));
+    float2 h01 = make_float2(__uint_as_float((w & 0x000000F0u) | kMagic23),
+                             __uint_as_float((w & 0x0000F000u) | kMagic23));
+    float2 h23 = make_float2(__uint_as_float((w2 & 0x00000F00u) | kMagic23),
+                             __uint_as_float((w2 & 0x000F0000u) | kMagic23));
+    l01 = add2(l01, neg); l23 = add2(l23, neg);
+    h01 = add2(h01, neg); h23 = add2(h23, neg);
+    acc_lo = fma2(l01, make_float2(xa.x, xa.y), acc_lo);
+    acc_lo = fma2(l23, make_float2(xa.z, xa.w), acc_lo);
+    acc_hi = fma2(h01, make_float2(xb.x, xb.y), acc_hi);
+    acc_hi = fma2(h23, make_float2(xb.z, xb.w), acc_hi);
+}
+
+// Contribution of chunk c (64 weights) of one Q4_K superblock, given its
+// 16-byte header `hdr`, its 32 qs bytes (q0 = bytes 0..15, q1 = 16..31), the
+// prepared x chunk `xp` (shared memory, 64 floats) and the two sub-block sums.
+__device__ __forceinline__ float q4k_chunk_dot(uint4 hdr, uint4 q0, uint4 q1, int c,
+                                               const float* __restrict__ xp, float gs0, float gs1) {
+    float2 acc_lo = make_float2(0.f, 0.f), acc_hi = make_float2(0.f, 0.f);
+    const float4* x4 = reinterpret_cast<const float4*>(xp);
+    q4k_word(q0.x, x4[0], x4[1], acc_lo, acc_hi);
+    q4k_word(q0.y, x4[2], x4[3], acc_lo, acc_hi);
+    q4k_word(q0.z, x4[4], x4[5], acc_lo, acc_hi);
+    q4k_word(q0.w, x4[6], x4[7], acc_lo, acc_hi);
+    q4k_word(q1.x, x4[8], x4[9], acc_lo, acc_hi);
+    q4k_word(q1.y, x4[10], x4[11], acc_lo, acc_hi);
+    q4k_word(q1.z, x4[12], x4[13], acc_lo, acc_hi);
+    q4k_word(q1.w, x4[14], x4[15], acc_lo, acc_hi);
+    const float d = half_bits_to_float(hdr.x);
+    const float dmin = half_bits_to_float(hdr.x >> 16);
+    float s0, m0, s1, m1;
+    q4k_scale_min_pair(hdr.y, hdr.z, hdr.w, c, s0, m0, s1, m1);
+    const float sum_lo = acc_lo.x + acc_lo.y;
+    const float sum_hi = acc_hi.x + acc_hi.y;
+    // (d*s) and (dmin*m) are formed exactly as the reference forms ds0/dm0.
+    const float ds0 = d * s0, dm0 = dmin * m0, ds1 = d * s1, dm1 = dmin * m1;
+    float r = ds0 * sum_lo;
+    r = fmaf(-dm0, gs0, r);
+    r = fmaf(ds1, sum_hi, r);
+    r = fmaf(-dm1, gs1, r);
+    return r;
+}
+
+// ---------------------------------------------------------------------------
+// Generic scheme: decode one 32-weight group g of a row held in shared memory
+// (bytes, any alignment) and dot it with x[g*32 .. g*32+31] (shared memory).
+// Arithmetic per weight follows the reference decoders exactly.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t sm_u16(const uint8_t* p) {
+    return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8);
+}
+
+template <uint32_t T>
+__device__ __forceinline__ float group_dot(const uint8_t* __restrict__ row, int g,
+                                           const float* __restrict__ x) {
+    const float* xg = x + g * 32;
+    float acc = 0.0f;
+    if constexpr (T == kF32) {
+        const float* w = reinterpret_cast<const float*>(row) + g * 32;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) acc = fmaf(w[i], xg[i], acc);
+    } else if constexpr (T == kQ8_0) {
+        const uint8_t* blk = row + g * 34;
+        const float d = half_bits_to_float(sm_u16(blk));
+        const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
+        float s = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) s = fmaf(static_cast<float>(q[i]), xg[i], s);
+        acc = d * s;
+    } else if constexpr (T == kQ4_K || T == kQ5_K) {
+        const int sb = g >> 3, j = g & 7;
+        const uint8_t* blk = row + sb * block_bytes(T);
+        const float d = half_bits_to_float(sm_u16(blk));
+        const float dmin = half_bits_to_float(sm_u16(blk + 2));
+        const uint8_t* packed = blk + 4;
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = packed[j] & 63u; mn = packed[j + 4] & 63u;
+        } else {
+            sc = (packed[j + 4] & 0x0fu) | ((packed[j - 4] >> 6) << 4);
+            mn = (packed[j + 4] >> 4) | ((packed[j] >> 6) << 4);
+        }
+        const float ds = d * static_cast<float>(sc), dm = dmin * static_cast<float>(mn);
+        const int chunk = j >> 1, part = j & 1;
+        const uint8_t* qs = blk + (T == kQ4_K ? 16 : 48) + chunk * 32;
+        if constexpr (T == kQ4_K) {
+#pragma unroll 8
+            for (int i = 0; i < 32; ++i) {
+                const uint32_t q = part ? (qs[i] >> 4) : (qs[i] & 0x0fu);
+                acc = fmaf(ds * static_cast<float>(q) - dm, xg[i], acc);
+            }
+        } else {
+            const uint8_t* qh = blk + 16;
+            const uint32_t bit = 1u << (2 * chunk + part);
+#pragma unroll 8
+            for (int i = 0; i < 32; ++i) {
+                const uint32_t q = (part ? (qs[i] >> 4) : (qs[i] & 0x0fu)) + ((qh[i] & bit) ? 16u : 0u);
+                acc = fmaf(ds * static_cast<float>(q) - dm, xg[i], acc);
+            }
+        }
+    } else if constexpr (T == kQ6_K) {
+        const int sb = g >> 3, j = g & 7;
+        const uint8_t* blk = row + sb * 210;
+        const float d = half_bits_to_float(sm_u16(blk + 208));
+        const int half = j >> 2, jj = j & 3;
+        const uint8_t* ql = blk + half * 64 + (jj & 1) * 32;
+        const uint8_t* qh = blk + 128 + half * 32;
+        const int8_t* scales = reinterpret_cast<const int8_t*>(blk + 192 + half * 8);
+        const int shift_lo = (jj >> 1) * 4, shift_hi = jj * 2;
+#pragma unroll 8
+        for (int l = 0; l < 32; ++l) {
+            const int q = static_cast<int>(((ql[l] >> shift_lo) & 0x0fu) |
+                                           (((qh[l] >> shift_hi) & 0x03u) << 4)) - 32;
+            const float s = static_cast<float>(scales[l / 16 + 2 * jj]);
+            acc = fmaf(d * s * static_cast<float>(q), xg[l], acc);
+        }
+    }
+    return acc;
+}
+
+// Warp-cooperative copy of `bytes` of a weight row from global to shared
+// memory.  Uses 16-byte loads when source and size allow it, else 4- or
+// 2-byte loads (GGUF rows of Q6_K/Q8_0 are only 2-byte aligned in general).
+__device__ __forceinline__ void warp_stage_row(const uint8_t* __restrict__ src, uint32_t bytes,
+                                               uint8_t* __restrict__ dst, int lane) {
+    const uint64_t a = reinterpret_cast<uint64_t>(src);
+    if ((a & 15u) == 0 && (bytes & 15u) == 0) {
+        for (uint32_t o = lane * 16u; o < bytes; o += 32u * 16u)
+            *reinterpret_cast<uint4*>(dst + o) = ldg_stream128(src + o);
+    } else if ((a & 3u) == 0 && (bytes & 3u) == 0) {
+        for (uint32_t o = lane * 4u; o < bytes; o += 32u * 4u)
+            *reinterpret_cast<uint32_t*>(dst + o) = ldg_stream32(src + o);
+    } else {
+        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+        uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);
+        for (uint32_t o = lane; o < bytes / 2u; o += 32u) d16[o] = __ldg(s16 + o);
+    }
+}
+
+}  // namespace pokit
