@@ -265,7 +265,8 @@ def main() -> None:
     be = B.CudaMoeBackend(layers=layers, hidden=H, inter=I, experts=E, top_k=K_TOP,
                           rms_epsilon=EPS, device=local)
     build_model(be, layers)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     from pokitlms_b200 import synth
     n_in = args.steps + args.warmup
     inputs = torch.from_numpy(np.stack([synth.activation(H, SEED + rank, i) for i in range(n_in)])).cuda()

@@ -32,11 +32,17 @@ def _ptr(t) -> int | None:
     return int(t.data_ptr())
 
 
-def _stream(stream) -> int | None:
+# cudaStreamLegacy: the C ABI reads a NULL stream as "the handle's own
+# stream", so torch's legacy default stream (handle 0) is passed explicitly.
+_CUDA_STREAM_LEGACY = 0x1
+
+
+def _stream(stream) -> int:
     if stream is None:
         import torch
-        return int(torch.cuda.current_stream().cuda_stream)
-    return int(getattr(stream, "cuda_stream", stream))
+        stream = torch.cuda.current_stream()
+    handle = int(getattr(stream, "cuda_stream", stream) or 0)
+    return handle if handle else _CUDA_STREAM_LEGACY
 
 
 def _np_ptr(a: np.ndarray | None):

@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <array>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -130,6 +131,16 @@ public:
         check(cudaMalloc(&scratch_, scratch_bytes_), "cudaMalloc(scratch)");
         check(cudaMemset(scratch_, 0, scratch_bytes_), "cudaMemset(scratch)");
         S_ = moe_scratch_carve(devs_[0], scratch_);
+        for (size_t l = 0; l < c.layers; ++l) check(prepare_moe_block(devs_[l]), "prepare MoE kernels");
+        check(cudaMalloc(&devs_dev_, sizeof(MoeLayerDev) * c.layers), "cudaMalloc(layer table)");
+        check(cudaMemcpy(devs_dev_, devs_.data(), sizeof(MoeLayerDev) * c.layers,
+                         cudaMemcpyHostToDevice), "upload layer table");
+        // The decode chain runs as one persistent cooperative kernel per token
+        // when every CTA fits on the device at once; otherwise as a CUDA graph
+        // of per-block kernels.  POKIT_CUDA_DECODE=graph selects the latter.
+        const char* mode = std::getenv("POKIT_CUDA_DECODE");
+        const bool want_graph = mode && std::string(mode) == "graph";
+        decode_grid_ = want_graph ? 0u : moe_decode_grid(devs_[0]);
         check(cudaMalloc(&io_, align256(c.hidden * 4) * 2), "cudaMalloc(io)");
         check(cudaMallocHost(&pinned_, align256(c.hidden * 4) * 2 + 4096), "cudaMallocHost");
     }
@@ -139,6 +150,7 @@ public:
         if (pinned_) cudaFreeHost(pinned_);
         if (io_) cudaFree(io_);
         if (scratch_) cudaFree(scratch_);
+        if (devs_dev_) cudaFree(devs_dev_);
         if (pool_) cudaFree(pool_);
         if (capture_stream_) cudaStreamDestroy(capture_stream_);
         if (stream_) cudaStreamDestroy(stream_);
@@ -266,6 +278,16 @@ public:
             if (!resident_complete(l)) throw std::invalid_argument("layer weights were not uploaded");
         DeviceScope scope(device_);
         cudaStream_t st = s ? s : stream_;
+        if (decode_grid_) {
+            guard(launch_moe_decode(devs_dev_, devs_[first], static_cast<uint32_t>(first),
+                                    static_cast<uint32_t>(count), S_, hidden, barrier_count_,
+                                    decode_grid_, st), "decode kernel");
+            barrier_count_ += static_cast<uint32_t>(count) * moe_barriers_per_layer() * decode_grid_;
+            forward_calls_ += count;
+            hits_ += count * cfg_.top_k;
+            kernel_launches_ += 1;
+            return;
+        }
         const auto key = std::make_tuple(first, count, hidden);
         auto it = graphs_.find(key);
         if (it == graphs_.end()) {
@@ -310,6 +332,13 @@ public:
         guard(cudaStreamSynchronize(s ? s : stream_), "synchronize");
         uint32_t status = 0;
         guard(cudaMemcpy(&status, S_.status, 4, cudaMemcpyDeviceToHost), "status");
+        if (status & kStatusWaitTimeout) {
+            // A grid barrier gave up: the launch was abandoned and the barrier
+            // counter no longer matches the host's count.  Sticky, like a CUDA error.
+            failed_ = true;
+            failure_ = "persistent decode kernel abandoned a grid barrier (wait timeout)";
+            throw std::runtime_error(failure_);
+        }
         if (status) {
             guard(cudaMemset(S_.status, 0, 4), "status reset");
             if (status & kStatusNonFiniteLogits)
@@ -403,6 +432,9 @@ private:
     uint64_t pool_bytes_ = 0;
     std::vector<MoeLayerDev> devs_;
     void* scratch_ = nullptr;
+    MoeLayerDev* devs_dev_ = nullptr;
+    uint32_t decode_grid_ = 0;
+    uint32_t barrier_count_ = 0;
     uint64_t scratch_bytes_ = 0;
     MoeScratch S_;
     void* io_ = nullptr;

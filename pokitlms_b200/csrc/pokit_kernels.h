@@ -68,6 +68,11 @@ uint64_t moe_scratch_bytes(const MoeLayerDev& L);
 // Carves `base` (256-byte aligned, moe_scratch_bytes(L) long) into a MoeScratch.
 MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base);
 
+// Validates the block's shapes and raises the kernels' shared-memory limits
+// without launching anything; call once per configuration before capturing
+// launch_moe_block into a CUDA graph.
+cudaError_t prepare_moe_block(const MoeLayerDev& L);
+
 // One MoE block: routes `x_in` (already normalised) or, when `hidden` is
 // non-null, rms_norm(hidden, ffn_norm); writes the routed (+ shared) MoE
 // output to `moe_out`, or adds it into `hidden` when moe_out is null.
@@ -75,5 +80,20 @@ MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base);
 cudaError_t launch_moe_block(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
                              float* hidden, float* moe_out, const float* next_router,
                              cudaStream_t stream);
+
+// Grid-wide barriers one layer of launch_moe_decode performs.
+uint32_t moe_barriers_per_layer();
+
+// CTAs of the persistent decode kernel for this shape (all co-resident), or 0
+// if the shape cannot run it.
+uint32_t moe_decode_grid(const MoeLayerDev& shape);
+
+// One token through layers [first, first + count) of the device array
+// `layers_dev` in a single cooperative launch: hidden += MoE_l(rms_norm(hidden)).
+// `barrier_base` is the value of S.counter when the launch starts; the launch
+// adds count * moe_barriers_per_layer() * grid to it.
+cudaError_t launch_moe_decode(const MoeLayerDev* layers_dev, const MoeLayerDev& shape,
+                              uint32_t first, uint32_t count, const MoeScratch& S, float* hidden,
+                              uint32_t barrier_base, uint32_t grid, cudaStream_t stream);
 
 }  // namespace pokit
