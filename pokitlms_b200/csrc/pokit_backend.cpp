@@ -135,12 +135,13 @@ public:
         check(cudaMalloc(&devs_dev_, sizeof(MoeLayerDev) * c.layers), "cudaMalloc(layer table)");
         check(cudaMemcpy(devs_dev_, devs_.data(), sizeof(MoeLayerDev) * c.layers,
                          cudaMemcpyHostToDevice), "upload layer table");
-        // The decode chain runs as one persistent cooperative kernel per token
-        // when every CTA fits on the device at once; otherwise as a CUDA graph
-        // of per-block kernels.  POKIT_CUDA_DECODE=graph selects the latter.
+        // The decode chain runs as a CUDA graph of per-block kernels (a graph
+        // kernel boundary costs ~0.6 us on B200, a 148-CTA software grid
+        // barrier ~1.3 us).  POKIT_CUDA_DECODE=persistent selects the single
+        // cooperative kernel with three grid barriers per layer instead.
         const char* mode = std::getenv("POKIT_CUDA_DECODE");
-        const bool want_graph = mode && std::string(mode) == "graph";
-        decode_grid_ = want_graph ? 0u : moe_decode_grid(devs_[0]);
+        const bool want_persistent = mode && std::string(mode) == "persistent";
+        decode_grid_ = want_persistent ? moe_decode_grid(devs_[0]) : 0u;
         check(cudaMalloc(&io_, align256(c.hidden * 4) * 2), "cudaMalloc(io)");
         check(cudaMallocHost(&pinned_, align256(c.hidden * 4) * 2 + 4096), "cudaMallocHost");
     }
