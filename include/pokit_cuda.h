@@ -286,6 +286,58 @@ pokit_cuda_status pokit_cuda_moe_get_stats(const pokit_cuda_moe* moe,
  * tensor does not exist in this configuration). */
 size_t pokit_cuda_moe_tensor_bytes(const pokit_cuda_moe* moe, size_t layer, uint32_t tensor);
 
+/* ------------------------------------------------------------------------ */
+/* One MoE block without any device allocation                              */
+/* ------------------------------------------------------------------------ */
+
+/* Size of the scratch array compiled into the library for
+ * pokit_cuda_moe_forward_static_scratch (router partials, routes,
+ * activations of one block). */
+#define POKIT_CUDA_STATIC_SCRATCH_BYTES (256u * 1024u)
+
+/* One MoE block's tensors in device memory the caller owns (GGUF layouts as
+ * for pokit_cuda_moe_upload_tensor; shared_* only for the Qwen3.5 flavour). */
+typedef struct pokit_cuda_moe_block_device {
+    size_t hidden, inter, experts, top_k;
+    uint32_t flavour;                 /* pokit_cuda_moe_flavour */
+    int normalize_top_k;
+    float expert_weights_scale;
+    const float* router;              /* F32 [experts, hidden] */
+    uint32_t gate_type, up_type, down_type;
+    const void* gate;                 /* [hidden, inter, experts] */
+    const void* up;
+    const void* down;                 /* [inter, hidden, experts] */
+    size_t shared_inter;              /* 0 = no shared expert */
+    const float* shared_router;
+    uint32_t shared_gate_type, shared_up_type, shared_down_type;
+    const void* shared_gate;
+    const void* shared_up;
+    const void* shared_down;
+} pokit_cuda_moe_block_device;
+
+/* No counterpart in the reference.  The same MoE block as
+ * pokit_cuda_moe_forward (same kernels, same results), for callers that cannot
+ * allocate device memory: a host that hands all of the GPU's memory to its own
+ * pool leaves nothing for cudaMalloc, and a latency-critical thread may not
+ * make a call that can synchronise the device.  No handle is needed and
+ * nothing is allocated: the caller passes the block's tensors, the input and
+ * the outputs as device pointers it owns, and the block's scratch is a fixed
+ * POKIT_CUDA_STATIC_SCRATCH_BYTES array compiled into the library, which every
+ * GPU that loads the library holds until the process exits.  A block whose
+ * scratch would not fit is rejected with INVALID_ARGUMENT before any GPU work.
+ * The first call on a device looks up that device's copy of the array
+ * (cudaGetSymbolAddress, with the device current); make that first call
+ * before any stream capture.  Every call shares the array and it keeps the
+ * previous call's contents (the status word is cleared at the start of each
+ * call); calls whose work overlaps on the GPU race on it.  Runs on `stream`
+ * (a cudaStream_t; NULL = the legacy default stream) and waits for it; returns
+ * RUNTIME_ERROR when the router produced non-finite logits, as the reference
+ * throws.  route_ids/route_weights (device, top_k entries) may be NULL. */
+pokit_cuda_status pokit_cuda_moe_forward_static_scratch(
+    const pokit_cuda_moe_block_device* block, const float* input, float* output,
+    uint32_t* route_ids, float* route_weights, void* stream, char* error_buffer,
+    size_t error_capacity);
+
 #ifdef __cplusplus
 }
 #endif

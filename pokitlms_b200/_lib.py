@@ -92,6 +92,22 @@ class LinearStats(C.Structure):
         "model_cache_capacity_bytes", "model_cache_uploaded_bytes", "model_cache_upload_time_ns")]
 
 
+class MoeBlockDevice(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_size_t), ("inter", C.c_size_t), ("experts", C.c_size_t),
+        ("top_k", C.c_size_t), ("flavour", C.c_uint32), ("normalize_top_k", C.c_int),
+        ("expert_weights_scale", C.c_float), ("router", C.c_void_p),
+        ("gate_type", C.c_uint32), ("up_type", C.c_uint32), ("down_type", C.c_uint32),
+        ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+        ("shared_inter", C.c_size_t), ("shared_router", C.c_void_p),
+        ("shared_gate_type", C.c_uint32), ("shared_up_type", C.c_uint32),
+        ("shared_down_type", C.c_uint32), ("shared_gate", C.c_void_p),
+        ("shared_up", C.c_void_p), ("shared_down", C.c_void_p),
+    ]
+
+
+STATIC_SCRATCH_BYTES = 256 * 1024
+
 _ERR = C.c_char_p
 _SZ = C.c_size_t
 _VP = C.c_void_p
@@ -125,6 +141,8 @@ SIGNATURES = {
     "pokit_cuda_moe_synchronize": (C.c_int, [_VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_get_stats": (C.c_int, [_VP, C.POINTER(MoeStats)]),
     "pokit_cuda_moe_tensor_bytes": (C.c_size_t, [_VP, _SZ, C.c_uint32]),
+    "pokit_cuda_moe_forward_static_scratch": (C.c_int, [C.POINTER(MoeBlockDevice), _VP, _VP, _VP,
+                                                        _VP, _VP, _ERR, _SZ]),
 }
 
 _lib = None
