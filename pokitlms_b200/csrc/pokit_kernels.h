@@ -59,6 +59,10 @@ struct MoeScratch {
     uint32_t* ids = nullptr;       // [top_k]
     float* weights = nullptr;      // [top_k + 1] combine weights (last = shared gate)
     float* act = nullptr;          // [(top_k + 1) * max(inter, shared_inter)]
+    float* act2 = nullptr;         // [(top_k + 1) * max(inter, shared_inter)] (up outputs)
+    uint32_t* xfrag = nullptr;     // tensor-core fragments of x, one record per superblock
+    uint32_t* afrag = nullptr;     // fragments of silu(gate) * up, per slot and superblock
+    uint32_t* sbcnt = nullptr;     // gate/up tiles finished per (slot, superblock); returns to 0
     uint32_t* counter = nullptr;   // last-block hand-off counter (must start at 0)
     uint32_t* status = nullptr;    // sticky StatusBits
 };

@@ -24,6 +24,7 @@
 // ld.global.cg so a stale L1 line can never be observed.  Weights are read-only
 // for the kernel's lifetime and use the non-coherent path.
 #include "pokit_kernels.h"
+#include "pokit_mma.cuh"
 #include "pokit_quant.cuh"
 
 #include <algorithm>
@@ -238,6 +239,32 @@ __device__ __forceinline__ void copy_coherent(const float* __restrict__ src, flo
         for (int j = 0; j < kMaxPerThread; ++j) {
             const uint32_t i = base + threadIdx.x + j * kThreads;
             if (i < n) dst[i] = v[j];
+        }
+    }
+}
+
+// The tensor-core path (gate_up_mma / down_mma) serves blocks whose expert
+// matrices are all Q4_K, without a shared expert, with at most one slot per
+// warp and whole superblocks of the intermediate.
+__host__ __device__ inline bool mma_path_ok(const MoeLayerDev& L) {
+    return L.gate_type == kQ4_K && L.up_type == kQ4_K && L.down_type == kQ4_K && L.shared_inter == 0 &&
+           L.top_k <= static_cast<uint32_t>(kWarps) && (L.inter % 256u) == 0;
+}
+
+// Same as copy_coherent for 16-byte aligned buffers of n4 uint4 elements.
+__device__ __forceinline__ void copy_coherent4(const uint4* __restrict__ src, uint4* dst, uint32_t n4) {
+    constexpr int kPer = 6;
+    for (uint32_t base = 0; base < n4; base += kThreads * kPer) {
+        uint4 v[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const uint32_t i = base + threadIdx.x + j * kThreads;
+            v[j] = i < n4 ? __ldcg(src + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const uint32_t i = base + threadIdx.x + j * kThreads;
+            if (i < n4) dst[i] = v[j];
         }
     }
 }
@@ -794,6 +821,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_route_kernel(BlockArgs a) {
     phase_input(a.L, a.hidden, a.x_in, s);
     if (blockIdx.x == 0)
         for (uint32_t i = threadIdx.x; i < a.L.hidden; i += kThreads) a.S.x[i] = s.xs[i];
+    // Tensor-core fragments of x: superblock sb is built by warp 0 of CTA sb mod grid.
+    if ((threadIdx.x >> 5) == 0 && mma_path_ok(a.L))
+        for (uint32_t sb = blockIdx.x; sb < (a.L.hidden >> 8); sb += gridDim.x)
+            q4k_frag_superblock(s.xs + sb * 256u, a.S.xfrag + sb * kFragWords, threadIdx.x & 31);
     router_finish(a.L, gw, nw, rr, s, a.S.partial);
 }
 
@@ -899,6 +930,271 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(DecodeArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-core path: every routed matrix Q4_K, no shared expert.
+//
+// gate_up: CTA b of n owns tiles [b*T/n, (b+1)*T/n) of the T = k * 2 * (I/16)
+// (slot, gate|up, 16-row) tiles, at most kMmaTilesPerCta of them.  Tile p is
+// computed by warps 2p and 2p+1, one half of the superblocks each; each warp
+// TMA-copies its half of the 16 rows into padded shared memory as soon as the
+// routes are known, so the copies overlap the activation preparation.
+// down: CTA b owns output rows [16b, 16b+16); warp w < k computes slot w's
+// 16 rows (TMA-copied, L2-resident after gate_up's prefetch), then the rows
+// are combined in route order and added to the residual.
+// ---------------------------------------------------------------------------
+constexpr int kMmaTilesPerCta = kWarps / 2;
+
+struct MmaLayout {
+    uint32_t bars, recs, lg, red, sel_id, sel_w, pbuf, tmp, part, flags, tiles;
+    uint32_t total, nsb, stride;
+};
+
+__host__ __device__ inline MmaLayout mma_gate_up_layout(const MoeLayerDev& L) {
+    MmaLayout m{};
+    const uint32_t H = L.hidden, nsb = H >> 8;
+    m.nsb = nsb;
+    m.stride = q4k_tile_stride(nsb * 144u);
+    uint32_t off = 0;
+    m.bars = off; off += 128;
+    m.recs = off; off += al16(nsb * kFragWords * 4u);
+    m.lg = off; off += al16(L.experts * 4u);
+    m.red = off; off += al16(64u * 8u);
+    m.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
+    m.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
+    m.pbuf = off; off += al16((L.experts + 1u) * route_splits(H) * 4u);
+    m.tmp = off; off += al16(256u * 4u);
+    m.part = off; off += al16(kWarps * 16u * 4u);
+    m.flags = off; off += al16(kMmaTilesPerCta * 4u + 4u);
+    off = (off + 127u) & ~127u;
+    m.tiles = off; off += kMmaTilesPerCta * 16u * m.stride;
+    m.total = off;
+    return m;
+}
+
+__host__ __device__ inline MmaLayout mma_down_layout(const MoeLayerDev& L) {
+    MmaLayout m{};
+    const uint32_t I = L.inter, nsb = I >> 8, k = L.top_k;
+    m.nsb = nsb;
+    m.stride = q4k_tile_stride(nsb * 144u);
+    uint32_t off = 0;
+    m.bars = off; off += 128;
+    m.recs = off; off += al16(k * nsb * kFragWords * 4u);
+    m.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
+    m.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
+    m.part = off; off += al16(k * 16u * 4u);
+    off = (off + 127u) & ~127u;
+    m.tiles = off; off += k * 16u * m.stride;
+    m.total = off;
+    return m;
+}
+
+struct MmaArgs {
+    MoeLayerDev L;
+    MoeScratch S;
+    float* hidden;
+    float* moe_out;
+    const float* next_router;
+    MmaLayout m;
+    uint32_t down_ctas;   // CTAs of the down kernel (gate_up prefetches their rows)
+};
+
+__device__ __forceinline__ void gate_up_tile_coords(uint32_t tile, uint32_t tiles_per_mat, uint32_t& slot,
+                                                    uint32_t& mat, uint32_t& row0) {
+    slot = tile / (2u * tiles_per_mat);
+    const uint32_t rem = tile % (2u * tiles_per_mat);
+    mat = rem / tiles_per_mat;
+    row0 = (rem % tiles_per_mat) * 16u;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(MmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const MoeLayerDev& L = a.L;
+    const MmaLayout& m = a.m;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + m.bars);
+    uint32_t* recs = reinterpret_cast<uint32_t*>(smem + m.recs);
+    float* tmp = reinterpret_cast<float*>(smem + m.tmp);
+    float* part = reinterpret_cast<float*>(smem + m.part);
+    uint32_t* flags = reinterpret_cast<uint32_t*>(smem + m.flags);
+    uint8_t* tiles = smem + m.tiles;
+    Shared s{};
+    s.lg = reinterpret_cast<float*>(smem + m.lg);
+    s.red = reinterpret_cast<double*>(smem + m.red);
+    s.sel_id = reinterpret_cast<uint32_t*>(smem + m.sel_id);
+    s.sel_w = reinterpret_cast<float*>(smem + m.sel_w);
+    s.act_plain = reinterpret_cast<float*>(smem + m.pbuf);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int i = 0; i < kWarps; ++i) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+    }
+    // R2: the routes, from the router partials (every CTA; CTA 0 publishes them).
+    phase_route(L, a.S.partial, s, a.S.status, blockIdx.x == 0, a.S);
+
+    const uint32_t I = L.inter, nsb = m.nsb, nsbI = I >> 8;
+    const uint32_t row_bytes_g = nsb * 144u;
+    const uint32_t tiles_per_mat = I / 16u;
+    const uint32_t T = L.top_k * 2u * tiles_per_mat;
+    const uint32_t t0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * T / gridDim.x);
+    const uint32_t t1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * T / gridDim.x);
+    const uint32_t p = warp >> 1, half = warp & 1;
+    const uint32_t sb_split = nsb / 2;
+    const uint32_t sb0 = half ? sb_split : 0u, sb1 = half ? nsb : sb_split;
+    const uint32_t tile = t0 + p;
+    const bool has_tile = p < static_cast<uint32_t>(kMmaTilesPerCta) && tile < t1 && sb1 > sb0;
+    uint8_t* mytile = tiles + p * 16u * m.stride;
+    if (has_tile && lane == 0) {
+        uint32_t slot, mat, row0;
+        gate_up_tile_coords(tile, tiles_per_mat, slot, mat, row0);
+        const uint64_t id = s.sel_id[slot];
+        const uint8_t* base = (mat ? L.up + id * L.up_slice : L.gate + id * L.gate_slice) +
+                              static_cast<uint64_t>(row0) * row_bytes_g + sb0 * 144u;
+        const uint32_t bytes = (sb1 - sb0) * 144u;
+        mbar_expect_tx(&bars[warp], 16u * bytes);
+        for (uint32_t r = 0; r < 16u; ++r)
+            tma_load(mytile + r * m.stride + sb0 * 144u, base + static_cast<uint64_t>(r) * row_bytes_g,
+                     bytes, &bars[warp]);
+    }
+    // Stream this CTA's share of every slot's down rows into L2.
+    if (blockIdx.x < a.down_ctas && tid < static_cast<int>(L.top_k)) {
+        uint32_t r0, r1;
+        down_rows(L.hidden, blockIdx.x, a.down_ctas, r0, r1);
+        if (r1 > r0) {
+            const uint64_t rd = row_bytes(L.down_type, I);
+            prefetch_l2_range(L.down + s.sel_id[tid] * L.down_slice + r0 * rd, (r1 - r0) * rd);
+        }
+    }
+    // x fragments (published by the route kernel).
+    copy_coherent4(reinterpret_cast<const uint4*>(a.S.xfrag), reinterpret_cast<uint4*>(recs),
+                   nsb * kFragWords / 4u);
+    __syncthreads();
+
+    if (has_tile) {
+        float acc0 = 0.0f, acc1 = 0.0f;
+        if (mbar_wait(&bars[warp], 0)) {
+            q4k_mma_tile(mytile + sb0 * 144u, m.stride, static_cast<int>(sb1 - sb0), recs + sb0 * kFragWords,
+                         acc0, acc1);
+        } else if (lane == 0) {
+            atomicOr(a.S.status, kStatusWaitTimeout);
+        }
+        if ((lane & 3) == 0) {
+            part[warp * 16 + (lane >> 2)] = acc0;
+            part[warp * 16 + (lane >> 2) + 8] = acc1;
+        }
+    } else if (lane < 16) {
+        part[warp * 16 + lane] = 0.0f;
+    }
+    __syncthreads();
+    // Rows of every tile: sum of the two halves, to the gate (act) or up (act2) buffer.
+    for (uint32_t i = tid; i < kMmaTilesPerCta * 16u; i += kThreads) {
+        const uint32_t pp = i >> 4, r = i & 15u, tt = t0 + pp;
+        if (tt >= t1) continue;
+        uint32_t sl, mt, rw;
+        gate_up_tile_coords(tt, tiles_per_mat, sl, mt, rw);
+        const float v = part[(2 * pp) * 16 + r] + part[(2 * pp + 1) * 16 + r];
+        (mt ? a.S.act2 : a.S.act)[sl * I + rw + r] = v;
+    }
+    __syncthreads();
+    // Count finished tiles per (slot, superblock of the intermediate); the CTA
+    // that completes a superblock (16 gate + 16 up tiles) builds its activation
+    // fragments.  No CTA waits for another.
+    if (tid < kMmaTilesPerCta) {
+        uint32_t done = 0xffffffffu;
+        const uint32_t tt = t0 + tid;
+        if (tt < t1) {
+            uint32_t sl, mt, rw;
+            gate_up_tile_coords(tt, tiles_per_mat, sl, mt, rw);
+            const uint32_t key = sl * nsbI + (rw >> 8);
+            __threadfence();
+            if (atomicAdd(&a.S.sbcnt[key], 1u) == 31u) done = key;
+            __threadfence();
+        }
+        flags[tid] = done;
+    }
+    __syncthreads();
+    for (int f = 0; f < kMmaTilesPerCta; ++f) {
+        const uint32_t key = flags[f];
+        if (key == 0xffffffffu) continue;
+        __threadfence();
+        const uint32_t sl = key / nsbI, sb = key % nsbI;
+        for (uint32_t i = tid; i < 256u; i += kThreads) {
+            const uint32_t idx = sl * I + sb * 256u + i;
+            tmp[i] = silu_mul(__ldcg(a.S.act + idx), __ldcg(a.S.act2 + idx), L.flavour);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            q4k_frag_superblock(tmp, a.S.afrag + key * kFragWords, lane);
+            if (lane == 0) a.S.sbcnt[key] = 0u;
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(MmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const MoeLayerDev& L = a.L;
+    const MmaLayout& m = a.m;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + m.bars);
+    uint32_t* recs = reinterpret_cast<uint32_t*>(smem + m.recs);
+    uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + m.sel_id);
+    float* sel_w = reinterpret_cast<float*>(smem + m.sel_w);
+    float* part = reinterpret_cast<float*>(smem + m.part);
+    uint8_t* tiles = smem + m.tiles;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t k = L.top_k, nsb = m.nsb, H = L.hidden;
+    const uint32_t j0 = blockIdx.x * 16u;
+
+    if (tid == 0) {
+        for (int i = 0; i < kWarps; ++i) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+    }
+    for (uint32_t r = tid; r < k; r += kThreads) {
+        sel_id[r] = __ldcg(a.S.ids + r);
+        sel_w[r] = __ldcg(a.S.weights + r);
+    }
+    __syncthreads();
+    const uint32_t rbd = nsb * 144u;
+    if (static_cast<uint32_t>(warp) < k && lane == 0) {
+        const uint8_t* base = L.down + static_cast<uint64_t>(sel_id[warp]) * L.down_slice +
+                              static_cast<uint64_t>(j0) * rbd;
+        mbar_expect_tx(&bars[warp], 16u * rbd);
+        for (uint32_t r = 0; r < 16u; ++r)
+            tma_load(tiles + (warp * 16u + r) * m.stride, base + static_cast<uint64_t>(r) * rbd, rbd,
+                     &bars[warp]);
+    }
+    if (a.next_router && tid == 0) {
+        const uint64_t bytes = static_cast<uint64_t>(L.experts) * H * 4u;
+        const uint64_t lo = (bytes * blockIdx.x / gridDim.x) & ~uint64_t(15);
+        const uint64_t hi = blockIdx.x + 1 == gridDim.x ? bytes : (bytes * (blockIdx.x + 1) / gridDim.x) & ~uint64_t(15);
+        if (hi > lo) prefetch_l2_range(reinterpret_cast<const uint8_t*>(a.next_router) + lo, hi - lo);
+    }
+    // Activation fragments of every slot (built by the gate/up kernel).
+    copy_coherent4(reinterpret_cast<const uint4*>(a.S.afrag), reinterpret_cast<uint4*>(recs),
+                   k * nsb * kFragWords / 4u);
+    __syncthreads();
+    if (static_cast<uint32_t>(warp) < k) {
+        float acc0 = 0.0f, acc1 = 0.0f;
+        if (mbar_wait(&bars[warp], 0)) {
+            q4k_mma_tile(tiles + warp * 16u * m.stride, m.stride, static_cast<int>(nsb),
+                         recs + warp * nsb * kFragWords, acc0, acc1);
+        } else if (lane == 0) {
+            atomicOr(a.S.status, kStatusWaitTimeout);
+        }
+        if ((lane & 3) == 0) {
+            part[warp * 16 + (lane >> 2)] = acc0;
+            part[warp * 16 + (lane >> 2) + 8] = acc1;
+        }
+    }
+    __syncthreads();
+    if (tid < 16) {
+        float acc = 0.0f;
+        for (uint32_t sl = 0; sl < k; ++sl) acc += sel_w[sl] * part[sl * 16 + tid];
+        const uint32_t row = j0 + tid;
+        if (a.moe_out) a.moe_out[row] = acc;
+        else a.hidden[row] = __ldcg(a.hidden + row) + acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
 template <typename K>
 cudaError_t ensure_smem(K kernel, size_t bytes, size_t& granted) {
     if (bytes <= 48u * 1024u || bytes <= granted) return cudaSuccess;
@@ -909,6 +1205,7 @@ cudaError_t ensure_smem(K kernel, size_t bytes, size_t& granted) {
 }
 
 size_t g_route_smem = 0, g_gate_up_smem = 0, g_down_smem = 0, g_decode_smem = 0;
+size_t g_gate_up_mma_smem = 0, g_down_mma_smem = 0;
 
 uint64_t align256(uint64_t v) { return (v + 255u) & ~uint64_t(255); }
 
@@ -933,6 +1230,10 @@ uint64_t moe_scratch_bytes(const MoeLayerDev& L) {
     b += align256(L.top_k * 4u);                                          // ids
     b += align256(slots * 4u);                                            // weights
     b += align256(slots * max_inter_of(L) * 4u);                          // act
+    b += align256(slots * max_inter_of(L) * 4u);                          // act2
+    b += align256((L.hidden >> 8) * kFragWords * 4u);                     // xfrag
+    b += align256(slots * ((max_inter_of(L) + 255u) >> 8) * kFragWords * 4u);  // afrag
+    b += align256(slots * ((max_inter_of(L) + 255u) >> 8) * 4u);         // sbcnt
     b += align256(4u);                                                    // counter
     b += align256(4u);                                                    // status
     return b;
@@ -948,6 +1249,11 @@ MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base) {
     s.ids = reinterpret_cast<uint32_t*>(p); p += align256(L.top_k * 4u);
     s.weights = reinterpret_cast<float*>(p); p += align256(slots * 4u);
     s.act = reinterpret_cast<float*>(p); p += align256(slots * max_inter_of(L) * 4u);
+    s.act2 = reinterpret_cast<float*>(p); p += align256(slots * max_inter_of(L) * 4u);
+    s.xfrag = reinterpret_cast<uint32_t*>(p); p += align256((L.hidden >> 8) * kFragWords * 4u);
+    s.afrag = reinterpret_cast<uint32_t*>(p);
+    p += align256(slots * ((max_inter_of(L) + 255u) >> 8) * kFragWords * 4u);
+    s.sbcnt = reinterpret_cast<uint32_t*>(p); p += align256(slots * ((max_inter_of(L) + 255u) >> 8) * 4u);
     s.counter = reinterpret_cast<uint32_t*>(p); p += align256(4u);
     s.status = reinterpret_cast<uint32_t*>(p);
     return s;
@@ -986,7 +1292,32 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
     cudaError_t e = ensure_smem(moe_route_kernel, a.m.total, g_route_smem);
     if (e == cudaSuccess) e = ensure_smem(moe_gate_up_kernel, a.m.total, g_gate_up_smem);
     if (e == cudaSuccess) e = ensure_smem(moe_down_kernel, a.m.total, g_down_smem);
-    if (e != cudaSuccess || dry_run) return e;
+    if (e != cudaSuccess) return e;
+    if (mma_path_ok(L)) {
+        MmaArgs ma{};
+        ma.L = L;
+        ma.S = S;
+        ma.hidden = hidden;
+        ma.moe_out = moe_out;
+        ma.next_router = next_router;
+        const MmaLayout gl = mma_gate_up_layout(L), dl = mma_down_layout(L);
+        if (gl.total > 227u * 1024u || dl.total > 227u * 1024u) return cudaErrorInvalidValue;
+        e = ensure_smem(moe_gate_up_mma_kernel, gl.total, g_gate_up_mma_smem);
+        if (e == cudaSuccess) e = ensure_smem(moe_down_mma_kernel, dl.total, g_down_mma_smem);
+        if (e != cudaSuccess || dry_run) return e;
+        const uint32_t T = L.top_k * 2u * (L.inter / 16u);
+        const uint32_t g2 = std::max<uint32_t>(static_cast<uint32_t>(sms),
+                                               (T + kMmaTilesPerCta - 1) / kMmaTilesPerCta);
+        const uint32_t g3 = L.hidden / 16u;
+        ma.down_ctas = g3;
+        moe_route_kernel<<<g1, kThreads, a.m.total, stream>>>(a);
+        ma.m = gl;
+        moe_gate_up_mma_kernel<<<g2, kThreads, gl.total, stream>>>(ma);
+        ma.m = dl;
+        moe_down_mma_kernel<<<g3, kThreads, dl.total, stream>>>(ma);
+        return cudaGetLastError();
+    }
+    if (dry_run) return cudaSuccess;
     moe_route_kernel<<<g1, kThreads, a.m.total, stream>>>(a);
     moe_gate_up_kernel<<<sms, kThreads, a.m.total, stream>>>(a);
     moe_down_kernel<<<down_ctas, kThreads, a.m.total, stream>>>(a);
