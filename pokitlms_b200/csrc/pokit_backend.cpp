@@ -147,7 +147,7 @@ public:
     }
 
     ~MoeBackend() {
-        for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+        for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second.first);
         if (pinned_) cudaFreeHost(pinned_);
         if (io_) cudaFree(io_);
         if (scratch_) cudaFree(scratch_);
@@ -242,13 +242,13 @@ public:
         if (!x || !out) throw std::invalid_argument("input and output are required");
         DeviceScope scope(device_);
         cudaStream_t st = s ? s : stream_;
-        const float* next = layer + 1 < cfg_.layers ? devs_[layer + 1].router : nullptr;
-        guard(launch_moe_block(devs_[layer], S_, x, nullptr, out, next, st), "moe block");
+        uint32_t n = 0;
+        guard(launch_moe_block(devs_[layer], S_, x, nullptr, out, nullptr, nullptr, st, &n), "moe block");
+        kernel_launches_ += n;
         if (ids) guard(cudaMemcpyAsync(ids, S_.ids, cfg_.top_k * 4, cudaMemcpyDeviceToDevice, st), "ids");
         if (w) guard(cudaMemcpyAsync(w, S_.weights, cfg_.top_k * 4, cudaMemcpyDeviceToDevice, st), "weights");
         forward_calls_ += 1;
         hits_ += cfg_.top_k;
-        kernel_launches_ += 3;
     }
 
     void forward_host(size_t layer, const float* x, float* out, uint32_t* ids, float* w) {
@@ -295,9 +295,13 @@ public:
             cudaGraph_t graph = nullptr;
             guard(cudaStreamBeginCapture(capture_stream_, cudaStreamCaptureModeThreadLocal), "capture");
             cudaError_t e = cudaSuccess;
+            uint32_t launches = 0;
             for (size_t l = first; l < first + count && e == cudaSuccess; ++l) {
-                const float* next = l + 1 < first + count ? devs_[l + 1].router : nullptr;
-                e = launch_moe_block(devs_[l], S_, nullptr, hidden, nullptr, next, capture_stream_);
+                const MoeLayerDev* prev = l > first ? &devs_[l - 1] : nullptr;
+                const MoeLayerDev* next = l + 1 < first + count ? &devs_[l + 1] : nullptr;
+                uint32_t n = 0;
+                e = launch_moe_block(devs_[l], S_, nullptr, hidden, nullptr, prev, next, capture_stream_, &n);
+                launches += n;
             }
             const cudaError_t end = cudaStreamEndCapture(capture_stream_, &graph);
             if (e != cudaSuccess) { if (graph) cudaGraphDestroy(graph); guard(e, "capture launch"); }
@@ -306,12 +310,12 @@ public:
             const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
             guard(inst, "instantiate");
-            it = graphs_.emplace(key, exec).first;
+            it = graphs_.emplace(key, std::make_pair(exec, launches)).first;
         }
-        guard(cudaGraphLaunch(it->second, st), "graph launch");
+        guard(cudaGraphLaunch(it->second.first, st), "graph launch");
         forward_calls_ += count;
         hits_ += count * cfg_.top_k;
-        kernel_launches_ += 3 * count;
+        kernel_launches_ += it->second.second;
     }
 
     void decode_layers_host(size_t first, size_t count, const float* in, float* out) {
@@ -442,7 +446,8 @@ private:
     void* pinned_ = nullptr;
     cudaStream_t stream_ = nullptr;
     cudaStream_t capture_stream_ = nullptr;
-    std::map<std::tuple<size_t, size_t, float*>, cudaGraphExec_t> graphs_;
+    // (first, count, hidden) -> (graph, kernels it launches)
+    std::map<std::tuple<size_t, size_t, float*>, std::pair<cudaGraphExec_t, uint32_t>> graphs_;
     std::vector<uint32_t> resident_;   // per layer: bit t = tensor t written
     std::mutex mutex_;
     bool failed_ = false;

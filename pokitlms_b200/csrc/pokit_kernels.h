@@ -59,10 +59,17 @@ struct MoeScratch {
     uint32_t* ids = nullptr;       // [top_k]
     float* weights = nullptr;      // [top_k + 1] combine weights (last = shared gate)
     float* act = nullptr;          // [(top_k + 1) * max(inter, shared_inter)]
-    float* act2 = nullptr;         // [(top_k + 1) * max(inter, shared_inter)] (up outputs)
-    uint32_t* xfrag = nullptr;     // tensor-core fragments of x, one record per superblock
-    uint32_t* afrag = nullptr;     // fragments of silu(gate) * up, per slot and superblock
-    uint32_t* sbcnt = nullptr;     // gate/up tiles finished per (slot, superblock); returns to 0
+    // Tensor-core path: router dots summed exactly in carry-save fixed point
+    // [experts][8 limbs],
+    // per-chunk sums of squares [hidden / 16], the out-of-range flag, x'
+    // fragment records, the rms scale and the routing-tail counter (racc, rbad
+    // and route_count are zero between launches).
+    unsigned long long* racc = nullptr;
+    float* rsq = nullptr;
+    uint32_t* rbad = nullptr;
+    uint32_t* xrec = nullptr;
+    float* scale = nullptr;
+    uint32_t* route_count = nullptr;
     uint32_t* counter = nullptr;   // last-block hand-off counter (must start at 0)
     uint32_t* status = nullptr;    // sticky StatusBits
 };
@@ -80,10 +87,13 @@ cudaError_t prepare_moe_block(const MoeLayerDev& L);
 // One MoE block: routes `x_in` (already normalised) or, when `hidden` is
 // non-null, rms_norm(hidden, ffn_norm); writes the routed (+ shared) MoE
 // output to `moe_out`, or adds it into `hidden` when moe_out is null.
-// `next_router` (may be null) is prefetched into L2 for the following layer.
+// In a decode chain `prev` and `next` (may be null) are the neighbouring
+// blocks: a block may take its router partials from `prev`'s last kernel and
+// produce `next`'s (or warm L2 with `next`'s router).  `launches` (may be
+// null) receives the number of kernels launched.
 cudaError_t launch_moe_block(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
-                             float* hidden, float* moe_out, const float* next_router,
-                             cudaStream_t stream);
+                             float* hidden, float* moe_out, const MoeLayerDev* prev,
+                             const MoeLayerDev* next, cudaStream_t stream, uint32_t* launches);
 
 // Grid-wide barriers one layer of launch_moe_decode performs.
 uint32_t moe_barriers_per_layer();

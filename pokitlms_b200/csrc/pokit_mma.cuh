@@ -29,6 +29,8 @@
 // chunk, k = 2t, 2t+1, 2t+8, 2t+9  <->  bytes 8t+4s + {0, 2, 1, 3}.
 #pragma once
 
+#include <cuda.h>   // CUtensorMap
+
 #include "pokit_common.cuh"
 
 namespace pokit {
@@ -64,7 +66,7 @@ __device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uin
 }
 
 // ---------------------------------------------------------------------------
-// TMA bulk copies with an mbarrier; every wait is bounded.
+// TMA tensor copies with an mbarrier; every wait is bounded.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -92,23 +94,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, uint32_t
     }
     return ok != 0;
 }
-// Global -> shared bulk copy (16-byte aligned addresses, size a multiple of 16).
-__device__ __forceinline__ void tma_load(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+// One box of a 3-D tensor map (x = byte column, y = row, z = expert) into
+// shared memory, completing on `bar`.  x must be a multiple of 16.
+__device__ __forceinline__ void tma_box_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
             smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(m))
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
-
-// Shared-memory row stride for a tile of Q4_K rows: row bytes + padding so
-// that stride % 128 is 32 or 96 -- the 16 lanes of a half-warp then read 8
-// bytes each from distinct banks (lane (g, t) at g*stride + 8t + const).
-__host__ __device__ constexpr uint32_t q4k_tile_stride(uint32_t row_bytes) {
-    uint32_t s = row_bytes;
-    while ((s % 128u) != 32u && (s % 128u) != 96u) s += 16u;
-    return s;
+// 16-byte asynchronous global -> shared copy through L2 (no L1 allocation);
+// completion by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// A superblock box: 16 rows x 144 bytes, rows 144 bytes apart in shared
+// memory.  With that pitch the (row g, lane t) 8-byte reads of a fragment
+// fall on distinct bank pairs two lanes at a time: two wavefronts, the
+// minimum for 256 bytes.
+constexpr uint32_t kBoxRows = 16, kBoxBytes = 16u * 144u;
 
 // ---------------------------------------------------------------------------
 // Activation fragments.  One record of kFragWords 32-bit words per superblock
@@ -128,16 +135,34 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 }
 __device__ __forceinline__ float half_round(float a) { return __half2float(__float2half_rn(a)); }
 
-// One warp builds the record of one superblock from v[0..256) (any memory
-// space the warp can read).  rec may be global or shared memory.
-__device__ __forceinline__ void q4k_frag_superblock(const float* __restrict__ v, uint32_t* __restrict__ rec,
-                                                    int lane) {
+// One warp builds the record of one superblock from v[0..256).  Every input
+// is read into registers before the first write, so v may alias rec (the
+// values staged in the record's own space) and be in global or shared memory;
+// v and rec are 16-byte aligned.
+// The eight 32-element group sums come from one reduce-scatter (lane L ends
+// with the sum of group (L >> 2) & 7) instead of eight warp reductions.
+__device__ __forceinline__ void q4k_frag_superblock(const float* v, uint32_t* rec, int lane) {
     float x[8];
     float m = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         x[j] = v[32 * j + lane];
         m = fmaxf(m, fabsf(x[j]));
+    }
+    // B-fragment items (j, s, t) = lane and lane + 32: elements
+    // 32j + 8t + 4s + {0, 2, 1, 3} (chunk c = j/2, nibble half j%2).
+    // Item (j, s, t) = lane + 32h covers elements 4 (8j + 2t + s) + {0, 2, 1, 3}:
+    // one 16-byte read per item (a permutation of the warp's slots).
+    float it[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int item = lane + 32 * h;
+        const int t = item & 3, s = (item >> 2) & 1, j = item >> 3;
+        const float4 q = *reinterpret_cast<const float4*>(v + 4 * (8 * j + 2 * t + s));
+        it[h][0] = q.x;
+        it[h][1] = q.z;
+        it[h][2] = q.y;
+        it[h][3] = q.w;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -150,109 +175,117 @@ __device__ __forceinline__ void q4k_frag_superblock(const float* __restrict__ v,
         e = ex - 10;
     }
     const float inv = ldexpf(1.0f, -e);
-    float gs[8];
+    // Reduce-scatter of the eight group sums of x' (lane bits 4, 3, 2 pick
+    // the group, bits 1, 0 are summed last).
+    const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+    float y[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) gs[j] = warp_sum(x[j] * inv);
-    // B fragments: item (j, s, t) -> bytes 8t + 4s + {0, 2, 1, 3} of chunk c = j/2,
-    // nibble half h = j%2, i.e. elements 64c + 32h + 8t + 4s + {0, 2, 1, 3}.
-    for (int item = lane; item < 64; item += 32) {
-        const int t = item & 3, s = (item >> 2) & 1, j = item >> 3;
-        const int c = j >> 1, h = j & 1;
-        const int base = 64 * c + 32 * h + 8 * t + 4 * s;
-        const float e0 = v[base + 0] * inv, e1 = v[base + 2] * inv;
-        const float e2 = v[base + 1] * inv, e3 = v[base + 3] * inv;
-        uint32_t* dst = rec + ((j * 2 + s) * 8 + t * 2) * 2;
-        dst[0] = pack_half2(e0, e1);
-        dst[1] = pack_half2(e2, e3);
-        dst[2] = pack_half2(e0 - half_round(e0), e1 - half_round(e1));
-        dst[3] = pack_half2(e2 - half_round(e2), e3 - half_round(e3));
+    for (int i = 0; i < 4; ++i) {
+        const float keep = (b4 ? x[4 + i] : x[i]) * inv, send = (b4 ? x[i] : x[4 + i]) * inv;
+        y[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    float z[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float keep = b3 ? y[2 + i] : y[i], send = b3 ? y[i] : y[2 + i];
+        z[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float w = (b2 ? z[1] : z[0]) + __shfl_xor_sync(0xffffffffu, b2 ? z[0] : z[1], 4);
+    w += __shfl_xor_sync(0xffffffffu, w, 2);
+    w += __shfl_xor_sync(0xffffffffu, w, 1);
+    // Lanes 0..7 write min word t*2 + half: groups 2t and 2t+1.
+    const int tq = (lane >> 1) & 3;
+    const float gA = __shfl_sync(0xffffffffu, w, (2 * tq) << 2);
+    const float gB = __shfl_sync(0xffffffffu, w, (2 * tq + 1) << 2);
+    __syncwarp();                                   // all reads of v are done
+    // Item (j, s, t) fills words ((j*2 + s)*8 + t*2)*2 .. +3 = 4 * item: one
+    // 16-byte write per item.
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int item = lane + 32 * h;
+        const float e0 = it[h][0] * inv, e1 = it[h][1] * inv;
+        const float e2 = it[h][2] * inv, e3 = it[h][3] * inv;
+        *reinterpret_cast<uint4*>(rec + 4 * item) =
+            make_uint4(pack_half2(e0, e1), pack_half2(e2, e3), pack_half2(e0 - half_round(e0), e1 - half_round(e1)),
+                       pack_half2(e2 - half_round(e2), e3 - half_round(e3)));
     }
     if (lane < 8) {
-        const int t = lane >> 1, half = lane & 1;
-        const float g0 = -gs[2 * t], g1 = -gs[2 * t + 1];
+        const int half = lane & 1;
+        const float g0 = -gA, g1 = -gB;
         rec[256 + lane] = half == 0 ? pack_half2(g0, g1)
                                     : pack_half2(g0 - half_round(g0), g1 - half_round(g1));
     }
     if (lane == 0) rec[264] = __float_as_uint(ldexpf(1.0f, e));
 }
 
-// 16 rows (rows g and g+8 of the warp's tile, in shared memory with `stride`
-// bytes between rows) dotted with the activation records of nsb superblocks.
-// Returns the FP32 results for rows g (acc0) and g+8 (acc1), valid in lanes
-// with t == 0.
-__device__ __forceinline__ void q4k_mma_tile(const uint8_t* __restrict__ tile, uint32_t stride,
-                                             int nsb, const uint32_t* __restrict__ recs, float& acc0,
-                                             float& acc1) {
+// One superblock of 16 rows (rows g and g+8 at `sb0p` / `sb1p`, 144 bytes
+// each, in shared memory) dotted with the activation record `rec`.  Adds the
+// FP32 results for rows g (acc0) and g+8 (acc1); valid in lanes with t == 0.
+__device__ __forceinline__ void q4k_mma_superblock(const uint8_t* __restrict__ b0p, const uint8_t* __restrict__ b1p,
+                                                   const uint32_t* __restrict__ rec, float& acc0, float& acc1) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const uint8_t* r0 = tile + g * stride;
-    const uint8_t* r1 = tile + (g + 8) * stride;
     const bool bact = g < 2;
-    acc0 = 0.0f;
-    acc1 = 0.0f;
-    for (int sb = 0; sb < nsb; ++sb) {
-        const uint32_t* rec = recs + sb * kFragWords;
-        const uint8_t* b0p = r0 + sb * 144;
-        const uint8_t* b1p = r1 + sb * 144;
-        const uint4 h0 = *reinterpret_cast<const uint4*>(b0p);
-        const uint4 h1 = *reinterpret_cast<const uint4*>(b1p);
-        uint2 q0[4], q1[4];
+    const uint4 h0 = *reinterpret_cast<const uint4*>(b0p);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(b1p);
+    uint2 q0[4], q1[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            q0[c] = *reinterpret_cast<const uint2*>(b0p + 16 + 32 * c + 8 * t);
-            q1[c] = *reinterpret_cast<const uint2*>(b1p + 16 + 32 * c + 8 * t);
-        }
-        // 6-bit scales s0..7 and mins m0..7 as bytes (decode_q4_k's scale_min).
-        const uint32_t sA0 = h0.y & 0x3F3F3F3Fu, sB0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
-        const uint32_t sA1 = h1.y & 0x3F3F3F3Fu, sB1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
-        const uint32_t mA0 = h0.z & 0x3F3F3F3Fu, mB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
-        const uint32_t mA1 = h1.z & 0x3F3F3F3Fu, mB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
-        const uint32_t* xbl = rec + (t * 2 + (g & 1)) * 2;
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint32_t sw0 = c < 2 ? sA0 : sB0, sw1 = c < 2 ? sA1 : sB1;
-            const uint32_t jl = (2 * c) & 3, jh = (2 * c + 1) & 3;
-            const uint32_t Sl0 = hsub2u(__byte_perm(sw0, 0x64u, 0x4040u | (jl << 8) | jl), kHalfMagic);
-            const uint32_t Sl1 = hsub2u(__byte_perm(sw1, 0x64u, 0x4040u | (jl << 8) | jl), kHalfMagic);
-            uint32_t Sh0 = hsub2u(__byte_perm(sw0, 0x64u, 0x4040u | (jh << 8) | jh), kHalfMagic);
-            uint32_t Sh1 = hsub2u(__byte_perm(sw1, 0x64u, 0x4040u | (jh << 8) | jh), kHalfMagic);
-            const uint32_t Cl0 = hmul2u(Sl0, kHalfNeg1024), Cl1 = hmul2u(Sl1, kHalfNeg1024);
-            const uint32_t Ch0 = hmul2u(Sh0, kHalfNeg64), Ch1 = hmul2u(Sh1, kHalfNeg64);
-            Sh0 = hmul2u(Sh0, kHalfInv16);
-            Sh1 = hmul2u(Sh1, kHalfInv16);
-#pragma unroll
-            for (int s = 0; s < 2; ++s) {
-                const uint32_t w0 = s ? q0[c].y : q0[c].x, w1 = s ? q1[c].y : q1[c].x;
-                const uint32_t w08 = w0 >> 8, w18 = w1 >> 8;
-                const uint32_t a0 = hfma2u((w0 & 0x000F000Fu) | kHalfMagic, Sl0, Cl0);
-                const uint32_t a1 = hfma2u((w1 & 0x000F000Fu) | kHalfMagic, Sl1, Cl1);
-                const uint32_t a2 = hfma2u((w08 & 0x000F000Fu) | kHalfMagic, Sl0, Cl0);
-                const uint32_t a3 = hfma2u((w18 & 0x000F000Fu) | kHalfMagic, Sl1, Cl1);
-                const uint2 bl = bact ? *reinterpret_cast<const uint2*>(xbl + ((2 * c) * 2 + s) * 16)
-                                      : make_uint2(0u, 0u);
-                mma16816(d, a0, a1, a2, a3, bl.x, bl.y);
-                const uint32_t e0 = hfma2u((w0 & 0x00F000F0u) | kHalfMagic, Sh0, Ch0);
-                const uint32_t e1 = hfma2u((w1 & 0x00F000F0u) | kHalfMagic, Sh1, Ch1);
-                const uint32_t e2 = hfma2u((w08 & 0x00F000F0u) | kHalfMagic, Sh0, Ch0);
-                const uint32_t e3 = hfma2u((w18 & 0x00F000F0u) | kHalfMagic, Sh1, Ch1);
-                const uint2 bh = bact ? *reinterpret_cast<const uint2*>(xbl + ((2 * c + 1) * 2 + s) * 16)
-                                      : make_uint2(0u, 0u);
-                mma16816(d, e0, e1, e2, e3, bh.x, bh.y);
-            }
-        }
-        const uint32_t mw0 = t < 2 ? mA0 : mB0, mw1 = t < 2 ? mA1 : mB1;
-        const uint32_t ja = (2 * t) & 3;
-        const uint32_t M0 = hsub2u(__byte_perm(mw0, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
-        const uint32_t M1 = hsub2u(__byte_perm(mw1, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
-        const uint32_t bm = bact ? rec[256 + t * 2 + (g & 1)] : 0u;
-        float d2[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816(d2, M0, M1, 0u, 0u, bm, 0u);
-        const float sc = __uint_as_float(rec[264]);
-        const float dd0 = half_bits_to_float(h0.x) * sc, dm0 = half_bits_to_float(h0.x >> 16) * sc;
-        const float dd1 = half_bits_to_float(h1.x) * sc, dm1 = half_bits_to_float(h1.x >> 16) * sc;
-        acc0 = fmaf(dd0, d[0] + d[1], fmaf(dm0, d2[0] + d2[1], acc0));
-        acc1 = fmaf(dd1, d[2] + d[3], fmaf(dm1, d2[2] + d2[3], acc1));
+    for (int c = 0; c < 4; ++c) {
+        q0[c] = *reinterpret_cast<const uint2*>(b0p + 16 + 32 * c + 8 * t);
+        q1[c] = *reinterpret_cast<const uint2*>(b1p + 16 + 32 * c + 8 * t);
     }
+    // 6-bit scales s0..7 and mins m0..7 as bytes (decode_q4_k's scale_min).
+    const uint32_t sA0 = h0.y & 0x3F3F3F3Fu, sB0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+    const uint32_t sA1 = h1.y & 0x3F3F3F3Fu, sB1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+    const uint32_t mA0 = h0.z & 0x3F3F3F3Fu, mB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+    const uint32_t mA1 = h1.z & 0x3F3F3F3Fu, mB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+    const uint32_t* xbl = rec + (t * 2 + (g & 1)) * 2;
+    // Two accumulators (even and odd chunks) halve the dependent mma chain.
+    float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t sw0 = c < 2 ? sA0 : sB0, sw1 = c < 2 ? sA1 : sB1;
+        const uint32_t jl = (2 * c) & 3, jh = (2 * c + 1) & 3;
+        const uint32_t Sl0 = hsub2u(__byte_perm(sw0, 0x64u, 0x4040u | (jl << 8) | jl), kHalfMagic);
+        const uint32_t Sl1 = hsub2u(__byte_perm(sw1, 0x64u, 0x4040u | (jl << 8) | jl), kHalfMagic);
+        uint32_t Sh0 = hsub2u(__byte_perm(sw0, 0x64u, 0x4040u | (jh << 8) | jh), kHalfMagic);
+        uint32_t Sh1 = hsub2u(__byte_perm(sw1, 0x64u, 0x4040u | (jh << 8) | jh), kHalfMagic);
+        const uint32_t Cl0 = hmul2u(Sl0, kHalfNeg1024), Cl1 = hmul2u(Sl1, kHalfNeg1024);
+        const uint32_t Ch0 = hmul2u(Sh0, kHalfNeg64), Ch1 = hmul2u(Sh1, kHalfNeg64);
+        Sh0 = hmul2u(Sh0, kHalfInv16);
+        Sh1 = hmul2u(Sh1, kHalfInv16);
+        float* dc = d[c & 1];
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            const uint32_t w0 = s ? q0[c].y : q0[c].x, w1 = s ? q1[c].y : q1[c].x;
+            const uint32_t w08 = w0 >> 8, w18 = w1 >> 8;
+            const uint32_t a0 = hfma2u((w0 & 0x000F000Fu) | kHalfMagic, Sl0, Cl0);
+            const uint32_t a1 = hfma2u((w1 & 0x000F000Fu) | kHalfMagic, Sl1, Cl1);
+            const uint32_t a2 = hfma2u((w08 & 0x000F000Fu) | kHalfMagic, Sl0, Cl0);
+            const uint32_t a3 = hfma2u((w18 & 0x000F000Fu) | kHalfMagic, Sl1, Cl1);
+            const uint2 bl = bact ? *reinterpret_cast<const uint2*>(xbl + ((2 * c) * 2 + s) * 16)
+                                  : make_uint2(0u, 0u);
+            mma16816(dc, a0, a1, a2, a3, bl.x, bl.y);
+            const uint32_t e0 = hfma2u((w0 & 0x00F000F0u) | kHalfMagic, Sh0, Ch0);
+            const uint32_t e1 = hfma2u((w1 & 0x00F000F0u) | kHalfMagic, Sh1, Ch1);
+            const uint32_t e2 = hfma2u((w08 & 0x00F000F0u) | kHalfMagic, Sh0, Ch0);
+            const uint32_t e3 = hfma2u((w18 & 0x00F000F0u) | kHalfMagic, Sh1, Ch1);
+            const uint2 bh = bact ? *reinterpret_cast<const uint2*>(xbl + ((2 * c + 1) * 2 + s) * 16)
+                                  : make_uint2(0u, 0u);
+            mma16816(dc, e0, e1, e2, e3, bh.x, bh.y);
+        }
+    }
+    const uint32_t mw0 = t < 2 ? mA0 : mB0, mw1 = t < 2 ? mA1 : mB1;
+    const uint32_t ja = (2 * t) & 3;
+    const uint32_t M0 = hsub2u(__byte_perm(mw0, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
+    const uint32_t M1 = hsub2u(__byte_perm(mw1, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
+    const uint32_t bm = bact ? rec[256 + t * 2 + (g & 1)] : 0u;
+    float d2[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816(d2, M0, M1, 0u, 0u, bm, 0u);
+    const float sc = __uint_as_float(rec[264]);
+    const float dd0 = half_bits_to_float(h0.x) * sc, dm0 = half_bits_to_float(h0.x >> 16) * sc;
+    const float dd1 = half_bits_to_float(h1.x) * sc, dm1 = half_bits_to_float(h1.x >> 16) * sc;
+    acc0 = fmaf(dd0, (d[0][0] + d[1][0]) + (d[0][1] + d[1][1]), fmaf(dm0, d2[0] + d2[1], acc0));
+    acc1 = fmaf(dd1, (d[0][2] + d[1][2]) + (d[0][3] + d[1][3]), fmaf(dm1, d2[2] + d2[3], acc1));
 }
 
 }  // namespace pokit

@@ -27,8 +27,13 @@
 #include "pokit_mma.cuh"
 #include "pokit_quant.cuh"
 
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cfloat>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 namespace pokit {
 namespace {
@@ -36,6 +41,8 @@ namespace {
 constexpr int kThreads = 384;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRouteColsPerWarp = 512;
+constexpr uint32_t kMaxRouteSplits = 8;       // route_warp: hidden <= 8 * 512
+constexpr uint32_t kRouteWarpMaxSlots = 16;   // route_warp: experts <= 16 * 32
 constexpr int kMaxTopK = 64;
 constexpr int kMaxExperts = 1024;
 constexpr int kSbChunk = 8;                 // gate/up superblocks whose loads go out together
@@ -110,6 +117,22 @@ __host__ __device__ inline SmemLayout make_layout(const MoeLayerDev& L, uint32_t
     m.ybuf = off; off += al16(slots * m.rows_cap * 4u);
     m.stage_bytes = stage_bytes_of(L);
     m.stage = off; off += m.stage_bytes * kWarps;
+    m.total = off;
+    return m;
+}
+
+// Layout of the route kernel: input, logits, reductions, routes and the
+// router partials only.
+__host__ __device__ inline SmemLayout route_layout(const MoeLayerDev& L) {
+    SmemLayout m{};
+    uint32_t off = 0;
+    m.xs = off; off += al16(L.hidden * 4u);
+    m.lg = off; off += al16(L.experts * 4u);
+    m.red = off; off += al16(64u * 8u);
+    m.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
+    m.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
+    m.act_plain = off; off += al16((L.experts + 1u) * route_splits(L.hidden) * 4u);
+    m.xp = m.gsum = m.act_prep = m.act_gsum = m.ybuf = m.stage = off;
     m.total = off;
     return m;
 }
@@ -248,25 +271,8 @@ __device__ __forceinline__ void copy_coherent(const float* __restrict__ src, flo
 // warp and whole superblocks of the intermediate.
 __host__ __device__ inline bool mma_path_ok(const MoeLayerDev& L) {
     return L.gate_type == kQ4_K && L.up_type == kQ4_K && L.down_type == kQ4_K && L.shared_inter == 0 &&
-           L.top_k <= static_cast<uint32_t>(kWarps) && (L.inter % 256u) == 0;
-}
-
-// Same as copy_coherent for 16-byte aligned buffers of n4 uint4 elements.
-__device__ __forceinline__ void copy_coherent4(const uint4* __restrict__ src, uint4* dst, uint32_t n4) {
-    constexpr int kPer = 6;
-    for (uint32_t base = 0; base < n4; base += kThreads * kPer) {
-        uint4 v[kPer];
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-            const uint32_t i = base + threadIdx.x + j * kThreads;
-            v[j] = i < n4 ? __ldcg(src + i) : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-            const uint32_t i = base + threadIdx.x + j * kThreads;
-            if (i < n4) dst[i] = v[j];
-        }
-    }
+           L.top_k <= static_cast<uint32_t>(kWarps) && (L.inter % 256u) == 0 &&
+           route_splits(L.hidden) <= kMaxRouteSplits && L.experts <= 32u * kRouteWarpMaxSlots;
 }
 
 __device__ void phase_input(const MoeLayerDev& L, const float* hidden, const float* x_in,
@@ -492,6 +498,119 @@ __device__ void phase_route(const MoeLayerDev& L, const float* partial, Shared& 
             S.weights[r] = s.sel_w[r];
         }
     }
+}
+
+// R2 in one warp, from logits already in shared memory.  Same selection as
+// phase_route: expert f precedes e when its logit is larger, ties to the
+// lower id.  Lane l holds the logits of experts l, l + 32, ... in registers;
+// each of the k rounds takes the warp maximum of the order-preserving logit
+// bits (redux.sync) and, among the lanes at that maximum, the lowest id.  With
+// renormalisation the softmax denominator cancels and is not formed: the
+// weights are exp(l - max) / sum over the selection (the reference's two
+// divisions folded, equal to rounding).  Writes sel_id[0..k), sel_w[0..k]
+// (sel_w[k] = shared gate) and, for `writer`, logits, ids and weights to S.
+// Requires E <= 32 * kSlots and top_k < 32.
+__device__ __forceinline__ uint32_t route_ord(float v) {
+    const uint32_t b = v == 0.0f ? 0u : __float_as_uint(v);      // -0 ranks as +0
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+template <uint32_t kSlots>
+__device__ void route_select(const MoeLayerDev& L, const float* lg, float shared_logit, uint32_t* sel_id,
+                             float* sel_w, uint32_t* status, bool writer, const MoeScratch& S) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t E = L.experts, k = L.top_k;
+    float lgv[kSlots];
+    int bad = 0;
+#pragma unroll
+    for (uint32_t i = 0; i < kSlots; ++i) {
+        const uint32_t e = lane + 32u * i;
+        lgv[i] = e < E ? lg[e] : 0.0f;
+        if (e < E) bad |= !isfinite(lgv[i]);
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    if (writer) {
+#pragma unroll
+        for (uint32_t i = 0; i < kSlots; ++i)
+            if (lane + 32u * i < E) S.logits[lane + 32u * i] = lgv[i];
+    }
+    if (bad) {
+        if (lane == 0 && status) atomicOr(status, kStatusNonFiniteLogits);
+        if (static_cast<uint32_t>(lane) < k) { sel_id[lane] = lane; sel_w[lane] = 0.0f; }
+        if (static_cast<uint32_t>(lane) == k) sel_w[k] = 0.0f;
+    } else {
+        // Order-preserving keys; 0 marks a taken or absent slot (a real key
+        // has bit 31 set or is the complement of a negative float, never 0
+        // for finite logits).
+        uint32_t ord[kSlots];
+#pragma unroll
+        for (uint32_t i = 0; i < kSlots; ++i) ord[i] = lane + 32u * i < E ? route_ord(lgv[i]) : 0u;
+        uint32_t my_id = 0;
+        float my_v = 0.0f, mx = 0.0f;
+        for (uint32_t r = 0; r < k; ++r) {
+            uint32_t best_ord = 0, best_e = 0xffffffffu;
+#pragma unroll
+            for (uint32_t i = 0; i < kSlots; ++i)
+                if (ord[i] > best_ord) { best_ord = ord[i]; best_e = lane + 32u * i; }
+            const uint32_t top = __reduce_max_sync(0xffffffffu, best_ord);
+            // The lowest id among the lanes at the maximum.
+            const uint32_t win = __reduce_min_sync(0xffffffffu, best_ord == top ? best_e : 0xffffffffu);
+#pragma unroll
+            for (uint32_t i = 0; i < kSlots; ++i)
+                if (lane + 32u * i == win) ord[i] = 0u;
+            // The logit back from its key.
+            const float v = __uint_as_float((top & 0x80000000u) ? (top & 0x7fffffffu) : ~top);
+            if (r == 0) mx = v;
+            if (static_cast<uint32_t>(lane) == r) { my_id = win; my_v = v; }
+        }
+        double den_d = 0.0;
+        float den_f = 0.0f;
+        if (!L.normalize) {
+#pragma unroll
+            for (uint32_t i = 0; i < kSlots; ++i)
+                if (lane + 32u * i < E) {
+                    if (L.flavour == 0) den_d += exp(static_cast<double>(lgv[i] - mx));
+                    else den_f += expf(lgv[i] - mx);
+                }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                if (L.flavour == 0) den_d += __shfl_xor_sync(0xffffffffu, den_d, o);
+                else den_f += __shfl_xor_sync(0xffffffffu, den_f, o);
+            }
+        }
+        float p = 0.0f;
+        if (static_cast<uint32_t>(lane) < k) {
+            if (L.normalize) p = expf(my_v - mx);
+            else p = L.flavour == 0 ? static_cast<float>(exp(static_cast<double>(my_v - mx)) / den_d)
+                                    : expf(my_v - mx) / den_f;
+        }
+        float sum = p;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        bool invalid = L.flavour == 1 && !L.normalize && (!isfinite(den_f) || den_f <= 0.0f);
+        if (L.normalize) {
+            if (L.flavour == 1 && (!isfinite(sum) || sum <= 0.0f)) invalid = true;
+            p *= 1.0f / sum;                 // one division for the warp
+        }
+        if (invalid && lane == 0 && status) atomicOr(status, kStatusBadSoftmax);
+        if (static_cast<uint32_t>(lane) < k) {
+            sel_id[lane] = my_id;
+            sel_w[lane] = invalid ? 0.0f : (L.flavour == 0 ? p : p * L.expert_weights_scale);
+        }
+        if (static_cast<uint32_t>(lane) == k) sel_w[k] = L.shared_inter ? sigmoid_qwen35(shared_logit) : 0.0f;
+    }
+    __syncwarp();
+    if (writer) {
+        if (static_cast<uint32_t>(lane) < k) S.ids[lane] = sel_id[lane];
+        if (static_cast<uint32_t>(lane) <= k) S.weights[lane] = sel_w[lane];
+    }
+}
+
+__device__ __forceinline__ void route_select_any(const MoeLayerDev& L, const float* lg, uint32_t* sel_id,
+                                                 float* sel_w, uint32_t* status, bool writer, const MoeScratch& S) {
+    if (L.experts <= 128u) route_select<4>(L, lg, 0.0f, sel_id, sel_w, status, writer, S);
+    else if (L.experts <= 256u) route_select<8>(L, lg, 0.0f, sel_id, sel_w, status, writer, S);
+    else route_select<kRouteWarpMaxSlots>(L, lg, 0.0f, sel_id, sel_w, status, writer, S);
 }
 
 // ---------------------------------------------------------------------------
@@ -813,7 +932,7 @@ struct BlockArgs {
 
 // Kernel 1 of a block: R0 + R1 (CTA 0 also publishes x).
 __global__ void __launch_bounds__(kThreads, 1) moe_route_kernel(BlockArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     Shared s = carve(smem, a.m);
     const uint32_t gw = blockIdx.x * kWarps + (threadIdx.x >> 5), nw = gridDim.x * kWarps;
     RouterRegs rr;
@@ -821,16 +940,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_route_kernel(BlockArgs a) {
     phase_input(a.L, a.hidden, a.x_in, s);
     if (blockIdx.x == 0)
         for (uint32_t i = threadIdx.x; i < a.L.hidden; i += kThreads) a.S.x[i] = s.xs[i];
-    // Tensor-core fragments of x: superblock sb is built by warp 0 of CTA sb mod grid.
-    if ((threadIdx.x >> 5) == 0 && mma_path_ok(a.L))
-        for (uint32_t sb = blockIdx.x; sb < (a.L.hidden >> 8); sb += gridDim.x)
-            q4k_frag_superblock(s.xs + sb * 256u, a.S.xfrag + sb * kFragWords, threadIdx.x & 31);
     router_finish(a.L, gw, nw, rr, s, a.S.partial);
 }
 
 // Kernel 2: R2 (every CTA; CTA 0 publishes the routes) + G.
 __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_kernel(BlockArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     Shared s = carve(smem, a.m);
     phase_route(a.L, a.S.partial, s, a.S.status, blockIdx.x == 0, a.S);
     copy_coherent(a.S.x, s.xs, a.L.hidden);
@@ -840,7 +955,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_kernel(BlockArgs a) {
 
 // Kernel 3: D.
 __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(BlockArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     Shared s = carve(smem, a.m);
     for (uint32_t r = threadIdx.x; r <= a.L.top_k; r += kThreads) {
         if (r < a.L.top_k) s.sel_id[r] = __ldcg(a.S.ids + r);
@@ -887,7 +1002,7 @@ struct DecodeArgs {
 };
 
 __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(DecodeArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t abort_flag;
     Shared s = carve(smem, a.m);
     if (threadIdx.x == 0) abort_flag = 0u;
@@ -930,207 +1045,403 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(DecodeArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core path: every routed matrix Q4_K, no shared expert.
-//
-// gate_up: CTA b of n owns tiles [b*T/n, (b+1)*T/n) of the T = k * 2 * (I/16)
-// (slot, gate|up, 16-row) tiles, at most kMmaTilesPerCta of them.  Tile p is
-// computed by warps 2p and 2p+1, one half of the superblocks each; each warp
-// TMA-copies its half of the 16 rows into padded shared memory as soon as the
-// routes are known, so the copies overlap the activation preparation.
-// down: CTA b owns output rows [16b, 16b+16); warp w < k computes slot w's
-// 16 rows (TMA-copied, L2-resident after gate_up's prefetch), then the rows
-// are combined in route order and added to the residual.
+// Tensor-core path: every routed matrix Q4_K, no shared expert.  Two
+// launches per block; the router runs inside them:
+//   partials  (only for a block whose predecessor did not produce them) CTA c
+//             adds sum_{j in [16c, 16c+16)} W_r[e][j] * x'[j] to logit e,
+//             x' = ffn_norm * hidden (decode) or x_in (forward).
+//   gate_up   every CTA sums the partials in chunk order, applies the rms
+//             scale (linearity: W (s x') = s (W x')), selects the routes in
+//             one warp (CTA 0 publishes them) and builds the fragment records
+//             of x'; CTA b then owns row groups [3b, 3b+3) of the k * I/16
+//             (slot, 16-row) groups, four warps per group computing gate and
+//             up over the two halves of the superblocks; act = silu(s g) * (s u).
+//   down      CTA b owns output rows [16b, 16b+16): it requests its k down
+//             tiles, builds the activation fragments of every slot, runs the
+//             (slot, superblock) units over all warps and combines the rows
+//             in route order into the output (or the residual).  In a decode
+//             chain it then writes the next block's router partials for its
+//             16 new hidden rows.
 // ---------------------------------------------------------------------------
-constexpr int kMmaTilesPerCta = kWarps / 2;
+constexpr uint32_t kGuGroups = kWarps / 4;
+constexpr uint32_t kPartRows = 16;             // hidden rows per router-partial chunk
+
+__host__ __device__ inline uint32_t al128(uint32_t v) { return (v + 127u) & ~127u; }
+
+// Router partial dots are summed across CTAs exactly and independently of
+// arrival order: each float m * 2^ex is added to a carry-save fixed-point
+// accumulator of kRaccLimbs 64-bit limbs, limb i holding bits
+// [32 i + kRaccBase, 32 i + kRaccBase + 32) with 31 bits of headroom for
+// carries (at most 2^31 additions), resolved when the sum is read.  The
+// 24-bit mantissa lands in at most two adjacent limbs; bits below 2^kRaccBase
+// are dropped (below 1e-19 in absolute value).  Non-finite partials set a flag.
+constexpr int kRaccLimbs = 8;                  // covers 2^-64 .. 2^192
+constexpr int kRaccBase = -64;
+__device__ __forceinline__ void racc_add(unsigned long long* limbs, uint32_t* bad, float p) {
+    const uint32_t b = __float_as_uint(p);
+    const uint32_t eb = (b >> 23) & 0xffu;
+    if (eb == 0xffu) {
+        atomicOr(bad, 1u);
+        return;
+    }
+    uint32_t m = b & 0x7fffffu;
+    int ex;
+    if (eb == 0u) {
+        if (m == 0u) return;
+        ex = -149;
+    } else {
+        m |= 0x800000u;
+        ex = static_cast<int>(eb) - 150;
+    }
+    int pos = ex - kRaccBase;
+    if (pos < 0) {
+        if (pos <= -24) return;
+        m >>= -pos;
+        pos = 0;
+        if (m == 0u) return;
+    }
+    const int i = pos >> 5, o = pos & 31;
+    long long v = static_cast<long long>(m) << o;            // below 2^55
+    if (b >> 31) v = -v;
+    const unsigned long long lo = static_cast<unsigned long long>(v & 0xffffffffll);
+    const long long hi = v >> 32;                             // floor division
+    if (lo) atomicAdd(limbs + i, lo);
+    if (hi) atomicAdd(limbs + i + 1, static_cast<unsigned long long>(hi));
+}
+
+// The accumulated value, carries resolved; the three limbs from the most
+// significant non-trivial one are combined in double (53 bits, below which
+// the float result cannot change by more than its last-place rounding), then
+// rounded to float.  The limbs are left zero.
+__device__ __forceinline__ float racc_take(unsigned long long* limbs) {
+    long long l[kRaccLimbs];
+    const ulonglong2* p = reinterpret_cast<const ulonglong2*>(limbs);
+#pragma unroll
+    for (int i = 0; i < kRaccLimbs / 2; ++i) {
+        const ulonglong2 v = __ldcg(p + i);
+        l[2 * i] = static_cast<long long>(v.x);
+        l[2 * i + 1] = static_cast<long long>(v.y);
+    }
+    ulonglong2* q = reinterpret_cast<ulonglong2*>(limbs);
+#pragma unroll
+    for (int i = 0; i < kRaccLimbs / 2; ++i) q[i] = make_ulonglong2(0ull, 0ull);
+#pragma unroll
+    for (int i = 0; i + 1 < kRaccLimbs; ++i) {
+        const long long carry = l[i] >> 32;
+        l[i] -= carry * 4294967296ll;
+        l[i + 1] += carry;
+    }
+    // Limbs 0..6 are now in [0, 2^32); the top limb carries the sign.  The
+    // highest limb that is not a pure sign extension (0 or -1 above a limb
+    // with the matching top bit) leads; unrolled so the limbs stay in
+    // registers.
+    int j = kRaccLimbs - 1;
+#pragma unroll
+    for (int i = kRaccLimbs - 1; i > 2; --i) {
+        if (j == i && (l[i] == 0 || l[i] == -1) && ((l[i - 1] >> 31) & 1) == (l[i] & 1)) {
+            if (l[i] == -1) l[i - 1] -= 4294967296ll;
+            j = i - 1;
+        }
+    }
+    long long top = 0, mid = 0, low = 0;
+#pragma unroll
+    for (int i = 2; i < kRaccLimbs; ++i)
+        if (i == j) { top = l[i]; mid = l[i - 1]; low = l[i - 2]; }
+    const double d = (static_cast<double>(top) * 4294967296.0 + static_cast<double>(mid)) * 4294967296.0 +
+                     static_cast<double>(low);
+    // 2^(32 (j - 2) + kRaccBase) built from its exponent bits (normal range).
+    const double unit = __longlong_as_double(static_cast<long long>(1023 + 32 * (j - 2) + kRaccBase) << 52);
+    return static_cast<float>(d * unit);
+}
+
+// Shared memory of the routing tail (run by the last CTA of the partials
+// kernel or of a down kernel), at byte offset `base`.
+struct TailLayout {
+    uint32_t lg, sel_id, sel_w, stage, end;
+};
+__host__ __device__ inline TailLayout tail_layout(const MoeLayerDev& L, uint32_t base) {
+    TailLayout t{};
+    uint32_t off = base;
+    t.lg = off; off += al16(L.experts * 4u);
+    t.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
+    t.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
+    t.stage = off; off += (kWarps - 1u) * 1024u;
+    t.end = off;
+    return t;
+}
 
 struct MmaLayout {
-    uint32_t bars, recs, lg, red, sel_id, sel_w, pbuf, tmp, part, flags, tiles;
-    uint32_t total, nsb, stride;
+    uint32_t bars, recs, sel_id, sel_w, part, comb, hrow, tiles;
+    TailLayout tail;
+    uint32_t total, nsb, boxes;      // boxes: superblock boxes (and mbarriers) per warp or slot
 };
 
 __host__ __device__ inline MmaLayout mma_gate_up_layout(const MoeLayerDev& L) {
     MmaLayout m{};
-    const uint32_t H = L.hidden, nsb = H >> 8;
+    const uint32_t nsb = L.hidden >> 8, half_sb = (nsb + 1u) / 2u;
     m.nsb = nsb;
-    m.stride = q4k_tile_stride(nsb * 144u);
+    m.boxes = half_sb;
     uint32_t off = 0;
-    m.bars = off; off += 128;
+    m.bars = off; off += al16(kWarps * half_sb * 8u);
     m.recs = off; off += al16(nsb * kFragWords * 4u);
-    m.lg = off; off += al16(L.experts * 4u);
-    m.red = off; off += al16(64u * 8u);
     m.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
-    m.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
-    m.pbuf = off; off += al16((L.experts + 1u) * route_splits(H) * 4u);
-    m.tmp = off; off += al16(256u * 4u);
+    m.sel_w = off;
     m.part = off; off += al16(kWarps * 16u * 4u);
-    m.flags = off; off += al16(kMmaTilesPerCta * 4u + 4u);
-    off = (off + 127u) & ~127u;
-    m.tiles = off; off += kMmaTilesPerCta * 16u * m.stride;
+    m.comb = m.hrow = off;
+    off = al128(off);
+    m.tiles = off; off += kWarps * half_sb * kBoxBytes;
     m.total = off;
     return m;
 }
 
-__host__ __device__ inline MmaLayout mma_down_layout(const MoeLayerDev& L) {
+// The down kernel's routing tail reuses the record space.
+__host__ __device__ inline MmaLayout mma_down_layout(const MoeLayerDev& L, const MoeLayerDev& next) {
     MmaLayout m{};
-    const uint32_t I = L.inter, nsb = I >> 8, k = L.top_k;
+    const uint32_t nsb = L.inter >> 8, k = L.top_k;
     m.nsb = nsb;
-    m.stride = q4k_tile_stride(nsb * 144u);
+    m.boxes = nsb;
     uint32_t off = 0;
-    m.bars = off; off += 128;
-    m.recs = off; off += al16(k * nsb * kFragWords * 4u);
+    m.bars = off; off += al16(k * nsb * 8u);
+    m.recs = off;
+    m.tail = tail_layout(next, off);
+    off = umax(off + al16(k * nsb * kFragWords * 4u), m.tail.end);
     m.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
     m.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
-    m.part = off; off += al16(k * 16u * 4u);
-    off = (off + 127u) & ~127u;
-    m.tiles = off; off += k * 16u * m.stride;
+    m.part = off; off += al16(k * nsb * 16u * 4u);
+    m.comb = off; off += al16(k * 16u * 4u);
+    m.hrow = off; off += al16(2u * kPartRows * 4u);
+    off = al128(off);
+    m.tiles = off; off += k * nsb * kBoxBytes;
     m.total = off;
     return m;
 }
 
 struct MmaArgs {
+    // 3-D tensor maps (byte column, row, expert) of the block's Q4_K gate, up
+    // and down tensors; boxes of 144 bytes x 16 rows.
+    CUtensorMap tm_gate, tm_up, tm_down;
     MoeLayerDev L;
+    MoeLayerDev next;           // decode chain: the following block (valid when has_next)
     MoeScratch S;
-    float* hidden;
-    float* moe_out;
-    const float* next_router;
+    const float* x_in;          // forward: the normalised input
+    float* hidden;              // decode: the residual stream (rms_norm'd on the way in)
+    float* moe_out;             // forward: the block output
+    uint32_t has_next;          // the down kernel routes `next` (partials, tail)
     MmaLayout m;
-    uint32_t down_ctas;   // CTAs of the down kernel (gate_up prefetches their rows)
 };
 
-__device__ __forceinline__ void gate_up_tile_coords(uint32_t tile, uint32_t tiles_per_mat, uint32_t& slot,
-                                                    uint32_t& mat, uint32_t& row0) {
-    slot = tile / (2u * tiles_per_mat);
-    const uint32_t rem = tile % (2u * tiles_per_mat);
-    mat = rem / tiles_per_mat;
-    row0 = (rem % tiles_per_mat) * 16u;
+// Router weights W_r[e][16c .. 16c+16) and their dot with x'[0..16) in row
+// order.
+struct RouterSlice {
+    float4 w[4];
+};
+__device__ __forceinline__ RouterSlice router_slice(const float* router, uint32_t H, uint32_t e, uint32_t c) {
+    const float4* p = reinterpret_cast<const float4*>(router + static_cast<uint64_t>(e) * H + c * kPartRows);
+    return RouterSlice{{__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3)}};
+}
+__device__ __forceinline__ float router_dot16(const RouterSlice& r, const float* xr) {
+    const float wv[16] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w, r.w[1].x, r.w[1].y, r.w[1].z, r.w[1].w,
+                          r.w[2].x, r.w[2].y, r.w[2].z, r.w[2].w, r.w[3].x, r.w[3].y, r.w[3].z, r.w[3].w};
+    float p = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p = fmaf(wv[i], xr[i], p);
+    return p;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(MmaArgs a) {
+// The routing tail of block L, run by the one CTA that finished last after
+// every chunk added its router partials: logits = s * (fixed-point sum of the
+// partial dots), s the rms_norm scale from the per-chunk sums of squares (1
+// for a normalised input); the routes (published to S.ids / S.weights /
+// S.logits); s (S.scale); and the fragment records of x' = ffn_norm * hidden
+// (or x_in) for the gate/up kernel (S.xrec).  The accumulators are left zero.
+__device__ void route_tail(const MoeLayerDev& L, const MoeScratch& S, const float* x, bool hidden_mode,
+                           uint8_t* smem, const TailLayout& t) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t E = L.experts, H = L.hidden, nsb = H >> 8, chunks = H / kPartRows;
+    float* lg = reinterpret_cast<float*>(smem + t.lg);
+    uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + t.sel_id);
+    float* sel_w = reinterpret_cast<float*>(smem + t.sel_w);
+    __shared__ float red[kWarps];
+    __shared__ uint32_t bad_flag;
+    // Loads first: this warp's first record (warps 1.. build records), the
+    // accumulated dots and the per-chunk sums of squares.
+    const uint32_t builders = static_cast<uint32_t>(kWarps) - 1u;
+    const uint32_t q0 = static_cast<uint32_t>(warp) - 1u;
+    const bool rec_now = warp >= 1 && q0 < nsb;
+    float hv[8], nv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t i = q0 * 256u + 32u * j + lane;
+        hv[j] = rec_now ? __ldcg(x + i) : 0.0f;
+        nv[j] = (rec_now && hidden_mode) ? __ldg(L.ffn_norm + i) : 1.0f;
+    }
+    float sq = 0.0f;
+    for (uint32_t c = tid; c < chunks; c += kThreads) sq += __ldcg(S.rsq + c);
+    for (uint32_t e = tid; e < E; e += kThreads) lg[e] = racc_take(S.racc + static_cast<uint64_t>(e) * kRaccLimbs);
+    if (tid == 0) {
+        bad_flag = __ldcg(S.rbad);
+        *S.rbad = 0u;
+    }
+    // Records of x' (warps 1..): staged per warp, built straight into S.xrec.
+    if (warp >= 1) {
+        float* stage = reinterpret_cast<float*>(smem + t.stage) + q0 * 256u;
+        for (uint32_t q = q0; q < nsb; q += builders) {
+            if (q != q0) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t i = q * 256u + 32u * j + lane;
+                    hv[j] = __ldcg(x + i);
+                    nv[j] = hidden_mode ? __ldg(L.ffn_norm + i) : 1.0f;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) stage[32 * j + lane] = hidden_mode ? nv[j] * hv[j] : hv[j];
+            __syncwarp();
+            q4k_frag_superblock(stage, S.xrec + q * kFragWords, lane);
+            __syncwarp();
+        }
+    }
+    // rms_norm scale (src/rms_norm.cpp:20-26).
+    sq = warp_sum(sq);
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    float scale = 1.0f;
+    if (hidden_mode) {
+        float total = 0.0f;
+        for (int w = 0; w < kWarps; ++w) total += red[w];
+        scale = 1.0f / sqrtf(total / static_cast<float>(H) + L.rms_eps);
+    }
+    for (uint32_t e = tid; e < E; e += kThreads) lg[e] = bad_flag ? __int_as_float(0x7fc00000) : lg[e] * scale;
+    __syncthreads();
+    if (warp == 0) route_select_any(L, lg, sel_id, sel_w, S.status, true, S);
+    if (tid == 0) *S.scale = scale;
+}
+
+// Returns true in every thread of the CTA that arrives last at `count`
+// (after all of this CTA's global writes), and resets the counter there.
+__device__ __forceinline__ bool last_cta_arrival(uint32_t* count, uint32_t* flag) {
+    __syncthreads();
+    if (threadIdx.x == 0) *flag = atomic_add_acq_rel_gpu(count, 1u) == gridDim.x - 1u ? 1u : 0u;
+    __syncthreads();
+    const bool last = *flag != 0u;
+    if (last && threadIdx.x == 0) *count = 0u;
+    return last;
+}
+
+// Router partials of block L for the first block of a chain or a single
+// block, then its routing tail.
+__global__ void __launch_bounds__(kThreads, 1) moe_partials_kernel(const __grid_constant__ MmaArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float xr[kPartRows];
+    __shared__ uint32_t flag;
+    const MoeLayerDev& L = a.L;
+    const uint32_t c = blockIdx.x, j0 = c * kPartRows;
+    const float* x = a.hidden ? a.hidden : a.x_in;
+    if (threadIdx.x < 32) {
+        const uint32_t r = threadIdx.x & 15u;
+        const float h = __ldcg(x + j0 + r);
+        float sq = threadIdx.x < 16 ? h * h : 0.0f;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (threadIdx.x < 16) xr[r] = a.hidden ? __ldg(L.ffn_norm + j0 + r) * h : h;
+        if (threadIdx.x == 0) a.S.rsq[c] = sq;
+    }
+    __syncthreads();
+    for (uint32_t e = threadIdx.x; e < L.experts; e += kThreads)
+        racc_add(a.S.racc + static_cast<uint64_t>(e) * kRaccLimbs, a.S.rbad,
+                 router_dot16(router_slice(L.router, L.hidden, e, c), xr));
+    if (last_cta_arrival(a.S.route_count, &flag))
+        route_tail(L, a.S, x, a.hidden != nullptr, smem, a.m.tail);
+}
+
+// Kernel 2 (tensor-core path): act = silu(s g) * (s u) for the CTA's row
+// groups, with the routes, s and the x records from the routing tail.  Each
+// warp's superblocks arrive in their own cp.async group and are multiplied
+// as they land.
+__global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(const __grid_constant__ MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const MoeLayerDev& L = a.L;
     const MmaLayout& m = a.m;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + m.bars);
     uint32_t* recs = reinterpret_cast<uint32_t*>(smem + m.recs);
-    float* tmp = reinterpret_cast<float*>(smem + m.tmp);
+    uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + m.sel_id);
     float* part = reinterpret_cast<float*>(smem + m.part);
-    uint32_t* flags = reinterpret_cast<uint32_t*>(smem + m.flags);
     uint8_t* tiles = smem + m.tiles;
-    Shared s{};
-    s.lg = reinterpret_cast<float*>(smem + m.lg);
-    s.red = reinterpret_cast<double*>(smem + m.red);
-    s.sel_id = reinterpret_cast<uint32_t*>(smem + m.sel_id);
-    s.sel_w = reinterpret_cast<float*>(smem + m.sel_w);
-    s.act_plain = reinterpret_cast<float*>(smem + m.pbuf);
-
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        for (int i = 0; i < kWarps; ++i) mbar_init(&bars[i], 1);
+    const uint32_t H = L.hidden, I = L.inter, nsb = m.nsb, per_slot = I / 16u;
+    const uint32_t groups = L.top_k * per_slot;
+
+    for (uint32_t p = tid; p < nsb * (kFragWords / 4u); p += kThreads)
+        cp_async16(recs + p * 4u, a.S.xrec + p * 4u);
+    cp_async_commit();
+    if (lane == 0) {
+        for (uint32_t i = 0; i < m.boxes; ++i) mbar_init(&bars[warp * m.boxes + i], 1);
         mbar_fence_init();
     }
-    // R2: the routes, from the router partials (every CTA; CTA 0 publishes them).
-    phase_route(L, a.S.partial, s, a.S.status, blockIdx.x == 0, a.S);
-
-    const uint32_t I = L.inter, nsb = m.nsb, nsbI = I >> 8;
-    const uint32_t row_bytes_g = nsb * 144u;
-    const uint32_t tiles_per_mat = I / 16u;
-    const uint32_t T = L.top_k * 2u * tiles_per_mat;
-    const uint32_t t0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * T / gridDim.x);
-    const uint32_t t1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * T / gridDim.x);
-    const uint32_t p = warp >> 1, half = warp & 1;
-    const uint32_t sb_split = nsb / 2;
-    const uint32_t sb0 = half ? sb_split : 0u, sb1 = half ? nsb : sb_split;
-    const uint32_t tile = t0 + p;
-    const bool has_tile = p < static_cast<uint32_t>(kMmaTilesPerCta) && tile < t1 && sb1 > sb0;
-    uint8_t* mytile = tiles + p * 16u * m.stride;
-    if (has_tile && lane == 0) {
-        uint32_t slot, mat, row0;
-        gate_up_tile_coords(tile, tiles_per_mat, slot, mat, row0);
-        const uint64_t id = s.sel_id[slot];
-        const uint8_t* base = (mat ? L.up + id * L.up_slice : L.gate + id * L.gate_slice) +
-                              static_cast<uint64_t>(row0) * row_bytes_g + sb0 * 144u;
-        const uint32_t bytes = (sb1 - sb0) * 144u;
-        mbar_expect_tx(&bars[warp], 16u * bytes);
-        for (uint32_t r = 0; r < 16u; ++r)
-            tma_load(mytile + r * m.stride + sb0 * 144u, base + static_cast<uint64_t>(r) * row_bytes_g,
-                     bytes, &bars[warp]);
-    }
-    // Stream this CTA's share of every slot's down rows into L2.
-    if (blockIdx.x < a.down_ctas && tid < static_cast<int>(L.top_k)) {
-        uint32_t r0, r1;
-        down_rows(L.hidden, blockIdx.x, a.down_ctas, r0, r1);
-        if (r1 > r0) {
-            const uint64_t rd = row_bytes(L.down_type, I);
-            prefetch_l2_range(L.down + s.sel_id[tid] * L.down_slice + r0 * rd, (r1 - r0) * rd);
-        }
-    }
-    // x fragments (published by the route kernel).
-    copy_coherent4(reinterpret_cast<const uint4*>(a.S.xfrag), reinterpret_cast<uint4*>(recs),
-                   nsb * kFragWords / 4u);
+    for (uint32_t r = tid; r < L.top_k; r += kThreads) sel_id[r] = __ldcg(a.S.ids + r);
+    const float scale = __ldcg(a.S.scale);
     __syncthreads();
 
-    if (has_tile) {
-        float acc0 = 0.0f, acc1 = 0.0f;
-        if (mbar_wait(&bars[warp], 0)) {
-            q4k_mma_tile(mytile + sb0 * 144u, m.stride, static_cast<int>(sb1 - sb0), recs + sb0 * kFragWords,
-                         acc0, acc1);
-        } else if (lane == 0) {
-            atomicOr(a.S.status, kStatusWaitTimeout);
+    const uint32_t rg = blockIdx.x * kGuGroups + static_cast<uint32_t>(warp >> 2);
+    const uint32_t mat = (warp >> 1) & 1, half = warp & 1;
+    const uint32_t split = (nsb + 1u) / 2u;
+    const uint32_t sb0 = half ? split : 0u, sb1 = half ? nsb : split;
+    const uint32_t nmine = (rg < groups && sb1 > sb0) ? sb1 - sb0 : 0u;
+    uint8_t* mytile = tiles + warp * m.boxes * kBoxBytes;
+    uint64_t* mybars = bars + warp * m.boxes;
+    // One TMA box per superblock of the warp's half, each on its own
+    // mbarrier: the mma on superblock i overlaps the copies of i+1...
+    if (nmine && lane == 0) {
+        const uint32_t slot = rg / per_slot, row0 = (rg % per_slot) * 16u;
+        const int id = static_cast<int>(sel_id[slot]);
+        const CUtensorMap* map = mat ? &a.tm_up : &a.tm_gate;
+        for (uint32_t i = 0; i < nmine; ++i) {
+            mbar_expect_tx(&mybars[i], kBoxBytes);
+            tma_box_3d(mytile + i * kBoxBytes, map, static_cast<int>((sb0 + i) * 144u), static_cast<int>(row0), id,
+                       &mybars[i]);
         }
-        if ((lane & 3) == 0) {
-            part[warp * 16 + (lane >> 2)] = acc0;
-            part[warp * 16 + (lane >> 2) + 8] = acc1;
+    }
+    // Warm L2 with the down rows of the down CTA with this index.
+    if (blockIdx.x < H / 16u && tid < static_cast<int>(L.top_k)) {
+        const uint64_t rd = static_cast<uint64_t>(I >> 8) * 144u;
+        prefetch_l2_range(L.down + static_cast<uint64_t>(sel_id[tid]) * L.down_slice +
+                              static_cast<uint64_t>(blockIdx.x) * 16u * rd,
+                          16u * rd);
+    }
+    cp_async_wait_all();      // the x records
+    __syncthreads();
+    const int g = lane >> 2;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (uint32_t i = 0; i < nmine; ++i) {
+        if (!mbar_wait(&mybars[i], 0)) {
+            if (lane == 0) atomicOr(a.S.status, kStatusWaitTimeout);
+            mbar_wait(&mybars[i], 0);          // the copy may still land: wait once more
         }
-    } else if (lane < 16) {
-        part[warp * 16 + lane] = 0.0f;
+        const uint8_t* box = mytile + i * kBoxBytes;
+        q4k_mma_superblock(box + g * 144u, box + (g + 8) * 144u, recs + (sb0 + i) * kFragWords, acc0, acc1);
+    }
+    if ((lane & 3) == 0) {
+        part[warp * 16 + g] = acc0;
+        part[warp * 16 + g + 8] = acc1;
     }
     __syncthreads();
-    // Rows of every tile: sum of the two halves, to the gate (act) or up (act2) buffer.
-    for (uint32_t i = tid; i < kMmaTilesPerCta * 16u; i += kThreads) {
-        const uint32_t pp = i >> 4, r = i & 15u, tt = t0 + pp;
-        if (tt >= t1) continue;
-        uint32_t sl, mt, rw;
-        gate_up_tile_coords(tt, tiles_per_mat, sl, mt, rw);
-        const float v = part[(2 * pp) * 16 + r] + part[(2 * pp + 1) * 16 + r];
-        (mt ? a.S.act2 : a.S.act)[sl * I + rw + r] = v;
-    }
-    __syncthreads();
-    // Count finished tiles per (slot, superblock of the intermediate); the CTA
-    // that completes a superblock (16 gate + 16 up tiles) builds its activation
-    // fragments.  No CTA waits for another.
-    if (tid < kMmaTilesPerCta) {
-        uint32_t done = 0xffffffffu;
-        const uint32_t tt = t0 + tid;
-        if (tt < t1) {
-            uint32_t sl, mt, rw;
-            gate_up_tile_coords(tt, tiles_per_mat, sl, mt, rw);
-            const uint32_t key = sl * nsbI + (rw >> 8);
-            __threadfence();
-            if (atomicAdd(&a.S.sbcnt[key], 1u) == 31u) done = key;
-            __threadfence();
+    if (tid < static_cast<int>(kGuGroups * 16u)) {
+        const uint32_t gl = tid >> 4, r = tid & 15, rgx = blockIdx.x * kGuGroups + gl;
+        if (rgx < groups) {
+            const float gv = part[(gl * 4 + 0) * 16 + r] + part[(gl * 4 + 1) * 16 + r];
+            const float uv = part[(gl * 4 + 2) * 16 + r] + part[(gl * 4 + 3) * 16 + r];
+            const uint32_t slot = rgx / per_slot, row0 = (rgx % per_slot) * 16u;
+            a.S.act[slot * I + row0 + r] = silu_mul(gv * scale, uv * scale, L.flavour);
         }
-        flags[tid] = done;
-    }
-    __syncthreads();
-    for (int f = 0; f < kMmaTilesPerCta; ++f) {
-        const uint32_t key = flags[f];
-        if (key == 0xffffffffu) continue;
-        __threadfence();
-        const uint32_t sl = key / nsbI, sb = key % nsbI;
-        for (uint32_t i = tid; i < 256u; i += kThreads) {
-            const uint32_t idx = sl * I + sb * 256u + i;
-            tmp[i] = silu_mul(__ldcg(a.S.act + idx), __ldcg(a.S.act2 + idx), L.flavour);
-        }
-        __syncthreads();
-        if (warp == 0) {
-            q4k_frag_superblock(tmp, a.S.afrag + key * kFragWords, lane);
-            if (lane == 0) a.S.sbcnt[key] = 0u;
-        }
-        __syncthreads();
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(MmaArgs a) {
+// Kernel 3 (tensor-core path): 16 rows of the block output per CTA; in a
+// decode chain also the next block's router partials for those rows, and in
+// the CTA that finishes last the next block's routing tail.
+__global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(const __grid_constant__ MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t flag;
     const MoeLayerDev& L = a.L;
     const MmaLayout& m = a.m;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + m.bars);
@@ -1138,60 +1449,124 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(MmaArgs a) {
     uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + m.sel_id);
     float* sel_w = reinterpret_cast<float*>(smem + m.sel_w);
     float* part = reinterpret_cast<float*>(smem + m.part);
+    float* hrow = reinterpret_cast<float*>(smem + m.hrow);
     uint8_t* tiles = smem + m.tiles;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t k = L.top_k, nsb = m.nsb, H = L.hidden;
+    const uint32_t units = k * nsb;
     const uint32_t j0 = blockIdx.x * 16u;
+    const MoeLayerDev& N = a.next;
 
-    if (tid == 0) {
-        for (int i = 0; i < kWarps; ++i) mbar_init(&bars[i], 1);
-        mbar_fence_init();
-    }
     for (uint32_t r = tid; r < k; r += kThreads) {
         sel_id[r] = __ldcg(a.S.ids + r);
         sel_w[r] = __ldcg(a.S.weights + r);
     }
+    if (tid == 0) {
+        for (uint32_t i = 0; i < units; ++i) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+    }
+    const float resid = (!a.moe_out && tid < 16) ? __ldcg(a.hidden + j0 + tid) : 0.0f;
+    const float nnorm = (a.has_next && tid < 16) ? __ldg(N.ffn_norm + j0 + tid) : 0.0f;
+    // The next block's router weights for these 16 rows (thread e; E above
+    // the block size loads the rest at the end).
+    const bool slice_now = a.has_next && static_cast<uint32_t>(tid) < N.experts;
+    RouterSlice rs{};
+    if (slice_now) rs = router_slice(N.router, H, tid, blockIdx.x);
+    // Activation values of this warp's records (q = warp, warp + kWarps, ...
+    // of k * nsb), requested before the routes arrive.
+    constexpr int kRecPerWarp = 2;
+    float v[kRecPerWarp][8];
+#pragma unroll
+    for (int i = 0; i < kRecPerWarp; ++i) {
+        const uint32_t q = warp + i * kWarps;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            v[i][j] = q < units ? __ldcg(a.S.act + static_cast<uint64_t>(q) * 256u + 32 * j + lane) : 0.0f;
+    }
     __syncthreads();
-    const uint32_t rbd = nsb * 144u;
+    // Box (slot, superblock) u = slot * nsb + sb on mbarrier u.
     if (static_cast<uint32_t>(warp) < k && lane == 0) {
-        const uint8_t* base = L.down + static_cast<uint64_t>(sel_id[warp]) * L.down_slice +
-                              static_cast<uint64_t>(j0) * rbd;
-        mbar_expect_tx(&bars[warp], 16u * rbd);
-        for (uint32_t r = 0; r < 16u; ++r)
-            tma_load(tiles + (warp * 16u + r) * m.stride, base + static_cast<uint64_t>(r) * rbd, rbd,
-                     &bars[warp]);
+        const int id = static_cast<int>(sel_id[warp]);
+        for (uint32_t sb = 0; sb < nsb; ++sb) {
+            const uint32_t u = warp * nsb + sb;
+            mbar_expect_tx(&bars[u], kBoxBytes);
+            tma_box_3d(tiles + u * kBoxBytes, &a.tm_down, static_cast<int>(sb * 144u), static_cast<int>(j0), id, &bars[u]);
+        }
     }
-    if (a.next_router && tid == 0) {
-        const uint64_t bytes = static_cast<uint64_t>(L.experts) * H * 4u;
-        const uint64_t lo = (bytes * blockIdx.x / gridDim.x) & ~uint64_t(15);
-        const uint64_t hi = blockIdx.x + 1 == gridDim.x ? bytes : (bytes * (blockIdx.x + 1) / gridDim.x) & ~uint64_t(15);
-        if (hi > lo) prefetch_l2_range(reinterpret_cast<const uint8_t*>(a.next_router) + lo, hi - lo);
+    // Records staged in their own space, then built in place.
+#pragma unroll
+    for (int i = 0; i < kRecPerWarp; ++i) {
+        const uint32_t q = warp + i * kWarps;
+        if (q < units) {
+            float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) stage[32 * j + lane] = v[i][j];
+        }
     }
-    // Activation fragments of every slot (built by the gate/up kernel).
-    copy_coherent4(reinterpret_cast<const uint4*>(a.S.afrag), reinterpret_cast<uint4*>(recs),
-                   k * nsb * kFragWords / 4u);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < kRecPerWarp; ++i) {
+        const uint32_t q = warp + i * kWarps;
+        if (q < units) q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords, lane);
+    }
+    for (uint32_t q = warp + kRecPerWarp * kWarps; q < units; q += kWarps) {
+        float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = __ldcg(a.S.act + static_cast<uint64_t>(q) * 256u + 32 * j + lane);
+        __syncwarp();
+        q4k_frag_superblock(stage, recs + q * kFragWords, lane);
+    }
     __syncthreads();
-    if (static_cast<uint32_t>(warp) < k) {
+    const int g = lane >> 2;
+    for (uint32_t u = warp; u < units; u += kWarps) {
+        if (!mbar_wait(&bars[u], 0)) {
+            if (lane == 0) atomicOr(a.S.status, kStatusWaitTimeout);
+            mbar_wait(&bars[u], 0);            // the copy may still land: wait once more
+        }
+        const uint8_t* box = tiles + u * kBoxBytes;
         float acc0 = 0.0f, acc1 = 0.0f;
-        if (mbar_wait(&bars[warp], 0)) {
-            q4k_mma_tile(tiles + warp * 16u * m.stride, m.stride, static_cast<int>(nsb),
-                         recs + warp * nsb * kFragWords, acc0, acc1);
-        } else if (lane == 0) {
-            atomicOr(a.S.status, kStatusWaitTimeout);
-        }
+        q4k_mma_superblock(box + g * 144u, box + (g + 8) * 144u, recs + u * kFragWords, acc0, acc1);
         if ((lane & 3) == 0) {
-            part[warp * 16 + (lane >> 2)] = acc0;
-            part[warp * 16 + (lane >> 2) + 8] = acc1;
+            part[u * 16 + g] = acc0;
+            part[u * 16 + g + 8] = acc1;
         }
+    }
+    __syncthreads();
+    // Weighted slot rows (row, slot) in parallel, then the sum over slots in
+    // route order.
+    float* comb = reinterpret_cast<float*>(smem + m.comb);
+    for (uint32_t t = tid; t < 16u * k; t += kThreads) {
+        const uint32_t row = t & 15u, sl = t >> 4;
+        float y = 0.0f;
+        for (uint32_t sb = 0; sb < nsb; ++sb) y += part[(sl * nsb + sb) * 16 + row];
+        comb[sl * 16 + row] = sel_w[sl] * y;
     }
     __syncthreads();
     if (tid < 16) {
         float acc = 0.0f;
-        for (uint32_t sl = 0; sl < k; ++sl) acc += sel_w[sl] * part[sl * 16 + tid];
+        for (uint32_t sl = 0; sl < k; ++sl) acc += comb[sl * 16 + tid];
         const uint32_t row = j0 + tid;
-        if (a.moe_out) a.moe_out[row] = acc;
-        else a.hidden[row] = __ldcg(a.hidden + row) + acc;
+        if (a.moe_out) {
+            a.moe_out[row] = acc;
+        } else {
+            const float h = resid + acc;
+            a.hidden[row] = h;
+            hrow[tid] = nnorm * h;
+            hrow[kPartRows + tid] = h * h;
+        }
     }
+    if (!a.has_next) return;
+    __syncthreads();
+    if (slice_now) racc_add(a.S.racc + static_cast<uint64_t>(tid) * kRaccLimbs, a.S.rbad, router_dot16(rs, hrow));
+    for (uint32_t e = tid + kThreads; e < N.experts; e += kThreads)
+        racc_add(a.S.racc + static_cast<uint64_t>(e) * kRaccLimbs, a.S.rbad,
+                 router_dot16(router_slice(N.router, H, e, blockIdx.x), hrow));
+    if (tid == 0) {
+        float sq = 0.0f;
+        for (uint32_t r = 0; r < kPartRows; ++r) sq += hrow[kPartRows + r];
+        a.S.rsq[blockIdx.x] = sq;
+    }
+    if (last_cta_arrival(a.S.route_count, &flag)) route_tail(N, a.S, a.hidden, true, smem, m.tail);
 }
 
 // ---------------------------------------------------------------------------
@@ -1205,7 +1580,7 @@ cudaError_t ensure_smem(K kernel, size_t bytes, size_t& granted) {
 }
 
 size_t g_route_smem = 0, g_gate_up_smem = 0, g_down_smem = 0, g_decode_smem = 0;
-size_t g_gate_up_mma_smem = 0, g_down_mma_smem = 0;
+size_t g_gate_up_mma_smem = 0, g_down_mma_smem = 0, g_partials_smem = 0;
 
 uint64_t align256(uint64_t v) { return (v + 255u) & ~uint64_t(255); }
 
@@ -1230,10 +1605,12 @@ uint64_t moe_scratch_bytes(const MoeLayerDev& L) {
     b += align256(L.top_k * 4u);                                          // ids
     b += align256(slots * 4u);                                            // weights
     b += align256(slots * max_inter_of(L) * 4u);                          // act
-    b += align256(slots * max_inter_of(L) * 4u);                          // act2
-    b += align256((L.hidden >> 8) * kFragWords * 4u);                     // xfrag
-    b += align256(slots * ((max_inter_of(L) + 255u) >> 8) * kFragWords * 4u);  // afrag
-    b += align256(slots * ((max_inter_of(L) + 255u) >> 8) * 4u);         // sbcnt
+    b += align256((L.hidden >> 8) * kFragWords * 4u);                     // xrec
+    b += align256(4u);                                                    // scale
+    b += align256((L.hidden / kPartRows) * 4u);                           // rsq
+    b += align256(L.experts * kRaccLimbs * 8u);                           // racc
+    b += align256(4u);                                                    // rbad
+    b += align256(4u);                                                    // route_count
     b += align256(4u);                                                    // counter
     b += align256(4u);                                                    // status
     return b;
@@ -1249,11 +1626,13 @@ MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base) {
     s.ids = reinterpret_cast<uint32_t*>(p); p += align256(L.top_k * 4u);
     s.weights = reinterpret_cast<float*>(p); p += align256(slots * 4u);
     s.act = reinterpret_cast<float*>(p); p += align256(slots * max_inter_of(L) * 4u);
-    s.act2 = reinterpret_cast<float*>(p); p += align256(slots * max_inter_of(L) * 4u);
-    s.xfrag = reinterpret_cast<uint32_t*>(p); p += align256((L.hidden >> 8) * kFragWords * 4u);
-    s.afrag = reinterpret_cast<uint32_t*>(p);
-    p += align256(slots * ((max_inter_of(L) + 255u) >> 8) * kFragWords * 4u);
-    s.sbcnt = reinterpret_cast<uint32_t*>(p); p += align256(slots * ((max_inter_of(L) + 255u) >> 8) * 4u);
+    s.xrec = reinterpret_cast<uint32_t*>(p); p += align256((L.hidden >> 8) * kFragWords * 4u);
+    s.scale = reinterpret_cast<float*>(p); p += align256(4u);
+    s.rsq = reinterpret_cast<float*>(p); p += align256((L.hidden / kPartRows) * 4u);
+    // racc .. status end the carve and must be zero before a launch.
+    s.racc = reinterpret_cast<unsigned long long*>(p); p += align256(L.experts * kRaccLimbs * 8u);
+    s.rbad = reinterpret_cast<uint32_t*>(p); p += align256(4u);
+    s.route_count = reinterpret_cast<uint32_t*>(p); p += align256(4u);
     s.counter = reinterpret_cast<uint32_t*>(p); p += align256(4u);
     s.status = reinterpret_cast<uint32_t*>(p);
     return s;
@@ -1268,13 +1647,117 @@ cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, ui
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Tensor maps of the expert tensors, encoded once per (tensor, shape).
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// (byte column, row, expert) view of a Q4_K expert tensor: `rows` rows of
+// `row_bytes` per expert, experts `slice` bytes apart; boxes of one
+// superblock (144 bytes) by 16 rows.
+static bool encode_expert_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows,
+                              uint64_t experts, uint64_t slice) {
+    static std::mutex mu;
+    static std::map<std::tuple<const uint8_t*, uint64_t, uint64_t, uint64_t, uint64_t>, CUtensorMap> cache;
+    const auto key = std::make_tuple(base, row_bytes, rows, experts, slice);
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) {
+        *map = it->second;
+        return true;
+    }
+    const auto encode = tensor_map_encoder();
+    if (!encode) return false;
+    const cuuint64_t dims[3] = {row_bytes, rows, experts};
+    const cuuint64_t strides[2] = {row_bytes, slice};
+    const cuuint32_t box[3] = {144u, kBoxRows, 1u};
+    const cuuint32_t elem[3] = {1u, 1u, 1u};
+    if (encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    cache.emplace(key, *map);
+    return true;
+}
+
+static bool aligned16(const void* p, uint64_t slice) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && (slice & 15u) == 0;
+}
+
+// The tensor-core path serves the block (shapes, TMA alignment and
+// shared-memory budgets).
+static bool tensor_path(const MoeLayerDev& L) {
+    return mma_path_ok(L) && aligned16(L.gate, L.gate_slice) && aligned16(L.up, L.up_slice) &&
+           aligned16(L.down, L.down_slice) && mma_gate_up_layout(L).total <= 227u * 1024u &&
+           mma_down_layout(L, L).total <= 227u * 1024u && tail_layout(L, 0).end <= 227u * 1024u;
+}
+
 static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
-                              float* hidden, float* moe_out, const float* next_router,
-                              cudaStream_t stream, bool dry_run) {
+                              float* hidden, float* moe_out, const MoeLayerDev* prev,
+                              const MoeLayerDev* next, cudaStream_t stream, bool dry_run,
+                              uint32_t* launches) {
+    if (launches) *launches = 0;
     if (!layer_valid(L)) return cudaErrorInvalidValue;
     if (!hidden && (!x_in || !moe_out)) return cudaErrorInvalidValue;
     if (hidden && !L.ffn_norm) return cudaErrorInvalidValue;
     const int sms = device_sm_count();
+    if (tensor_path(L)) {
+        // In a decode chain of tensor-path blocks of one shape, each down
+        // kernel routes the next block (partials and tail).
+        const auto chains = [&](const MoeLayerDev* o) {
+            return hidden && o && tensor_path(*o) && o->hidden == L.hidden && o->experts == L.experts &&
+                   o->inter == L.inter && o->top_k == L.top_k;
+        };
+        const bool from_prev = chains(prev), to_next = chains(next);
+        const MoeLayerDev& nx = to_next ? *next : L;
+        const MmaLayout gl = mma_gate_up_layout(L), dl = mma_down_layout(L, nx);
+        MmaLayout pl{};
+        pl.tail = tail_layout(L, 0);
+        pl.total = pl.tail.end;
+        cudaError_t e = ensure_smem(moe_gate_up_mma_kernel, gl.total, g_gate_up_mma_smem);
+        if (e == cudaSuccess) e = ensure_smem(moe_down_mma_kernel, dl.total, g_down_mma_smem);
+        if (e == cudaSuccess) e = ensure_smem(moe_partials_kernel, pl.total, g_partials_smem);
+        if (e != cudaSuccess || dry_run) return e;
+        MmaArgs ma{};
+        const uint64_t rb_in = static_cast<uint64_t>(L.hidden >> 8) * 144u;
+        const uint64_t rb_down = static_cast<uint64_t>(L.inter >> 8) * 144u;
+        if (!encode_expert_map(&ma.tm_gate, L.gate, rb_in, L.inter, L.experts, L.gate_slice) ||
+            !encode_expert_map(&ma.tm_up, L.up, rb_in, L.inter, L.experts, L.up_slice) ||
+            !encode_expert_map(&ma.tm_down, L.down, rb_down, L.hidden, L.experts, L.down_slice))
+            return cudaErrorInvalidValue;
+        ma.L = L;
+        ma.next = nx;
+        ma.has_next = to_next ? 1u : 0u;
+        ma.S = S;
+        ma.x_in = x_in;
+        ma.hidden = hidden;
+        ma.moe_out = hidden ? nullptr : moe_out;
+        const uint32_t chunks = L.hidden / kPartRows;
+        const uint32_t groups = L.top_k * (L.inter / 16u);
+        uint32_t n = 0;
+        if (!from_prev) {
+            ma.m = pl;
+            moe_partials_kernel<<<chunks, kThreads, pl.total, stream>>>(ma);
+            ++n;
+        }
+        ma.m = gl;
+        moe_gate_up_mma_kernel<<<(groups + kGuGroups - 1u) / kGuGroups, kThreads, gl.total, stream>>>(ma);
+        ma.m = dl;
+        moe_down_mma_kernel<<<chunks, kThreads, dl.total, stream>>>(ma);
+        n += 2;
+        if (launches) *launches = n;
+        return cudaGetLastError();
+    }
     const uint32_t down_ctas = block_down_ctas(L);
     BlockArgs a{};
     a.L = L;
@@ -1282,58 +1765,37 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
     a.x_in = x_in;
     a.hidden = hidden;
     a.moe_out = moe_out;
-    a.next_router = next_router;
+    a.next_router = next ? next->router : nullptr;
     a.down_ctas = down_ctas;
     // Kernel 1 uses enough CTAs to give every router task its own warp.
     const uint32_t tasks = (L.experts + (L.shared_inter ? 1u : 0u)) * route_splits(L.hidden);
     const uint32_t g1 = std::min<uint32_t>(static_cast<uint32_t>(sms), (tasks + kWarps - 1) / kWarps);
+    const SmemLayout rl = route_layout(L);
     a.m = make_layout(L, down_ctas);
-    if (a.m.total > 227u * 1024u) return cudaErrorInvalidValue;
-    cudaError_t e = ensure_smem(moe_route_kernel, a.m.total, g_route_smem);
+    if (a.m.total > 227u * 1024u || rl.total > 227u * 1024u) return cudaErrorInvalidValue;
+    cudaError_t e = ensure_smem(moe_route_kernel, rl.total, g_route_smem);
     if (e == cudaSuccess) e = ensure_smem(moe_gate_up_kernel, a.m.total, g_gate_up_smem);
     if (e == cudaSuccess) e = ensure_smem(moe_down_kernel, a.m.total, g_down_smem);
-    if (e != cudaSuccess) return e;
-    if (mma_path_ok(L)) {
-        MmaArgs ma{};
-        ma.L = L;
-        ma.S = S;
-        ma.hidden = hidden;
-        ma.moe_out = moe_out;
-        ma.next_router = next_router;
-        const MmaLayout gl = mma_gate_up_layout(L), dl = mma_down_layout(L);
-        if (gl.total > 227u * 1024u || dl.total > 227u * 1024u) return cudaErrorInvalidValue;
-        e = ensure_smem(moe_gate_up_mma_kernel, gl.total, g_gate_up_mma_smem);
-        if (e == cudaSuccess) e = ensure_smem(moe_down_mma_kernel, dl.total, g_down_mma_smem);
-        if (e != cudaSuccess || dry_run) return e;
-        const uint32_t T = L.top_k * 2u * (L.inter / 16u);
-        const uint32_t g2 = std::max<uint32_t>(static_cast<uint32_t>(sms),
-                                               (T + kMmaTilesPerCta - 1) / kMmaTilesPerCta);
-        const uint32_t g3 = L.hidden / 16u;
-        ma.down_ctas = g3;
-        moe_route_kernel<<<g1, kThreads, a.m.total, stream>>>(a);
-        ma.m = gl;
-        moe_gate_up_mma_kernel<<<g2, kThreads, gl.total, stream>>>(ma);
-        ma.m = dl;
-        moe_down_mma_kernel<<<g3, kThreads, dl.total, stream>>>(ma);
-        return cudaGetLastError();
-    }
-    if (dry_run) return cudaSuccess;
-    moe_route_kernel<<<g1, kThreads, a.m.total, stream>>>(a);
+    if (e != cudaSuccess || dry_run) return e;
+    BlockArgs ra = a;
+    ra.m = rl;
+    moe_route_kernel<<<g1, kThreads, rl.total, stream>>>(ra);
     moe_gate_up_kernel<<<sms, kThreads, a.m.total, stream>>>(a);
     moe_down_kernel<<<down_ctas, kThreads, a.m.total, stream>>>(a);
+    if (launches) *launches = 3;
     return cudaGetLastError();
 }
 
 cudaError_t launch_moe_block(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
-                             float* hidden, float* moe_out, const float* next_router,
-                             cudaStream_t stream) {
-    return block_impl(L, S, x_in, hidden, moe_out, next_router, stream, false);
+                             float* hidden, float* moe_out, const MoeLayerDev* prev,
+                             const MoeLayerDev* next, cudaStream_t stream, uint32_t* launches) {
+    return block_impl(L, S, x_in, hidden, moe_out, prev, next, stream, false, launches);
 }
 
 cudaError_t prepare_moe_block(const MoeLayerDev& L) {
     MoeScratch none;
     float dummy = 0.0f;
-    cudaError_t e = block_impl(L, none, &dummy, nullptr, &dummy, nullptr, nullptr, true);
+    cudaError_t e = block_impl(L, none, &dummy, nullptr, &dummy, nullptr, nullptr, nullptr, true, nullptr);
     if (e != cudaSuccess) return e;
     const SmemLayout m = make_layout(L, static_cast<uint32_t>(device_sm_count()));
     if (m.total > 227u * 1024u) return cudaErrorInvalidValue;

@@ -139,12 +139,12 @@ extern "C" pokit_cuda_status pokit_cuda_moe_forward_static_scratch(
         void* base = scratch_for_current_device();
         const pokit::MoeScratch S = pokit::moe_scratch_carve(L, base);
         check(pokit::prepare_moe_block(L), "prepare MoE kernels");
-        // The superblock counters, the completion counter and the status word are
-        // adjacent at the end of the carve: one clear covers the three.
+        // The router accumulators, the counters and the status word end the
+        // carve: one clear covers them.
         const size_t tail = static_cast<size_t>(reinterpret_cast<const uint8_t*>(S.status) + sizeof(uint32_t) -
-                                                reinterpret_cast<const uint8_t*>(S.sbcnt));
-        check(cudaMemsetAsync(S.sbcnt, 0, tail, st), "clear counters and status");
-        check(pokit::launch_moe_block(L, S, input, nullptr, output, nullptr, st), "MoE block");
+                                                reinterpret_cast<const uint8_t*>(S.racc));
+        check(cudaMemsetAsync(S.racc, 0, tail, st), "clear accumulators, counters and status");
+        check(pokit::launch_moe_block(L, S, input, nullptr, output, nullptr, nullptr, st, nullptr), "MoE block");
         if (route_ids)
             check(cudaMemcpyAsync(route_ids, S.ids, L.top_k * sizeof(uint32_t),
                                   cudaMemcpyDeviceToDevice, st), "route ids");
