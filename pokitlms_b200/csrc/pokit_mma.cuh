@@ -1,32 +1,35 @@
 // pokit_mma.cuh -- tensor-core Q4_K dequant-dot for decode batch 1 (sm_100a).
 //
-// A warp computes 16 rows of y = W x for a Q4_K matrix W with one
-// mma.sync.m16n8k16 (f16 inputs, f32 accumulate) per (sub-block, 16 weights):
+// A warp computes 16 rows of y = W x for a Q4_K matrix W with integer
+// tensor-core MMAs, mma.sync.m16n8k32 (u8 x s8 -> s32), one per 32-weight
+// sub-block:
 //
-//   A (16 x 16)  = q * s  for 16 rows and 16 weights of one 32-weight sub-block
-//                  (q the 4-bit quant, s its 6-bit scale).  q*s <= 945 is an
-//                  integer, exact in fp16; it is formed with one fp16x2 FMA from
-//                  the nibble OR-ed into the mantissa of 1024 (or 1024 + 16q for
-//                  high nibbles): (1024 + q)*s - 1024*s.
-//   B (16 x 8)   = column 0: x_hi = fp16(x'), column 1: x_lo = fp16(x' - x_hi),
-//                  columns 2..7 zero, with x' = x * 2^-e per superblock so that
-//                  |x'| stays inside fp16 range.  x_hi + x_lo carries ~22
-//                  significant bits of x'.
-//   D (16 x 8)   accumulates all 8 sub-blocks of a superblock; D[r][0] + D[r][1]
-//                = sum_j s_j sum_i q_ij x'_i.
-//   mins         one more mma with A = m_j (k = j) and B = -sum_{i in j} x'_i.
-//   per superblock and row: acc += (d * 2^e) * D1 + (dmin * 2^e) * D2, FP32.
+//   A (16 x 32)  the sub-block's 4-bit quants as bytes: q (low nibbles, one
+//                LOP3 per four weights) or 16 q (high nibbles, masked in place).
+//   B (32 x 8)   columns 0..3: x split into four int8 pieces per superblock,
+//                x ~ s0 (p0 + p1 / 2^7 + p2 / 2^14 + p3 / 2^21) with s0 = 2^E0
+//                the power of two that brings max|x| to <= 127 (|p1..p3| <=
+//                64); columns 4..7 zero.  The residual is below 2^-28 of
+//                max|x|, so elements next to a large outlier keep their
+//                precision.
+//   D (16 x 8)   the exact int32 dot of each piece with the sub-block's quants;
+//                multiplied by the sub-block's 6-bit scale (IMAD) and summed
+//                over the superblock in int32 (at most 2^28).
+//   mins         one fp16 mma with A = m_j (k = j) and B = -sum_{i in j} x_i.
+//   per superblock and row: acc += d * s0 * (piece sums, high nibbles / 16)
+//                + dmin * 2^e * mins, FP32, in the lanes holding each piece
+//                column; callers add the four lanes of a row group (quad_sum).
 //
 // Algebraically this is sum_i (d*s_j*q_i - dmin*m_j) * x_i, the reference's
-// decode_q4_k (src/quantized_linear.cpp:166-205) dotted with x; the products
-// are exact and the sums are FP32, so results agree with the reference's FP32
-// loop to ~1e-6 relative.
+// decode_q4_k (src/quantized_linear.cpp:166-205) dotted with x; the integer
+// products are exact and the scale arithmetic is FP32, so results agree with
+// the reference's FP32 loop to ~1e-6 relative.
 //
-// Fragment layout (PTX m16n8k16 .f16): thread (g = lane/4, t = lane%4) holds
-// A rows g and g+8 at k = {2t, 2t+1, 2t+8, 2t+9} and B column g at the same k.
-// The 16 k-positions of a slice map to weight bytes of a 32-byte qs chunk so
-// that thread t reads 8 contiguous bytes per row and chunk: slice s of the
-// chunk, k = 2t, 2t+1, 2t+8, 2t+9  <->  bytes 8t+4s + {0, 2, 1, 3}.
+// Fragment layout (PTX m16n8k32 .s8/.u8): thread (g = lane/4, t = lane%4)
+// holds A rows g and g+8 at k = 4t..4t+3 and 4t+16..4t+19, B column g at the
+// same k, and D rows g, g+8 at columns 2t, 2t+1.  k = 4t + i is weight byte
+// 8t + i of a 32-byte qs chunk and k = 4t + 16 + i is byte 8t + 4 + i, so
+// thread t reads 8 contiguous bytes per row and chunk.
 #pragma once
 
 #include <cuda.h>   // CUtensorMap
@@ -120,12 +123,14 @@ constexpr uint32_t kBoxRows = 16, kBoxBytes = 16u * 144u;
 // ---------------------------------------------------------------------------
 // Activation fragments.  One record of kFragWords 32-bit words per superblock
 // (256 activations):
-//   [0, 256)   B fragments: word ((j*2 + s)*8 + t*2 + half)*2 + {0, 1} holds the
-//              two fp16x2 pairs thread t needs for sub-block j, slice s, hi
-//              (half 0) or lo (half 1) -- the 8 lanes that load B read 8
-//              consecutive 8-byte slots, so the loads are bank-conflict free
-//   [256, 264) min fragments: word t*2 + half = fp16x2 (-gsum_{2t}, -gsum_{2t+1})
-//   264        the superblock's scale 2^e (float bits); x' = x * 2^-e
+//   bytes [0, 1024) B fragments: byte (j*4 + p)*32 + e = piece p of element e
+//                   of sub-block j (int8); thread (g, t) loads the 8 bytes at
+//                   (j*4 + g)*32 + 8t for piece g < 4
+//   words [256, 264) min fragments: word t*2 + half = fp16x2 of
+//                   -(sum of sub-blocks 2t, 2t+1) * 2^-e, hi (half 0) or lo
+//   word 264        2^e (float bits), the min fragments' scale
+//   word 265        s0 = 2^E0 (float bits), the pieces' scale
+// 256 floats can be staged in the record's own space before it is built.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kFragWords = 272;
 
@@ -139,8 +144,9 @@ __device__ __forceinline__ float half_round(float a) { return __half2float(__flo
 // is read into registers before the first write, so v may alias rec (the
 // values staged in the record's own space) and be in global or shared memory;
 // v and rec are 16-byte aligned.
-// The eight 32-element group sums come from one reduce-scatter (lane L ends
-// with the sum of group (L >> 2) & 7) instead of eight warp reductions.
+// 2^k as a float for k in the normal range, from its exponent bits.
+__device__ __forceinline__ float pow2f(int k) { return __int_as_float((127 + k) << 23); }
+
 __device__ __forceinline__ void q4k_frag_superblock(const float* v, uint32_t* rec, int lane) {
     float x[8];
     float m = 0.0f;
@@ -149,39 +155,44 @@ __device__ __forceinline__ void q4k_frag_superblock(const float* v, uint32_t* re
         x[j] = v[32 * j + lane];
         m = fmaxf(m, fabsf(x[j]));
     }
-    // B-fragment items (j, s, t) = lane and lane + 32: elements
-    // 32j + 8t + 4s + {0, 2, 1, 3} (chunk c = j/2, nibble half j%2).
-    // Item (j, s, t) = lane + 32h covers elements 4 (8j + 2t + s) + {0, 2, 1, 3}:
-    // one 16-byte read per item (a permutation of the warp's slots).
-    float it[2][4];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int item = lane + 32 * h;
-        const int t = item & 3, s = (item >> 2) & 1, j = item >> 3;
-        const float4 q = *reinterpret_cast<const float4*>(v + 4 * (8 * j + 2 * t + s));
-        it[h][0] = q.x;
-        it[h][1] = q.z;
-        it[h][2] = q.y;
-        it[h][3] = q.w;
-    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    // Keep |x'| <= 2^10 so that x' and the 32-element group sums (<= 2^15)
-    // stay inside fp16 range.
-    int e = 0;
-    if (m > 1024.0f) {
-        int ex;
-        frexpf(m, &ex);
-        e = ex - 10;
+    // s0 = 2^E0 >= max|x| / 127 (E0 from the exponent bits of max|x| / 127,
+    // rounded up; the lowest exponents are clamped, where every piece is 0).
+    const uint32_t mb = __float_as_uint(m * (1.0f / 127.0f));
+    int e0 = static_cast<int>(mb >> 23) - 126;           // 2^e0 > m / 127 for normal m / 127
+    e0 = max(e0, -100);
+    // N = rint(x * 2^(21 - E0)), |N| < 2^28, split into balanced base-128
+    // digits: x ~ 2^E0 (p0 + p1 2^-7 + p2 2^-14 + p3 2^-21), |p1..p3| <= 64.
+    const float upN = pow2f(21 - e0), unitN = pow2f(e0 - 21);
+    // The min fragments' scale keeps the 32-element sums inside fp16.
+    const int e = m > 1024.0f ? static_cast<int>(__float_as_uint(m) >> 23) - 127 - 9 : 0;
+    const float inv = pow2f(-e) * unitN;
+    int8_t q[8][4];
+    float xh[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        int n = __float2int_rn(x[j] * upN);
+        xh[j] = static_cast<float>(n) * inv;             // the value the pieces carry, scaled
+        const int d3 = ((n + 64) & 127) - 64;
+        n = (n - d3) >> 7;
+        const int d2 = ((n + 64) & 127) - 64;
+        n = (n - d2) >> 7;
+        const int d1 = ((n + 64) & 127) - 64;
+        n = (n - d1) >> 7;
+        q[j][0] = static_cast<int8_t>(max(-127, min(127, n)));
+        q[j][1] = static_cast<int8_t>(d1);
+        q[j][2] = static_cast<int8_t>(d2);
+        q[j][3] = static_cast<int8_t>(d3);
     }
-    const float inv = ldexpf(1.0f, -e);
-    // Reduce-scatter of the eight group sums of x' (lane bits 4, 3, 2 pick
-    // the group, bits 1, 0 are summed last).
+    // Reduce-scatter of the eight group sums of the represented values (lane
+    // bits 4, 3, 2 pick the group, bits 1, 0 are summed last): lane L ends
+    // with the sum of group (L >> 2) & 7.
     const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
     float y[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float keep = (b4 ? x[4 + i] : x[i]) * inv, send = (b4 ? x[i] : x[4 + i]) * inv;
+        const float keep = b4 ? xh[4 + i] : xh[i], send = b4 ? xh[i] : xh[4 + i];
         y[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
     }
     float z[2];
@@ -198,33 +209,40 @@ __device__ __forceinline__ void q4k_frag_superblock(const float* v, uint32_t* re
     const float gA = __shfl_sync(0xffffffffu, w, (2 * tq) << 2);
     const float gB = __shfl_sync(0xffffffffu, w, (2 * tq + 1) << 2);
     __syncwarp();                                   // all reads of v are done
-    // Item (j, s, t) fills words ((j*2 + s)*8 + t*2)*2 .. +3 = 4 * item: one
-    // 16-byte write per item.
+    int8_t* bytes = reinterpret_cast<int8_t*>(rec);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int item = lane + 32 * h;
-        const float e0 = it[h][0] * inv, e1 = it[h][1] * inv;
-        const float e2 = it[h][2] * inv, e3 = it[h][3] * inv;
-        *reinterpret_cast<uint4*>(rec + 4 * item) =
-            make_uint4(pack_half2(e0, e1), pack_half2(e2, e3), pack_half2(e0 - half_round(e0), e1 - half_round(e1)),
-                       pack_half2(e2 - half_round(e2), e3 - half_round(e3)));
-    }
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) bytes[(j * 4 + p) * 32 + lane] = q[j][p];
     if (lane < 8) {
         const int half = lane & 1;
         const float g0 = -gA, g1 = -gB;
         rec[256 + lane] = half == 0 ? pack_half2(g0, g1)
                                     : pack_half2(g0 - half_round(g0), g1 - half_round(g1));
     }
-    if (lane == 0) rec[264] = __float_as_uint(ldexpf(1.0f, e));
+    if (lane == 0) {
+        rec[264] = __float_as_uint(pow2f(e));
+        rec[265] = __float_as_uint(pow2f(e0));
+    }
 }
 
-// One superblock of 16 rows (rows g and g+8 at `sb0p` / `sb1p`, 144 bytes
-// each, in shared memory) dotted with the activation record `rec`.  Adds the
-// FP32 results for rows g (acc0) and g+8 (acc1); valid in lanes with t == 0.
+__device__ __forceinline__ void imma16832(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// One superblock of 16 rows (rows g and g+8 at b0p / b1p, 144 bytes each, in
+// shared memory) dotted with the activation record `rec`.  Adds this lane's
+// share of rows g (acc0) and g+8 (acc1): the row totals are the sums over
+// the four lanes t of the row group (quad_sum).
 __device__ __forceinline__ void q4k_mma_superblock(const uint8_t* __restrict__ b0p, const uint8_t* __restrict__ b1p,
                                                    const uint32_t* __restrict__ rec, float& acc0, float& acc1) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const bool bact = g < 2;
+    const bool bact = g < 4;
     const uint4 h0 = *reinterpret_cast<const uint4*>(b0p);
     const uint4 h1 = *reinterpret_cast<const uint4*>(b1p);
     uint2 q0[4], q1[4];
@@ -238,54 +256,60 @@ __device__ __forceinline__ void q4k_mma_superblock(const uint8_t* __restrict__ b
     const uint32_t sA1 = h1.y & 0x3F3F3F3Fu, sB1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
     const uint32_t mA0 = h0.z & 0x3F3F3F3Fu, mB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
     const uint32_t mA1 = h1.z & 0x3F3F3F3Fu, mB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
-    const uint32_t* xbl = rec + (t * 2 + (g & 1)) * 2;
-    // Two accumulators (even and odd chunks) halve the dependent mma chain.
-    float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const uint8_t* rb = reinterpret_cast<const uint8_t*>(rec) + g * 32 + 8 * t;
+    int lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         const uint32_t sw0 = c < 2 ? sA0 : sB0, sw1 = c < 2 ? sA1 : sB1;
-        const uint32_t jl = (2 * c) & 3, jh = (2 * c + 1) & 3;
-        const uint32_t Sl0 = hsub2u(__byte_perm(sw0, 0x64u, 0x4040u | (jl << 8) | jl), kHalfMagic);
-        const uint32_t Sl1 = hsub2u(__byte_perm(sw1, 0x64u, 0x4040u | (jl << 8) | jl), kHalfMagic);
-        uint32_t Sh0 = hsub2u(__byte_perm(sw0, 0x64u, 0x4040u | (jh << 8) | jh), kHalfMagic);
-        uint32_t Sh1 = hsub2u(__byte_perm(sw1, 0x64u, 0x4040u | (jh << 8) | jh), kHalfMagic);
-        const uint32_t Cl0 = hmul2u(Sl0, kHalfNeg1024), Cl1 = hmul2u(Sl1, kHalfNeg1024);
-        const uint32_t Ch0 = hmul2u(Sh0, kHalfNeg64), Ch1 = hmul2u(Sh1, kHalfNeg64);
-        Sh0 = hmul2u(Sh0, kHalfInv16);
-        Sh1 = hmul2u(Sh1, kHalfInv16);
-        float* dc = d[c & 1];
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            const uint32_t w0 = s ? q0[c].y : q0[c].x, w1 = s ? q1[c].y : q1[c].x;
-            const uint32_t w08 = w0 >> 8, w18 = w1 >> 8;
-            const uint32_t a0 = hfma2u((w0 & 0x000F000Fu) | kHalfMagic, Sl0, Cl0);
-            const uint32_t a1 = hfma2u((w1 & 0x000F000Fu) | kHalfMagic, Sl1, Cl1);
-            const uint32_t a2 = hfma2u((w08 & 0x000F000Fu) | kHalfMagic, Sl0, Cl0);
-            const uint32_t a3 = hfma2u((w18 & 0x000F000Fu) | kHalfMagic, Sl1, Cl1);
-            const uint2 bl = bact ? *reinterpret_cast<const uint2*>(xbl + ((2 * c) * 2 + s) * 16)
-                                  : make_uint2(0u, 0u);
-            mma16816(dc, a0, a1, a2, a3, bl.x, bl.y);
-            const uint32_t e0 = hfma2u((w0 & 0x00F000F0u) | kHalfMagic, Sh0, Ch0);
-            const uint32_t e1 = hfma2u((w1 & 0x00F000F0u) | kHalfMagic, Sh1, Ch1);
-            const uint32_t e2 = hfma2u((w08 & 0x00F000F0u) | kHalfMagic, Sh0, Ch0);
-            const uint32_t e3 = hfma2u((w18 & 0x00F000F0u) | kHalfMagic, Sh1, Ch1);
-            const uint2 bh = bact ? *reinterpret_cast<const uint2*>(xbl + ((2 * c + 1) * 2 + s) * 16)
-                                  : make_uint2(0u, 0u);
-            mma16816(dc, e0, e1, e2, e3, bh.x, bh.y);
-        }
+        const uint32_t bl = (2 * c) & 3, bh = (2 * c + 1) & 3;
+        const int sl0 = static_cast<int>(__byte_perm(sw0, 0u, 0x4440u | bl));
+        const int sl1 = static_cast<int>(__byte_perm(sw1, 0u, 0x4440u | bl));
+        const int sh0 = static_cast<int>(__byte_perm(sw0, 0u, 0x4440u | bh));
+        const int sh1 = static_cast<int>(__byte_perm(sw1, 0u, 0x4440u | bh));
+        const uint2 xl = bact ? *reinterpret_cast<const uint2*>(rb + (2 * c) * 128) : make_uint2(0u, 0u);
+        const uint2 xh = bact ? *reinterpret_cast<const uint2*>(rb + (2 * c + 1) * 128) : make_uint2(0u, 0u);
+        int dl[4], dh[4];
+        imma16832(dl, q0[c].x & 0x0F0F0F0Fu, q1[c].x & 0x0F0F0F0Fu, q0[c].y & 0x0F0F0F0Fu, q1[c].y & 0x0F0F0F0Fu,
+                  xl.x, xl.y);
+        imma16832(dh, q0[c].x & 0xF0F0F0F0u, q1[c].x & 0xF0F0F0F0u, q0[c].y & 0xF0F0F0F0u, q1[c].y & 0xF0F0F0F0u,
+                  xh.x, xh.y);
+        lo[0] += dl[0] * sl0;
+        lo[1] += dl[1] * sl0;
+        lo[2] += dl[2] * sl1;
+        lo[3] += dl[3] * sl1;
+        hi[0] += dh[0] * sh0;
+        hi[1] += dh[1] * sh0;
+        hi[2] += dh[2] * sh1;
+        hi[3] += dh[3] * sh1;
     }
     const uint32_t mw0 = t < 2 ? mA0 : mB0, mw1 = t < 2 ? mA1 : mB1;
     const uint32_t ja = (2 * t) & 3;
     const uint32_t M0 = hsub2u(__byte_perm(mw0, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
     const uint32_t M1 = hsub2u(__byte_perm(mw1, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
-    const uint32_t bm = bact ? rec[256 + t * 2 + (g & 1)] : 0u;
+    const uint32_t bm = g < 2 ? rec[256 + t * 2 + (g & 1)] : 0u;
     float d2[4] = {0.f, 0.f, 0.f, 0.f};
     mma16816(d2, M0, M1, 0u, 0u, bm, 0u);
-    const float sc = __uint_as_float(rec[264]);
-    const float dd0 = half_bits_to_float(h0.x) * sc, dm0 = half_bits_to_float(h0.x >> 16) * sc;
-    const float dd1 = half_bits_to_float(h1.x) * sc, dm1 = half_bits_to_float(h1.x >> 16) * sc;
-    acc0 = fmaf(dd0, (d[0][0] + d[1][0]) + (d[0][1] + d[1][1]), fmaf(dm0, d2[0] + d2[1], acc0));
-    acc1 = fmaf(dd1, (d[0][2] + d[1][2]) + (d[0][3] + d[1][3]), fmaf(dm1, d2[2] + d2[3], acc1));
+    // Columns 2t, 2t+1 hold pieces 2t, 2t+1: scales s0, s0/2^7 (t = 0),
+    // s0/2^14, s0/2^21 (t = 1), none for t >= 2.
+    const float s0 = __uint_as_float(rec[265]);
+    const float ca = t == 0 ? s0 : (t == 1 ? s0 * (1.0f / 16384.0f) : 0.0f);
+    const float cb = t == 0 ? s0 * (1.0f / 128.0f) : (t == 1 ? s0 * (1.0f / 2097152.0f) : 0.0f);
+    const float y0 = ca * (static_cast<float>(lo[0]) + static_cast<float>(hi[0]) * 0.0625f) +
+                     cb * (static_cast<float>(lo[1]) + static_cast<float>(hi[1]) * 0.0625f);
+    const float y1 = ca * (static_cast<float>(lo[2]) + static_cast<float>(hi[2]) * 0.0625f) +
+                     cb * (static_cast<float>(lo[3]) + static_cast<float>(hi[3]) * 0.0625f);
+    const float me = __uint_as_float(rec[264]);
+    const float dd0 = half_bits_to_float(h0.x), dm0 = half_bits_to_float(h0.x >> 16) * me;
+    const float dd1 = half_bits_to_float(h1.x), dm1 = half_bits_to_float(h1.x >> 16) * me;
+    acc0 = fmaf(dd0, y0, fmaf(dm0, d2[0] + d2[1], acc0));
+    acc1 = fmaf(dd1, y1, fmaf(dm1, d2[2] + d2[3], acc1));
+}
+
+// The row total from the four lanes t of a row group (all four lanes get it).
+__device__ __forceinline__ float quad_sum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    return v;
 }
 
 }  // namespace pokit

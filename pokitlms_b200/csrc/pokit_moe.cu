@@ -1411,15 +1411,31 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(const __gr
     cp_async_wait_all();      // the x records
     __syncthreads();
     const int g = lane >> 2;
-    float acc0 = 0.0f, acc1 = 0.0f;
-    for (uint32_t i = 0; i < nmine; ++i) {
+    const auto wait_box = [&](uint32_t i) {
         if (!mbar_wait(&mybars[i], 0)) {
             if (lane == 0) atomicOr(a.S.status, kStatusWaitTimeout);
             mbar_wait(&mybars[i], 0);          // the copy may still land: wait once more
         }
-        const uint8_t* box = mytile + i * kBoxBytes;
-        q4k_mma_superblock(box + g * 144u, box + (g + 8) * 144u, recs + (sb0 + i) * kFragWords, acc0, acc1);
+    };
+    // Superblocks two at a time with separate accumulators: two independent
+    // dependency chains per warp.
+    float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+    uint32_t i = 0;
+    for (; i + 2 <= nmine; i += 2) {
+        wait_box(i);
+        wait_box(i + 1);
+        const uint8_t* b0 = mytile + i * kBoxBytes;
+        const uint8_t* b1 = b0 + kBoxBytes;
+        q4k_mma_superblock(b0 + g * 144u, b0 + (g + 8) * 144u, recs + (sb0 + i) * kFragWords, acc0, acc1);
+        q4k_mma_superblock(b1 + g * 144u, b1 + (g + 8) * 144u, recs + (sb0 + i + 1) * kFragWords, acc2, acc3);
     }
+    if (i < nmine) {
+        wait_box(i);
+        const uint8_t* b0 = mytile + i * kBoxBytes;
+        q4k_mma_superblock(b0 + g * 144u, b0 + (g + 8) * 144u, recs + (sb0 + i) * kFragWords, acc0, acc1);
+    }
+    acc0 = quad_sum(acc0 + acc2);
+    acc1 = quad_sum(acc1 + acc3);
     if ((lane & 3) == 0) {
         part[warp * 16 + g] = acc0;
         part[warp * 16 + g + 8] = acc1;
@@ -1518,17 +1534,35 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(const __grid_
     }
     __syncthreads();
     const int g = lane >> 2;
-    for (uint32_t u = warp; u < units; u += kWarps) {
+    const auto wait_box = [&](uint32_t u) {
         if (!mbar_wait(&bars[u], 0)) {
             if (lane == 0) atomicOr(a.S.status, kStatusWaitTimeout);
             mbar_wait(&bars[u], 0);            // the copy may still land: wait once more
         }
-        const uint8_t* box = tiles + u * kBoxBytes;
-        float acc0 = 0.0f, acc1 = 0.0f;
-        q4k_mma_superblock(box + g * 144u, box + (g + 8) * 144u, recs + u * kFragWords, acc0, acc1);
+    };
+    // Units u and u + kWarps side by side (two independent chains).
+    for (uint32_t u = warp; u < units; u += 2 * kWarps) {
+        const uint32_t v2 = u + kWarps;
+        float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+        wait_box(u);
+        if (v2 < units) wait_box(v2);
+        const uint8_t* bx = tiles + u * kBoxBytes;
+        q4k_mma_superblock(bx + g * 144u, bx + (g + 8) * 144u, recs + u * kFragWords, a0, a1);
+        if (v2 < units) {
+            const uint8_t* by = tiles + v2 * kBoxBytes;
+            q4k_mma_superblock(by + g * 144u, by + (g + 8) * 144u, recs + v2 * kFragWords, b0, b1);
+        }
+        a0 = quad_sum(a0);
+        a1 = quad_sum(a1);
+        b0 = quad_sum(b0);
+        b1 = quad_sum(b1);
         if ((lane & 3) == 0) {
-            part[u * 16 + g] = acc0;
-            part[u * 16 + g + 8] = acc1;
+            part[u * 16 + g] = a0;
+            part[u * 16 + g + 8] = a1;
+            if (v2 < units) {
+                part[v2 * 16 + g] = b0;
+                part[v2 * 16 + g + 8] = b1;
+            }
         }
     }
     __syncthreads();
