@@ -11,8 +11,15 @@ attention half of each decoder layer is outside this path.
   value   decode tokens/s with inputs resident in HBM (CUDA events, max over ranks)
   e2e     the same through pokit_cuda_moe_decode_layers_host: host hidden in
           (pinned) -> device -> 48 layers -> host hidden out, every step
-  roofline  per MoE block: 22,298,624 algorithmic bytes (router 1 MiB + 8
-          experts x 2,654,208 B + 16 KiB in/out) / (step time / 48)
+  roofline  the dominant kernel, the Q4_K gate/up matvec of one MoE block:
+          14,188,544 algorithmic bytes per launch (8 experts x (gate + up)
+          x 884,736 B + 8 x-fragment records + 8 x 768 act floats out) / its
+          average device time: CUDA events around 4 x 48 back-to-back launches
+          over the 48 layers (pokit_cuda_moe_time_kernel; no expert is
+          L2-resident), taken after the timed region; traffic = DRAM bytes of
+          one launch from the committed ncu summary
+  block_roofline  per MoE block: 22,298,624 algorithmic bytes (router 1 MiB +
+          8 experts x 2,654,208 B + 16 KiB in/out) / (step time / 48)
 
 Between steps nothing is flushed: one step streams 1.07 GB of distinct expert
 and router bytes, far above the 126 MB L2.
@@ -44,9 +51,25 @@ EXPERT_BYTES = 3 * 884_736                     # gate + up + down, Q4_K
 ROUTER_BYTES = E * H * 4
 BLOCK_BYTES = ROUTER_BYTES + K_TOP * EXPERT_BYTES + 2 * H * 4
 ROUTED_BYTES = K_TOP * EXPERT_BYTES
+# gate/up kernel: 8 experts x (gate + up) Q4_K + 8 x-fragment records (1088 B)
+# in + 8 x 768 act floats out.
+GATE_UP_BYTES = K_TOP * 2 * 884_736 + (H // 256) * 1088 + K_TOP * I * 4
+TRAFFIC_FILE = ROOT / "profiles" / "gate_up_mma_q4k_h2048_e128_k8.md"
 METRIC = "decode tokens/sec and routed-expert HBM GB/s (% of peak) at 1/2/4/8 B200"
 WORKLOAD = ("qwen3-30b-a3b-shaped MoE expert path: 48 MoE FFN layers (hidden 2048, 128 experts "
             "top-8 renormalised, inter 768, Q4_K experts, F32 router), decode batch 1")
+
+
+def ncu_traffic_bytes() -> float | None:
+    """DRAM bytes (read + write) of one gate/up launch, from the committed ncu
+    summary (line 'traffic_bytes_per_launch: N')."""
+    try:
+        for line in TRAFFIC_FILE.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
 
 
 def measured_peaks() -> dict:
@@ -318,10 +341,20 @@ def main() -> None:
     e2e_s = max_over_ranks(t1 - t0)
     e2e_rate = world * e2e_steps / e2e_s
 
+    # Dominant kernel: gate/up (and down, for the record) launched back to back
+    # over all layers (CUDA events around the run), after the timed region.
+    work_dev = torch.from_numpy(synth.activation(H, SEED + rank, 777)).cuda()
+    reps = max(4 * layers, 96)
+    gate_up_us = be.time_kernel(0, 0, layers, reps, work_dev, stream)
+    down_us = be.time_kernel(1, 0, layers, reps, work_dev, stream)
+    be.synchronize(stream)
+    kernel_us = {"gate_up": gate_up_us, "down": down_us}
+
     peaks = measured_peaks()
     block_s = ms_per_step / 1e3 / layers
-    achieved = BLOCK_BYTES / block_s / 1e9
+    block_achieved = BLOCK_BYTES / block_s / 1e9
     routed_gbs = ROUTED_BYTES / block_s / 1e9
+    achieved = GATE_UP_BYTES / (gate_up_us / 1e6) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -340,10 +373,15 @@ def main() -> None:
                        "l2": "no flush: each step streams 1.07 GB of distinct weights (> 126 MB L2)"},
             "routed_expert_gbs": routed_gbs,
             "routed_expert_frac_of_peak": routed_gbs / peaks["hbm_gbs"],
-            "roofline": {"bound": "hbm", "kernel": "moe block (route + gate_up + down, 3 launches)",
+            "roofline": {"bound": "hbm", "kernel": "moe_gate_up_mma_kernel (Q4_K gate/up matvec)",
                          "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
-                         "bytes_per_launch": BLOCK_BYTES, "traffic": None},
+                         "bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": gate_up_us,
+                         "traffic": ncu_traffic_bytes()},
+            "block_roofline": {"bound": "hbm", "kernel": "moe block (2 launches per layer in the chain)",
+                               "achieved": block_achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                               "frac": block_achieved / peaks["hbm_gbs"], "bytes_per_block": BLOCK_BYTES},
+            "kernel_us": kernel_us,
             "e2e": {"value": e2e_rate, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
                     "d2h_bytes_per_step": H * 4},
             "gpu_launches": int(gpu_launches),

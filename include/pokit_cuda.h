@@ -250,6 +250,18 @@ pokit_cuda_status pokit_cuda_moe_forward(pokit_cuda_moe* moe, size_t layer, cons
                                          float* route_weights, void* stream,
                                          char* error_buffer, size_t error_capacity);
 
+/* Measurement hook for benchmarks: the average device time (microseconds) of
+ * one launch of a tensor-core path kernel (kernel 0: the Q4_K gate/up matvec,
+ * 1: the down matvec and combine), launched `repetitions` times back to back
+ * over layers [first_layer, first_layer + layer_count) cyclically, as in a
+ * decode chain (replayed from a CUDA graph, timed with CUDA events).  The routes are those of one forward of first_layer on the
+ * contents of `work` (device, hidden floats), which also receives outputs.
+ * INVALID_ARGUMENT when a layer does not use the tensor-core path. */
+pokit_cuda_status pokit_cuda_moe_time_kernel(pokit_cuda_moe* moe, uint32_t kernel, size_t first_layer,
+                                             size_t layer_count, uint32_t repetitions, float* work,
+                                             void* stream, float* average_us, char* error_buffer,
+                                             size_t error_capacity);
+
 /* Host-span variant of pokit_cuda_moe_forward: copies in, runs, copies out and
  * synchronises; returns RUNTIME_ERROR (nothing written to output) when the
  * router produced non-finite logits, as the reference throws. */

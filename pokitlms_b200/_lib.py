@@ -135,6 +135,7 @@ SIGNATURES = {
     "pokit_cuda_moe_expert_view": (C.c_int, [_VP, _SZ, C.c_uint32, _SZ, C.POINTER(_VP),
                                              C.POINTER(_SZ)]),
     "pokit_cuda_moe_forward": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_time_kernel": (C.c_int, [_VP, C.c_uint32, _SZ, _SZ, C.c_uint32, _VP, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_host": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_decode_layers": (C.c_int, [_VP, _SZ, _SZ, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_decode_layers_host": (C.c_int, [_VP, _SZ, _SZ, _VP, _VP, _ERR, _SZ]),

@@ -169,6 +169,14 @@ class CudaMoeBackend:
         call("pokit_cuda_moe_forward", self._h, layer, _ptr(x), _ptr(out), _ptr(route_ids),
              _ptr(route_weights), _stream(stream))
 
+    def time_kernel(self, kernel: int, first: int, count: int, reps: int, work, stream=None) -> float:
+        """Average device time (us) of one back-to-back launch of a tensor-core
+        kernel (0 gate/up, 1 down) over layers [first, first + count)."""
+        us = C.c_float(0.0)
+        call("pokit_cuda_moe_time_kernel", self._h, kernel, first, count, reps, _ptr(work), _stream(stream),
+             C.cast(C.pointer(us), C.c_void_p))
+        return us.value
+
     def forward_host(self, layer: int, x: np.ndarray):
         x = np.ascontiguousarray(x, dtype=np.float32)
         out = np.empty(self.hidden, dtype=np.float32)

@@ -251,6 +251,23 @@ public:
         hits_ += cfg_.top_k;
     }
 
+    // Average device time of one launch of a tensor-core kernel over the
+    // layers [first, first + count), launched back to back.
+    float time_kernel(uint32_t which, size_t first, size_t count, uint32_t reps, float* work, cudaStream_t s) {
+        ensure_ok();
+        if (count == 0 || first + count > cfg_.layers) throw std::invalid_argument("layer range out of bounds");
+        if (!work) throw std::invalid_argument("a device buffer of hidden floats is required");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        float us = 0.0f;
+        const cudaError_t e = time_moe_kernel(devs_.data() + first, static_cast<uint32_t>(count), S_, which, reps,
+                                              work, st, &us);
+        if (e == cudaErrorNotSupported) throw std::invalid_argument("the layers do not use the tensor-core path");
+        guard(e, "kernel timing");
+        kernel_launches_ += reps + 4;
+        return us;
+    }
+
     void forward_host(size_t layer, const float* x, float* out, uint32_t* ids, float* w) {
         ensure_ok();
         if (!x || !out) throw std::invalid_argument("input and output are required");
@@ -769,6 +786,18 @@ pokit_cuda_status pokit_cuda_moe_forward(pokit_cuda_moe* moe, size_t layer, cons
         if (!moe) throw std::invalid_argument("MoE handle is required");
         std::lock_guard<std::mutex> lock(moe->impl.mutex());
         moe->impl.forward(layer, input, output, route_ids, route_weights, as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_time_kernel(pokit_cuda_moe* moe, uint32_t kernel, size_t first_layer,
+                                              size_t layer_count, uint32_t repetitions, float* work,
+                                              void* stream, float* average_us, char* error_buffer,
+                                              size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe || !average_us) throw std::invalid_argument("handle and average_us are required");
+        if (kernel > 1 || repetitions == 0) throw std::invalid_argument("kernel must be 0 or 1, repetitions > 0");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        *average_us = moe->impl.time_kernel(kernel, first_layer, layer_count, repetitions, work, as_stream(stream));
     });
 }
 

@@ -91,9 +91,19 @@ cudaError_t prepare_moe_block(const MoeLayerDev& L);
 // blocks: a block may take its router partials from `prev`'s last kernel and
 // produce `next`'s (or warm L2 with `next`'s router).  `launches` (may be
 // null) receives the number of kernels launched.
+// `marks` (may be null; one more entry than kernels launched) receives an
+// event record before the first kernel and after each kernel.
 cudaError_t launch_moe_block(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
                              float* hidden, float* moe_out, const MoeLayerDev* prev,
-                             const MoeLayerDev* next, cudaStream_t stream, uint32_t* launches);
+                             const MoeLayerDev* next, cudaStream_t stream, uint32_t* launches,
+                             cudaEvent_t* marks = nullptr);
+
+// Measurement: the average device time (us) of one launch of a tensor-core
+// path kernel (which = 0 gate/up, 1 down), launched `reps` times back to back
+// over layers[0 .. count) cyclically, with the routes of one forward of
+// layers[0] (x and the output in `out`, hidden floats).
+cudaError_t time_moe_kernel(const MoeLayerDev* layers, uint32_t count, const MoeScratch& S, uint32_t which,
+                            uint32_t reps, float* out, cudaStream_t stream, float* avg_us);
 
 // Grid-wide barriers one layer of launch_moe_decode performs.
 uint32_t moe_barriers_per_layer();

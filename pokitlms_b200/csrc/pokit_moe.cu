@@ -34,6 +34,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <vector>
 
 namespace pokit {
 namespace {
@@ -1739,7 +1740,10 @@ static bool tensor_path(const MoeLayerDev& L) {
 static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
                               float* hidden, float* moe_out, const MoeLayerDev* prev,
                               const MoeLayerDev* next, cudaStream_t stream, bool dry_run,
-                              uint32_t* launches) {
+                              uint32_t* launches, cudaEvent_t* marks) {
+    const auto mark = [&](uint32_t i) {
+        if (marks) cudaEventRecord(marks[i], stream);
+    };
     if (launches) *launches = 0;
     if (!layer_valid(L)) return cudaErrorInvalidValue;
     if (!hidden && (!x_in || !moe_out)) return cudaErrorInvalidValue;
@@ -1779,16 +1783,18 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
         const uint32_t chunks = L.hidden / kPartRows;
         const uint32_t groups = L.top_k * (L.inter / 16u);
         uint32_t n = 0;
+        mark(0);
         if (!from_prev) {
             ma.m = pl;
             moe_partials_kernel<<<chunks, kThreads, pl.total, stream>>>(ma);
-            ++n;
+            mark(++n);
         }
         ma.m = gl;
         moe_gate_up_mma_kernel<<<(groups + kGuGroups - 1u) / kGuGroups, kThreads, gl.total, stream>>>(ma);
+        mark(++n);
         ma.m = dl;
         moe_down_mma_kernel<<<chunks, kThreads, dl.total, stream>>>(ma);
-        n += 2;
+        mark(++n);
         if (launches) *launches = n;
         return cudaGetLastError();
     }
@@ -1813,23 +1819,92 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
     if (e != cudaSuccess || dry_run) return e;
     BlockArgs ra = a;
     ra.m = rl;
+    mark(0);
     moe_route_kernel<<<g1, kThreads, rl.total, stream>>>(ra);
+    mark(1);
     moe_gate_up_kernel<<<sms, kThreads, a.m.total, stream>>>(a);
+    mark(2);
     moe_down_kernel<<<down_ctas, kThreads, a.m.total, stream>>>(a);
+    mark(3);
     if (launches) *launches = 3;
     return cudaGetLastError();
 }
 
 cudaError_t launch_moe_block(const MoeLayerDev& L, const MoeScratch& S, const float* x_in,
                              float* hidden, float* moe_out, const MoeLayerDev* prev,
-                             const MoeLayerDev* next, cudaStream_t stream, uint32_t* launches) {
-    return block_impl(L, S, x_in, hidden, moe_out, prev, next, stream, false, launches);
+                             const MoeLayerDev* next, cudaStream_t stream, uint32_t* launches,
+                             cudaEvent_t* marks) {
+    return block_impl(L, S, x_in, hidden, moe_out, prev, next, stream, false, launches, marks);
+}
+
+cudaError_t time_moe_kernel(const MoeLayerDev* layers, uint32_t count, const MoeScratch& S, uint32_t which,
+                            uint32_t reps, float* out, cudaStream_t stream, float* avg_us) {
+    if (!layers || count == 0 || reps == 0 || !out || !avg_us || which > 1) return cudaErrorInvalidValue;
+    for (uint32_t l = 0; l < count; ++l)
+        if (!tensor_path(layers[l])) return cudaErrorNotSupported;
+    // Routes, x records and scale of layers[0] for every launch.
+    cudaError_t e = block_impl(layers[0], S, out, nullptr, out, nullptr, nullptr, stream, false, nullptr, nullptr);
+    if (e != cudaSuccess) return e;
+    std::vector<MmaArgs> args(count);
+    for (uint32_t l = 0; l < count; ++l) {
+        const MoeLayerDev& L = layers[l];
+        MmaArgs& ma = args[l];
+        const uint64_t rb_in = static_cast<uint64_t>(L.hidden >> 8) * 144u;
+        const uint64_t rb_down = static_cast<uint64_t>(L.inter >> 8) * 144u;
+        if (!encode_expert_map(&ma.tm_gate, L.gate, rb_in, L.inter, L.experts, L.gate_slice) ||
+            !encode_expert_map(&ma.tm_up, L.up, rb_in, L.inter, L.experts, L.up_slice) ||
+            !encode_expert_map(&ma.tm_down, L.down, rb_down, L.hidden, L.experts, L.down_slice))
+            return cudaErrorInvalidValue;
+        ma.L = L;
+        ma.next = L;
+        ma.S = S;
+        ma.x_in = out;
+        ma.moe_out = out;
+        ma.m = which == 0 ? mma_gate_up_layout(L) : mma_down_layout(L, L);
+    }
+    const uint32_t groups = layers[0].top_k * (layers[0].inter / 16u);
+    const uint32_t g_gate_up = (groups + kGuGroups - 1u) / kGuGroups, g_down = layers[0].hidden / kPartRows;
+    // The repetitions replay from a CUDA graph (captured on a private stream)
+    // so the host launch rate does not pace the device.
+    e = cudaStreamSynchronize(stream);
+    cudaStream_t cap = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        for (uint32_t i = 0; i < reps; ++i) {
+            const MmaArgs& ma = args[i % count];
+            if (which == 0) moe_gate_up_mma_kernel<<<g_gate_up, kThreads, ma.m.total, cap>>>(ma);
+            else moe_down_mma_kernel<<<g_down, kThreads, ma.m.total, cap>>>(ma);
+        }
+        const cudaError_t end = cudaStreamEndCapture(cap, &graph);
+        e = end;
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, cap);          // warm-up replay
+    if (e == cudaSuccess) e = cudaEventCreate(&a);
+    if (e == cudaSuccess) e = cudaEventCreate(&b);
+    if (e == cudaSuccess) e = cudaEventRecord(a, cap);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, cap);
+    if (e == cudaSuccess) e = cudaEventRecord(b, cap);
+    if (e == cudaSuccess) e = cudaEventSynchronize(b);
+    float ms = 0.0f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+    if (a) cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (cap) cudaStreamDestroy(cap);
+    if (e == cudaSuccess) *avg_us = ms * 1e3f / static_cast<float>(reps);
+    return e;
 }
 
 cudaError_t prepare_moe_block(const MoeLayerDev& L) {
     MoeScratch none;
     float dummy = 0.0f;
-    cudaError_t e = block_impl(L, none, &dummy, nullptr, &dummy, nullptr, nullptr, nullptr, true, nullptr);
+    cudaError_t e = block_impl(L, none, &dummy, nullptr, &dummy, nullptr, nullptr, nullptr, true, nullptr, nullptr);
     if (e != cudaSuccess) return e;
     const SmemLayout m = make_layout(L, static_cast<uint32_t>(device_sm_count()));
     if (m.total > 227u * 1024u) return cudaErrorInvalidValue;
