@@ -34,6 +34,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <type_traits>
 #include <vector>
 
 namespace pokit {
@@ -43,7 +44,8 @@ constexpr int kThreads = 384;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRouteColsPerWarp = 512;
 constexpr uint32_t kMaxRouteSplits = 8;       // route_warp: hidden <= 8 * 512
-constexpr uint32_t kRouteWarpMaxSlots = 16;   // route_warp: experts <= 16 * 32
+constexpr uint32_t kRouteWarpMaxSlots = 8;    // tensor-core path routing: experts <= 8 * 32
+constexpr uint32_t kTailLogitWarps = 4;       // routing tail: warps reading the accumulators
 constexpr int kMaxTopK = 64;
 constexpr int kMaxExperts = 1024;
 constexpr int kSbChunk = 8;                 // gate/up superblocks whose loads go out together
@@ -517,18 +519,15 @@ __device__ __forceinline__ uint32_t route_ord(float v) {
 }
 
 template <uint32_t kSlots>
-__device__ void route_select(const MoeLayerDev& L, const float* lg, float shared_logit, uint32_t* sel_id,
-                             float* sel_w, uint32_t* status, bool writer, const MoeScratch& S) {
+__device__ void route_select_regs(const MoeLayerDev& L, const float (&lgv)[kSlots], float shared_logit,
+                                  uint32_t* sel_id, float* sel_w, uint32_t* status, bool writer,
+                                  const MoeScratch& S) {
     const int lane = threadIdx.x & 31;
     const uint32_t E = L.experts, k = L.top_k;
-    float lgv[kSlots];
     int bad = 0;
 #pragma unroll
-    for (uint32_t i = 0; i < kSlots; ++i) {
-        const uint32_t e = lane + 32u * i;
-        lgv[i] = e < E ? lg[e] : 0.0f;
-        if (e < E) bad |= !isfinite(lgv[i]);
-    }
+    for (uint32_t i = 0; i < kSlots; ++i)
+        if (lane + 32u * i < E) bad |= !isfinite(lgv[i]);
     bad = __any_sync(0xffffffffu, bad);
     if (writer) {
 #pragma unroll
@@ -607,12 +606,7 @@ __device__ void route_select(const MoeLayerDev& L, const float* lg, float shared
     }
 }
 
-__device__ __forceinline__ void route_select_any(const MoeLayerDev& L, const float* lg, uint32_t* sel_id,
-                                                 float* sel_w, uint32_t* status, bool writer, const MoeScratch& S) {
-    if (L.experts <= 128u) route_select<4>(L, lg, 0.0f, sel_id, sel_w, status, writer, S);
-    else if (L.experts <= 256u) route_select<8>(L, lg, 0.0f, sel_id, sel_w, status, writer, S);
-    else route_select<kRouteWarpMaxSlots>(L, lg, 0.0f, sel_id, sel_w, status, writer, S);
-}
+
 
 // ---------------------------------------------------------------------------
 // Expert slot matrices.
@@ -1110,49 +1104,20 @@ __device__ __forceinline__ void racc_add(unsigned long long* limbs, uint32_t* ba
     if (hi) atomicAdd(limbs + i + 1, static_cast<unsigned long long>(hi));
 }
 
-// The accumulated value, carries resolved; the three limbs from the most
-// significant non-trivial one are combined in double (53 bits, below which
-// the float result cannot change by more than its last-place rounding), then
-// rounded to float.  The limbs are left zero.
-__device__ __forceinline__ float racc_take(unsigned long long* limbs) {
-    long long l[kRaccLimbs];
-    const ulonglong2* p = reinterpret_cast<const ulonglong2*>(limbs);
+// The accumulated value of the limbs (as loaded): Horner's rule in double from
+// the top limb, without resolving carries first.  Each step is exact until
+// the running value passes 2^53, after which every step rounds relative to
+// the value itself, so the float result is within one unit in the last place
+// of the exact sum and depends only on the limbs (not on arrival order).
+__device__ __forceinline__ float racc_value(const ulonglong2 (&v)[kRaccLimbs / 2]) {
+    double d = static_cast<double>(static_cast<long long>(v[kRaccLimbs / 2 - 1].y));
 #pragma unroll
-    for (int i = 0; i < kRaccLimbs / 2; ++i) {
-        const ulonglong2 v = __ldcg(p + i);
-        l[2 * i] = static_cast<long long>(v.x);
-        l[2 * i + 1] = static_cast<long long>(v.y);
+    for (int i = kRaccLimbs - 2; i >= 0; --i) {
+        const unsigned long long li = (i & 1) ? v[i / 2].y : v[i / 2].x;
+        d = fma(d, 4294967296.0, static_cast<double>(static_cast<long long>(li)));
     }
-    ulonglong2* q = reinterpret_cast<ulonglong2*>(limbs);
-#pragma unroll
-    for (int i = 0; i < kRaccLimbs / 2; ++i) q[i] = make_ulonglong2(0ull, 0ull);
-#pragma unroll
-    for (int i = 0; i + 1 < kRaccLimbs; ++i) {
-        const long long carry = l[i] >> 32;
-        l[i] -= carry * 4294967296ll;
-        l[i + 1] += carry;
-    }
-    // Limbs 0..6 are now in [0, 2^32); the top limb carries the sign.  The
-    // highest limb that is not a pure sign extension (0 or -1 above a limb
-    // with the matching top bit) leads; unrolled so the limbs stay in
-    // registers.
-    int j = kRaccLimbs - 1;
-#pragma unroll
-    for (int i = kRaccLimbs - 1; i > 2; --i) {
-        if (j == i && (l[i] == 0 || l[i] == -1) && ((l[i - 1] >> 31) & 1) == (l[i] & 1)) {
-            if (l[i] == -1) l[i - 1] -= 4294967296ll;
-            j = i - 1;
-        }
-    }
-    long long top = 0, mid = 0, low = 0;
-#pragma unroll
-    for (int i = 2; i < kRaccLimbs; ++i)
-        if (i == j) { top = l[i]; mid = l[i - 1]; low = l[i - 2]; }
-    const double d = (static_cast<double>(top) * 4294967296.0 + static_cast<double>(mid)) * 4294967296.0 +
-                     static_cast<double>(low);
-    // 2^(32 (j - 2) + kRaccBase) built from its exponent bits (normal range).
-    const double unit = __longlong_as_double(static_cast<long long>(1023 + 32 * (j - 2) + kRaccBase) << 52);
-    return static_cast<float>(d * unit);
+    // 2^kRaccBase from its exponent bits.
+    return static_cast<float>(d * __longlong_as_double(static_cast<long long>(1023 + kRaccBase) << 52));
 }
 
 // Shared memory of the routing tail (run by the last CTA of the partials
@@ -1166,7 +1131,7 @@ __host__ __device__ inline TailLayout tail_layout(const MoeLayerDev& L, uint32_t
     t.lg = off; off += al16(L.experts * 4u);
     t.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
     t.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
-    t.stage = off; off += (kWarps - 1u) * 1024u;
+    t.stage = off; off += (kWarps - kTailLogitWarps) * 1024u;
     t.end = off;
     return t;
 }
@@ -1249,73 +1214,93 @@ __device__ __forceinline__ float router_dot16(const RouterSlice& r, const float*
     return p;
 }
 
+// The routing tail's selection in warp 0 (lane l owns experts l, l + 32, ...):
+// the rms scale from the per-chunk sums of squares (hidden_mode), the exact
+// logits from the accumulators (left zero), then route_select_regs.  The
+// selection order does not depend on the scale, which only enters the
+// weights.  Writes S.scale.
 // The routing tail of block L, run by the one CTA that finished last after
-// every chunk added its router partials: logits = s * (fixed-point sum of the
-// partial dots), s the rms_norm scale from the per-chunk sums of squares (1
-// for a normalised input); the routes (published to S.ids / S.weights /
-// S.logits); s (S.scale); and the fragment records of x' = ffn_norm * hidden
-// (or x_in) for the gate/up kernel (S.xrec).  The accumulators are left zero.
+// every chunk added its router partials.  Warps 0..kTailLogitWarps-1 read the
+// accumulators (one expert per lane, leaving them zero) into exact-order-free
+// logits in shared memory, warp 0 also the per-chunk sums of squares for the
+// rms scale (1 for a normalised input); after a barrier of those warps, warp
+// 0 selects the routes and publishes them with the scale (S.ids / S.weights /
+// S.logits / S.scale).  The other warps build the fragment records of
+// x' = ffn_norm * hidden (or x_in) for the gate/up kernel (S.xrec).  The
+// selection order does not depend on the scale, which only enters the
+// weights.
 __device__ void route_tail(const MoeLayerDev& L, const MoeScratch& S, const float* x, bool hidden_mode,
                            uint8_t* smem, const TailLayout& t) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t E = L.experts, H = L.hidden, nsb = H >> 8, chunks = H / kPartRows;
-    float* lg = reinterpret_cast<float*>(smem + t.lg);
-    uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + t.sel_id);
-    float* sel_w = reinterpret_cast<float*>(smem + t.sel_w);
-    __shared__ float red[kWarps];
-    __shared__ uint32_t bad_flag;
-    // Loads first: this warp's first record (warps 1.. build records), the
-    // accumulated dots and the per-chunk sums of squares.
-    const uint32_t builders = static_cast<uint32_t>(kWarps) - 1u;
-    const uint32_t q0 = static_cast<uint32_t>(warp) - 1u;
-    const bool rec_now = warp >= 1 && q0 < nsb;
-    float hv[8], nv[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (warp < static_cast<int>(kTailLogitWarps)) {
+        float* lg = reinterpret_cast<float*>(smem + t.lg);
+        const uint32_t E = L.experts;
+        __shared__ float tail_scale;
+        __shared__ uint32_t tail_bad;
+        if (warp == 0) {
+            const uint32_t chunks = L.hidden / kPartRows;
+            float sq = 0.0f;
+            for (uint32_t c = lane; c < chunks; c += 32) sq += __ldcg(S.rsq + c);
+            uint32_t bad = lane == 0 ? __ldcg(S.rbad) : 0u;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const uint32_t i = q0 * 256u + 32u * j + lane;
-        hv[j] = rec_now ? __ldcg(x + i) : 0.0f;
-        nv[j] = (rec_now && hidden_mode) ? __ldg(L.ffn_norm + i) : 1.0f;
-    }
-    float sq = 0.0f;
-    for (uint32_t c = tid; c < chunks; c += kThreads) sq += __ldcg(S.rsq + c);
-    for (uint32_t e = tid; e < E; e += kThreads) lg[e] = racc_take(S.racc + static_cast<uint64_t>(e) * kRaccLimbs);
-    if (tid == 0) {
-        bad_flag = __ldcg(S.rbad);
-        *S.rbad = 0u;
-    }
-    // Records of x' (warps 1..): staged per warp, built straight into S.xrec.
-    if (warp >= 1) {
-        float* stage = reinterpret_cast<float*>(smem + t.stage) + q0 * 256u;
-        for (uint32_t q = q0; q < nsb; q += builders) {
-            if (q != q0) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t i = q * 256u + 32u * j + lane;
-                    hv[j] = __ldcg(x + i);
-                    nv[j] = hidden_mode ? __ldg(L.ffn_norm + i) : 1.0f;
-                }
+            for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            if (lane == 0) {
+                // rms_norm scale (src/rms_norm.cpp:20-26).
+                tail_scale = hidden_mode ? 1.0f / sqrtf(sq / static_cast<float>(L.hidden) + L.rms_eps) : 1.0f;
+                tail_bad = bad;
+                if (bad) *S.rbad = 0u;
             }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) stage[32 * j + lane] = hidden_mode ? nv[j] * hv[j] : hv[j];
-            __syncwarp();
-            q4k_frag_superblock(stage, S.xrec + q * kFragWords, lane);
-            __syncwarp();
         }
+        for (uint32_t e0 = warp * 32u; e0 < E; e0 += kTailLogitWarps * 32u) {
+            const uint32_t e = e0 + lane;
+            ulonglong2 limbs[kRaccLimbs / 2];
+            ulonglong2* p = reinterpret_cast<ulonglong2*>(S.racc + static_cast<uint64_t>(e) * kRaccLimbs);
+#pragma unroll
+            for (int h = 0; h < kRaccLimbs / 2; ++h) limbs[h] = e < E ? __ldcg(p + h) : make_ulonglong2(0ull, 0ull);
+            if (e < E) {
+#pragma unroll
+                for (int h = 0; h < kRaccLimbs / 2; ++h) p[h] = make_ulonglong2(0ull, 0ull);
+                lg[e] = racc_value(limbs);
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kTailLogitWarps * 32u) : "memory");
+        if (warp != 0) return;
+        uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + t.sel_id);
+        float* sel_w = reinterpret_cast<float*>(smem + t.sel_w);
+        const float scale = tail_scale;
+        const bool bad = tail_bad != 0u;
+        const auto select = [&](auto slots) {
+            constexpr uint32_t kSlots = decltype(slots)::value;
+            float lgv[kSlots];
+#pragma unroll
+            for (uint32_t i = 0; i < kSlots; ++i) {
+                const uint32_t e = lane + 32u * i;
+                lgv[i] = e < E ? (bad ? __int_as_float(0x7fc00000) : lg[e] * scale) : 0.0f;
+            }
+            route_select_regs<kSlots>(L, lgv, 0.0f, sel_id, sel_w, S.status, true, S);
+        };
+        if (E <= 128u) select(std::integral_constant<uint32_t, 4>{});
+        else select(std::integral_constant<uint32_t, kRouteWarpMaxSlots>{});
+        if (lane == 0) *S.scale = scale;
+        return;
     }
-    // rms_norm scale (src/rms_norm.cpp:20-26).
-    sq = warp_sum(sq);
-    if (lane == 0) red[warp] = sq;
-    __syncthreads();
-    float scale = 1.0f;
-    if (hidden_mode) {
-        float total = 0.0f;
-        for (int w = 0; w < kWarps; ++w) total += red[w];
-        scale = 1.0f / sqrtf(total / static_cast<float>(H) + L.rms_eps);
+    const uint32_t nsb = L.hidden >> 8, builders = static_cast<uint32_t>(kWarps) - kTailLogitWarps;
+    const uint32_t b = static_cast<uint32_t>(warp) - kTailLogitWarps;
+    float* stage = reinterpret_cast<float*>(smem + t.stage) + b * 256u;
+    for (uint32_t q = b; q < nsb; q += builders) {
+        float hv[8], nv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t i = q * 256u + 32u * j + lane;
+            hv[j] = __ldcg(x + i);
+            nv[j] = hidden_mode ? __ldg(L.ffn_norm + i) : 1.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = hidden_mode ? nv[j] * hv[j] : hv[j];
+        __syncwarp();
+        q4k_frag_superblock(stage, S.xrec + q * kFragWords, lane);
+        __syncwarp();
     }
-    for (uint32_t e = tid; e < E; e += kThreads) lg[e] = bad_flag ? __int_as_float(0x7fc00000) : lg[e] * scale;
-    __syncthreads();
-    if (warp == 0) route_select_any(L, lg, sel_id, sel_w, S.status, true, S);
-    if (tid == 0) *S.scale = scale;
 }
 
 // Returns true in every thread of the CTA that arrives last at `count`
