@@ -114,6 +114,14 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before its predecessor in the stream ends;
+// grid_dep_wait blocks until the predecessor grid has completed and its
+// writes are visible, grid_dep_launch lets the successor start launching.
+// Both are no-ops for a normal launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // A superblock box: 16 rows x 144 bytes, rows 144 bytes apart in shared
 // memory.  With that pitch the (row g, lane t) 8-byte reads of a fragment
 // fall on distinct bank pairs two lanes at a time: two wavefronts, the

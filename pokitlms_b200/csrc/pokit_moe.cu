@@ -1323,6 +1323,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_partials_kernel(const __grid_
     const MoeLayerDev& L = a.L;
     const uint32_t c = blockIdx.x, j0 = c * kPartRows;
     const float* x = a.hidden ? a.hidden : a.x_in;
+    grid_dep_launch();
     if (threadIdx.x < 32) {
         const uint32_t r = threadIdx.x & 15u;
         const float h = __ldcg(x + j0 + r);
@@ -1357,13 +1358,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(const __gr
     const uint32_t H = L.hidden, I = L.inter, nsb = m.nsb, per_slot = I / 16u;
     const uint32_t groups = L.top_k * per_slot;
 
-    for (uint32_t p = tid; p < nsb * (kFragWords / 4u); p += kThreads)
-        cp_async16(recs + p * 4u, a.S.xrec + p * 4u);
-    cp_async_commit();
     if (lane == 0) {
         for (uint32_t i = 0; i < m.boxes; ++i) mbar_init(&bars[warp * m.boxes + i], 1);
         mbar_fence_init();
     }
+    // Launched early behind the routing tail of the previous kernel: nothing
+    // above reads its results.  The down kernel may launch once every CTA is
+    // past this point (the routes it reads are then complete).
+    grid_dep_wait();
+    grid_dep_launch();
+    for (uint32_t p = tid; p < nsb * (kFragWords / 4u); p += kThreads)
+        cp_async16(recs + p * 4u, a.S.xrec + p * 4u);
+    cp_async_commit();
     for (uint32_t r = tid; r < L.top_k; r += kThreads) sel_id[r] = __ldcg(a.S.ids + r);
     const float scale = __ldcg(a.S.scale);
     __syncthreads();
@@ -1387,6 +1393,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(const __gr
                        &mybars[i]);
         }
     }
+    // Warm L2 with the next block's router slice the down CTA with this index
+    // reads (16 floats of every expert row).
+    if (a.has_next && blockIdx.x < H / kPartRows)
+        for (uint32_t e = tid; e < a.next.experts; e += kThreads)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.next.router + static_cast<uint64_t>(e) * H +
+                                                          blockIdx.x * kPartRows));
     // Warm L2 with the down rows of the down CTA with this index.
     if (blockIdx.x < H / 16u && tid < static_cast<int>(L.top_k)) {
         const uint64_t rd = static_cast<uint64_t>(I >> 8) * 144u;
@@ -1441,7 +1453,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(const __gr
 // Kernel 3 (tensor-core path): 16 rows of the block output per CTA; in a
 // decode chain also the next block's router partials for those rows, and in
 // the CTA that finishes last the next block's routing tail.
-__global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(const __grid_constant__ MmaArgs a) {
+// At most 88 registers a thread: with the gate/up kernel's 80 both CTAs fit
+// one SM's register file, so the down grid can start behind the gate/up one.
+__global__ void __maxnreg__(88) moe_down_mma_kernel(const __grid_constant__ MmaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t flag;
     const MoeLayerDev& L = a.L;
@@ -1458,6 +1472,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(const __grid_
     const uint32_t units = k * nsb;
     const uint32_t j0 = blockIdx.x * 16u;
     const MoeLayerDev& N = a.next;
+    // Launched early behind the gate/up kernel: the routes, the residual and
+    // the weights are complete; act is read after grid_dep_wait.  The next
+    // gate/up kernel may launch right away (it waits for this grid).
+    grid_dep_launch();
 
     for (uint32_t r = tid; r < k; r += kThreads) {
         sel_id[r] = __ldcg(a.S.ids + r);
@@ -1474,17 +1492,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(const __grid_
     const bool slice_now = a.has_next && static_cast<uint32_t>(tid) < N.experts;
     RouterSlice rs{};
     if (slice_now) rs = router_slice(N.router, H, tid, blockIdx.x);
-    // Activation values of this warp's records (q = warp, warp + kWarps, ...
-    // of k * nsb), requested before the routes arrive.
-    constexpr int kRecPerWarp = 2;
-    float v[kRecPerWarp][8];
-#pragma unroll
-    for (int i = 0; i < kRecPerWarp; ++i) {
-        const uint32_t q = warp + i * kWarps;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            v[i][j] = q < units ? __ldcg(a.S.act + static_cast<uint64_t>(q) * 256u + 32 * j + lane) : 0.0f;
-    }
     __syncthreads();
     // Box (slot, superblock) u = slot * nsb + sb on mbarrier u.
     if (static_cast<uint32_t>(warp) < k && lane == 0) {
@@ -1494,6 +1501,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_mma_kernel(const __grid_
             mbar_expect_tx(&bars[u], kBoxBytes);
             tma_box_3d(tiles + u * kBoxBytes, &a.tm_down, static_cast<int>(sb * 144u), static_cast<int>(j0), id, &bars[u]);
         }
+    }
+    grid_dep_wait();          // act of the gate/up kernel
+    // Activation values of this warp's records (q = warp, warp + kWarps, ...
+    // of k * nsb).
+    constexpr int kRecPerWarp = 2;
+    float v[kRecPerWarp][8];
+#pragma unroll
+    for (int i = 0; i < kRecPerWarp; ++i) {
+        const uint32_t q = warp + i * kWarps;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            v[i][j] = q < units ? __ldcg(a.S.act + static_cast<uint64_t>(q) * 256u + 32 * j + lane) : 0.0f;
     }
     // Records staged in their own space, then built in place.
 #pragma unroll
@@ -1775,10 +1794,38 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
             mark(++n);
         }
         ma.m = gl;
-        moe_gate_up_mma_kernel<<<(groups + kGuGroups - 1u) / kGuGroups, kThreads, gl.total, stream>>>(ma);
+        {
+            // The gate/up grid may launch while the routing tail (one CTA of
+            // the previous kernel) finishes; it waits for it in-kernel.
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3((groups + kGuGroups - 1u) / kGuGroups);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = gl.total;
+            cfg.stream = stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = marks ? 0 : 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            const cudaError_t le = cudaLaunchKernelEx(&cfg, moe_gate_up_mma_kernel, ma);
+            if (le != cudaSuccess) return le;
+        }
         mark(++n);
         ma.m = dl;
-        moe_down_mma_kernel<<<chunks, kThreads, dl.total, stream>>>(ma);
+        {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(chunks);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = dl.total;
+            cfg.stream = stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = marks ? 0 : 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            const cudaError_t le = cudaLaunchKernelEx(&cfg, moe_down_mma_kernel, ma);
+            if (le != cudaSuccess) return le;
+        }
         mark(++n);
         if (launches) *launches = n;
         return cudaGetLastError();
