@@ -64,6 +64,10 @@ struct MoeScratch {
     // per-chunk sums of squares [hidden / 16], the out-of-range flag, x'
     // fragment records, the rms scale and the routing-tail counter (racc, rbad
     // and route_count are zero between launches).
+    // The activations written in `rep` replicas [rep][top_k * inter] so the
+    // down kernel's CTAs spread their reads (CTA b reads copy b % rep).
+    uint32_t rep = 1;
+    float* actr = nullptr;
     unsigned long long* racc = nullptr;
     float* rsq = nullptr;
     uint32_t* rbad = nullptr;
@@ -74,10 +78,12 @@ struct MoeScratch {
     uint32_t* status = nullptr;    // sticky StatusBits
 };
 
-// Scratch sizing helper (bytes), shared by the allocator and the no-alloc path.
-uint64_t moe_scratch_bytes(const MoeLayerDev& L);
-// Carves `base` (256-byte aligned, moe_scratch_bytes(L) long) into a MoeScratch.
-MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base);
+// Scratch sizing helper (bytes) for `rep` activation replicas, shared by the
+// allocator and the no-alloc path.
+constexpr uint32_t kActReplicas = 8;
+uint64_t moe_scratch_bytes(const MoeLayerDev& L, uint32_t rep = kActReplicas);
+// Carves `base` (256-byte aligned, moe_scratch_bytes(L, rep) long) into a MoeScratch.
+MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base, uint32_t rep = kActReplicas);
 
 // Validates the block's shapes and raises the kernels' shared-memory limits
 // without launching anything; call once per configuration before capturing

@@ -1445,7 +1445,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_mma_kernel(const __gr
             const float gv = part[(gl * 4 + 0) * 16 + r] + part[(gl * 4 + 1) * 16 + r];
             const float uv = part[(gl * 4 + 2) * 16 + r] + part[(gl * 4 + 3) * 16 + r];
             const uint32_t slot = rgx / per_slot, row0 = (rgx % per_slot) * 16u;
-            a.S.act[slot * I + row0 + r] = silu_mul(gv * scale, uv * scale, L.flavour);
+            const float av = silu_mul(gv * scale, uv * scale, L.flavour);
+            for (uint32_t cp = 0; cp < a.S.rep; ++cp)
+                a.S.actr[static_cast<uint64_t>(cp) * L.top_k * I + slot * I + row0 + r] = av;
         }
     }
 }
@@ -1504,7 +1506,8 @@ __global__ void __maxnreg__(88) moe_down_mma_kernel(const __grid_constant__ MmaA
     }
     grid_dep_wait();          // act of the gate/up kernel
     // Activation values of this warp's records (q = warp, warp + kWarps, ...
-    // of k * nsb).
+    // of k * nsb), from this CTA's replica.
+    const float* act = a.S.actr + static_cast<uint64_t>(blockIdx.x % a.S.rep) * k * L.inter;
     constexpr int kRecPerWarp = 2;
     float v[kRecPerWarp][8];
 #pragma unroll
@@ -1512,7 +1515,7 @@ __global__ void __maxnreg__(88) moe_down_mma_kernel(const __grid_constant__ MmaA
         const uint32_t q = warp + i * kWarps;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            v[i][j] = q < units ? __ldcg(a.S.act + static_cast<uint64_t>(q) * 256u + 32 * j + lane) : 0.0f;
+            v[i][j] = q < units ? __ldcg(act + static_cast<uint64_t>(q) * 256u + 32 * j + lane) : 0.0f;
     }
     // Records staged in their own space, then built in place.
 #pragma unroll
@@ -1533,7 +1536,7 @@ __global__ void __maxnreg__(88) moe_down_mma_kernel(const __grid_constant__ MmaA
     for (uint32_t q = warp + kRecPerWarp * kWarps; q < units; q += kWarps) {
         float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = __ldcg(a.S.act + static_cast<uint64_t>(q) * 256u + 32 * j + lane);
+        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = __ldcg(act + static_cast<uint64_t>(q) * 256u + 32 * j + lane);
         __syncwarp();
         q4k_frag_superblock(stage, recs + q * kFragWords, lane);
     }
@@ -1635,7 +1638,7 @@ uint32_t block_down_ctas(const MoeLayerDev& L) { return (L.hidden + 15u) / 16u; 
 
 uint32_t moe_barriers_per_layer() { return 3u; }
 
-uint64_t moe_scratch_bytes(const MoeLayerDev& L) {
+uint64_t moe_scratch_bytes(const MoeLayerDev& L, uint32_t rep) {
     const uint64_t slots = L.top_k + 1u;
     uint64_t b = 0;
     b += align256(L.hidden * 4u);                                         // x
@@ -1645,6 +1648,7 @@ uint64_t moe_scratch_bytes(const MoeLayerDev& L) {
     b += align256(slots * 4u);                                            // weights
     b += align256(slots * max_inter_of(L) * 4u);                          // act
     b += align256((L.hidden >> 8) * kFragWords * 4u);                     // xrec
+    b += align256(static_cast<uint64_t>(rep) * L.top_k * L.inter * 4u);  // actr
     b += align256(4u);                                                    // scale
     b += align256((L.hidden / kPartRows) * 4u);                           // rsq
     b += align256(L.experts * kRaccLimbs * 8u);                           // racc
@@ -1655,7 +1659,7 @@ uint64_t moe_scratch_bytes(const MoeLayerDev& L) {
     return b;
 }
 
-MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base) {
+MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base, uint32_t rep) {
     const uint64_t slots = L.top_k + 1u;
     uint8_t* p = static_cast<uint8_t*>(base);
     MoeScratch s;
@@ -1666,6 +1670,8 @@ MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base) {
     s.weights = reinterpret_cast<float*>(p); p += align256(slots * 4u);
     s.act = reinterpret_cast<float*>(p); p += align256(slots * max_inter_of(L) * 4u);
     s.xrec = reinterpret_cast<uint32_t*>(p); p += align256((L.hidden >> 8) * kFragWords * 4u);
+    s.rep = rep;
+    s.actr = reinterpret_cast<float*>(p); p += align256(static_cast<uint64_t>(rep) * L.top_k * L.inter * 4u);
     s.scale = reinterpret_cast<float*>(p); p += align256(4u);
     s.rsq = reinterpret_cast<float*>(p); p += align256((L.hidden / kPartRows) * 4u);
     // racc .. status end the carve and must be zero before a launch.

@@ -130,14 +130,17 @@ extern "C" pokit_cuda_status pokit_cuda_moe_forward_static_scratch(
     try {
         if (!block || !input || !output) throw std::invalid_argument("block, input and output are required");
         const pokit::MoeLayerDev L = to_layer(*block);
-        const uint64_t need = pokit::moe_scratch_bytes(L);
+        // As many activation replicas as fit (at least one).
+        uint32_t rep = pokit::kActReplicas;
+        while (rep > 1 && pokit::moe_scratch_bytes(L, rep) > kStaticScratchBytes) rep /= 2;
+        const uint64_t need = pokit::moe_scratch_bytes(L, rep);
         if (need > kStaticScratchBytes)
             throw std::invalid_argument("MoE block needs " + std::to_string(need) +
                                         " bytes of scratch, above the static scratch limit of " +
                                         std::to_string(kStaticScratchBytes) + " bytes");
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
         void* base = scratch_for_current_device();
-        const pokit::MoeScratch S = pokit::moe_scratch_carve(L, base);
+        const pokit::MoeScratch S = pokit::moe_scratch_carve(L, base, rep);
         check(pokit::prepare_moe_block(L), "prepare MoE kernels");
         // The router accumulators, the counters and the status word end the
         // carve: one clear covers them.
