@@ -250,6 +250,38 @@ pokit_cuda_status pokit_cuda_moe_forward(pokit_cuda_moe* moe, size_t layer, cons
                                          float* route_weights, void* stream,
                                          char* error_buffer, size_t error_capacity);
 
+/* Activation element type of a batched forward's input rows. */
+typedef enum pokit_cuda_input_type {
+    POKIT_CUDA_INPUT_F32 = 0,
+    POKIT_CUDA_INPUT_BF16 = 1
+} pokit_cuda_input_type;
+
+/* A batch of `tokens` (1..65536) rows through one MoE block on device
+ * pointers: output[t] = MoE(input[t]) for each row independently, the same
+ * block as pokit_cuda_moe_forward (the reference runs a prompt's tokens one
+ * forward_into call at a time, src/qwen3_moe_runner.cpp:785-790).
+ * input: [tokens][hidden] of input_type.  router_logits (may be NULL):
+ * [tokens][experts] F32 logits to route by instead of the layer's router.
+ * route_ids / route_weights (may be NULL): [tokens][top_k].
+ * Layers with Q4_K gate/up/down experts and no shared expert run the
+ * grouped-expert tensor-core GEMM (tokens sorted by expert, one GEMM tile per
+ * <= 64 tokens of an expert); other layers run the single-token block per row
+ * and then require F32 input and router_logits == NULL.  Asynchronous. */
+pokit_cuda_status pokit_cuda_moe_forward_batch(pokit_cuda_moe* moe, size_t layer, const void* input,
+                                               uint32_t input_type, size_t tokens,
+                                               const float* router_logits, float* output,
+                                               uint32_t* route_ids, float* route_weights, void* stream,
+                                               char* error_buffer, size_t error_capacity);
+
+/* Host-span variant of pokit_cuda_moe_forward_batch: copies in, runs, copies
+ * out and synchronises (RUNTIME_ERROR for non-finite router logits). */
+pokit_cuda_status pokit_cuda_moe_forward_batch_host(pokit_cuda_moe* moe, size_t layer,
+                                                    const void* input_host, uint32_t input_type,
+                                                    size_t tokens, const float* router_logits_host,
+                                                    float* output_host, uint32_t* route_ids_host,
+                                                    float* route_weights_host, char* error_buffer,
+                                                    size_t error_capacity);
+
 /* Measurement hook for benchmarks: the average device time (microseconds) of
  * one launch of a tensor-core path kernel (kernel 0: the Q4_K gate/up matvec,
  * 1: the down matvec and combine), launched `repetitions` times back to back

@@ -208,6 +208,34 @@ def moe_forward(layer: MoeLayer, x: np.ndarray):
     return out, ids, probs, logits
 
 
+def moe_forward_batch(layer: MoeLayer, x: np.ndarray, logits: np.ndarray | None = None):
+    """Rows of x ([tokens, hidden] f32) through the block one at a time, as the
+    reference's prefill does (src/qwen3_moe_runner.cpp:785-790); routed by the
+    given logits ([tokens, experts]) when not None.  Returns (out, ids, probs)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, layer.hidden)
+    T = x.shape[0]
+    out = np.empty((T, layer.hidden), dtype=np.float32)
+    ids = np.empty((T, layer.top_k), dtype=np.uint32)
+    probs = np.empty((T, layer.top_k), dtype=np.float32)
+    width = max(layer.inter, layer.shared_inter)
+    act = np.empty(3 * width, dtype=np.float32)
+    ys = np.empty(layer.hidden, dtype=np.float32)
+    lg_scratch = np.empty(layer.experts, dtype=np.float32)
+    d = layer.desc()
+    if logits is not None:
+        logits = np.ascontiguousarray(logits, dtype=np.float32).reshape(T, layer.experts)
+    for t in range(T):
+        row, o, i, p = x[t], out[t], ids[t], probs[t]
+        if logits is None:
+            st = port().po_moe_forward(C.byref(d), _fptr(row), _fptr(o), _fptr(i), _fptr(p),
+                                       _fptr(lg_scratch), _fptr(act), _fptr(ys))
+        else:
+            st = port().po_moe_forward_routed(C.byref(d), _fptr(row), _fptr(logits[t]), _fptr(o), _fptr(i),
+                                              _fptr(p), _fptr(act), _fptr(ys))
+        _check(st, "po_moe_forward")
+    return out, ids, probs
+
+
 def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     w = np.ascontiguousarray(w, dtype=np.float32)

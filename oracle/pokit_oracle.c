@@ -379,11 +379,27 @@ static size_t row_bytes_of(uint32_t type, size_t cols) {
     return cols / be * bb;
 }
 
+static int moe_body(const po_moe_layer* L, const float* x, float* out, uint32_t* ids, float* probs,
+                    float* logits, float* act_scratch, float* y_scratch, int run_router);
+
 int po_moe_forward(const po_moe_layer* L, const float* x, float* out, uint32_t* ids, float* probs,
                    float* logits, float* act_scratch, float* y_scratch) {
+    return moe_body(L, x, out, ids, probs, logits, act_scratch, y_scratch, 1);
+}
+
+/* po_moe_forward with the router logits given (`logits`, experts entries)
+ * instead of computed from L->router: the routes, experts and combine are
+ * the same.  Serves batched-token checks whose logits are inputs. */
+int po_moe_forward_routed(const po_moe_layer* L, const float* x, const float* logits, float* out,
+                          uint32_t* ids, float* probs, float* act_scratch, float* y_scratch) {
+    return moe_body(L, x, out, ids, probs, (float*)logits, act_scratch, y_scratch, 0);
+}
+
+static int moe_body(const po_moe_layer* L, const float* x, float* out, uint32_t* ids, float* probs,
+                    float* logits, float* act_scratch, float* y_scratch, int run_router) {
     if (!L || !x || !out || L->top_k == 0 || L->top_k > L->experts) return PO_INVALID;
     const size_t H = L->hidden, I = L->inter;
-    int st = po_linear(0, x, H, L->router, L->experts, logits);
+    int st = run_router ? po_linear(0, x, H, L->router, L->experts, logits) : PO_OK;
     if (st) return st;
     st = L->flavour == 0 ? po_route_qwen3(logits, L->experts, L->top_k, L->normalize, ids, probs)
                          : po_route_qwen35(logits, L->experts, L->top_k, L->normalize, ids, probs);

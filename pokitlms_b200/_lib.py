@@ -22,6 +22,7 @@ STATUS_BUFFER_TOO_SMALL, STATUS_INTERNAL_ERROR = 3, 4
 (ROUTER, GATE, UP, DOWN, FFN_NORM, SHARED_ROUTER, SHARED_GATE, SHARED_UP,
  SHARED_DOWN) = range(9)
 QWEN3, QWEN35 = 0, 1
+INPUT_F32, INPUT_BF16 = 0, 1
 
 
 def row_bytes(ggml_type: int, cols: int) -> int:
@@ -135,6 +136,10 @@ SIGNATURES = {
     "pokit_cuda_moe_expert_view": (C.c_int, [_VP, _SZ, C.c_uint32, _SZ, C.POINTER(_VP),
                                              C.POINTER(_SZ)]),
     "pokit_cuda_moe_forward": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_forward_batch": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, _VP, _VP, _VP,
+                                               _ERR, _SZ]),
+    "pokit_cuda_moe_forward_batch_host": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, _VP, _VP,
+                                                    _ERR, _SZ]),
     "pokit_cuda_moe_time_kernel": (C.c_int, [_VP, C.c_uint32, _SZ, _SZ, C.c_uint32, _VP, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_host": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_decode_layers": (C.c_int, [_VP, _SZ, _SZ, _VP, _VP, _ERR, _SZ]),

@@ -169,6 +169,38 @@ class CudaMoeBackend:
         call("pokit_cuda_moe_forward", self._h, layer, _ptr(x), _ptr(out), _ptr(route_ids),
              _ptr(route_weights), _stream(stream))
 
+    def forward_batch(self, layer: int, x, out, *, logits=None, route_ids=None, route_weights=None,
+                      stream=None) -> None:
+        """out[t] = MoE(x[t]) for the rows of a device tensor x ([tokens, hidden],
+        float32 or bfloat16); `logits` ([tokens, experts] float32) replaces the
+        layer's router when given.  Q4_K layers run the grouped-expert GEMM."""
+        import torch
+        kind = _lib.INPUT_BF16 if x.dtype == torch.bfloat16 else _lib.INPUT_F32
+        if kind == _lib.INPUT_F32 and x.dtype != torch.float32:
+            raise InvalidArgument(1, "x must be float32 or bfloat16")
+        tokens = x.numel() // self.hidden
+        call("pokit_cuda_moe_forward_batch", self._h, layer, _ptr(x), kind, tokens, _ptr(logits), _ptr(out),
+             _ptr(route_ids), _ptr(route_weights), _stream(stream))
+
+    def forward_batch_host(self, layer: int, x: np.ndarray, *, bf16_bits: bool = False,
+                           logits: np.ndarray | None = None):
+        """Host-array batch: x float32 [tokens, hidden], or uint16 BF16 bit
+        patterns when bf16_bits.  Returns (out, ids, weights)."""
+        if bf16_bits:
+            x = np.ascontiguousarray(x, dtype=np.uint16)
+            kind = _lib.INPUT_BF16
+        else:
+            x = np.ascontiguousarray(x, dtype=np.float32)
+            kind = _lib.INPUT_F32
+        tokens = x.size // self.hidden
+        lg = None if logits is None else np.ascontiguousarray(logits, dtype=np.float32)
+        out = np.empty((tokens, self.hidden), dtype=np.float32)
+        ids = np.empty((tokens, self.top_k), dtype=np.uint32)
+        w = np.empty((tokens, self.top_k), dtype=np.float32)
+        call("pokit_cuda_moe_forward_batch_host", self._h, layer, _np_ptr(x), kind, tokens, _np_ptr(lg),
+             _np_ptr(out), _np_ptr(ids), _np_ptr(w))
+        return out, ids, w
+
     def time_kernel(self, kernel: int, first: int, count: int, reps: int, work, stream=None) -> float:
         """Average device time (us) of one back-to-back launch of a tensor-core
         kernel (0 gate/up, 1 down) over layers [first, first + count)."""

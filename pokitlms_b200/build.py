@@ -23,9 +23,10 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libpokit_cuda.so"
 
-SOURCES = ["pokit_linear.cu", "pokit_moe.cu", "pokit_synth.cu", "pokit_backend.cpp",
+SOURCES = ["pokit_linear.cu", "pokit_moe.cu", "pokit_grouped.cu", "pokit_synth.cu", "pokit_backend.cpp",
            "pokit_static_scratch.cu"]
-HEADERS = ["pokit_common.cuh", "pokit_quant.cuh", "pokit_mma.cuh", "pokit_kernels.h", "pokit_types.h"]
+HEADERS = ["pokit_common.cuh", "pokit_quant.cuh", "pokit_mma.cuh", "pokit_tc.cuh", "pokit_kernels.h",
+           "pokit_types.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-Wall",

@@ -148,6 +148,9 @@ public:
 
     ~MoeBackend() {
         for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second.first);
+        if (batch_pinned_) cudaFreeHost(batch_pinned_);
+        if (batch_io_) cudaFree(batch_io_);
+        if (batch_scratch_) cudaFree(batch_scratch_);
         if (pinned_) cudaFreeHost(pinned_);
         if (io_) cudaFree(io_);
         if (scratch_) cudaFree(scratch_);
@@ -249,6 +252,76 @@ public:
         if (w) guard(cudaMemcpyAsync(w, S_.weights, cfg_.top_k * 4, cudaMemcpyDeviceToDevice, st), "weights");
         forward_calls_ += 1;
         hits_ += cfg_.top_k;
+    }
+
+    // A batch of tokens through one MoE block: the grouped-expert tensor-core
+    // path when the layer allows it (Q4_K experts, no shared expert), else
+    // one block launch sequence per token (F32 input, layer router only).
+    void forward_batch(size_t layer, const void* x, uint32_t x_type, size_t tokens, const float* logits,
+                       float* out, uint32_t* ids, float* w, cudaStream_t s) {
+        ensure_ok();
+        if (layer >= cfg_.layers) throw std::invalid_argument("layer out of range");
+        if (!x || !out) throw std::invalid_argument("input and output are required");
+        if (tokens == 0 || tokens > kMaxBatchTokens) throw std::invalid_argument("tokens must be 1..65536");
+        if (x_type > POKIT_CUDA_INPUT_BF16) throw std::invalid_argument("unknown input type");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        const MoeLayerDev& L = devs_[layer];
+        const uint32_t T = static_cast<uint32_t>(tokens), k = static_cast<uint32_t>(cfg_.top_k);
+        if (moe_batch_grouped(L)) {
+            ensure_batch_scratch(L, T);
+            uint32_t n = 0;
+            guard(launch_moe_batch(L, B_, x, x_type, T, logits, out, ids, w, S_.status, st, &n),
+                  "grouped MoE batch");
+            kernel_launches_ += n;
+        } else {
+            if (x_type != POKIT_CUDA_INPUT_F32)
+                throw std::invalid_argument("BF16 input needs the grouped path (Q4_K experts, no shared expert)");
+            if (logits) throw std::invalid_argument("caller logits need the grouped path (Q4_K experts, no shared expert)");
+            const float* xf = static_cast<const float*>(x);
+            for (uint32_t t = 0; t < T; ++t) {
+                uint32_t n = 0;
+                guard(launch_moe_block(L, S_, xf + size_t(t) * cfg_.hidden, nullptr, out + size_t(t) * cfg_.hidden,
+                                       nullptr, nullptr, st, &n),
+                      "moe block");
+                kernel_launches_ += n;
+                if (ids) guard(cudaMemcpyAsync(ids + size_t(t) * k, S_.ids, k * 4, cudaMemcpyDeviceToDevice, st), "ids");
+                if (w) guard(cudaMemcpyAsync(w + size_t(t) * k, S_.weights, k * 4, cudaMemcpyDeviceToDevice, st),
+                             "weights");
+            }
+        }
+        forward_calls_ += tokens;
+        hits_ += tokens * cfg_.top_k;
+    }
+
+    // Host-span batch: copies the inputs through pinned staging, runs, copies
+    // the outputs back and synchronises.
+    void forward_batch_host(size_t layer, const void* x, uint32_t x_type, size_t tokens, const float* logits,
+                            float* out, uint32_t* ids, float* w) {
+        ensure_ok();
+        if (!x || !out) throw std::invalid_argument("input and output are required");
+        if (tokens == 0 || tokens > kMaxBatchTokens) throw std::invalid_argument("tokens must be 1..65536");
+        if (x_type > POKIT_CUDA_INPUT_BF16) throw std::invalid_argument("unknown input type");
+        DeviceScope scope(device_);
+        const size_t H = cfg_.hidden, E = cfg_.experts, k = cfg_.top_k;
+        const size_t xb = tokens * H * (x_type == POKIT_CUDA_INPUT_BF16 ? 2 : 4), lb = logits ? tokens * E * 4 : 0;
+        const size_t ob = tokens * H * 4, rb = tokens * k * 4;
+        const size_t need = align256(xb) + align256(lb) + align256(ob) + 2 * align256(rb);
+        ensure_batch_io(need);
+        uint8_t* d = static_cast<uint8_t*>(batch_io_);
+        uint8_t* h = static_cast<uint8_t*>(batch_pinned_);
+        const size_t ox = 0, ol = align256(xb), oo = ol + align256(lb), oi = oo + align256(ob), ow = oi + align256(rb);
+        std::memcpy(h + ox, x, xb);
+        if (logits) std::memcpy(h + ol, logits, lb);
+        guard(cudaMemcpyAsync(d + ox, h + ox, logits ? ol + lb : xb, cudaMemcpyHostToDevice, stream_), "h2d");
+        forward_batch(layer, d + ox, x_type, tokens, logits ? reinterpret_cast<const float*>(d + ol) : nullptr,
+                      reinterpret_cast<float*>(d + oo), reinterpret_cast<uint32_t*>(d + oi),
+                      reinterpret_cast<float*>(d + ow), stream_);
+        guard(cudaMemcpyAsync(h + oo, d + oo, ow + rb - oo, cudaMemcpyDeviceToHost, stream_), "d2h");
+        synchronize(stream_);
+        std::memcpy(out, h + oo, ob);
+        if (ids) std::memcpy(ids, h + oi, rb);
+        if (w) std::memcpy(w, h + ow, rb);
     }
 
     // Average device time of one launch of a tensor-core kernel over the
@@ -358,7 +431,7 @@ public:
             // A grid barrier gave up: the launch was abandoned and the barrier
             // counter no longer matches the host's count.  Sticky, like a CUDA error.
             failed_ = true;
-            failure_ = "persistent decode kernel abandoned a grid barrier (wait timeout)";
+            failure_ = "a kernel abandoned its work after a bounded device-side wait timed out";
             throw std::runtime_error(failure_);
         }
         if (status) {
@@ -384,6 +457,32 @@ public:
     }
 
 private:
+    static constexpr size_t kMaxBatchTokens = 65536;
+
+    void ensure_batch_scratch(const MoeLayerDev& L, uint32_t tokens) {
+        if (batch_scratch_ && tokens <= B_.max_tokens) return;
+        uint32_t cap = std::max<uint32_t>(tokens, 64u);
+        if (batch_scratch_) {
+            guard(cudaStreamSynchronize(stream_), "batch scratch");
+            cudaFree(batch_scratch_);
+            batch_scratch_ = nullptr;
+        }
+        guard(cudaMalloc(&batch_scratch_, moe_batch_scratch_bytes(L, cap)), "cudaMalloc(batch scratch)");
+        B_ = moe_batch_scratch_carve(L, cap, batch_scratch_);
+    }
+
+    void ensure_batch_io(size_t bytes) {
+        if (bytes <= batch_io_bytes_) return;
+        if (batch_io_) cudaFree(batch_io_);
+        if (batch_pinned_) cudaFreeHost(batch_pinned_);
+        batch_io_ = nullptr;
+        batch_pinned_ = nullptr;
+        batch_io_bytes_ = 0;
+        guard(cudaMalloc(&batch_io_, bytes), "cudaMalloc(batch io)");
+        guard(cudaMallocHost(&batch_pinned_, bytes), "cudaMallocHost(batch io)");
+        batch_io_bytes_ = bytes;
+    }
+
     MoeLayerDev make_layer_dev(size_t l) const {
         MoeLayerDev L;
         L.hidden = static_cast<uint32_t>(cfg_.hidden);
@@ -459,6 +558,11 @@ private:
     uint32_t barrier_count_ = 0;
     uint64_t scratch_bytes_ = 0;
     MoeScratch S_;
+    void* batch_scratch_ = nullptr;   // grouped-path scratch, grown on demand
+    MoeBatchScratch B_;
+    void* batch_io_ = nullptr;        // host-span batch staging (device, pinned host)
+    void* batch_pinned_ = nullptr;
+    size_t batch_io_bytes_ = 0;
     void* io_ = nullptr;
     void* pinned_ = nullptr;
     cudaStream_t stream_ = nullptr;
@@ -786,6 +890,31 @@ pokit_cuda_status pokit_cuda_moe_forward(pokit_cuda_moe* moe, size_t layer, cons
         if (!moe) throw std::invalid_argument("MoE handle is required");
         std::lock_guard<std::mutex> lock(moe->impl.mutex());
         moe->impl.forward(layer, input, output, route_ids, route_weights, as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_forward_batch(pokit_cuda_moe* moe, size_t layer, const void* input,
+                                               uint32_t input_type, size_t tokens, const float* router_logits,
+                                               float* output, uint32_t* route_ids, float* route_weights,
+                                               void* stream, char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.forward_batch(layer, input, input_type, tokens, router_logits, output, route_ids, route_weights,
+                                as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_forward_batch_host(pokit_cuda_moe* moe, size_t layer, const void* input_host,
+                                                    uint32_t input_type, size_t tokens,
+                                                    const float* router_logits_host, float* output_host,
+                                                    uint32_t* route_ids_host, float* route_weights_host,
+                                                    char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.forward_batch_host(layer, input_host, input_type, tokens, router_logits_host, output_host,
+                                     route_ids_host, route_weights_host);
     });
 }
 

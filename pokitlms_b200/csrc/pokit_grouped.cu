@@ -1,0 +1,955 @@
+// pokit_grouped.cu -- the MoE block for a batch of tokens (prefill, batched
+// decode): tokens grouped by expert and every expert's Q4_K gate/up/down
+// applied to its tokens as a GEMM on the fifth-generation tensor cores.
+//
+// The reference runs a batch token by token (Qwen3MoeRunner prefill calls
+// forward_into per prompt token, src/qwen3_moe_runner.cpp:785-790, each MoE
+// block as in 643-692).  Per token this computes the same thing:
+//   out[t] = sum_r w_r * down_e(silu(gate_e x_t) * up_e x_t),  e = ids[t][r]
+// with routes from route_experts (qwen3_moe_runner.cpp:267-305).
+//
+// Launches (one stream):
+//   1. router logits [T][E] in F32 (skipped when the caller gives logits)
+//   2. route: softmax top-k per token (the single-token router, one CTA/row)
+//   3. group: stable counting sort of the T*k (token, rank) pairs by expert;
+//      each expert's pairs are cut into tiles of <= 64 tokens
+//   4. pack x: per tile and 256-wide superblock, the tile's activation rows
+//      as fp16 in the GEMM operand layout (below), with a power-of-two scale
+//      per (row, superblock) and per-sub-block sums for the Q4_K mins
+//   5. gate/up GEMM: a unit is (tile, 64 rows of gate and the same 64 rows
+//      of up); writes silu(g) * u in F32
+//   6. pack the activations (fp16 hi + lo parts: 22 significant bits)
+//   7. down GEMM: a unit is (tile, 128 rows of down); writes w_r * y per pair
+//   8. combine: out[t] = sum over ranks in rank order (the reference's order)
+//
+// GEMM arithmetic.  For a Q4_K superblock (d, dmin, 6-bit scales s_j and
+// mins m_j, 4-bit q) the reference weight is d*s_j*q - dmin*m_j
+// (src/quantized_linear.cpp:166-205), so a row's dot with x is
+//   sum_sb [ d * sum_k (s_j q_k) x_k  -  dmin * sum_j m_j (sum_{k in j} x_k) ].
+// s_j q_k <= 945 is an integer, exact in fp16; x is exact in fp16 for BF16
+// inputs (scaled by a power of two into fp16 range) and split into fp16 hi +
+// lo for F32 inputs and for the down GEMM's activations.  Per superblock one
+// tensor-core MMA chain (A = s_j q_k from tensor memory, B = x from shared
+// memory, K = 256) gives the first sum and one MMA (A = m_j, B = the sub-block
+// sums as hi + lo) the second, both exactly up to F32 accumulation; the
+// epilogue applies d, dmin and the activation scale in F32 per superblock.
+//
+// Operand layout of a tile's packed activations (one superblock, Np = tile
+// tokens rounded up to 16): chunks of 8 fp16 (16 bytes) for chunk c (0..31,
+// or 0..63 with the lo parts in 32..63) and token row n at
+// (c * Np + n) * 16, then two chunks of sub-block sums (hi, lo).  Within a
+// superblock the K order is permuted to match the dequantiser's output: the
+// 32-bit tensor-memory column j = 32c + 4w + o (chunk c = 0..3 of the Q4_K
+// nibbles, word w = 0..7, nibble pair o = 0..3) holds the weights of
+// sub-block 2c + (o >> 1) at positions 4w + (o & 1) and 4w + (o & 1) + 2.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "pokit_common.cuh"
+#include "pokit_kernels.h"
+#include "pokit_tc.cuh"
+#include "pokit_types.h"
+
+namespace pokit {
+namespace {
+
+constexpr uint32_t kTileTokens = 64;                  // N of one GEMM tile
+constexpr uint32_t kEpiWarps = 8;                     // dequantise + epilogue
+constexpr uint32_t kGemmThreads = (kEpiWarps + 2) * 32;  // + loader warp + MMA warp
+constexpr uint32_t kQStage = 128u * 144u;             // one superblock of 128 rows
+constexpr uint32_t kSortThreads = 512;
+constexpr uint32_t kSortWarps = kSortThreads / 32;
+constexpr uint32_t kPackThreads = 256;
+
+__host__ __device__ constexpr uint32_t round16(uint32_t n) { return (n + 15u) & ~15u; }
+// Padded slots of an expert with c pairs: full tiles of 64, the last rounded to 16.
+__host__ __device__ constexpr uint32_t padded_slots(uint32_t c) { return (c / 64u) * 64u + round16(c % 64u); }
+
+__device__ __forceinline__ float silu_times(float g, float u, uint32_t flavour) {
+    // Qwen3-MoE: g / (1 + exp(-g)) * u (qwen3_moe_runner.cpp:683);
+    // Qwen3.5:   g * sigmoid(g) * u  (qwen35_runner.cpp:111-123).
+    if (flavour == 0) return (g / (1.0f + expf(-g))) * u;
+    float sg;
+    if (g >= 0.0f) sg = 1.0f / (1.0f + expf(-g));
+    else { const float e = expf(g); sg = e / (1.0f + e); }
+    return (g * sg) * u;
+}
+
+// ---------------------------------------------------------------------------
+// 1. Router logits for a batch: logits[t][e] = router[e] . x[t] (F32 sums in
+// hidden order).  A CTA computes 16 tokens x 64 experts.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) router_batch_kernel(const float* __restrict__ router,
+                                                           const void* __restrict__ x, uint32_t x_bf16,
+                                                           uint32_t T, uint32_t E, uint32_t H,
+                                                           float* __restrict__ logits) {
+    __shared__ float xs[16][65];
+    __shared__ float ws[64][65];
+    const uint32_t t0 = blockIdx.x * 16, e0 = blockIdx.y * 64;
+    const uint32_t ti = threadIdx.x / 16, eb = threadIdx.x % 16;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t k0 = 0; k0 < H; k0 += 64) {
+        for (uint32_t i = threadIdx.x; i < 16 * 64; i += 256) {
+            const uint32_t row = i / 64, col = i % 64, t = t0 + row;
+            float v = 0.f;
+            if (t < T) {
+                const size_t at = static_cast<size_t>(t) * H + k0 + col;
+                v = x_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[at])
+                           : reinterpret_cast<const float*>(x)[at];
+            }
+            xs[row][col] = v;
+        }
+        for (uint32_t i = threadIdx.x; i < 64 * 64; i += 256) {
+            const uint32_t row = i / 64, col = i % 64, e = e0 + row;
+            ws[row][col] = e < E ? router[static_cast<size_t>(e) * H + k0 + col] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (uint32_t kk = 0; kk < 64; ++kk) {
+            const float xv = xs[ti][kk];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] = fmaf(ws[eb + 16 * j][kk], xv, acc[j]);
+        }
+        __syncthreads();
+    }
+    const uint32_t t = t0 + ti;
+    if (t < T) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t e = e0 + eb + 16 * j;
+            if (e < E) logits[static_cast<size_t>(t) * E + e] = acc[j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3. Group: stable counting sort of pairs p = t * k + r by expert ids[p].
+// Pairs of one expert keep increasing p.  Writes the tile list and the slot
+// -> pair map.  One CTA.
+// ---------------------------------------------------------------------------
+struct GroupOut {
+    uint32_t* plan;        // [0] tiles, [1] padded slots
+    uint32_t* tile_expert;
+    uint32_t* tile_first;  // first slot (index into slot_pair)
+    uint32_t* tile_n;      // tokens in the tile (1..64)
+    uint32_t* tile_pad0;   // first padded slot
+    uint32_t* slot_pair;
+    uint32_t* rank;        // scratch [pairs]
+};
+
+__global__ void __launch_bounds__(kSortThreads, 1) group_kernel(const uint32_t* __restrict__ ids, uint32_t pairs,
+                                                                uint32_t E, GroupOut o) {
+    extern __shared__ uint32_t sm[];
+    uint32_t* wc = sm;                          // [kSortWarps][E]
+    uint32_t* total = wc + kSortWarps * E;      // [E]
+    uint32_t* off_slot = total + E;             // [E]
+    uint32_t* off_tile = off_slot + E;          // [E]
+    uint32_t* off_pad = off_tile + E;           // [E]
+    const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    for (uint32_t e = tid; e < E; e += kSortThreads) total[e] = 0;
+    __syncthreads();
+    for (uint32_t base = 0; base < pairs; base += kSortThreads) {
+        const uint32_t p = base + tid;
+        const bool valid = p < pairs;
+        const uint32_t e = valid ? min(ids[p], E - 1) : 0xFFFFFFFFu;
+        for (uint32_t i = lane; i < E; i += 32) wc[warp * E + i] = 0;
+        __syncwarp();
+        const uint32_t m = __match_any_sync(0xFFFFFFFFu, e);
+        const uint32_t lr = __popc(m & ((1u << lane) - 1u));
+        if (valid && lr == 0) wc[warp * E + e] = __popc(m);
+        __syncthreads();
+        for (uint32_t i = tid; i < E; i += kSortThreads) {
+            uint32_t run = total[i];
+            for (uint32_t w = 0; w < kSortWarps; ++w) {
+                const uint32_t c = wc[w * E + i];
+                wc[w * E + i] = run;
+                run += c;
+            }
+            total[i] = run;
+        }
+        __syncthreads();
+        if (valid) o.rank[p] = wc[warp * E + e] + lr;
+        __syncthreads();
+    }
+    if (warp == 0) {
+        const uint32_t per = (E + 31) / 32, lo = min(E, lane * per), hi = min(E, lo + per);
+        uint32_t sc = 0, st = 0, sp = 0;
+        for (uint32_t e = lo; e < hi; ++e) {
+            const uint32_t c = total[e];
+            sc += c;
+            st += (c + kTileTokens - 1) / kTileTokens;
+            sp += padded_slots(c);
+        }
+        uint32_t ic = sc, it = st, ip = sp;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t a = __shfl_up_sync(0xFFFFFFFFu, ic, d), b = __shfl_up_sync(0xFFFFFFFFu, it, d),
+                           c = __shfl_up_sync(0xFFFFFFFFu, ip, d);
+            if (lane >= static_cast<uint32_t>(d)) { ic += a; it += b; ip += c; }
+        }
+        uint32_t rc = ic - sc, rt = it - st, rp = ip - sp;
+        for (uint32_t e = lo; e < hi; ++e) {
+            const uint32_t c = total[e];
+            off_slot[e] = rc;
+            off_tile[e] = rt;
+            off_pad[e] = rp;
+            rc += c;
+            rt += (c + kTileTokens - 1) / kTileTokens;
+            rp += padded_slots(c);
+        }
+        if (lane == 31) {
+            o.plan[0] = it;
+            o.plan[1] = ip;
+        }
+    }
+    __syncthreads();
+    for (uint32_t e = tid; e < E; e += kSortThreads) {
+        const uint32_t c = total[e];
+        for (uint32_t i = 0; i * kTileTokens < c; ++i) {
+            const uint32_t tile = off_tile[e] + i;
+            o.tile_expert[tile] = e;
+            o.tile_first[tile] = off_slot[e] + i * kTileTokens;
+            o.tile_n[tile] = min(kTileTokens, c - i * kTileTokens);
+            o.tile_pad0[tile] = off_pad[e] + i * kTileTokens;
+        }
+    }
+    for (uint32_t p = tid; p < pairs; p += kSortThreads) {
+        const uint32_t e = min(ids[p], E - 1);
+        o.slot_pair[off_slot[e] + o.rank[p]] = p;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 4/6. Pack GEMM activations.  One CTA per tile, a warp per (row, superblock).
+// ---------------------------------------------------------------------------
+struct PackArgs {
+    const void* src;       // rows of `cols` elements (F32, or BF16 when src_bf16)
+    uint32_t src_bf16;
+    uint32_t by_token;     // 1: source row = token of the slot's pair; 0: row = padded slot
+    uint32_t top_k;
+    uint32_t cols;
+    uint32_t split;        // 1: fp16 hi and lo parts
+    const uint32_t* plan;
+    const uint32_t* tile_first;
+    const uint32_t* tile_n;
+    const uint32_t* tile_pad0;
+    const uint32_t* slot_pair;
+    uint8_t* dst;
+    float* dst_scale;
+};
+
+__device__ __forceinline__ uint4 pack8_half(const float (&v)[8]) {
+    uint4 r;
+    r.x = pack_half2(v[0], v[1]);
+    r.y = pack_half2(v[2], v[3]);
+    r.z = pack_half2(v[4], v[5]);
+    r.w = pack_half2(v[6], v[7]);
+    return r;
+}
+
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
+    __shared__ float stage[kPackThreads / 32][8 * 33];
+    const uint32_t tile = blockIdx.x;
+    if (tile >= a.plan[0]) return;
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t n_valid = a.tile_n[tile], np = round16(n_valid), pad0 = a.tile_pad0[tile];
+    const uint32_t first = a.tile_first[tile];
+    const uint32_t S = a.cols / 256, kc8 = a.split ? 64u : 32u;
+    const uint32_t stage_bytes = (kc8 + 2) * np * 16;
+    uint8_t* tile_base = a.dst + static_cast<size_t>(pad0) * S * (kc8 + 2) * 16;
+    float* st = stage[warp];
+    for (uint32_t item = warp; item < np * S; item += kPackThreads / 32) {
+        const uint32_t n = item / S, s = item % S;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        if (n < n_valid) {
+            const uint32_t row = a.by_token ? a.slot_pair[first + n] / a.top_k : pad0 + n;
+            const size_t at = static_cast<size_t>(row) * a.cols + s * 256 + lane * 8;
+            if (a.src_bf16) {
+                const uint4 q = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.src) + at);
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    v[2 * i] = __uint_as_float(w[i] << 16);
+                    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+                }
+            } else {
+                const float4 p0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + at);
+                const float4 p1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + at + 4);
+                v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+                v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+            }
+        }
+        // Power-of-two scale bringing max |v| of the superblock into [512, 1024):
+        // sub-block sums stay below 2^15 and the scaling itself is exact.
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
+        int ex = 0;
+        if (amax > 0.f && amax <= 3.0e38f) frexpf(amax, &ex);
+        const int sig = max(-100, min(100, ex - 10));
+        const float down = __int_as_float((127 - sig) << 23);
+        float part = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            v[i] *= down;
+            part += v[i];
+            st[33 * (lane / 4) + 8 * (lane % 4) + i] = v[i];
+        }
+        // Sub-block j = lane / 4 sums over its four lanes.
+        part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+        part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
+        __syncwarp();
+        uint8_t* region = tile_base + static_cast<size_t>(s) * stage_bytes;
+        {
+            const uint32_t c = lane >> 3, w = lane & 7;
+            const float* b0 = st + 33 * (2 * c) + 4 * w;
+            const float* b1 = st + 33 * (2 * c + 1) + 4 * w;
+            float e[8] = {b0[0], b0[2], b0[1], b0[3], b1[0], b1[2], b1[1], b1[3]};
+            float hi[8], lo[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                hi[i] = __half2float(__float2half_rn(e[i]));
+                lo[i] = e[i] - hi[i];
+            }
+            *reinterpret_cast<uint4*>(region + (static_cast<size_t>(lane) * np + n) * 16) = pack8_half(hi);
+            if (a.split)
+                *reinterpret_cast<uint4*>(region + (static_cast<size_t>(32 + lane) * np + n) * 16) = pack8_half(lo);
+        }
+        if ((lane & 3) == 0) {
+            const uint32_t j = lane >> 2;
+            const __half h = __float2half_rn(part);
+            const __half l = __float2half_rn(part - __half2float(h));
+            reinterpret_cast<__half*>(region + (static_cast<size_t>(kc8) * np + n) * 16)[j] = h;
+            reinterpret_cast<__half*>(region + (static_cast<size_t>(kc8 + 1) * np + n) * 16)[j] = l;
+        }
+        if (lane == 0)
+            a.dst_scale[static_cast<size_t>(pad0) * S + s * np + n] = __int_as_float((127 + sig) << 23);
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 5/7. The grouped GEMM.  Persistent: one CTA per SM takes units
+// blockIdx.x, blockIdx.x + gridDim.x, ...
+//
+// Warps 0..7 (two per tensor-memory lane quarter) dequantise the Q4_K rows
+// of superblock s + 1 into tensor memory while the tensor core works on s,
+// then fold s's accumulators into registers.  Warp 8 loads weights (TMA
+// boxes of 144 bytes x 64/128 rows) and the packed activations (one bulk
+// copy per superblock).  Warp 9 owns tensor memory and issues the MMAs.
+//
+// Tensor memory (512 columns): A (scales x quants, fp16) double-buffered in
+// columns [0, 256); per buffer b the accumulators of the quants at 256 + 128b
+// and of the mins at 256 + 128b + 64 (N <= 64 tokens).
+// ---------------------------------------------------------------------------
+struct GemmArgs {
+    CUtensorMap tm0;          // gate (mode 0) or down (mode 1)
+    CUtensorMap tm1;          // up (mode 0)
+    const uint8_t* b;
+    const float* b_scale;
+    const uint32_t* plan;
+    const uint32_t* tile_expert;
+    const uint32_t* tile_first;
+    const uint32_t* tile_n;
+    const uint32_t* tile_pad0;
+    const uint32_t* slot_pair;
+    const float* route_w;     // [pairs] combine weights (mode 1)
+    float* out;               // mode 0: act [padded][rows]; mode 1: pair_out [pairs][rows]
+    uint32_t K;               // reduction length (hidden or inter)
+    uint32_t rows;            // output rows per expert (inter or hidden)
+    uint32_t flavour;
+    uint32_t* status;
+};
+
+template <int kMode, int kSplit, int kQ, int kB>
+struct GemmLayout {
+    static constexpr uint32_t kc8 = kSplit ? 64u : 32u;
+    static constexpr uint32_t bstage = (kc8 + 2) * kTileTokens * 16;
+    static constexpr uint32_t q_off = 0;
+    static constexpr uint32_t b_off = q_off + kQ * kQStage;
+    static constexpr uint32_t amin_off = b_off + kB * bstage;            // [2][2][128][16 B]
+    static constexpr uint32_t dd_off = amin_off + 2 * 4096;               // [2][2][128] float2
+    static constexpr uint32_t xch_off = dd_off + 2 * 2 * 128 * 8;         // [64 cols][64 rows] (mode 0)
+    static constexpr uint32_t bar_off = xch_off + (kMode == 0 ? 64 * 64 * 4 : 0);
+    static constexpr uint32_t nbars = 2 * kQ + 2 * kB + 8 + 3;
+    static constexpr uint32_t misc_off = bar_off + nbars * 8;
+    static constexpr uint32_t total = misc_off + 16;
+};
+
+template <int kMode, int kSplit, int kQ, int kB>
+__global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __grid_constant__ GemmArgs a) {
+    using Lay = GemmLayout<kMode, kSplit, kQ, kB>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* qbuf = smem + Lay::q_off;
+    uint8_t* bbuf = smem + Lay::b_off;
+    uint8_t* amin = smem + Lay::amin_off;
+    float2* dd = reinterpret_cast<float2*>(smem + Lay::dd_off);
+    float* xch = reinterpret_cast<float*>(smem + Lay::xch_off);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::bar_off);
+    uint64_t* q_full = bars;
+    uint64_t* q_empty = q_full + kQ;
+    uint64_t* b_full = q_empty + kQ;
+    uint64_t* b_empty = b_full + kB;
+    uint64_t* a_full = b_empty + kB;     // [2] dequantised A (and mins) ready
+    uint64_t* a_free = a_full + 2;       // [2] MMAs reading A done
+    uint64_t* acc_full = a_free + 2;     // [2] accumulators ready
+    uint64_t* acc_free = acc_full + 2;   // [2] accumulators read
+    uint64_t* xch_full = acc_free + 2;   // up rows written (mode 0)
+    uint64_t* xch_free = xch_full + 1;   // up rows consumed (mode 0)
+    uint64_t* drain = xch_free + 1;      // all MMAs complete
+    uint32_t* misc = reinterpret_cast<uint32_t*>(smem + Lay::misc_off);
+    volatile uint32_t* abort_flag = misc + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == kEpiWarps + 1) {
+        tmem_alloc(misc, 512);
+        tmem_relinquish();
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kQ; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, kEpiWarps); }
+        for (int i = 0; i < kB; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(a_full + i, kEpiWarps);
+            mbar_init(a_free + i, 1);
+            mbar_init(acc_full + i, 1);
+            mbar_init(acc_free + i, kEpiWarps);
+        }
+        mbar_init(xch_full, kEpiWarps / 2);
+        mbar_init(xch_free, kEpiWarps / 2);
+        mbar_init(drain, 1);
+        misc[1] = 0;
+        mbar_fence_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = misc[0];
+
+    const uint32_t S = a.K / 256;
+    constexpr uint32_t kRowsPerUnit = kMode == 0 ? 64u : 128u;
+    const uint32_t mblocks = a.rows / kRowsPerUnit;
+    const uint32_t units = a.plan[0] * mblocks;
+
+    const auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (*abort_flag) return false;
+        if (mbar_wait_ns(bar, parity)) return true;
+        atomicOr(a.status, kStatusWaitTimeout);
+        *abort_flag = 1;
+        return false;
+    };
+
+    if (warp == kEpiWarps) {
+        // ---------------- loader ----------------
+        if (lane == 0) {
+            int32_t last_q[kQ], last_b[kB];
+            for (int i = 0; i < kQ; ++i) last_q[i] = -1;
+            for (int i = 0; i < kB; ++i) last_b[i] = -1;
+            uint32_t g = 0;
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
+                const uint32_t tile = u / mblocks, mb = u % mblocks;
+                const uint32_t e = a.tile_expert[tile], np = round16(a.tile_n[tile]);
+                const uint32_t stage = (Lay::kc8 + 2) * np * 16;
+                const uint8_t* bsrc = a.b + static_cast<size_t>(a.tile_pad0[tile]) * S * (Lay::kc8 + 2) * 16;
+                for (uint32_t s = 0; s < S; ++s, ++g) {
+                    const uint32_t qs = g % kQ, bs = g % kB;
+                    if (!(ok = wait(q_empty + qs, ((g / kQ) & 1) ^ 1))) break;
+                    mbar_expect_tx(q_full + qs, kQStage);
+                    if (kMode == 0) {
+                        tma_box_3d(qbuf + qs * kQStage, &a.tm0, s * 144, mb * 64, e, q_full + qs);
+                        tma_box_3d(qbuf + qs * kQStage + 64 * 144, &a.tm1, s * 144, mb * 64, e, q_full + qs);
+                    } else {
+                        tma_box_3d(qbuf + qs * kQStage, &a.tm0, s * 144, mb * 128, e, q_full + qs);
+                    }
+                    last_q[qs] = static_cast<int32_t>(g);
+                    if (!(ok = wait(b_empty + bs, ((g / kB) & 1) ^ 1))) break;
+                    mbar_expect_tx(b_full + bs, stage);
+                    bulk_g2s(bbuf + bs * Lay::bstage, bsrc + static_cast<size_t>(s) * stage, stage, b_full + bs);
+                    last_b[bs] = static_cast<int32_t>(g);
+                }
+            }
+            if (*abort_flag) {
+                // Let the copies in flight land before the CTA exits.
+                for (int i = 0; i < kQ; ++i)
+                    if (last_q[i] >= 0) mbar_wait_ns(q_full + i, (static_cast<uint32_t>(last_q[i]) / kQ) & 1);
+                for (int i = 0; i < kB; ++i)
+                    if (last_b[i] >= 0) mbar_wait_ns(b_full + i, (static_cast<uint32_t>(last_b[i]) / kB) & 1);
+            }
+        }
+    } else if (warp == kEpiWarps + 1) {
+        // ---------------- MMA issue ----------------
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
+                const uint32_t tile = u / mblocks;
+                const uint32_t np = round16(a.tile_n[tile]);
+                const uint32_t idesc = tc_idesc_f16(128, np);
+                const uint32_t lbo = np * 16;
+                for (uint32_t s = 0; s < S; ++s, ++g) {
+                    const uint32_t buf = g & 1, ph = (g >> 1) & 1, bs = g % kB;
+                    if (!(ok = wait(a_full + buf, ph))) break;
+                    if (!(ok = wait(b_full + bs, (g / kB) & 1))) break;
+                    if (!(ok = wait(acc_free + buf, ph ^ 1))) break;
+                    tc_fence_after();
+                    const uint32_t a_col = tbase + buf * 128;
+                    const uint32_t acc_q = tbase + 256 + buf * 128, acc_m = acc_q + 64;
+                    const uint32_t bb = smem_addr(bbuf + bs * Lay::bstage);
+#pragma unroll
+                    for (uint32_t ks = 0; ks < 16; ++ks)
+                        tc_mma_ts(acc_q, a_col + 8 * ks, tc_smem_desc(bb + 2 * ks * lbo, lbo, 128), idesc, ks > 0);
+                    if (kSplit) {
+#pragma unroll
+                        for (uint32_t ks = 0; ks < 16; ++ks)
+                            tc_mma_ts(acc_q, a_col + 8 * ks, tc_smem_desc(bb + (32 + 2 * ks) * lbo, lbo, 128), idesc,
+                                      1);
+                    }
+                    tc_mma_ss(acc_m, tc_smem_desc(smem_addr(amin + buf * 4096), 2048, 128),
+                              tc_smem_desc(bb + Lay::kc8 * lbo, lbo, 128), idesc, 0);
+                    tc_commit(b_empty + bs);
+                    tc_commit(a_free + buf);
+                    tc_commit(acc_full + buf);
+                }
+            }
+            tc_commit(drain);
+            mbar_wait_ns(drain, 0);
+        }
+    } else {
+        // ---------------- dequantise + epilogue ----------------
+        const uint32_t q4 = warp & 3, kh = warp >> 2;   // lane quarter; K half (dequantise) and N half (epilogue)
+        const uint32_t r = 32 * q4 + lane;                 // tile row = tensor-memory lane
+        const uint32_t lane_base = (32 * q4) << 16;
+        float acc[32];
+        uint32_t g = 0, ui = 0;
+        bool ok = true;
+        // The warp's lanes take every wait together so that the warp-wide
+        // tensor-memory instructions after it run converged.
+        const auto wait_warp = [&](uint64_t* bar, uint32_t parity) -> bool {
+            return __all_sync(0xFFFFFFFFu, wait(bar, parity)) != 0;
+        };
+
+        // Superblock gg of the CTA's sequence: A = s_j * q (fp16, exact) into
+        // tensor-memory buffer gg & 1, the mins m_j into shared memory.
+        const auto dequant = [&](uint32_t gg) -> bool {
+            const uint32_t qs = gg % kQ, buf = gg & 1;
+            if (!wait_warp(q_full + qs, (gg / kQ) & 1)) return false;
+            if (!wait_warp(a_free + buf, ((gg >> 1) & 1) ^ 1)) return false;
+            const uint8_t* row = qbuf + qs * kQStage + r * 144;
+            const uint32_t dm = *reinterpret_cast<const uint32_t*>(row);
+            const uint32_t w0 = *reinterpret_cast<const uint32_t*>(row + 4);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t*>(row + 8);
+            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(row + 12);
+            // 6-bit scales / mins (k_scale_min): bytes q[0..11] = w0 | w1 | w2.
+            uint32_t sc[8], mn[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t qj = (w0 >> (8 * j)) & 0xFF, qj4 = (w1 >> (8 * j)) & 0xFF, qj8 = (w2 >> (8 * j)) & 0xFF;
+                sc[j] = qj & 63;
+                mn[j] = qj4 & 63;
+                sc[j + 4] = (qj8 & 0xF) | ((qj >> 6) << 4);
+                mn[j + 4] = (qj8 >> 4) | ((qj4 >> 6) << 4);
+            }
+            dd[(buf * 2 + kh) * 128 + r] = make_float2(half_bits_to_float(dm & 0xFFFF), half_bits_to_float(dm >> 16));
+            {
+                uint4 mv;
+                mv.x = pack_half2(static_cast<float>(mn[0]), static_cast<float>(mn[1]));
+                mv.y = pack_half2(static_cast<float>(mn[2]), static_cast<float>(mn[3]));
+                mv.z = pack_half2(static_cast<float>(mn[4]), static_cast<float>(mn[5]));
+                mv.w = pack_half2(static_cast<float>(mn[6]), static_cast<float>(mn[7]));
+                *reinterpret_cast<uint4*>(amin + buf * 4096 + kh * 2048 + r * 16) = mv;
+            }
+#pragma unroll
+            for (uint32_t cc = 0; cc < 2; ++cc) {
+                const uint32_t c = 2 * kh + cc;
+                const uint4 qa = *reinterpret_cast<const uint4*>(row + 16 + 32 * c);
+                const uint4 qb = *reinterpret_cast<const uint4*>(row + 16 + 32 * c + 16);
+                const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                const float slo = static_cast<float>(sc[2 * c]), shi = static_cast<float>(sc[2 * c + 1]);
+                const uint32_t s2lo = pack_half2(slo, slo), s2hi = pack_half2(shi, shi);
+                const uint32_t n2lo = pack_half2(-1024.f * slo, -1024.f * slo);
+                const uint32_t n2hi = pack_half2(-1024.f * shi, -1024.f * shi);
+                uint32_t v[32];
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    const uint32_t W = words[w];
+                    v[4 * w + 0] = hfma2u((W & 0x000F000Fu) | kHalfMagic, s2lo, n2lo);
+                    v[4 * w + 1] = hfma2u(((W >> 8) & 0x000F000Fu) | kHalfMagic, s2lo, n2lo);
+                    v[4 * w + 2] = hfma2u(((W >> 4) & 0x000F000Fu) | kHalfMagic, s2hi, n2hi);
+                    v[4 * w + 3] = hfma2u(((W >> 12) & 0x000F000Fu) | kHalfMagic, s2hi, n2hi);
+                }
+                const uint32_t col = tbase + lane_base + buf * 128 + 32 * c;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t (&vv)[8] = *reinterpret_cast<const uint32_t(*)[8]>(v + 8 * i);
+                    tmem_st8(col + 8 * i, vv);
+                }
+            }
+            tmem_wait_st();
+            fence_async_shared();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(a_full + buf);
+                mbar_arrive(q_empty + qs);
+            }
+            return true;
+        };
+
+        // Folds superblock gg (index s within the unit) into acc.
+        const auto epilogue = [&](uint32_t gg, uint32_t s, uint32_t np, uint32_t pad0) -> bool {
+            const uint32_t buf = gg & 1;
+            if (!wait_warp(acc_full + buf, (gg >> 1) & 1)) return false;
+            tc_fence_after();
+            const float2 dm = dd[(buf * 2 + kh) * 128 + r];
+            const float* scl = a.b_scale + static_cast<size_t>(pad0) * S + s * np;
+            const uint32_t hn = np >> 1;
+            const uint32_t acc_q = tbase + lane_base + 256 + buf * 128, acc_m = acc_q + 64;
+#pragma unroll
+            for (uint32_t c = 0; c < 4; ++c) {
+                if (8 * c < hn) {
+                    const uint32_t col = kh * hn + 8 * c;
+                    uint32_t qv[8], mv[8];
+                    tmem_ld8(acc_q + col, qv);
+                    tmem_ld8(acc_m + col, mv);
+                    tmem_wait_ld();
+                    const float4 s0 = *reinterpret_cast<const float4*>(scl + col);
+                    const float4 s1 = *reinterpret_cast<const float4*>(scl + col + 4);
+                    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        acc[8 * c + i] = fmaf(
+                            fmaf(dm.x, __uint_as_float(qv[i]), -dm.y * __uint_as_float(mv[i])), sv[i], acc[8 * c + i]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_free + buf);
+            return true;
+        };
+
+        for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ui) {
+            const uint32_t tile = u / mblocks, mb = u % mblocks;
+            const uint32_t n_valid = a.tile_n[tile], np = round16(n_valid), pad0 = a.tile_pad0[tile];
+            const uint32_t hn = np >> 1;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+            if (!(ok = dequant(g))) break;
+            for (uint32_t s = 0; ok && s < S; ++s) {
+                if (s + 1 < S && !(ok = dequant(g + s + 1))) break;
+                ok = epilogue(g + s, s, np, pad0);
+            }
+            if (!ok) break;
+            g += S;
+            if (kMode == 0) {
+                // Rows 0..63 hold gate, 64..127 up: silu(gate) * up per token.
+                if (q4 >= 2) {
+                    if (!(ok = wait_warp(xch_free, (ui & 1) ^ 1))) break;
+#pragma unroll
+                    for (uint32_t c = 0; c < 4; ++c)
+                        if (8 * c < hn)
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) xch[(kh * hn + 8 * c + i) * 64 + (r - 64)] = acc[8 * c + i];
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_full);
+                } else {
+                    if (!(ok = wait_warp(xch_full, ui & 1))) break;
+#pragma unroll
+                    for (uint32_t c = 0; c < 4; ++c) {
+                        if (8 * c < hn) {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const uint32_t col = kh * hn + 8 * c + i;
+                                if (col < n_valid) {
+                                    const float h = silu_times(acc[8 * c + i], xch[col * 64 + r], a.flavour);
+                                    a.out[static_cast<size_t>(pad0 + col) * a.rows + mb * 64 + r] = h;
+                                }
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(xch_free);
+                }
+            } else {
+                const uint32_t first = a.tile_first[tile];
+#pragma unroll
+                for (uint32_t c = 0; c < 4; ++c) {
+                    if (8 * c < hn) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const uint32_t col = kh * hn + 8 * c + i;
+                            if (col < n_valid) {
+                                const uint32_t p = a.slot_pair[first + col];
+                                a.out[static_cast<size_t>(p) * a.rows + mb * 128 + r] = a.route_w[p] * acc[8 * c + i];
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kEpiWarps + 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 8. Combine: out[t] = sum_r pair_out[t * k + r] in rank order from 0
+// (the reference adds w_r * y_r in that order, qwen3_moe_runner.cpp:688-690).
+// ---------------------------------------------------------------------------
+__global__ void combine_kernel(const float* __restrict__ pair_out, uint32_t tokens, uint32_t k, uint32_t H,
+                               float* __restrict__ out) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;   // float4 index
+    const size_t per_token = H / 4;
+    if (i >= static_cast<size_t>(tokens) * per_token) return;
+    const size_t t = i / per_token, c = i % per_token;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t r = 0; r < k; ++r) {
+        const float4 v = reinterpret_cast<const float4*>(pair_out + (t * k + r) * H)[c];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    reinterpret_cast<float4*>(out + t * H)[c] = acc;
+}
+
+// Gate/up operand from BF16 inputs (no lo part) or F32 inputs (hi + lo); the
+// down operand always has the lo part.
+using GateUpBf16 = GemmLayout<0, 0, 4, 3>;
+using GateUpF32 = GemmLayout<0, 1, 3, 2>;
+using DownLay = GemmLayout<1, 1, 4, 2>;
+static_assert(GateUpBf16::total <= 227 * 1024, "gate/up (bf16) shared memory");
+static_assert(GateUpF32::total <= 227 * 1024, "gate/up (f32) shared memory");
+static_assert(DownLay::total <= 227 * 1024, "down shared memory");
+
+uint32_t max_tiles_for(uint32_t pairs, uint32_t E) { return pairs / kTileTokens + std::min(E, pairs) + 1; }
+
+size_t al256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+struct BatchSizes {
+    uint32_t pairs, max_tiles, max_padded;
+    size_t logits, ids, weights, rank, plan, tiles, slot_pair, bgu, sgu, act, bdn, sdn, pair_out;
+    size_t total;
+};
+
+BatchSizes batch_sizes(const MoeLayerDev& L, uint32_t T) {
+    BatchSizes z{};
+    z.pairs = T * L.top_k;
+    z.max_tiles = max_tiles_for(z.pairs, L.experts);
+    z.max_padded = z.pairs + 15u * z.max_tiles;
+    const size_t Sg = L.hidden / 256, Sd = L.inter / 256;
+    z.logits = al256(size_t(T) * L.experts * 4);
+    z.ids = al256(size_t(z.pairs) * 4);
+    z.weights = z.ids;
+    z.rank = z.ids;
+    z.plan = 256;
+    z.tiles = al256(size_t(z.max_tiles) * 4);
+    z.slot_pair = z.ids;
+    z.bgu = al256(size_t(z.max_padded) * Sg * (64 + 2) * 16);   // room for the hi + lo form
+    z.sgu = al256(size_t(z.max_padded) * Sg * 4);
+    z.act = al256(size_t(z.max_padded) * L.inter * 4);
+    z.bdn = al256(size_t(z.max_padded) * Sd * (64 + 2) * 16);
+    z.sdn = al256(size_t(z.max_padded) * Sd * 4);
+    z.pair_out = al256(size_t(z.pairs) * L.hidden * 4);
+    z.total = z.logits + z.ids + z.weights + z.rank + z.plan + 4 * z.tiles + z.slot_pair + z.bgu + z.sgu + z.act +
+              z.bdn + z.sdn + z.pair_out;
+    return z;
+}
+
+template <typename Kern>
+cudaError_t set_smem(Kern k, uint32_t bytes) {
+    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
+}  // namespace
+
+bool moe_batch_grouped(const MoeLayerDev& L) {
+    const auto al16 = [](const void* p, uint64_t n) {
+        return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && (n & 15u) == 0;
+    };
+    return L.gate_type == kQ4_K && L.up_type == kQ4_K && L.down_type == kQ4_K && L.shared_inter == 0 &&
+           L.hidden % 256 == 0 && L.inter % 256 == 0 && L.hidden >= 256 && L.inter >= 256 && L.gate && L.up &&
+           L.down && al16(L.gate, L.gate_slice) && al16(L.up, L.up_slice) && al16(L.down, L.down_slice) &&
+           L.experts >= 1 && L.experts <= 1024 && L.top_k >= 1 && L.top_k <= 64 && L.top_k <= L.experts;
+}
+
+uint64_t moe_batch_scratch_bytes(const MoeLayerDev& L, uint32_t max_tokens) {
+    return batch_sizes(L, max_tokens).total;
+}
+
+MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_tokens, void* base) {
+    const BatchSizes z = batch_sizes(L, max_tokens);
+    MoeBatchScratch S{};
+    S.max_tokens = max_tokens;
+    S.max_tiles = z.max_tiles;
+    S.max_padded = z.max_padded;
+    uint8_t* p = static_cast<uint8_t*>(base);
+    const auto take = [&](size_t n) {
+        uint8_t* q = p;
+        p += n;
+        return q;
+    };
+    S.logits = reinterpret_cast<float*>(take(z.logits));
+    S.ids = reinterpret_cast<uint32_t*>(take(z.ids));
+    S.weights = reinterpret_cast<float*>(take(z.weights));
+    S.rank = reinterpret_cast<uint32_t*>(take(z.rank));
+    S.plan = reinterpret_cast<uint32_t*>(take(z.plan));
+    S.tile_expert = reinterpret_cast<uint32_t*>(take(z.tiles));
+    S.tile_first = reinterpret_cast<uint32_t*>(take(z.tiles));
+    S.tile_n = reinterpret_cast<uint32_t*>(take(z.tiles));
+    S.tile_pad0 = reinterpret_cast<uint32_t*>(take(z.tiles));
+    S.slot_pair = reinterpret_cast<uint32_t*>(take(z.slot_pair));
+    S.b_gate_up = take(z.bgu);
+    S.s_gate_up = reinterpret_cast<float*>(take(z.sgu));
+    S.act = reinterpret_cast<float*>(take(z.act));
+    S.b_down = take(z.bdn);
+    S.s_down = reinterpret_cast<float*>(take(z.sdn));
+    S.pair_out = reinterpret_cast<float*>(take(z.pair_out));
+    return S;
+}
+
+cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, const void* x, uint32_t x_bf16,
+                             uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
+                             uint32_t* status, cudaStream_t stream, uint32_t* launches) {
+    uint32_t n = 0;
+    if (launches) *launches = 0;
+    if (!moe_batch_grouped(L) || tokens == 0 || tokens > S.max_tokens || !x || !out || !status)
+        return cudaErrorInvalidValue;
+    if (!logits && !L.router) return cudaErrorInvalidValue;
+    const uint32_t E = L.experts, k = L.top_k, H = L.hidden, I = L.inter;
+    const uint32_t pairs = tokens * k;
+    cudaError_t err;
+
+    CUtensorMap tg{}, tu{}, td{};
+    const uint64_t rb_in = row_bytes(kQ4_K, H), rb_dn = row_bytes(kQ4_K, I);
+    if (!encode_expert_map(&tg, L.gate, rb_in, I, E, L.gate_slice, 64) ||
+        !encode_expert_map(&tu, L.up, rb_in, I, E, L.up_slice, 64) ||
+        !encode_expert_map(&td, L.down, rb_dn, H, E, L.down_slice, 128))
+        return cudaErrorInvalidValue;
+
+    // 1. router
+    const float* lg = logits;
+    if (!lg) {
+        router_batch_kernel<<<dim3((tokens + 15) / 16, (E + 63) / 64), 256, 0, stream>>>(L.router, x, x_bf16, tokens,
+                                                                                          E, H, S.logits);
+        ++n;
+        lg = S.logits;
+    }
+    // 2. routes
+    if ((err = launch_route_experts(lg, E, k, L.flavour, L.normalize, L.expert_weights_scale, S.ids, S.weights,
+                                    status, stream, tokens)) != cudaSuccess)
+        return err;
+    ++n;
+    // 3. group
+    {
+        GroupOut o{S.plan, S.tile_expert, S.tile_first, S.tile_n, S.tile_pad0, S.slot_pair, S.rank};
+        const uint32_t smem = (kSortWarps + 4) * E * 4;
+        if ((err = set_smem(group_kernel, smem)) != cudaSuccess) return err;
+        group_kernel<<<1, kSortThreads, smem, stream>>>(S.ids, pairs, E, o);
+        ++n;
+    }
+    const int sms = device_sm_count();
+    // 4. pack x
+    PackArgs px{};
+    px.src = x;
+    px.src_bf16 = x_bf16;
+    px.by_token = 1;
+    px.top_k = k;
+    px.cols = H;
+    px.split = x_bf16 ? 0 : 1;
+    px.plan = S.plan;
+    px.tile_first = S.tile_first;
+    px.tile_n = S.tile_n;
+    px.tile_pad0 = S.tile_pad0;
+    px.slot_pair = S.slot_pair;
+    px.dst = S.b_gate_up;
+    px.dst_scale = S.s_gate_up;
+    const uint32_t max_tiles = max_tiles_for(pairs, E);
+    pack_kernel<<<max_tiles, kPackThreads, 0, stream>>>(px);
+    ++n;
+    // 5. gate/up
+    GemmArgs ga{};
+    ga.tm0 = tg;
+    ga.tm1 = tu;
+    ga.b = S.b_gate_up;
+    ga.b_scale = S.s_gate_up;
+    ga.plan = S.plan;
+    ga.tile_expert = S.tile_expert;
+    ga.tile_first = S.tile_first;
+    ga.tile_n = S.tile_n;
+    ga.tile_pad0 = S.tile_pad0;
+    ga.slot_pair = S.slot_pair;
+    ga.route_w = S.weights;
+    ga.out = S.act;
+    ga.K = H;
+    ga.rows = I;
+    ga.flavour = L.flavour;
+    ga.status = status;
+    if (x_bf16) {
+        auto kern = grouped_gemm_kernel<0, 0, 4, 3>;
+        if ((err = set_smem(kern, GateUpBf16::total)) != cudaSuccess) return err;
+        kern<<<sms, kGemmThreads, GateUpBf16::total, stream>>>(ga);
+    } else {
+        auto kern = grouped_gemm_kernel<0, 1, 3, 2>;
+        if ((err = set_smem(kern, GateUpF32::total)) != cudaSuccess) return err;
+        kern<<<sms, kGemmThreads, GateUpF32::total, stream>>>(ga);
+    }
+    ++n;
+    // 6. pack activations
+    PackArgs pa = px;
+    pa.src = S.act;
+    pa.src_bf16 = 0;
+    pa.by_token = 0;
+    pa.cols = I;
+    pa.split = 1;
+    pa.dst = S.b_down;
+    pa.dst_scale = S.s_down;
+    pack_kernel<<<max_tiles, kPackThreads, 0, stream>>>(pa);
+    ++n;
+    // 7. down
+    GemmArgs da = ga;
+    da.tm0 = td;
+    da.tm1 = td;
+    da.b = S.b_down;
+    da.b_scale = S.s_down;
+    da.out = S.pair_out;
+    da.K = I;
+    da.rows = H;
+    {
+        auto kern = grouped_gemm_kernel<1, 1, 4, 2>;
+        if ((err = set_smem(kern, DownLay::total)) != cudaSuccess) return err;
+        kern<<<sms, kGemmThreads, DownLay::total, stream>>>(da);
+    }
+    ++n;
+    // 8. combine
+    {
+        const size_t quads = static_cast<size_t>(tokens) * H / 4;
+        combine_kernel<<<static_cast<uint32_t>((quads + 255) / 256), 256, 0, stream>>>(S.pair_out, tokens, k, H, out);
+        ++n;
+    }
+    if (ids && ids != S.ids) {
+        if ((err = cudaMemcpyAsync(ids, S.ids, size_t(pairs) * 4, cudaMemcpyDeviceToDevice, stream)) != cudaSuccess)
+            return err;
+    }
+    if (weights && weights != S.weights) {
+        if ((err = cudaMemcpyAsync(weights, S.weights, size_t(pairs) * 4, cudaMemcpyDeviceToDevice, stream)) !=
+            cudaSuccess)
+            return err;
+    }
+    if (launches) *launches = n;
+    return cudaGetLastError();
+}
+
+}  // namespace pokit

@@ -2,6 +2,7 @@
 // sm_100a kernels.  Not part of the public C ABI (include/pokit_cuda.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,10 +19,16 @@ cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t 
 cudaError_t launch_dequantize(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
                               float* out, cudaStream_t stream);
 
-// Softmax top-k routing of E device logits (one warp); see route_warp.
+// Softmax top-k routing of `rows` device logits vectors of E entries (one CTA
+// per row): ids/weights receive k entries per row.
 cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, uint32_t flavour,
                                  uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
-                                 uint32_t* status, cudaStream_t stream);
+                                 uint32_t* status, cudaStream_t stream, uint32_t rows = 1);
+
+// TMA tensor map over a Q4_K expert tensor: (byte column, row, expert), boxes
+// of one superblock (144 bytes) by box_rows rows; cached per argument set.
+bool encode_expert_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows,
+                       uint64_t experts, uint64_t slice, uint32_t box_rows);
 
 // Fills `nblocks` GGUF blocks of `type` at dst from the counter-based
 // synthetic generator (seed, stream_id); see pokitlms_b200/synth.py.
@@ -110,6 +117,43 @@ cudaError_t launch_moe_block(const MoeLayerDev& L, const MoeScratch& S, const fl
 // layers[0] (x and the output in `out`, hidden floats).
 cudaError_t time_moe_kernel(const MoeLayerDev* layers, uint32_t count, const MoeScratch& S, uint32_t which,
                             uint32_t reps, float* out, cudaStream_t stream, float* avg_us);
+
+// ---------------------------------------------------------------------------
+// Batched tokens (prefill / batched decode): the grouped-expert path.
+// ---------------------------------------------------------------------------
+// Device scratch of one batched forward for up to `max_tokens` tokens.
+struct MoeBatchScratch {
+    uint32_t max_tokens = 0;
+    uint32_t max_tiles = 0;      // tile list capacity
+    uint32_t max_padded = 0;     // padded token-slot capacity
+    float* logits = nullptr;     // [tokens][experts] when the router runs here
+    uint32_t* ids = nullptr;     // [tokens][top_k] routes in rank order
+    float* weights = nullptr;    // [tokens][top_k] combine weights
+    uint32_t* rank = nullptr;    // [pairs] position of a (token, rank) pair within its expert
+    uint32_t* plan = nullptr;    // [4]: tiles, padded slots
+    uint32_t* tile_expert = nullptr, *tile_first = nullptr, *tile_n = nullptr, *tile_pad0 = nullptr;
+    uint32_t* slot_pair = nullptr;   // [pairs] expert-sorted slot -> pair (token * top_k + rank)
+    uint8_t* b_gate_up = nullptr;    // packed fp16 activations per tile (gate/up GEMM operand)
+    float* s_gate_up = nullptr;      // their per-(row, superblock) power-of-two scales
+    float* act = nullptr;            // [padded][inter] silu(gate) * up
+    uint8_t* b_down = nullptr;       // packed fp16 hi/lo activations (down GEMM operand)
+    float* s_down = nullptr;
+    float* pair_out = nullptr;       // [pairs][hidden] weighted expert outputs
+};
+
+// The grouped path serves this layer (Q4_K gate/up/down, no shared expert,
+// hidden and inter multiples of 256, TMA-aligned expert tensors).
+bool moe_batch_grouped(const MoeLayerDev& L);
+uint64_t moe_batch_scratch_bytes(const MoeLayerDev& L, uint32_t max_tokens);
+MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_tokens, void* base);
+
+// out[t] = MoE(x[t]) for `tokens` rows of x (F32, or BF16 when x_bf16), each
+// routed independently: by `logits` ([tokens][experts] F32 on the device)
+// when given, else by the layer's router.  ids/weights (may be null) receive
+// the routes.  `status` collects the sticky StatusBits.
+cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, const void* x, uint32_t x_bf16,
+                             uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
+                             uint32_t* status, cudaStream_t stream, uint32_t* launches);
 
 // Grid-wide barriers one layer of launch_moe_decode performs.
 uint32_t moe_barriers_per_layer();

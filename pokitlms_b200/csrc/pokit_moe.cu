@@ -963,7 +963,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(BlockArgs a) {
                a.next_router, nrb, [] { return true; }, ok);
 }
 
-// Routing of a standalone logits vector (pokit_cuda_route_experts).
+// Routing of standalone logits vectors (pokit_cuda_route_experts; the
+// batched MoE forward routes one row per token).
 __global__ void __launch_bounds__(kThreads, 1)
 route_logits_kernel(const float* __restrict__ logits, uint32_t E, uint32_t k, uint32_t flavour,
                     uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
@@ -976,6 +977,10 @@ route_logits_kernel(const float* __restrict__ logits, uint32_t E, uint32_t k, ui
     s.red = red;
     s.sel_id = sel_id;
     s.sel_w = sel_w;
+    // One CTA per logits row (a batch of tokens routes row by row).
+    logits += static_cast<size_t>(blockIdx.x) * E;
+    ids += static_cast<size_t>(blockIdx.x) * k;
+    weights += static_cast<size_t>(blockIdx.x) * k;
     for (uint32_t e = threadIdx.x; e < E; e += kThreads) lg[e] = logits[e];
     __syncthreads();
     route_core(lg, E, k, flavour, normalize, ew_scale, false, 0.0f, s, status);
@@ -1685,10 +1690,10 @@ MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base, uint32_t rep) {
 
 cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, uint32_t flavour,
                                  uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
-                                 uint32_t* status, cudaStream_t stream) {
-    if (k == 0 || k > E || k > kMaxTopK || E > kMaxExperts) return cudaErrorInvalidValue;
-    route_logits_kernel<<<1, kThreads, 0, stream>>>(logits, E, k, flavour, normalize, ew_scale,
-                                                    ids, weights, status);
+                                 uint32_t* status, cudaStream_t stream, uint32_t rows) {
+    if (k == 0 || k > E || k > kMaxTopK || E > kMaxExperts || rows == 0) return cudaErrorInvalidValue;
+    route_logits_kernel<<<rows, kThreads, 0, stream>>>(logits, E, k, flavour, normalize, ew_scale,
+                                                       ids, weights, status);
     return cudaGetLastError();
 }
 
@@ -1709,12 +1714,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // (byte column, row, expert) view of a Q4_K expert tensor: `rows` rows of
 // `row_bytes` per expert, experts `slice` bytes apart; boxes of one
-// superblock (144 bytes) by 16 rows.
-static bool encode_expert_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows,
-                              uint64_t experts, uint64_t slice) {
+// superblock (144 bytes) by `box_rows` rows.
+bool encode_expert_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows,
+                       uint64_t experts, uint64_t slice, uint32_t box_rows) {
     static std::mutex mu;
-    static std::map<std::tuple<const uint8_t*, uint64_t, uint64_t, uint64_t, uint64_t>, CUtensorMap> cache;
-    const auto key = std::make_tuple(base, row_bytes, rows, experts, slice);
+    static std::map<std::tuple<const uint8_t*, uint64_t, uint64_t, uint64_t, uint64_t, uint32_t>, CUtensorMap>
+        cache;
+    const auto key = std::make_tuple(base, row_bytes, rows, experts, slice, box_rows);
     std::lock_guard<std::mutex> lock(mu);
     const auto it = cache.find(key);
     if (it != cache.end()) {
@@ -1725,7 +1731,8 @@ static bool encode_expert_map(CUtensorMap* map, const uint8_t* base, uint64_t ro
     if (!encode) return false;
     const cuuint64_t dims[3] = {row_bytes, rows, experts};
     const cuuint64_t strides[2] = {row_bytes, slice};
-    const cuuint32_t box[3] = {144u, kBoxRows, 1u};
+    if (box_rows == 0 || box_rows > 256 || box_rows > rows) return false;
+    const cuuint32_t box[3] = {144u, box_rows, 1u};
     const cuuint32_t elem[3] = {1u, 1u, 1u};
     if (encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, elem,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1779,9 +1786,9 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
         MmaArgs ma{};
         const uint64_t rb_in = static_cast<uint64_t>(L.hidden >> 8) * 144u;
         const uint64_t rb_down = static_cast<uint64_t>(L.inter >> 8) * 144u;
-        if (!encode_expert_map(&ma.tm_gate, L.gate, rb_in, L.inter, L.experts, L.gate_slice) ||
-            !encode_expert_map(&ma.tm_up, L.up, rb_in, L.inter, L.experts, L.up_slice) ||
-            !encode_expert_map(&ma.tm_down, L.down, rb_down, L.hidden, L.experts, L.down_slice))
+        if (!encode_expert_map(&ma.tm_gate, L.gate, rb_in, L.inter, L.experts, L.gate_slice, kBoxRows) ||
+            !encode_expert_map(&ma.tm_up, L.up, rb_in, L.inter, L.experts, L.up_slice, kBoxRows) ||
+            !encode_expert_map(&ma.tm_down, L.down, rb_down, L.hidden, L.experts, L.down_slice, kBoxRows))
             return cudaErrorInvalidValue;
         ma.L = L;
         ma.next = nx;
@@ -1889,9 +1896,9 @@ cudaError_t time_moe_kernel(const MoeLayerDev* layers, uint32_t count, const Moe
         MmaArgs& ma = args[l];
         const uint64_t rb_in = static_cast<uint64_t>(L.hidden >> 8) * 144u;
         const uint64_t rb_down = static_cast<uint64_t>(L.inter >> 8) * 144u;
-        if (!encode_expert_map(&ma.tm_gate, L.gate, rb_in, L.inter, L.experts, L.gate_slice) ||
-            !encode_expert_map(&ma.tm_up, L.up, rb_in, L.inter, L.experts, L.up_slice) ||
-            !encode_expert_map(&ma.tm_down, L.down, rb_down, L.hidden, L.experts, L.down_slice))
+        if (!encode_expert_map(&ma.tm_gate, L.gate, rb_in, L.inter, L.experts, L.gate_slice, kBoxRows) ||
+            !encode_expert_map(&ma.tm_up, L.up, rb_in, L.inter, L.experts, L.up_slice, kBoxRows) ||
+            !encode_expert_map(&ma.tm_down, L.down, rb_down, L.hidden, L.experts, L.down_slice, kBoxRows))
             return cudaErrorInvalidValue;
         ma.L = L;
         ma.next = L;

@@ -103,9 +103,30 @@ def activation(hidden: int, seed: int, index: int = 0) -> np.ndarray:
     return rng.standard_normal(hidden, dtype=np.float32)
 
 
+def bf16_round(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """(BF16 bit patterns uint16, their F32 values) of x, rounded to nearest even."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    bits = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return bits, (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def grouped_inputs(tokens: int, experts: int, hidden: int, seed: int = 0, zipf: float = 1.1):
+    """A batch for the grouped-expert GEMM: activations ~ N(0, 1) rounded to
+    BF16 ([tokens, hidden] as BF16 bits and as F32) and router logits ~ N(0, 1)
+    plus a popularity bias -zipf * log(rank) over a seeded ranking of the
+    experts (a Zipf(zipf) skew of how often each expert is chosen)."""
+    rng = np.random.default_rng([seed, 0x6770])
+    bits, xf = bf16_round(rng.standard_normal((tokens, hidden), dtype=np.float32))
+    rank = rng.permutation(experts).astype(np.float64) + 1.0
+    bias = (-zipf * np.log(rank)).astype(np.float32)
+    logits = rng.standard_normal((tokens, experts), dtype=np.float32) + bias[None, :]
+    return bits, xf, logits.astype(np.float32)
+
+
 def stream_id(layer: int, tensor: int) -> int:
     """Stream id of one tensor of one layer (tensor ids as in pokit_cuda_moe_tensor)."""
     return layer * 16 + tensor
 
 
-__all__ = ["synth_blocks", "synth_matrix", "router_weights", "activation", "stream_id", "F32"]
+__all__ = ["synth_blocks", "synth_matrix", "router_weights", "activation", "bf16_round", "grouped_inputs",
+           "stream_id", "F32"]
