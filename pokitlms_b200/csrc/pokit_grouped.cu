@@ -37,7 +37,8 @@
 // Operand layout of a tile's packed activations (one superblock, Np = tile
 // tokens rounded up to 16): chunks of 8 fp16 (16 bytes) for chunk c (0..31,
 // or 0..63 with the lo parts in 32..63) and token row n at
-// (c * Np + n) * 16, then two chunks of sub-block sums (hi, lo).  Within a
+// (c * Np + n) * 16, then two chunks of sub-block sums (hi, lo), then Np
+// floats: each row's power-of-two scale.  Within a
 // superblock the K order is permuted to match the dequantiser's output: the
 // 32-bit tensor-memory column j = 32c + 4w + o (chunk c = 0..3 of the Q4_K
 // nibbles, word w = 0..7, nibble pair o = 0..3) holds the weights of
@@ -58,8 +59,6 @@ namespace pokit {
 namespace {
 
 constexpr uint32_t kTileTokens = 64;                  // N of one GEMM tile
-constexpr uint32_t kEpiWarps = 8;                     // dequantise + epilogue
-constexpr uint32_t kGemmThreads = (kEpiWarps + 2) * 32;  // + loader warp + MMA warp
 constexpr uint32_t kQStage = 128u * 144u;             // one superblock of 128 rows
 constexpr uint32_t kSortThreads = 512;
 constexpr uint32_t kSortWarps = kSortThreads / 32;
@@ -239,8 +238,10 @@ struct PackArgs {
     const uint32_t* tile_pad0;
     const uint32_t* slot_pair;
     uint8_t* dst;
-    float* dst_scale;
 };
+
+// Bytes of one packed superblock row: (kc8 + 2) chunks of 16 bytes + a scale.
+__host__ __device__ constexpr uint32_t packed_row_bytes(uint32_t kc8) { return (kc8 + 2) * 16 + 4; }
 
 __device__ __forceinline__ uint4 pack8_half(const float (&v)[8]) {
     uint4 r;
@@ -251,110 +252,137 @@ __device__ __forceinline__ uint4 pack8_half(const float (&v)[8]) {
     return r;
 }
 
+// Loads lane's 8 elements of superblock s of a source row.
+__device__ __forceinline__ void pack_load(const PackArgs& a, size_t at, float (&v)[8]) {
+    if (a.src_bf16) {
+        const uint4 q = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.src) + at);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+    } else {
+        const float4 p0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + at);
+        const float4 p1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + at + 4);
+        v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+        v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+    }
+}
+
+// One warp per padded row n of a tile (grid: tiles x 8, 8 warps per CTA);
+// the row's superblocks are loaded four at a time before any is packed.
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
     __shared__ float stage[kPackThreads / 32][8 * 33];
     const uint32_t tile = blockIdx.x;
     if (tile >= a.plan[0]) return;
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t n = blockIdx.y * (kPackThreads / 32) + warp;
     const uint32_t n_valid = a.tile_n[tile], np = round16(n_valid), pad0 = a.tile_pad0[tile];
-    const uint32_t first = a.tile_first[tile];
+    if (n >= np) return;
     const uint32_t S = a.cols / 256, kc8 = a.split ? 64u : 32u;
-    const uint32_t stage_bytes = (kc8 + 2) * np * 16;
-    uint8_t* tile_base = a.dst + static_cast<size_t>(pad0) * S * (kc8 + 2) * 16;
+    const uint32_t stage_bytes = packed_row_bytes(kc8) * np;
+    uint8_t* tile_base = a.dst + static_cast<size_t>(pad0) * S * packed_row_bytes(kc8);
+    const bool valid = n < n_valid;
+    const uint32_t row = !valid ? 0u : a.by_token ? a.slot_pair[a.tile_first[tile] + n] / a.top_k : pad0 + n;
     float* st = stage[warp];
-    for (uint32_t item = warp; item < np * S; item += kPackThreads / 32) {
-        const uint32_t n = item / S, s = item % S;
-        float v[8];
+    for (uint32_t s0 = 0; s0 < S; s0 += 4) {
+        float v[4][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-        if (n < n_valid) {
-            const uint32_t row = a.by_token ? a.slot_pair[first + n] / a.top_k : pad0 + n;
-            const size_t at = static_cast<size_t>(row) * a.cols + s * 256 + lane * 8;
-            if (a.src_bf16) {
-                const uint4 q = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.src) + at);
-                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        for (uint32_t q = 0; q < 4; ++q) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    v[2 * i] = __uint_as_float(w[i] << 16);
-                    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-                }
-            } else {
-                const float4 p0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + at);
-                const float4 p1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.src) + at + 4);
-                v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
-                v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
-            }
+            for (int i = 0; i < 8; ++i) v[q][i] = 0.f;
+            if (valid && s0 + q < S)
+                pack_load(a, static_cast<size_t>(row) * a.cols + (s0 + q) * 256 + lane * 8, v[q]);
         }
-        // Power-of-two scale bringing max |v| of the superblock into [512, 1024):
-        // sub-block sums stay below 2^15 and the scaling itself is exact.
-        float amax = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        for (uint32_t q = 0; q < 4; ++q) {
+            const uint32_t s = s0 + q;
+            if (s >= S) break;
+            // Power-of-two scale bringing max |v| of the superblock into
+            // [512, 1024): sub-block sums stay below 2^15 and the scaling is exact.
+            float amax = 0.f;
 #pragma unroll
-        for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
-        int ex = 0;
-        if (amax > 0.f && amax <= 3.0e38f) frexpf(amax, &ex);
-        const int sig = max(-100, min(100, ex - 10));
-        const float down = __int_as_float((127 - sig) << 23);
-        float part = 0.f;
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[q][i]));
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            v[i] *= down;
-            part += v[i];
-            st[33 * (lane / 4) + 8 * (lane % 4) + i] = v[i];
-        }
-        // Sub-block j = lane / 4 sums over its four lanes.
-        part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
-        part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
-        __syncwarp();
-        uint8_t* region = tile_base + static_cast<size_t>(s) * stage_bytes;
-        {
-            const uint32_t c = lane >> 3, w = lane & 7;
-            const float* b0 = st + 33 * (2 * c) + 4 * w;
-            const float* b1 = st + 33 * (2 * c + 1) + 4 * w;
-            float e[8] = {b0[0], b0[2], b0[1], b0[3], b1[0], b1[2], b1[1], b1[3]};
-            float hi[8], lo[8];
+            for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
+            int ex = 0;
+            if (amax > 0.f && amax <= 3.0e38f) frexpf(amax, &ex);
+            const int sig = max(-100, min(100, ex - 10));
+            const float down = __int_as_float((127 - sig) << 23);
+            float part = 0.f;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                hi[i] = __half2float(__float2half_rn(e[i]));
-                lo[i] = e[i] - hi[i];
+                const float x = v[q][i] * down;
+                part += x;
+                st[33 * (lane / 4) + 8 * (lane % 4) + i] = x;
             }
-            *reinterpret_cast<uint4*>(region + (static_cast<size_t>(lane) * np + n) * 16) = pack8_half(hi);
-            if (a.split)
-                *reinterpret_cast<uint4*>(region + (static_cast<size_t>(32 + lane) * np + n) * 16) = pack8_half(lo);
+            // Sub-block j = lane / 4 sums over its four lanes.
+            part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
+            part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
+            __syncwarp();
+            uint8_t* region = tile_base + static_cast<size_t>(s) * stage_bytes;
+            {
+                const uint32_t c = lane >> 3, w = lane & 7;
+                const float* b0 = st + 33 * (2 * c) + 4 * w;
+                const float* b1 = st + 33 * (2 * c + 1) + 4 * w;
+                const float e[8] = {b0[0], b0[2], b0[1], b0[3], b1[0], b1[2], b1[1], b1[3]};
+                float hi[8], lo[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    hi[i] = __half2float(__float2half_rn(e[i]));
+                    lo[i] = e[i] - hi[i];
+                }
+                *reinterpret_cast<uint4*>(region + (static_cast<size_t>(lane) * np + n) * 16) = pack8_half(hi);
+                if (a.split)
+                    *reinterpret_cast<uint4*>(region + (static_cast<size_t>(32 + lane) * np + n) * 16) =
+                        pack8_half(lo);
+            }
+            if ((lane & 3) == 0) {
+                const uint32_t j = lane >> 2;
+                const __half h = __float2half_rn(part);
+                const __half l = __float2half_rn(part - __half2float(h));
+                reinterpret_cast<__half*>(region + (static_cast<size_t>(kc8) * np + n) * 16)[j] = h;
+                reinterpret_cast<__half*>(region + (static_cast<size_t>(kc8 + 1) * np + n) * 16)[j] = l;
+            }
+            if (lane == 0)
+                reinterpret_cast<float*>(region + static_cast<size_t>(kc8 + 2) * np * 16)[n] =
+                    __int_as_float((127 + sig) << 23);
+            __syncwarp();
         }
-        if ((lane & 3) == 0) {
-            const uint32_t j = lane >> 2;
-            const __half h = __float2half_rn(part);
-            const __half l = __float2half_rn(part - __half2float(h));
-            reinterpret_cast<__half*>(region + (static_cast<size_t>(kc8) * np + n) * 16)[j] = h;
-            reinterpret_cast<__half*>(region + (static_cast<size_t>(kc8 + 1) * np + n) * 16)[j] = l;
-        }
-        if (lane == 0)
-            a.dst_scale[static_cast<size_t>(pad0) * S + s * np + n] = __int_as_float((127 + sig) << 23);
-        __syncwarp();
     }
 }
 
 // ---------------------------------------------------------------------------
 // 5/7. The grouped GEMM.  Persistent: one CTA per SM takes units
-// blockIdx.x, blockIdx.x + gridDim.x, ...
+// blockIdx.x, blockIdx.x + gridDim.x, ...  Warp roles:
+//   warps 0..7    epilogue: two per tensor-memory lane quarter, each folds
+//                 half of the tile's token columns of every superblock's
+//                 accumulators into registers (d, dmin, activation scale)
+//   warps 8..15   dequantise: two per lane quarter, each writes half of a
+//                 superblock's K columns of A = s_j * q (fp16) into tensor
+//                 memory, and the mins m_j into shared memory
+//   warp 16       loader: TMA boxes of the Q4_K rows (144 bytes x 64 or 128
+//                 rows), one bulk copy of packed activations per superblock
+//   warp 17       owns tensor memory; one lane issues the MMAs
 //
-// Warps 0..7 (two per tensor-memory lane quarter) dequantise the Q4_K rows
-// of superblock s + 1 into tensor memory while the tensor core works on s,
-// then fold s's accumulators into registers.  Warp 8 loads weights (TMA
-// boxes of 144 bytes x 64/128 rows) and the packed activations (one bulk
-// copy per superblock).  Warp 9 owns tensor memory and issues the MMAs.
+// Tensor memory (512 columns): A double-buffered in columns [0, 256); per
+// buffer b the accumulators of the quants at 256 + 128b and of the mins at
+// 256 + 128b + 64 (N <= 64 tokens).
 //
-// Tensor memory (512 columns): A (scales x quants, fp16) double-buffered in
-// columns [0, 256); per buffer b the accumulators of the quants at 256 + 128b
-// and of the mins at 256 + 128b + 64 (N <= 64 tokens).
+// The tensor core takes ~68 cycles per M = 128, K = 16 MMA for any N <= 128
+// (measured on B200), so a superblock costs 17 MMAs x 68 cycles whatever the
+// tile's token count.
 // ---------------------------------------------------------------------------
+constexpr uint32_t kEpWarps = 8, kDqWarps = 8;
+constexpr uint32_t kLoadWarp = kEpWarps + kDqWarps, kMmaWarp = kLoadWarp + 1;
+constexpr uint32_t kGemmThreads = (kMmaWarp + 1) * 32;
+constexpr uint32_t kDdRing = 4;   // (d, dmin) hand-off ring from dequantisers to epilogue
+
 struct GemmArgs {
     CUtensorMap tm0;          // gate (mode 0) or down (mode 1)
     CUtensorMap tm1;          // up (mode 0)
-    const uint8_t* b;
-    const float* b_scale;
+    const uint8_t* b;         // packed activations (pack_kernel layout)
     const uint32_t* plan;
     const uint32_t* tile_expert;
     const uint32_t* tile_first;
@@ -372,17 +400,41 @@ struct GemmArgs {
 template <int kMode, int kSplit, int kQ, int kB>
 struct GemmLayout {
     static constexpr uint32_t kc8 = kSplit ? 64u : 32u;
-    static constexpr uint32_t bstage = (kc8 + 2) * kTileTokens * 16;
+    static constexpr uint32_t bstage = packed_row_bytes(kc8) * kTileTokens;
     static constexpr uint32_t q_off = 0;
     static constexpr uint32_t b_off = q_off + kQ * kQStage;
-    static constexpr uint32_t amin_off = b_off + kB * bstage;            // [2][2][128][16 B]
-    static constexpr uint32_t dd_off = amin_off + 2 * 4096;               // [2][2][128] float2
-    static constexpr uint32_t xch_off = dd_off + 2 * 2 * 128 * 8;         // [64 cols][64 rows] (mode 0)
+    static constexpr uint32_t amin_off = b_off + kB * bstage;             // [2][2][128][16 B]
+    static constexpr uint32_t dd_off = amin_off + 2 * 4096;                // [kDdRing][128] float2
+    static constexpr uint32_t xch_off = dd_off + kDdRing * 128 * 8;        // [64 cols][64 rows] (mode 0)
     static constexpr uint32_t bar_off = xch_off + (kMode == 0 ? 64 * 64 * 4 : 0);
-    static constexpr uint32_t nbars = 2 * kQ + 2 * kB + 8 + 3;
+    static constexpr uint32_t nbars = 2 * kQ + 2 * kB + 8 + kDdRing + 3;
     static constexpr uint32_t misc_off = bar_off + nbars * 8;
     static constexpr uint32_t total = misc_off + 16;
 };
+
+// Eight fp16 pairs s * q of one 32-bit word of nibbles: byte pairs (0, 2) and
+// (1, 3), low nibbles scaled by s_lo, high nibbles by s_hi.  A low nibble q
+// becomes 1024 + q and a high nibble 1024 + 16 q (masked in place); one fp16
+// FMA then gives q * s exactly.
+struct NibbleScales {
+    uint32_t lo_mul, lo_add, hi_mul, hi_add;
+};
+__device__ __forceinline__ NibbleScales nibble_scales(uint32_t s_lo, uint32_t s_hi) {
+    const float lo = static_cast<float>(s_lo), hi = static_cast<float>(s_hi);
+    NibbleScales n;
+    n.lo_mul = pack_half2(lo, lo);
+    n.lo_add = pack_half2(-1024.f * lo, -1024.f * lo);
+    n.hi_mul = pack_half2(hi * 0.0625f, hi * 0.0625f);
+    n.hi_add = pack_half2(-64.f * hi, -64.f * hi);
+    return n;
+}
+__device__ __forceinline__ void dequant_word(uint32_t W, const NibbleScales& n, uint32_t* out4) {
+    const uint32_t W8 = W >> 8;
+    out4[0] = hfma2u((W & 0x000F000Fu) | kHalfMagic, n.lo_mul, n.lo_add);    // bytes 0, 2 low
+    out4[1] = hfma2u((W8 & 0x000F000Fu) | kHalfMagic, n.lo_mul, n.lo_add);   // bytes 1, 3 low
+    out4[2] = hfma2u((W & 0x00F000F0u) | kHalfMagic, n.hi_mul, n.hi_add);    // bytes 0, 2 high
+    out4[3] = hfma2u((W8 & 0x00F000F0u) | kHalfMagic, n.hi_mul, n.hi_add);   // bytes 1, 3 high
+}
 
 template <int kMode, int kSplit, int kQ, int kB>
 __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __grid_constant__ GemmArgs a) {
@@ -402,28 +454,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
     uint64_t* a_free = a_full + 2;       // [2] MMAs reading A done
     uint64_t* acc_full = a_free + 2;     // [2] accumulators ready
     uint64_t* acc_free = acc_full + 2;   // [2] accumulators read
-    uint64_t* xch_full = acc_free + 2;   // up rows written (mode 0)
-    uint64_t* xch_free = xch_full + 1;   // up rows consumed (mode 0)
-    uint64_t* drain = xch_free + 1;      // all MMAs complete
+    uint64_t* dd_full = acc_free + 2;    // [kDdRing] (d, dmin) of a superblock written
+    uint64_t* xch_full = dd_full + kDdRing;   // up rows written (mode 0)
+    uint64_t* xch_free = xch_full + 1;        // up rows consumed (mode 0)
+    uint64_t* drain = xch_free + 1;           // all MMAs complete
     uint32_t* misc = reinterpret_cast<uint32_t*>(smem + Lay::misc_off);
     volatile uint32_t* abort_flag = misc + 1;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp == kEpiWarps + 1) {
+    if (warp == kMmaWarp) {
         tmem_alloc(misc, 512);
         tmem_relinquish();
     }
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kQ; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, kEpiWarps); }
-        for (int i = 0; i < kB; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1); }
+        for (int i = 0; i < kQ; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, kDqWarps); }
+        // A slot of packed activations is free once the MMAs read it (commit)
+        // and the epilogue warps read its scales.
+        for (int i = 0; i < kB; ++i) { mbar_init(b_full + i, 1); mbar_init(b_empty + i, 1 + kEpWarps); }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(a_full + i, kEpiWarps);
+            mbar_init(a_full + i, kDqWarps);
             mbar_init(a_free + i, 1);
             mbar_init(acc_full + i, 1);
-            mbar_init(acc_free + i, kEpiWarps);
+            mbar_init(acc_free + i, kEpWarps);
         }
-        mbar_init(xch_full, kEpiWarps / 2);
-        mbar_init(xch_free, kEpiWarps / 2);
+        for (uint32_t i = 0; i < kDdRing; ++i) mbar_init(dd_full + i, kDqWarps);
+        mbar_init(xch_full, kEpWarps / 2);
+        mbar_init(xch_free, kEpWarps / 2);
         mbar_init(drain, 1);
         misc[1] = 0;
         mbar_fence_init();
@@ -445,8 +501,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
         *abort_flag = 1;
         return false;
     };
+    // A warp's lanes take every wait together so that the warp-wide
+    // tensor-memory instructions after it run converged.
+    const auto wait_warp = [&](uint64_t* bar, uint32_t parity) -> bool {
+        return __all_sync(0xFFFFFFFFu, wait(bar, parity)) != 0;
+    };
 
-    if (warp == kEpiWarps) {
+    if (warp == kLoadWarp) {
         // ---------------- loader ----------------
         if (lane == 0) {
             int32_t last_q[kQ], last_b[kB];
@@ -457,8 +518,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
             for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
                 const uint32_t tile = u / mblocks, mb = u % mblocks;
                 const uint32_t e = a.tile_expert[tile], np = round16(a.tile_n[tile]);
-                const uint32_t stage = (Lay::kc8 + 2) * np * 16;
-                const uint8_t* bsrc = a.b + static_cast<size_t>(a.tile_pad0[tile]) * S * (Lay::kc8 + 2) * 16;
+                const uint32_t stage = packed_row_bytes(Lay::kc8) * np;
+                const uint8_t* bsrc = a.b + static_cast<size_t>(a.tile_pad0[tile]) * S * packed_row_bytes(Lay::kc8);
                 for (uint32_t s = 0; s < S; ++s, ++g) {
                     const uint32_t qs = g % kQ, bs = g % kB;
                     if (!(ok = wait(q_empty + qs, ((g / kQ) & 1) ^ 1))) break;
@@ -484,7 +545,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
                     if (last_b[i] >= 0) mbar_wait_ns(b_full + i, (static_cast<uint32_t>(last_b[i]) / kB) & 1);
             }
         }
-    } else if (warp == kEpiWarps + 1) {
+    } else if (warp == kMmaWarp) {
         // ---------------- MMA issue ----------------
         if (lane == 0) {
             uint32_t g = 0;
@@ -522,132 +583,128 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
             tc_commit(drain);
             mbar_wait_ns(drain, 0);
         }
-    } else {
-        // ---------------- dequantise + epilogue ----------------
-        const uint32_t q4 = warp & 3, kh = warp >> 2;   // lane quarter; K half (dequantise) and N half (epilogue)
+    } else if (warp >= kEpWarps) {
+        // ---------------- dequantise ----------------
+        const uint32_t dw = warp - kEpWarps;
+        const uint32_t q4 = dw & 3, kh = dw >> 2;          // lane quarter, K half
         const uint32_t r = 32 * q4 + lane;                 // tile row = tensor-memory lane
+        const uint32_t lane_base = (32 * q4) << 16;
+        uint32_t g = 0;
+        bool ok = true;
+        for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
+            for (uint32_t s = 0; s < S; ++s, ++g) {
+                const uint32_t qs = g % kQ, buf = g & 1;
+                if (!(ok = wait_warp(q_full + qs, (g / kQ) & 1))) break;
+                if (!(ok = wait_warp(a_free + buf, ((g >> 1) & 1) ^ 1))) break;
+                const uint8_t* row = qbuf + qs * kQStage + r * 144;
+                const uint32_t dm = *reinterpret_cast<const uint32_t*>(row);
+                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(row + 4);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(row + 8);
+                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(row + 12);
+                // 6-bit scales / mins (k_scale_min): bytes q[0..11] = w0 | w1 | w2.
+                uint32_t sc[8], mn[8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t qj = (w0 >> (8 * j)) & 0xFF, qj4 = (w1 >> (8 * j)) & 0xFF;
+                    const uint32_t qj8 = (w2 >> (8 * j)) & 0xFF;
+                    sc[j] = qj & 63;
+                    mn[j] = qj4 & 63;
+                    sc[j + 4] = (qj8 & 0xF) | ((qj >> 6) << 4);
+                    mn[j + 4] = (qj8 >> 4) | ((qj4 >> 6) << 4);
+                }
+                if (kh == 0)
+                    dd[(g % kDdRing) * 128 + r] =
+                        make_float2(half_bits_to_float(dm & 0xFFFF), half_bits_to_float(dm >> 16));
+                {
+                    uint4 mv;
+                    mv.x = pack_half2(static_cast<float>(mn[0]), static_cast<float>(mn[1]));
+                    mv.y = pack_half2(static_cast<float>(mn[2]), static_cast<float>(mn[3]));
+                    mv.z = pack_half2(static_cast<float>(mn[4]), static_cast<float>(mn[5]));
+                    mv.w = pack_half2(static_cast<float>(mn[6]), static_cast<float>(mn[7]));
+                    *reinterpret_cast<uint4*>(amin + buf * 4096 + kh * 2048 + r * 16) = mv;
+                }
+#pragma unroll
+                for (uint32_t cc = 0; cc < 2; ++cc) {
+                    const uint32_t c = 2 * kh + cc;
+                    const uint4 qa = *reinterpret_cast<const uint4*>(row + 16 + 32 * c);
+                    const uint4 qb = *reinterpret_cast<const uint4*>(row + 16 + 32 * c + 16);
+                    const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                    const NibbleScales ns = nibble_scales(sc[2 * c], sc[2 * c + 1]);
+                    uint32_t v[32];
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) dequant_word(words[w], ns, v + 4 * w);
+                    tmem_st32(tbase + lane_base + buf * 128 + 32 * c, v);
+                }
+                tmem_wait_st();
+                fence_async_shared();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(a_full + buf);
+                    mbar_arrive(q_empty + qs);
+                    mbar_arrive(dd_full + g % kDdRing);
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const uint32_t q4 = warp & 3, nh = warp >> 2;      // lane quarter, N half
+        const uint32_t r = 32 * q4 + lane;
         const uint32_t lane_base = (32 * q4) << 16;
         float acc[32];
         uint32_t g = 0, ui = 0;
         bool ok = true;
-        // The warp's lanes take every wait together so that the warp-wide
-        // tensor-memory instructions after it run converged.
-        const auto wait_warp = [&](uint64_t* bar, uint32_t parity) -> bool {
-            return __all_sync(0xFFFFFFFFu, wait(bar, parity)) != 0;
-        };
-
-        // Superblock gg of the CTA's sequence: A = s_j * q (fp16, exact) into
-        // tensor-memory buffer gg & 1, the mins m_j into shared memory.
-        const auto dequant = [&](uint32_t gg) -> bool {
-            const uint32_t qs = gg % kQ, buf = gg & 1;
-            if (!wait_warp(q_full + qs, (gg / kQ) & 1)) return false;
-            if (!wait_warp(a_free + buf, ((gg >> 1) & 1) ^ 1)) return false;
-            const uint8_t* row = qbuf + qs * kQStage + r * 144;
-            const uint32_t dm = *reinterpret_cast<const uint32_t*>(row);
-            const uint32_t w0 = *reinterpret_cast<const uint32_t*>(row + 4);
-            const uint32_t w1 = *reinterpret_cast<const uint32_t*>(row + 8);
-            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(row + 12);
-            // 6-bit scales / mins (k_scale_min): bytes q[0..11] = w0 | w1 | w2.
-            uint32_t sc[8], mn[8];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t qj = (w0 >> (8 * j)) & 0xFF, qj4 = (w1 >> (8 * j)) & 0xFF, qj8 = (w2 >> (8 * j)) & 0xFF;
-                sc[j] = qj & 63;
-                mn[j] = qj4 & 63;
-                sc[j + 4] = (qj8 & 0xF) | ((qj >> 6) << 4);
-                mn[j + 4] = (qj8 >> 4) | ((qj4 >> 6) << 4);
-            }
-            dd[(buf * 2 + kh) * 128 + r] = make_float2(half_bits_to_float(dm & 0xFFFF), half_bits_to_float(dm >> 16));
-            {
-                uint4 mv;
-                mv.x = pack_half2(static_cast<float>(mn[0]), static_cast<float>(mn[1]));
-                mv.y = pack_half2(static_cast<float>(mn[2]), static_cast<float>(mn[3]));
-                mv.z = pack_half2(static_cast<float>(mn[4]), static_cast<float>(mn[5]));
-                mv.w = pack_half2(static_cast<float>(mn[6]), static_cast<float>(mn[7]));
-                *reinterpret_cast<uint4*>(amin + buf * 4096 + kh * 2048 + r * 16) = mv;
-            }
-#pragma unroll
-            for (uint32_t cc = 0; cc < 2; ++cc) {
-                const uint32_t c = 2 * kh + cc;
-                const uint4 qa = *reinterpret_cast<const uint4*>(row + 16 + 32 * c);
-                const uint4 qb = *reinterpret_cast<const uint4*>(row + 16 + 32 * c + 16);
-                const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                const float slo = static_cast<float>(sc[2 * c]), shi = static_cast<float>(sc[2 * c + 1]);
-                const uint32_t s2lo = pack_half2(slo, slo), s2hi = pack_half2(shi, shi);
-                const uint32_t n2lo = pack_half2(-1024.f * slo, -1024.f * slo);
-                const uint32_t n2hi = pack_half2(-1024.f * shi, -1024.f * shi);
-                uint32_t v[32];
-#pragma unroll
-                for (int w = 0; w < 8; ++w) {
-                    const uint32_t W = words[w];
-                    v[4 * w + 0] = hfma2u((W & 0x000F000Fu) | kHalfMagic, s2lo, n2lo);
-                    v[4 * w + 1] = hfma2u(((W >> 8) & 0x000F000Fu) | kHalfMagic, s2lo, n2lo);
-                    v[4 * w + 2] = hfma2u(((W >> 4) & 0x000F000Fu) | kHalfMagic, s2hi, n2hi);
-                    v[4 * w + 3] = hfma2u(((W >> 12) & 0x000F000Fu) | kHalfMagic, s2hi, n2hi);
-                }
-                const uint32_t col = tbase + lane_base + buf * 128 + 32 * c;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t (&vv)[8] = *reinterpret_cast<const uint32_t(*)[8]>(v + 8 * i);
-                    tmem_st8(col + 8 * i, vv);
-                }
-            }
-            tmem_wait_st();
-            fence_async_shared();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(a_full + buf);
-                mbar_arrive(q_empty + qs);
-            }
-            return true;
-        };
-
-        // Folds superblock gg (index s within the unit) into acc.
-        const auto epilogue = [&](uint32_t gg, uint32_t s, uint32_t np, uint32_t pad0) -> bool {
-            const uint32_t buf = gg & 1;
-            if (!wait_warp(acc_full + buf, (gg >> 1) & 1)) return false;
-            tc_fence_after();
-            const float2 dm = dd[(buf * 2 + kh) * 128 + r];
-            const float* scl = a.b_scale + static_cast<size_t>(pad0) * S + s * np;
-            const uint32_t hn = np >> 1;
-            const uint32_t acc_q = tbase + lane_base + 256 + buf * 128, acc_m = acc_q + 64;
-#pragma unroll
-            for (uint32_t c = 0; c < 4; ++c) {
-                if (8 * c < hn) {
-                    const uint32_t col = kh * hn + 8 * c;
-                    uint32_t qv[8], mv[8];
-                    tmem_ld8(acc_q + col, qv);
-                    tmem_ld8(acc_m + col, mv);
-                    tmem_wait_ld();
-                    const float4 s0 = *reinterpret_cast<const float4*>(scl + col);
-                    const float4 s1 = *reinterpret_cast<const float4*>(scl + col + 4);
-                    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        acc[8 * c + i] = fmaf(
-                            fmaf(dm.x, __uint_as_float(qv[i]), -dm.y * __uint_as_float(mv[i])), sv[i], acc[8 * c + i]);
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_free + buf);
-            return true;
-        };
-
         for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ui) {
             const uint32_t tile = u / mblocks, mb = u % mblocks;
             const uint32_t n_valid = a.tile_n[tile], np = round16(n_valid), pad0 = a.tile_pad0[tile];
-            const uint32_t hn = np >> 1;
+            const uint32_t hn = np >> 1, c0 = nh * hn;
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-            if (!(ok = dequant(g))) break;
-            for (uint32_t s = 0; ok && s < S; ++s) {
-                if (s + 1 < S && !(ok = dequant(g + s + 1))) break;
-                ok = epilogue(g + s, s, np, pad0);
+            for (uint32_t s = 0; s < S; ++s, ++g) {
+                const uint32_t buf = g & 1, bs = g % kB;
+                if (!(ok = wait_warp(acc_full + buf, (g >> 1) & 1))) break;
+                if (!(ok = wait_warp(dd_full + g % kDdRing, (g / kDdRing) & 1))) break;
+                if (!(ok = wait_warp(b_full + bs, (g / kB) & 1))) break;   // scales visible here
+                tc_fence_after();
+                const float2 dm = dd[(g % kDdRing) * 128 + r];
+                const float* scl = reinterpret_cast<const float*>(bbuf + bs * Lay::bstage + (Lay::kc8 + 2) * np * 16);
+                const uint32_t acc_q = tbase + lane_base + 256 + buf * 128 + c0, acc_m = acc_q + 64;
+#pragma unroll
+                for (uint32_t c2 = 0; c2 < 4; c2 += 2) {
+                    if (8 * c2 < hn) {
+                        uint32_t qv[2][8], mv[2][8];
+#pragma unroll
+                        for (uint32_t c = 0; c < 2; ++c) {
+                            if (8 * (c2 + c) < hn) {
+                                tmem_ld8(acc_q + 8 * (c2 + c), qv[c]);
+                                tmem_ld8(acc_m + 8 * (c2 + c), mv[c]);
+                            }
+                        }
+                        tmem_wait_ld();
+#pragma unroll
+                        for (uint32_t c = 0; c < 2; ++c) {
+                            if (8 * (c2 + c) < hn) {
+                                const float4 s0 = *reinterpret_cast<const float4*>(scl + c0 + 8 * (c2 + c));
+                                const float4 s1 = *reinterpret_cast<const float4*>(scl + c0 + 8 * (c2 + c) + 4);
+                                const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    float& A = acc[8 * (c2 + c) + i];
+                                    A = fmaf(fmaf(dm.x, __uint_as_float(qv[c][i]), -dm.y * __uint_as_float(mv[c][i])),
+                                             sv[i], A);
+                                }
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(acc_free + buf);
+                    mbar_arrive(b_empty + bs);
+                }
             }
             if (!ok) break;
-            g += S;
             if (kMode == 0) {
                 // Rows 0..63 hold gate, 64..127 up: silu(gate) * up per token.
                 if (q4 >= 2) {
@@ -656,7 +713,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
                     for (uint32_t c = 0; c < 4; ++c)
                         if (8 * c < hn)
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) xch[(kh * hn + 8 * c + i) * 64 + (r - 64)] = acc[8 * c + i];
+                            for (int i = 0; i < 8; ++i) xch[(c0 + 8 * c + i) * 64 + (r - 64)] = acc[8 * c + i];
                     __syncwarp();
                     if (lane == 0) mbar_arrive(xch_full);
                 } else {
@@ -666,7 +723,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
                         if (8 * c < hn) {
 #pragma unroll
                             for (int i = 0; i < 8; ++i) {
-                                const uint32_t col = kh * hn + 8 * c + i;
+                                const uint32_t col = c0 + 8 * c + i;
                                 if (col < n_valid) {
                                     const float h = silu_times(acc[8 * c + i], xch[col * 64 + r], a.flavour);
                                     a.out[static_cast<size_t>(pad0 + col) * a.rows + mb * 64 + r] = h;
@@ -684,7 +741,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
                     if (8 * c < hn) {
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const uint32_t col = kh * hn + 8 * c + i;
+                            const uint32_t col = c0 + 8 * c + i;
                             if (col < n_valid) {
                                 const uint32_t p = a.slot_pair[first + col];
                                 a.out[static_cast<size_t>(p) * a.rows + mb * 128 + r] = a.route_w[p] * acc[8 * c + i];
@@ -698,7 +755,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
 
     tc_fence_before();
     __syncthreads();
-    if (warp == kEpiWarps + 1) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
     }
@@ -740,7 +797,7 @@ size_t al256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
 struct BatchSizes {
     uint32_t pairs, max_tiles, max_padded;
-    size_t logits, ids, weights, rank, plan, tiles, slot_pair, bgu, sgu, act, bdn, sdn, pair_out;
+    size_t logits, ids, weights, rank, plan, tiles, slot_pair, bgu, act, bdn, pair_out;
     size_t total;
 };
 
@@ -757,14 +814,12 @@ BatchSizes batch_sizes(const MoeLayerDev& L, uint32_t T) {
     z.plan = 256;
     z.tiles = al256(size_t(z.max_tiles) * 4);
     z.slot_pair = z.ids;
-    z.bgu = al256(size_t(z.max_padded) * Sg * (64 + 2) * 16);   // room for the hi + lo form
-    z.sgu = al256(size_t(z.max_padded) * Sg * 4);
+    z.bgu = al256(size_t(z.max_padded) * Sg * packed_row_bytes(64));   // room for the hi + lo form
     z.act = al256(size_t(z.max_padded) * L.inter * 4);
-    z.bdn = al256(size_t(z.max_padded) * Sd * (64 + 2) * 16);
-    z.sdn = al256(size_t(z.max_padded) * Sd * 4);
+    z.bdn = al256(size_t(z.max_padded) * Sd * packed_row_bytes(64));
     z.pair_out = al256(size_t(z.pairs) * L.hidden * 4);
-    z.total = z.logits + z.ids + z.weights + z.rank + z.plan + 4 * z.tiles + z.slot_pair + z.bgu + z.sgu + z.act +
-              z.bdn + z.sdn + z.pair_out;
+    z.total = z.logits + z.ids + z.weights + z.rank + z.plan + 4 * z.tiles + z.slot_pair + z.bgu + z.act + z.bdn +
+              z.pair_out;
     return z;
 }
 
@@ -812,10 +867,8 @@ MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_token
     S.tile_pad0 = reinterpret_cast<uint32_t*>(take(z.tiles));
     S.slot_pair = reinterpret_cast<uint32_t*>(take(z.slot_pair));
     S.b_gate_up = take(z.bgu);
-    S.s_gate_up = reinterpret_cast<float*>(take(z.sgu));
     S.act = reinterpret_cast<float*>(take(z.act));
     S.b_down = take(z.bdn);
-    S.s_down = reinterpret_cast<float*>(take(z.sdn));
     S.pair_out = reinterpret_cast<float*>(take(z.pair_out));
     return S;
 }
@@ -875,16 +928,15 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     px.tile_pad0 = S.tile_pad0;
     px.slot_pair = S.slot_pair;
     px.dst = S.b_gate_up;
-    px.dst_scale = S.s_gate_up;
     const uint32_t max_tiles = max_tiles_for(pairs, E);
-    pack_kernel<<<max_tiles, kPackThreads, 0, stream>>>(px);
+    const dim3 pack_grid(max_tiles, kTileTokens / (kPackThreads / 32));
+    pack_kernel<<<pack_grid, kPackThreads, 0, stream>>>(px);
     ++n;
     // 5. gate/up
     GemmArgs ga{};
     ga.tm0 = tg;
     ga.tm1 = tu;
     ga.b = S.b_gate_up;
-    ga.b_scale = S.s_gate_up;
     ga.plan = S.plan;
     ga.tile_expert = S.tile_expert;
     ga.tile_first = S.tile_first;
@@ -915,15 +967,13 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     pa.cols = I;
     pa.split = 1;
     pa.dst = S.b_down;
-    pa.dst_scale = S.s_down;
-    pack_kernel<<<max_tiles, kPackThreads, 0, stream>>>(pa);
+    pack_kernel<<<pack_grid, kPackThreads, 0, stream>>>(pa);
     ++n;
     // 7. down
     GemmArgs da = ga;
     da.tm0 = td;
     da.tm1 = td;
     da.b = S.b_down;
-    da.b_scale = S.s_down;
     da.out = S.pair_out;
     da.K = I;
     da.rows = H;

@@ -133,11 +133,9 @@ struct MoeBatchScratch {
     uint32_t* plan = nullptr;    // [4]: tiles, padded slots
     uint32_t* tile_expert = nullptr, *tile_first = nullptr, *tile_n = nullptr, *tile_pad0 = nullptr;
     uint32_t* slot_pair = nullptr;   // [pairs] expert-sorted slot -> pair (token * top_k + rank)
-    uint8_t* b_gate_up = nullptr;    // packed fp16 activations per tile (gate/up GEMM operand)
-    float* s_gate_up = nullptr;      // their per-(row, superblock) power-of-two scales
+    uint8_t* b_gate_up = nullptr;    // packed fp16 activations + scales per tile (gate/up operand)
     float* act = nullptr;            // [padded][inter] silu(gate) * up
-    uint8_t* b_down = nullptr;       // packed fp16 hi/lo activations (down GEMM operand)
-    float* s_down = nullptr;
+    uint8_t* b_down = nullptr;       // packed fp16 hi/lo activations + scales (down operand)
     float* pair_out = nullptr;       // [pairs][hidden] weighted expert outputs
 };
 

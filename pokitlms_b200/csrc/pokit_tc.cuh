@@ -94,6 +94,17 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                  "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                  : "memory");
 }
+// 32 consecutive columns per lane in one instruction.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
@@ -123,19 +134,22 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 // Waits for phase `parity` of the mbarrier for at most `limit_ns` of wall
-// time; false when it gave up.
+// time; false when it gave up.  Each try_wait suspends the thread until the
+// phase completes or `kSuspendNs` passes, so waiting warps take no issue
+// slots from working ones.
+constexpr uint32_t kSuspendNs = 1000000u;
 __device__ __forceinline__ bool mbar_wait_ns(uint64_t* m, uint32_t parity, uint64_t limit_ns = 1000000000ull) {
     uint32_t ok = 0;
     uint64_t start = 0;
     for (uint32_t it = 0; !ok; ++it) {
         asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
             : "=r"(ok)
-            : "r"(smem_addr(m)), "r"(parity)
+            : "r"(smem_addr(m)), "r"(parity), "r"(kSuspendNs)
             : "memory");
         if (ok) break;
         if (it == 0) start = global_ns();
-        else if ((it & 63u) == 0 && global_ns() - start > limit_ns) return false;
+        else if (global_ns() - start > limit_ns) return false;
     }
     return true;
 }

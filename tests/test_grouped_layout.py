@@ -1,0 +1,138 @@
+"""CPU check of the grouped-expert GEMM's operand layout (pokit_grouped.cu).
+
+Restates, in numpy, what the kernels put where:
+  * the dequantiser's tensor-memory columns: column j = 32c + 4w + o holds
+    the fp16 pair (low, high) of s_j * q for the Q4_K nibbles picked by one
+    mask (and one 8-bit shift) of qs word w of chunk c;
+  * pack_kernel's activation chunks: chunk 8c + w holds eight activations in
+    the order that makes K element 2j + h of the activation operand meet the
+    half h of column j;
+  * the min operand: A = (m_0..m_7, m_0..m_7), B = (sub-block sums hi, lo);
+and checks that d * (A . B) - dmin * (mins) reproduces the reference dot of
+the decoded row (the oracle's decode of src/quantized_linear.cpp:166-205)
+with every fp16 rounding the kernels make.
+"""
+import numpy as np
+
+import cases
+from oracle import oracle as O
+from pokitlms_b200 import synth
+
+
+def scales_mins(block):
+    q = block[4:16].astype(np.uint32)
+    sc = np.zeros(8, np.uint32)
+    mn = np.zeros(8, np.uint32)
+    for j in range(4):
+        sc[j] = q[j] & 63
+        mn[j] = q[j + 4] & 63
+        sc[j + 4] = (q[j + 8] & 0xF) | ((q[j] >> 6) << 4)
+        mn[j + 4] = (q[j + 8] >> 4) | ((q[j + 4] >> 6) << 4)
+    return sc, mn
+
+
+def fp16_fma(a, b, c):
+    """One fp16 FMA (exact product and sum, one rounding to fp16)."""
+    return np.float16(float(a) * float(b) + float(c))
+
+
+def a_columns(block):
+    """(128, 2) fp16 values of the tensor-memory columns for one superblock row,
+    produced the way dequant_word does: low nibbles as 1024 + q times s minus
+    1024 s, high nibbles masked in place as 1024 + 16 q times s / 16 minus 64 s."""
+    sc, _ = scales_mins(block)
+    qs = block[16:144]
+    cols = np.zeros((128, 2), np.float16)
+    for c in range(4):
+        s_lo, s_hi = float(sc[2 * c]), float(sc[2 * c + 1])
+        for w in range(8):
+            W = int.from_bytes(bytes(qs[32 * c + 4 * w: 32 * c + 4 * w + 4]), "little")
+            W8 = W >> 8
+            for o, (word, mask) in enumerate([(W, 0x000F000F), (W8, 0x000F000F), (W, 0x00F000F0),
+                                              (W8, 0x00F000F0)]):
+                m = word & mask
+                for h in range(2):
+                    biased = 1024 + ((m >> (16 * h)) & 0xFF)      # fp16 bits 0x6400 | field
+                    if mask == 0x000F000F:
+                        cols[32 * c + 4 * w + o, h] = fp16_fma(biased, s_lo, -1024 * s_lo)
+                    else:
+                        cols[32 * c + 4 * w + o, h] = fp16_fma(biased, s_hi / 16, -64 * s_hi)
+    return cols
+
+
+def b_chunks(x):
+    """(32, 8) activation chunks of one superblock (pack_kernel's order)."""
+    xs = x.reshape(8, 32)
+    out = np.zeros((32, 8), x.dtype)
+    for c in range(4):
+        for w in range(8):
+            b0, b1 = xs[2 * c, 4 * w:4 * w + 4], xs[2 * c + 1, 4 * w:4 * w + 4]
+            out[8 * c + w] = [b0[0], b0[2], b0[1], b0[3], b1[0], b1[2], b1[1], b1[3]]
+    return out
+
+
+def grouped_dot(block, x, split):
+    """One superblock row . x the way the kernels compute it (float64 sums)."""
+    d = float(np.frombuffer(bytes(block[0:2]), np.float16)[0])
+    dmin = float(np.frombuffer(bytes(block[2:4]), np.float16)[0])
+    _, mn = scales_mins(block)
+    amax = float(np.max(np.abs(x)))
+    ex = int(np.frexp(amax)[1]) if amax > 0 else 0
+    sig = max(-100, min(100, ex - 10))
+    xs = (x.astype(np.float64) * 2.0 ** -sig).astype(np.float32)   # exact power-of-two scaling
+    hi = xs.astype(np.float16)
+    lo = (xs - hi.astype(np.float32)).astype(np.float16)
+    cols = a_columns(block).astype(np.float64)
+    main = 0.0
+    for part in ([hi, lo] if split else [hi]):
+        bk = b_chunks(part.astype(np.float64)).reshape(-1)       # K order kappa = 0..255
+        main += float(np.sum(cols[:, 0] * bk[0::2] + cols[:, 1] * bk[1::2]))
+    sums = xs.reshape(8, 32).sum(axis=1, dtype=np.float32)
+    s_hi = sums.astype(np.float16)
+    s_lo = (sums - s_hi.astype(np.float32)).astype(np.float16)
+    mins = float(np.sum(mn.astype(np.float64) * (s_hi.astype(np.float64) + s_lo.astype(np.float64))))
+    return (d * main - dmin * mins) * 2.0 ** sig
+
+
+def test_dequantised_columns_are_exact_scale_times_quant():
+    blocks = synth.synth_blocks(cases.Q4_K, 16, seed=5, stream_id=1).reshape(16, 144)
+    for b in range(16):
+        sc, _ = scales_mins(blocks[b])
+        cols = a_columns(blocks[b]).astype(np.float64)
+        qs = blocks[b][16:144]
+        for c in range(4):
+            lo = (qs[32 * c:32 * c + 32] & 0xF).astype(np.float64) * sc[2 * c]
+            hi = (qs[32 * c:32 * c + 32] >> 4).astype(np.float64) * sc[2 * c + 1]
+            assert sorted(cols[32 * c:32 * c + 32][:, :].ravel()) == sorted(np.concatenate([lo, hi]))
+
+
+def test_operand_layout_reproduces_q4k_dot():
+    blocks = synth.synth_blocks(cases.Q4_K, 24, seed=7, stream_id=3).reshape(24, 144)
+    rng = np.random.default_rng(1)
+    for b in range(24):
+        block = blocks[b]
+        w = O.dequantize_row(cases.Q4_K, block, 256).astype(np.float64)
+        # BF16 activations (exact in fp16 after scaling, no lo part) ...
+        _, xb = synth.bf16_round(rng.standard_normal(256, dtype=np.float32))
+        ref = float(np.dot(w, xb.astype(np.float64)))
+        scale = float(np.sum(np.abs(w * xb)))
+        assert abs(grouped_dot(block, xb, split=False) - ref) <= 1e-6 * scale
+        # ... and F32 activations of any magnitude with the hi + lo split.
+        xf = rng.standard_normal(256).astype(np.float32) * np.float32(10.0 ** rng.uniform(-3, 4))
+        ref = float(np.dot(w, xf.astype(np.float64)))
+        scale = float(np.sum(np.abs(w * xf)))
+        assert abs(grouped_dot(block, xf, split=True) - ref) <= 1e-6 * scale
+
+
+def test_single_fp16_part_is_not_enough_for_f32():
+    """Why F32 activations carry a lo part: hi alone misses ~2^-12 per element."""
+    blocks = synth.synth_blocks(cases.Q4_K, 8, seed=8, stream_id=3).reshape(8, 144)
+    rng = np.random.default_rng(2)
+    worst = 0.0
+    for b in range(8):
+        w = O.dequantize_row(cases.Q4_K, blocks[b], 256).astype(np.float64)
+        xf = rng.standard_normal(256).astype(np.float32)
+        ref = float(np.dot(w, xf.astype(np.float64)))
+        scale = float(np.sum(np.abs(w * xf)))
+        worst = max(worst, abs(grouped_dot(blocks[b], xf, split=False) - ref) / scale)
+    assert worst > 1e-5
