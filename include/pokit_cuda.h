@@ -172,6 +172,13 @@ typedef struct pokit_cuda_moe_config {
     const uint32_t* layer_down_types; /* optional [layers] override of down_type */
     size_t shared_inter;              /* 0 = no shared expert */
     uint32_t shared_gate_type, shared_up_type, shared_down_type;
+    /* Expert parallelism: the handle holds experts [expert_first,
+     * expert_first + expert_count) of every layer (expert_count 0 = all).
+     * The router stays whole; a sharded handle serves the batched forward
+     * only and returns the contribution of its experts (the partial sums of
+     * all shards add up to the block's output). */
+    size_t expert_first;
+    size_t expert_count;
 } pokit_cuda_moe_config;
 
 /* Host payloads of one layer in GGUF layout.  NULL entries are skipped. */

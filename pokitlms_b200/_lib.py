@@ -63,6 +63,8 @@ class MoeConfig(C.Structure):
         ("shared_gate_type", C.c_uint32),
         ("shared_up_type", C.c_uint32),
         ("shared_down_type", C.c_uint32),
+        ("expert_first", C.c_size_t),
+        ("expert_count", C.c_size_t),
     ]
 
 

@@ -121,7 +121,10 @@ class CudaMoeBackend:
                  gate_type: int = 12, up_type: int = 12, down_type: int = 12,
                  layer_down_types: list[int] | None = None, shared_inter: int = 0,
                  shared_gate_type: int = 8, shared_up_type: int = 8, shared_down_type: int = 8,
-                 device: int = 0):
+                 device: int = 0, expert_first: int = 0, expert_count: int = 0):
+        """expert_first / expert_count select an expert shard (count 0 = all
+        experts): the handle then holds only those experts' gate/up/down
+        slices and its batched forward returns their contribution."""
         self._ldt = None
         if layer_down_types is not None:
             self._ldt = (C.c_uint32 * layers)(*layer_down_types)
@@ -129,13 +132,16 @@ class CudaMoeBackend:
                         int(normalize_top_k), expert_weights_scale, rms_epsilon, gate_type,
                         up_type, down_type,
                         C.cast(self._ldt, C.POINTER(C.c_uint32)) if self._ldt else None,
-                        shared_inter, shared_gate_type, shared_up_type, shared_down_type)
+                        shared_inter, shared_gate_type, shared_up_type, shared_down_type,
+                        expert_first, expert_count)
         h = C.c_void_p()
         call("pokit_cuda_moe_create", C.byref(cfg), C.byref(h))
         self._h = h
         self.layers, self.hidden, self.inter = layers, hidden, inter
         self.experts, self.top_k, self.flavour = experts, top_k, flavour
         self.shared_inter = shared_inter
+        self.expert_first = expert_first if expert_count else 0
+        self.expert_count = expert_count if expert_count else experts
 
     # -- weights ------------------------------------------------------------
     def tensor_bytes(self, layer: int, tensor: int) -> int:

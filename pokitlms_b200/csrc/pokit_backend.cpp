@@ -90,6 +90,10 @@ public:
         if (!quant_supported(c.gate_type) || !quant_supported(c.up_type) ||
             !quant_supported(c.down_type))
             throw std::invalid_argument("unsupported expert tensor type");
+        if (c.expert_count && (c.expert_first >= c.experts || c.expert_count > c.experts - c.expert_first))
+            throw std::invalid_argument("expert shard out of range");
+        if (c.expert_count && c.expert_count < c.experts && c.shared_inter)
+            throw std::invalid_argument("an expert shard cannot hold the shared expert");
         if (c.shared_inter) {
             if (c.flavour != POKIT_CUDA_MOE_QWEN35 || c.shared_inter % 256 ||
                 !quant_supported(c.shared_gate_type) || !quant_supported(c.shared_up_type) ||
@@ -97,6 +101,8 @@ public:
                 throw std::invalid_argument("invalid shared expert configuration");
         }
         device_ = c.device;
+        expert_first_ = c.expert_count ? c.expert_first : 0;
+        expert_local_ = c.expert_count ? c.expert_count : c.experts;
         DeviceScope scope(device_);
         layer_down_.assign(c.layers, c.down_type);
         if (c.layer_down_types) {
@@ -131,7 +137,8 @@ public:
         check(cudaMalloc(&scratch_, scratch_bytes_), "cudaMalloc(scratch)");
         check(cudaMemset(scratch_, 0, scratch_bytes_), "cudaMemset(scratch)");
         S_ = moe_scratch_carve(devs_[0], scratch_);
-        for (size_t l = 0; l < c.layers; ++l) check(prepare_moe_block(devs_[l]), "prepare MoE kernels");
+        if (!sharded())
+            for (size_t l = 0; l < c.layers; ++l) check(prepare_moe_block(devs_[l]), "prepare MoE kernels");
         check(cudaMalloc(&devs_dev_, sizeof(MoeLayerDev) * c.layers), "cudaMalloc(layer table)");
         check(cudaMemcpy(devs_dev_, devs_.data(), sizeof(MoeLayerDev) * c.layers,
                          cudaMemcpyHostToDevice), "upload layer table");
@@ -170,9 +177,9 @@ public:
         if (layer >= cfg_.layers) return 0;
         switch (t) {
             case POKIT_CUDA_MOE_ROUTER: return E * H * 4;
-            case POKIT_CUDA_MOE_GATE: return E * I * row_bytes(cfg_.gate_type, H);
-            case POKIT_CUDA_MOE_UP: return E * I * row_bytes(cfg_.up_type, H);
-            case POKIT_CUDA_MOE_DOWN: return E * H * row_bytes(layer_down_[layer], I);
+            case POKIT_CUDA_MOE_GATE: return expert_local_ * I * row_bytes(cfg_.gate_type, H);
+            case POKIT_CUDA_MOE_UP: return expert_local_ * I * row_bytes(cfg_.up_type, H);
+            case POKIT_CUDA_MOE_DOWN: return expert_local_ * H * row_bytes(layer_down_[layer], I);
             case POKIT_CUDA_MOE_FFN_NORM: return H * 4;
             case POKIT_CUDA_MOE_SHARED_ROUTER: return SI ? H * 4 : 0;
             case POKIT_CUDA_MOE_SHARED_GATE: return SI ? SI * row_bytes(cfg_.shared_gate_type, H) : 0;
@@ -222,25 +229,32 @@ public:
         if (bytes == 0 || !quant_supported(type))
             throw std::invalid_argument("only quantised expert tensors can be synthesised");
         DeviceScope scope(device_);
-        guard(launch_synth_blocks(type, seed, stream_id, bytes / block_bytes(type), tensor_ptr(layer, t),
-                                  stream_), "synthesize");
+        // A shard holds blocks [first * per_expert, ...) of the whole tensor's
+        // stream, so every shard sees the same weights as one whole pool.
+        const bool expert_tensor =
+            t == POKIT_CUDA_MOE_GATE || t == POKIT_CUDA_MOE_UP || t == POKIT_CUDA_MOE_DOWN;
+        const uint64_t nblocks = bytes / block_bytes(type);
+        const uint64_t first_block = expert_tensor ? expert_first_ * (nblocks / expert_local_) : 0;
+        guard(launch_synth_blocks(type, seed, stream_id, nblocks, tensor_ptr(layer, t), stream_, first_block),
+              "synthesize");
         guard(cudaStreamSynchronize(stream_), "synthesize");
         kernel_launches_ += 1;
         mark_resident(layer, t);
     }
 
     void expert_view(size_t layer, uint32_t matrix, size_t expert, const void** ptr, size_t* bytes) const {
-        if (layer >= cfg_.layers || expert >= cfg_.experts ||
+        if (layer >= cfg_.layers || expert < expert_first_ || expert >= expert_first_ + expert_local_ ||
             (matrix != POKIT_CUDA_MOE_GATE && matrix != POKIT_CUDA_MOE_UP && matrix != POKIT_CUDA_MOE_DOWN))
-            throw std::invalid_argument("expert view out of range");
-        const uint64_t slice = tensor_bytes(layer, matrix) / cfg_.experts;
-        *ptr = tensor_ptr(layer, matrix) + expert * slice;
+            throw std::invalid_argument("expert view out of range (or not held by this shard)");
+        const uint64_t slice = tensor_bytes(layer, matrix) / expert_local_;
+        *ptr = tensor_ptr(layer, matrix) + (expert - expert_first_) * slice;
         *bytes = slice;
         ++hits_;
     }
 
     void forward(size_t layer, const float* x, float* out, uint32_t* ids, float* w, cudaStream_t s) {
         ensure_ok();
+        refuse_sharded();
         if (layer >= cfg_.layers) throw std::invalid_argument("layer out of range");
         if (!x || !out) throw std::invalid_argument("input and output are required");
         DeviceScope scope(device_);
@@ -275,6 +289,7 @@ public:
                   "grouped MoE batch");
             kernel_launches_ += n;
         } else {
+            refuse_sharded();
             if (x_type != POKIT_CUDA_INPUT_F32)
                 throw std::invalid_argument("BF16 input needs the grouped path (Q4_K experts, no shared expert)");
             if (logits) throw std::invalid_argument("caller logits need the grouped path (Q4_K experts, no shared expert)");
@@ -328,6 +343,7 @@ public:
     // layers [first, first + count), launched back to back.
     float time_kernel(uint32_t which, size_t first, size_t count, uint32_t reps, float* work, cudaStream_t s) {
         ensure_ok();
+        refuse_sharded();
         if (count == 0 || first + count > cfg_.layers) throw std::invalid_argument("layer range out of bounds");
         if (!work) throw std::invalid_argument("a device buffer of hidden floats is required");
         DeviceScope scope(device_);
@@ -362,6 +378,7 @@ public:
 
     void decode_layers(size_t first, size_t count, float* hidden, cudaStream_t s) {
         ensure_ok();
+        refuse_sharded();
         if (count == 0 || first >= cfg_.layers || count > cfg_.layers - first)
             throw std::invalid_argument("layer range out of bounds");
         if (!hidden) throw std::invalid_argument("hidden state is required");
@@ -488,6 +505,8 @@ private:
         L.hidden = static_cast<uint32_t>(cfg_.hidden);
         L.inter = static_cast<uint32_t>(cfg_.inter);
         L.experts = static_cast<uint32_t>(cfg_.experts);
+        L.expert_first = static_cast<uint32_t>(expert_first_);
+        L.expert_local = static_cast<uint32_t>(expert_local_);
         L.top_k = static_cast<uint32_t>(cfg_.top_k);
         L.flavour = cfg_.flavour;
         L.normalize = cfg_.normalize_top_k ? 1u : 0u;
@@ -500,9 +519,9 @@ private:
         L.gate = tensor_ptr(l, POKIT_CUDA_MOE_GATE);
         L.up = tensor_ptr(l, POKIT_CUDA_MOE_UP);
         L.down = tensor_ptr(l, POKIT_CUDA_MOE_DOWN);
-        L.gate_slice = tensor_bytes(l, POKIT_CUDA_MOE_GATE) / cfg_.experts;
-        L.up_slice = tensor_bytes(l, POKIT_CUDA_MOE_UP) / cfg_.experts;
-        L.down_slice = tensor_bytes(l, POKIT_CUDA_MOE_DOWN) / cfg_.experts;
+        L.gate_slice = tensor_bytes(l, POKIT_CUDA_MOE_GATE) / expert_local_;
+        L.up_slice = tensor_bytes(l, POKIT_CUDA_MOE_UP) / expert_local_;
+        L.down_slice = tensor_bytes(l, POKIT_CUDA_MOE_DOWN) / expert_local_;
         L.ffn_norm = reinterpret_cast<const float*>(tensor_ptr(l, POKIT_CUDA_MOE_FFN_NORM));
         if (cfg_.shared_inter) {
             L.shared_inter = static_cast<uint32_t>(cfg_.shared_inter);
@@ -532,6 +551,12 @@ private:
         return (resident_[layer] & need) == need;
     }
 
+    bool sharded() const { return expert_local_ != cfg_.experts; }
+    void refuse_sharded() const {
+        if (sharded())
+            throw std::invalid_argument("an expert-shard handle serves pokit_cuda_moe_forward_batch (grouped path) only");
+    }
+
     void ensure_ok() const {
         if (failed_) throw std::runtime_error("CUDA MoE backend failed earlier: " + failure_);
     }
@@ -547,6 +572,7 @@ private:
 
     pokit_cuda_moe_config cfg_;
     int device_ = 0;
+    size_t expert_first_ = 0, expert_local_ = 0;   // experts this handle holds
     std::vector<uint32_t> layer_down_;
     std::vector<std::array<uint64_t, 9>> offsets_;
     uint8_t* pool_ = nullptr;

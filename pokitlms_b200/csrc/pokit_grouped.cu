@@ -126,9 +126,11 @@ __global__ void __launch_bounds__(256) router_batch_kernel(const float* __restri
 }
 
 // ---------------------------------------------------------------------------
-// 3. Group: stable counting sort of pairs p = t * k + r by expert ids[p].
-// Pairs of one expert keep increasing p.  Writes the tile list and the slot
-// -> pair map.  One CTA.
+// 3. Group: stable counting sort of pairs p = t * k + r by expert ids[p],
+// keeping the pairs whose expert this device holds ([e_first, e_first + E));
+// the sort runs over local expert indices ids[p] - e_first.  Pairs of one
+// expert keep increasing p.  Writes the tile list and the slot -> pair map.
+// One CTA.
 // ---------------------------------------------------------------------------
 struct GroupOut {
     uint32_t* plan;        // [0] tiles, [1] padded slots
@@ -141,7 +143,7 @@ struct GroupOut {
 };
 
 __global__ void __launch_bounds__(kSortThreads, 1) group_kernel(const uint32_t* __restrict__ ids, uint32_t pairs,
-                                                                uint32_t E, GroupOut o) {
+                                                                uint32_t e_first, uint32_t E, GroupOut o) {
     extern __shared__ uint32_t sm[];
     uint32_t* wc = sm;                          // [kSortWarps][E]
     uint32_t* total = wc + kSortWarps * E;      // [E]
@@ -153,8 +155,9 @@ __global__ void __launch_bounds__(kSortThreads, 1) group_kernel(const uint32_t* 
     __syncthreads();
     for (uint32_t base = 0; base < pairs; base += kSortThreads) {
         const uint32_t p = base + tid;
-        const bool valid = p < pairs;
-        const uint32_t e = valid ? min(ids[p], E - 1) : 0xFFFFFFFFu;
+        const uint32_t el = p < pairs ? ids[p] - e_first : 0xFFFFFFFFu;   // wraps when below e_first
+        const bool valid = el < E;
+        const uint32_t e = valid ? el : 0xFFFFFFFFu;
         for (uint32_t i = lane; i < E; i += 32) wc[warp * E + i] = 0;
         __syncwarp();
         const uint32_t m = __match_any_sync(0xFFFFFFFFu, e);
@@ -217,8 +220,8 @@ __global__ void __launch_bounds__(kSortThreads, 1) group_kernel(const uint32_t* 
         }
     }
     for (uint32_t p = tid; p < pairs; p += kSortThreads) {
-        const uint32_t e = min(ids[p], E - 1);
-        o.slot_pair[off_slot[e] + o.rank[p]] = p;
+        const uint32_t e = ids[p] - e_first;
+        if (e < E) o.slot_pair[off_slot[e] + o.rank[p]] = p;
     }
 }
 
@@ -763,9 +766,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
 
 // ---------------------------------------------------------------------------
 // 8. Combine: out[t] = sum_r pair_out[t * k + r] in rank order from 0
-// (the reference adds w_r * y_r in that order, qwen3_moe_runner.cpp:688-690).
+// (the reference adds w_r * y_r in that order, qwen3_moe_runner.cpp:688-690),
+// over the ranks whose expert this device holds.
 // ---------------------------------------------------------------------------
-__global__ void combine_kernel(const float* __restrict__ pair_out, uint32_t tokens, uint32_t k, uint32_t H,
+__global__ void combine_kernel(const float* __restrict__ pair_out, const uint32_t* __restrict__ ids,
+                               uint32_t e_first, uint32_t e_count, uint32_t tokens, uint32_t k, uint32_t H,
                                float* __restrict__ out) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;   // float4 index
     const size_t per_token = H / 4;
@@ -773,6 +778,7 @@ __global__ void combine_kernel(const float* __restrict__ pair_out, uint32_t toke
     const size_t t = i / per_token, c = i % per_token;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (uint32_t r = 0; r < k; ++r) {
+        if (ids[t * k + r] - e_first >= e_count) continue;   // an expert of another shard
         const float4 v = reinterpret_cast<const float4*>(pair_out + (t * k + r) * H)[c];
         acc.x += v.x;
         acc.y += v.y;
@@ -804,7 +810,7 @@ struct BatchSizes {
 BatchSizes batch_sizes(const MoeLayerDev& L, uint32_t T) {
     BatchSizes z{};
     z.pairs = T * L.top_k;
-    z.max_tiles = max_tiles_for(z.pairs, L.experts);
+    z.max_tiles = max_tiles_for(z.pairs, L.expert_local);
     z.max_padded = z.pairs + 15u * z.max_tiles;
     const size_t Sg = L.hidden / 256, Sd = L.inter / 256;
     z.logits = al256(size_t(T) * L.experts * 4);
@@ -837,7 +843,8 @@ bool moe_batch_grouped(const MoeLayerDev& L) {
     return L.gate_type == kQ4_K && L.up_type == kQ4_K && L.down_type == kQ4_K && L.shared_inter == 0 &&
            L.hidden % 256 == 0 && L.inter % 256 == 0 && L.hidden >= 256 && L.inter >= 256 && L.gate && L.up &&
            L.down && al16(L.gate, L.gate_slice) && al16(L.up, L.up_slice) && al16(L.down, L.down_slice) &&
-           L.experts >= 1 && L.experts <= 1024 && L.top_k >= 1 && L.top_k <= 64 && L.top_k <= L.experts;
+           L.experts >= 1 && L.experts <= 1024 && L.top_k >= 1 && L.top_k <= 64 && L.top_k <= L.experts &&
+           L.expert_local >= 1 && L.expert_first + L.expert_local <= L.experts;
 }
 
 uint64_t moe_batch_scratch_bytes(const MoeLayerDev& L, uint32_t max_tokens) {
@@ -882,14 +889,15 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         return cudaErrorInvalidValue;
     if (!logits && !L.router) return cudaErrorInvalidValue;
     const uint32_t E = L.experts, k = L.top_k, H = L.hidden, I = L.inter;
+    const uint32_t EL = L.expert_local, E0 = L.expert_first;   // experts held here
     const uint32_t pairs = tokens * k;
     cudaError_t err;
 
     CUtensorMap tg{}, tu{}, td{};
     const uint64_t rb_in = row_bytes(kQ4_K, H), rb_dn = row_bytes(kQ4_K, I);
-    if (!encode_expert_map(&tg, L.gate, rb_in, I, E, L.gate_slice, 64) ||
-        !encode_expert_map(&tu, L.up, rb_in, I, E, L.up_slice, 64) ||
-        !encode_expert_map(&td, L.down, rb_dn, H, E, L.down_slice, 128))
+    if (!encode_expert_map(&tg, L.gate, rb_in, I, EL, L.gate_slice, 64) ||
+        !encode_expert_map(&tu, L.up, rb_in, I, EL, L.up_slice, 64) ||
+        !encode_expert_map(&td, L.down, rb_dn, H, EL, L.down_slice, 128))
         return cudaErrorInvalidValue;
 
     // 1. router
@@ -908,9 +916,9 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     // 3. group
     {
         GroupOut o{S.plan, S.tile_expert, S.tile_first, S.tile_n, S.tile_pad0, S.slot_pair, S.rank};
-        const uint32_t smem = (kSortWarps + 4) * E * 4;
+        const uint32_t smem = (kSortWarps + 4) * EL * 4;
         if ((err = set_smem(group_kernel, smem)) != cudaSuccess) return err;
-        group_kernel<<<1, kSortThreads, smem, stream>>>(S.ids, pairs, E, o);
+        group_kernel<<<1, kSortThreads, smem, stream>>>(S.ids, pairs, E0, EL, o);
         ++n;
     }
     const int sms = device_sm_count();
@@ -928,7 +936,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     px.tile_pad0 = S.tile_pad0;
     px.slot_pair = S.slot_pair;
     px.dst = S.b_gate_up;
-    const uint32_t max_tiles = max_tiles_for(pairs, E);
+    const uint32_t max_tiles = max_tiles_for(pairs, EL);
     const dim3 pack_grid(max_tiles, kTileTokens / (kPackThreads / 32));
     pack_kernel<<<pack_grid, kPackThreads, 0, stream>>>(px);
     ++n;
@@ -986,7 +994,8 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     // 8. combine
     {
         const size_t quads = static_cast<size_t>(tokens) * H / 4;
-        combine_kernel<<<static_cast<uint32_t>((quads + 255) / 256), 256, 0, stream>>>(S.pair_out, tokens, k, H, out);
+        combine_kernel<<<static_cast<uint32_t>((quads + 255) / 256), 256, 0, stream>>>(S.pair_out, S.ids, E0, EL,
+                                                                                       tokens, k, H, out);
         ++n;
     }
     if (ids && ids != S.ids) {

@@ -30,14 +30,18 @@ cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, ui
 bool encode_expert_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows,
                        uint64_t experts, uint64_t slice, uint32_t box_rows);
 
-// Fills `nblocks` GGUF blocks of `type` at dst from the counter-based
-// synthetic generator (seed, stream_id); see pokitlms_b200/synth.py.
+// Fills blocks [first_block, first_block + nblocks) of the counter-based
+// synthetic stream (seed, stream_id) of GGUF `type` into dst; see
+// pokitlms_b200/synth.py.
 cudaError_t launch_synth_blocks(uint32_t type, uint64_t seed, uint64_t stream_id,
-                                uint64_t nblocks, void* dst, cudaStream_t stream);
+                                uint64_t nblocks, void* dst, cudaStream_t stream, uint64_t first_block = 0);
 
 // Everything one MoE FFN block needs on the device.
 struct MoeLayerDev {
     uint32_t hidden = 0, inter = 0, experts = 0, top_k = 0;
+    // Experts held by this device: [expert_first, expert_first + expert_local);
+    // gate/up/down hold expert_local slices (expert e at e - expert_first).
+    uint32_t expert_first = 0, expert_local = 0;
     uint32_t flavour = 0;        // 0 = Qwen3-MoE block, 1 = Qwen3.5-MoE block
     uint32_t normalize = 1;      // renormalise the selected probabilities
     float expert_weights_scale = 1.0f;

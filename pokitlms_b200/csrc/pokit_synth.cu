@@ -38,19 +38,19 @@ __device__ __forceinline__ uint16_t scale_half(uint64_t skey, uint64_t j) {
     return __half_as_ushort(__float2half_rn(v));
 }
 
-// One thread per 8-byte word of the payload.
-__global__ void synth_kernel(uint32_t type, uint64_t key, uint64_t skey, uint64_t nbytes,
+// One thread per 8-byte word of the stream covering bytes [start, start +
+// nbytes); dst receives those bytes (dst[0] = stream byte `start`).
+__global__ void synth_kernel(uint32_t type, uint64_t key, uint64_t skey, uint64_t start, uint64_t nbytes,
                              uint8_t* __restrict__ dst) {
     const uint32_t B = block_bytes(type);
-    const uint64_t nwords = (nbytes + 7) / 8;
-    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < nwords;
+    const uint64_t w_first = start / 8, w_end = (start + nbytes + 7) / 8;
+    for (uint64_t i = w_first + blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < w_end;
          i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         uint64_t w = mix64(key + (i + 1) * kG);
         const uint64_t o0 = i * 8;
         // Patch the fp16 scale bytes that fall inside this word.
         for (int b = 0; b < 8; ++b) {
             const uint64_t o = o0 + b;
-            if (o >= nbytes) break;
             const uint64_t blk = o / B;
             const uint32_t off = static_cast<uint32_t>(o - blk * B);
             int field = -1, hi = 0;
@@ -67,10 +67,13 @@ __global__ void synth_kernel(uint32_t type, uint64_t key, uint64_t skey, uint64_
                 w = (w & ~(0xffull << (8 * b))) | (byte << (8 * b));
             }
         }
-        if (o0 + 8 <= nbytes && (reinterpret_cast<uint64_t>(dst + o0) & 7u) == 0) {
-            *reinterpret_cast<uint64_t*>(dst + o0) = w;
+        if (o0 >= start && o0 + 8 <= start + nbytes && (reinterpret_cast<uint64_t>(dst + (o0 - start)) & 7u) == 0) {
+            *reinterpret_cast<uint64_t*>(dst + (o0 - start)) = w;
         } else {
-            for (int b = 0; b < 8 && o0 + b < nbytes; ++b) dst[o0 + b] = static_cast<uint8_t>(w >> (8 * b));
+            for (int b = 0; b < 8; ++b) {
+                const uint64_t o = o0 + b;
+                if (o >= start && o < start + nbytes) dst[o - start] = static_cast<uint8_t>(w >> (8 * b));
+            }
         }
     }
 }
@@ -78,7 +81,7 @@ __global__ void synth_kernel(uint32_t type, uint64_t key, uint64_t skey, uint64_
 }  // namespace
 
 cudaError_t launch_synth_blocks(uint32_t type, uint64_t seed, uint64_t stream_id,
-                                uint64_t nblocks, void* dst, cudaStream_t stream) {
+                                uint64_t nblocks, void* dst, cudaStream_t stream, uint64_t first_block) {
     if (type != kQ4_K && type != kQ5_K && type != kQ6_K && type != kQ8_0) return cudaErrorInvalidValue;
     if (nblocks == 0) return cudaSuccess;
     const uint64_t key = [&] {
@@ -91,12 +94,12 @@ cudaError_t launch_synth_blocks(uint32_t type, uint64_t seed, uint64_t stream_id
     skey = (skey ^ (skey >> 30)) * 0xBF58476D1CE4E5B9ull;
     skey = (skey ^ (skey >> 27)) * 0x94D049BB133111EBull;
     skey = skey ^ (skey >> 31);
-    const uint64_t nbytes = nblocks * block_bytes(type);
-    const uint64_t nwords = (nbytes + 7) / 8;
+    const uint64_t nbytes = nblocks * block_bytes(type), start = first_block * block_bytes(type);
+    const uint64_t nwords = (start + nbytes + 7) / 8 - start / 8;
     uint64_t grid = (nwords + 255) / 256;
     const uint64_t cap = static_cast<uint64_t>(device_sm_count()) * 32u;
     if (grid > cap) grid = cap;
-    synth_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(type, key, skey, nbytes,
+    synth_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(type, key, skey, start, nbytes,
                                                                    static_cast<uint8_t*>(dst));
     return cudaGetLastError();
 }
