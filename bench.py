@@ -24,6 +24,19 @@ attention half of each decoder layer is outside this path.
 Between steps nothing is flushed: one step streams 1.07 GB of distinct expert
 and router bytes, far above the 126 MB L2.
 
+  grouped  (N = 1) benchmark configuration 4 beside the headline: 512 tokens,
+          BF16 activations ~N(0, 1), router logits ~N(0, 1) + a Zipf(1.1)
+          popularity bias, one MoE block (hidden 2048, 128 experts top-8,
+          inter 768, Q4_K) through the grouped-expert tensor-core GEMM
+          (pokit_cuda_moe_forward_batch); L2 flushed (256 MiB write) between
+          timed batches; per-kernel times from pokit_cuda_moe_time_batch.
+
+With N > 1 (torchrun) the ranks run expert parallelism: every step decodes N
+tokens (one per rank, the batch replicated on all ranks) through the 48
+layers; each rank holds 128 / N experts of every layer and runs the batched
+block on them, and the partial outputs are summed by an NCCL all-reduce
+(pokitlms_b200.ep).  value = N tokens per step / the slowest rank's step time.
+
 --impl reference times the PokitLMs reference's own CPU kernels and row
 executor (oracle/_ref) on the host cores, same metric and unit.
 """
@@ -137,7 +150,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_model(be, layers: int) -> None:
+def build_model(be, layers: int, router_dtype=None) -> None:
     from pokitlms_b200 import synth
     from pokitlms_b200._lib import DOWN, FFN_NORM, GATE, ROUTER, UP
     ones = np.ones(H, dtype=np.float32)
@@ -244,6 +257,230 @@ def run_reference(args) -> None:
     }))
 
 
+GROUPED_TOKENS = 512
+GROUPED_FLOPS = GROUPED_TOKENS * K_TOP * 2 * 3 * I * H          # 38.65 GFLOP
+GATE_UP_SLICE = 2 * 884_736                                      # gate + up of one expert
+
+
+def measure_grouped(device: int, stream) -> dict:
+    """Benchmark configuration 4 through the grouped-expert GEMM (see the
+    module docstring).  Returns the "grouped" object of the JSON line."""
+    import torch
+    from pokitlms_b200 import backend as B
+    from pokitlms_b200 import synth
+    from pokitlms_b200._lib import DOWN, GATE, ROUTER, UP
+    be = B.CudaMoeBackend(layers=1, hidden=H, inter=I, experts=E, top_k=K_TOP, rms_epsilon=EPS, device=device)
+    be.upload_tensor(0, ROUTER, synth.router_weights(E, H, SEED, 0))
+    for t in (GATE, UP, DOWN):
+        be.synthesize_tensor(0, t, SEED, synth.stream_id(0, t))
+    bits, _, logits = synth.grouped_inputs(GROUPED_TOKENS, E, H, seed=SEED)
+    x = torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16)
+    lg = torch.from_numpy(logits).cuda()
+    out = torch.empty(GROUPED_TOKENS, H, device="cuda")
+    ids = torch.empty(GROUPED_TOKENS, K_TOP, dtype=torch.int32, device="cuda")
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")   # 256 MiB > L2
+    for _ in range(3):
+        be.forward_batch(0, x, out, logits=lg, route_ids=ids, stream=stream)
+    be.synchronize(stream)
+    launches0 = be.stats()["kernel_launches"]
+    times = []
+    for i in range(20):
+        flush.fill_(float(i))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        be.forward_batch(0, x, out, logits=lg, stream=stream)
+        b.record(stream)
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    be.synchronize(stream)
+    launches = (be.stats()["kernel_launches"] - launches0) // 20
+    us = statistics.median(times)
+    stage_names = ["route", "group", "pack_x", "gate_up_gemm", "pack_act", "down_gemm", "combine"]
+    stages = be.time_batch(0, x, out, logits=lg, reps=10, stream=stream)
+    stage_us = dict(zip(stage_names, stages))
+    touched = int(np.unique(ids.cpu().numpy()).size)
+    # End to end: BF16 rows and logits from the host, output and routes back.
+    for _ in range(2):
+        be.forward_batch_host(0, bits, bf16_bits=True, logits=logits)
+    t0 = time.perf_counter()
+    reps = 10
+    for _ in range(reps):
+        be.forward_batch_host(0, bits, bf16_bits=True, logits=logits)
+    e2e_us = (time.perf_counter() - t0) / reps * 1e6
+    be.close()
+    peaks = measured_peaks()
+    weight_bytes = touched * EXPERT_BYTES
+    act_bytes = GROUPED_TOKENS * H * (2 + 4) + logits.nbytes
+    gu_us = stage_us["gate_up_gemm"]
+    gu_bytes = touched * GATE_UP_SLICE
+    tflops = GROUPED_FLOPS / (us * 1e-6) / 1e12
+    return {
+        "workload": ("benchmark configuration 4: 512 tokens, BF16 x ~N(0,1), logits ~N(0,1) + Zipf(1.1) bias, "
+                     "one block hidden 2048 / 128 experts top-8 / inter 768 / Q4_K"),
+        "value": GROUPED_TOKENS / (us * 1e-6), "unit": "tokens/s", "us_per_batch": us,
+        "l2": "flushed (256 MiB write) between timed batches",
+        "experts_touched": touched, "gpu_launches_per_batch": int(launches), "stage_us": stage_us,
+        "hbm": {"algorithmic_bytes": weight_bytes + act_bytes,
+                "achieved_gbs": (weight_bytes + act_bytes) / (us * 1e-6) / 1e9,
+                "frac": (weight_bytes + act_bytes) / (us * 1e-6) / 1e9 / peaks["hbm_gbs"],
+                "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]},
+        "tensor": {"flops": GROUPED_FLOPS, "achieved_tflops": tflops,
+                   "frac_of_measured_bf16": tflops / measured_tflops()},
+        "roofline": {"bound": "hbm", "kernel": "grouped_gemm_kernel<0> (Q4_K gate/up, tcgen05)",
+                     "achieved": gu_bytes / (gu_us * 1e-6) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gu_bytes / (gu_us * 1e-6) / 1e9 / peaks["hbm_gbs"],
+                     "bytes_per_launch": gu_bytes, "avg_launch_us": gu_us},
+        "e2e": {"value": GROUPED_TOKENS / (e2e_us * 1e-6), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(bits.nbytes + logits.nbytes),
+                "d2h_bytes_per_step": int(GROUPED_TOKENS * (H + 2 * K_TOP) * 4)},
+    }
+
+
+def measured_tflops() -> float:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        for k in ("bf16_tflops", "bf16_tflops_burst"):
+            if k in d:
+                return float(d[k])
+    return 1590.0
+
+
+def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_over_ranks) -> None:
+    """N > 1: expert-parallel decode of N tokens per step (module docstring)."""
+    import torch
+    import torch.distributed as dist
+    from pokitlms_b200 import synth
+    from pokitlms_b200._lib import DOWN, FFN_NORM, GATE, ROUTER, UP
+    from pokitlms_b200.ep import ExpertParallelMoe
+    layers = args.layers
+    ep = ExpertParallelMoe(rank=rank, world=world, layers=layers, hidden=H, inter=I, experts=E, top_k=K_TOP,
+                           rms_epsilon=EPS, device=local)
+    be = ep.backend
+    ones = np.ones(H, dtype=np.float32)
+    for l in range(layers):
+        be.upload_tensor(l, ROUTER, synth.router_weights(E, H, SEED, l))
+        be.upload_tensor(l, FFN_NORM, ones)
+        for t in (GATE, UP, DOWN):
+            be.synthesize_tensor(l, t, SEED, synth.stream_id(l, t))
+    n_in = args.steps + args.warmup
+    inputs = torch.from_numpy(np.stack([np.stack([synth.activation(H, SEED + j, i) for j in range(world)])
+                                        for i in range(n_in)])).cuda()            # [steps][world][H]
+    static_in = torch.empty(world, H, device="cuda")
+    hidden = torch.empty(world, H, device="cuda")
+    x = torch.empty(world, H, device="cuda")
+    part = torch.empty(world, H, device="cuda")
+
+    def body():
+        hidden.copy_(static_in)
+        for l in range(layers):
+            # rms_norm with ffn_norm = 1 (src/rms_norm.cpp:9-27), then the block.
+            torch.mul(hidden, torch.rsqrt(hidden.pow(2).mean(dim=1, keepdim=True) + EPS), out=x)
+            ep.forward_batch(l, x, part)
+            hidden.add_(part)
+
+    # Eager warm-up (sizes the batch scratch, sets kernel attributes), then the
+    # whole step -- 48 blocks and their all-reduces -- captured once and
+    # replayed: a step is otherwise bound by host-side launch cost.
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for i in range(3):
+            static_in.copy_(inputs[i])
+            body()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    l0 = be.stats()["kernel_launches"]
+    static_in.copy_(inputs[0])
+    body()
+    torch.cuda.synchronize()
+    launches_per_step = be.stats()["kernel_launches"] - l0
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            body()
+        torch.cuda.synchronize()
+    except Exception as exc:   # capture refused: run eagerly and say so
+        graph = None
+        print(f"[bench] rank {rank}: CUDA graph capture failed ({exc}); timing eager steps", file=sys.stderr)
+    barrier()
+
+    def step(i):
+        static_in.copy_(inputs[i], non_blocking=True)
+        if graph is not None:
+            graph.replay()
+        else:
+            body()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    cur = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(cur)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    ev1.record(cur)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    be.synchronize()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    gpu_launches = launches_per_step * args.steps
+    ms_per_step = ms / args.steps
+
+    # End to end: the step's hidden states from pinned host memory, the result back.
+    host_in = inputs[:8].cpu().pin_memory()
+    host_out = torch.empty(world, H).pin_memory()
+    e2e_steps = max(args.steps // 2, 5)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        static_in.copy_(host_in[i % 8], non_blocking=True)
+        if graph is not None:
+            graph.replay()
+        else:
+            body()
+        host_out.copy_(hidden, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    graph_used = graph is not None
+    graph = None                      # release the graph (it holds NCCL calls) before the group goes
+    torch.cuda.synchronize()
+    peaks = measured_peaks()
+    per_rank_gbs = K_TOP * EXPERT_BYTES / (ms_per_step / 1e3 / layers) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": world * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seed 0): Q4_K experts synthesised in HBM per shard, F32 router N(0,0.02)",
+            "config": {"workload": WORKLOAD + f", expert parallel: {world} tokens per step (one per rank)",
+                       "layers": layers, "hidden": H, "experts": E, "top_k": K_TOP, "inter": I,
+                       "expert_type": "Q4_K", "parallelism": f"ep{world} (experts {E // world} per GPU, "
+                       "NCCL all-reduce combine)", "cuda_graph": graph_used,
+                       "l2": "no flush: each rank streams its shard's routed experts every layer"},
+            "roofline": {"bound": "hbm", "kernel": "moe block per rank (grouped path + all-reduce)",
+                         "achieved": per_rank_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": per_rank_gbs / peaks["hbm_gbs"], "traffic": None,
+                         "bytes_per_block": K_TOP * EXPERT_BYTES,
+                         "note": ("per rank: N tokens x 8 routes over N shards = 8 expert slices per layer "
+                                  "(distinct experts assumed) / (step time / layers)")},
+            "e2e": {"value": world * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": world * H * 4,
+                    "d2h_bytes_per_step": world * H * 4},
+            "gpu_launches": int(gpu_launches), "clocks": clocks, "cpu_baseline": None,
+        }))
+    ep.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -285,6 +522,10 @@ def main() -> None:
         return float(t.item())
 
     layers = args.layers
+    if world > 1:
+        run_expert_parallel(args, rank, world, local, barrier, max_over_ranks)
+        dist.destroy_process_group()
+        return
     be = B.CudaMoeBackend(layers=layers, hidden=H, inter=I, experts=E, top_k=K_TOP,
                           rms_epsilon=EPS, device=local)
     build_model(be, layers)
@@ -356,10 +597,15 @@ def main() -> None:
     routed_gbs = ROUTED_BYTES / block_s / 1e9
     achieved = GATE_UP_BYTES / (gate_up_us / 1e6) / 1e9
 
+    grouped = measure_grouped(local, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, kind, cores, sample = cpu_reference_rate(args.cpu_seconds)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+        # One configuration-4 token is one block evaluation of the same shape.
+        grouped["cpu_baseline"] = {"value": v * LAYERS, "unit": "tokens/s", "cores": cores, "kind": kind,
+                                   "sample": sample + "; one config-4 token = one of those block evaluations"}
 
     if rank == 0:
         print(json.dumps({
@@ -369,7 +615,7 @@ def main() -> None:
             "data": "synthetic (seed 0): Q4_K experts synthesised in HBM, F32 router N(0,0.02)",
             "config": {"workload": WORKLOAD, "layers": layers, "hidden": H, "experts": E,
                        "top_k": K_TOP, "inter": I, "expert_type": "Q4_K",
-                       "parallelism": f"replicas x{world} (independent decode streams)",
+                       "parallelism": "single GPU (N > 1 runs expert parallelism)",
                        "l2": "no flush: each step streams 1.07 GB of distinct weights (> 126 MB L2)"},
             "routed_expert_gbs": routed_gbs,
             "routed_expert_frac_of_peak": routed_gbs / peaks["hbm_gbs"],
@@ -387,10 +633,9 @@ def main() -> None:
             "gpu_launches": int(gpu_launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "grouped": grouped,
         }))
     be.close()
-    if world > 1:
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

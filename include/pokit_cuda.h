@@ -280,6 +280,19 @@ pokit_cuda_status pokit_cuda_moe_forward_batch(pokit_cuda_moe* moe, size_t layer
                                                uint32_t* route_ids, float* route_weights, void* stream,
                                                char* error_buffer, size_t error_capacity);
 
+/* Measurement hook for benchmarks (no counterpart in the reference): runs the
+ * grouped-path batched forward `repetitions` times on device buffers with an
+ * event between its kernels and writes the average device time (us) of each
+ * stage to stage_us: [router,] route, group, pack activations, gate/up GEMM,
+ * pack intermediate, down GEMM, combine (*stages = 8, or 7 when router_logits
+ * is given).  INVALID_ARGUMENT for layers off the grouped path. */
+pokit_cuda_status pokit_cuda_moe_time_batch(pokit_cuda_moe* moe, size_t layer, const void* input,
+                                            uint32_t input_type, size_t tokens,
+                                            const float* router_logits, float* output,
+                                            uint32_t repetitions, float* stage_us,
+                                            size_t stage_capacity, size_t* stages, void* stream,
+                                            char* error_buffer, size_t error_capacity);
+
 /* Host-span variant of pokit_cuda_moe_forward_batch: copies in, runs, copies
  * out and synchronises (RUNTIME_ERROR for non-finite router logits). */
 pokit_cuda_status pokit_cuda_moe_forward_batch_host(pokit_cuda_moe* moe, size_t layer,

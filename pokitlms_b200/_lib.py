@@ -140,6 +140,8 @@ SIGNATURES = {
     "pokit_cuda_moe_forward": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_batch": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, _VP, _VP, _VP,
                                                _ERR, _SZ]),
+    "pokit_cuda_moe_time_batch": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, C.c_uint32, _VP, _SZ,
+                                            C.POINTER(_SZ), _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_batch_host": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, _VP, _VP,
                                                     _ERR, _SZ]),
     "pokit_cuda_moe_time_kernel": (C.c_int, [_VP, C.c_uint32, _SZ, _SZ, C.c_uint32, _VP, _VP, _VP, _ERR, _SZ]),

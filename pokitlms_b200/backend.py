@@ -188,6 +188,19 @@ class CudaMoeBackend:
         call("pokit_cuda_moe_forward_batch", self._h, layer, _ptr(x), kind, tokens, _ptr(logits), _ptr(out),
              _ptr(route_ids), _ptr(route_weights), _stream(stream))
 
+    def time_batch(self, layer: int, x, out, *, logits=None, reps: int = 10, stream=None) -> list[float]:
+        """Average device time (us) of each kernel of the grouped batched
+        forward over `reps` runs: [router,] route, group, pack, gate/up,
+        pack, down, combine."""
+        import torch
+        kind = _lib.INPUT_BF16 if x.dtype == torch.bfloat16 else _lib.INPUT_F32
+        tokens = x.numel() // self.hidden
+        us = (C.c_float * 8)()
+        n = C.c_size_t(0)
+        call("pokit_cuda_moe_time_batch", self._h, layer, _ptr(x), kind, tokens, _ptr(logits), _ptr(out), reps,
+             C.cast(us, C.c_void_p), 8, C.byref(n), _stream(stream))
+        return [float(us[i]) for i in range(n.value)]
+
     def forward_batch_host(self, layer: int, x: np.ndarray, *, bf16_bits: bool = False,
                            logits: np.ndarray | None = None):
         """Host-array batch: x float32 [tokens, hidden], or uint16 BF16 bit

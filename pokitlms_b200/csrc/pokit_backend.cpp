@@ -309,6 +309,43 @@ public:
         hits_ += tokens * cfg_.top_k;
     }
 
+    // Measurement: the batched forward on device buffers `repetitions` times
+    // with an event between its kernels; stage_us[i] receives the average
+    // device time of stage i (grouped path only).  Returns the stage count.
+    size_t time_batch(size_t layer, const void* x, uint32_t x_type, size_t tokens, const float* logits,
+                      float* out, uint32_t reps, float* stage_us, size_t capacity, cudaStream_t s) {
+        ensure_ok();
+        if (layer >= cfg_.layers) throw std::invalid_argument("layer out of range");
+        if (!x || !out || !stage_us || reps == 0) throw std::invalid_argument("buffers and repetitions required");
+        if (tokens == 0 || tokens > kMaxBatchTokens) throw std::invalid_argument("tokens must be 1..65536");
+        const MoeLayerDev& L = devs_[layer];
+        if (!moe_batch_grouped(L)) throw std::invalid_argument("the layer does not use the grouped path");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        const uint32_t T = static_cast<uint32_t>(tokens);
+        ensure_batch_scratch(L, T);
+        const size_t stages = logits ? 7 : 8;
+        if (capacity < stages) throw std::invalid_argument("stage_us needs room for 8 stages");
+        std::vector<cudaEvent_t> ev(stages + 1);
+        for (auto& e : ev) guard(cudaEventCreate(&e), "event");
+        std::vector<double> sum(stages, 0.0);
+        for (uint32_t r = 0; r < reps; ++r) {
+            uint32_t n = 0;
+            guard(launch_moe_batch(L, B_, x, x_type, T, logits, out, nullptr, nullptr, S_.status, st, &n, ev.data()),
+                  "grouped MoE batch");
+            kernel_launches_ += n;
+            guard(cudaEventSynchronize(ev[stages]), "timing");
+            for (size_t i = 0; i < stages; ++i) {
+                float ms = 0.f;
+                guard(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "timing");
+                sum[i] += ms * 1e3;
+            }
+        }
+        for (auto& e : ev) cudaEventDestroy(e);
+        for (size_t i = 0; i < stages; ++i) stage_us[i] = static_cast<float>(sum[i] / reps);
+        return stages;
+    }
+
     // Host-span batch: copies the inputs through pinned staging, runs, copies
     // the outputs back and synchronises.
     void forward_batch_host(size_t layer, const void* x, uint32_t x_type, size_t tokens, const float* logits,
@@ -928,6 +965,19 @@ pokit_cuda_status pokit_cuda_moe_forward_batch(pokit_cuda_moe* moe, size_t layer
         std::lock_guard<std::mutex> lock(moe->impl.mutex());
         moe->impl.forward_batch(layer, input, input_type, tokens, router_logits, output, route_ids, route_weights,
                                 as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_time_batch(pokit_cuda_moe* moe, size_t layer, const void* input,
+                                            uint32_t input_type, size_t tokens, const float* router_logits,
+                                            float* output, uint32_t repetitions, float* stage_us,
+                                            size_t stage_capacity, size_t* stages, void* stream,
+                                            char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe || !stages) throw std::invalid_argument("handle and stages are required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        *stages = moe->impl.time_batch(layer, input, input_type, tokens, router_logits, output, repetitions, stage_us,
+                                       stage_capacity, as_stream(stream));
     });
 }
 

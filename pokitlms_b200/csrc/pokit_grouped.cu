@@ -49,6 +49,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "pokit_common.cuh"
 #include "pokit_kernels.h"
@@ -79,49 +81,48 @@ __device__ __forceinline__ float silu_times(float g, float u, uint32_t flavour) 
 }
 
 // ---------------------------------------------------------------------------
-// 1. Router logits for a batch: logits[t][e] = router[e] . x[t] (F32 sums in
-// hidden order).  A CTA computes 16 tokens x 64 experts.
+// 1. Router logits for a batch: logits[t][e] = router[e] . x[t] in F32.  One
+// warp per (expert, group of 8 tokens): the expert's router row is read once
+// per group with 16-byte loads, lanes stride the hidden dimension by 128.
 // ---------------------------------------------------------------------------
+constexpr uint32_t kRouterTokens = 8;
+
+__device__ __forceinline__ float4 load4(const void* x, uint32_t x_bf16, size_t at) {
+    if (x_bf16) {
+        const uint2 q = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(x) + at);
+        return make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xFFFF0000u),
+                           __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xFFFF0000u));
+    }
+    return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + at);
+}
+
 __global__ void __launch_bounds__(256) router_batch_kernel(const float* __restrict__ router,
                                                            const void* __restrict__ x, uint32_t x_bf16,
                                                            uint32_t T, uint32_t E, uint32_t H,
                                                            float* __restrict__ logits) {
-    __shared__ float xs[16][65];
-    __shared__ float ws[64][65];
-    const uint32_t t0 = blockIdx.x * 16, e0 = blockIdx.y * 64;
-    const uint32_t ti = threadIdx.x / 16, eb = threadIdx.x % 16;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (uint32_t k0 = 0; k0 < H; k0 += 64) {
-        for (uint32_t i = threadIdx.x; i < 16 * 64; i += 256) {
-            const uint32_t row = i / 64, col = i % 64, t = t0 + row;
-            float v = 0.f;
-            if (t < T) {
-                const size_t at = static_cast<size_t>(t) * H + k0 + col;
-                v = x_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[at])
-                           : reinterpret_cast<const float*>(x)[at];
+    const uint32_t gw = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t e = gw % E, t0 = (gw / E) * kRouterTokens;
+    if (t0 >= T) return;
+    const uint32_t nt = min(kRouterTokens, T - t0);
+    float acc[kRouterTokens];
+#pragma unroll
+    for (uint32_t j = 0; j < kRouterTokens; ++j) acc[j] = 0.f;
+    const float* w = router + static_cast<size_t>(e) * H;
+#pragma unroll 4
+    for (uint32_t h = lane * 4; h < H; h += 128) {
+        const float4 wv = *reinterpret_cast<const float4*>(w + h);
+#pragma unroll
+        for (uint32_t j = 0; j < kRouterTokens; ++j) {
+            if (j < nt) {
+                const float4 xv = load4(x, x_bf16, static_cast<size_t>(t0 + j) * H + h);
+                acc[j] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[j]))));
             }
-            xs[row][col] = v;
         }
-        for (uint32_t i = threadIdx.x; i < 64 * 64; i += 256) {
-            const uint32_t row = i / 64, col = i % 64, e = e0 + row;
-            ws[row][col] = e < E ? router[static_cast<size_t>(e) * H + k0 + col] : 0.f;
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (uint32_t kk = 0; kk < 64; ++kk) {
-            const float xv = xs[ti][kk];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) acc[j] = fmaf(ws[eb + 16 * j][kk], xv, acc[j]);
-        }
-        __syncthreads();
     }
-    const uint32_t t = t0 + ti;
-    if (t < T) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t e = e0 + eb + 16 * j;
-            if (e < E) logits[static_cast<size_t>(t) * E + e] = acc[j];
-        }
+    for (uint32_t j = 0; j < kRouterTokens; ++j) {
+        const float v = warp_sum(acc[j]);
+        if (lane == 0 && j < nt) logits[static_cast<size_t>(t0 + j) * E + e] = v;
     }
 }
 
@@ -829,9 +830,21 @@ BatchSizes batch_sizes(const MoeLayerDev& L, uint32_t T) {
     return z;
 }
 
+// Raises a kernel's dynamic shared-memory limit once per device (the call
+// is then kept out of later launches, so they can be captured in graphs).
 template <typename Kern>
 cudaError_t set_smem(Kern k, uint32_t bytes) {
-    return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, uint32_t> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    uint32_t& have = done[{reinterpret_cast<const void*>(k), dev}];
+    if (have >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess) have = bytes;
+    return e;
 }
 
 }  // namespace
@@ -882,8 +895,11 @@ MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_token
 
 cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, const void* x, uint32_t x_bf16,
                              uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
-                             uint32_t* status, cudaStream_t stream, uint32_t* launches) {
+                             uint32_t* status, cudaStream_t stream, uint32_t* launches, cudaEvent_t* marks) {
     uint32_t n = 0;
+    const auto mark = [&]() {
+        if (marks) cudaEventRecord(marks[n], stream);
+    };
     if (launches) *launches = 0;
     if (!moe_batch_grouped(L) || tokens == 0 || tokens > S.max_tokens || !x || !out || !status)
         return cudaErrorInvalidValue;
@@ -900,12 +916,14 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         !encode_expert_map(&td, L.down, rb_dn, H, EL, L.down_slice, 128))
         return cudaErrorInvalidValue;
 
+    mark();
     // 1. router
     const float* lg = logits;
     if (!lg) {
-        router_batch_kernel<<<dim3((tokens + 15) / 16, (E + 63) / 64), 256, 0, stream>>>(L.router, x, x_bf16, tokens,
-                                                                                          E, H, S.logits);
+        const uint32_t warps = E * ((tokens + kRouterTokens - 1) / kRouterTokens);
+        router_batch_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H, S.logits);
         ++n;
+        mark();
         lg = S.logits;
     }
     // 2. routes
@@ -913,6 +931,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
                                     status, stream, tokens)) != cudaSuccess)
         return err;
     ++n;
+    mark();
     // 3. group
     {
         GroupOut o{S.plan, S.tile_expert, S.tile_first, S.tile_n, S.tile_pad0, S.slot_pair, S.rank};
@@ -920,6 +939,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         if ((err = set_smem(group_kernel, smem)) != cudaSuccess) return err;
         group_kernel<<<1, kSortThreads, smem, stream>>>(S.ids, pairs, E0, EL, o);
         ++n;
+        mark();
     }
     const int sms = device_sm_count();
     // 4. pack x
@@ -940,6 +960,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     const dim3 pack_grid(max_tiles, kTileTokens / (kPackThreads / 32));
     pack_kernel<<<pack_grid, kPackThreads, 0, stream>>>(px);
     ++n;
+    mark();
     // 5. gate/up
     GemmArgs ga{};
     ga.tm0 = tg;
@@ -967,6 +988,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         kern<<<sms, kGemmThreads, GateUpF32::total, stream>>>(ga);
     }
     ++n;
+    mark();
     // 6. pack activations
     PackArgs pa = px;
     pa.src = S.act;
@@ -977,6 +999,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     pa.dst = S.b_down;
     pack_kernel<<<pack_grid, kPackThreads, 0, stream>>>(pa);
     ++n;
+    mark();
     // 7. down
     GemmArgs da = ga;
     da.tm0 = td;
@@ -991,12 +1014,14 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         kern<<<sms, kGemmThreads, DownLay::total, stream>>>(da);
     }
     ++n;
+    mark();
     // 8. combine
     {
         const size_t quads = static_cast<size_t>(tokens) * H / 4;
         combine_kernel<<<static_cast<uint32_t>((quads + 255) / 256), 256, 0, stream>>>(S.pair_out, S.ids, E0, EL,
                                                                                        tokens, k, H, out);
         ++n;
+        mark();
     }
     if (ids && ids != S.ids) {
         if ((err = cudaMemcpyAsync(ids, S.ids, size_t(pairs) * 4, cudaMemcpyDeviceToDevice, stream)) != cudaSuccess)

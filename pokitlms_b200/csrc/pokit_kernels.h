@@ -155,7 +155,11 @@ MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_token
 // the routes.  `status` collects the sticky StatusBits.
 cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, const void* x, uint32_t x_bf16,
                              uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
-                             uint32_t* status, cudaStream_t stream, uint32_t* launches);
+                             uint32_t* status, cudaStream_t stream, uint32_t* launches,
+                             cudaEvent_t* marks = nullptr);
+// Stages (kernels) of one launch_moe_batch: 8, or 7 when logits are given.
+// marks (one more than stages) receive an event before the first and after
+// each kernel.
 
 // Grid-wide barriers one layer of launch_moe_decode performs.
 uint32_t moe_barriers_per_layer();
