@@ -490,6 +490,9 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "grouped"],
+                    help="grouped: only the configuration-4 measurement (one GPU; a small process for "
+                         "profiling the grouped kernels)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -522,6 +525,13 @@ def main() -> None:
         return float(t.item())
 
     layers = args.layers
+    if args.workload == "grouped":
+        if rank == 0:
+            print(json.dumps({"metric": "configuration-4 grouped-expert batch tokens/s", "n_gpus": 1,
+                              **measure_grouped(local, torch.cuda.current_stream())}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if world > 1:
         run_expert_parallel(args, rank, world, local, barrier, max_over_ranks)
         dist.destroy_process_group()
