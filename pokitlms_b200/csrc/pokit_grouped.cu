@@ -601,10 +601,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
                 if (!(ok = wait_warp(q_full + qs, (g / kQ) & 1))) break;
                 if (!(ok = wait_warp(a_free + buf, ((g >> 1) & 1) ^ 1))) break;
                 const uint8_t* row = qbuf + qs * kQStage + r * 144;
-                const uint32_t dm = *reinterpret_cast<const uint32_t*>(row);
-                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(row + 4);
-                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(row + 8);
-                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(row + 12);
+                // d, dmin and the 12 scale bytes in one 16-byte load (rows are 144 bytes
+                // apart: a quarter warp's loads fall on distinct bank groups).
+                const uint4 hdr = *reinterpret_cast<const uint4*>(row);
+                const uint32_t dm = hdr.x, w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
                 // 6-bit scales / mins (k_scale_min): bytes q[0..11] = w0 | w1 | w2.
                 uint32_t sc[8], mn[8];
 #pragma unroll
@@ -739,17 +739,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
                     if (lane == 0) mbar_arrive(xch_free);
                 }
             } else {
+                // The pair and combine weight of each of this warp's (<= 32)
+                // columns: lane j loads column c0 + j once, the elements get
+                // them by shuffle.
                 const uint32_t first = a.tile_first[tile];
+                const uint32_t lc = c0 + lane;
+                const uint32_t pr = lc < n_valid ? a.slot_pair[first + lc] : 0u;
+                const float wt = lc < n_valid ? a.route_w[pr] : 0.f;
 #pragma unroll
                 for (uint32_t c = 0; c < 4; ++c) {
                     if (8 * c < hn) {
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const uint32_t col = c0 + 8 * c + i;
-                            if (col < n_valid) {
-                                const uint32_t p = a.slot_pair[first + col];
-                                a.out[static_cast<size_t>(p) * a.rows + mb * 128 + r] = a.route_w[p] * acc[8 * c + i];
-                            }
+                            const uint32_t j = 8 * c + i;              // column within this warp's half
+                            const uint32_t p = __shfl_sync(0xFFFFFFFFu, pr, j);
+                            const float w = __shfl_sync(0xFFFFFFFFu, wt, j);
+                            if (col < n_valid) a.out[static_cast<size_t>(p) * a.rows + mb * 128 + r] = w * acc[j];
                         }
                     }
                 }
