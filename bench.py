@@ -336,6 +336,125 @@ def measure_grouped(device: int, stream) -> dict:
     }
 
 
+# Benchmark configuration 3's MoE path (Qwen3.5-MoE-style): 48 layers, H 2048, 512 experts top-10,
+# I 512, sigmoid-gated shared expert I 512 (Q8_0), Q4_K gate/up, down Q5_K / Q6_K alternating.
+CFG3 = {"layers": 48, "hidden": 2048, "inter": 512, "experts": 512, "top_k": 10, "shared_inter": 512}
+
+
+def cfg3_layer_bytes(down_type: int) -> int:
+    """Algorithmic bytes of one configuration-3 MoE block per token: F32 router, 10 routed
+    experts (gate + up Q4_K, down Q5_K or Q6_K), the shared expert (Q8_0) and its gate row."""
+    Hc, Ic = CFG3["hidden"], CFG3["inter"]
+    q4 = Ic * (Hc // 256) * 144
+    down = Hc * (Ic // 256) * (176 if down_type == 13 else 210)
+    shared = 3 * Ic * (Hc // 32) * 34
+    return CFG3["experts"] * Hc * 4 + CFG3["top_k"] * (2 * q4 + down) + shared + Hc * 4 + 2 * Hc * 4
+
+
+def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None) -> dict:
+    """Configuration 3's MoE path: a 48-layer decode chain of Qwen3.5-MoE blocks (generic path),
+    weights synthesised in HBM from seed 0; tokens/s device-resident and end to end."""
+    import torch
+    from pokitlms_b200 import backend as B
+    from pokitlms_b200 import synth
+    from pokitlms_b200._lib import (DOWN, FFN_NORM, GATE, Q5_K, Q6_K, Q8_0, QWEN35, ROUTER, SHARED_DOWN,
+                                    SHARED_GATE, SHARED_ROUTER, SHARED_UP, UP)
+    c = CFG3
+    downs = [Q5_K if l % 2 == 0 else Q6_K for l in range(c["layers"])]
+    be = B.CudaMoeBackend(layers=c["layers"], hidden=c["hidden"], inter=c["inter"], experts=c["experts"],
+                          top_k=c["top_k"], flavour=QWEN35, expert_weights_scale=1.0, rms_epsilon=EPS,
+                          down_type=Q5_K, layer_down_types=downs, shared_inter=c["shared_inter"],
+                          shared_gate_type=Q8_0, shared_up_type=Q8_0, shared_down_type=Q8_0, device=device)
+    ones = np.ones(c["hidden"], dtype=np.float32)
+    for l in range(c["layers"]):
+        be.upload_tensor(l, ROUTER, synth.router_weights(c["experts"], c["hidden"], SEED, l))
+        be.upload_tensor(l, FFN_NORM, ones)
+        be.upload_tensor(l, SHARED_ROUTER, synth.router_weights(1, c["hidden"], SEED, 1000 + l)[0])
+        for t in (GATE, UP, DOWN, SHARED_GATE, SHARED_UP, SHARED_DOWN):
+            be.synthesize_tensor(l, t, SEED, synth.stream_id(l, t))
+    inputs = torch.from_numpy(np.stack([synth.activation(c["hidden"], SEED, 30_000 + i)
+                                        for i in range(16)])).cuda()
+    work = torch.empty(c["hidden"], device="cuda")
+    for i in range(3):
+        work.copy_(inputs[i])
+        be.decode_layers(0, c["layers"], work, stream)
+    be.synchronize(stream)
+    l0 = be.stats()["kernel_launches"]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        work.copy_(inputs[i % 16], non_blocking=True)
+        be.decode_layers(0, c["layers"], work, stream)
+    b.record(stream)
+    torch.cuda.synchronize()
+    be.synchronize(stream)
+    ms = a.elapsed_time(b) / steps
+    launches = (be.stats()["kernel_launches"] - l0) // steps
+    hin = np.stack([synth.activation(c["hidden"], SEED, 31_000 + i) for i in range(4)])
+    hout = np.empty(c["hidden"], dtype=np.float32)
+    be.decode_layers_host(0, c["layers"], hin[0], hout)
+    t0 = time.perf_counter()
+    e2e_steps = max(steps // 4, 5)
+    for i in range(e2e_steps):
+        be.decode_layers_host(0, c["layers"], hin[i % 4], hout)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    be.close()
+    tok_bytes = sum(cfg3_layer_bytes(d) for d in downs)
+    peaks = measured_peaks()
+    gbs = tok_bytes / (ms * 1e-3) / 1e9
+    res = {
+        "workload": ("benchmark configuration 3's MoE path: 48 Qwen3.5-MoE blocks (hidden 2048, 512 experts "
+                     "top-10, inter 512, sigmoid-gated Q8_0 shared expert, Q4_K gate/up, Q5_K/Q6_K down "
+                     "alternating), decode batch 1; DeltaNet / attention layers outside the path"),
+        "value": 1e3 / ms, "unit": "tokens/s", "ms_per_token": ms, "gpu_launches_per_token": int(launches),
+        "hbm": {"bytes_per_token": tok_bytes, "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"],
+                "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]},
+        "e2e": {"value": 1.0 / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": c["hidden"] * 4,
+                "d2h_bytes_per_step": c["hidden"] * 4},
+        "path": "generic (FP32 dequant-dot; the tensor-core decode kernels serve all-Q4_K blocks without a shared expert)",
+    }
+    if cpu_seconds:
+        res["cpu_baseline"] = cpu_config3_rate(cpu_seconds)
+    return res
+
+
+def cpu_config3_rate(target_seconds: float) -> dict:
+    """The reference's CPU kernels and row executor (oracle/_ref) on configuration-3 blocks: two
+    synthesised layers (Q5_K and Q6_K down) cycled over the 48 layer evaluations of each token."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import cases
+    from oracle import oracle as O
+    from pokitlms_b200 import synth
+    c = CFG3
+    layers = [cases.moe_layer(hidden=c["hidden"], inter=c["inter"], experts=c["experts"], top_k=c["top_k"],
+                              seed=SEED, layer=l, flavour=1, down_type=(13 if l == 0 else 14),
+                              shared_inter=c["shared_inter"], with_norm=True) for l in range(2)]
+    if O.ref_available():
+        kind, cores = "reference", min(6, max(2, (os.cpu_count() or 1) - 1))
+        runners = [O.RefMoe(L) for L in layers]
+        norm = O.ref_rms_norm
+
+        def block(l, x):
+            return runners[l % 2].forward(x)[0]
+    else:
+        kind, cores, norm = "port", 1, O.rms_norm
+
+        def block(l, x):
+            return O.moe_forward(layers[l % 2], x)[0]
+    ones = np.ones(c["hidden"], dtype=np.float32)
+    tokens, t0 = 0, time.perf_counter()
+    while True:
+        h = synth.activation(c["hidden"], SEED, 40_000 + tokens)
+        for l in range(c["layers"]):
+            h = (h + block(l, norm(h, ones, EPS))).astype(np.float32)
+        tokens += 1
+        el = time.perf_counter() - t0
+        if el >= target_seconds:
+            break
+    return {"value": tokens / el, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{tokens} decode tokens x 48 MoE blocks (2 synthesised layers cycled), {el:.1f} s"}
+
+
 def measured_tflops() -> float:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -346,30 +465,44 @@ def measured_tflops() -> float:
     return 1590.0
 
 
-def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_over_ranks) -> None:
-    """N > 1: expert-parallel decode of N tokens per step (module docstring)."""
+# Benchmark configuration 5's MoE path: Qwen3-235B-A22B-shaped, decode batch 64.
+CFG5 = {"hidden": 4096, "inter": 1536, "experts": 128, "top_k": 8, "layers": 94, "tokens": 64}
+CFG5_WORKLOAD = ("qwen3-235b-a22b-shaped MoE expert path: 94 MoE FFN layers (hidden 4096, 128 experts top-8 "
+                 "renormalised, inter 1536, Q4_K experts, F32 router), decode batch 64")
+
+
+def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_over_ranks,
+                        shape: dict | None = None) -> None:
+    """Expert-parallel decode (module docstring).  Default shape: configuration 2
+    with one token per rank per step; `shape` = CFG5 runs configuration 5
+    (64 tokens per step whatever the rank count)."""
     import torch
     import torch.distributed as dist
     from pokitlms_b200 import synth
     from pokitlms_b200._lib import DOWN, FFN_NORM, GATE, ROUTER, UP
     from pokitlms_b200.ep import ExpertParallelMoe
-    layers = args.layers
-    ep = ExpertParallelMoe(rank=rank, world=world, layers=layers, hidden=H, inter=I, experts=E, top_k=K_TOP,
+    cfg5 = shape is not None
+    Hs = shape["hidden"] if cfg5 else H
+    Is = shape["inter"] if cfg5 else I
+    layers = (args.layers if args.layers != LAYERS else shape["layers"]) if cfg5 else args.layers
+    T = shape["tokens"] if cfg5 else world
+    ep = ExpertParallelMoe(rank=rank, world=world, layers=layers, hidden=Hs, inter=Is, experts=E, top_k=K_TOP,
                            rms_epsilon=EPS, device=local)
     be = ep.backend
-    ones = np.ones(H, dtype=np.float32)
+    ones = np.ones(Hs, dtype=np.float32)
     for l in range(layers):
-        be.upload_tensor(l, ROUTER, synth.router_weights(E, H, SEED, l))
+        be.upload_tensor(l, ROUTER, synth.router_weights(E, Hs, SEED, l))
         be.upload_tensor(l, FFN_NORM, ones)
         for t in (GATE, UP, DOWN):
             be.synthesize_tensor(l, t, SEED, synth.stream_id(l, t))
     n_in = args.steps + args.warmup
-    inputs = torch.from_numpy(np.stack([np.stack([synth.activation(H, SEED + j, i) for j in range(world)])
-                                        for i in range(n_in)])).cuda()            # [steps][world][H]
-    static_in = torch.empty(world, H, device="cuda")
-    hidden = torch.empty(world, H, device="cuda")
-    x = torch.empty(world, H, device="cuda")
-    part = torch.empty(world, H, device="cuda")
+    n_distinct = min(n_in, 16)
+    inputs = torch.from_numpy(np.stack([np.stack([synth.activation(Hs, SEED + j, i) for j in range(T)])
+                                        for i in range(n_distinct)])).cuda()      # [16][T][H]
+    static_in = torch.empty(T, Hs, device="cuda")
+    hidden = torch.empty(T, Hs, device="cuda")
+    x = torch.empty(T, Hs, device="cuda")
+    part = torch.empty(T, Hs, device="cuda")
 
     def body():
         hidden.copy_(static_in)
@@ -407,7 +540,7 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     barrier()
 
     def step(i):
-        static_in.copy_(inputs[i], non_blocking=True)
+        static_in.copy_(inputs[i % n_distinct], non_blocking=True)
         if graph is not None:
             graph.replay()
         else:
@@ -437,13 +570,13 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
 
     # End to end: the step's hidden states from pinned host memory, the result back.
     host_in = inputs[:8].cpu().pin_memory()
-    host_out = torch.empty(world, H).pin_memory()
+    host_out = torch.empty(T, Hs).pin_memory()
     e2e_steps = max(args.steps // 2, 5)
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
-        static_in.copy_(host_in[i % 8], non_blocking=True)
+        static_in.copy_(host_in[i % host_in.shape[0]], non_blocking=True)
         if graph is not None:
             graph.replay()
         else:
@@ -456,26 +589,36 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     graph = None                      # release the graph (it holds NCCL calls) before the group goes
     torch.cuda.synchronize()
     peaks = measured_peaks()
-    per_rank_gbs = K_TOP * EXPERT_BYTES / (ms_per_step / 1e3 / layers) / 1e9
+    expert_bytes = 3 * Is * (Hs // 256) * 144
+    if cfg5:
+        # Distinct experts the step's routes touch on this rank: all of its shard in practice
+        # (64 tokens x 8 routes over 128 experts), read once per layer.
+        per_rank_bytes = ep.expert_count * expert_bytes
+    else:
+        per_rank_bytes = K_TOP * expert_bytes
+    per_rank_gbs = per_rank_bytes / (ms_per_step / 1e3 / layers) / 1e9
     if rank == 0:
         print(json.dumps({
-            "metric": METRIC, "value": world * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC, "value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if cfg5 else "weak", "vs_baseline": None,
+            "dtype": "f32",
             "data": "synthetic (seed 0): Q4_K experts synthesised in HBM per shard, F32 router N(0,0.02)",
-            "config": {"workload": WORKLOAD + f", expert parallel: {world} tokens per step (one per rank)",
-                       "layers": layers, "hidden": H, "experts": E, "top_k": K_TOP, "inter": I,
+            "config": {"workload": (CFG5_WORKLOAD if cfg5 else WORKLOAD + f", expert parallel: {world} tokens "
+                                    "per step (one per rank)"),
+                       "tokens_per_step": T,
+                       "layers": layers, "hidden": Hs, "experts": E, "top_k": K_TOP, "inter": Is,
                        "expert_type": "Q4_K", "parallelism": f"ep{world} (experts {E // world} per GPU, "
                        "NCCL all-reduce combine)", "cuda_graph": graph_used,
                        "l2": "no flush: each rank streams its shard's routed experts every layer"},
             "roofline": {"bound": "hbm", "kernel": "moe block per rank (grouped path + all-reduce)",
                          "achieved": per_rank_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": per_rank_gbs / peaks["hbm_gbs"], "traffic": None,
-                         "bytes_per_block": K_TOP * EXPERT_BYTES,
-                         "note": ("per rank: N tokens x 8 routes over N shards = 8 expert slices per layer "
-                                  "(distinct experts assumed) / (step time / layers)")},
-            "e2e": {"value": world * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": world * H * 4,
-                    "d2h_bytes_per_step": world * H * 4},
+                         "bytes_per_block": per_rank_bytes,
+                         "note": ("per rank and layer: the shard's expert slices the step reads (config 5: the "
+                                  "whole shard; else 8 slices, distinct experts assumed) / (step time / layers)")},
+            "e2e": {"value": T * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * Hs * 4,
+                    "d2h_bytes_per_step": T * Hs * 4},
             "gpu_launches": int(gpu_launches), "clocks": clocks, "cpu_baseline": None,
         }))
     ep.close()
@@ -490,9 +633,10 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "grouped"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "grouped", "config5"],
                     help="grouped: only the configuration-4 measurement (one GPU; a small process for "
-                         "profiling the grouped kernels)")
+                         "profiling the grouped kernels); config5: configuration 5 (94 layers, hidden "
+                         "4096, batch 64) through the expert-parallel path on 1..N GPUs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -529,6 +673,11 @@ def main() -> None:
         if rank == 0:
             print(json.dumps({"metric": "configuration-4 grouped-expert batch tokens/s", "n_gpus": 1,
                               **measure_grouped(local, torch.cuda.current_stream())}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    if args.workload == "config5":
+        run_expert_parallel(args, rank, world, local, barrier, max_over_ranks, shape=CFG5)
         if world > 1:
             dist.destroy_process_group()
         return
@@ -608,6 +757,8 @@ def main() -> None:
     achieved = GATE_UP_BYTES / (gate_up_us / 1e6) / 1e9
 
     grouped = measure_grouped(local, stream)
+    config3 = measure_config3(local, stream, steps=max(args.steps // 10, 20),
+                              cpu_seconds=None if (args.no_cpu_baseline or rank != 0) else 6.0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -644,6 +795,7 @@ def main() -> None:
             "clocks": clocks,
             "cpu_baseline": cpu,
             "grouped": grouped,
+            "config3": config3,
         }))
     be.close()
 
