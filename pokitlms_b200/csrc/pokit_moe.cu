@@ -90,13 +90,14 @@ __host__ __device__ inline uint32_t stage_bytes_of(const MoeLayerDev& L) {
     if (!fast_pair(L.gate_type, L.up_type))
         s = umax(s, umax(al16(static_cast<uint32_t>(row_bytes(L.gate_type, L.hidden))),
                          al16(static_cast<uint32_t>(row_bytes(L.up_type, L.hidden)))));
-    if (L.down_type != kQ4_K) s = umax(s, al16(static_cast<uint32_t>(row_bytes(L.down_type, L.inter))));
+    // Generic down rows are staged eight at a time (one warp task = 8 rows).
+    if (L.down_type != kQ4_K) s = umax(s, 8u * al16(static_cast<uint32_t>(row_bytes(L.down_type, L.inter))));
     if (L.shared_inter) {
         if (!fast_pair(L.shared_gate_type, L.shared_up_type))
             s = umax(s, umax(al16(static_cast<uint32_t>(row_bytes(L.shared_gate_type, L.hidden))),
                              al16(static_cast<uint32_t>(row_bytes(L.shared_up_type, L.hidden)))));
         if (L.shared_down_type != kQ4_K)
-            s = umax(s, al16(static_cast<uint32_t>(row_bytes(L.shared_down_type, L.shared_inter))));
+            s = umax(s, 8u * al16(static_cast<uint32_t>(row_bytes(L.shared_down_type, L.shared_inter))));
     }
     return s;
 }
@@ -641,18 +642,7 @@ __device__ float generic_row_dot(uint32_t type, const uint8_t* row_g, uint32_t c
     const uint32_t rb = static_cast<uint32_t>(row_bytes(type, cols));
     warp_stage_row(row_g, rb, stage, lane);
     __syncwarp();
-    float acc = 0.0f;
-    const int groups = static_cast<int>(cols >> 5);
-    for (int g = lane; g < groups; g += 32) {
-        switch (type) {
-            case kQ4_K: acc += group_dot<kQ4_K>(stage, g, xs); break;
-            case kQ5_K: acc += group_dot<kQ5_K>(stage, g, xs); break;
-            case kQ6_K: acc += group_dot<kQ6_K>(stage, g, xs); break;
-            case kQ8_0: acc += group_dot<kQ8_0>(stage, g, xs); break;
-            default: acc += group_dot<kF32>(stage, g, xs); break;
-        }
-    }
-    acc = warp_sum(acc);
+    float acc = warp_sum(lane_row_dot_any(type, stage, cols, xs, lane));
     __syncwarp();
     return acc;
 }
@@ -889,15 +879,21 @@ __device__ void phase_down(const MoeLayerDev& L, Shared& s, const float* act, ui
             acc += __shfl_xor_sync(0xffffffffu, acc, 2);
             if (c == 0 && row < r1) s.ybuf[slot * cap + (row - r0)] = acc;
         } else {
+            // The task's (up to) 8 rows staged together: one memory latency,
+            // then one warp-wide dot per row.
             uint8_t* my_stage = s.stage + warp * s.m.stage_bytes;
             const uint64_t rb = row_bytes(m.down_type, m.rows);
-            for (uint32_t rr = 0; rr < 8; ++rr) {
-                const uint32_t row = r0 + o * 8u + rr;
-                if (row >= r1) break;
-                const float y = generic_row_dot(m.down_type, m.down + row * rb, m.rows,
-                                                s.act_plain + slot * mi, my_stage, lane);
-                if (lane == 0) s.ybuf[slot * cap + (row - r0)] = y;
+            const uint32_t rs = al16(static_cast<uint32_t>(rb));
+            const uint32_t row0 = r0 + o * 8u;
+            const uint32_t nr = min(8u, r1 - row0);
+            warp_stage_rows(m.down + row0 * rb, rb, nr, static_cast<uint32_t>(rb), my_stage, rs, lane);
+            __syncwarp();
+            const float* xa = s.act_plain + slot * mi;
+            for (uint32_t rr = 0; rr < nr; ++rr) {
+                const float acc = warp_sum(lane_row_dot_any(m.down_type, my_stage + rr * rs, m.rows, xa, lane));
+                if (lane == 0) s.ybuf[slot * cap + (row0 + rr - r0)] = acc;
             }
+            __syncwarp();
         }
     }
     __syncthreads();
@@ -925,7 +921,18 @@ struct BlockArgs {
     uint32_t down_ctas;
 };
 
-// Kernel 1 of a block: R0 + R1 (CTA 0 also publishes x).
+// Returns true in every thread of the CTA that arrives last at `count`
+// (after all of this CTA's global writes), and resets the counter there.
+__device__ __forceinline__ bool last_cta_arrival(uint32_t* count, uint32_t* flag) {
+    __syncthreads();
+    if (threadIdx.x == 0) *flag = atomic_add_acq_rel_gpu(count, 1u) == gridDim.x - 1u ? 1u : 0u;
+    __syncthreads();
+    const bool last = *flag != 0u;
+    if (last && threadIdx.x == 0) *count = 0u;
+    return last;
+}
+
+// Kernel 1 of a block: R0 + R1 (CTA 0 also publishes x), then R2 in the last CTA.
 __global__ void __launch_bounds__(kThreads, 1) moe_route_kernel(BlockArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     Shared s = carve(smem, a.m);
@@ -936,13 +943,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_route_kernel(BlockArgs a) {
     if (blockIdx.x == 0)
         for (uint32_t i = threadIdx.x; i < a.L.hidden; i += kThreads) a.S.x[i] = s.xs[i];
     router_finish(a.L, gw, nw, rr, s, a.S.partial);
+    // R2 once per block: the CTA that finishes last sums the partials and
+    // routes; the gate/up kernel's CTAs read the routes it publishes.
+    __shared__ uint32_t last;
+    __threadfence();
+    if (last_cta_arrival(a.S.route_count, &last)) phase_route(a.L, a.S.partial, s, a.S.status, true, a.S);
 }
 
-// Kernel 2: R2 (every CTA; CTA 0 publishes the routes) + G.
+// Kernel 2: G, on the routes the route kernel's last CTA published.
 __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_kernel(BlockArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     Shared s = carve(smem, a.m);
-    phase_route(a.L, a.S.partial, s, a.S.status, blockIdx.x == 0, a.S);
+    for (uint32_t r = threadIdx.x; r <= a.L.top_k; r += kThreads) {
+        if (r < a.L.top_k) s.sel_id[r] = __ldcg(a.S.ids + r);
+        s.sel_w[r] = __ldcg(a.S.weights + r);
+    }
     copy_coherent(a.S.x, s.xs, a.L.hidden);
     __syncthreads();
     phase_gate_up(a.L, s, a.S.act, max_inter_of(a.L), blockIdx.x, gridDim.x, a.down_ctas);
@@ -1308,16 +1323,6 @@ __device__ void route_tail(const MoeLayerDev& L, const MoeScratch& S, const floa
     }
 }
 
-// Returns true in every thread of the CTA that arrives last at `count`
-// (after all of this CTA's global writes), and resets the counter there.
-__device__ __forceinline__ bool last_cta_arrival(uint32_t* count, uint32_t* flag) {
-    __syncthreads();
-    if (threadIdx.x == 0) *flag = atomic_add_acq_rel_gpu(count, 1u) == gridDim.x - 1u ? 1u : 0u;
-    __syncthreads();
-    const bool last = *flag != 0u;
-    if (last && threadIdx.x == 0) *count = 0u;
-    return last;
-}
 
 // Router partials of block L for the first block of a chain or a single
 // block, then its routing tail.

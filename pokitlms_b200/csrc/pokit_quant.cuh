@@ -237,4 +237,140 @@ __device__ __forceinline__ void warp_stage_row(const uint8_t* __restrict__ src, 
     }
 }
 
+// Stages n rows (row i at src + i * stride, `bytes` each) into dst (row i at
+// dst + i * dst_stride) with a batch of loads per lane in flight before the
+// stores: one memory latency per batch instead of one per row.
+__device__ __forceinline__ void warp_stage_rows(const uint8_t* __restrict__ src, uint64_t stride, uint32_t n,
+                                                uint32_t bytes, uint8_t* __restrict__ dst, uint32_t dst_stride,
+                                                int lane) {
+    const uint64_t a = reinterpret_cast<uint64_t>(src);
+    if ((a & 15u) == 0 && (bytes & 15u) == 0 && (stride & 15u) == 0 && (dst_stride & 15u) == 0) {
+        const uint32_t units = bytes / 16u, total = units * n;
+        constexpr uint32_t kBatch = 8;
+        for (uint32_t base = lane; base < total; base += 32u * kBatch) {
+            uint4 v[kBatch];
+#pragma unroll
+            for (uint32_t j = 0; j < kBatch; ++j) {
+                const uint32_t w = base + 32u * j;
+                if (w < total) v[j] = ldg_stream128(src + (w / units) * stride + (w % units) * 16u);
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < kBatch; ++j) {
+                const uint32_t w = base + 32u * j;
+                if (w < total) *reinterpret_cast<uint4*>(dst + (w / units) * dst_stride + (w % units) * 16u) = v[j];
+            }
+        }
+    } else if ((a & 3u) == 0 && (bytes & 3u) == 0 && (stride & 3u) == 0 && (dst_stride & 3u) == 0) {
+        const uint32_t words = bytes / 4u, total = words * n;
+        constexpr uint32_t kBatch = 16;
+        for (uint32_t base = lane; base < total; base += 32u * kBatch) {
+            uint32_t v[kBatch];
+#pragma unroll
+            for (uint32_t j = 0; j < kBatch; ++j) {
+                const uint32_t w = base + 32u * j;
+                if (w < total) v[j] = ldg_stream32(src + (w / words) * stride + (w % words) * 4u);
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < kBatch; ++j) {
+                const uint32_t w = base + 32u * j;
+                if (w < total) *reinterpret_cast<uint32_t*>(dst + (w / words) * dst_stride + (w % words) * 4u) = v[j];
+            }
+        }
+    } else {
+        for (uint32_t i = 0; i < n; ++i) warp_stage_row(src + i * stride, bytes, dst + i * dst_stride, lane);
+    }
+}
+
+// This lane's share of the dot of a staged row (cols weights) with x: lane l
+// takes elements l, l + 32, l + 64, ...  With that mapping a warp reads 32
+// consecutive activations and 32 consecutive quant bytes per step (no shared-
+// memory bank conflicts) and, inside a 256-weight superblock, element
+// 32 i + l belongs to sub-block i (Q4_K/Q5_K: the low nibbles of qs[32 (i/2) + l]
+// for even i, the high ones for odd i; Q5_K's fifth bit is bit i of qh[l];
+// Q6_K: quarter i % 4 of half i / 4, scale 8 (i / 4) + l / 16 + 2 (i % 4)).
+// Weights are formed as the reference's decoders form them (quantized_linear.cpp
+// :166-205, :286-328, :330-358, Q8_0 :430-451); callers sum the lanes.
+template <uint32_t T>
+__device__ __forceinline__ float lane_row_dot(const uint8_t* __restrict__ row, uint32_t cols,
+                                              const float* __restrict__ x, int lane) {
+    float acc = 0.0f;
+    if constexpr (T == kF32) {
+        const float* w = reinterpret_cast<const float*>(row);
+        for (uint32_t k = lane; k < cols; k += 32) acc = fmaf(w[k], x[k], acc);
+    } else if constexpr (T == kQ8_0) {
+        for (uint32_t b = 0; b < cols / 32; ++b) {
+            const uint8_t* blk = row + b * 34;
+            const float d = half_bits_to_float(sm_u16(blk));
+            const float q = static_cast<float>(static_cast<int8_t>(blk[2 + lane]));
+            acc = fmaf(d * q, x[32 * b + lane], acc);
+        }
+    } else if constexpr (T == kQ4_K || T == kQ5_K) {
+        constexpr uint32_t BB = T == kQ4_K ? 144u : 176u, QS = T == kQ4_K ? 16u : 48u;
+        for (uint32_t sb = 0; sb < cols / 256; ++sb) {
+            const uint8_t* blk = row + sb * BB;
+            const float d = half_bits_to_float(sm_u16(blk)), dmin = half_bits_to_float(sm_u16(blk + 2));
+            const uint8_t* packed = blk + 4;
+            uint32_t hbits = 0;
+            if constexpr (T == kQ5_K) hbits = blk[16 + lane];
+            const float* xs = x + sb * 256 + lane;
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+                uint32_t sc, mn;
+                if (i < 4) {
+                    sc = packed[i] & 63u;
+                    mn = packed[i + 4] & 63u;
+                } else {
+                    sc = (packed[i + 4] & 0x0fu) | ((packed[i - 4] >> 6) << 4);
+                    mn = (packed[i + 4] >> 4) | ((packed[i] >> 6) << 4);
+                }
+                const uint32_t byte = blk[QS + 32 * (i / 2) + lane];
+                uint32_t v = (i & 1) ? (byte >> 4) : (byte & 0x0fu);
+                if constexpr (T == kQ5_K) v += ((hbits >> i) & 1u) << 4;
+                const float w = (d * static_cast<float>(sc)) * static_cast<float>(v) - dmin * static_cast<float>(mn);
+                acc = fmaf(w, xs[32 * i], acc);
+            }
+        }
+    } else if constexpr (T == kQ6_K) {
+        for (uint32_t sb = 0; sb < cols / 256; ++sb) {
+            const uint8_t* blk = row + sb * 210;
+            const float d = half_bits_to_float(sm_u16(blk + 208));
+            const float* xs = x + sb * 256 + lane;
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+                const uint32_t half = i >> 2, quarter = i & 3;
+                const uint32_t lo = blk[half * 64 + lane + 32 * (quarter & 1)];
+                const uint32_t hi = blk[128 + half * 32 + lane];
+                const int q = static_cast<int>(((lo >> (4 * (quarter >> 1))) & 0x0fu) |
+                                               (((hi >> (2 * quarter)) & 3u) << 4)) - 32;
+                const int8_t sc = static_cast<int8_t>(blk[192 + half * 8 + lane / 16 + 2 * quarter]);
+                const float w = d * static_cast<float>(sc) * static_cast<float>(q);
+                acc = fmaf(w, xs[32 * i], acc);
+            }
+        }
+    }
+    return acc;
+}
+
+__device__ __forceinline__ float lane_row_dot_any(uint32_t type, const uint8_t* row, uint32_t cols, const float* x,
+                                                  int lane) {
+    switch (type) {
+        case kQ4_K: return lane_row_dot<kQ4_K>(row, cols, x, lane);
+        case kQ5_K: return lane_row_dot<kQ5_K>(row, cols, x, lane);
+        case kQ6_K: return lane_row_dot<kQ6_K>(row, cols, x, lane);
+        case kQ8_0: return lane_row_dot<kQ8_0>(row, cols, x, lane);
+        default: return lane_row_dot<kF32>(row, cols, x, lane);
+    }
+}
+
+// Dot of 32-weight group g of a staged row of any supported type with x.
+__device__ __forceinline__ float group_dot_any(uint32_t type, const uint8_t* row, int g, const float* x) {
+    switch (type) {
+        case kQ4_K: return group_dot<kQ4_K>(row, g, x);
+        case kQ5_K: return group_dot<kQ5_K>(row, g, x);
+        case kQ6_K: return group_dot<kQ6_K>(row, g, x);
+        case kQ8_0: return group_dot<kQ8_0>(row, g, x);
+        default: return group_dot<kF32>(row, g, x);
+    }
+}
+
 }  // namespace pokit
