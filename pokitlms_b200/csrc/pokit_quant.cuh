@@ -351,13 +351,112 @@ __device__ __forceinline__ float lane_row_dot(const uint8_t* __restrict__ row, u
     return acc;
 }
 
+// Four bytes at any (shared-memory) address as one word: two aligned loads and a
+// funnel shift (Q6_K superblocks are 210 bytes, so odd superblocks start 2 bytes
+// off a word boundary).  Reads up to 3 bytes past p + 3 within the same row.
+__device__ __forceinline__ uint32_t load_u32_any(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
+    const uint32_t sh = static_cast<uint32_t>(a & 3u) * 8u;
+    return sh ? __funnelshift_r(w[0], w[1], sh) : w[0];
+}
+
+// Four bytes of a 32-bit word as floats: byte j -> (2^23 + byte) - bias.
+__device__ __forceinline__ float4 bytes_to_float4(uint32_t w, float bias) {
+    const float k = 8388608.0f + bias;
+    // __byte_perm selector nibbles: result byte 0 = byte j of w (0..3), bytes
+    // 1, 2 = byte 4 (0x00 of the constant), byte 3 = byte 7 (0x4B).
+    return make_float4(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440)) - k,
+                       __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441)) - k,
+                       __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442)) - k,
+                       __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443)) - k);
+}
+
+// lane_row_dot with four consecutive elements per lane and step: lane l takes
+// elements 128 s + 4 l .. 128 s + 4 l + 3, whose quants share one 32-bit word
+// (and one sub-block scale); the four are decoded byte-parallel and the scale
+// is applied once per four.  cols must be a multiple of 256 (K-quants) or 128
+// (Q8_0).  The sum differs from lane_row_dot's only in rounding.
+template <uint32_t T>
+__device__ __forceinline__ float lane_row_dot4(const uint8_t* __restrict__ row, uint32_t cols,
+                                               const float* __restrict__ x, int lane) {
+    float acc = 0.0f;
+    if constexpr (T == kQ6_K) {
+        const uint32_t quarter = lane >> 3, l0 = 4u * (lane & 7);
+        for (uint32_t sb = 0; sb < cols / 256; ++sb) {
+            const uint8_t* blk = row + sb * 210;
+            const float d = half_bits_to_float(sm_u16(blk + 208));
+#pragma unroll
+            for (uint32_t half = 0; half < 2; ++half) {
+                const uint32_t lo = load_u32_any(blk + half * 64 + 32 * (quarter & 1) + l0);
+                const uint32_t hi = load_u32_any(blk + 128 + half * 32 + l0);
+                const uint32_t q = ((lo >> (4 * (quarter >> 1))) & 0x0F0F0F0Fu) | (((hi >> (2 * quarter)) & 0x03030303u) << 4);
+                const float sc = static_cast<float>(static_cast<int8_t>(blk[192 + half * 8 + (l0 >> 4) + 2 * quarter]));
+                const float4 f = bytes_to_float4(q, 32.0f);
+                const float4 xv = *reinterpret_cast<const float4*>(x + sb * 256 + half * 128 + 4 * lane);
+                const float part = fmaf(f.x, xv.x, fmaf(f.y, xv.y, fmaf(f.z, xv.z, f.w * xv.w)));
+                acc = fmaf(d * sc, part, acc);
+            }
+        }
+    } else if constexpr (T == kQ4_K || T == kQ5_K) {
+        constexpr uint32_t BB = T == kQ4_K ? 144u : 176u, QS = T == kQ4_K ? 16u : 48u;
+        const bool high = (lane & 8) != 0;
+        const uint32_t l0 = 4u * (lane & 7);
+        for (uint32_t sb = 0; sb < cols / 256; ++sb) {
+            const uint8_t* blk = row + sb * BB;
+            const float d = half_bits_to_float(sm_u16(blk)), dmin = half_bits_to_float(sm_u16(blk + 2));
+            const uint8_t* packed = blk + 4;
+            uint32_t qh = 0;
+            if constexpr (T == kQ5_K) qh = *reinterpret_cast<const uint32_t*>(blk + 16 + l0);
+#pragma unroll
+            for (uint32_t st = 0; st < 2; ++st) {
+                const uint32_t chunk = 2 * st + (lane >> 4);
+                const uint32_t j = 2 * chunk + (high ? 1u : 0u);
+                uint32_t sc, mn;
+                if (j < 4) {
+                    sc = packed[j] & 63u;
+                    mn = packed[j + 4] & 63u;
+                } else {
+                    sc = (packed[j + 4] & 0x0fu) | ((packed[j - 4] >> 6) << 4);
+                    mn = (packed[j + 4] >> 4) | ((packed[j] >> 6) << 4);
+                }
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(blk + QS + 32 * chunk + l0);
+                uint32_t q = high ? ((w >> 4) & 0x0F0F0F0Fu) : (w & 0x0F0F0F0Fu);
+                if constexpr (T == kQ5_K) q |= ((qh >> j) & 0x01010101u) << 4;
+                const float4 f = bytes_to_float4(q, 0.0f);
+                const float4 xv = *reinterpret_cast<const float4*>(x + sb * 256 + st * 128 + 4 * lane);
+                const float part = fmaf(f.x, xv.x, fmaf(f.y, xv.y, fmaf(f.z, xv.z, f.w * xv.w)));
+                const float xsum = (xv.x + xv.y) + (xv.z + xv.w);
+                acc = fmaf(d * static_cast<float>(sc), part, fmaf(-(dmin * static_cast<float>(mn)), xsum, acc));
+            }
+        }
+    } else if constexpr (T == kQ8_0) {
+        const uint32_t l0 = 4u * (lane & 7);
+        for (uint32_t s0 = 0; s0 < cols; s0 += 128) {
+            const uint8_t* blk = row + (s0 / 32 + (lane >> 3)) * 34;
+            const float d = half_bits_to_float(sm_u16(blk));
+            const uint8_t* q = blk + 2 + l0;
+            const float4 xv = *reinterpret_cast<const float4*>(x + s0 + 4 * lane);
+            const float part = fmaf(static_cast<float>(static_cast<int8_t>(q[0])), xv.x,
+                                    fmaf(static_cast<float>(static_cast<int8_t>(q[1])), xv.y,
+                                         fmaf(static_cast<float>(static_cast<int8_t>(q[2])), xv.z,
+                                              static_cast<float>(static_cast<int8_t>(q[3])) * xv.w)));
+            acc = fmaf(d, part, acc);
+        }
+    } else {
+        acc = lane_row_dot<T>(row, cols, x, lane);
+    }
+    return acc;
+}
+
 __device__ __forceinline__ float lane_row_dot_any(uint32_t type, const uint8_t* row, uint32_t cols, const float* x,
                                                   int lane) {
     switch (type) {
-        case kQ4_K: return lane_row_dot<kQ4_K>(row, cols, x, lane);
-        case kQ5_K: return lane_row_dot<kQ5_K>(row, cols, x, lane);
-        case kQ6_K: return lane_row_dot<kQ6_K>(row, cols, x, lane);
-        case kQ8_0: return lane_row_dot<kQ8_0>(row, cols, x, lane);
+        case kQ4_K: return lane_row_dot4<kQ4_K>(row, cols, x, lane);
+        case kQ5_K: return lane_row_dot4<kQ5_K>(row, cols, x, lane);
+        case kQ6_K: return lane_row_dot4<kQ6_K>(row, cols, x, lane);
+        case kQ8_0: return (cols & 127u) ? lane_row_dot<kQ8_0>(row, cols, x, lane)
+                                         : lane_row_dot4<kQ8_0>(row, cols, x, lane);
         default: return lane_row_dot<kF32>(row, cols, x, lane);
     }
 }
