@@ -472,6 +472,11 @@ __device__ void route_core(const float* lg, uint32_t E, uint32_t k, uint32_t fla
 
 // Logits from the router partials (summed in split order), then route_core.
 // The `writer` CTA also stores logits, ids and weights to global memory.
+template <uint32_t kSlots>
+__device__ void route_select_regs(const MoeLayerDev& L, const float (&lgv)[kSlots], float shared_logit,
+                                  uint32_t* sel_id, float* sel_w, uint32_t* status, bool writer,
+                                  const MoeScratch& S);
+
 __device__ void phase_route(const MoeLayerDev& L, const float* partial, Shared& s,
                             uint32_t* status, bool writer, const MoeScratch& S) {
     const uint32_t splits = route_splits(L.hidden);
@@ -493,6 +498,26 @@ __device__ void phase_route(const MoeLayerDev& L, const float* partial, Shared& 
         for (uint32_t sp = 1; sp < splits; ++sp) shared_logit += p[sp];
     }
     __syncthreads();
+    if (L.experts <= 32u * 16u && L.top_k < 32u) {
+        // One warp selects from logits held in registers (k rounds of a warp
+        // maximum); the rest of the CTA waits.
+        if (threadIdx.x < 32) {
+            const uint32_t lane = threadIdx.x;
+            if (L.experts <= 32u * 8u) {
+                float lgv[8];
+#pragma unroll
+                for (uint32_t i = 0; i < 8; ++i) lgv[i] = lane + 32u * i < L.experts ? s.lg[lane + 32u * i] : 0.0f;
+                route_select_regs<8>(L, lgv, shared_logit, s.sel_id, s.sel_w, status, writer, S);
+            } else {
+                float lgv[16];
+#pragma unroll
+                for (uint32_t i = 0; i < 16; ++i) lgv[i] = lane + 32u * i < L.experts ? s.lg[lane + 32u * i] : 0.0f;
+                route_select_regs<16>(L, lgv, shared_logit, s.sel_id, s.sel_w, status, writer, S);
+            }
+        }
+        __syncthreads();
+        return;
+    }
     route_core(s.lg, L.experts, L.top_k, L.flavour, L.normalize, L.expert_weights_scale,
                L.shared_inter != 0, shared_logit, s, status);
     if (writer) {
