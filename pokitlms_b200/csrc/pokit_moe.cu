@@ -90,14 +90,15 @@ __host__ __device__ inline uint32_t stage_bytes_of(const MoeLayerDev& L) {
     if (!fast_pair(L.gate_type, L.up_type))
         s = umax(s, umax(al16(static_cast<uint32_t>(row_bytes(L.gate_type, L.hidden))),
                          al16(static_cast<uint32_t>(row_bytes(L.up_type, L.hidden)))));
-    // Generic down rows are staged eight at a time (one warp task = 8 rows).
-    if (L.down_type != kQ4_K) s = umax(s, 8u * al16(static_cast<uint32_t>(row_bytes(L.down_type, L.inter))));
+    // Generic down rows are staged eight at a time (one warp task = 8 contiguous
+    // rows, from a 16-byte boundary).
+    if (L.down_type != kQ4_K) s = umax(s, al16(8u * static_cast<uint32_t>(row_bytes(L.down_type, L.inter)) + 16u));
     if (L.shared_inter) {
         if (!fast_pair(L.shared_gate_type, L.shared_up_type))
             s = umax(s, umax(al16(static_cast<uint32_t>(row_bytes(L.shared_gate_type, L.hidden))),
                              al16(static_cast<uint32_t>(row_bytes(L.shared_up_type, L.hidden)))));
         if (L.shared_down_type != kQ4_K)
-            s = umax(s, 8u * al16(static_cast<uint32_t>(row_bytes(L.shared_down_type, L.shared_inter))));
+            s = umax(s, al16(8u * static_cast<uint32_t>(row_bytes(L.shared_down_type, L.shared_inter)) + 16u));
     }
     return s;
 }
@@ -906,16 +907,17 @@ __device__ void phase_down(const MoeLayerDev& L, Shared& s, const float* act, ui
         } else {
             // The task's (up to) 8 rows staged together: one memory latency,
             // then one warp-wide dot per row.
+            // The rows of a down matrix are contiguous: one span of nr rows.
             uint8_t* my_stage = s.stage + warp * s.m.stage_bytes;
             const uint64_t rb = row_bytes(m.down_type, m.rows);
-            const uint32_t rs = al16(static_cast<uint32_t>(rb));
             const uint32_t row0 = r0 + o * 8u;
             const uint32_t nr = min(8u, r1 - row0);
-            warp_stage_rows(m.down + row0 * rb, rb, nr, static_cast<uint32_t>(rb), my_stage, rs, lane);
+            const uint32_t delta = warp_stage_span(m.down + row0 * rb, static_cast<uint32_t>(nr * rb), my_stage, lane);
             __syncwarp();
             const float* xa = s.act_plain + slot * mi;
             for (uint32_t rr = 0; rr < nr; ++rr) {
-                const float acc = warp_sum(lane_row_dot_any(m.down_type, my_stage + rr * rs, m.rows, xa, lane));
+                const float acc =
+                    warp_sum(lane_row_dot_any(m.down_type, my_stage + delta + rr * rb, m.rows, xa, lane));
                 if (lane == 0) s.ybuf[slot * cap + (row0 + rr - r0)] = acc;
             }
             __syncwarp();
