@@ -503,13 +503,22 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     hidden = torch.empty(T, Hs, device="cuda")
     x = torch.empty(T, Hs, device="cuda")
     part = torch.empty(T, Hs, device="cuda")
+    # Configuration 5 routes by per-layer synthetic logits N(0, 1): with random
+    # weights the residual stream of this synthetic model collapses onto one
+    # direction within a few layers, after which every token of the batch would
+    # pick the same 8 experts; caller logits keep the spread of a real batch
+    # (64 x 8 routes over 128 experts, nearly all experts touched per layer).
+    route_logits = None
+    if cfg5:
+        rng = np.random.default_rng([SEED, 0x6c67])
+        route_logits = torch.from_numpy(rng.standard_normal((layers, T, E), dtype=np.float32)).cuda()
 
     def body():
         hidden.copy_(static_in)
         for l in range(layers):
             # rms_norm with ffn_norm = 1 (src/rms_norm.cpp:9-27), then the block.
             torch.mul(hidden, torch.rsqrt(hidden.pow(2).mean(dim=1, keepdim=True) + EPS), out=x)
-            ep.forward_batch(l, x, part)
+            ep.forward_batch(l, x, part, logits=None if route_logits is None else route_logits[l])
             hidden.add_(part)
 
     # Eager warm-up (sizes the batch scratch, sets kernel attributes), then the
@@ -607,6 +616,8 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
             "config": {"workload": (CFG5_WORKLOAD if cfg5 else WORKLOAD + f", expert parallel: {world} tokens "
                                     "per step (one per rank)"),
                        "tokens_per_step": T,
+                       "routing": ("per-layer synthetic logits N(0,1) (caller logits)" if cfg5 else
+                                   "the layer's F32 router"),
                        "layers": layers, "hidden": Hs, "experts": E, "top_k": K_TOP, "inter": Is,
                        "expert_type": "Q4_K", "parallelism": f"ep{world} (experts {E // world} per GPU, "
                        "NCCL all-reduce combine)", "cuda_graph": graph_used,
