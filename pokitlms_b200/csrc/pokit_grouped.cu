@@ -81,11 +81,15 @@ __device__ __forceinline__ float silu_times(float g, float u, uint32_t flavour) 
 }
 
 // ---------------------------------------------------------------------------
-// 1. Router logits for a batch: logits[t][e] = router[e] . x[t] in F32.  One
-// warp per (expert, group of 8 tokens): the expert's router row is read once
-// per group with 16-byte loads, lanes stride the hidden dimension by 128.
+// 1. Router logits for a batch: logits[t][e] = router[e] . x[t] in F32,
+// tiled and split over the hidden dimension.  A CTA computes 64 tokens x 8
+// experts over one slice of hidden (512 wide, or 256 when hidden is not a
+// multiple of 512; chunks of 128 staged in shared memory) and writes its
+// partial sums to partial[slice][t][e]; the
+// routing kernel adds the slices in order, so the logits are reproducible.
 // ---------------------------------------------------------------------------
-constexpr uint32_t kRouterTokens = 8;
+constexpr uint32_t kRtTok = 64, kRtExp = 8, kRtChunk = 128;
+__host__ __device__ constexpr uint32_t router_slice(uint32_t H) { return H % 512u == 0 ? 512u : 256u; }
 
 __device__ __forceinline__ float4 load4(const void* x, uint32_t x_bf16, size_t at) {
     if (x_bf16) {
@@ -98,31 +102,41 @@ __device__ __forceinline__ float4 load4(const void* x, uint32_t x_bf16, size_t a
 
 __global__ void __launch_bounds__(256) router_batch_kernel(const float* __restrict__ router,
                                                            const void* __restrict__ x, uint32_t x_bf16,
-                                                           uint32_t T, uint32_t E, uint32_t H,
-                                                           float* __restrict__ logits) {
-    const uint32_t gw = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint32_t e = gw % E, t0 = (gw / E) * kRouterTokens;
-    if (t0 >= T) return;
-    const uint32_t nt = min(kRouterTokens, T - t0);
-    float acc[kRouterTokens];
-#pragma unroll
-    for (uint32_t j = 0; j < kRouterTokens; ++j) acc[j] = 0.f;
-    const float* w = router + static_cast<size_t>(e) * H;
-#pragma unroll 4
-    for (uint32_t h = lane * 4; h < H; h += 128) {
-        const float4 wv = *reinterpret_cast<const float4*>(w + h);
-#pragma unroll
-        for (uint32_t j = 0; j < kRouterTokens; ++j) {
-            if (j < nt) {
-                const float4 xv = load4(x, x_bf16, static_cast<size_t>(t0 + j) * H + h);
-                acc[j] = fmaf(wv.x, xv.x, fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[j]))));
-            }
+                                                           uint32_t T, uint32_t E, uint32_t H, uint32_t slice,
+                                                           float* __restrict__ partial) {
+    __shared__ float xs[kRtTok][kRtChunk + 1];
+    __shared__ float ws[kRtExp][kRtChunk + 1];
+    const uint32_t t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, h0 = blockIdx.z * slice;
+    const uint32_t ti = threadIdx.x >> 2, ej = threadIdx.x & 3;
+    float a0 = 0.f, a1 = 0.f;
+    for (uint32_t c = 0; c < slice; c += kRtChunk) {
+        for (uint32_t i = threadIdx.x; i < kRtTok * kRtChunk / 4; i += 256) {
+            const uint32_t row = i / (kRtChunk / 4), col = 4 * (i % (kRtChunk / 4)), t = t0 + row;
+            const float4 v = t < T ? load4(x, x_bf16, static_cast<size_t>(t) * H + h0 + c + col)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            xs[row][col] = v.x; xs[row][col + 1] = v.y; xs[row][col + 2] = v.z; xs[row][col + 3] = v.w;
         }
+        if (threadIdx.x < kRtExp * kRtChunk / 4) {
+            const uint32_t row = threadIdx.x / (kRtChunk / 4), col = 4 * (threadIdx.x % (kRtChunk / 4));
+            const uint32_t e = e0 + row;
+            const float4 v = e < E ? *reinterpret_cast<const float4*>(router + static_cast<size_t>(e) * H + h0 + c + col)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            ws[row][col] = v.x; ws[row][col + 1] = v.y; ws[row][col + 2] = v.z; ws[row][col + 3] = v.w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (uint32_t k = 0; k < kRtChunk; ++k) {
+            const float xv = xs[ti][k];
+            a0 = fmaf(ws[ej][k], xv, a0);
+            a1 = fmaf(ws[ej + 4][k], xv, a1);
+        }
+        __syncthreads();
     }
-#pragma unroll
-    for (uint32_t j = 0; j < kRouterTokens; ++j) {
-        const float v = warp_sum(acc[j]);
-        if (lane == 0 && j < nt) logits[static_cast<size_t>(t0 + j) * E + e] = v;
+    const uint32_t t = t0 + ti;
+    if (t < T) {
+        float* out = partial + (static_cast<size_t>(blockIdx.z) * T + t) * E;
+        if (e0 + ej < E) out[e0 + ej] = a0;
+        if (e0 + ej + 4 < E) out[e0 + ej + 4] = a1;
     }
 }
 
@@ -820,7 +834,7 @@ BatchSizes batch_sizes(const MoeLayerDev& L, uint32_t T) {
     z.max_tiles = max_tiles_for(z.pairs, L.expert_local);
     z.max_padded = z.pairs + 15u * z.max_tiles;
     const size_t Sg = L.hidden / 256, Sd = L.inter / 256;
-    z.logits = al256(size_t(T) * L.experts * 4);
+    z.logits = al256(size_t(T) * L.experts * 4 * std::max<uint32_t>(1u, L.hidden / router_slice(L.hidden)));
     z.ids = al256(size_t(z.pairs) * 4);
     z.weights = z.ids;
     z.rank = z.ids;
@@ -923,18 +937,21 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         return cudaErrorInvalidValue;
 
     mark();
-    // 1. router
+    // 1. router (partials over hidden slices when it runs here)
     const float* lg = logits;
+    uint32_t splits = 1;
     if (!lg) {
-        const uint32_t warps = E * ((tokens + kRouterTokens - 1) / kRouterTokens);
-        router_batch_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H, S.logits);
+        const uint32_t slice = router_slice(H);
+        const dim3 rgrid((tokens + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, H / slice);
+        router_batch_kernel<<<rgrid, 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H, slice, S.logits);
+        splits = H / slice;
         ++n;
         mark();
         lg = S.logits;
     }
     // 2. routes
     if ((err = launch_route_experts(lg, E, k, L.flavour, L.normalize, L.expert_weights_scale, S.ids, S.weights,
-                                    status, stream, tokens)) != cudaSuccess)
+                                    status, stream, tokens, splits)) != cudaSuccess)
         return err;
     ++n;
     mark();

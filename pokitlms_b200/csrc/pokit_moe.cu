@@ -1010,7 +1010,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(BlockArgs a) {
 __global__ void __launch_bounds__(kThreads, 1)
 route_logits_kernel(const float* __restrict__ logits, uint32_t E, uint32_t k, uint32_t flavour,
                     uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
-                    uint32_t* status) {
+                    uint32_t* status, uint32_t splits) {
     __shared__ float lg[kMaxExperts];
     __shared__ double red[64];
     __shared__ uint32_t sel_id[kMaxTopK + 1];
@@ -1019,11 +1019,17 @@ route_logits_kernel(const float* __restrict__ logits, uint32_t E, uint32_t k, ui
     s.red = red;
     s.sel_id = sel_id;
     s.sel_w = sel_w;
-    // One CTA per logits row (a batch of tokens routes row by row).
-    logits += static_cast<size_t>(blockIdx.x) * E;
+    // One CTA per logits row (a batch of tokens routes row by row); a row may
+    // arrive as `splits` partial rows (slices of the hidden dimension, split s
+    // at logits + (s * rows + row) * E), added here in slice order.
+    const size_t rows = gridDim.x;
     ids += static_cast<size_t>(blockIdx.x) * k;
     weights += static_cast<size_t>(blockIdx.x) * k;
-    for (uint32_t e = threadIdx.x; e < E; e += kThreads) lg[e] = logits[e];
+    for (uint32_t e = threadIdx.x; e < E; e += kThreads) {
+        float v = logits[static_cast<size_t>(blockIdx.x) * E + e];
+        for (uint32_t sp = 1; sp < splits; ++sp) v += logits[(sp * rows + blockIdx.x) * E + e];
+        lg[e] = v;
+    }
     __syncthreads();
     route_core(lg, E, k, flavour, normalize, ew_scale, false, 0.0f, s, status);
     for (uint32_t r = threadIdx.x; r < k; r += kThreads) {
@@ -1722,10 +1728,11 @@ MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base, uint32_t rep) {
 
 cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, uint32_t flavour,
                                  uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
-                                 uint32_t* status, cudaStream_t stream, uint32_t rows) {
-    if (k == 0 || k > E || k > kMaxTopK || E > kMaxExperts || rows == 0) return cudaErrorInvalidValue;
+                                 uint32_t* status, cudaStream_t stream, uint32_t rows, uint32_t splits) {
+    if (k == 0 || k > E || k > kMaxTopK || E > kMaxExperts || rows == 0 || splits == 0)
+        return cudaErrorInvalidValue;
     route_logits_kernel<<<rows, kThreads, 0, stream>>>(logits, E, k, flavour, normalize, ew_scale,
-                                                       ids, weights, status);
+                                                       ids, weights, status, splits);
     return cudaGetLastError();
 }
 
