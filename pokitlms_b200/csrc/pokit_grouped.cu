@@ -54,6 +54,7 @@
 
 #include "pokit_common.cuh"
 #include "pokit_kernels.h"
+#include "pokit_quant.cuh"
 #include "pokit_tc.cuh"
 #include "pokit_types.h"
 
@@ -61,6 +62,7 @@ namespace pokit {
 namespace {
 
 constexpr uint32_t kTileTokens = 64;                  // N of one GEMM tile
+constexpr uint32_t kSkinny = 8;                       // tiles of <= 8 tokens take the mma.sync path
 constexpr uint32_t kQStage = 128u * 144u;             // one superblock of 128 rows
 constexpr uint32_t kSortThreads = 512;
 constexpr uint32_t kSortWarps = kSortThreads / 32;
@@ -148,7 +150,8 @@ __global__ void __launch_bounds__(256) router_batch_kernel(const float* __restri
 // One CTA.
 // ---------------------------------------------------------------------------
 struct GroupOut {
-    uint32_t* plan;        // [0] tiles, [1] padded slots
+    uint32_t* plan;        // [0] tiles, [1] padded slots, [2] tiles of > kSkinny tokens, [3] the others
+    uint32_t* tile_order;  // the large tiles, then the skinny ones
     uint32_t* tile_expert;
     uint32_t* tile_first;  // first slot (index into slot_pair)
     uint32_t* tile_n;      // tokens in the tile (1..64)
@@ -165,6 +168,8 @@ __global__ void __launch_bounds__(kSortThreads, 1) group_kernel(const uint32_t* 
     uint32_t* off_slot = total + E;             // [E]
     uint32_t* off_tile = off_slot + E;          // [E]
     uint32_t* off_pad = off_tile + E;           // [E]
+    uint32_t* off_thin = off_pad + E;           // [E] skinny tiles before expert e
+    uint32_t* n_large = off_thin + E;           // [1]
     const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     for (uint32_t e = tid; e < E; e += kSortThreads) total[e] = 0;
     __syncthreads();
@@ -194,44 +199,56 @@ __global__ void __launch_bounds__(kSortThreads, 1) group_kernel(const uint32_t* 
     }
     if (warp == 0) {
         const uint32_t per = (E + 31) / 32, lo = min(E, lane * per), hi = min(E, lo + per);
-        uint32_t sc = 0, st = 0, sp = 0;
+        // An expert's last tile is skinny when it holds 1..kSkinny tokens.
+        const auto thin = [](uint32_t c) -> uint32_t { return (c % kTileTokens) != 0 && (c % kTileTokens) <= kSkinny; };
+        uint32_t sc = 0, st = 0, sp = 0, ss = 0;
         for (uint32_t e = lo; e < hi; ++e) {
             const uint32_t c = total[e];
             sc += c;
             st += (c + kTileTokens - 1) / kTileTokens;
             sp += padded_slots(c);
+            ss += thin(c);
         }
-        uint32_t ic = sc, it = st, ip = sp;
+        uint32_t ic = sc, it = st, ip = sp, is = ss;
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
             const uint32_t a = __shfl_up_sync(0xFFFFFFFFu, ic, d), b = __shfl_up_sync(0xFFFFFFFFu, it, d),
-                           c = __shfl_up_sync(0xFFFFFFFFu, ip, d);
-            if (lane >= static_cast<uint32_t>(d)) { ic += a; it += b; ip += c; }
+                           c = __shfl_up_sync(0xFFFFFFFFu, ip, d), f = __shfl_up_sync(0xFFFFFFFFu, is, d);
+            if (lane >= static_cast<uint32_t>(d)) { ic += a; it += b; ip += c; is += f; }
         }
-        uint32_t rc = ic - sc, rt = it - st, rp = ip - sp;
+        uint32_t rc = ic - sc, rt = it - st, rp = ip - sp, rs = is - ss;
         for (uint32_t e = lo; e < hi; ++e) {
             const uint32_t c = total[e];
             off_slot[e] = rc;
             off_tile[e] = rt;
             off_pad[e] = rp;
+            off_thin[e] = rs;
             rc += c;
             rt += (c + kTileTokens - 1) / kTileTokens;
             rp += padded_slots(c);
+            rs += thin(c);
         }
         if (lane == 31) {
             o.plan[0] = it;
             o.plan[1] = ip;
+            o.plan[2] = it - is;
+            o.plan[3] = is;
+            *n_large = it - is;
         }
     }
     __syncthreads();
+    const uint32_t large = *n_large;
     for (uint32_t e = tid; e < E; e += kSortThreads) {
         const uint32_t c = total[e];
         for (uint32_t i = 0; i * kTileTokens < c; ++i) {
             const uint32_t tile = off_tile[e] + i;
+            const uint32_t n = min(kTileTokens, c - i * kTileTokens);
             o.tile_expert[tile] = e;
             o.tile_first[tile] = off_slot[e] + i * kTileTokens;
-            o.tile_n[tile] = min(kTileTokens, c - i * kTileTokens);
+            o.tile_n[tile] = n;
             o.tile_pad0[tile] = off_pad[e] + i * kTileTokens;
+            // Large tiles before expert e: its tile index minus the skinny ones.
+            o.tile_order[n <= kSkinny ? large + off_thin[e] : tile - off_thin[e]] = tile;
         }
     }
     for (uint32_t p = tid; p < pairs; p += kSortThreads) {
@@ -260,6 +277,28 @@ struct PackArgs {
 
 // Bytes of one packed superblock row: (kc8 + 2) chunks of 16 bytes + a scale.
 __host__ __device__ constexpr uint32_t packed_row_bytes(uint32_t kc8) { return (kc8 + 2) * 16 + 4; }
+
+// Skinny tiles (<= kSkinny tokens) are packed as mma.sync B fragments, per
+// superblock s at tile base + s * thin_stage_bytes(split):
+//   [0, 256)    sub-block sums, token n, lane quarter t: fp16 {hi(2t),
+//               hi(2t+1), lo(2t), lo(2t+1)} at (4n + t) * 8
+//   [256, 288)  the tokens' power-of-two scales (float)
+//   [288, ...)  token n at 288 + n * thin_token_bytes: its hi parts (512
+//               bytes), then its lo parts (split only).  Lane quarter t's
+//               128 bytes at t * 128 hold eight 16-byte chunks; chunk w (the
+//               qs word w of Q4_K chunk t) sits at slot w ^ ((4n + t) & 7) and
+//               holds the fp16 x of K positions 64t + 4w + {0, 2, 1, 3} and
+//               64t + 32 + 4w + {0, 2, 1, 3}: the B registers of k-steps 2w
+//               (low nibbles) and 2w + 1 (high nibbles).
+// The tile's region is the one the tensor-core layout would use (16 padded
+// slots hold more than 288 + 8 * 1024 bytes per superblock).
+constexpr uint32_t kThinTail = 288;
+__host__ __device__ constexpr uint32_t thin_token_bytes(uint32_t split) { return split ? 1024u : 512u; }
+__host__ __device__ constexpr uint32_t thin_stage_bytes(uint32_t split) {
+    return kThinTail + kSkinny * thin_token_bytes(split);
+}
+static_assert(thin_stage_bytes(1) <= 16 * packed_row_bytes(64) && thin_stage_bytes(0) <= 16 * packed_row_bytes(32),
+              "skinny packing fits a 16-slot tile");
 
 __device__ __forceinline__ uint4 pack8_half(const float (&v)[8]) {
     uint4 r;
@@ -297,7 +336,8 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t n = blockIdx.y * (kPackThreads / 32) + warp;
     const uint32_t n_valid = a.tile_n[tile], np = round16(n_valid), pad0 = a.tile_pad0[tile];
-    if (n >= np) return;
+    const bool thin = n_valid <= kSkinny;
+    if (n >= (thin ? kSkinny : np)) return;
     const uint32_t S = a.cols / 256, kc8 = a.split ? 64u : 32u;
     const uint32_t stage_bytes = packed_row_bytes(kc8) * np;
     uint8_t* tile_base = a.dst + static_cast<size_t>(pad0) * S * packed_row_bytes(kc8);
@@ -339,6 +379,34 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
             part += __shfl_xor_sync(0xFFFFFFFFu, part, 1);
             part += __shfl_xor_sync(0xFFFFFFFFu, part, 2);
             __syncwarp();
+            if (thin) {
+                // Rows n_valid..7 are written as zeros, so every fragment of the tile is finite.
+                uint8_t* region = tile_base + static_cast<size_t>(s) * thin_stage_bytes(a.split);
+                const uint32_t t = lane >> 3, w = lane & 7;
+                const float* b0 = st + 33 * (2 * t) + 4 * w;
+                const float* b1 = st + 33 * (2 * t + 1) + 4 * w;
+                const float e[8] = {b0[0], b0[2], b0[1], b0[3], b1[0], b1[2], b1[1], b1[3]};
+                float hi[8], lo[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    hi[i] = __half2float(__float2half_rn(e[i]));
+                    lo[i] = e[i] - hi[i];
+                }
+                uint8_t* tok = region + kThinTail + n * thin_token_bytes(a.split) + t * 128 + ((w ^ ((4 * n + t) & 7)) << 4);
+                *reinterpret_cast<uint4*>(tok) = pack8_half(hi);
+                if (a.split) *reinterpret_cast<uint4*>(tok + 512) = pack8_half(lo);
+                if ((lane & 3) == 0) {
+                    const uint32_t j = lane >> 2;
+                    const __half h = __float2half_rn(part);
+                    const __half l = __float2half_rn(part - __half2float(h));
+                    __half* sums = reinterpret_cast<__half*>(region) + (4 * n + (j >> 1)) * 4 + (j & 1);
+                    sums[0] = h;
+                    sums[2] = l;
+                }
+                if (lane == 0) reinterpret_cast<float*>(region + 256)[n] = __int_as_float((127 + sig) << 23);
+                __syncwarp();
+                continue;
+            }
             uint8_t* region = tile_base + static_cast<size_t>(s) * stage_bytes;
             {
                 const uint32_t c = lane >> 3, w = lane & 7;
@@ -402,6 +470,7 @@ struct GemmArgs {
     CUtensorMap tm1;          // up (mode 0)
     const uint8_t* b;         // packed activations (pack_kernel layout)
     const uint32_t* plan;
+    const uint32_t* tile_order;   // [0, plan[2]): the tiles of > kSkinny tokens
     const uint32_t* tile_expert;
     const uint32_t* tile_first;
     const uint32_t* tile_n;
@@ -510,7 +579,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
     const uint32_t S = a.K / 256;
     constexpr uint32_t kRowsPerUnit = kMode == 0 ? 64u : 128u;
     const uint32_t mblocks = a.rows / kRowsPerUnit;
-    const uint32_t units = a.plan[0] * mblocks;
+    const uint32_t units = a.plan[2] * mblocks;
 
     const auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
         if (*abort_flag) return false;
@@ -534,7 +603,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
             uint32_t g = 0;
             bool ok = true;
             for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
-                const uint32_t tile = u / mblocks, mb = u % mblocks;
+                const uint32_t tile = a.tile_order[u / mblocks], mb = u % mblocks;
                 const uint32_t e = a.tile_expert[tile], np = round16(a.tile_n[tile]);
                 const uint32_t stage = packed_row_bytes(Lay::kc8) * np;
                 const uint8_t* bsrc = a.b + static_cast<size_t>(a.tile_pad0[tile]) * S * packed_row_bytes(Lay::kc8);
@@ -569,7 +638,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
             uint32_t g = 0;
             bool ok = true;
             for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
-                const uint32_t tile = u / mblocks;
+                const uint32_t tile = a.tile_order[u / mblocks];
                 const uint32_t np = round16(a.tile_n[tile]);
                 const uint32_t idesc = tc_idesc_f16(128, np);
                 const uint32_t lbo = np * 16;
@@ -673,7 +742,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
         uint32_t g = 0, ui = 0;
         bool ok = true;
         for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ui) {
-            const uint32_t tile = u / mblocks, mb = u % mblocks;
+            const uint32_t tile = a.tile_order[u / mblocks], mb = u % mblocks;
             const uint32_t n_valid = a.tile_n[tile], np = round16(n_valid), pad0 = a.tile_pad0[tile];
             const uint32_t hn = np >> 1, c0 = nh * hn;
 #pragma unroll
@@ -786,6 +855,284 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
 }
 
 // ---------------------------------------------------------------------------
+// 5b/7b. Skinny tiles (<= kSkinny tokens) on mma.sync.m16n8k16 (fp16 in,
+// F32 accumulate).  A tcgen05 MMA costs the same for 8 tokens as for 128, so
+// a tile of a few tokens would leave the weights' HBM stream waiting on the
+// tensor core; here the weights go straight from shared memory into A
+// registers and each MMA multiplies 16 rows by the tile's 8 token columns.
+//
+// Persistent, one CTA per SM; a unit is (skinny tile, 128 rows of gate and the
+// same 128 rows of up) or (skinny tile, 128 rows of down).  The last warp (one
+// lane) loads each superblock of the unit into a ring stage: the Q4_K rows by
+// TMA (144 bytes x 128 rows per matrix) and the tile's packed activations (the
+// skinny layout above) by one bulk copy.  Two groups of eight warps take the
+// unit's even and odd superblocks; in a group, warp w owns rows 16w..16w+15:
+// thread (g = lane / 4, t = lane % 4) dequantises Q4_K chunk t (qs bytes
+// 32t..32t+31: sub-blocks 2t, 2t+1) of rows g and g + 8 into fp16 s_j q
+// (exact; the tensor-core path's nibble arithmetic) and feeds them as A with
+// the activation fragments as B; one more MMA (A = m_j, B = the sub-block
+// sums as hi + lo) gives the mins; d, dmin and the tokens' scales are applied
+// per superblock in F32.  The odd group hands its sums to the even group,
+// which writes the unit's outputs.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kThinRowWarps = 8;                        // 16 rows each: 128 rows
+constexpr uint32_t kThinWarps = 2 * kThinRowWarps;           // two superblock groups
+constexpr uint32_t kThinThreads = (kThinWarps + 1) * 32;     // + the loader
+
+template <int kMode, int kSplit>
+struct ThinLayout {
+    static constexpr uint32_t mats = kMode == 0 ? 2u : 1u;
+    static constexpr uint32_t wbytes = mats * kQStage;
+    static constexpr uint32_t stage = (wbytes + thin_stage_bytes(kSplit) + 127u) & ~127u;
+    static constexpr uint32_t xch_bytes = kThinRowWarps * 32 * mats * 4 * 4;   // odd group's sums
+    static constexpr uint32_t budget = 220u * 1024u - xch_bytes;
+    static constexpr uint32_t stages = budget / stage < 8u ? budget / stage : 8u;
+    static constexpr uint32_t xch_off = stages * stage;
+    static constexpr uint32_t bar_off = xch_off + xch_bytes;
+    static constexpr uint32_t total = bar_off + (2 * stages + 2) * 8 + 16;
+};
+
+struct ThinArgs {
+    CUtensorMap tm0;          // gate (mode 0) or down (mode 1), 128-row boxes
+    CUtensorMap tm1;          // up (mode 0)
+    const uint8_t* b;         // packed activations
+    const uint32_t* plan;
+    const uint32_t* tile_order;   // [plan[2], plan[2] + plan[3]): the skinny tiles
+    const uint32_t* tile_expert;
+    const uint32_t* tile_first;
+    const uint32_t* tile_n;
+    const uint32_t* tile_pad0;
+    const uint32_t* slot_pair;
+    const float* route_w;
+    float* out;               // mode 0: act [padded][rows]; mode 1: pair_out [pairs][rows]
+    uint32_t K, rows, flavour;
+    uint32_t* status;
+};
+
+// 6-bit scales (s0, s1) and mins (m0, m1) of sub-blocks 2t and 2t + 1 from a
+// Q4_K header's scale words (hy, hz, hw = bytes 0..3, 4..7, 8..11), both
+// sub-blocks at once and without a branch on t: the k_scale_min unpacking of
+// decode_q4_k (src/quantized_linear.cpp:176-188).
+__device__ __forceinline__ void q4k_pair_scales(uint32_t hy, uint32_t hz, uint32_t hw, uint32_t t, uint32_t& sc,
+                                                uint32_t& mn) {
+    const uint32_t sh = 16 * (t & 1);
+    const uint32_t a = hy >> sh, b = hz >> sh, c = hw >> sh;
+    const uint32_t sc_lo = a & 0x3F3Fu, mn_lo = b & 0x3F3Fu;                      // sub-blocks 0..3
+    const uint32_t sc_hi = (c & 0x0F0Fu) | ((a >> 2) & 0x3030u);                   // sub-blocks 4..7
+    const uint32_t mn_hi = ((c >> 4) & 0x0F0Fu) | ((b >> 2) & 0x3030u);
+    sc = t >= 2 ? sc_hi : sc_lo;   // byte 0: sub-block 2t, byte 1: 2t + 1
+    mn = t >= 2 ? mn_hi : mn_lo;
+}
+// (v, v) in fp16 for an integer v < 1024: 1024 + v has v as its mantissa.
+__device__ __forceinline__ uint32_t half2_small(uint32_t v) {
+    return hsub2u((v * 0x10001u) | kHalfMagic, kHalfMagic);
+}
+// nibble_scales for the 6-bit scales in bytes 0 (low nibbles) and 1 (high) of sc.
+__device__ __forceinline__ NibbleScales nibble_scales_packed(uint32_t sc) {
+    NibbleScales n;
+    const uint32_t lo = half2_small(sc & 0xFFu), hi = half2_small((sc >> 8) & 0xFFu);
+    n.lo_mul = lo;
+    n.lo_add = hmul2u(lo, kHalfNeg1024);
+    n.hi_mul = hmul2u(hi, kHalfInv16);
+    n.hi_add = hmul2u(hi, kHalfNeg64);
+    return n;
+}
+
+template <int kMode, int kSplit>
+__global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid_constant__ ThinArgs a) {
+    using Lay = ThinLayout<kMode, kSplit>;
+    constexpr uint32_t kMats = Lay::mats, kStages = Lay::stages;
+    constexpr uint32_t kTok = thin_token_bytes(kSplit);
+    extern __shared__ __align__(1024) uint8_t smem[];
+    float* xch = reinterpret_cast<float*>(smem + Lay::xch_off);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::bar_off);
+    uint64_t* empty = full + kStages;
+    uint64_t* xch_full = empty + kStages;   // odd group's sums written
+    uint64_t* xch_free = xch_full + 1;      // ... and read
+    volatile uint32_t* abort_flag = reinterpret_cast<uint32_t*>(xch_free + 1);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < kStages; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, kThinRowWarps);
+        }
+        mbar_init(xch_full, kThinRowWarps);
+        mbar_init(xch_free, kThinRowWarps);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    const uint32_t S = a.K / 256;
+    const uint32_t mblocks = a.rows / 128;
+    const uint32_t first_thin = a.plan[2];
+    const uint32_t units = a.plan[3] * mblocks;
+    const size_t tile_stride = static_cast<size_t>(S) * packed_row_bytes(kSplit ? 64u : 32u);
+
+    const auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (*abort_flag) return false;
+        if (mbar_wait_ns(bar, parity)) return true;
+        atomicOr(a.status, kStatusWaitTimeout);
+        *abort_flag = 1;
+        return false;
+    };
+    const auto wait_warp = [&](uint64_t* bar, uint32_t parity) -> bool {
+        return __all_sync(0xFFFFFFFFu, wait(bar, parity)) != 0;
+    };
+
+    if (warp == kThinWarps) {
+        // ---------------- loader ----------------
+        if (lane == 0) {
+            int32_t last[kStages];
+            for (uint32_t i = 0; i < kStages; ++i) last[i] = -1;
+            uint32_t g = 0;
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
+                const uint32_t tile = a.tile_order[first_thin + u / mblocks], mb = u % mblocks;
+                const uint32_t e = a.tile_expert[tile];
+                const uint8_t* src = a.b + a.tile_pad0[tile] * tile_stride;
+                for (uint32_t s = 0; s < S; ++s, ++g) {
+                    const uint32_t slot = g % kStages;
+                    if (!(ok = wait(empty + slot, ((g / kStages) & 1) ^ 1))) break;
+                    uint8_t* st = smem + slot * Lay::stage;
+                    mbar_expect_tx(full + slot, Lay::wbytes + thin_stage_bytes(kSplit));
+                    tma_box_3d(st, &a.tm0, s * 144, mb * 128, e, full + slot);
+                    if (kMode == 0) tma_box_3d(st + kQStage, &a.tm1, s * 144, mb * 128, e, full + slot);
+                    bulk_g2s(st + Lay::wbytes, src + static_cast<size_t>(s) * thin_stage_bytes(kSplit),
+                             thin_stage_bytes(kSplit), full + slot);
+                    last[slot] = static_cast<int32_t>(g);
+                }
+            }
+            if (*abort_flag) {
+                // Let the copies in flight land before the CTA exits.
+                for (uint32_t i = 0; i < kStages; ++i)
+                    if (last[i] >= 0) mbar_wait_ns(full + i, (static_cast<uint32_t>(last[i]) / kStages) & 1);
+            }
+        }
+        return;
+    }
+
+    // ---------------- compute ----------------
+    const uint32_t grp = warp / kThinRowWarps, rw = warp % kThinRowWarps;
+    const uint32_t g8 = lane >> 2, t = lane & 3;
+    const uint32_t r0 = 16 * rw + g8;
+    const uint32_t swz = (4 * g8 + t) & 7;
+    uint32_t g = 0, ui = 0;
+    bool ok = true;
+    for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ui) {
+        const uint32_t tile = a.tile_order[first_thin + u / mblocks], mb = u % mblocks;
+        float tot[kMats][4];
+#pragma unroll
+        for (uint32_t m = 0; m < kMats; ++m)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tot[m][i] = 0.f;
+        for (uint32_t s = 0; s < S; ++s, ++g) {
+            if ((s & 1) != grp) continue;
+            const uint32_t slot = g % kStages;
+            if (!(ok = wait_warp(full + slot, (g / kStages) & 1))) break;
+            const uint8_t* st = smem + slot * Lay::stage;
+            const uint8_t* xs = st + Lay::wbytes;
+            const uint8_t* xt = xs + kThinTail + g8 * kTok + t * 128;
+            const uint2 bm = *reinterpret_cast<const uint2*>(xs + (4 * g8 + t) * 8);   // token g8's sums
+            const float2 sc = *reinterpret_cast<const float2*>(xs + 256 + 8 * t);     // tokens 2t, 2t + 1
+            // One matrix at a time (not unrolled): the registers of one set of rows.
+#pragma unroll 1
+            for (uint32_t m = 0; m < kMats; ++m) {
+                const uint8_t* row0 = st + m * kQStage + r0 * 144;
+                const uint8_t* row1 = row0 + 8 * 144;
+                const uint4 h0 = *reinterpret_cast<const uint4*>(row0);
+                const uint4 h1 = *reinterpret_cast<const uint4*>(row1);
+                const uint4 qa0 = *reinterpret_cast<const uint4*>(row0 + 16 + 32 * t);
+                const uint4 qa1 = *reinterpret_cast<const uint4*>(row0 + 32 + 32 * t);
+                const uint4 qb0 = *reinterpret_cast<const uint4*>(row1 + 16 + 32 * t);
+                const uint4 qb1 = *reinterpret_cast<const uint4*>(row1 + 32 + 32 * t);
+                uint32_t sca, mna, scb, mnb;
+                q4k_pair_scales(h0.y, h0.z, h0.w, t, sca, mna);
+                q4k_pair_scales(h1.y, h1.z, h1.w, t, scb, mnb);
+                const NibbleScales na = nibble_scales_packed(sca), nb = nibble_scales_packed(scb);
+                const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
+                const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
+                // acc[parity]: low-nibble k-steps (parity 0) and high (1), hi and lo activations.
+                float acc[2][4] = {};
+#pragma unroll
+                for (uint32_t w = 0; w < 8; ++w) {
+                    const uint4 xh = *reinterpret_cast<const uint4*>(xt + ((w ^ swz) << 4));
+                    uint32_t ra[4], rb[4];   // rows g8 and g8 + 8
+                    dequant_word(wa[w], na, ra);
+                    dequant_word(wb[w], nb, rb);
+                    mma16816(acc[0], ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
+                    mma16816(acc[1], ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
+                    if (kSplit) {
+                        const uint4 xl = *reinterpret_cast<const uint4*>(xt + 512 + ((w ^ swz) << 4));
+                        mma16816(acc[0], ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
+                        mma16816(acc[1], ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
+                    }
+                }
+                float mn[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint32_t am0 = half2_small(mna & 0xFFu) & 0xFFFFu | (half2_small(mna >> 8) << 16);
+                const uint32_t am1 = half2_small(mnb & 0xFFu) & 0xFFFFu | (half2_small(mnb >> 8) << 16);
+                mma16816(mn, am0, am1, am0, am1, bm.x, bm.y);
+                const float d0 = half_bits_to_float(h0.x), dm0 = half_bits_to_float(h0.x >> 16);
+                const float d1 = half_bits_to_float(h1.x), dm1 = half_bits_to_float(h1.x >> 16);
+                float part[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float q = acc[0][i] + acc[1][i];
+                    const float d = i < 2 ? d0 : d1, dmin = i < 2 ? dm0 : dm1;
+                    part[i] = fmaf(d, q, -dmin * mn[i]) * ((i & 1) ? sc.y : sc.x);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (m == 0) tot[0][i] += part[i];
+                    else tot[kMats - 1][i] += part[i];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + slot);
+        }
+        if (!ok) break;
+        // The odd group's sums go to the even group through shared memory.
+        float* mine = xch + (rw * 32 + lane) * (kMats * 4);
+        if (grp == 1) {
+            if (!(ok = wait_warp(xch_free, (ui & 1) ^ 1))) break;
+#pragma unroll
+            for (uint32_t m = 0; m < kMats; ++m)
+                *reinterpret_cast<float4*>(mine + 4 * m) = make_float4(tot[m][0], tot[m][1], tot[m][2], tot[m][3]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(xch_full);
+            continue;
+        }
+        if (!(ok = wait_warp(xch_full, ui & 1))) break;
+#pragma unroll
+        for (uint32_t m = 0; m < kMats; ++m) {
+            const float4 o = *reinterpret_cast<const float4*>(mine + 4 * m);
+            tot[m][0] += o.x;
+            tot[m][1] += o.y;
+            tot[m][2] += o.z;
+            tot[m][3] += o.w;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xch_free);
+        // Columns 2t, 2t + 1 of rows r0 and r0 + 8.
+        const uint32_t n_valid = a.tile_n[tile], first = a.tile_first[tile], pad0 = a.tile_pad0[tile];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t col = 2 * t + (i & 1);
+            const uint32_t row = mb * 128 + r0 + (i < 2 ? 0u : 8u);
+            if (col < n_valid) {
+                if (kMode == 0) {
+                    a.out[static_cast<size_t>(pad0 + col) * a.rows + row] =
+                        silu_times(tot[0][i], tot[kMats - 1][i], a.flavour);
+                } else {
+                    const uint32_t p = a.slot_pair[first + col];
+                    a.out[static_cast<size_t>(p) * a.rows + row] = a.route_w[p] * tot[0][i];
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // 8. Combine: out[t] = sum_r pair_out[t * k + r] in rank order from 0
 // (the reference adds w_r * y_r in that order, qwen3_moe_runner.cpp:688-690),
 // over the ranks whose expert this device holds.
@@ -817,6 +1164,9 @@ using DownLay = GemmLayout<1, 1, 4, 2>;
 static_assert(GateUpBf16::total <= 227 * 1024, "gate/up (bf16) shared memory");
 static_assert(GateUpF32::total <= 227 * 1024, "gate/up (f32) shared memory");
 static_assert(DownLay::total <= 227 * 1024, "down shared memory");
+static_assert(ThinLayout<0, 0>::total <= 227 * 1024 && ThinLayout<0, 1>::total <= 227 * 1024 &&
+                  ThinLayout<1, 1>::total <= 227 * 1024,
+              "skinny shared memory");
 
 uint32_t max_tiles_for(uint32_t pairs, uint32_t E) { return pairs / kTileTokens + std::min(E, pairs) + 1; }
 
@@ -845,7 +1195,7 @@ BatchSizes batch_sizes(const MoeLayerDev& L, uint32_t T) {
     z.act = al256(size_t(z.max_padded) * L.inter * 4);
     z.bdn = al256(size_t(z.max_padded) * Sd * packed_row_bytes(64));
     z.pair_out = al256(size_t(z.pairs) * L.hidden * 4);
-    z.total = z.logits + z.ids + z.weights + z.rank + z.plan + 4 * z.tiles + z.slot_pair + z.bgu + z.act + z.bdn +
+    z.total = z.logits + z.ids + z.weights + z.rank + z.plan + 5 * z.tiles + z.slot_pair + z.bgu + z.act + z.bdn +
               z.pair_out;
     return z;
 }
@@ -901,6 +1251,7 @@ MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_token
     S.weights = reinterpret_cast<float*>(take(z.weights));
     S.rank = reinterpret_cast<uint32_t*>(take(z.rank));
     S.plan = reinterpret_cast<uint32_t*>(take(z.plan));
+    S.tile_order = reinterpret_cast<uint32_t*>(take(z.tiles));
     S.tile_expert = reinterpret_cast<uint32_t*>(take(z.tiles));
     S.tile_first = reinterpret_cast<uint32_t*>(take(z.tiles));
     S.tile_n = reinterpret_cast<uint32_t*>(take(z.tiles));
@@ -916,9 +1267,9 @@ MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_token
 cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, const void* x, uint32_t x_bf16,
                              uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
                              uint32_t* status, cudaStream_t stream, uint32_t* launches, cudaEvent_t* marks) {
-    uint32_t n = 0;
+    uint32_t n = 0, stage = 0;   // kernels launched; stage boundaries marked
     const auto mark = [&]() {
-        if (marks) cudaEventRecord(marks[n], stream);
+        if (marks) cudaEventRecord(marks[stage++], stream);
     };
     if (launches) *launches = 0;
     if (!moe_batch_grouped(L) || tokens == 0 || tokens > S.max_tokens || !x || !out || !status)
@@ -929,10 +1280,12 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     const uint32_t pairs = tokens * k;
     cudaError_t err;
 
-    CUtensorMap tg{}, tu{}, td{};
+    CUtensorMap tg{}, tu{}, td{}, tg128{}, tu128{};
     const uint64_t rb_in = row_bytes(kQ4_K, H), rb_dn = row_bytes(kQ4_K, I);
     if (!encode_expert_map(&tg, L.gate, rb_in, I, EL, L.gate_slice, 64) ||
         !encode_expert_map(&tu, L.up, rb_in, I, EL, L.up_slice, 64) ||
+        !encode_expert_map(&tg128, L.gate, rb_in, I, EL, L.gate_slice, 128) ||
+        !encode_expert_map(&tu128, L.up, rb_in, I, EL, L.up_slice, 128) ||
         !encode_expert_map(&td, L.down, rb_dn, H, EL, L.down_slice, 128))
         return cudaErrorInvalidValue;
 
@@ -957,8 +1310,8 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     mark();
     // 3. group
     {
-        GroupOut o{S.plan, S.tile_expert, S.tile_first, S.tile_n, S.tile_pad0, S.slot_pair, S.rank};
-        const uint32_t smem = (kSortWarps + 4) * EL * 4;
+        GroupOut o{S.plan, S.tile_order, S.tile_expert, S.tile_first, S.tile_n, S.tile_pad0, S.slot_pair, S.rank};
+        const uint32_t smem = (kSortWarps + 5) * EL * 4 + 16;
         if ((err = set_smem(group_kernel, smem)) != cudaSuccess) return err;
         group_kernel<<<1, kSortThreads, smem, stream>>>(S.ids, pairs, E0, EL, o);
         ++n;
@@ -990,6 +1343,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     ga.tm1 = tu;
     ga.b = S.b_gate_up;
     ga.plan = S.plan;
+    ga.tile_order = S.tile_order;
     ga.tile_expert = S.tile_expert;
     ga.tile_first = S.tile_first;
     ga.tile_n = S.tile_n;
@@ -1001,16 +1355,39 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     ga.rows = I;
     ga.flavour = L.flavour;
     ga.status = status;
+    ThinArgs ta{};
+    ta.tm0 = tg128;
+    ta.tm1 = tu128;
+    ta.b = S.b_gate_up;
+    ta.plan = S.plan;
+    ta.tile_order = S.tile_order;
+    ta.tile_expert = S.tile_expert;
+    ta.tile_first = S.tile_first;
+    ta.tile_n = S.tile_n;
+    ta.tile_pad0 = S.tile_pad0;
+    ta.slot_pair = S.slot_pair;
+    ta.route_w = S.weights;
+    ta.out = S.act;
+    ta.K = H;
+    ta.rows = I;
+    ta.flavour = L.flavour;
+    ta.status = status;
     if (x_bf16) {
         auto kern = grouped_gemm_kernel<0, 0, 4, 3>;
         if ((err = set_smem(kern, GateUpBf16::total)) != cudaSuccess) return err;
         kern<<<sms, kGemmThreads, GateUpBf16::total, stream>>>(ga);
+        auto thin = thin_gemm_kernel<0, 0>;
+        if ((err = set_smem(thin, ThinLayout<0, 0>::total)) != cudaSuccess) return err;
+        thin<<<sms, kThinThreads, ThinLayout<0, 0>::total, stream>>>(ta);
     } else {
         auto kern = grouped_gemm_kernel<0, 1, 3, 2>;
         if ((err = set_smem(kern, GateUpF32::total)) != cudaSuccess) return err;
         kern<<<sms, kGemmThreads, GateUpF32::total, stream>>>(ga);
+        auto thin = thin_gemm_kernel<0, 1>;
+        if ((err = set_smem(thin, ThinLayout<0, 1>::total)) != cudaSuccess) return err;
+        thin<<<sms, kThinThreads, ThinLayout<0, 1>::total, stream>>>(ta);
     }
-    ++n;
+    n += 2;
     mark();
     // 6. pack activations
     PackArgs pa = px;
@@ -1035,8 +1412,18 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         auto kern = grouped_gemm_kernel<1, 1, 4, 2>;
         if ((err = set_smem(kern, DownLay::total)) != cudaSuccess) return err;
         kern<<<sms, kGemmThreads, DownLay::total, stream>>>(da);
+        ThinArgs tda = ta;
+        tda.tm0 = td;
+        tda.tm1 = td;
+        tda.b = S.b_down;
+        tda.out = S.pair_out;
+        tda.K = I;
+        tda.rows = H;
+        auto thin = thin_gemm_kernel<1, 1>;
+        if ((err = set_smem(thin, ThinLayout<1, 1>::total)) != cudaSuccess) return err;
+        thin<<<sms, kThinThreads, ThinLayout<1, 1>::total, stream>>>(tda);
     }
-    ++n;
+    n += 2;
     mark();
     // 8. combine
     {

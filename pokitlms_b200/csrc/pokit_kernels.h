@@ -135,7 +135,8 @@ struct MoeBatchScratch {
     uint32_t* ids = nullptr;     // [tokens][top_k] routes in rank order
     float* weights = nullptr;    // [tokens][top_k] combine weights
     uint32_t* rank = nullptr;    // [pairs] position of a (token, rank) pair within its expert
-    uint32_t* plan = nullptr;    // [4]: tiles, padded slots
+    uint32_t* plan = nullptr;    // [4]: tiles, padded slots, large tiles, skinny tiles
+    uint32_t* tile_order = nullptr;  // [max_tiles] large tiles, then skinny tiles (<= 8 tokens)
     uint32_t* tile_expert = nullptr, *tile_first = nullptr, *tile_n = nullptr, *tile_pad0 = nullptr;
     uint32_t* slot_pair = nullptr;   // [pairs] expert-sorted slot -> pair (token * top_k + rank)
     uint8_t* b_gate_up = nullptr;    // packed fp16 activations + scales per tile (gate/up operand)

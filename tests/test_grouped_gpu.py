@@ -103,6 +103,32 @@ def test_grouped_large_activations(cuda):
     be.close()
 
 
+@pytest.mark.parametrize("bf16", [False, True])
+def test_grouped_skinny_tile_boundary(cuda, bf16):
+    """Experts of 1, 7, 8, 9, 16, 64, 72 and 73 tokens: tiles on both sides of
+    the 8-token limit of the mma.sync path, and large experts whose last tile
+    is skinny (72 = 64 + 8) or not (73 = 64 + 9)."""
+    counts = [1, 7, 8, 9, 16, 64, 72, 73]
+    L = cases.moe_layer(hidden=512, inter=256, experts=8, top_k=1, seed=6)
+    be = make_backend(L)
+    tokens = sum(counts)
+    rng = np.random.default_rng(6)
+    owner = np.repeat(np.arange(8), counts)
+    rng.shuffle(owner)
+    logits = rng.standard_normal((tokens, 8)).astype(np.float32) * np.float32(0.1)
+    logits[np.arange(tokens), owner] += np.float32(4.0)
+    x = rng.standard_normal((tokens, 512), dtype=np.float32)
+    if bf16:
+        bits, x = synth.bf16_round(x)
+        out, ids, w = be.forward_batch_host(0, bits, bf16_bits=True, logits=logits)
+    else:
+        out, ids, w = be.forward_batch_host(0, x, logits=logits)
+    assert np.array_equal(ids[:, 0], owner)
+    ref_out, ref_ids, ref_p = O.moe_forward_batch(L, x, logits)
+    check_batch(L, out, ids, w, ref_out, ref_ids, ref_p, logits)
+    be.close()
+
+
 @pytest.fixture(scope="module")
 def config4(cuda):
     L = cases.moe_layer()   # hidden 2048, 128 experts top-8, inter 768, Q4_K

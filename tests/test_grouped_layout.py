@@ -136,3 +136,105 @@ def test_single_fp16_part_is_not_enough_for_f32():
         scale = float(np.sum(np.abs(w * xf)))
         worst = max(worst, abs(grouped_dot(blocks[b], xf, split=False) - ref) / scale)
     assert worst > 1e-5
+
+
+# ---------------------------------------------------------------------------
+# Skinny tiles (thin_gemm_kernel): mma.sync.m16n8k16 fragments.
+# ---------------------------------------------------------------------------
+
+def pair_scales(hdr_words, t):
+    """q4k_pair_scales: (scale, min) bytes of sub-blocks 2t, 2t + 1 without a
+    branch on t, from the header's scale words hy, hz, hw."""
+    hy, hz, hw = hdr_words
+    sh = 16 * (t & 1)
+    a, b, c = hy >> sh, hz >> sh, hw >> sh
+    sc_lo, mn_lo = a & 0x3F3F, b & 0x3F3F
+    sc_hi = (c & 0x0F0F) | ((a >> 2) & 0x3030)
+    mn_hi = ((c >> 4) & 0x0F0F) | ((b >> 2) & 0x3030)
+    sc, mn = (sc_hi, mn_hi) if t >= 2 else (sc_lo, mn_lo)
+    return (sc & 0xFF, (sc >> 8) & 0xFF), (mn & 0xFF, (mn >> 8) & 0xFF)
+
+
+def test_pair_scales_match_k_scale_min():
+    rng = np.random.default_rng(11)
+    for _ in range(500):
+        block = np.zeros(144, np.uint8)
+        block[4:16] = rng.integers(0, 256, 12, dtype=np.uint8)
+        sc, mn = scales_mins(block)
+        words = [int.from_bytes(bytes(block[4 + 4 * i:8 + 4 * i]), "little") for i in range(3)]
+        for t in range(4):
+            (s0, s1), (m0, m1) = pair_scales(words, t)
+            assert (s0, s1, m0, m1) == (sc[2 * t], sc[2 * t + 1], mn[2 * t], mn[2 * t + 1])
+
+
+def thin_token_region(chunks, n):
+    """pack_kernel's skinny placement of one token's 32 chunks (8 fp16 each):
+    lane quarter t's 128 bytes, chunk w at slot w ^ ((4n + t) & 7)."""
+    region = np.zeros((4, 8, 8), chunks.dtype)
+    for t in range(4):
+        for w in range(8):
+            region[t, w ^ ((4 * n + t) & 7)] = chunks[8 * t + w]
+    return region
+
+
+def thin_dot(block, x, split, n=3):
+    """One superblock row . x through the mma.sync fragments: thread (g, t)
+    supplies, for qs word w and nibble parity h, A = dequant_word output
+    2h + u (u = 0: logical k 2t, 2t+1; u = 1: k 2t+8, 2t+9) and B = the
+    chunk's fp16 pair 2h + u read back from the swizzled slot."""
+    d = float(np.frombuffer(bytes(block[0:2]), np.float16)[0])
+    dmin = float(np.frombuffer(bytes(block[2:4]), np.float16)[0])
+    _, mn = scales_mins(block)
+    amax = float(np.max(np.abs(x)))
+    ex = int(np.frexp(amax)[1]) if amax > 0 else 0
+    sig = max(-100, min(100, ex - 10))
+    xs = (x.astype(np.float64) * 2.0 ** -sig).astype(np.float32)
+    hi = xs.astype(np.float16)
+    lo = (xs - hi.astype(np.float32)).astype(np.float16)
+    cols = a_columns(block).astype(np.float64)          # dequant_word outputs, (128 columns, 2 halves)
+    main = 0.0
+    for part in ([hi, lo] if split else [hi]):
+        region = thin_token_region(b_chunks(part), n)
+        for t in range(4):
+            for w in range(8):
+                chunk = region[t, w ^ ((4 * n + t) & 7)].astype(np.float64)
+                for h in range(2):
+                    for u in range(2):
+                        for e in range(2):
+                            main += cols[32 * t + 4 * w + 2 * h + u, e] * chunk[4 * h + 2 * u + e]
+    sums = xs.reshape(8, 32).sum(axis=1, dtype=np.float32)
+    s_hi = sums.astype(np.float16).astype(np.float64)
+    s_lo = (sums - s_hi.astype(np.float32)).astype(np.float16).astype(np.float64)
+    # min MMA: a0 = a2 = (m_2t, m_2t+1), b0 = (hi_2t, hi_2t+1), b1 = (lo_2t, lo_2t+1)
+    mins = sum(mn[2 * t + e] * (s_hi[2 * t + e] + s_lo[2 * t + e]) for t in range(4) for e in range(2))
+    return (d * main - dmin * mins) * 2.0 ** sig
+
+
+def test_thin_fragments_cover_every_k_once():
+    seen = set()
+    for t in range(4):
+        for w in range(8):
+            for h in range(2):
+                for u in range(2):
+                    for e in range(2):
+                        j = 32 * t + 4 * w + 2 * h + u
+                        seen.add((j, e, 8 * (8 * t + w) + 4 * h + 2 * u + e))
+    # Each (column, half) meets chunk element 2 * (2j + half) ... exactly the tensor-core pairing.
+    assert len(seen) == 256
+    assert all(k == 2 * j + e for j, e, k in seen)
+
+
+def test_thin_layout_reproduces_q4k_dot():
+    blocks = synth.synth_blocks(cases.Q4_K, 12, seed=9, stream_id=4).reshape(12, 144)
+    rng = np.random.default_rng(3)
+    for b in range(12):
+        block = blocks[b]
+        w = O.dequantize_row(cases.Q4_K, block, 256).astype(np.float64)
+        _, xb = synth.bf16_round(rng.standard_normal(256, dtype=np.float32))
+        ref = float(np.dot(w, xb.astype(np.float64)))
+        scale = float(np.sum(np.abs(w * xb)))
+        assert abs(thin_dot(block, xb, split=False, n=b % 8) - ref) <= 1e-6 * scale
+        xf = rng.standard_normal(256).astype(np.float32) * np.float32(10.0 ** rng.uniform(-3, 4))
+        ref = float(np.dot(w, xf.astype(np.float64)))
+        scale = float(np.sum(np.abs(w * xf)))
+        assert abs(thin_dot(block, xf, split=True, n=b % 8) - ref) <= 1e-6 * scale
