@@ -987,10 +987,19 @@ __global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid
             for (uint32_t i = 0; i < kStages; ++i) last[i] = -1;
             uint32_t g = 0;
             bool ok = true;
+            // A unit's expert and activation region, read one unit ahead so the
+            // two dependent global loads overlap the previous unit's copies.
+            const auto fetch = [&](uint32_t u) -> uint2 {
+                if (u >= units) return make_uint2(0u, 0u);
+                const uint32_t tile = a.tile_order[first_thin + u / mblocks];
+                return make_uint2(a.tile_expert[tile], a.tile_pad0[tile]);
+            };
+            uint2 cur = fetch(blockIdx.x);
             for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
-                const uint32_t tile = a.tile_order[first_thin + u / mblocks], mb = u % mblocks;
-                const uint32_t e = a.tile_expert[tile];
-                const uint8_t* src = a.b + a.tile_pad0[tile] * tile_stride;
+                const uint2 nxt = fetch(u + gridDim.x);
+                const uint32_t mb = u % mblocks, e = cur.x;
+                const uint8_t* src = a.b + cur.y * tile_stride;
+                cur = nxt;
                 for (uint32_t s = 0; s < S; ++s, ++g) {
                     const uint32_t slot = g % kStages;
                     if (!(ok = wait(empty + slot, ((g / kStages) & 1) ^ 1))) break;
