@@ -351,15 +351,16 @@ def cfg3_layer_bytes(down_type: int) -> int:
     return CFG3["experts"] * Hc * 4 + CFG3["top_k"] * (2 * q4 + down) + shared + Hc * 4 + 2 * Hc * 4
 
 
-def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None) -> dict:
+def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None, layers: int | None = None) -> dict:
     """Configuration 3's MoE path: a 48-layer decode chain of Qwen3.5-MoE blocks (generic path),
-    weights synthesised in HBM from seed 0; tokens/s device-resident and end to end."""
+    weights synthesised in HBM from seed 0; tokens/s device-resident and end to end.  `layers`
+    shortens the chain (a small process for profiling its kernels)."""
     import torch
     from pokitlms_b200 import backend as B
     from pokitlms_b200 import synth
     from pokitlms_b200._lib import (DOWN, FFN_NORM, GATE, Q5_K, Q6_K, Q8_0, QWEN35, ROUTER, SHARED_DOWN,
                                     SHARED_GATE, SHARED_ROUTER, SHARED_UP, UP)
-    c = CFG3
+    c = dict(CFG3, layers=layers or CFG3["layers"])
     downs = [Q5_K if l % 2 == 0 else Q6_K for l in range(c["layers"])]
     be = B.CudaMoeBackend(layers=c["layers"], hidden=c["hidden"], inter=c["inter"], experts=c["experts"],
                           top_k=c["top_k"], flavour=QWEN35, expert_weights_scale=1.0, rms_epsilon=EPS,
@@ -403,7 +404,7 @@ def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None) 
     peaks = measured_peaks()
     gbs = tok_bytes / (ms * 1e-3) / 1e9
     res = {
-        "workload": ("benchmark configuration 3's MoE path: 48 Qwen3.5-MoE blocks (hidden 2048, 512 experts "
+        "workload": (f"benchmark configuration 3's MoE path: {c['layers']} Qwen3.5-MoE blocks (hidden 2048, 512 experts "
                      "top-10, inter 512, sigmoid-gated Q8_0 shared expert, Q4_K gate/up, Q5_K/Q6_K down "
                      "alternating), decode batch 1; DeltaNet / attention layers outside the path"),
         "value": 1e3 / ms, "unit": "tokens/s", "ms_per_token": ms, "gpu_launches_per_token": int(launches),
@@ -652,9 +653,10 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "grouped", "config5"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "grouped", "config3", "config5"],
                     help="grouped: only the configuration-4 measurement (one GPU; a small process for "
-                         "profiling the grouped kernels); config5: configuration 5 (94 layers, hidden "
+                         "profiling the grouped kernels); config3: only the configuration-3 chain (one "
+                         "GPU; --layers shortens it); config5: configuration 5 (94 layers, hidden "
                          "4096, batch 64) through the expert-parallel path on 1..N GPUs")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -692,6 +694,16 @@ def main() -> None:
         if rank == 0:
             print(json.dumps({"metric": "configuration-4 grouped-expert batch tokens/s", "n_gpus": 1,
                               **measure_grouped(local, torch.cuda.current_stream())}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    if args.workload == "config3":
+        if rank == 0:
+            short = args.layers if args.layers != LAYERS else None
+            print(json.dumps({"metric": "configuration-3 MoE chain tokens/s", "n_gpus": 1,
+                              **measure_config3(local, torch.cuda.current_stream(), max(args.steps, 5),
+                                                None if args.no_cpu_baseline else args.cpu_seconds,
+                                                layers=short)}))
         if world > 1:
             dist.destroy_process_group()
         return

@@ -360,7 +360,9 @@ size_t pokit_cuda_moe_tensor_bytes(const pokit_cuda_moe* moe, size_t layer, uint
 #define POKIT_CUDA_STATIC_SCRATCH_BYTES (256u * 1024u)
 
 /* One MoE block's tensors in device memory the caller owns (GGUF layouts as
- * for pokit_cuda_moe_upload_tensor; shared_* only for the Qwen3.5 flavour). */
+ * for pokit_cuda_moe_upload_tensor; shared_* only for the Qwen3.5 flavour).
+ * Expert tensors start on 16-byte boundaries and routers on 4-byte ones (as
+ * cudaMalloc returns them); others are rejected with INVALID_ARGUMENT. */
 typedef struct pokit_cuda_moe_block_device {
     size_t hidden, inter, experts, top_k;
     uint32_t flavour;                 /* pokit_cuda_moe_flavour */

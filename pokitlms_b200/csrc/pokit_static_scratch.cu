@@ -79,6 +79,12 @@ pokit::MoeLayerDev to_layer(const pokit_cuda_moe_block_device& b) {
         throw std::invalid_argument("router, gate, up and down tensors are required");
     if (!quant_type(b.gate_type) || !quant_type(b.up_type) || !quant_type(b.down_type))
         throw std::invalid_argument("unsupported expert tensor type");
+    // The kernels read the tensors with 16-byte (weights) and 4-byte (router) loads.
+    const auto a16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!a16(b.gate) || !a16(b.up) || !a16(b.down) || !a16(b.shared_gate) || !a16(b.shared_up) ||
+        !a16(b.shared_down) || (reinterpret_cast<uintptr_t>(b.router) & 3u) ||
+        (reinterpret_cast<uintptr_t>(b.shared_router) & 3u))
+        throw std::invalid_argument("expert tensors must be 16-byte aligned and routers 4-byte aligned");
     pokit::MoeLayerDev L;
     L.hidden = static_cast<uint32_t>(b.hidden);
     L.inter = static_cast<uint32_t>(b.inter);
