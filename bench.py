@@ -594,13 +594,12 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
         host_out.copy_(hidden, non_blocking=True)
         torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    stage_us = None
-    if cfg5:
-        # Device time of each kernel of one layer's batched block on this rank's shard
-        # (local to the rank: no collective), on the last step's normalised rows.
-        names = ["route", "group", "pack_x", "gate_up_gemm", "pack_act", "down_gemm", "combine"]
-        st = be.time_batch(0, x, part, logits=route_logits[0], reps=20)
-        stage_us = {"layer": 0, **{n_: round(v, 2) for n_, v in zip(names, st)}}
+    # Device time of each kernel of one layer's batched block on this rank's shard
+    # (local to the rank: no collective), on the last step's normalised rows.
+    names = (["route", "group", "pack_x", "gate_up_gemm", "pack_act", "down_gemm", "combine"] if cfg5 else
+             ["router", "route", "group", "pack_x", "gate_up_gemm", "pack_act", "down_gemm", "combine"])
+    st = be.time_batch(0, x, part, logits=route_logits[0] if cfg5 else None, reps=20)
+    stage_us = {"layer": 0, **{n_: round(v, 2) for n_, v in zip(names, st)}}
     barrier()
     graph_used = graph is not None
     graph = None                      # release the graph (it holds NCCL calls) before the group goes
