@@ -142,6 +142,49 @@ __global__ void __launch_bounds__(256) router_batch_kernel(const float* __restri
     }
 }
 
+// The router for a few tokens (T <= kRtSmall): one warp per (expert, hidden
+// slice) computes the slice's dot with every token; the warp's loads (its
+// router slice and the tokens' activations) all go out before any arithmetic,
+// so the kernel costs about one memory latency.  Lane l takes the float4s l
+// and l + 32 of the slice (slice 256) or l, l + 32, l + 64, l + 96 (512); the
+// lanes are summed by the same butterfly for every token, so a partial does
+// not depend on T, and the routing kernel adds the slices in order.
+constexpr uint32_t kRtSmall = 8;
+__global__ void __launch_bounds__(256) router_small_kernel(const float* __restrict__ router,
+                                                           const void* __restrict__ x, uint32_t x_bf16,
+                                                           uint32_t T, uint32_t E, uint32_t H, uint32_t slice,
+                                                           float* __restrict__ partial) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t e = blockIdx.x * 8 + warp, sl = blockIdx.y, h0 = sl * slice;
+    if (e >= E) return;
+    const uint32_t nq = slice / 128;   // float4s per lane: 2 or 4
+    float4 w[4], xv[kRtSmall][4];
+#pragma unroll
+    for (uint32_t q = 0; q < 4; ++q) {
+        if (q < nq) w[q] = *reinterpret_cast<const float4*>(router + static_cast<size_t>(e) * H + h0 + 4 * (lane + 32 * q));
+#pragma unroll
+        for (uint32_t t = 0; t < kRtSmall; ++t)
+            if (q < nq && t < T) xv[t][q] = load4(x, x_bf16, static_cast<size_t>(t) * H + h0 + 4 * (lane + 32 * q));
+    }
+#pragma unroll
+    for (uint32_t t = 0; t < kRtSmall; ++t) {
+        if (t >= T) break;
+        float a = 0.f;
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) {
+            if (q < nq) {
+                a = fmaf(w[q].x, xv[t][q].x, a);
+                a = fmaf(w[q].y, xv[t][q].y, a);
+                a = fmaf(w[q].z, xv[t][q].z, a);
+                a = fmaf(w[q].w, xv[t][q].w, a);
+            }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, d);
+        if (lane == 0) partial[(static_cast<size_t>(sl) * T + t) * E + e] = a;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // 3. Group: stable counting sort of pairs p = t * k + r by expert ids[p],
 // keeping the pairs whose expert this device holds ([e_first, e_first + E));
@@ -283,19 +326,24 @@ __host__ __device__ constexpr uint32_t packed_row_bytes(uint32_t kc8) { return (
 //   [0, 256)    sub-block sums, token n, lane quarter t: fp16 {hi(2t),
 //               hi(2t+1), lo(2t), lo(2t+1)} at (4n + t) * 8
 //   [256, 288)  the tokens' power-of-two scales (float)
-//   [288, ...)  token n at 288 + n * thin_token_bytes: its hi parts (512
-//               bytes), then its lo parts (split only).  Lane quarter t's
-//               128 bytes at t * 128 hold eight 16-byte chunks; chunk w (the
-//               qs word w of Q4_K chunk t) sits at slot w ^ ((4n + t) & 7) and
-//               holds the fp16 x of K positions 64t + 4w + {0, 2, 1, 3} and
-//               64t + 32 + 4w + {0, 2, 1, 3}: the B registers of k-steps 2w
-//               (low nibbles) and 2w + 1 (high nibbles).
+//   [288, ...)  the hi parts, token n at 288 + n * 576 (kThinTokPitch),
+//               then (split only) the lo parts at + kThinPart in the same
+//               layout.  Lane quarter t's eight 16-byte chunks start at t *
+//               144 (kThinSegPitch: 128 bytes and 16 of padding); chunk w
+//               (the qs word w of Q4_K chunk t) holds the fp16 x of K
+//               positions 64t + 4w + {0, 2, 1, 3} and 64t + 32 + 4w +
+//               {0, 2, 1, 3}: the B registers of k-steps 2w (low nibbles) and
+//               2w + 1 (high nibbles).  With segments 144 bytes and tokens
+//               576 bytes (64 mod 128) apart, the eight (token, lane
+//               quarter) reads of a quarter warp land on eight distinct
+//               16-byte bank groups at constant offsets.
 // The tile's region is the one the tensor-core layout would use (16 padded
-// slots hold more than 288 + 8 * 1024 bytes per superblock).
+// slots hold more than a superblock's 288 + 2 * 8 * 576 bytes).
 constexpr uint32_t kThinTail = 288;
-__host__ __device__ constexpr uint32_t thin_token_bytes(uint32_t split) { return split ? 1024u : 512u; }
+constexpr uint32_t kThinSegPitch = 144, kThinTokPitch = 4 * kThinSegPitch;
+constexpr uint32_t kThinPart = kSkinny * kThinTokPitch;
 __host__ __device__ constexpr uint32_t thin_stage_bytes(uint32_t split) {
-    return kThinTail + kSkinny * thin_token_bytes(split);
+    return kThinTail + (split ? 2u : 1u) * kThinPart;
 }
 static_assert(thin_stage_bytes(1) <= 16 * packed_row_bytes(64) && thin_stage_bytes(0) <= 16 * packed_row_bytes(32),
               "skinny packing fits a 16-slot tile");
@@ -392,9 +440,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
                     hi[i] = __half2float(__float2half_rn(e[i]));
                     lo[i] = e[i] - hi[i];
                 }
-                uint8_t* tok = region + kThinTail + n * thin_token_bytes(a.split) + t * 128 + ((w ^ ((4 * n + t) & 7)) << 4);
+                uint8_t* tok = region + kThinTail + n * kThinTokPitch + t * kThinSegPitch + (w << 4);
                 *reinterpret_cast<uint4*>(tok) = pack8_half(hi);
-                if (a.split) *reinterpret_cast<uint4*>(tok + 512) = pack8_half(lo);
+                if (a.split) *reinterpret_cast<uint4*>(tok + kThinPart) = pack8_half(lo);
                 if ((lane & 3) == 0) {
                     const uint32_t j = lane >> 2;
                     const __half h = __float2half_rn(part);
@@ -942,7 +990,6 @@ template <int kMode, int kSplit>
 __global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid_constant__ ThinArgs a) {
     using Lay = ThinLayout<kMode, kSplit>;
     constexpr uint32_t kMats = Lay::mats, kStages = Lay::stages;
-    constexpr uint32_t kTok = thin_token_bytes(kSplit);
     extern __shared__ __align__(1024) uint8_t smem[];
     float* xch = reinterpret_cast<float*>(smem + Lay::xch_off);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::bar_off);
@@ -1025,7 +1072,6 @@ __global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid
     const uint32_t grp = warp / kThinRowWarps, rw = warp % kThinRowWarps;
     const uint32_t g8 = lane >> 2, t = lane & 3;
     const uint32_t r0 = 16 * rw + g8;
-    const uint32_t swz = (4 * g8 + t) & 7;
     uint32_t g = 0, ui = 0;
     bool ok = true;
     for (uint32_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ui) {
@@ -1041,7 +1087,7 @@ __global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid
             if (!(ok = wait_warp(full + slot, (g / kStages) & 1))) break;
             const uint8_t* st = smem + slot * Lay::stage;
             const uint8_t* xs = st + Lay::wbytes;
-            const uint8_t* xt = xs + kThinTail + g8 * kTok + t * 128;
+            const uint8_t* xt = xs + kThinTail + g8 * kThinTokPitch + t * kThinSegPitch;
             const uint2 bm = *reinterpret_cast<const uint2*>(xs + (4 * g8 + t) * 8);   // token g8's sums
             const float2 sc = *reinterpret_cast<const float2*>(xs + 256 + 8 * t);     // tokens 2t, 2t + 1
             // One matrix at a time (not unrolled): the registers of one set of rows.
@@ -1065,14 +1111,14 @@ __global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid
                 float acc[2][4] = {};
 #pragma unroll
                 for (uint32_t w = 0; w < 8; ++w) {
-                    const uint4 xh = *reinterpret_cast<const uint4*>(xt + ((w ^ swz) << 4));
+                    const uint4 xh = *reinterpret_cast<const uint4*>(xt + (w << 4));
                     uint32_t ra[4], rb[4];   // rows g8 and g8 + 8
                     dequant_word(wa[w], na, ra);
                     dequant_word(wb[w], nb, rb);
                     mma16816(acc[0], ra[0], rb[0], ra[1], rb[1], xh.x, xh.y);
                     mma16816(acc[1], ra[2], rb[2], ra[3], rb[3], xh.z, xh.w);
                     if (kSplit) {
-                        const uint4 xl = *reinterpret_cast<const uint4*>(xt + 512 + ((w ^ swz) << 4));
+                        const uint4 xl = *reinterpret_cast<const uint4*>(xt + kThinPart + (w << 4));
                         mma16816(acc[0], ra[0], rb[0], ra[1], rb[1], xl.x, xl.y);
                         mma16816(acc[1], ra[2], rb[2], ra[3], rb[3], xl.z, xl.w);
                     }
@@ -1304,8 +1350,13 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     uint32_t splits = 1;
     if (!lg) {
         const uint32_t slice = router_slice(H);
-        const dim3 rgrid((tokens + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, H / slice);
-        router_batch_kernel<<<rgrid, 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H, slice, S.logits);
+        if (tokens <= kRtSmall) {
+            router_small_kernel<<<dim3((E + 7) / 8, H / slice), 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H,
+                                                                                  slice, S.logits);
+        } else {
+            const dim3 rgrid((tokens + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, H / slice);
+            router_batch_kernel<<<rgrid, 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H, slice, S.logits);
+        }
         splits = H / slice;
         ++n;
         mark();
@@ -1381,22 +1432,26 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     ta.rows = I;
     ta.flavour = L.flavour;
     ta.status = status;
+    // A token's routes are distinct experts, so an expert holds at most `tokens`
+    // pairs: with tokens <= kSkinny every tile is skinny and the tensor-core
+    // GEMMs would find no unit.
+    const bool any_large = tokens > kSkinny;
     if (x_bf16) {
         auto kern = grouped_gemm_kernel<0, 0, 4, 3>;
         if ((err = set_smem(kern, GateUpBf16::total)) != cudaSuccess) return err;
-        kern<<<sms, kGemmThreads, GateUpBf16::total, stream>>>(ga);
+        if (any_large) kern<<<sms, kGemmThreads, GateUpBf16::total, stream>>>(ga);
         auto thin = thin_gemm_kernel<0, 0>;
         if ((err = set_smem(thin, ThinLayout<0, 0>::total)) != cudaSuccess) return err;
         thin<<<sms, kThinThreads, ThinLayout<0, 0>::total, stream>>>(ta);
     } else {
         auto kern = grouped_gemm_kernel<0, 1, 3, 2>;
         if ((err = set_smem(kern, GateUpF32::total)) != cudaSuccess) return err;
-        kern<<<sms, kGemmThreads, GateUpF32::total, stream>>>(ga);
+        if (any_large) kern<<<sms, kGemmThreads, GateUpF32::total, stream>>>(ga);
         auto thin = thin_gemm_kernel<0, 1>;
         if ((err = set_smem(thin, ThinLayout<0, 1>::total)) != cudaSuccess) return err;
         thin<<<sms, kThinThreads, ThinLayout<0, 1>::total, stream>>>(ta);
     }
-    n += 2;
+    n += any_large ? 2u : 1u;
     mark();
     // 6. pack activations
     PackArgs pa = px;
@@ -1420,7 +1475,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     {
         auto kern = grouped_gemm_kernel<1, 1, 4, 2>;
         if ((err = set_smem(kern, DownLay::total)) != cudaSuccess) return err;
-        kern<<<sms, kGemmThreads, DownLay::total, stream>>>(da);
+        if (any_large) kern<<<sms, kGemmThreads, DownLay::total, stream>>>(da);
         ThinArgs tda = ta;
         tda.tm0 = td;
         tda.tm1 = td;
@@ -1432,7 +1487,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         if ((err = set_smem(thin, ThinLayout<1, 1>::total)) != cudaSuccess) return err;
         thin<<<sms, kThinThreads, ThinLayout<1, 1>::total, stream>>>(tda);
     }
-    n += 2;
+    n += any_large ? 2u : 1u;
     mark();
     // 8. combine
     {

@@ -167,13 +167,39 @@ def test_pair_scales_match_k_scale_min():
             assert (s0, s1, m0, m1) == (sc[2 * t], sc[2 * t + 1], mn[2 * t], mn[2 * t + 1])
 
 
+THIN_TAIL, THIN_SEG, THIN_TOK = 288, 144, 576
+
+
+def thin_chunk_offset(n, t, w):
+    """pack_kernel's skinny placement: byte offset of token n's chunk w of lane
+    quarter t within a superblock's hi (or lo) part."""
+    return THIN_TAIL + n * THIN_TOK + t * THIN_SEG + 16 * w
+
+
+def test_thin_reads_are_conflict_free_and_disjoint():
+    """A quarter warp (tokens g = 0, 1 x lane quarters t = 0..3) reads chunk w
+    of its (g, t) segment: eight distinct 16-byte bank groups; and no two
+    chunks of the 8 x 4 x 8 overlap or spill past the part."""
+    for w in range(8):
+        for g0 in range(0, 8, 2):
+            groups = {(thin_chunk_offset(g, t, w) // 16) % 8 for g in (g0, g0 + 1) for t in range(4)}
+            assert len(groups) == 8
+    offs = sorted(thin_chunk_offset(n, t, w) for n in range(8) for t in range(4) for w in range(8))
+    assert all(b - a >= 16 for a, b in zip(offs, offs[1:]))
+    assert offs[-1] + 16 <= THIN_TAIL + 8 * THIN_TOK
+
+
 def thin_token_region(chunks, n):
-    """pack_kernel's skinny placement of one token's 32 chunks (8 fp16 each):
-    lane quarter t's 128 bytes, chunk w at slot w ^ ((4n + t) & 7)."""
+    """One token's 32 chunks (8 fp16 each) placed as pack_kernel writes them,
+    read back at the consumer's offsets."""
+    mem = {}
+    for t in range(4):
+        for w in range(8):
+            mem[thin_chunk_offset(n, t, w)] = chunks[8 * t + w]
     region = np.zeros((4, 8, 8), chunks.dtype)
     for t in range(4):
         for w in range(8):
-            region[t, w ^ ((4 * n + t) & 7)] = chunks[8 * t + w]
+            region[t, w] = mem[THIN_TAIL + n * THIN_TOK + t * THIN_SEG + (w << 4)]
     return region
 
 
@@ -181,7 +207,7 @@ def thin_dot(block, x, split, n=3):
     """One superblock row . x through the mma.sync fragments: thread (g, t)
     supplies, for qs word w and nibble parity h, A = dequant_word output
     2h + u (u = 0: logical k 2t, 2t+1; u = 1: k 2t+8, 2t+9) and B = the
-    chunk's fp16 pair 2h + u read back from the swizzled slot."""
+    chunk's fp16 pair 2h + u read back from its packed place."""
     d = float(np.frombuffer(bytes(block[0:2]), np.float16)[0])
     dmin = float(np.frombuffer(bytes(block[2:4]), np.float16)[0])
     _, mn = scales_mins(block)
@@ -197,7 +223,7 @@ def thin_dot(block, x, split, n=3):
         region = thin_token_region(b_chunks(part), n)
         for t in range(4):
             for w in range(8):
-                chunk = region[t, w ^ ((4 * n + t) & 7)].astype(np.float64)
+                chunk = region[t, w].astype(np.float64)
                 for h in range(2):
                     for u in range(2):
                         for e in range(2):
