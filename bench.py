@@ -517,9 +517,10 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     def body():
         hidden.copy_(static_in)
         for l in range(layers):
-            # rms_norm with ffn_norm = 1 (src/rms_norm.cpp:9-27), then the block.
-            torch.mul(hidden, torch.rsqrt(hidden.pow(2).mean(dim=1, keepdim=True) + EPS), out=x)
-            ep.forward_batch(l, x, part, logits=None if route_logits is None else route_logits[l])
+            # rms_norm with ffn_norm = 1 (src/rms_norm.cpp:9-27; torch's fused
+            # kernel), then the block.
+            xn = torch.nn.functional.rms_norm(hidden, (Hs,), eps=EPS)
+            ep.forward_batch(l, xn, part, logits=None if route_logits is None else route_logits[l])
             hidden.add_(part)
 
     # Eager warm-up (sizes the batch scratch, sets kernel attributes), then the
@@ -596,6 +597,7 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     # Device time of each kernel of one layer's batched block on this rank's shard
     # (local to the rank: no collective), on the last step's normalised rows.
+    x.copy_(torch.nn.functional.rms_norm(hidden, (Hs,), eps=EPS))
     names = (["route", "group", "pack_x", "gate_up_gemm", "pack_act", "down_gemm", "combine"] if cfg5 else
              ["router", "route", "group", "pack_x", "gate_up_gemm", "pack_act", "down_gemm", "combine"])
     st = be.time_batch(0, x, part, logits=route_logits[0] if cfg5 else None, reps=20)
