@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(256) router_batch_kernel(const float* __restri
                                                            float* __restrict__ partial) {
     __shared__ float xs[kRtTok][kRtChunk + 1];
     __shared__ float ws[kRtExp][kRtChunk + 1];
+    grid_dep_wait();      // x from the previous kernel (programmatic launch; no-op otherwise)
+    grid_dep_launch();
     const uint32_t t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, h0 = blockIdx.z * slice;
     const uint32_t ti = threadIdx.x >> 2, ej = threadIdx.x & 3;
     float a0 = 0.f, a1 = 0.f;
@@ -154,6 +156,8 @@ __global__ void __launch_bounds__(256) router_small_kernel(const float* __restri
                                                            const void* __restrict__ x, uint32_t x_bf16,
                                                            uint32_t T, uint32_t E, uint32_t H, uint32_t slice,
                                                            float* __restrict__ partial) {
+    grid_dep_wait();
+    grid_dep_launch();
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t e = blockIdx.x * 8 + warp, sl = blockIdx.y, h0 = sl * slice;
     if (e >= E) return;
@@ -213,6 +217,8 @@ __global__ void __launch_bounds__(kSortThreads, 1) group_kernel(const uint32_t* 
     uint32_t* off_pad = off_tile + E;           // [E]
     uint32_t* off_thin = off_pad + E;           // [E] skinny tiles before expert e
     uint32_t* n_large = off_thin + E;           // [1]
+    grid_dep_wait();
+    grid_dep_launch();
     const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     for (uint32_t e = tid; e < E; e += kSortThreads) total[e] = 0;
     __syncthreads();
@@ -379,6 +385,8 @@ __device__ __forceinline__ void pack_load(const PackArgs& a, size_t at, float (&
 // the row's superblocks are loaded four at a time before any is packed.
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(PackArgs a) {
     __shared__ float stage[kPackThreads / 32][8 * 33];
+    grid_dep_wait();
+    grid_dep_launch();
     const uint32_t tile = blockIdx.x;
     if (tile >= a.plan[0]) return;
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -623,6 +631,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const __g
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = misc[0];
+    // The tile list and packed activations come from the previous kernels
+    // (programmatic launch: the set-up above overlapped their tail).
+    grid_dep_wait();
+    grid_dep_launch();
 
     const uint32_t S = a.K / 256;
     constexpr uint32_t kRowsPerUnit = kMode == 0 ? 64u : 128u;
@@ -1009,6 +1021,8 @@ __global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid
         mbar_fence_init();
     }
     __syncthreads();
+    grid_dep_wait();      // tile list and packed activations of the previous kernels
+    grid_dep_launch();
 
     const uint32_t S = a.K / 256;
     const uint32_t mblocks = a.rows / 128;
@@ -1195,6 +1209,8 @@ __global__ void __launch_bounds__(kThinThreads, 1) thin_gemm_kernel(const __grid
 __global__ void combine_kernel(const float* __restrict__ pair_out, const uint32_t* __restrict__ ids,
                                uint32_t e_first, uint32_t e_count, uint32_t tokens, uint32_t k, uint32_t H,
                                float* __restrict__ out) {
+    grid_dep_wait();
+    grid_dep_launch();
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;   // float4 index
     const size_t per_token = H / 4;
     if (i >= static_cast<size_t>(tokens) * per_token) return;
@@ -1272,6 +1288,26 @@ cudaError_t set_smem(Kern k, uint32_t bytes) {
     return e;
 }
 
+// Launches kernel k, as a programmatic dependent of the previous kernel in the
+// stream when pdl (every kernel of the batched block waits for its
+// predecessor with griddepcontrol.wait before reading what it wrote, and lets
+// its own dependent start launching right after).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                     Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 }  // namespace
 
 bool moe_batch_grouped(const MoeLayerDev& L) {
@@ -1323,6 +1359,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
                              uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
                              uint32_t* status, cudaStream_t stream, uint32_t* launches, cudaEvent_t* marks) {
     uint32_t n = 0, stage = 0;   // kernels launched; stage boundaries marked
+    const bool pdl = marks == nullptr;   // per-stage events need the kernels serialised
     const auto mark = [&]() {
         if (marks) cudaEventRecord(marks[stage++], stream);
     };
@@ -1351,11 +1388,14 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     if (!lg) {
         const uint32_t slice = router_slice(H);
         if (tokens <= kRtSmall) {
-            router_small_kernel<<<dim3((E + 7) / 8, H / slice), 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H,
-                                                                                  slice, S.logits);
+            if ((err = launch_k(router_small_kernel, dim3((E + 7) / 8, H / slice), dim3(256), 0, stream, pdl,
+                                L.router, x, x_bf16, tokens, E, H, slice, S.logits)) != cudaSuccess)
+                return err;
         } else {
             const dim3 rgrid((tokens + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, H / slice);
-            router_batch_kernel<<<rgrid, 256, 0, stream>>>(L.router, x, x_bf16, tokens, E, H, slice, S.logits);
+            if ((err = launch_k(router_batch_kernel, rgrid, dim3(256), 0, stream, pdl, L.router, x, x_bf16, tokens, E,
+                                H, slice, S.logits)) != cudaSuccess)
+                return err;
         }
         splits = H / slice;
         ++n;
@@ -1364,7 +1404,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     }
     // 2. routes
     if ((err = launch_route_experts(lg, E, k, L.flavour, L.normalize, L.expert_weights_scale, S.ids, S.weights,
-                                    status, stream, tokens, splits)) != cudaSuccess)
+                                    status, stream, tokens, splits, pdl)) != cudaSuccess)
         return err;
     ++n;
     mark();
@@ -1373,7 +1413,9 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         GroupOut o{S.plan, S.tile_order, S.tile_expert, S.tile_first, S.tile_n, S.tile_pad0, S.slot_pair, S.rank};
         const uint32_t smem = (kSortWarps + 5) * EL * 4 + 16;
         if ((err = set_smem(group_kernel, smem)) != cudaSuccess) return err;
-        group_kernel<<<1, kSortThreads, smem, stream>>>(S.ids, pairs, E0, EL, o);
+        if ((err = launch_k(group_kernel, dim3(1), dim3(kSortThreads), smem, stream, pdl, S.ids, pairs, E0, EL, o)) !=
+            cudaSuccess)
+            return err;
         ++n;
         mark();
     }
@@ -1394,7 +1436,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     px.dst = S.b_gate_up;
     const uint32_t max_tiles = max_tiles_for(pairs, EL);
     const dim3 pack_grid(max_tiles, kTileTokens / (kPackThreads / 32));
-    pack_kernel<<<pack_grid, kPackThreads, 0, stream>>>(px);
+    if ((err = launch_k(pack_kernel, pack_grid, dim3(kPackThreads), 0, stream, pdl, px)) != cudaSuccess) return err;
     ++n;
     mark();
     // 5. gate/up
@@ -1439,17 +1481,25 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     if (x_bf16) {
         auto kern = grouped_gemm_kernel<0, 0, 4, 3>;
         if ((err = set_smem(kern, GateUpBf16::total)) != cudaSuccess) return err;
-        if (any_large) kern<<<sms, kGemmThreads, GateUpBf16::total, stream>>>(ga);
+        if (any_large &&
+            (err = launch_k(kern, dim3(sms), dim3(kGemmThreads), GateUpBf16::total, stream, pdl, ga)) != cudaSuccess)
+            return err;
         auto thin = thin_gemm_kernel<0, 0>;
         if ((err = set_smem(thin, ThinLayout<0, 0>::total)) != cudaSuccess) return err;
-        thin<<<sms, kThinThreads, ThinLayout<0, 0>::total, stream>>>(ta);
+        if ((err = launch_k(thin, dim3(sms), dim3(kThinThreads), ThinLayout<0, 0>::total, stream, pdl, ta)) !=
+            cudaSuccess)
+            return err;
     } else {
         auto kern = grouped_gemm_kernel<0, 1, 3, 2>;
         if ((err = set_smem(kern, GateUpF32::total)) != cudaSuccess) return err;
-        if (any_large) kern<<<sms, kGemmThreads, GateUpF32::total, stream>>>(ga);
+        if (any_large &&
+            (err = launch_k(kern, dim3(sms), dim3(kGemmThreads), GateUpF32::total, stream, pdl, ga)) != cudaSuccess)
+            return err;
         auto thin = thin_gemm_kernel<0, 1>;
         if ((err = set_smem(thin, ThinLayout<0, 1>::total)) != cudaSuccess) return err;
-        thin<<<sms, kThinThreads, ThinLayout<0, 1>::total, stream>>>(ta);
+        if ((err = launch_k(thin, dim3(sms), dim3(kThinThreads), ThinLayout<0, 1>::total, stream, pdl, ta)) !=
+            cudaSuccess)
+            return err;
     }
     n += any_large ? 2u : 1u;
     mark();
@@ -1461,7 +1511,7 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     pa.cols = I;
     pa.split = 1;
     pa.dst = S.b_down;
-    pack_kernel<<<pack_grid, kPackThreads, 0, stream>>>(pa);
+    if ((err = launch_k(pack_kernel, pack_grid, dim3(kPackThreads), 0, stream, pdl, pa)) != cudaSuccess) return err;
     ++n;
     mark();
     // 7. down
@@ -1475,7 +1525,9 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     {
         auto kern = grouped_gemm_kernel<1, 1, 4, 2>;
         if ((err = set_smem(kern, DownLay::total)) != cudaSuccess) return err;
-        if (any_large) kern<<<sms, kGemmThreads, DownLay::total, stream>>>(da);
+        if (any_large &&
+            (err = launch_k(kern, dim3(sms), dim3(kGemmThreads), DownLay::total, stream, pdl, da)) != cudaSuccess)
+            return err;
         ThinArgs tda = ta;
         tda.tm0 = td;
         tda.tm1 = td;
@@ -1485,15 +1537,19 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
         tda.rows = H;
         auto thin = thin_gemm_kernel<1, 1>;
         if ((err = set_smem(thin, ThinLayout<1, 1>::total)) != cudaSuccess) return err;
-        thin<<<sms, kThinThreads, ThinLayout<1, 1>::total, stream>>>(tda);
+        if ((err = launch_k(thin, dim3(sms), dim3(kThinThreads), ThinLayout<1, 1>::total, stream, pdl, tda)) !=
+            cudaSuccess)
+            return err;
     }
     n += any_large ? 2u : 1u;
     mark();
     // 8. combine
     {
         const size_t quads = static_cast<size_t>(tokens) * H / 4;
-        combine_kernel<<<static_cast<uint32_t>((quads + 255) / 256), 256, 0, stream>>>(S.pair_out, S.ids, E0, EL,
-                                                                                       tokens, k, H, out);
+        if ((err = launch_k(combine_kernel, dim3(static_cast<uint32_t>((quads + 255) / 256)), dim3(256), 0, stream,
+                            pdl, static_cast<const float*>(S.pair_out), static_cast<const uint32_t*>(S.ids), E0, EL,
+                            tokens, k, H, out)) != cudaSuccess)
+            return err;
         ++n;
         mark();
     }

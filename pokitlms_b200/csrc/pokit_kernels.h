@@ -22,9 +22,12 @@ cudaError_t launch_dequantize(uint32_t type, const void* w, uint32_t rows, uint3
 // Softmax top-k routing of `rows` device logits vectors of E entries (one CTA
 // per row): ids/weights receive k entries per row.  With splits > 1 a row is
 // the sum of `splits` partial rows (partial s of row r at (s * rows + r) * E).
+// pdl: launched as a programmatic dependent of the previous kernel in the
+// stream (the kernel waits for it before reading the logits).
 cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, uint32_t flavour,
                                  uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
-                                 uint32_t* status, cudaStream_t stream, uint32_t rows = 1, uint32_t splits = 1);
+                                 uint32_t* status, cudaStream_t stream, uint32_t rows = 1, uint32_t splits = 1,
+                                 bool pdl = false);
 
 // TMA tensor map over a Q4_K expert tensor: (byte column, row, expert), boxes
 // of one superblock (144 bytes) by box_rows rows; cached per argument set.

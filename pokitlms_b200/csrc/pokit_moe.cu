@@ -1015,6 +1015,8 @@ route_logits_kernel(const float* __restrict__ logits, uint32_t E, uint32_t k, ui
     __shared__ double red[64];
     __shared__ uint32_t sel_id[kMaxTopK + 1];
     __shared__ float sel_w[kMaxTopK + 1];
+    grid_dep_wait();      // logits of the previous kernel (programmatic launch; no-op otherwise)
+    grid_dep_launch();
     Shared s{};
     s.red = red;
     s.sel_id = sel_id;
@@ -1728,12 +1730,21 @@ MoeScratch moe_scratch_carve(const MoeLayerDev& L, void* base, uint32_t rep) {
 
 cudaError_t launch_route_experts(const float* logits, uint32_t E, uint32_t k, uint32_t flavour,
                                  uint32_t normalize, float ew_scale, uint32_t* ids, float* weights,
-                                 uint32_t* status, cudaStream_t stream, uint32_t rows, uint32_t splits) {
+                                 uint32_t* status, cudaStream_t stream, uint32_t rows, uint32_t splits,
+                                 bool pdl) {
     if (k == 0 || k > E || k > kMaxTopK || E > kMaxExperts || rows == 0 || splits == 0)
         return cudaErrorInvalidValue;
-    route_logits_kernel<<<rows, kThreads, 0, stream>>>(logits, E, k, flavour, normalize, ew_scale,
-                                                       ids, weights, status, splits);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, route_logits_kernel, logits, E, k, flavour, normalize, ew_scale, ids, weights,
+                              status, splits);
 }
 
 // ---------------------------------------------------------------------------
