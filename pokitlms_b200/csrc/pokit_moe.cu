@@ -966,6 +966,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_route_kernel(BlockArgs a) {
     const uint32_t gw = blockIdx.x * kWarps + (threadIdx.x >> 5), nw = gridDim.x * kWarps;
     RouterRegs rr;
     router_issue(a.L, gw, nw, rr);
+    // The router weights' loads above may overlap the previous kernel (a
+    // programmatic dependent launch); the hidden state is read after it ends.
+    grid_dep_wait();
+    grid_dep_launch();
     phase_input(a.L, a.hidden, a.x_in, s);
     if (blockIdx.x == 0)
         for (uint32_t i = threadIdx.x; i < a.L.hidden; i += kThreads) a.S.x[i] = s.xs[i];
@@ -981,6 +985,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_route_kernel(BlockArgs a) {
 __global__ void __launch_bounds__(kThreads, 1) moe_gate_up_kernel(BlockArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     Shared s = carve(smem, a.m);
+    grid_dep_wait();      // routes and input of the route kernel
+    grid_dep_launch();
     for (uint32_t r = threadIdx.x; r <= a.L.top_k; r += kThreads) {
         if (r < a.L.top_k) s.sel_id[r] = __ldcg(a.S.ids + r);
         s.sel_w[r] = __ldcg(a.S.weights + r);
@@ -1001,8 +1007,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(BlockArgs a) {
     __syncthreads();
     bool ok = true;
     const uint64_t nrb = static_cast<uint64_t>(a.L.experts) * a.L.hidden * 4u;
+    // The routes were published two kernels back; the first task's weight loads
+    // go out before the wait for the gate/up kernel's act.
     phase_down(a.L, s, a.S.act, max_inter_of(a.L), blockIdx.x, gridDim.x, a.hidden, a.moe_out,
-               a.next_router, nrb, [] { return true; }, ok);
+               a.next_router, nrb, [] { grid_dep_wait(); grid_dep_launch(); return true; }, ok);
 }
 
 // Routing of standalone logits vectors (pokit_cuda_route_experts; the
@@ -1914,12 +1922,28 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
     if (e != cudaSuccess || dry_run) return e;
     BlockArgs ra = a;
     ra.m = rl;
+    // Each kernel is a programmatic dependent of the one before (it waits in-
+    // kernel before reading its predecessor's output); plain launches when
+    // per-kernel events are recorded.
+    const auto launch = [&](void (*k)(BlockArgs), uint32_t grid, uint32_t smem, const BlockArgs& args) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = marks ? 0 : 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, k, args);
+    };
     mark(0);
-    moe_route_kernel<<<g1, kThreads, rl.total, stream>>>(ra);
+    if ((e = launch(moe_route_kernel, g1, rl.total, ra)) != cudaSuccess) return e;
     mark(1);
-    moe_gate_up_kernel<<<sms, kThreads, a.m.total, stream>>>(a);
+    if ((e = launch(moe_gate_up_kernel, sms, a.m.total, a)) != cudaSuccess) return e;
     mark(2);
-    moe_down_kernel<<<down_ctas, kThreads, a.m.total, stream>>>(a);
+    if ((e = launch(moe_down_kernel, down_ctas, a.m.total, a)) != cudaSuccess) return e;
     mark(3);
     if (launches) *launches = 3;
     return cudaGetLastError();
