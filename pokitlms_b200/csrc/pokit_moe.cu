@@ -666,7 +666,7 @@ __device__ __forceinline__ SlotMats slot_mats(const MoeLayerDev& L, const uint32
 __device__ float generic_row_dot(uint32_t type, const uint8_t* row_g, uint32_t cols,
                                  const float* xs, uint8_t* stage, int lane) {
     const uint32_t rb = static_cast<uint32_t>(row_bytes(type, cols));
-    warp_stage_row(row_g, rb, stage, lane);
+    warp_stage_row<2>(row_g, rb, stage, lane);  // a small batch: the kernel is at its register limit
     __syncwarp();
     float acc = warp_sum(lane_row_dot_any(type, stage, cols, xs, lane));
     __syncwarp();

@@ -221,13 +221,14 @@ __device__ __forceinline__ float group_dot(const uint8_t* __restrict__ row, int 
 // Warp-cooperative copy of `bytes` of a weight row from global to shared
 // memory.  Uses 16-byte loads when source and size allow it, else 4- or
 // 2-byte loads (GGUF rows of Q6_K/Q8_0 are only 2-byte aligned in general).
+// kBatch 16-byte loads per lane (4 x kBatch for 4-byte rows) go out before
+// their stores: one memory latency per batch (a 2-4 KB row is one batch at
+// the default); callers short of registers take smaller batches.
+template <uint32_t kBatch = 8>
 __device__ __forceinline__ void warp_stage_row(const uint8_t* __restrict__ src, uint32_t bytes,
                                                uint8_t* __restrict__ dst, int lane) {
-    // Batches of loads per lane in flight before their stores: one memory
-    // latency per batch (a 2-4 KB row is one batch).
     const uint64_t a = reinterpret_cast<uint64_t>(src);
     if ((a & 15u) == 0 && (bytes & 15u) == 0) {
-        constexpr uint32_t kBatch = 8;
         for (uint32_t o0 = lane * 16u; o0 < bytes; o0 += 32u * 16u * kBatch) {
             uint4 v[kBatch];
 #pragma unroll
@@ -238,14 +239,14 @@ __device__ __forceinline__ void warp_stage_row(const uint8_t* __restrict__ src, 
                 if (o0 + j * 512u < bytes) *reinterpret_cast<uint4*>(dst + o0 + j * 512u) = v[j];
         }
     } else if ((a & 3u) == 0 && (bytes & 3u) == 0) {
-        constexpr uint32_t kBatch = 16;
-        for (uint32_t o0 = lane * 4u; o0 < bytes; o0 += 32u * 4u * kBatch) {
-            uint32_t v[kBatch];
+        constexpr uint32_t kB4 = 2 * kBatch;
+        for (uint32_t o0 = lane * 4u; o0 < bytes; o0 += 32u * 4u * kB4) {
+            uint32_t v[kB4];
 #pragma unroll
-            for (uint32_t j = 0; j < kBatch; ++j)
+            for (uint32_t j = 0; j < kB4; ++j)
                 if (o0 + j * 128u < bytes) v[j] = ldg_stream32(src + o0 + j * 128u);
 #pragma unroll
-            for (uint32_t j = 0; j < kBatch; ++j)
+            for (uint32_t j = 0; j < kB4; ++j)
                 if (o0 + j * 128u < bytes) *reinterpret_cast<uint32_t*>(dst + o0 + j * 128u) = v[j];
         }
     } else {
