@@ -483,13 +483,13 @@ __device__ __forceinline__ float lane_row_dot_any(uint32_t type, const uint8_t* 
 // Stages the contiguous byte span [src, src + bytes) with 16-byte loads from
 // the 16-byte boundary at or below src (all of a lane's loads in flight before
 // its stores); returns where src landed in dst (0..15).  dst needs bytes + 16.
+template <uint32_t kBatch = 8>
 __device__ __forceinline__ uint32_t warp_stage_span(const uint8_t* __restrict__ src, uint32_t bytes,
                                                     uint8_t* __restrict__ dst, int lane) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(src);
     const uint32_t delta = static_cast<uint32_t>(a & 15u);
     const uint8_t* base = reinterpret_cast<const uint8_t*>(a - delta);
     const uint32_t units = (delta + bytes + 15u) / 16u;
-    constexpr uint32_t kBatch = 8;
     for (uint32_t u0 = lane; u0 < units; u0 += 32u * kBatch) {
         uint4 v[kBatch];
 #pragma unroll
