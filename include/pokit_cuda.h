@@ -280,6 +280,27 @@ pokit_cuda_status pokit_cuda_moe_forward_batch(pokit_cuda_moe* moe, size_t layer
                                                uint32_t* route_ids, float* route_weights, void* stream,
                                                char* error_buffer, size_t error_capacity);
 
+/* Expert parallelism over peer memory (no counterpart in the reference, which
+ * runs on one device; the north star shards the experts over the GPUs of one
+ * box).  One process per GPU, each with an expert-shard handle
+ * (expert_first / expert_count) of the same model, calling
+ * pokit_cuda_moe_forward_batch on the same rows in the same order.  After
+ * pokit_cuda_moe_exchange_create on every rank (it returns this rank's
+ * POKIT_CUDA_IPC_HANDLE_BYTES-byte CUDA IPC handle) and
+ * pokit_cuda_moe_exchange_connect with all ranks' handles in rank order, a
+ * grouped-path forward_batch of <= max_tokens rows returns the whole block's
+ * output on every rank: its last kernel stores the shard's partial sums into
+ * every rank's region over NVLink, raises a flag there, waits for the other
+ * ranks' flags (at most ~1 s, then a sticky RUNTIME_ERROR) and adds the
+ * ranks' partials in rank order.  Every rank must make the same forward_batch
+ * calls (as with a collective); pokit_cuda_moe_time_batch stays local. */
+#define POKIT_CUDA_IPC_HANDLE_BYTES 64
+pokit_cuda_status pokit_cuda_moe_exchange_create(pokit_cuda_moe* moe, size_t world, size_t rank,
+                                                 size_t max_tokens, void* ipc_handle_out,
+                                                 char* error_buffer, size_t error_capacity);
+pokit_cuda_status pokit_cuda_moe_exchange_connect(pokit_cuda_moe* moe, const void* ipc_handles,
+                                                  char* error_buffer, size_t error_capacity);
+
 /* Measurement hook for benchmarks (no counterpart in the reference): runs the
  * grouped-path batched forward `repetitions` times on device buffers with an
  * event between its kernels and writes the average device time (us) of each

@@ -23,6 +23,7 @@ STATUS_BUFFER_TOO_SMALL, STATUS_INTERNAL_ERROR = 3, 4
  SHARED_DOWN) = range(9)
 QWEN3, QWEN35 = 0, 1
 INPUT_F32, INPUT_BF16 = 0, 1
+IPC_HANDLE_BYTES = 64   # POKIT_CUDA_IPC_HANDLE_BYTES
 
 
 def row_bytes(ggml_type: int, cols: int) -> int:
@@ -140,6 +141,8 @@ SIGNATURES = {
     "pokit_cuda_moe_forward": (C.c_int, [_VP, _SZ, _VP, _VP, _VP, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_batch": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, _VP, _VP, _VP,
                                                _ERR, _SZ]),
+    "pokit_cuda_moe_exchange_create": (C.c_int, [_VP, _SZ, _SZ, _SZ, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_exchange_connect": (C.c_int, [_VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_time_batch": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, C.c_uint32, _VP, _SZ,
                                             C.POINTER(_SZ), _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_batch_host": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, _VP, _VP,

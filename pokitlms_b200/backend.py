@@ -188,6 +188,20 @@ class CudaMoeBackend:
         call("pokit_cuda_moe_forward_batch", self._h, layer, _ptr(x), kind, tokens, _ptr(logits), _ptr(out),
              _ptr(route_ids), _ptr(route_weights), _stream(stream))
 
+    def exchange_create(self, world: int, rank: int, max_tokens: int) -> bytes:
+        """This rank's part of the peer-memory exchange (pokit_cuda_moe_exchange_create):
+        returns its CUDA IPC handle for the other ranks."""
+        buf = C.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        call("pokit_cuda_moe_exchange_create", self._h, world, rank, max_tokens, C.cast(buf, C.c_void_p))
+        return buf.raw
+
+    def exchange_connect(self, handles: list[bytes]) -> None:
+        """Maps the other ranks' regions (handles in rank order); from then on
+        forward_batch returns the whole block's output (pokit_cuda_moe_exchange_connect)."""
+        raw = b"".join(handles)
+        buf = C.create_string_buffer(raw, len(raw))
+        call("pokit_cuda_moe_exchange_connect", self._h, C.cast(buf, C.c_void_p))
+
     def time_batch(self, layer: int, x, out, *, logits=None, reps: int = 10, stream=None) -> list[float]:
         """Average device time (us) of each kernel of the grouped batched
         forward over `reps` runs: [router,] route, group, pack, gate/up,

@@ -154,6 +154,9 @@ public:
     }
 
     ~MoeBackend() {
+        for (void* p : ex_opened_) cudaIpcCloseMemHandle(p);
+        if (ex_region_) cudaFree(ex_region_);
+        if (ex_words_) cudaFree(ex_words_);
         for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second.first);
         if (batch_pinned_) cudaFreeHost(batch_pinned_);
         if (batch_io_) cudaFree(batch_io_);
@@ -285,11 +288,13 @@ public:
         if (moe_batch_grouped(L)) {
             ensure_batch_scratch(L, T);
             uint32_t n = 0;
-            guard(launch_moe_batch(L, B_, x, x_type, T, logits, out, ids, w, S_.status, st, &n),
+            guard(launch_moe_batch(L, B_, x, x_type, T, logits, out, ids, w, S_.status, st, &n, nullptr,
+                                   ex_connected_ ? &ex_ : nullptr),
                   "grouped MoE batch");
             kernel_launches_ += n;
         } else {
             refuse_sharded();
+            if (ex_connected_) throw std::invalid_argument("the peer-memory exchange needs the grouped path");
             if (x_type != POKIT_CUDA_INPUT_F32)
                 throw std::invalid_argument("BF16 input needs the grouped path (Q4_K experts, no shared expert)");
             if (logits) throw std::invalid_argument("caller logits need the grouped path (Q4_K experts, no shared expert)");
@@ -510,6 +515,58 @@ public:
         return s;
     }
 
+    // Expert-parallel exchange over peer memory: this rank's region (partial
+    // outputs of every rank, flags), exported for the other processes.
+    void exchange_create(size_t world, size_t rank, size_t max_tokens, void* handle_out) {
+        ensure_ok();
+        if (ex_region_) throw std::invalid_argument("the exchange is already created");
+        if (world < 1 || world > kMaxExchangeRanks || rank >= world || max_tokens == 0 || max_tokens > kMaxBatchTokens ||
+            !handle_out)
+            throw std::invalid_argument("exchange needs 1..8 ranks, rank < world, 1..65536 tokens and a handle buffer");
+        DeviceScope scope(device_);
+        const uint64_t bytes = ep_exchange_bytes(static_cast<uint32_t>(world), static_cast<uint32_t>(max_tokens),
+                                                 static_cast<uint32_t>(cfg_.hidden));
+        guard(cudaMalloc(&ex_region_, bytes), "cudaMalloc(exchange)");
+        guard(cudaMemset(ex_region_, 0, bytes), "exchange");
+        guard(cudaMalloc(reinterpret_cast<void**>(&ex_words_), 256), "cudaMalloc(exchange counters)");
+        guard(cudaMemset(ex_words_, 0, 256), "exchange");
+        cudaIpcMemHandle_t h{};
+        guard(cudaIpcGetMemHandle(&h, ex_region_), "cudaIpcGetMemHandle");
+        static_assert(sizeof(h) == POKIT_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
+        std::memcpy(handle_out, &h, sizeof(h));
+        ex_ = EpExchange{};
+        ex_.world = static_cast<uint32_t>(world);
+        ex_.rank = static_cast<uint32_t>(rank);
+        ex_.max_tokens = static_cast<uint32_t>(max_tokens);
+        ex_.hidden = static_cast<uint32_t>(cfg_.hidden);
+        ex_.epoch = ex_words_;
+        ex_.arrive = ex_words_ + 32;
+    }
+
+    // Maps the other ranks' regions (handles in rank order) and routes the
+    // batched forward through the exchange.
+    void exchange_connect(const void* handles) {
+        ensure_ok();
+        if (!ex_region_) throw std::invalid_argument("create the exchange first");
+        if (ex_connected_) throw std::invalid_argument("the exchange is already connected");
+        if (!handles) throw std::invalid_argument("the ranks' IPC handles are required");
+        DeviceScope scope(device_);
+        guard(cudaDeviceSynchronize(), "exchange");
+        for (uint32_t r = 0; r < ex_.world; ++r) {
+            if (r == ex_.rank) {
+                ex_.peers[r] = static_cast<uint8_t*>(ex_region_);
+                continue;
+            }
+            cudaIpcMemHandle_t h{};
+            std::memcpy(&h, static_cast<const uint8_t*>(handles) + r * sizeof(h), sizeof(h));
+            void* p = nullptr;
+            guard(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+            ex_opened_.push_back(p);
+            ex_.peers[r] = static_cast<uint8_t*>(p);
+        }
+        ex_connected_ = true;
+    }
+
 private:
     static constexpr size_t kMaxBatchTokens = 65536;
 
@@ -623,6 +680,11 @@ private:
     MoeScratch S_;
     void* batch_scratch_ = nullptr;   // grouped-path scratch, grown on demand
     MoeBatchScratch B_;
+    void* ex_region_ = nullptr;          // this rank's exchange region (exported)
+    uint32_t* ex_words_ = nullptr;       // call number and arrival counter of the exchange kernel
+    std::vector<void*> ex_opened_;       // the other ranks' regions, mapped here
+    EpExchange ex_{};
+    bool ex_connected_ = false;
     void* batch_io_ = nullptr;        // host-span batch staging (device, pinned host)
     void* batch_pinned_ = nullptr;
     size_t batch_io_bytes_ = 0;
@@ -965,6 +1027,24 @@ pokit_cuda_status pokit_cuda_moe_forward_batch(pokit_cuda_moe* moe, size_t layer
         std::lock_guard<std::mutex> lock(moe->impl.mutex());
         moe->impl.forward_batch(layer, input, input_type, tokens, router_logits, output, route_ids, route_weights,
                                 as_stream(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_exchange_create(pokit_cuda_moe* moe, size_t world, size_t rank, size_t max_tokens,
+                                                 void* ipc_handle_out, char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.exchange_create(world, rank, max_tokens, ipc_handle_out);
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_exchange_connect(pokit_cuda_moe* moe, const void* ipc_handles, char* error_buffer,
+                                                  size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.exchange_connect(ipc_handles);
     });
 }
 

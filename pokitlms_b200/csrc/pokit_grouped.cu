@@ -1227,6 +1227,120 @@ __global__ void combine_kernel(const float* __restrict__ pair_out, const uint32_
     reinterpret_cast<float4*>(out + t * H)[c] = acc;
 }
 
+// ---------------------------------------------------------------------------
+// 8'. Combine and exchange (expert parallelism over peer memory).  One kernel
+// per block replaces the local combine and the all-reduce of the ranks'
+// partial outputs:
+//   1. this rank's partial (its experts' pairs, rank order) is stored into
+//      slot [parity][rank] of every rank's exchange region (NVLink stores);
+//   2. the CTA that arrives last raises flag [parity][rank] = call number on
+//      every rank (release, after a system fence);
+//   3. every CTA waits until all ranks' flags of this call are up (acquire;
+//      at most ~1 s, then the status bit and no wait), then sums the ranks'
+//      partials in rank order, so every rank writes the same values.
+// The call number lives in device memory (read by every CTA before the last
+// one advances it), so graph replays count correctly; the parity double
+// buffer keeps a rank that runs one call ahead from overwriting a slot
+// another rank is still reading.  All CTAs are co-resident (grid <= SMs),
+// which the wait of step 3 needs.
+// ---------------------------------------------------------------------------
+struct ExchangeArgs {
+    const float* pair_out;
+    const uint32_t* ids;
+    uint32_t e_first, e_count, tokens, k, H;
+    float* out;
+    uint32_t* status;
+    EpExchange ex;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+constexpr uint32_t kExchangeSpins = 1u << 22;   // x >= 256 ns sleeps: about a second
+
+__global__ void __launch_bounds__(256) exchange_combine_kernel(const __grid_constant__ ExchangeArgs a) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const EpExchange& ex = a.ex;
+    __shared__ uint32_t s_target, s_last;
+    if (threadIdx.x == 0) s_target = *reinterpret_cast<volatile const uint32_t*>(ex.epoch) + 1u;
+    __syncthreads();
+    const uint32_t target = s_target, par = target & 1u;
+    const size_t slot = static_cast<size_t>(ex.max_tokens) * ex.hidden;   // floats per (parity, source) slot
+    const size_t recv_floats = 2ull * ex.world * slot;
+    const size_t per_token = a.H / 4, quads = static_cast<size_t>(a.tokens) * per_token;
+    const size_t step = static_cast<size_t>(gridDim.x) * blockDim.x;
+    // 1. The local partial into slot [par][rank] of every rank.
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < quads; i += step) {
+        const size_t t = i / per_token, c = i % per_token;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t r = 0; r < a.k; ++r) {
+            if (a.ids[t * a.k + r] - a.e_first >= a.e_count) continue;   // an expert of another shard
+            const float4 v = reinterpret_cast<const float4*>(a.pair_out + (t * a.k + r) * a.H)[c];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        for (uint32_t d = 0; d < ex.world; ++d) {
+            float* dst = reinterpret_cast<float*>(ex.peers[d]) + (static_cast<size_t>(par) * ex.world + ex.rank) * slot;
+            reinterpret_cast<float4*>(dst)[t * per_token + c] = acc;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    // 2. The last CTA raises this rank's flag on every rank.
+    if (threadIdx.x == 0) s_last = atomicAdd(ex.arrive, 1u) == gridDim.x - 1u ? 1u : 0u;
+    __syncthreads();
+    if (s_last) {
+        __threadfence_system();
+        if (threadIdx.x < ex.world) {
+            uint32_t* fl = reinterpret_cast<uint32_t*>(reinterpret_cast<float*>(ex.peers[threadIdx.x]) + recv_floats);
+            st_release_sys(fl + par * ex.world + ex.rank, target);
+        }
+        if (threadIdx.x == 0) {
+            *ex.arrive = 0u;
+            *ex.epoch = target;
+        }
+    }
+    // 3. Wait for every rank's partial, then sum them in rank order.
+    if (threadIdx.x == 0) {
+        const uint32_t* fl =
+            reinterpret_cast<const uint32_t*>(reinterpret_cast<const float*>(ex.peers[ex.rank]) + recv_floats) +
+            par * ex.world;
+        for (uint32_t src = 0; src < ex.world; ++src) {
+            uint32_t spins = 0;
+            while (ld_acquire_sys(fl + src) != target) {
+                if (++spins > kExchangeSpins) {
+                    atomicOr(a.status, kStatusWaitTimeout);
+                    break;
+                }
+                __nanosleep(256);
+            }
+            if (spins > kExchangeSpins) break;
+        }
+    }
+    __syncthreads();
+    const float* mine = reinterpret_cast<const float*>(ex.peers[ex.rank]) + static_cast<size_t>(par) * ex.world * slot;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < quads; i += step) {
+        const size_t t = i / per_token, c = i % per_token;
+        float4 acc = __ldcg(reinterpret_cast<const float4*>(mine) + t * per_token + c);
+        for (uint32_t src = 1; src < ex.world; ++src) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(mine + src * slot) + t * per_token + c);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        reinterpret_cast<float4*>(a.out + t * a.H)[c] = acc;
+    }
+}
+
 // Gate/up operand from BF16 inputs (no lo part) or F32 inputs (hi + lo); the
 // down operand always has the lo part.
 using GateUpBf16 = GemmLayout<0, 0, 4, 3>;
@@ -1310,6 +1424,10 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
 
 }  // namespace
 
+uint64_t ep_exchange_bytes(uint32_t world, uint32_t max_tokens, uint32_t hidden) {
+    return al256(2ull * world * max_tokens * hidden * 4ull + 2ull * world * 4ull);
+}
+
 bool moe_batch_grouped(const MoeLayerDev& L) {
     const auto al16 = [](const void* p, uint64_t n) {
         return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && (n & 15u) == 0;
@@ -1357,7 +1475,8 @@ MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_token
 
 cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, const void* x, uint32_t x_bf16,
                              uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
-                             uint32_t* status, cudaStream_t stream, uint32_t* launches, cudaEvent_t* marks) {
+                             uint32_t* status, cudaStream_t stream, uint32_t* launches, cudaEvent_t* marks,
+                             const EpExchange* ex) {
     uint32_t n = 0, stage = 0;   // kernels launched; stage boundaries marked
     const bool pdl = marks == nullptr;   // per-stage events need the kernels serialised
     const auto mark = [&]() {
@@ -1365,6 +1484,9 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     };
     if (launches) *launches = 0;
     if (!moe_batch_grouped(L) || tokens == 0 || tokens > S.max_tokens || !x || !out || !status)
+        return cudaErrorInvalidValue;
+    if (ex && (ex->world < 1 || ex->world > kMaxExchangeRanks || ex->rank >= ex->world || tokens > ex->max_tokens ||
+               ex->hidden != L.hidden || !ex->epoch || !ex->arrive))
         return cudaErrorInvalidValue;
     if (!logits && !L.router) return cudaErrorInvalidValue;
     const uint32_t E = L.experts, k = L.top_k, H = L.hidden, I = L.inter;
@@ -1543,8 +1665,26 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
     }
     n += any_large ? 2u : 1u;
     mark();
-    // 8. combine
-    {
+    // 8. combine (and, with an exchange, the sum over the ranks)
+    if (ex) {
+        const size_t quads = static_cast<size_t>(tokens) * H / 4;
+        const uint32_t grid = static_cast<uint32_t>(std::min<size_t>(static_cast<size_t>(sms), (quads + 255) / 256));
+        ExchangeArgs xa{};
+        xa.pair_out = S.pair_out;
+        xa.ids = S.ids;
+        xa.e_first = E0;
+        xa.e_count = EL;
+        xa.tokens = tokens;
+        xa.k = k;
+        xa.H = H;
+        xa.out = out;
+        xa.status = status;
+        xa.ex = *ex;
+        if ((err = launch_k(exchange_combine_kernel, dim3(grid), dim3(256), 0, stream, pdl, xa)) != cudaSuccess)
+            return err;
+        ++n;
+        mark();
+    } else {
         const size_t quads = static_cast<size_t>(tokens) * H / 4;
         if ((err = launch_k(combine_kernel, dim3(static_cast<uint32_t>((quads + 255) / 256)), dim3(256), 0, stream,
                             pdl, static_cast<const float*>(S.pair_out), static_cast<const uint32_t*>(S.ids), E0, EL,

@@ -154,14 +154,32 @@ bool moe_batch_grouped(const MoeLayerDev& L);
 uint64_t moe_batch_scratch_bytes(const MoeLayerDev& L, uint32_t max_tokens);
 MoeBatchScratch moe_batch_scratch_carve(const MoeLayerDev& L, uint32_t max_tokens, void* base);
 
+// Expert-parallel exchange over peer memory (one process per GPU, the same
+// rows on every rank).  Every rank owns one exchange region, mapped into the
+// others' address spaces: [2 parities][world][max_tokens][hidden] F32 partial
+// outputs, then [2 parities][world] uint32 flags.  peers[r] is rank r's region
+// as seen from this GPU (peers[rank] the local one); epoch and arrive are two
+// local device words (zero at set-up).
+constexpr uint32_t kMaxExchangeRanks = 8;
+struct EpExchange {
+    uint32_t world = 0, rank = 0, max_tokens = 0, hidden = 0;
+    uint8_t* peers[kMaxExchangeRanks] = {};
+    uint32_t* epoch = nullptr;
+    uint32_t* arrive = nullptr;
+};
+// Bytes of one rank's exchange region.
+uint64_t ep_exchange_bytes(uint32_t world, uint32_t max_tokens, uint32_t hidden);
+
 // out[t] = MoE(x[t]) for `tokens` rows of x (F32, or BF16 when x_bf16), each
 // routed independently: by `logits` ([tokens][experts] F32 on the device)
 // when given, else by the layer's router.  ids/weights (may be null) receive
-// the routes.  `status` collects the sticky StatusBits.
+// the routes.  `status` collects the sticky StatusBits.  With `ex`, the
+// combine kernel also exchanges the shard's partial outputs with the other
+// ranks over peer memory and writes their sum (every rank the same values).
 cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, const void* x, uint32_t x_bf16,
                              uint32_t tokens, const float* logits, float* out, uint32_t* ids, float* weights,
                              uint32_t* status, cudaStream_t stream, uint32_t* launches,
-                             cudaEvent_t* marks = nullptr);
+                             cudaEvent_t* marks = nullptr, const EpExchange* ex = nullptr);
 // Stages (kernels) of one launch_moe_batch: 8, or 7 when logits are given.
 // marks (one more than stages) receive an event before the first and after
 // each kernel.

@@ -136,3 +136,87 @@ def test_two_rank_expert_parallel_over_nccl(cuda):
     assert all(p.exitcode == 0 for p in procs)
     rel = q.get(timeout=10)
     assert float(rel.max()) <= TOL
+
+
+def _exchange_rank(rank, world, port, q):
+    """One rank of the peer-memory exchange: two eager batches of different
+    sizes and input types (both exchange parities), then one batch captured in
+    a CUDA graph and replayed twice (the call counter lives on the device)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    from pokitlms_b200.ep import ExpertParallelMoe
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    L = cases.moe_layer(hidden=512, inter=256, experts=16, top_k=4, seed=2)
+    ep = ExpertParallelMoe(rank=rank, world=world, layers=1, hidden=512, inter=256, experts=16, top_k=4,
+                           device=rank, exchange_tokens=64)
+    assert ep.peer_exchange
+    upload_shard(ep.backend, L, ep.expert_first, ep.expert_count)
+    results = []
+    bits, xf, logits = synth.grouped_inputs(40, 16, 512, seed=9)
+    x = torch.from_numpy(bits.view(np.int16)).cuda().view(torch.bfloat16)
+    out = torch.empty(40, 512, device="cuda")
+    ep.forward_batch(0, x, out, logits=torch.from_numpy(logits).cuda())
+    ep.backend.synchronize()
+    results.append((out.cpu().numpy(), xf, logits))
+    rng = np.random.default_rng(4)
+    x2 = rng.standard_normal((8, 512), dtype=np.float32)
+    lg2 = rng.standard_normal((8, 16), dtype=np.float32)
+    x2d, lg2d = torch.from_numpy(x2).cuda(), torch.from_numpy(lg2).cuda()
+    out2 = torch.empty(8, 512, device="cuda")
+    ep.forward_batch(0, x2d, out2, logits=lg2d)
+    ep.backend.synchronize()
+    results.append((out2.cpu().numpy(), x2, lg2))
+    side = torch.cuda.Stream()
+    out3 = torch.empty(8, 512, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        ep.forward_batch(0, x2d, out3, logits=lg2d, stream=side)
+    replays = []
+    for _ in range(2):
+        out3.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        replays.append(out3.cpu().numpy())
+    del g
+    ep.backend.synchronize()
+    q.put((rank, [r[0] for r in results], replays))
+    if rank == 0:
+        q.put(("inputs", [(r[1], r[2]) for r in results]))
+    ep.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_expert_parallel_over_peer_memory(cuda):
+    """The block's last kernel sums the two shards' partials over NVLink:
+    every rank gets the oracle's output, both ranks the same values, and a
+    captured batch replays to the eager result."""
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_exchange_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=300) for _ in range(3)]
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs)
+    inputs = next(v for k, v in got if k == "inputs")
+    outs = {k: v for k, v in ((g[0], g) for g in got if g[0] != "inputs")}
+    L = cases.moe_layer(hidden=512, inter=256, experts=16, top_k=4, seed=2)
+    for i, (xi, li) in enumerate(inputs):
+        ref, _, _ = O.moe_forward_batch(L, xi, li)
+        rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2, axis=1))
+        for rank in (0, 1):
+            out = outs[rank][1][i]
+            assert float((np.abs(out - ref).max(axis=1) / rms).max()) <= TOL
+        assert np.array_equal(outs[0][1][i], outs[1][1][i])
+    for rank in (0, 1):
+        for rep in outs[rank][2]:
+            assert np.array_equal(rep, outs[rank][1][1])
