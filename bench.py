@@ -487,8 +487,9 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     Is = shape["inter"] if cfg5 else I
     layers = (args.layers if args.layers != LAYERS else shape["layers"]) if cfg5 else args.layers
     T = shape["tokens"] if cfg5 else world
+    peer = world > 1 and args.ep_combine == "peer"
     ep = ExpertParallelMoe(rank=rank, world=world, layers=layers, hidden=Hs, inter=Is, experts=E, top_k=K_TOP,
-                           rms_epsilon=EPS, device=local)
+                           rms_epsilon=EPS, device=local, exchange_tokens=T if peer else None)
     be = ep.backend
     ones = np.ones(Hs, dtype=np.float32)
     for l in range(layers):
@@ -629,7 +630,8 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
                                    "the layer's F32 router"),
                        "layers": layers, "hidden": Hs, "experts": E, "top_k": K_TOP, "inter": Is,
                        "expert_type": "Q4_K", "parallelism": f"ep{world} (experts {E // world} per GPU, "
-                       "NCCL all-reduce combine)", "cuda_graph": graph_used,
+                       + ("combine over NVLink peer memory in the block's last kernel)" if peer else
+                          "NCCL all-reduce combine)"), "cuda_graph": graph_used,
                        "l2": "no flush: each rank streams its shard's routed experts every layer"},
             "roofline": {"bound": "hbm", "kernel": "moe block per rank (grouped path + all-reduce)",
                          "achieved": per_rank_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -654,6 +656,9 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-combine", default="nccl", choices=["peer", "nccl"],
+                    help="N > 1: sum the shards' outputs in the block's last kernel over NVLink peer memory "
+                         "(peer) or with an NCCL all-reduce (nccl)")
     ap.add_argument("--workload", default="decode", choices=["decode", "grouped", "config3", "config5"],
                     help="grouped: only the configuration-4 measurement (one GPU; a small process for "
                          "profiling the grouped kernels); config3: only the configuration-3 chain (one "

@@ -207,8 +207,8 @@ def test_two_rank_expert_parallel_over_peer_memory(cuda):
     for p in procs:
         p.join(120)
     assert all(p.exitcode == 0 for p in procs)
-    inputs = next(v for k, v in got if k == "inputs")
-    outs = {k: v for k, v in ((g[0], g) for g in got if g[0] != "inputs")}
+    inputs = next(g[1] for g in got if g[0] == "inputs")
+    outs = {g[0]: g for g in got if g[0] != "inputs"}
     L = cases.moe_layer(hidden=512, inter=256, experts=16, top_k=4, seed=2)
     for i, (xi, li) in enumerate(inputs):
         ref, _, _ = O.moe_forward_batch(L, xi, li)
