@@ -300,6 +300,12 @@ pokit_cuda_status pokit_cuda_moe_exchange_create(pokit_cuda_moe* moe, size_t wor
                                                  char* error_buffer, size_t error_capacity);
 pokit_cuda_status pokit_cuda_moe_exchange_connect(pokit_cuda_moe* moe, const void* ipc_handles,
                                                   char* error_buffer, size_t error_capacity);
+/* Unmaps the other ranks' regions (waiting for this handle's work first) and
+ * returns forward_batch to this rank's partial output.  Call it on every rank
+ * before any rank destroys its handle: a rank's region must not be freed
+ * while another process still maps it.  Allowed on a failed handle. */
+pokit_cuda_status pokit_cuda_moe_exchange_disconnect(pokit_cuda_moe* moe, char* error_buffer,
+                                                     size_t error_capacity);
 
 /* Measurement hook for benchmarks (no counterpart in the reference): runs the
  * grouped-path batched forward `repetitions` times on device buffers with an

@@ -143,6 +143,7 @@ SIGNATURES = {
                                                _ERR, _SZ]),
     "pokit_cuda_moe_exchange_create": (C.c_int, [_VP, _SZ, _SZ, _SZ, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_exchange_connect": (C.c_int, [_VP, _VP, _ERR, _SZ]),
+    "pokit_cuda_moe_exchange_disconnect": (C.c_int, [_VP, _ERR, _SZ]),
     "pokit_cuda_moe_time_batch": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, C.c_uint32, _VP, _SZ,
                                             C.POINTER(_SZ), _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_batch_host": (C.c_int, [_VP, _SZ, _VP, C.c_uint32, _SZ, _VP, _VP, _VP, _VP,

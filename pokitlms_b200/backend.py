@@ -202,6 +202,11 @@ class CudaMoeBackend:
         buf = C.create_string_buffer(raw, len(raw))
         call("pokit_cuda_moe_exchange_connect", self._h, C.cast(buf, C.c_void_p))
 
+    def exchange_disconnect(self) -> None:
+        """Unmaps the other ranks' regions (pokit_cuda_moe_exchange_disconnect); every
+        rank disconnects before any rank closes its handle."""
+        call("pokit_cuda_moe_exchange_disconnect", self._h)
+
     def time_batch(self, layer: int, x, out, *, logits=None, reps: int = 10, stream=None) -> list[float]:
         """Average device time (us) of each kernel of the grouped batched
         forward over `reps` runs: [router,] route, group, pack, gate/up,

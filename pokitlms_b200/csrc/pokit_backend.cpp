@@ -567,6 +567,19 @@ public:
         ex_connected_ = true;
     }
 
+    // Unmaps the other ranks' regions (after this rank's work on them is done)
+    // and returns forward_batch to the local combine.  Every rank disconnects
+    // before any rank destroys its handle: an exported region must not be
+    // freed while another process still maps it.  Works on a failed handle.
+    void exchange_disconnect() {
+        DeviceScope scope(device_);
+        cudaStreamSynchronize(stream_);
+        for (void* p : ex_opened_) cudaIpcCloseMemHandle(p);
+        ex_opened_.clear();
+        for (auto& p : ex_.peers) p = nullptr;
+        ex_connected_ = false;
+    }
+
 private:
     static constexpr size_t kMaxBatchTokens = 65536;
 
@@ -1045,6 +1058,14 @@ pokit_cuda_status pokit_cuda_moe_exchange_connect(pokit_cuda_moe* moe, const voi
         if (!moe) throw std::invalid_argument("MoE handle is required");
         std::lock_guard<std::mutex> lock(moe->impl.mutex());
         moe->impl.exchange_connect(ipc_handles);
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_exchange_disconnect(pokit_cuda_moe* moe, char* error_buffer, size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("MoE handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        moe->impl.exchange_disconnect();
     });
 }
 

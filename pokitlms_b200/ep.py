@@ -68,6 +68,6 @@ class ExpertParallelMoe:
     def close(self) -> None:
         if self.peer_exchange:
             import torch.distributed as dist
-            self.backend.synchronize()
-            dist.barrier(group=self.group)  # no rank frees its region while another still stores into it
+            self.backend.exchange_disconnect()   # waits for this rank's stores, unmaps the others
+            dist.barrier(group=self.group)       # no rank frees its region while another still maps it
         self.backend.close()

@@ -220,3 +220,66 @@ def test_two_rank_expert_parallel_over_peer_memory(cuda):
     for rank in (0, 1):
         for rep in outs[rank][2]:
             assert np.array_equal(rep, outs[rank][1][1])
+
+
+
+def _silent_rank(to_child, to_parent):
+    """Rank 1 of a two-rank exchange on the same GPU as rank 0: it creates
+    and maps its region but never runs a block, so rank 0 waits for a flag
+    that nothing raises.  It launches no kernel, so no two kernels wait on one
+    another."""
+    from pokitlms_b200 import backend as B
+    torch.cuda.set_device(0)
+    be = B.CudaMoeBackend(layers=1, hidden=512, inter=256, experts=16, top_k=4, expert_first=8, expert_count=8,
+                          device=0)
+    mine = be.exchange_create(2, 1, 16)
+    to_parent.put(mine)
+    h0 = to_child.get(timeout=120)
+    be.exchange_connect([h0, mine])
+    to_parent.put("connected")
+    assert to_child.get(timeout=300) == "disconnect"
+    be.exchange_disconnect()
+    be.close()
+    to_parent.put("closed")
+
+
+def test_peer_exchange_wait_runs_out_when_a_rank_never_arrives(cuda):
+    """A bounded device-side wait: rank 0's combine waits for rank 1's flag,
+    which rank 1 (another process, same GPU) never raises; after ~1-2 s the
+    kernel gives up, sets the status word, and the handle reports a sticky
+    runtime error instead of hanging."""
+    import time
+    import torch.multiprocessing as mp
+    from pokitlms_b200._lib import PokitCudaError
+    ctx = mp.get_context("spawn")
+    to_child, to_parent = ctx.Queue(), ctx.Queue()
+    child = ctx.Process(target=_silent_rank, args=(to_child, to_parent))
+    child.start()
+    L = cases.moe_layer(hidden=512, inter=256, experts=16, top_k=4, seed=2)
+    be = B.CudaMoeBackend(layers=1, hidden=512, inter=256, experts=16, top_k=4, expert_first=0, expert_count=8,
+                          device=0)
+    upload_shard(be, L, 0, 8)
+    try:
+        mine = be.exchange_create(2, 0, 16)
+        h1 = to_parent.get(timeout=120)
+        to_child.put(mine)
+        be.exchange_connect([mine, h1])
+        assert to_parent.get(timeout=120) == "connected"
+        rng = np.random.default_rng(5)
+        x = torch.from_numpy(rng.standard_normal((4, 512), dtype=np.float32)).cuda()
+        lg = torch.from_numpy(rng.standard_normal((4, 16), dtype=np.float32)).cuda()
+        out = torch.empty(4, 512, device="cuda")
+        t0 = time.perf_counter()
+        be.forward_batch(0, x, out, logits=lg)
+        with pytest.raises(PokitCudaError, match="timed out"):
+            be.synchronize()
+        assert time.perf_counter() - t0 < 60
+        with pytest.raises(PokitCudaError):          # sticky
+            be.forward_batch(0, x, out, logits=lg)
+    finally:
+        be.exchange_disconnect()                   # unmap rank 1's region before it is freed
+        to_child.put("disconnect")
+        assert to_parent.get(timeout=120) == "closed"
+        child.join(60)
+        be.close()
+    assert child.exitcode == 0
