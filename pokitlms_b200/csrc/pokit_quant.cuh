@@ -256,50 +256,6 @@ __device__ __forceinline__ void warp_stage_row(const uint8_t* __restrict__ src, 
     }
 }
 
-// Stages n rows (row i at src + i * stride, `bytes` each) into dst (row i at
-// dst + i * dst_stride) with a batch of loads per lane in flight before the
-// stores: one memory latency per batch instead of one per row.
-__device__ __forceinline__ void warp_stage_rows(const uint8_t* __restrict__ src, uint64_t stride, uint32_t n,
-                                                uint32_t bytes, uint8_t* __restrict__ dst, uint32_t dst_stride,
-                                                int lane) {
-    const uint64_t a = reinterpret_cast<uint64_t>(src);
-    if ((a & 15u) == 0 && (bytes & 15u) == 0 && (stride & 15u) == 0 && (dst_stride & 15u) == 0) {
-        const uint32_t units = bytes / 16u, total = units * n;
-        constexpr uint32_t kBatch = 8;
-        for (uint32_t base = lane; base < total; base += 32u * kBatch) {
-            uint4 v[kBatch];
-#pragma unroll
-            for (uint32_t j = 0; j < kBatch; ++j) {
-                const uint32_t w = base + 32u * j;
-                if (w < total) v[j] = ldg_stream128(src + (w / units) * stride + (w % units) * 16u);
-            }
-#pragma unroll
-            for (uint32_t j = 0; j < kBatch; ++j) {
-                const uint32_t w = base + 32u * j;
-                if (w < total) *reinterpret_cast<uint4*>(dst + (w / units) * dst_stride + (w % units) * 16u) = v[j];
-            }
-        }
-    } else if ((a & 3u) == 0 && (bytes & 3u) == 0 && (stride & 3u) == 0 && (dst_stride & 3u) == 0) {
-        const uint32_t words = bytes / 4u, total = words * n;
-        constexpr uint32_t kBatch = 16;
-        for (uint32_t base = lane; base < total; base += 32u * kBatch) {
-            uint32_t v[kBatch];
-#pragma unroll
-            for (uint32_t j = 0; j < kBatch; ++j) {
-                const uint32_t w = base + 32u * j;
-                if (w < total) v[j] = ldg_stream32(src + (w / words) * stride + (w % words) * 4u);
-            }
-#pragma unroll
-            for (uint32_t j = 0; j < kBatch; ++j) {
-                const uint32_t w = base + 32u * j;
-                if (w < total) *reinterpret_cast<uint32_t*>(dst + (w / words) * dst_stride + (w % words) * 4u) = v[j];
-            }
-        }
-    } else {
-        for (uint32_t i = 0; i < n; ++i) warp_stage_row(src + i * stride, bytes, dst + i * dst_stride, lane);
-    }
-}
-
 // This lane's share of the dot of a staged row (cols weights) with x: lane l
 // takes elements l, l + 32, l + 64, ...  With that mapping a warp reads 32
 // consecutive activations and 32 consecutive quant bytes per step (no shared-
@@ -500,17 +456,6 @@ __device__ __forceinline__ uint32_t warp_stage_span(const uint8_t* __restrict__ 
             if (u0 + 32u * j < units) *reinterpret_cast<uint4*>(dst + (u0 + 32u * j) * 16u) = v[j];
     }
     return delta;
-}
-
-// Dot of 32-weight group g of a staged row of any supported type with x.
-__device__ __forceinline__ float group_dot_any(uint32_t type, const uint8_t* row, int g, const float* x) {
-    switch (type) {
-        case kQ4_K: return group_dot<kQ4_K>(row, g, x);
-        case kQ5_K: return group_dot<kQ5_K>(row, g, x);
-        case kQ6_K: return group_dot<kQ6_K>(row, g, x);
-        case kQ8_0: return group_dot<kQ8_0>(row, g, x);
-        default: return group_dot<kF32>(row, g, x);
-    }
 }
 
 }  // namespace pokit
