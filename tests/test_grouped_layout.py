@@ -264,3 +264,39 @@ def test_thin_layout_reproduces_q4k_dot():
         ref = float(np.dot(w, xf.astype(np.float64)))
         scale = float(np.sum(np.abs(w * xf)))
         assert abs(thin_dot(block, xf, split=True, n=b % 8) - ref) <= 1e-6 * scale
+
+
+def group_tiles(counts, tile=64, skinny=8):
+    """group_kernel's tile bookkeeping for per-expert pair counts: tile ids in
+    expert order, and tile_order = the tiles of > skinny tokens, then the
+    others, each at the position the kernel writes it to."""
+    thin = [1 if (c % tile) and (c % tile) <= skinny else 0 for c in counts]
+    ntiles = [(c + tile - 1) // tile for c in counts]
+    off_tile = np.concatenate([[0], np.cumsum(ntiles)[:-1]]).astype(int)
+    off_thin = np.concatenate([[0], np.cumsum(thin)[:-1]]).astype(int)
+    total, n_thin = int(sum(ntiles)), int(sum(thin))
+    large = total - n_thin
+    order = [-1] * total
+    sizes = {}
+    for e, c in enumerate(counts):
+        for i in range(ntiles[e]):
+            t = off_tile[e] + i
+            n = min(tile, c - i * tile)
+            sizes[t] = n
+            pos = large + off_thin[e] if n <= skinny else t - off_thin[e]
+            assert 0 <= pos < total and order[pos] == -1, (e, i, pos)
+            order[pos] = t
+    return order, sizes, large
+
+
+def test_tile_order_puts_large_tiles_first_as_a_permutation():
+    rng = np.random.default_rng(12)
+    for _ in range(300):
+        E = int(rng.integers(1, 64))
+        counts = [int(v) for v in rng.choice([0, 1, 3, 8, 9, 40, 63, 64, 65, 72, 73, 128, 200], size=E)]
+        order, sizes, large = group_tiles(counts)
+        assert sorted(order) == list(range(len(order)))
+        assert all(sizes[t] > 8 for t in order[:large])
+        assert all(sizes[t] <= 8 for t in order[large:])
+        # within each list, tiles keep expert order (ids increase)
+        assert order[:large] == sorted(order[:large]) and order[large:] == sorted(order[large:])
