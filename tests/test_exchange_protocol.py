@@ -78,3 +78,27 @@ def test_a_rank_that_stops_makes_the_others_time_out_not_read_stale_slots():
             for r in range(n - 1):
                 assert len(results[r]) == 3        # calls 1..3 complete, call 4 never does
                 assert timeouts[r] == 1
+
+
+def exchange_bytes(world, max_tokens, hidden):
+    """ep_exchange_bytes: partials [2][world][max_tokens][hidden] F32, then
+    [2][world] uint32 flags, rounded up to 256 bytes."""
+    b = 2 * world * max_tokens * hidden * 4 + 2 * world * 4
+    return (b + 255) // 256 * 256
+
+
+def test_exchange_offsets_stay_inside_the_region():
+    """The byte offsets exchange_combine_kernel forms: float4 partial stores
+    and loads at ((par * world + src) * slot + t * hidden + 4c) * 4, flags at
+    2 * world * slot * 4 + (par * world + src) * 4."""
+    for world in (1, 2, 3, 4, 8):
+        for max_tokens in (1, 7, 16, 64):
+            for hidden in (256, 2048, 4096):
+                region = exchange_bytes(world, max_tokens, hidden)
+                slot = max_tokens * hidden
+                last_float4 = ((1 * world + (world - 1)) * slot + (max_tokens - 1) * hidden + hidden - 4) * 4
+                assert last_float4 + 16 <= 2 * world * slot * 4           # partials end before the flags
+                flags0 = 2 * world * slot * 4
+                last_flag = flags0 + (1 * world + (world - 1)) * 4
+                assert last_flag + 4 <= region
+                assert flags0 % 4 == 0 and (slot * 4) % 16 == 0         # aligned flags and float4 slots
