@@ -96,8 +96,13 @@ pokit_cuda_status pokit_cuda_synthesize_blocks(uint32_t ggml_type, uint64_t seed
 /* Device counterpart of model::TensorLinearBackend
  * (include/pokitlms/model/tensor_linear.hpp:11-18) and sibling of
  * gpu::VulkanLinearBackend (include/pokitlms/gpu/vulkan_linear.hpp:69-84).
- * Weight payloads are cached in HBM on first use, keyed by host address and
- * size (the Vulkan backend's whole-model device cache, vulkan_linear.cpp:516-563). */
+ * Plain try_linear streams the weight payload to the device on every call, as
+ * the Vulkan backend does for readers without a model file
+ * (vulkan_linear.cpp:516-563, 705-714): a host address is not an identity once
+ * the caller frees and reuses its buffer.  try_linear_cached keeps payloads in
+ * HBM under a key the caller chooses (the tensor's GGUF file offset, say: the
+ * Vulkan backend's whole-model device cache), least recently used first out
+ * beyond the cache capacity (default 16 GiB). */
 typedef struct pokit_cuda_linear_backend pokit_cuda_linear_backend;
 
 /* Mirrors the fields of VulkanLinearStats (vulkan_linear.hpp:41-67) that apply. */
@@ -111,7 +116,7 @@ typedef struct pokit_cuda_linear_stats {
     uint64_t other_dispatches;
     uint64_t weight_bytes;            /* bytes streamed by the kernels */
     uint64_t gpu_time_ns;             /* CUDA-event time of the kernels */
-    uint64_t model_cache_capacity_bytes;
+    uint64_t model_cache_capacity_bytes;  /* bytes held in HBM by try_linear_cached now */
     uint64_t model_cache_uploaded_bytes;
     uint64_t model_cache_upload_time_ns;
 } pokit_cuda_linear_stats;
@@ -129,6 +134,34 @@ pokit_cuda_status pokit_cuda_linear_backend_try_linear(
     pokit_cuda_linear_backend* backend, uint32_t ggml_type, const void* weights_host,
     size_t weights_bytes, size_t rows, size_t cols, const float* input_host,
     float* output_host, int* handled, char* error_buffer, size_t error_capacity);
+
+/* try_linear with the payload cached in HBM under weights_key: the first call
+ * with a key uploads the payload, later calls with that key use the device
+ * copy and do not read weights_host (which may then be NULL; weights_bytes
+ * must still give the payload's size).  A key reused for a matrix of
+ * another type or shape is INVALID_ARGUMENT; a payload larger than the cache
+ * capacity is streamed instead.  The caller must forget (or never reuse) a key
+ * whose bytes change. */
+pokit_cuda_status pokit_cuda_linear_backend_try_linear_cached(
+    pokit_cuda_linear_backend* backend, uint64_t weights_key, uint32_t ggml_type,
+    const void* weights_host, size_t weights_bytes, size_t rows, size_t cols,
+    const float* input_host, float* output_host, int* handled, char* error_buffer,
+    size_t error_capacity);
+
+/* 1 when a payload is cached under weights_key, else 0 (also for a NULL backend). */
+int pokit_cuda_linear_backend_is_cached(const pokit_cuda_linear_backend* backend, uint64_t weights_key);
+
+/* Bytes of payload try_linear_cached may keep in HBM (evicts down to it now). */
+pokit_cuda_status pokit_cuda_linear_backend_set_cache_capacity(pokit_cuda_linear_backend* backend,
+                                                               uint64_t capacity_bytes,
+                                                               char* error_buffer,
+                                                               size_t error_capacity);
+
+/* Drops the payload cached under weights_key; *was_cached (may be NULL) = 1 if
+ * there was one. */
+pokit_cuda_status pokit_cuda_linear_backend_forget(pokit_cuda_linear_backend* backend,
+                                                   uint64_t weights_key, int* was_cached,
+                                                   char* error_buffer, size_t error_capacity);
 
 pokit_cuda_status pokit_cuda_linear_backend_get_stats(const pokit_cuda_linear_backend* backend,
                                                       pokit_cuda_linear_stats* out_stats);
@@ -388,8 +421,9 @@ size_t pokit_cuda_moe_tensor_bytes(const pokit_cuda_moe* moe, size_t layer, uint
 
 /* One MoE block's tensors in device memory the caller owns (GGUF layouts as
  * for pokit_cuda_moe_upload_tensor; shared_* only for the Qwen3.5 flavour).
- * Expert tensors start on 16-byte boundaries and routers on 4-byte ones (as
- * cudaMalloc returns them); others are rejected with INVALID_ARGUMENT. */
+ * Expert tensors and routers start on 16-byte boundaries (as cudaMalloc
+ * returns them; the kernels read them with 16-byte loads); others are rejected
+ * with INVALID_ARGUMENT before any GPU work. */
 typedef struct pokit_cuda_moe_block_device {
     size_t hidden, inter, experts, top_k;
     uint32_t flavour;                 /* pokit_cuda_moe_flavour */
@@ -423,7 +457,8 @@ typedef struct pokit_cuda_moe_block_device {
  * before any stream capture.  Every call shares the array and it keeps the
  * previous call's contents (the status word is cleared at the start of each
  * call); calls whose work overlaps on the GPU race on it.  Runs on `stream`
- * (a cudaStream_t; NULL = the legacy default stream) and waits for it; returns
+ * (a cudaStream_t; NULL = the legacy default stream) and waits for that stream
+ * only (the status word is read back on it); returns
  * RUNTIME_ERROR when the router produced non-finite logits, as the reference
  * throws.  route_ids/route_weights (device, top_k entries) may be NULL. */
 pokit_cuda_status pokit_cuda_moe_forward_static_scratch(

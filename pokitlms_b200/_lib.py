@@ -129,6 +129,12 @@ SIGNATURES = {
     "pokit_cuda_linear_backend_destroy": (None, [_VP]),
     "pokit_cuda_linear_backend_try_linear": (C.c_int, [_VP, C.c_uint32, _VP, _SZ, _SZ, _SZ, _VP,
                                                        _VP, C.POINTER(C.c_int), _ERR, _SZ]),
+    "pokit_cuda_linear_backend_try_linear_cached": (C.c_int, [_VP, C.c_uint64, C.c_uint32, _VP, _SZ, _SZ,
+                                                              _SZ, _VP, _VP, C.POINTER(C.c_int), _ERR,
+                                                              _SZ]),
+    "pokit_cuda_linear_backend_is_cached": (C.c_int, [_VP, C.c_uint64]),
+    "pokit_cuda_linear_backend_set_cache_capacity": (C.c_int, [_VP, C.c_uint64, _ERR, _SZ]),
+    "pokit_cuda_linear_backend_forget": (C.c_int, [_VP, C.c_uint64, C.POINTER(C.c_int), _ERR, _SZ]),
     "pokit_cuda_linear_backend_get_stats": (C.c_int, [_VP, C.POINTER(LinearStats)]),
     "pokit_cuda_moe_create": (C.c_int, [C.POINTER(MoeConfig), C.POINTER(_VP), _ERR, _SZ]),
     "pokit_cuda_moe_destroy": (None, [_VP]),

@@ -78,7 +78,8 @@ def synthesize_blocks(ggml_type: int, seed: int, stream_id: int, nblocks: int, d
 
 
 class CudaLinearBackend:
-    """TensorLinearBackend with host spans and an HBM weight cache."""
+    """TensorLinearBackend with host spans; payloads are streamed per call, or
+    cached in HBM under a caller-chosen key (try_linear(..., key=...))."""
 
     def __init__(self, device: int = 0):
         h = C.c_void_p()
@@ -86,14 +87,27 @@ class CudaLinearBackend:
         self._h = h
 
     def try_linear(self, ggml_type: int, weights: np.ndarray, rows: int, cols: int,
-                   x: np.ndarray, out: np.ndarray) -> bool:
+                   x: np.ndarray, out: np.ndarray, key: int | None = None) -> bool:
         x = np.ascontiguousarray(x, dtype=np.float32)
         if out.dtype != np.float32 or not out.flags.c_contiguous or out.size != rows:
             raise ValueError("output must be a contiguous float32 array of `rows` elements")
         handled = C.c_int(0)
-        call("pokit_cuda_linear_backend_try_linear", self._h, ggml_type, _np_ptr(weights),
-             weights.nbytes, rows, cols, _np_ptr(x), _np_ptr(out), C.byref(handled))
+        if key is None:
+            call("pokit_cuda_linear_backend_try_linear", self._h, ggml_type, _np_ptr(weights),
+                 weights.nbytes, rows, cols, _np_ptr(x), _np_ptr(out), C.byref(handled))
+        else:
+            call("pokit_cuda_linear_backend_try_linear_cached", self._h, key, ggml_type,
+                 _np_ptr(weights), weights.nbytes, rows, cols, _np_ptr(x), _np_ptr(out),
+                 C.byref(handled))
         return bool(handled.value)
+
+    def set_cache_capacity(self, nbytes: int) -> None:
+        call("pokit_cuda_linear_backend_set_cache_capacity", self._h, nbytes)
+
+    def forget(self, key: int) -> bool:
+        hit = C.c_int(0)
+        call("pokit_cuda_linear_backend_forget", self._h, key, C.byref(hit))
+        return bool(hit.value)
 
     def stats(self) -> dict:
         s = LinearStats()

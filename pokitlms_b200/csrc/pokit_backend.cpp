@@ -25,6 +25,7 @@
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <list>
 #include <map>
 #include <mutex>
 #include <stdexcept>
@@ -729,7 +730,8 @@ public:
         check(cudaEventCreate(&stop_), "cudaEventCreate");
     }
     ~LinearBackend() {
-        for (auto& kv : cache_) cudaFree(kv.second);
+        for (auto& kv : cache_) cudaFree(kv.second.dev);
+        if (stage_) cudaFree(stage_);
         if (io_) cudaFree(io_);
         if (start_) cudaEventDestroy(start_);
         if (stop_) cudaEventDestroy(stop_);
@@ -738,36 +740,33 @@ public:
     LinearBackend(const LinearBackend&) = delete;
     LinearBackend& operator=(const LinearBackend&) = delete;
 
+    // key == nullptr: the payload is streamed to the device on every call
+    // (the Vulkan backend does the same for readers without a model file,
+    // vulkan_linear.cpp:516-563, 705-714); a host address says nothing about
+    // the bytes behind it once the caller frees and reuses the buffer.
+    // key != nullptr: the caller names the matrix by a stable identity (the
+    // tensor's GGUF file offset, say) and its payload stays in HBM under that
+    // key, least recently used entries evicted beyond the cache capacity.
     bool try_linear(uint32_t type, const void* w, size_t w_bytes, size_t rows, size_t cols,
-                    const float* x, float* y) {
+                    const float* x, float* y, const uint64_t* key) {
         std::lock_guard<std::mutex> lock(mutex_);
         if (failed_) throw std::runtime_error("CUDA linear backend failed earlier: " + failure_);
         if (!type_supported(type)) return false;
-        if (!w || !x || !y || rows == 0 || cols == 0 || cols % block_elems(type) ||
-            rows > UINT32_MAX || cols > UINT32_MAX)
+        if (!x || !y || rows == 0 || cols == 0 || cols % block_elems(type) || rows > UINT32_MAX ||
+            cols > UINT32_MAX)
             throw std::invalid_argument("GGUF matrix dimensions do not match linear input/output");
         if (w_bytes != rows * row_bytes(type, cols))
             throw std::invalid_argument("weight byte size does not match dimensions");
+        if (!w && !(key && cache_.count(*key)))
+            throw std::invalid_argument("weights are required (the key holds no cached payload)");
         DeviceScope scope(device_);
         ++stats_.linear_calls;
-        void* dw = nullptr;
-        const auto key = std::make_pair(w, w_bytes);
-        auto it = cache_.find(key);
-        if (it == cache_.end()) {
-            const uint64_t t0 = now_ns();
-            guard(cudaMalloc(&dw, w_bytes), "cudaMalloc(weights)");
-            cache_.emplace(key, dw);
-            guard(cudaMemcpy(dw, w, w_bytes, cudaMemcpyHostToDevice), "upload");
-            stats_.model_cache_capacity_bytes += w_bytes;
-            stats_.model_cache_uploaded_bytes += w_bytes;
-            stats_.model_cache_upload_time_ns += now_ns() - t0;
-        } else {
-            dw = it->second;
-        }
+        const void* dw = key ? cached_weights(*key, type, w, w_bytes, rows, cols) : streamed_weights(w, w_bytes);
         const size_t need = align256(cols * 4) + align256(rows * 4);
         if (need > io_bytes_) {
             if (io_) cudaFree(io_);
             io_ = nullptr;
+            io_bytes_ = 0;
             guard(cudaMalloc(&io_, need), "cudaMalloc(io)");
             io_bytes_ = need;
         }
@@ -795,12 +794,40 @@ public:
         return true;
     }
 
+    void set_cache_capacity(uint64_t bytes) {
+        std::lock_guard<std::mutex> lock(mutex_);
+        DeviceScope scope(device_);
+        capacity_ = bytes;
+        evict_to(capacity_);
+    }
+
+    bool is_cached(uint64_t key) const {
+        std::lock_guard<std::mutex> lock(mutex_);
+        return cache_.count(key) != 0;
+    }
+
+    bool forget(uint64_t key) {
+        std::lock_guard<std::mutex> lock(mutex_);
+        DeviceScope scope(device_);
+        const auto it = cache_.find(key);
+        if (it == cache_.end()) return false;
+        drop(it);
+        return true;
+    }
+
     pokit_cuda_linear_stats stats() const {
         std::lock_guard<std::mutex> lock(mutex_);
         return stats_;
     }
 
 private:
+    struct Entry {
+        void* dev = nullptr;
+        uint32_t type = 0;
+        size_t bytes = 0, rows = 0, cols = 0;
+        std::list<uint64_t>::iterator lru;
+    };
+
     void guard(cudaError_t e, const char* what) {
         if (e == cudaSuccess) return;
         if (e == cudaErrorInvalidValue)
@@ -810,10 +837,72 @@ private:
         throw std::runtime_error(failure_);
     }
 
+    // One reusable device buffer, refilled from the host payload every call.
+    const void* streamed_weights(const void* w, size_t bytes) {
+        if (bytes > stage_bytes_) {
+            if (stage_) cudaFree(stage_);
+            stage_ = nullptr;
+            stage_bytes_ = 0;
+            guard(cudaMalloc(&stage_, bytes), "cudaMalloc(weight staging)");
+            stage_bytes_ = bytes;
+        }
+        guard(cudaMemcpyAsync(stage_, w, bytes, cudaMemcpyHostToDevice, stream_), "weights h2d");
+        return stage_;
+    }
+
+    const void* cached_weights(uint64_t key, uint32_t type, const void* w, size_t bytes, size_t rows,
+                               size_t cols) {
+        auto it = cache_.find(key);
+        if (it != cache_.end()) {
+            const Entry& e = it->second;
+            if (e.type != type || e.bytes != bytes || e.rows != rows || e.cols != cols)
+                throw std::invalid_argument("weight key was cached for a matrix of another type or shape");
+            lru_.splice(lru_.begin(), lru_, e.lru);
+            return e.dev;
+        }
+        if (bytes > capacity_) return streamed_weights(w, bytes);     // never fits: stream it
+        evict_to(capacity_ - bytes);
+        const uint64_t t0 = now_ns();
+        Entry e;
+        e.type = type;
+        e.bytes = bytes;
+        e.rows = rows;
+        e.cols = cols;
+        guard(cudaMalloc(&e.dev, bytes), "cudaMalloc(weights)");
+        const cudaError_t ce = cudaMemcpy(e.dev, w, bytes, cudaMemcpyHostToDevice);
+        if (ce != cudaSuccess) cudaFree(e.dev);
+        guard(ce, "upload");
+        lru_.push_front(key);
+        e.lru = lru_.begin();
+        cache_.emplace(key, e);
+        resident_ += bytes;
+        stats_.model_cache_capacity_bytes = resident_;
+        stats_.model_cache_uploaded_bytes += bytes;
+        stats_.model_cache_upload_time_ns += now_ns() - t0;
+        return e.dev;
+    }
+
+    void drop(std::map<uint64_t, Entry>::iterator it) {
+        cudaFree(it->second.dev);
+        resident_ -= it->second.bytes;
+        lru_.erase(it->second.lru);
+        cache_.erase(it);
+        stats_.model_cache_capacity_bytes = resident_;
+    }
+
+    void evict_to(uint64_t limit) {
+        while (resident_ > limit && !lru_.empty()) drop(cache_.find(lru_.back()));
+    }
+
     int device_;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t start_ = nullptr, stop_ = nullptr;
-    std::map<std::pair<const void*, size_t>, void*> cache_;
+    std::map<uint64_t, Entry> cache_;
+    std::list<uint64_t> lru_;                       // most recently used first
+    uint64_t resident_ = 0;
+    uint64_t capacity_ = uint64_t(16) << 30;        // bytes of cached payloads
+    void* stage_ = nullptr;
+    size_t stage_bytes_ = 0;
     void* io_ = nullptr;
     size_t io_bytes_ = 0;
     mutable std::mutex mutex_;
@@ -947,7 +1036,47 @@ pokit_cuda_status pokit_cuda_linear_backend_try_linear(
     return guarded(error_buffer, error_capacity, [&] {
         if (!backend || !handled) throw std::invalid_argument("backend and handled flag are required");
         *handled = backend->impl.try_linear(ggml_type, weights_host, weights_bytes, rows, cols,
-                                            input_host, output_host) ? 1 : 0;
+                                            input_host, output_host, nullptr) ? 1 : 0;
+    });
+}
+
+pokit_cuda_status pokit_cuda_linear_backend_try_linear_cached(
+    pokit_cuda_linear_backend* backend, uint64_t weights_key, uint32_t ggml_type, const void* weights_host,
+    size_t weights_bytes, size_t rows, size_t cols, const float* input_host, float* output_host,
+    int* handled, char* error_buffer, size_t error_capacity) {
+    if (handled) *handled = 0;
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!backend || !handled) throw std::invalid_argument("backend and handled flag are required");
+        *handled = backend->impl.try_linear(ggml_type, weights_host, weights_bytes, rows, cols,
+                                            input_host, output_host, &weights_key) ? 1 : 0;
+    });
+}
+
+int pokit_cuda_linear_backend_is_cached(const pokit_cuda_linear_backend* backend, uint64_t weights_key) {
+    if (!backend) return 0;
+    try {
+        return backend->impl.is_cached(weights_key) ? 1 : 0;
+    } catch (...) {
+        return 0;
+    }
+}
+
+pokit_cuda_status pokit_cuda_linear_backend_set_cache_capacity(pokit_cuda_linear_backend* backend,
+                                                               uint64_t capacity_bytes, char* error_buffer,
+                                                               size_t error_capacity) {
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!backend) throw std::invalid_argument("backend is required");
+        backend->impl.set_cache_capacity(capacity_bytes);
+    });
+}
+
+pokit_cuda_status pokit_cuda_linear_backend_forget(pokit_cuda_linear_backend* backend, uint64_t weights_key,
+                                                   int* was_cached, char* error_buffer, size_t error_capacity) {
+    if (was_cached) *was_cached = 0;
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!backend) throw std::invalid_argument("backend is required");
+        const bool hit = backend->impl.forget(weights_key);
+        if (was_cached) *was_cached = hit ? 1 : 0;
     });
 }
 

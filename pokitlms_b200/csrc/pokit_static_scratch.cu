@@ -79,12 +79,13 @@ pokit::MoeLayerDev to_layer(const pokit_cuda_moe_block_device& b) {
         throw std::invalid_argument("router, gate, up and down tensors are required");
     if (!quant_type(b.gate_type) || !quant_type(b.up_type) || !quant_type(b.down_type))
         throw std::invalid_argument("unsupported expert tensor type");
-    // The kernels read the tensors with 16-byte (weights) and 4-byte (router) loads.
+    // Every kernel reads the weights and the routers' rows with 16-byte loads
+    // (TMA boxes, float4), so a misaligned tensor is refused here rather than
+    // faulting on the GPU.
     const auto a16 = [](const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
     if (!a16(b.gate) || !a16(b.up) || !a16(b.down) || !a16(b.shared_gate) || !a16(b.shared_up) ||
-        !a16(b.shared_down) || (reinterpret_cast<uintptr_t>(b.router) & 3u) ||
-        (reinterpret_cast<uintptr_t>(b.shared_router) & 3u))
-        throw std::invalid_argument("expert tensors must be 16-byte aligned and routers 4-byte aligned");
+        !a16(b.shared_down) || !a16(b.router) || !a16(b.shared_router))
+        throw std::invalid_argument("expert tensors and routers must be 16-byte aligned");
     pokit::MoeLayerDev L;
     L.hidden = static_cast<uint32_t>(b.hidden);
     L.inter = static_cast<uint32_t>(b.inter);
@@ -160,9 +161,11 @@ extern "C" pokit_cuda_status pokit_cuda_moe_forward_static_scratch(
         if (route_weights)
             check(cudaMemcpyAsync(route_weights, S.weights, L.top_k * sizeof(float),
                                   cudaMemcpyDeviceToDevice, st), "route weights");
-        check(cudaStreamSynchronize(st), "synchronize");
+        // The status word comes back on the caller's stream, which is the only
+        // thing this call waits for (no legacy-stream copy, no device-wide sync).
         uint32_t status = 0;
-        check(cudaMemcpy(&status, S.status, sizeof status, cudaMemcpyDeviceToHost), "status");
+        check(cudaMemcpyAsync(&status, S.status, sizeof status, cudaMemcpyDeviceToHost, st), "status");
+        check(cudaStreamSynchronize(st), "synchronize");
         if (status & pokit::kStatusNonFiniteLogits)
             throw std::runtime_error("expert router produced non-finite logits");
         if (status) throw std::runtime_error("expert router softmax is invalid");

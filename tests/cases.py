@@ -213,3 +213,16 @@ def route_margin(logits: np.ndarray, k: int) -> float:
     required to match where it exceeds 1e-5)."""
     s = np.sort(np.asarray(logits, dtype=np.float64))[::-1]
     return float(s[k - 1] - s[k]) if k < s.size else float("inf")
+
+
+class MoeShape:
+    """The shape and type fields of a MoE block without its tensors (for
+    argument-validation tests that never reach a kernel)."""
+
+    def __init__(self, hidden, inter, experts, top_k, flavour=0, shared_inter=0,
+                 gate_type=Q4_K, up_type=Q4_K, down_type=Q4_K, normalize=True,
+                 expert_weights_scale=1.0):
+        self.hidden, self.inter, self.experts, self.top_k = hidden, inter, experts, top_k
+        self.flavour, self.shared_inter = flavour, shared_inter
+        self.gate_type, self.up_type, self.down_type = gate_type, up_type, down_type
+        self.normalize, self.expert_weights_scale = normalize, expert_weights_scale

@@ -185,5 +185,52 @@ def test_linear_backend_host_spans(cuda):
     s = be.stats()
     assert s["linear_calls"] == 4 and s["dispatches"] == 4 and s["q4_k_dispatches"] == 3
     assert s["q8_0_dispatches"] == 1
-    assert s["model_cache_uploaded_bytes"] == w.nbytes + w8.nbytes
+    assert s["model_cache_uploaded_bytes"] == 0          # unkeyed calls stream, cache nothing
+    be.close()
+
+
+def test_linear_backend_reused_host_buffer_gets_the_new_weights(cuda):
+    """The caller frees a matrix and the next one of the same size lands at
+    the same host address (gate and up of an expert are both 884,736 B): the
+    second call must see the second matrix's bytes."""
+    be = B.CudaLinearBackend(0)
+    buf = np.empty(768 * 8 * 144, dtype=np.uint8)
+    out = np.empty(768, dtype=np.float32)
+    x = synth.activation(2048, 5)
+    for sid in (11, 12, 13):
+        buf[:] = synth.synth_matrix(cases.Q4_K, 768, 2048, 5, sid)
+        assert be.try_linear(cases.Q4_K, buf, 768, 2048, x, out)
+        assert_close_rms(out, O.linear(cases.Q4_K, x, buf, 768))
+    be.close()
+
+
+def test_linear_backend_keyed_cache(cuda):
+    be = B.CudaLinearBackend(0)
+    w1 = synth.synth_matrix(cases.Q4_K, 256, 1024, 6, 1)
+    w2 = synth.synth_matrix(cases.Q4_K, 256, 1024, 6, 2)
+    x = synth.activation(1024, 6)
+    out = np.empty(256, dtype=np.float32)
+    assert be.try_linear(cases.Q4_K, w1, 256, 1024, x, out, key=1)
+    assert_close_rms(out, O.linear(cases.Q4_K, x, w1, 256))
+    assert be.try_linear(cases.Q4_K, w2, 256, 1024, x, out, key=2)
+    assert_close_rms(out, O.linear(cases.Q4_K, x, w2, 256))
+    s = be.stats()
+    assert s["model_cache_uploaded_bytes"] == 2 * w1.nbytes
+    assert s["model_cache_capacity_bytes"] == 2 * w1.nbytes
+    # A cached key answers from HBM (its host bytes are not read again).
+    assert be.try_linear(cases.Q4_K, w2, 256, 1024, x, out, key=1)
+    assert_close_rms(out, O.linear(cases.Q4_K, x, w1, 256))
+    # forget: the next call with the key uploads the new bytes.
+    assert be.forget(1) and not be.forget(1)
+    assert be.try_linear(cases.Q4_K, w2, 256, 1024, x, out, key=1)
+    assert_close_rms(out, O.linear(cases.Q4_K, x, w2, 256))
+    # A key reused for another shape is refused.
+    with pytest.raises(ValueError):
+        be.try_linear(cases.Q4_K, w1[: 128 * 4 * 144], 128, 1024, x, out[:128], key=2)
+    # Capacity bounds the cache: least recently used entries go first.
+    be.set_cache_capacity(w1.nbytes)
+    assert be.stats()["model_cache_capacity_bytes"] == w1.nbytes
+    be.try_linear(cases.Q4_K, w1, 256, 1024, x, out, key=3)
+    assert be.stats()["model_cache_capacity_bytes"] == w1.nbytes
+    assert_close_rms(out, O.linear(cases.Q4_K, x, w1, 256))
     be.close()
