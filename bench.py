@@ -11,13 +11,17 @@ attention half of each decoder layer is outside this path.
   value   decode tokens/s with inputs resident in HBM (CUDA events, max over ranks)
   e2e     the same through pokit_cuda_moe_decode_layers_host: host hidden in
           (pinned) -> device -> 48 layers -> host hidden out, every step
-  roofline  the dominant kernel, the Q4_K gate/up matvec of one MoE block:
-          14,188,544 algorithmic bytes per launch (8 experts x (gate + up)
-          x 884,736 B + 8 x-fragment records + 8 x 768 act floats out) / its
-          average device time: CUDA events around 4 x 48 back-to-back launches
-          over the 48 layers (pokit_cuda_moe_time_kernel; no expert is
-          L2-resident), taken after the timed region; traffic = DRAM bytes of
-          one launch from the committed ncu summary
+  roofline  the dominant kernel, moe_chain_kernel: the whole 48-layer chain is
+          one cooperative launch per token, so its algorithmic bytes per
+          launch are 48 x 22,298,624 (router + 8 routed experts + in/out per
+          layer) / its average launch duration (CUDA events around launches
+          back to back, after the timed region); traffic = DRAM bytes per
+          layer of the committed ncu capture x 48
+  chain_phases  per-layer phase times of the chain kernel from one traced
+          launch (globaltimer stamps of every CTA); gate_up_* is the in-kernel
+          Q4_K gate/up matvec: 8 experts x (gate + up) x 884,736 B + x' in +
+          act out / the window from the first CTA's routes to the last CTA's
+          gate/up products
   block_roofline  per MoE block: 22,298,624 algorithmic bytes (router 1 MiB +
           8 experts x 2,654,208 B + 16 KiB in/out) / (step time / 48)
 
@@ -64,25 +68,68 @@ EXPERT_BYTES = 3 * 884_736                     # gate + up + down, Q4_K
 ROUTER_BYTES = E * H * 4
 BLOCK_BYTES = ROUTER_BYTES + K_TOP * EXPERT_BYTES + 2 * H * 4
 ROUTED_BYTES = K_TOP * EXPERT_BYTES
-# gate/up kernel: 8 experts x (gate + up) Q4_K + 8 x-fragment records (1088 B)
-# in + 8 x 768 act floats out.
-GATE_UP_BYTES = K_TOP * 2 * 884_736 + (H // 256) * 1088 + K_TOP * I * 4
-TRAFFIC_FILE = ROOT / "profiles" / "gate_up_mma_q4k_h2048_e128_k8.md"
+# gate/up phase: 8 experts x (gate + up) Q4_K + x' (F32 [H]) in + 8 x 768 act
+# floats out.
+GATE_UP_BYTES = K_TOP * 2 * 884_736 + H * 4 + K_TOP * I * 4
+TRAFFIC_FILE = ROOT / "profiles" / "moe_chain_q4k_h2048_e128_k8.md"
+TRAFFIC_SOURCE = ("committed ncu capture (profiles/moe_chain_q4k_h2048_e128_k8.md) of a 4-layer launch, "
+                  "per-layer DRAM bytes x layers")
 METRIC = "decode tokens/sec and routed-expert HBM GB/s (% of peak) at 1/2/4/8 B200"
 WORKLOAD = ("qwen3-30b-a3b-shaped MoE expert path: 48 MoE FFN layers (hidden 2048, 128 experts "
             "top-8 renormalised, inter 768, Q4_K experts, F32 router), decode batch 1")
 
 
-def ncu_traffic_bytes() -> float | None:
-    """DRAM bytes (read + write) of one gate/up launch, from the committed ncu
-    summary (line 'traffic_bytes_per_launch: N')."""
+def ncu_traffic_bytes(layers: int) -> float | None:
+    """DRAM bytes (read + write) of one chain launch over `layers` layers, from
+    the committed ncu summary of a shorter launch (line
+    'traffic_bytes_per_layer: N', scaled by the layer count: every layer
+    streams its own distinct weights)."""
     try:
         for line in TRAFFIC_FILE.read_text().splitlines():
-            if line.strip().startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1])
+            if line.strip().startswith("traffic_bytes_per_layer:"):
+                return float(line.split(":", 1)[1]) * layers
     except OSError:
         pass
     return None
+
+
+def chain_phases(be, layers: int, work, stream) -> dict:
+    """Per-layer phase times of the chain kernel from one traced launch
+    (pokit_cuda_moe_trace_decode; globaltimer stamps of every CTA): medians
+    over the inner layers.  gate_up_us: first CTA's routes ready -> last CTA's
+    gate/up products done (the window in which the layer's 14.2 MB of gate/up
+    weights stream in)."""
+    import torch
+    grid = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    st = torch.zeros(layers * grid * 16, dtype=torch.int64, device="cuda")
+    g = be.trace_decode(0, layers, work, st, stream)
+    torch.cuda.synchronize()
+    ns = st.cpu().numpy().reshape(layers, g, 16)[:, :, :8].astype(np.float64)
+    units = H // 16
+    inner = range(1, layers - 1) if layers > 2 else range(layers)
+    med = lambda v: float(np.median(v)) / 1e3  # noqa: E731
+    return {
+        "layer_us": med([ns[l, :units, 7].max() - ns[l - 1, :units, 7].max() for l in inner if l > 0]) if layers > 1 else None,
+        "route_us": med([ns[l, :, 1].max() - ns[l, :, 0].min() for l in inner]),
+        "gate_up_us": med([ns[l, :, 2].max() - ns[l, :, 1].min() for l in inner]),
+        "act_publish_us": med([ns[l, :, 3].max() - ns[l, :, 2].max() for l in inner]),
+        "down_us": med([ns[l, :units, 7].max() - ns[l, :units, 4].min() for l in inner]),
+        "how": "pokit_cuda_moe_trace_decode: globaltimer stamps per CTA and phase, medians over layers",
+    }
+
+
+def host_cpu() -> dict:
+    """The box's CPU: logical cores and model name (the reference's row
+    executor uses min(6, cores - 1) worker threads, src/tensor_linear.cpp:27)."""
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"host_cores": os.cpu_count(), "cpu_model": model}
 
 
 def measured_peaks() -> dict:
@@ -251,7 +298,7 @@ def run_reference(args) -> None:
         "config": {"workload": WORKLOAD, "layers": LAYERS, "hidden": H, "experts": E,
                    "top_k": K_TOP, "inter": I, "expert_type": "Q4_K"},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind,
-                         "sample": sample},
+                         "sample": sample, **host_cpu()},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }))
@@ -453,7 +500,8 @@ def cpu_config3_rate(target_seconds: float) -> dict:
         if el >= target_seconds:
             break
     return {"value": tokens / el, "unit": "tokens/s", "cores": cores, "kind": kind,
-            "sample": f"{tokens} decode tokens x 48 MoE blocks (2 synthesised layers cycled), {el:.1f} s"}
+            "sample": f"{tokens} decode tokens x 48 MoE blocks (2 synthesised layers cycled), {el:.1f} s",
+            **host_cpu()}
 
 
 def measured_tflops() -> float:
@@ -659,8 +707,10 @@ def main() -> None:
     ap.add_argument("--ep-combine", default="nccl", choices=["peer", "nccl"],
                     help="N > 1: sum the shards' outputs in the block's last kernel over NVLink peer memory "
                          "(peer) or with an NCCL all-reduce (nccl)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "grouped", "config3", "config5"],
-                    help="grouped: only the configuration-4 measurement (one GPU; a small process for "
+    ap.add_argument("--workload", default="decode", choices=["decode", "chain", "grouped", "config3", "config5"],
+                    help="chain: only the decode chain of the headline (one GPU; --layers shortens it; a small "
+                         "process for profiling moe_chain_kernel); "
+                         "grouped: only the configuration-4 measurement (one GPU; a small process for "
                          "profiling the grouped kernels); config3: only the configuration-3 chain (one "
                          "GPU; --layers shortens it); config5: configuration 5 (94 layers, hidden "
                          "4096, batch 64) through the expert-parallel path on 1..N GPUs")
@@ -778,32 +828,43 @@ def main() -> None:
     e2e_s = max_over_ranks(t1 - t0)
     e2e_rate = world * e2e_steps / e2e_s
 
-    # Dominant kernel: gate/up (and down, for the record) launched back to back
-    # over all layers (CUDA events around the run), after the timed region.
-    work_dev = torch.from_numpy(synth.activation(H, SEED + rank, 777)).cuda()
-    reps = max(4 * layers, 96)
-    gate_up_us = be.time_kernel(0, 0, layers, reps, work_dev, stream)
-    down_us = be.time_kernel(1, 0, layers, reps, work_dev, stream)
-    be.synchronize(stream)
-    kernel_us = {"gate_up": gate_up_us, "down": down_us}
+    # Dominant kernel: the decode chain runs as one launch of moe_chain_kernel
+    # per token.  Its average launch duration: CUDA events around launches back
+    # to back (no host copies between them), after the timed region.
+    reps = 50
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    be.decode_layers(0, layers, work, stream)
+    ka.record(stream)
+    for _ in range(reps):
+        be.decode_layers(0, layers, work, stream)
+    kb.record(stream)
+    torch.cuda.synchronize()
+    chain_us = ka.elapsed_time(kb) * 1e3 / reps
+    phases = chain_phases(be, layers, work, stream)
 
     peaks = measured_peaks()
     block_s = ms_per_step / 1e3 / layers
     block_achieved = BLOCK_BYTES / block_s / 1e9
     routed_gbs = ROUTED_BYTES / block_s / 1e9
-    achieved = GATE_UP_BYTES / (gate_up_us / 1e6) / 1e9
+    chain_bytes = BLOCK_BYTES * layers
+    achieved = chain_bytes / (chain_us / 1e6) / 1e9
+    gu = phases["gate_up_us"]
+    phases["gate_up_gbs"] = GATE_UP_BYTES / (gu * 1e-6) / 1e9
+    phases["gate_up_frac"] = phases["gate_up_gbs"] / peaks["hbm_gbs"]
 
-    grouped = measure_grouped(local, stream)
-    config3 = measure_config3(local, stream, steps=max(args.steps // 10, 20),
-                              cpu_seconds=None if (args.no_cpu_baseline or rank != 0) else 6.0)
+    chain_only = args.workload == "chain"
+    grouped = None if chain_only else measure_grouped(local, stream)
+    config3 = None if chain_only else measure_config3(local, stream, steps=max(args.steps // 10, 20),
+                                                      cpu_seconds=None if (args.no_cpu_baseline or rank != 0) else 6.0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, kind, cores, sample = cpu_reference_rate(args.cpu_seconds)
-        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample}
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample, **host_cpu()}
         # One configuration-4 token is one block evaluation of the same shape.
-        grouped["cpu_baseline"] = {"value": v * LAYERS, "unit": "tokens/s", "cores": cores, "kind": kind,
-                                   "sample": sample + "; one config-4 token = one of those block evaluations"}
+        if grouped is not None:
+            grouped["cpu_baseline"] = {"value": v * LAYERS, "unit": "tokens/s", "cores": cores, "kind": kind,
+                                       "sample": sample + "; one config-4 token = one of those block evaluations"}
 
     if rank == 0:
         print(json.dumps({
@@ -817,22 +878,23 @@ def main() -> None:
                        "l2": "no flush: each step streams 1.07 GB of distinct weights (> 126 MB L2)"},
             "routed_expert_gbs": routed_gbs,
             "routed_expert_frac_of_peak": routed_gbs / peaks["hbm_gbs"],
-            "roofline": {"bound": "hbm", "kernel": "moe_gate_up_mma_kernel (Q4_K gate/up matvec)",
+            "roofline": {"bound": "hbm", "kernel": "moe_chain_kernel (48 MoE blocks, one cooperative launch)",
                          "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
-                         "bytes_per_launch": GATE_UP_BYTES, "avg_launch_us": gate_up_us,
-                         "traffic": ncu_traffic_bytes()},
-            "block_roofline": {"bound": "hbm", "kernel": "moe block (2 launches per layer in the chain)",
+                         "bytes_per_launch": chain_bytes, "avg_launch_us": chain_us,
+                         "traffic": ncu_traffic_bytes(layers),
+                         "traffic_source": TRAFFIC_SOURCE},
+            "block_roofline": {"bound": "hbm", "kernel": "moe block (one layer of the chain kernel)",
                                "achieved": block_achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                "frac": block_achieved / peaks["hbm_gbs"], "bytes_per_block": BLOCK_BYTES},
-            "kernel_us": kernel_us,
+            "chain_phases": phases,
             "e2e": {"value": e2e_rate, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
                     "d2h_bytes_per_step": H * 4},
             "gpu_launches": int(gpu_launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
-            "grouped": grouped,
-            "config3": config3,
+            **({"grouped": grouped} if grouped is not None else {}),
+            **({"config3": config3} if config3 is not None else {}),
         }))
     be.close()
 

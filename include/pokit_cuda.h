@@ -398,6 +398,20 @@ pokit_cuda_status pokit_cuda_moe_decode_layers_host(pokit_cuda_moe* moe, size_t 
                                                     float* hidden_out, char* error_buffer,
                                                     size_t error_capacity);
 
+/* Measurement hook (no counterpart in the reference): one
+ * pokit_cuda_moe_decode_layers call through the persistent decode-chain
+ * kernel, which also writes per-phase stamps to `stamps` (device, count x
+ * grid x 16 words: for layer l and CTA c at (l * grid + c) * 16 + i the
+ * globaltimer (ns) and at + 8 + i the SM clock (cycles), i = route wait
+ * done, routes and x records ready, gate/up products done, act published, act
+ * wait done, down records built, down products combined, router partials
+ * published).  *grid receives the
+ * kernel's CTA count.  INVALID_ARGUMENT when the layers do not run the chain
+ * kernel.  Asynchronous. */
+pokit_cuda_status pokit_cuda_moe_trace_decode(pokit_cuda_moe* moe, size_t first, size_t count, float* hidden,
+                                              uint64_t* stamps, size_t stamp_capacity, uint32_t* grid,
+                                              void* stream, char* error_buffer, size_t error_capacity);
+
 /* Waits for the handle's work and reports (then clears) any device-side router
  * failure; a CUDA error is sticky and fails every later call. */
 pokit_cuda_status pokit_cuda_moe_synchronize(pokit_cuda_moe* moe, void* stream,

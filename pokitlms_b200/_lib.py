@@ -161,6 +161,8 @@ SIGNATURES = {
     "pokit_cuda_moe_synchronize": (C.c_int, [_VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_get_stats": (C.c_int, [_VP, C.POINTER(MoeStats)]),
     "pokit_cuda_moe_tensor_bytes": (C.c_size_t, [_VP, _SZ, C.c_uint32]),
+    "pokit_cuda_moe_trace_decode": (C.c_int, [_VP, _SZ, _SZ, _VP, _VP, _SZ, C.POINTER(C.c_uint32), _VP, _ERR,
+                                              _SZ]),
     "pokit_cuda_moe_forward_static_scratch": (C.c_int, [C.POINTER(MoeBlockDevice), _VP, _VP, _VP,
                                                         _VP, _VP, _ERR, _SZ]),
 }

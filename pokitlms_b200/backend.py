@@ -273,6 +273,16 @@ class CudaMoeBackend:
     def decode_layers(self, first: int, count: int, hidden, stream=None) -> None:
         call("pokit_cuda_moe_decode_layers", self._h, first, count, _ptr(hidden), _stream(stream))
 
+    def trace_decode(self, first: int, count: int, hidden, stamps, stream=None) -> int:
+        """One decode_layers call through the chain kernel with per-phase
+        stamps (torch int64 device tensor of count x grid x 16 entries:
+        8 globaltimer readings, then the same 8 points in SM clock cycles);
+        returns the grid size."""
+        grid = C.c_uint32(0)
+        call("pokit_cuda_moe_trace_decode", self._h, first, count, _ptr(hidden), _ptr(stamps), stamps.numel(),
+             C.byref(grid), _stream(stream))
+        return int(grid.value)
+
     def decode_layers_host(self, first: int, count: int, hidden_in: np.ndarray,
                            hidden_out: np.ndarray | None = None) -> np.ndarray:
         hidden_in = np.ascontiguousarray(hidden_in, dtype=np.float32)

@@ -147,9 +147,21 @@ public:
         // kernel boundary costs ~0.6 us on B200, a 148-CTA software grid
         // barrier ~1.3 us).  POKIT_CUDA_DECODE=persistent selects the single
         // cooperative kernel with three grid barriers per layer instead.
+        // Tensor-core layers of one shape run the persistent chain kernel (one
+        // cooperative launch per call, phases handed off through counters);
+        // POKIT_CUDA_DECODE=graph keeps the per-block kernel graph for them.
         const char* mode = std::getenv("POKIT_CUDA_DECODE");
-        const bool want_persistent = mode && std::string(mode) == "persistent";
+        const std::string want = mode ? mode : "";
+        const bool want_persistent = want == "persistent";
         decode_grid_ = want_persistent ? moe_decode_grid(devs_[0]) : 0u;
+        if (!sharded() && !want_persistent && want != "graph" &&
+            moe_chain_plan(devs_.data(), static_cast<uint32_t>(c.layers), &chain_plan_)) {
+            const uint64_t cb = moe_chain_scratch_bytes(devs_[0]);
+            check(cudaMalloc(&chain_scratch_, cb), "cudaMalloc(chain scratch)");
+            check(cudaMemset(chain_scratch_, 0, cb), "cudaMemset(chain scratch)");
+            C_ = moe_chain_scratch_carve(devs_[0], chain_scratch_);
+            chain_ok_ = true;
+        }
         check(cudaMalloc(&io_, align256(c.hidden * 4) * 2), "cudaMalloc(io)");
         check(cudaMallocHost(&pinned_, align256(c.hidden * 4) * 2 + 4096), "cudaMallocHost");
     }
@@ -165,6 +177,7 @@ public:
         if (pinned_) cudaFreeHost(pinned_);
         if (io_) cudaFree(io_);
         if (scratch_) cudaFree(scratch_);
+        if (chain_scratch_) cudaFree(chain_scratch_);
         if (devs_dev_) cudaFree(devs_dev_);
         if (pool_) cudaFree(pool_);
         if (capture_stream_) cudaStreamDestroy(capture_stream_);
@@ -439,6 +452,14 @@ public:
             kernel_launches_ += 1;
             return;
         }
+        if (chain_ok_) {
+            guard(launch_moe_chain(chain_plan_, devs_dev_, static_cast<uint32_t>(first), static_cast<uint32_t>(count),
+                                   S_, C_, hidden, st), "decode chain kernel");
+            forward_calls_ += count;
+            hits_ += count * cfg_.top_k;
+            kernel_launches_ += 1;
+            return;
+        }
         const auto key = std::make_tuple(first, count, hidden);
         auto it = graphs_.find(key);
         if (it == graphs_.end()) {
@@ -466,6 +487,24 @@ public:
         forward_calls_ += count;
         hits_ += count * cfg_.top_k;
         kernel_launches_ += it->second.second;
+    }
+
+    // Measurement: one decode_layers call through the chain kernel with its
+    // per-phase stamps written to `stamps` (device, count * grid * 16 words).
+    uint32_t trace_decode(size_t first, size_t count, float* hidden, unsigned long long* stamps, size_t capacity,
+                          cudaStream_t s) {
+        ensure_ok();
+        if (!chain_ok_) throw std::invalid_argument("the layers do not run the persistent chain kernel");
+        if (count == 0 || first >= cfg_.layers || count > cfg_.layers - first || !hidden || !stamps)
+            throw std::invalid_argument("layer range, hidden state and stamp buffer are required");
+        if (capacity < count * chain_plan_.grid * kChainTraceStamps)
+            throw std::invalid_argument("stamp buffer too small (count x grid x 16 words)");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        guard(launch_moe_chain(chain_plan_, devs_dev_, static_cast<uint32_t>(first), static_cast<uint32_t>(count), S_,
+                               C_, hidden, st, stamps), "decode chain kernel");
+        kernel_launches_ += 1;
+        return chain_plan_.grid;
     }
 
     void decode_layers_host(size_t first, size_t count, const float* in, float* out) {
@@ -690,6 +729,10 @@ private:
     MoeLayerDev* devs_dev_ = nullptr;
     uint32_t decode_grid_ = 0;
     uint32_t barrier_count_ = 0;
+    bool chain_ok_ = false;              // decode_layers runs moe_chain_kernel
+    ChainPlan chain_plan_{};
+    void* chain_scratch_ = nullptr;
+    ChainScratch C_;
     uint64_t scratch_bytes_ = 0;
     MoeScratch S_;
     void* batch_scratch_ = nullptr;   // grouped-path scratch, grown on demand
@@ -1264,6 +1307,20 @@ pokit_cuda_status pokit_cuda_moe_decode_layers_host(pokit_cuda_moe* moe, size_t 
         if (!moe) throw std::invalid_argument("MoE handle is required");
         std::lock_guard<std::mutex> lock(moe->impl.mutex());
         moe->impl.decode_layers_host(first, count, hidden_in, hidden_out);
+    });
+}
+
+pokit_cuda_status pokit_cuda_moe_trace_decode(pokit_cuda_moe* moe, size_t first, size_t count, float* hidden,
+                                              uint64_t* stamps, size_t stamp_capacity, uint32_t* grid, void* stream,
+                                              char* error_buffer, size_t error_capacity) {
+    if (grid) *grid = 0;
+    return guarded(error_buffer, error_capacity, [&] {
+        if (!moe) throw std::invalid_argument("handle is required");
+        std::lock_guard<std::mutex> lock(moe->impl.mutex());
+        const uint32_t g = moe->impl.trace_decode(first, count, hidden,
+                                                  reinterpret_cast<unsigned long long*>(stamps), stamp_capacity,
+                                                  as_stream(stream));
+        if (grid) *grid = g;
     });
 }
 

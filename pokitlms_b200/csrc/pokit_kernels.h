@@ -184,6 +184,49 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
 // marks (one more than stages) receive an event before the first and after
 // each kernel.
 
+// ---------------------------------------------------------------------------
+// Persistent decode chain on the tensor-core path (one cooperative launch per
+// token; see moe_chain_kernel in pokit_moe.cu).
+// ---------------------------------------------------------------------------
+constexpr uint32_t kChainCounterStride = 64;   // uint32 words between the counters (256 B)
+struct ChainScratch {
+    unsigned long long* racc = nullptr;   // [2 parities][experts][8 limbs] router accumulators
+    float* rsq = nullptr;                 // [2][hidden / 16] per-chunk sums of squares
+    uint32_t* rbad = nullptr;             // [2] non-finite partial flags
+    float* xrep = nullptr;                // [kChainXReplicas][hidden] x' = ffn_norm * hidden of the next layer
+    uint32_t* counters = nullptr;         // route, act, exit counters, kChainCounterStride apart
+};
+constexpr uint32_t kChainXReplicas = 8;
+// Bytes of the chain scratch (must be zero before the first launch; every
+// launch leaves it at zero).
+uint64_t moe_chain_scratch_bytes(const MoeLayerDev& shape);
+ChainScratch moe_chain_scratch_carve(const MoeLayerDev& shape, void* base);
+
+// What one launch needs besides the per-call arguments: the 4-D TMA maps over
+// every layer's gate/up/down tensors, the common shape and the grid.
+struct ChainPlan {
+    CUtensorMap tm_gate, tm_up, tm_down;
+    MoeLayerDev shape;
+    uint64_t stride = 0;                  // bytes between consecutive layers' tensors
+    uint32_t layers = 0, grid = 0, smem = 0;
+};
+// Builds the plan for layers[0 .. n) (host copies of the device table) when
+// every layer takes the tensor-core path with one shape, their expert tensors
+// sit at one constant stride per layer, and the chain fits the device's SMs;
+// returns false (and leaves the plan unused) otherwise.
+bool moe_chain_plan(const MoeLayerDev* layers, uint32_t n, ChainPlan* plan);
+// hidden += MoE_l(rms_norm(hidden, ffn_norm_l)) for l in [first, first + count)
+// in one cooperative launch.
+// trace (may be null): [count][grid][16] stamps per layer and CTA, 8
+// globaltimer readings (ns) then the same 8 points in clock64 cycles: route
+// wait done, routes and x records ready, gate/up products done, act
+// published, act wait done, down records built, down products combined,
+// router partials published.
+constexpr uint32_t kChainTraceStamps = 16;
+cudaError_t launch_moe_chain(const ChainPlan& plan, const MoeLayerDev* layers_dev, uint32_t first, uint32_t count,
+                             const MoeScratch& S, const ChainScratch& C, float* hidden, cudaStream_t stream,
+                             unsigned long long* trace = nullptr);
+
 // Grid-wide barriers one layer of launch_moe_decode performs.
 uint32_t moe_barriers_per_layer();
 

@@ -1665,17 +1665,535 @@ __global__ void __maxnreg__(88) moe_down_mma_kernel(const __grid_constant__ MmaA
 }
 
 // ---------------------------------------------------------------------------
-template <typename K>
-cudaError_t ensure_smem(K kernel, size_t bytes, size_t& granted) {
-    if (bytes <= 48u * 1024u || bytes <= granted) return cudaSuccess;
-    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(bytes));
-    if (e == cudaSuccess) granted = bytes;
-    return e;
+// Persistent decode chain (tensor-core path): one cooperative launch carries
+// one token through a range of layers.  Every CTA is resident for the whole
+// launch; the phases of a layer hand off through three monotonic counters
+// instead of kernel boundaries, and each phase issues its weight loads as
+// soon as the routes are known:
+//
+//   route  wait until every D unit of the previous layer (or the prologue)
+//          has added its router partials; then EVERY CTA reads the exact
+//          router accumulators of this layer (parity layer & 1) and the
+//          per-chunk sums of squares, selects the routes in one warp (the
+//          reference's order, route_select_regs) and builds the x' fragment
+//          records of the hidden state in its own shared memory.  No CTA
+//          publishes routes to another: nothing waits on a single tail CTA.
+//   G      CTA c owns gate/up row groups c, c + G, c + 2G of the k * I/16
+//          (slot, 16-row) groups (4 warps each: gate/up x two superblock
+//          halves); its TMA boxes go out right after the selection, together
+//          with its D unit's down boxes (all k slots x I/256 superblocks of
+//          its 16 output rows) and the next layer's router slice (registers).
+//          act = silu(s g) * (s u) to global (rep replicas), then the CTA
+//          arrives on the act counter.
+//   D      CTA c < H/16 owns hidden rows [16c, 16c + 16): it waits for the
+//          act counter (every CTA's G done), builds the activation records,
+//          multiplies its already-landed down boxes, combines the slots in
+//          route order into the residual, and adds the next layer's router
+//          partials for its 16 rows into the other parity's accumulators
+//          before arriving on the route counter.
+//
+// Buffer reuse is ordered by the counters: a CTA zeroes its share of the
+// previous layer's accumulators (every CTA has read them: passing this
+// layer's route wait implies every CTA passed the previous layer's act
+// wait) before its act arrival, and D units add into them only after the
+// act wait.  The last CTA to leave zeroes the accumulators read last and
+// resets the counters, so the next launch finds them at zero.  Every wait
+// is bounded (~2 s): a timeout sets kStatusWaitTimeout (a sticky failure on
+// the host), the CTA drains its in-flight copies and returns.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kChainGroupsPerCta = kWarps / 4;
+constexpr uint32_t kChainStamps = 8;
+
+// The chain kernel's TMA boxes span two superblocks of 16 rows (288 bytes a
+// row, 8-byte elements): half the box count of single-superblock boxes, and
+// the 288-byte row pitch keeps the fragment reads free of bank conflicts.  A
+// pair that runs past the end of a row reads zeros there.
+constexpr uint32_t kPairRowBytes = 288u, kPairBytes = 16u * kPairRowBytes;
+
+struct ChainLayout {
+    uint32_t gbars, dbars, recs, lg, sel_id, sel_w, part, comb, hrow, gtiles, dtiles, total;
+    uint32_t nsb, half_sb, nsd, gpairs, dpairs;
+};
+
+__host__ __device__ inline ChainLayout chain_layout(const MoeLayerDev& L) {
+    ChainLayout c{};
+    const uint32_t nsb = L.hidden >> 8, half = (nsb + 1u) / 2u, nsd = L.inter >> 8, k = L.top_k;
+    c.nsb = nsb;
+    c.half_sb = half;
+    c.nsd = nsd;
+    c.gpairs = (half + 1u) / 2u;
+    c.dpairs = (nsd + 1u) / 2u;
+    uint32_t off = 0;
+    c.gbars = off; off += al16(kWarps * c.gpairs * 8u);
+    c.dbars = off; off += al16(k * c.dpairs * 8u);
+    c.recs = off; off += al16(umax(nsb, k * nsd) * kFragWords * 4u);
+    c.lg = off; off += al16(L.experts * 4u);
+    c.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
+    c.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
+    c.part = off; off += al16(umax(kWarps * 16u, k * nsd * 16u) * 4u);
+    c.comb = off; off += al16(k * 16u * 4u);
+    c.hrow = off; off += al16(2u * kPartRows * 4u);
+    off = al128(off);
+    c.gtiles = off; off += kWarps * c.gpairs * kPairBytes;
+    c.dtiles = off; off += k * c.dpairs * kPairBytes;
+    c.total = off;
+    return c;
 }
 
-size_t g_route_smem = 0, g_gate_up_smem = 0, g_down_smem = 0, g_decode_smem = 0;
-size_t g_gate_up_mma_smem = 0, g_down_mma_smem = 0, g_partials_smem = 0;
+struct ChainArgs {
+    // 4-D tensor maps (byte column, row, expert, layer) over the pool's gate,
+    // up and down tensors of every layer; boxes of 144 bytes x 16 rows.
+    CUtensorMap tm_gate, tm_up, tm_down;
+    const float* router0;        // layer 0's router and ffn_norm; layer l's sit
+    const float* norm0;          // `stride` bytes further per layer
+    uint64_t stride;
+    MoeLayerDev shape;           // the common shape of the layers
+    uint32_t first, count;
+    MoeScratch S;                // ids / weights / logits of the last layer, act replicas, status
+    ChainScratch C;
+    float* hidden;
+    ChainLayout c;
+    // Measurement: when non-null, thread 0 of each CTA stores kChainStamps
+    // globaltimer readings (ns) and then kChainStamps clock64 readings per
+    // layer at [(l * grid + cta) * 2 * kChainStamps + i].
+    unsigned long long* trace;
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void tma_box_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                           uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Thread 0 waits (bounded) until *ctr >= target, then the CTA goes on; false
+// when this or another CTA gave up.
+__device__ bool chain_wait(const uint32_t* ctr, uint32_t target, uint32_t* status, uint32_t* abort_sh) {
+    if (threadIdx.x == 0) {
+        const long long t0 = clock64();
+        uint32_t polls = 0;
+        while (static_cast<int32_t>(ld_acquire_gpu(ctr) - target) < 0) {
+            if ((++polls & 63u) == 0) {
+                if (ld_acquire_gpu(status) & kStatusWaitTimeout) { *abort_sh = 1u; break; }
+                if (clock64() - t0 > kBarrierTimeoutCycles) {
+                    atomicOr(status, kStatusWaitTimeout);
+                    *abort_sh = 1u;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    return *abort_sh == 0u;
+}
+
+// All of the CTA's writes so far become visible before the counter moves.
+__device__ __forceinline__ void chain_arrive(uint32_t* ctr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        red_release_gpu_add(ctr, 1u);
+    }
+}
+
+// Router partial dots of 16 hidden rows (hrow[0..16) = ffn_norm * h, with
+// hrow[16..32) = h^2) into the accumulators `racc` (E x kRaccLimbs) and the
+// chunk's sum of squares into rsq[chunk]; rs holds thread e's router slice.
+__device__ __forceinline__ void chain_partials(const float* router, uint32_t E, const RouterSlice& rs,
+                                               const float* hrow, unsigned long long* racc, uint32_t* rbad, float* rsq,
+                                               uint32_t chunk, uint32_t H) {
+    const uint32_t tid = threadIdx.x;
+    if (tid < E) racc_add(racc + static_cast<uint64_t>(tid) * kRaccLimbs, rbad, router_dot16(rs, hrow));
+    for (uint32_t e = tid + kThreads; e < E; e += kThreads)
+        racc_add(racc + static_cast<uint64_t>(e) * kRaccLimbs, rbad,
+                 router_dot16(router_slice(router, H, e, chunk), hrow));
+    if (tid == 0) {
+        float sq = 0.0f;
+        for (uint32_t r = 0; r < kPartRows; ++r) sq += hrow[kPartRows + r];
+        rsq[chunk] = sq;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_constant__ ChainArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t abort_sh, bad_sh, last_sh;
+    __shared__ float scale_sh;
+    const ChainLayout& c = a.c;
+    const MoeLayerDev& Ls = a.shape;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t G = gridDim.x, cta = blockIdx.x;
+    const uint32_t H = Ls.hidden, I = Ls.inter, E = Ls.experts, k = Ls.top_k;
+    const uint32_t nsb = c.nsb, nsd = c.nsd, half = c.half_sb;
+    const uint32_t per_slot = I / 16u, groups = k * per_slot, units = H / kPartRows;
+    const bool has_unit = cta < units;
+    const uint32_t j0 = cta * kPartRows;
+    uint64_t* gbars = reinterpret_cast<uint64_t*>(smem + c.gbars);
+    uint64_t* dbars = reinterpret_cast<uint64_t*>(smem + c.dbars);
+    uint32_t* recs = reinterpret_cast<uint32_t*>(smem + c.recs);
+    float* lg = reinterpret_cast<float*>(smem + c.lg);
+    uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + c.sel_id);
+    float* sel_w = reinterpret_cast<float*>(smem + c.sel_w);
+    float* part = reinterpret_cast<float*>(smem + c.part);
+    float* comb = reinterpret_cast<float*>(smem + c.comb);
+    float* hrow = reinterpret_cast<float*>(smem + c.hrow);
+    uint8_t* gtiles = smem + c.gtiles;
+    uint8_t* dtiles = smem + c.dtiles;
+    uint32_t* ctr_route = a.C.counters;
+    uint32_t* ctr_act = a.C.counters + kChainCounterStride;
+    uint32_t* ctr_exit = a.C.counters + 2u * kChainCounterStride;
+    uint32_t* status = a.S.status;
+    const uint64_t racc_span = static_cast<uint64_t>(E) * kRaccLimbs;
+    // x' = ffn_norm * hidden of the layer being routed, in kChainXReplicas
+    // copies (CTA c reads copy c % kChainXReplicas).
+    const float* xrep = a.C.xrep + static_cast<uint64_t>(cta % kChainXReplicas) * H;
+    // Layer l's router and ffn_norm sit at a constant stride from layer 0's.
+    const auto router_of = [&](uint32_t layer) {
+        return reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(a.router0) + a.stride * layer);
+    };
+    const auto norm_of = [&](uint32_t layer) {
+        return reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(a.norm0) + a.stride * layer);
+    };
+    const auto stamp = [&](uint32_t l, uint32_t i) {
+        if (a.trace && tid == 0) {
+            unsigned long long* t = a.trace + (static_cast<uint64_t>(l) * G + cta) * (2u * kChainStamps);
+            t[i] = global_ns();
+            t[kChainStamps + i] = static_cast<unsigned long long>(clock64());
+        }
+    };
+
+    if (tid == 0) abort_sh = 0u;
+    const uint32_t gpairs = c.gpairs, dpairs = c.dpairs;
+    if (lane == 0) {
+        for (uint32_t i = 0; i < gpairs; ++i) mbar_init(&gbars[warp * gpairs + i], 1);
+        if (warp == 0)
+            for (uint32_t u = 0; u < k * dpairs; ++u) mbar_init(&dbars[u], 1);
+        mbar_fence_init();
+    }
+    // This CTA's gate/up row group and superblock half per warp (the same
+    // every layer, so an mbarrier's phase flips once per layer it is used).
+    const uint32_t rg = cta + G * static_cast<uint32_t>(warp >> 2);
+    const uint32_t mat = (warp >> 1) & 1, hsel = warp & 1;
+    const uint32_t split = (nsb + 1u) / 2u;
+    const uint32_t sb0 = hsel ? split : 0u, sb1 = hsel ? nsb : split;
+    const uint32_t nmine = (rg < groups && sb1 > sb0) ? sb1 - sb0 : 0u;
+    const uint32_t npairs = (nmine + 1u) / 2u;
+    uint8_t* mytile = gtiles + warp * gpairs * kPairBytes;
+    uint64_t* mybars = gbars + warp * gpairs;
+    const int g = lane >> 2;
+    (void)half;
+
+    // Prologue: the first layer's router partials and x' rows from the input
+    // hidden state.
+    if (has_unit) {
+        if (tid < 16) {
+            const float h = __ldcg(a.hidden + j0 + tid);
+            const float xn = __ldg(norm_of(a.first) + j0 + tid) * h;
+            hrow[tid] = xn;
+            hrow[kPartRows + tid] = h * h;
+            for (uint32_t r = 0; r < kChainXReplicas; ++r) a.C.xrep[static_cast<uint64_t>(r) * H + j0 + tid] = xn;
+        }
+        __syncthreads();
+        RouterSlice rs{};
+        if (static_cast<uint32_t>(tid) < E) rs = router_slice(router_of(a.first), H, tid, cta);
+        const uint32_t p = a.first & 1u;
+        chain_partials(router_of(a.first), E, rs, hrow, a.C.racc + p * racc_span, a.C.rbad + p, a.C.rsq + p * units,
+                       cta, H);
+        chain_arrive(ctr_route);
+    }
+
+    uint32_t phase = 0;
+    bool ok = true;
+    for (uint32_t l = 0; l < a.count && ok; ++l, phase ^= 1u) {
+        const uint32_t layer = a.first + l, p = layer & 1u;
+        const bool has_next = l + 1 < a.count;
+        const uint32_t nlayer = has_next ? layer + 1 : layer;
+        // ---- route ----
+        if (!chain_wait(ctr_route, units * (l + 1u), status, &abort_sh)) { ok = false; break; }
+        stamp(l, 0);
+        const unsigned long long* racc = a.C.racc + p * racc_span;
+        if (warp < static_cast<int>(kTailLogitWarps)) {
+            if (warp == 0) {
+                float sq = 0.0f;
+                for (uint32_t u = lane; u < units; u += 32) sq += __ldcg(a.C.rsq + p * units + u);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                if (lane == 0) {
+                    // rms_norm scale (src/rms_norm.cpp:20-26).
+                    scale_sh = 1.0f / sqrtf(sq / static_cast<float>(H) + Ls.rms_eps);
+                    bad_sh = __ldcg(a.C.rbad + p);
+                }
+            }
+            for (uint32_t e0 = warp * 32u; e0 < E; e0 += kTailLogitWarps * 32u) {
+                const uint32_t e = e0 + lane;
+                if (e < E) {
+                    ulonglong2 limbs[kRaccLimbs / 2];
+                    const ulonglong2* q = reinterpret_cast<const ulonglong2*>(racc + static_cast<uint64_t>(e) * kRaccLimbs);
+#pragma unroll
+                    for (int h2 = 0; h2 < kRaccLimbs / 2; ++h2) limbs[h2] = __ldcg(q + h2);
+                    lg[e] = racc_value(limbs);
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kTailLogitWarps * 32u) : "memory");
+            if (warp == 0) {
+                const float scale = scale_sh;
+                const bool bad = bad_sh != 0u;
+                const auto select = [&](auto slots) {
+                    constexpr uint32_t kSlots = decltype(slots)::value;
+                    float lgv[kSlots];
+#pragma unroll
+                    for (uint32_t i = 0; i < kSlots; ++i) {
+                        const uint32_t e = lane + 32u * i;
+                        lgv[i] = e < E ? (bad ? __int_as_float(0x7fc00000) : lg[e] * scale) : 0.0f;
+                    }
+                    route_select_regs<kSlots>(Ls, lgv, 0.0f, sel_id, sel_w, status, cta == 0, a.S);
+                };
+                if (E <= 128u) select(std::integral_constant<uint32_t, 4>{});
+                else select(std::integral_constant<uint32_t, kRouteWarpMaxSlots>{});
+            }
+        } else {
+            // x' fragment records, one superblock per builder warp.
+            const uint32_t builders = static_cast<uint32_t>(kWarps) - kTailLogitWarps;
+            for (uint32_t q = static_cast<uint32_t>(warp) - kTailLogitWarps; q < nsb; q += builders) {
+                float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
+                float xv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) xv[j] = __ldcg(xrep + q * 256u + 32u * j + lane);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) stage[32 * j + lane] = xv[j];
+                __syncwarp();
+                q4k_frag_superblock(stage, recs + q * kFragWords, lane);
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        stamp(l, 1);
+        const float scale = scale_sh;
+        // ---- G: the gate/up boxes out first ----
+        if (nmine && lane == 0) {
+            const int id = static_cast<int>(sel_id[rg / per_slot]);
+            const int row0 = static_cast<int>((rg % per_slot) * 16u);
+            const CUtensorMap* map = mat ? &a.tm_up : &a.tm_gate;
+            for (uint32_t i = 0; i < npairs; ++i) {
+                mbar_expect_tx(&mybars[i], kPairBytes);
+                tma_box_4d(mytile + i * kPairBytes, map, static_cast<int>((sb0 + 2u * i) * 18u), row0, id,
+                           static_cast<int>(layer), &mybars[i]);
+            }
+        }
+        // The previous layer's accumulators and flag: every CTA has read them.
+        if (l > 0) {
+            for (uint32_t i = cta * kThreads + tid; i < racc_span; i += G * kThreads)
+                a.C.racc[(p ^ 1u) * racc_span + i] = 0ull;
+            if (cta == 0 && tid == 0) a.C.rbad[p ^ 1u] = 0u;
+        }
+        // The next layer's router slice and ffn_norm, this unit's residual rows.
+        RouterSlice rs{};
+        if (has_unit && has_next && static_cast<uint32_t>(tid) < E) rs = router_slice(router_of(nlayer), H, tid, cta);
+        const float resid = (has_unit && tid < 16) ? __ldcg(a.hidden + j0 + tid) : 0.0f;
+        const float nnorm = (has_unit && has_next && tid < 16) ? __ldg(norm_of(nlayer) + j0 + tid) : 0.0f;
+        // ---- G: multiply the boxes as they land ----
+        const auto wait_bar = [&](uint64_t* bar) {
+            if (!mbar_wait(bar, phase)) {
+                if (lane == 0) atomicOr(status, kStatusWaitTimeout);
+                mbar_wait(bar, phase);         // the copy may still land: wait once more
+            }
+        };
+        {
+            float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+            for (uint32_t i = 0; i < npairs; ++i) {
+                wait_bar(&mybars[i]);
+                const uint8_t* bx = mytile + i * kPairBytes;
+                const uint32_t s0 = sb0 + 2u * i;
+                q4k_mma_superblock(bx + g * kPairRowBytes, bx + (g + 8) * kPairRowBytes, recs + s0 * kFragWords, acc0,
+                                   acc1);
+                if (2u * i + 1u < nmine)
+                    q4k_mma_superblock(bx + g * kPairRowBytes + 144u, bx + (g + 8) * kPairRowBytes + 144u,
+                                       recs + (s0 + 1u) * kFragWords, acc2, acc3);
+            }
+            acc0 = quad_sum(acc0 + acc2);
+            acc1 = quad_sum(acc1 + acc3);
+            if ((lane & 3) == 0) {
+                part[warp * 16 + g] = acc0;
+                part[warp * 16 + g + 8] = acc1;
+            }
+        }
+        // The down boxes go out once this warp's gate/up boxes are in, so they
+        // do not compete with them for DRAM bandwidth (needed after the act wait).
+        if (has_unit && static_cast<uint32_t>(warp) < k && lane == 0) {
+            const int id = static_cast<int>(sel_id[warp]);
+            for (uint32_t j = 0; j < dpairs; ++j) {
+                const uint32_t u = warp * dpairs + j;
+                mbar_expect_tx(&dbars[u], kPairBytes);
+                tma_box_4d(dtiles + u * kPairBytes, &a.tm_down, static_cast<int>(j * 36u), static_cast<int>(j0), id,
+                           static_cast<int>(layer), &dbars[u]);
+            }
+        }
+        __syncthreads();
+        stamp(l, 2);
+        if (tid < static_cast<int>(kChainGroupsPerCta * 16u)) {
+            const uint32_t gl = tid >> 4, r = tid & 15, rgx = cta + G * gl;
+            if (rgx < groups) {
+                const float gv = part[(gl * 4 + 0) * 16 + r] + part[(gl * 4 + 1) * 16 + r];
+                const float uv = part[(gl * 4 + 2) * 16 + r] + part[(gl * 4 + 3) * 16 + r];
+                const uint32_t slot = rgx / per_slot, row = (rgx % per_slot) * 16u + r;
+                const float av = silu_mul(gv * scale, uv * scale, Ls.flavour);
+                for (uint32_t cp = 0; cp < a.S.rep; ++cp)
+                    a.S.actr[static_cast<uint64_t>(cp) * k * I + slot * I + row] = av;
+            }
+        }
+        chain_arrive(ctr_act);
+        stamp(l, 3);
+        if (!has_unit) continue;
+        // ---- D ----
+        if (!chain_wait(ctr_act, G * (l + 1u), status, &abort_sh)) {
+            if (static_cast<uint32_t>(warp) < k && lane == 0)
+                for (uint32_t j = 0; j < dpairs; ++j) mbar_wait(&dbars[warp * dpairs + j], phase);
+            ok = false;
+            break;
+        }
+        stamp(l, 4);
+        {
+            const float* act = a.S.actr + static_cast<uint64_t>(cta % a.S.rep) * k * I;
+            const uint32_t nrec = k * nsd;
+            // Two records per warp per pass, all of their loads in flight together.
+            for (uint32_t q0 = warp; q0 < nrec; q0 += 2 * kWarps) {
+                float v[2][8];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t q = q0 + i * kWarps;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        v[i][j] = q < nrec ? __ldcg(act + static_cast<uint64_t>(q) * 256u + 32 * j + lane) : 0.0f;
+                }
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t q = q0 + i * kWarps;
+                    if (q < nrec) {
+                        float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = v[i][j];
+                    }
+                }
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t q = q0 + i * kWarps;
+                    if (q < nrec)
+                        q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords, lane);
+                }
+            }
+            __syncthreads();
+            stamp(l, 5);
+            for (uint32_t u = warp; u < nrec; u += 2 * kWarps) {
+                const uint32_t v2 = u + kWarps;
+                float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+                // Unit (slot, sb) lives in pair box slot * dpairs + sb / 2.
+                const auto unit_box = [&](uint32_t q) {
+                    const uint32_t sl = q / nsd, sb = q % nsd, bi = sl * dpairs + (sb >> 1);
+                    wait_bar(&dbars[bi]);
+                    return dtiles + bi * kPairBytes + (sb & 1u) * 144u;
+                };
+                const uint8_t* bx = unit_box(u);
+                q4k_mma_superblock(bx + g * kPairRowBytes, bx + (g + 8) * kPairRowBytes, recs + u * kFragWords, a0, a1);
+                if (v2 < nrec) {
+                    const uint8_t* by = unit_box(v2);
+                    q4k_mma_superblock(by + g * kPairRowBytes, by + (g + 8) * kPairRowBytes, recs + v2 * kFragWords,
+                                       b0, b1);
+                }
+                a0 = quad_sum(a0);
+                a1 = quad_sum(a1);
+                b0 = quad_sum(b0);
+                b1 = quad_sum(b1);
+                if ((lane & 3) == 0) {
+                    part[u * 16 + g] = a0;
+                    part[u * 16 + g + 8] = a1;
+                    if (v2 < nrec) {
+                        part[v2 * 16 + g] = b0;
+                        part[v2 * 16 + g + 8] = b1;
+                    }
+                }
+            }
+            __syncthreads();
+            // Weighted slot rows, then the sum over slots in route order.
+            for (uint32_t t = tid; t < 16u * k; t += kThreads) {
+                const uint32_t row = t & 15u, sl = t >> 4;
+                float y = 0.0f;
+                for (uint32_t sb = 0; sb < nsd; ++sb) y += part[(sl * nsd + sb) * 16 + row];
+                comb[sl * 16 + row] = sel_w[sl] * y;
+            }
+            __syncthreads();
+            stamp(l, 6);
+            if (tid < 16) {
+                float acc = 0.0f;
+                for (uint32_t sl = 0; sl < k; ++sl) acc += comb[sl * 16 + tid];
+                const float h = resid + acc;
+                a.hidden[j0 + tid] = h;
+                if (has_next) {
+                    const float xn = nnorm * h;
+                    hrow[tid] = xn;
+                    hrow[kPartRows + tid] = h * h;
+                    for (uint32_t r = 0; r < kChainXReplicas; ++r)
+                        a.C.xrep[static_cast<uint64_t>(r) * H + j0 + tid] = xn;
+                }
+            }
+            if (has_next) {
+                __syncthreads();
+                chain_partials(router_of(nlayer), E, rs, hrow, a.C.racc + (p ^ 1u) * racc_span, a.C.rbad + (p ^ 1u),
+                               a.C.rsq + (p ^ 1u) * units, cta, H);
+            }
+        }
+        chain_arrive(ctr_route);
+        stamp(l, 7);
+    }
+    if (!ok) return;
+    // The last CTA out leaves the accumulators and counters at zero.
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        last_sh = atomicAdd(ctr_exit, 1u) == G - 1u ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!last_sh) return;
+    __threadfence();
+    const uint32_t plast = (a.first + a.count - 1u) & 1u;
+    for (uint32_t i = tid; i < racc_span; i += kThreads) a.C.racc[plast * racc_span + i] = 0ull;
+    __syncthreads();
+    if (tid == 0) {
+        a.C.rbad[plast] = 0u;
+        *ctr_route = 0u;
+        *ctr_act = 0u;
+        *ctr_exit = 0u;
+        __threadfence();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device):
+// cudaFuncSetAttribute applies to the current device only, so a grant made
+// on one GPU says nothing about another.  Later launches skip the call, so
+// they can be captured in graphs.
+template <typename K>
+cudaError_t ensure_smem(K kernel, size_t bytes) {
+    if (bytes <= 48u * 1024u) return cudaSuccess;
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> granted;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& have = granted[{reinterpret_cast<const void*>(kernel), dev}];
+    if (bytes <= have) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess) have = bytes;
+    return e;
+}
 
 uint64_t align256(uint64_t v) { return (v + 255u) & ~uint64_t(255); }
 
@@ -1796,6 +2314,11 @@ bool encode_expert_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
+    // Callers of the handle-free entry pass their own tensors, so the key set
+    // is open-ended: the cache is dropped whole once it holds kMaxMaps maps
+    // (an encode is a host computation of about a microsecond).
+    constexpr size_t kMaxMaps = 4096;
+    if (cache.size() >= kMaxMaps) cache.clear();
     cache.emplace(key, *map);
     return true;
 }
@@ -1837,9 +2360,9 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
         MmaLayout pl{};
         pl.tail = tail_layout(L, 0);
         pl.total = pl.tail.end;
-        cudaError_t e = ensure_smem(moe_gate_up_mma_kernel, gl.total, g_gate_up_mma_smem);
-        if (e == cudaSuccess) e = ensure_smem(moe_down_mma_kernel, dl.total, g_down_mma_smem);
-        if (e == cudaSuccess) e = ensure_smem(moe_partials_kernel, pl.total, g_partials_smem);
+        cudaError_t e = ensure_smem(moe_gate_up_mma_kernel, gl.total);
+        if (e == cudaSuccess) e = ensure_smem(moe_down_mma_kernel, dl.total);
+        if (e == cudaSuccess) e = ensure_smem(moe_partials_kernel, pl.total);
         if (e != cudaSuccess || dry_run) return e;
         MmaArgs ma{};
         const uint64_t rb_in = static_cast<uint64_t>(L.hidden >> 8) * 144u;
@@ -1916,9 +2439,9 @@ static cudaError_t block_impl(const MoeLayerDev& L, const MoeScratch& S, const f
     const SmemLayout rl = route_layout(L);
     a.m = make_layout(L, down_ctas);
     if (a.m.total > 227u * 1024u || rl.total > 227u * 1024u) return cudaErrorInvalidValue;
-    cudaError_t e = ensure_smem(moe_route_kernel, rl.total, g_route_smem);
-    if (e == cudaSuccess) e = ensure_smem(moe_gate_up_kernel, a.m.total, g_gate_up_smem);
-    if (e == cudaSuccess) e = ensure_smem(moe_down_kernel, a.m.total, g_down_smem);
+    cudaError_t e = ensure_smem(moe_route_kernel, rl.total);
+    if (e == cudaSuccess) e = ensure_smem(moe_gate_up_kernel, a.m.total);
+    if (e == cudaSuccess) e = ensure_smem(moe_down_kernel, a.m.total);
     if (e != cudaSuccess || dry_run) return e;
     BlockArgs ra = a;
     ra.m = rl;
@@ -2020,6 +2543,122 @@ cudaError_t time_moe_kernel(const MoeLayerDev* layers, uint32_t count, const Moe
     return e;
 }
 
+uint64_t moe_chain_scratch_bytes(const MoeLayerDev& L) {
+    return align256(2ull * L.experts * kRaccLimbs * 8u) + align256(2ull * (L.hidden / kPartRows) * 4u) +
+           align256(2u * 4u) + align256(static_cast<uint64_t>(kChainXReplicas) * L.hidden * 4u) +
+           3u * kChainCounterStride * 4u;
+}
+
+ChainScratch moe_chain_scratch_carve(const MoeLayerDev& L, void* base) {
+    uint8_t* p = static_cast<uint8_t*>(base);
+    ChainScratch c;
+    c.racc = reinterpret_cast<unsigned long long*>(p); p += align256(2ull * L.experts * kRaccLimbs * 8u);
+    c.rsq = reinterpret_cast<float*>(p); p += align256(2ull * (L.hidden / kPartRows) * 4u);
+    c.rbad = reinterpret_cast<uint32_t*>(p); p += align256(2u * 4u);
+    c.xrep = reinterpret_cast<float*>(p); p += align256(static_cast<uint64_t>(kChainXReplicas) * L.hidden * 4u);
+    c.counters = reinterpret_cast<uint32_t*>(p);
+    return c;
+}
+
+// (8-byte column, row, expert, layer) view of one Q4_K tensor kind across
+// the layers of a pool: `rows` rows of `row_bytes` per expert, experts
+// `slice` bytes apart, layers `layer_stride` bytes apart; boxes of two
+// superblocks (288 bytes) by 16 rows.
+static bool encode_pool_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows,
+                            uint64_t experts, uint64_t slice, uint64_t layers, uint64_t layer_stride) {
+    const auto encode = tensor_map_encoder();
+    if (!encode || (reinterpret_cast<uintptr_t>(base) & 15u) || (row_bytes & 15u) || (slice & 15u) ||
+        (layer_stride & 15u))
+        return false;
+    if (row_bytes % 8u) return false;
+    const cuuint64_t dims[4] = {row_bytes / 8u, rows, experts, layers};
+    const cuuint64_t strides[3] = {row_bytes, slice, layers > 1 ? layer_stride : slice * experts};
+    const cuuint32_t box[4] = {kPairRowBytes / 8u, kBoxRows, 1u, 1u};
+    const cuuint32_t elem[4] = {1u, 1u, 1u, 1u};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 4, const_cast<uint8_t*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool moe_chain_plan(const MoeLayerDev* layers, uint32_t n, ChainPlan* plan) {
+    if (!layers || n == 0 || !plan) return false;
+    const MoeLayerDev& L0 = layers[0];
+    if (!layer_valid(L0) || !tensor_path(L0) || !L0.ffn_norm || L0.expert_local != 0 && L0.expert_local != L0.experts)
+        return false;
+    const int64_t stride = n > 1 ? layers[1].gate - layers[0].gate : 0;
+    for (uint32_t l = 0; l < n; ++l) {
+        const MoeLayerDev& L = layers[l];
+        const auto at = [&](const void* q, const void* q0) {
+            return static_cast<const uint8_t*>(q) - static_cast<const uint8_t*>(q0) == stride * l;
+        };
+        if (!tensor_path(L) || !L.ffn_norm || !L.router || L.hidden != L0.hidden || L.inter != L0.inter ||
+            L.experts != L0.experts || L.top_k != L0.top_k || L.flavour != L0.flavour ||
+            L.normalize != L0.normalize || L.expert_weights_scale != L0.expert_weights_scale ||
+            L.rms_eps != L0.rms_eps || L.gate_slice != L0.gate_slice || L.up_slice != L0.up_slice ||
+            L.down_slice != L0.down_slice || !at(L.gate, L0.gate) || !at(L.up, L0.up) || !at(L.down, L0.down) ||
+            !at(L.router, L0.router) || !at(L.ffn_norm, L0.ffn_norm) || (reinterpret_cast<uintptr_t>(L.router) & 15u))
+            return false;
+    }
+    if (stride < 0) return false;
+    const uint32_t sms = static_cast<uint32_t>(device_sm_count());
+    const uint32_t units = L0.hidden / kPartRows, groups = L0.top_k * (L0.inter / 16u);
+    const ChainLayout c = chain_layout(L0);
+    if (units > sms || groups > kChainGroupsPerCta * sms || L0.experts > kThreads ||
+        c.total > 227u * 1024u || (L0.hidden >> 8) > 64u)
+        return false;
+    if (ensure_smem(moe_chain_kernel, c.total) != cudaSuccess) return false;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_chain_kernel, kThreads, c.total) != cudaSuccess ||
+        per_sm < 1)
+        return false;
+    const uint64_t rb_in = static_cast<uint64_t>(L0.hidden >> 8) * 144u;
+    const uint64_t rb_down = static_cast<uint64_t>(L0.inter >> 8) * 144u;
+    if (!encode_pool_map(&plan->tm_gate, L0.gate, rb_in, L0.inter, L0.experts, L0.gate_slice, n, stride) ||
+        !encode_pool_map(&plan->tm_up, L0.up, rb_in, L0.inter, L0.experts, L0.up_slice, n, stride) ||
+        !encode_pool_map(&plan->tm_down, L0.down, rb_down, L0.hidden, L0.experts, L0.down_slice, n, stride))
+        return false;
+    plan->shape = L0;
+    plan->stride = static_cast<uint64_t>(stride);
+    plan->layers = n;
+    plan->grid = sms;
+    plan->smem = c.total;
+    return true;
+}
+
+cudaError_t launch_moe_chain(const ChainPlan& plan, const MoeLayerDev* layers_dev, uint32_t first, uint32_t count,
+                             const MoeScratch& S, const ChainScratch& C, float* hidden, cudaStream_t stream,
+                             unsigned long long* trace) {
+    (void)layers_dev;
+    if (!hidden || count == 0 || first >= plan.layers || count > plan.layers - first || plan.grid == 0)
+        return cudaErrorInvalidValue;
+    ChainArgs a{};
+    a.tm_gate = plan.tm_gate;
+    a.tm_up = plan.tm_up;
+    a.tm_down = plan.tm_down;
+    a.router0 = plan.shape.router;
+    a.norm0 = plan.shape.ffn_norm;
+    a.stride = plan.stride;
+    a.shape = plan.shape;
+    a.first = first;
+    a.count = count;
+    a.S = S;
+    a.C = C;
+    a.hidden = hidden;
+    a.c = chain_layout(plan.shape);
+    a.trace = trace;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, moe_chain_kernel, a);
+}
+
 cudaError_t prepare_moe_block(const MoeLayerDev& L) {
     MoeScratch none;
     float dummy = 0.0f;
@@ -2027,7 +2666,7 @@ cudaError_t prepare_moe_block(const MoeLayerDev& L) {
     if (e != cudaSuccess) return e;
     const SmemLayout m = make_layout(L, static_cast<uint32_t>(device_sm_count()));
     if (m.total > 227u * 1024u) return cudaErrorInvalidValue;
-    return ensure_smem(moe_decode_kernel, m.total, g_decode_smem);
+    return ensure_smem(moe_decode_kernel, m.total);
 }
 
 uint32_t moe_decode_grid(const MoeLayerDev& L) {
@@ -2053,7 +2692,7 @@ cudaError_t launch_moe_decode(const MoeLayerDev* layers_dev, const MoeLayerDev& 
     a.m = make_layout(shape, grid);
     a.barrier_base = barrier_base;
     if (a.m.total > 227u * 1024u) return cudaErrorInvalidValue;
-    cudaError_t e = ensure_smem(moe_decode_kernel, a.m.total, g_decode_smem);
+    cudaError_t e = ensure_smem(moe_decode_kernel, a.m.total);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);

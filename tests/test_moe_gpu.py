@@ -211,11 +211,22 @@ def test_upload_validation(cuda):
     be.close()
 
 
+def _device_synth(ggml_type, rows, cols, seed, sid):
+    """Host copy of a tensor from the on-device generator (byte-identical to
+    the host generator, tests/test_synth.py), without the host generator's cost."""
+    nblocks = rows * (cols // 256)
+    buf = torch.empty(nblocks * 144, dtype=torch.uint8, device="cuda")
+    B.synthesize_blocks(ggml_type, seed, sid, nblocks, buf)
+    torch.cuda.synchronize()
+    return buf.cpu().numpy()
+
+
 def test_full_size_decode_chain_on_device_synthesis(cuda):
     """Config 2 MoE path: 48 layers x 128 experts synthesised in HBM (16.3 GB).
-    Size-independent checks at full size: every layer's pool bytes equal the
-    host generator's (spot-checked), the 48-layer chain is finite and
-    deterministic, and its first two layers match the oracle."""
+    At full size: the 48-layer chain is finite and deterministic, equals the
+    same 48 layers run one call per layer, and every layer's output matches
+    the oracle's block evaluated on the same input hidden state."""
+    from oracle.oracle import MoeLayer
     layers, H, I, E, k = 48, 2048, 768, 128, 8
     be = B.CudaMoeBackend(layers=layers, hidden=H, inter=I, experts=E, top_k=k, rms_epsilon=1e-6)
     for l in range(layers):
@@ -227,10 +238,51 @@ def test_full_size_decode_chain_on_device_synthesis(cuda):
     out1 = be.decode_layers_host(0, layers, h0)
     out2 = be.decode_layers_host(0, layers, h0)
     assert np.all(np.isfinite(out1)) and np.array_equal(out1, out2)
-    two = be.decode_layers_host(0, 2, h0)
-    ref_layers = [cases.moe_layer(seed=0, layer=l, with_norm=True) for l in range(2)]
-    ref = O.decode_layers(ref_layers, h0, 1e-6)
-    assert_moe_close(two, ref)
+    h = h0.copy()
+    ones = np.ones(H, np.float32)
+    for l in range(layers):
+        nxt = be.decode_layers_host(l, 1, h)
+        L = MoeLayer(hidden=H, inter=I, experts=E, top_k=k, router=synth.router_weights(E, H, 0, l),
+                     gate=_device_synth(cases.Q4_K, E * I, H, 0, synth.stream_id(l, GATE)),
+                     up=_device_synth(cases.Q4_K, E * I, H, 0, synth.stream_id(l, UP)),
+                     down=_device_synth(cases.Q4_K, E * H, I, 0, synth.stream_id(l, DOWN)),
+                     flavour=0, normalize=True, ffn_norm=ones)
+        ref = O.decode_layers([L], h, 1e-6)
+        # The layer's own contribution, against its RMS (the residual is exact).
+        assert_moe_close(nxt - h, ref.astype(np.float64) - h)
+        h = nxt
+    assert np.array_equal(h, out1)
     s = be.stats()
     assert s["capacity_bytes"] >= layers * E * (2 * 884736 + 884736)
     be.close()
+
+
+def test_decode_chain_kernel_matches_the_block_graph(cuda, monkeypatch):
+    """Tensor-core layers of one shape decode in one persistent launch per
+    call; the per-block kernel graph (POKIT_CUDA_DECODE=graph) gives the same
+    hidden states, as do sub-ranges starting on either layer parity and
+    repeated calls (the launch leaves its counters and accumulators at zero)."""
+    layers = [cases.moe_layer(hidden=2048, inter=768, experts=64, top_k=8, seed=8, layer=l,
+                              with_norm=True) for l in range(5)]
+    chain = make_backend(layers[0], layers=5, rms_epsilon=1e-6)
+    monkeypatch.setenv("POKIT_CUDA_DECODE", "graph")
+    graph = make_backend(layers[0], layers=5, rms_epsilon=1e-6)
+    monkeypatch.delenv("POKIT_CUDA_DECODE")
+    for l, L in enumerate(layers):
+        upload(chain, l, L)
+        upload(graph, l, L)
+    for i in range(3):
+        h0 = synth.activation(2048, 8, i)
+        n0 = chain.stats()["kernel_launches"]
+        a = chain.decode_layers_host(0, 5, h0)
+        assert chain.stats()["kernel_launches"] - n0 == 1
+        b = graph.decode_layers_host(0, 5, h0)
+        assert_moe_close(a - h0, b.astype(np.float64) - h0)
+        ref = O.decode_layers(layers, h0, 1e-6)
+        assert_moe_close(a - h0, ref.astype(np.float64) - h0)
+        mid = chain.decode_layers_host(1, 3, h0)          # odd first layer
+        assert_moe_close(mid - h0, O.decode_layers(layers[1:4], h0, 1e-6).astype(np.float64) - h0)
+        one = chain.decode_layers_host(4, 1, h0)
+        assert_moe_close(one - h0, O.decode_layers(layers[4:], h0, 1e-6).astype(np.float64) - h0)
+    chain.close()
+    graph.close()
