@@ -504,6 +504,64 @@ def cpu_config3_rate(target_seconds: float) -> dict:
             **host_cpu()}
 
 
+# Configuration 2 end to end: bytes one decoded token streams (experts and routers of 48
+# layers, the attention projections, the LM head and one embedding row).
+def decoder_token_bytes(shape) -> int:
+    H, L = shape.hidden, shape.layers
+    qd, kd = shape.q_heads * shape.head_dim, shape.kv_heads * shape.head_dim
+    q4 = lambda rows, cols: rows * (cols // 256) * 144          # noqa: E731
+    q6 = lambda rows, cols: rows * (cols // 256) * 210          # noqa: E731
+    attn = q4(qd + 2 * kd, H) + q4(H, qd)
+    experts = shape.top_k * (2 * q4(shape.expert_inter, H) + q4(H, shape.expert_inter))
+    router = shape.experts * H * 4
+    return L * (attn + experts + router) + q6(shape.vocab, H) + q6(1, H)
+
+
+def measure_decoder(device: int, stream, new_tokens: int = 128, layers: int = 48) -> dict:
+    """Benchmark configuration 2 end to end: the whole synthetic Qwen3-30B-A3B-shaped
+    decoder (48 layers, GQA 32/4 x 128, RoPE theta 1e6, FP16 KV ring, MoE 128 experts
+    top-8, Q4_K experts and attention, Q6_K embedding and LM head, vocabulary 151,936),
+    weights synthesised in HBM from seed 0, greedy decoding of `new_tokens` tokens after a
+    32-token uniform-random prompt through pokit_cuda_decoder_generate_tokens (the
+    reference's metric: generated tokens / decode time, host wall clock)."""
+    import torch
+    from pokitlms_b200 import backend as B
+    from pokitlms_b200 import gguf
+    shape = gguf.Qwen3MoeShape(layers=layers)
+    dec = B.CudaDecoder(shape, device=device)
+    dec.synthesize_model()
+    prompt = np.random.default_rng([0, 0x7072]).integers(0, shape.vocab, 32)
+    dec.generate_tokens(prompt, 8)                                   # warm-up, graphs captured
+    ids, st = dec.generate_tokens(prompt, new_tokens)
+    e2e = st["generated_tokens"] / (st["decode_time_ns"] * 1e-9)
+    # Device-resident: token steps back to back (each samples the next on the device).
+    dec.generate_tokens(prompt, 1)
+    steps = min(new_tokens, shape.context - 40)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    dec.run_steps(steps, stream)
+    b.record(stream)
+    torch.cuda.synchronize()
+    step_us = a.elapsed_time(b) * 1e3 / steps
+    launches = dec.launches_per_step()
+    dec.close()
+    peaks = measured_peaks()
+    tb = decoder_token_bytes(shape)
+    gbs = tb / (step_us * 1e-6) / 1e9
+    return {
+        "workload": (f"benchmark configuration 2 end to end: {layers}-layer synthetic Qwen3-30B-A3B-shaped decoder "
+                     "(attention + MoE + Q6_K LM head over vocabulary 151,936), 32-token prompt, greedy decode"),
+        "value": 1e6 / step_us, "unit": "tokens/s", "us_per_token": step_us,
+        "e2e": {"value": e2e, "unit": "tokens/s", "generated": int(st["generated_tokens"]),
+                "how": "pokit_cuda_decoder_generate_tokens: generated tokens / decode time (host clock), "
+                       "prompt ids in, generated ids out", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4},
+        "hbm": {"bytes_per_token": tb, "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"],
+                "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]},
+        "gpu_launches_per_token": int(launches),
+        "first_ids": [int(i) for i in ids[:8]],
+    }
+
+
 def measured_tflops() -> float:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -707,8 +765,9 @@ def main() -> None:
     ap.add_argument("--ep-combine", default="nccl", choices=["peer", "nccl"],
                     help="N > 1: sum the shards' outputs in the block's last kernel over NVLink peer memory "
                          "(peer) or with an NCCL all-reduce (nccl)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "chain", "grouped", "config3", "config5"],
-                    help="chain: only the decode chain of the headline (one GPU; --layers shortens it; a small "
+    ap.add_argument("--workload", default="decode", choices=["decode", "chain", "decoder", "grouped", "config3", "config5"],
+                    help="decoder: only configuration 2's whole decoder (one GPU; --layers shortens it); "
+                         "chain: only the decode chain of the headline (one GPU; --layers shortens it; a small "
                          "process for profiling moe_chain_kernel); "
                          "grouped: only the configuration-4 measurement (one GPU; a small process for "
                          "profiling the grouped kernels); config3: only the configuration-3 chain (one "
@@ -750,6 +809,14 @@ def main() -> None:
         if rank == 0:
             print(json.dumps({"metric": "configuration-4 grouped-expert batch tokens/s", "n_gpus": 1,
                               **measure_grouped(local, torch.cuda.current_stream())}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    if args.workload == "decoder":
+        if rank == 0:
+            print(json.dumps({"metric": "configuration-2 decoder tokens/s", "n_gpus": 1,
+                              **measure_decoder(local, torch.cuda.current_stream(),
+                                                layers=args.layers)}))
         if world > 1:
             dist.destroy_process_group()
         return
@@ -853,6 +920,7 @@ def main() -> None:
     phases["gate_up_frac"] = phases["gate_up_gbs"] / peaks["hbm_gbs"]
 
     chain_only = args.workload == "chain"
+    decoder = None if chain_only else measure_decoder(local, stream)
     grouped = None if chain_only else measure_grouped(local, stream)
     config3 = None if chain_only else measure_config3(local, stream, steps=max(args.steps // 10, 20),
                                                       cpu_seconds=None if (args.no_cpu_baseline or rank != 0) else 6.0)
@@ -893,6 +961,7 @@ def main() -> None:
             "gpu_launches": int(gpu_launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
+            **({"decoder": decoder} if decoder is not None else {}),
             **({"grouped": grouped} if grouped is not None else {}),
             **({"config3": config3} if config3 is not None else {}),
         }))

@@ -425,6 +425,111 @@ pokit_cuda_status pokit_cuda_moe_get_stats(const pokit_cuda_moe* moe,
 size_t pokit_cuda_moe_tensor_bytes(const pokit_cuda_moe* moe, size_t layer, uint32_t tensor);
 
 /* ------------------------------------------------------------------------ */
+/* The whole Qwen3-MoE decoder of one sequence                              */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces Qwen3MoeRunner (include/pokitlms/model/qwen3_moe_runner.hpp:56-101)
+ * for greedy decoding on one GPU: token embedding, per layer RMSNorm -> Q/K/V
+ * projections -> per-head Q/K RMSNorm -> rotate-half RoPE -> FP16 ring KV cache
+ * -> GQA attention -> output projection + residual -> the MoE block, then the
+ * final RMSNorm, the LM head and the argmax (src/qwen3_moe_runner.cpp:580-704,
+ * 751-821).  Every weight is resident in HBM; the MoE tensors (router,
+ * ffn_norm, experts) live in the handle returned by pokit_cuda_decoder_moe and
+ * are uploaded or synthesised with the pokit_cuda_moe_* calls. */
+typedef struct pokit_cuda_decoder pokit_cuda_decoder;
+
+typedef struct pokit_cuda_decoder_config {
+    int device;
+    size_t layers;                    /* block_count */
+    size_t hidden;                    /* embedding_length, multiple of 256 */
+    size_t vocab;                     /* tokenizer vocabulary size */
+    size_t q_heads, kv_heads;         /* attention.head_count(_kv) */
+    size_t head_dim;                  /* key_length = value_length = rope dimension */
+    size_t experts, top_k, expert_inter;
+    size_t context;                   /* context_length: positions 0 .. context - 1 */
+    size_t kv_window;                 /* KV ring capacity; 0 = min(context, 512), the reference's default */
+    float rms_epsilon;                /* attention.layer_norm_rms_epsilon */
+    float rope_theta;                 /* rope.freq_base */
+    int normalize_top_k;              /* expert_weights_norm */
+    uint32_t eos_token;               /* tokenizer.ggml.eos_token_id: generation stops after it */
+    uint32_t attn_type;               /* GGML type of attn_q/k/v/output */
+    uint32_t expert_type;             /* GGML type of the routed experts */
+    uint32_t embed_type;              /* GGML type of token_embd */
+    uint32_t output_type;             /* GGML type of output (the LM head) */
+} pokit_cuda_decoder_config;
+
+/* Decoder tensors outside the MoE blocks (GGUF names in comments). */
+typedef enum pokit_cuda_decoder_tensor {
+    POKIT_CUDA_DEC_TOKEN_EMBD = 0,    /* token_embd.weight   [hidden, vocab] */
+    POKIT_CUDA_DEC_OUTPUT_NORM = 1,   /* output_norm.weight  F32 [hidden] */
+    POKIT_CUDA_DEC_OUTPUT = 2,        /* output.weight       [hidden, vocab] */
+    POKIT_CUDA_DEC_ATTN_NORM = 3,     /* blk.L.attn_norm.weight   F32 [hidden] */
+    POKIT_CUDA_DEC_ATTN_Q = 4,        /* blk.L.attn_q.weight      [hidden, q_heads * head_dim] */
+    POKIT_CUDA_DEC_ATTN_Q_NORM = 5,   /* blk.L.attn_q_norm.weight F32 [head_dim] */
+    POKIT_CUDA_DEC_ATTN_K = 6,        /* blk.L.attn_k.weight      [hidden, kv_heads * head_dim] */
+    POKIT_CUDA_DEC_ATTN_K_NORM = 7,   /* blk.L.attn_k_norm.weight F32 [head_dim] */
+    POKIT_CUDA_DEC_ATTN_V = 8,        /* blk.L.attn_v.weight      [hidden, kv_heads * head_dim] */
+    POKIT_CUDA_DEC_ATTN_OUTPUT = 9    /* blk.L.attn_output.weight [q_heads * head_dim, hidden] */
+} pokit_cuda_decoder_tensor;
+
+/* Mirrors GenerationStats (qwen3_moe_runner.hpp:33-37). */
+typedef struct pokit_cuda_generation_stats {
+    uint64_t prefill_time_ns;
+    uint64_t decode_time_ns;
+    size_t generated_tokens;
+} pokit_cuda_generation_stats;
+
+pokit_cuda_status pokit_cuda_decoder_create(const pokit_cuda_decoder_config* config,
+                                            pokit_cuda_decoder** out_decoder, char* error_buffer,
+                                            size_t error_capacity);
+void pokit_cuda_decoder_destroy(pokit_cuda_decoder* decoder);
+
+/* The decoder's MoE blocks (owned by the decoder; do not destroy). */
+pokit_cuda_moe* pokit_cuda_decoder_moe(pokit_cuda_decoder* decoder);
+
+/* Bytes of one decoder tensor (layer ignored for the first three). */
+size_t pokit_cuda_decoder_tensor_bytes(const pokit_cuda_decoder* decoder, size_t layer, uint32_t tensor);
+
+/* Host payload in GGUF layout, bytes = pokit_cuda_decoder_tensor_bytes.  Synchronous. */
+pokit_cuda_status pokit_cuda_decoder_upload_tensor(pokit_cuda_decoder* decoder, size_t layer, uint32_t tensor,
+                                                   const void* host_bytes, size_t bytes, char* error_buffer,
+                                                   size_t error_capacity);
+
+/* Fills a quantised decoder tensor with the seeded synthetic block generator
+ * (pokitlms_b200.gguf writes the same bytes into a GGUF).  Benchmark utility. */
+pokit_cuda_status pokit_cuda_decoder_synthesize_tensor(pokit_cuda_decoder* decoder, size_t layer, uint32_t tensor,
+                                                       uint64_t seed, uint64_t stream_id, char* error_buffer,
+                                                       size_t error_capacity);
+
+/* Qwen3MoeRunner::forward_token: consumes `token` at `position` (must be the
+ * next position) and, when logits_host is not NULL, writes vocab F32 logits.
+ * A non-finite logit returns RUNTIME_ERROR and resets the state, as the
+ * reference throws and resets. */
+pokit_cuda_status pokit_cuda_decoder_forward_token(pokit_cuda_decoder* decoder, uint32_t token, uint64_t position,
+                                                   float* logits_host, char* error_buffer, size_t error_capacity);
+
+/* Qwen3MoeRunner::generate_tokens with greedy sampling: resets the state,
+ * prefills the prompt, then writes up to max_new_tokens ids to tokens_out
+ * (*generated of them; the end token is included when generated). */
+pokit_cuda_status pokit_cuda_decoder_generate_tokens(pokit_cuda_decoder* decoder, const uint32_t* prompt,
+                                                     size_t prompt_tokens, size_t max_new_tokens,
+                                                     uint32_t* tokens_out, size_t* generated,
+                                                     pokit_cuda_generation_stats* stats, char* error_buffer,
+                                                     size_t error_capacity);
+
+/* Measurement hook (no counterpart in the reference): enqueues `steps` greedy
+ * token steps on `stream` (each step's token is the previous step's argmax,
+ * all on the device) after the current position.  Asynchronous. */
+pokit_cuda_status pokit_cuda_decoder_run_steps(pokit_cuda_decoder* decoder, size_t steps, void* stream,
+                                               char* error_buffer, size_t error_capacity);
+
+/* Clears the decode state (position 0, empty KV cache). */
+pokit_cuda_status pokit_cuda_decoder_reset(pokit_cuda_decoder* decoder, char* error_buffer, size_t error_capacity);
+
+/* Kernels one token step with logits launches (measurement). */
+uint64_t pokit_cuda_decoder_launches_per_step(const pokit_cuda_decoder* decoder);
+
+/* ------------------------------------------------------------------------ */
 /* One MoE block without any device allocation                              */
 /* ------------------------------------------------------------------------ */
 

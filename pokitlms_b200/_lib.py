@@ -110,6 +110,26 @@ class MoeBlockDevice(C.Structure):
     ]
 
 
+class DecoderConfig(C.Structure):
+    _fields_ = [
+        ("device", C.c_int), ("layers", C.c_size_t), ("hidden", C.c_size_t), ("vocab", C.c_size_t),
+        ("q_heads", C.c_size_t), ("kv_heads", C.c_size_t), ("head_dim", C.c_size_t),
+        ("experts", C.c_size_t), ("top_k", C.c_size_t), ("expert_inter", C.c_size_t),
+        ("context", C.c_size_t), ("kv_window", C.c_size_t), ("rms_epsilon", C.c_float),
+        ("rope_theta", C.c_float), ("normalize_top_k", C.c_int), ("eos_token", C.c_uint32),
+        ("attn_type", C.c_uint32), ("expert_type", C.c_uint32), ("embed_type", C.c_uint32),
+        ("output_type", C.c_uint32),
+    ]
+
+
+class GenerationStats(C.Structure):
+    _fields_ = [("prefill_time_ns", C.c_uint64), ("decode_time_ns", C.c_uint64),
+                ("generated_tokens", C.c_size_t)]
+
+
+DEC_TOKEN_EMBD, DEC_OUTPUT_NORM, DEC_OUTPUT = 0, 1, 2
+DEC_ATTN_NORM, DEC_ATTN_Q, DEC_ATTN_Q_NORM, DEC_ATTN_K, DEC_ATTN_K_NORM, DEC_ATTN_V, DEC_ATTN_OUTPUT = range(3, 10)
+
 STATIC_SCRATCH_BYTES = 256 * 1024
 
 _ERR = C.c_char_p
@@ -163,6 +183,18 @@ SIGNATURES = {
     "pokit_cuda_moe_tensor_bytes": (C.c_size_t, [_VP, _SZ, C.c_uint32]),
     "pokit_cuda_moe_trace_decode": (C.c_int, [_VP, _SZ, _SZ, _VP, _VP, _SZ, C.POINTER(C.c_uint32), _VP, _ERR,
                                               _SZ]),
+    "pokit_cuda_decoder_create": (C.c_int, [C.POINTER(DecoderConfig), C.POINTER(_VP), _ERR, _SZ]),
+    "pokit_cuda_decoder_destroy": (None, [_VP]),
+    "pokit_cuda_decoder_moe": (_VP, [_VP]),
+    "pokit_cuda_decoder_tensor_bytes": (_SZ, [_VP, _SZ, C.c_uint32]),
+    "pokit_cuda_decoder_upload_tensor": (C.c_int, [_VP, _SZ, C.c_uint32, _VP, _SZ, _ERR, _SZ]),
+    "pokit_cuda_decoder_synthesize_tensor": (C.c_int, [_VP, _SZ, C.c_uint32, C.c_uint64, C.c_uint64, _ERR, _SZ]),
+    "pokit_cuda_decoder_forward_token": (C.c_int, [_VP, C.c_uint32, C.c_uint64, _VP, _ERR, _SZ]),
+    "pokit_cuda_decoder_generate_tokens": (C.c_int, [_VP, _VP, _SZ, _SZ, _VP, C.POINTER(_SZ),
+                                                     C.POINTER(GenerationStats), _ERR, _SZ]),
+    "pokit_cuda_decoder_run_steps": (C.c_int, [_VP, _SZ, _VP, _ERR, _SZ]),
+    "pokit_cuda_decoder_reset": (C.c_int, [_VP, _ERR, _SZ]),
+    "pokit_cuda_decoder_launches_per_step": (C.c_uint64, [_VP]),
     "pokit_cuda_moe_forward_static_scratch": (C.c_int, [C.POINTER(MoeBlockDevice), _VP, _VP, _VP,
                                                         _VP, _VP, _ERR, _SZ]),
 }

@@ -301,9 +301,9 @@ class CudaMoeBackend:
         return {n: getattr(s, n) for n, _ in s._fields_}
 
     def close(self) -> None:
-        if self._h:
+        if self._h and not getattr(self, "_borrowed", False):
             lib().pokit_cuda_moe_destroy(self._h)
-            self._h = None
+        self._h = None
 
     def __del__(self):
         try:
@@ -315,3 +315,97 @@ class CudaMoeBackend:
 __all__ = ["CudaLinearBackend", "CudaMoeBackend", "linear", "dequantize_rows", "route_experts",
            "synthesize_blocks", "version", "PokitCudaError", "InvalidArgument", "BLOCK",
            "row_bytes", "F32", "GATE", "UP", "DOWN", "QWEN3", "QWEN35", "_lib"]
+
+
+class CudaDecoder:
+    """The whole Qwen3-MoE decoder of one sequence on the GPU (the reference's
+    Qwen3MoeRunner: forward_token, generate_tokens with greedy sampling)."""
+
+    def __init__(self, shape, *, device: int = 0, kv_window: int = 0):
+        """`shape`: a pokitlms_b200.gguf.Qwen3MoeShape (the model's hyper-parameters and tensor types)."""
+        cfg = _lib.DecoderConfig(device, shape.layers, shape.hidden, shape.vocab, shape.q_heads, shape.kv_heads,
+                                 shape.head_dim, shape.experts, shape.top_k, shape.expert_inter, shape.context,
+                                 kv_window, shape.rms_epsilon, shape.rope_theta, 1, shape.eos, shape.attn_type,
+                                 shape.expert_type, shape.embed_type, shape.output_type)
+        h = C.c_void_p()
+        call("pokit_cuda_decoder_create", C.byref(cfg), C.byref(h))
+        self._h = h
+        self.shape = shape
+        moe = CudaMoeBackend.__new__(CudaMoeBackend)
+        moe._h = C.c_void_p(lib().pokit_cuda_decoder_moe(h))
+        moe._borrowed = True
+        moe._ldt = None
+        moe.layers, moe.hidden, moe.inter = shape.layers, shape.hidden, shape.expert_inter
+        moe.experts, moe.top_k, moe.flavour = shape.experts, shape.top_k, QWEN3
+        moe.shared_inter, moe.expert_first, moe.expert_count = 0, 0, shape.experts
+        self.moe = moe
+
+    def tensor_bytes(self, layer: int, tensor: int) -> int:
+        return int(lib().pokit_cuda_decoder_tensor_bytes(self._h, layer, tensor))
+
+    def upload_tensor(self, layer: int, tensor: int, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data)
+        call("pokit_cuda_decoder_upload_tensor", self._h, layer, tensor, _np_ptr(data), data.nbytes)
+
+    def synthesize_tensor(self, layer: int, tensor: int, seed: int, stream_id: int) -> None:
+        call("pokit_cuda_decoder_synthesize_tensor", self._h, layer, tensor, seed, stream_id)
+
+    def synthesize_model(self) -> None:
+        """Every tensor of the synthetic model that pokitlms_b200.gguf writes
+        for this shape, generated in HBM from the same seeds (F32 routers and
+        norms uploaded from the host)."""
+        from . import gguf, synth
+        from ._lib import DOWN as MD, FFN_NORM, GATE as MG, ROUTER, UP as MU
+        s = self.shape
+        seed = s.seed
+        H, d = s.hidden, s.head_dim
+        self.synthesize_tensor(0, _lib.DEC_TOKEN_EMBD, seed, gguf.EMBED_STREAM)
+        self.synthesize_tensor(0, _lib.DEC_OUTPUT, seed, gguf.OUTPUT_STREAM)
+        self.upload_tensor(0, _lib.DEC_OUTPUT_NORM, np.ones(H, np.float32))
+        for l in range(s.layers):
+            self.upload_tensor(l, _lib.DEC_ATTN_NORM, np.ones(H, np.float32))
+            self.upload_tensor(l, _lib.DEC_ATTN_Q_NORM, np.ones(d, np.float32))
+            self.upload_tensor(l, _lib.DEC_ATTN_K_NORM, np.ones(d, np.float32))
+            for t, sid in ((_lib.DEC_ATTN_Q, gguf.ATTN_Q), (_lib.DEC_ATTN_K, gguf.ATTN_K),
+                           (_lib.DEC_ATTN_V, gguf.ATTN_V), (_lib.DEC_ATTN_OUTPUT, gguf.ATTN_OUTPUT)):
+                self.synthesize_tensor(l, t, seed, synth.stream_id(l, sid))
+            self.moe.upload_tensor(l, ROUTER, synth.router_weights(s.experts, H, seed, l))
+            self.moe.upload_tensor(l, FFN_NORM, np.ones(H, np.float32))
+            for t in (MG, MU, MD):
+                self.moe.synthesize_tensor(l, t, seed, synth.stream_id(l, t))
+
+    def forward_token(self, token: int, position: int, logits: bool = True) -> np.ndarray | None:
+        out = np.empty(self.shape.vocab, np.float32) if logits else None
+        call("pokit_cuda_decoder_forward_token", self._h, token, position, _np_ptr(out))
+        return out
+
+    def generate_tokens(self, prompt, max_new: int):
+        """(generated ids, stats dict) of greedy decoding after `prompt`."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(max_new, 1), np.uint32)
+        n = C.c_size_t(0)
+        st = _lib.GenerationStats()
+        call("pokit_cuda_decoder_generate_tokens", self._h, _np_ptr(p), p.size, max_new, _np_ptr(out),
+             C.byref(n), C.byref(st))
+        return out[:n.value].copy(), {f: getattr(st, f) for f, _ in st._fields_}
+
+    def run_steps(self, steps: int, stream=None) -> None:
+        call("pokit_cuda_decoder_run_steps", self._h, steps, _stream(stream))
+
+    def reset(self) -> None:
+        call("pokit_cuda_decoder_reset", self._h)
+
+    def launches_per_step(self) -> int:
+        return int(lib().pokit_cuda_decoder_launches_per_step(self._h))
+
+    def close(self) -> None:
+        if self._h:
+            self.moe._h = None
+            lib().pokit_cuda_decoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,812 @@
+// pokit_decoder.cu -- the whole Qwen3-MoE decoder of one sequence on the GPU:
+// the reference's Qwen3MoeRunner (src/qwen3_moe_runner.cpp) with every
+// matrix, norm, attention and MoE step in HBM, so that greedy decoding runs
+// with no host round trip per layer.
+//
+// One token step (Qwen3MoeRunner::Impl::forward_into, qwen3_moe_runner.cpp:580-704):
+//   embed     the token's row of token_embd (any GGUF type, bit-exact decode)
+//   per layer rms_norm(attn_norm) -> one Q/K/V matvec over the concatenated
+//             [q | k | v] rows -> per-head RMSNorm of q and k, rotate-half
+//             RoPE from a position table, K/V appended to an FP16 ring (RNE,
+//             kv_cache.cpp:20-44) -> GQA attention over the ring
+//             (kv_cache.cpp:185-294) -> output projection added into the
+//             residual -> the MoE block (pokit_cuda_moe_decode_layers: rms_norm,
+//             router, top-k, experts, combine, residual)
+//   logits    rms_norm(output_norm) -> LM head -> greedy argmax (first maximum,
+//             :320-333) written as the next token of the sequence
+// The token and position live in device memory, so a step is position-free
+// and runs as one CUDA graph replay (captured on first use).
+#include "../../include/pokit_cuda.h"
+#include "pokit_kernels.h"
+#include "pokit_quant.cuh"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace pokit {
+namespace {
+
+constexpr uint32_t kStatusDecoderNonFinite = 1u;   // LM head produced NaN/Inf (the reference throws)
+constexpr uint32_t kMaxHeadDim = 256;
+constexpr uint32_t kMaxWindow = 8192;
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce_all(T v, T* red, Op op) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    T r = red[0];
+    for (int w = 1; w < nw; ++w) r = op(r, red[w]);
+    return r;
+}
+
+// The token's embedding row, decoded exactly as dequantize_quantized_row.
+template <uint32_t T>
+__global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t cols, const uint32_t* __restrict__ seq,
+                             const uint32_t* __restrict__ pos, float* __restrict__ out) {
+    const uint32_t token = seq[*pos];
+    const uint8_t* row = table + static_cast<uint64_t>(token) * row_bytes(T, cols);
+    for (uint32_t g = threadIdx.x; g < cols / 32u; g += blockDim.x) group_decode<T>(row, static_cast<int>(g), out + g * 32u);
+}
+
+// out = x * (1 / sqrt(mean(x^2) + eps)) * w   (src/rms_norm.cpp:9-27)
+__global__ void rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, float eps,
+                                float* __restrict__ out, uint32_t n) {
+    __shared__ float red[32];
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    const float total = block_reduce_all(ss, red, [](float a, float b) { return a + b; });
+    const float scale = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
+}
+
+// One CTA per query head and per KV head, one thread per dimension: per-head
+// RMSNorm (q_norm / k_norm), rotate-half RoPE (qwen3_moe_runner.cpp:141-172:
+// first = a cos - b sin, second = b cos + a sin), then the query to q_out or
+// the key and value to the FP16 ring at slot position % window.
+__global__ void attn_prep_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
+                                 const float* __restrict__ k_norm, float eps, const float* __restrict__ rope_cos,
+                                 const float* __restrict__ rope_sin, const uint32_t* __restrict__ pos_p,
+                                 uint32_t window, uint32_t qh, uint32_t kvh, float* __restrict__ q_out,
+                                 __half* __restrict__ kc, __half* __restrict__ vc) {
+    __shared__ float v[kMaxHeadDim];
+    __shared__ float red[32];
+    const uint32_t d = blockDim.x, half = d / 2, t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
+    const bool is_q = h < qh;
+    const uint32_t kh = h - qh;
+    const float x = is_q ? qkv[h * d + t] : qkv[(qh + kh) * d + t];
+    const float total = block_reduce_all(x * x, red, [](float a, float b) { return a + b; });
+    const float scale = 1.0f / sqrtf(total / static_cast<float>(d) + eps);
+    v[t] = __fmul_rn(__fmul_rn(x, scale), is_q ? q_norm[t] : k_norm[t]);
+    __syncthreads();
+    const uint32_t j = t < half ? t : t - half;
+    const float c = rope_cos[static_cast<uint64_t>(pos) * half + j], s = rope_sin[static_cast<uint64_t>(pos) * half + j];
+    const float a = v[j], b = v[j + half];
+    const float r = t < half ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)) : __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+    if (is_q) {
+        q_out[h * d + t] = r;
+    } else {
+        const uint64_t at = (static_cast<uint64_t>(pos % window) * kvh + kh) * d + t;
+        kc[at] = __float2half_rn(r);
+        vc[at] = __float2half_rn(qkv[(qh + kvh + kh) * d + t]);
+    }
+}
+
+// GQA decode attention of one query head over the ring's last min(pos + 1,
+// window) positions, oldest first (KvCache::attend, kv_cache.cpp:185-294):
+// scores = q . k * scale, softmax, out = sum_j (e_j / sum e) v_j.
+__global__ void attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
+                              const __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, uint32_t window,
+                              uint32_t qh, uint32_t kvh, float scale, float* __restrict__ out) {
+    extern __shared__ float sc[];
+    __shared__ float red[32];
+    const uint32_t d = blockDim.x, t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
+    const uint32_t kh = h / (qh / kvh);
+    const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
+    const int lane = t & 31, warp = t >> 5, nwarps = (d + 31) >> 5;
+    const float* qv = q + h * d;
+    for (uint32_t j = warp; j < n; j += nwarps) {
+        const __half* k = kc + (static_cast<uint64_t>((first + j) % window) * kvh + kh) * d;
+        float dot = 0.0f;
+        for (uint32_t e = lane; e < d; e += 32) dot = fmaf(qv[e], __half2float(k[e]), dot);
+        dot = warp_sum(dot);
+        if (lane == 0) sc[j] = dot * scale;
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (uint32_t j = t; j < n; j += d) m = fmaxf(m, sc[j]);
+    m = block_reduce_all(m, red, [](float a, float b) { return fmaxf(a, b); });
+    float den = 0.0f;
+    for (uint32_t j = t; j < n; j += d) {
+        const float e = expf(sc[j] - m);
+        sc[j] = e;
+        den += e;
+    }
+    den = block_reduce_all(den, red, [](float a, float b) { return a + b; });
+    float acc = 0.0f;
+    for (uint32_t j = 0; j < n; ++j) {
+        const __half* vv = vc + (static_cast<uint64_t>((first + j) % window) * kvh + kh) * d;
+        acc = fmaf(sc[j] / den, __half2float(vv[t]), acc);
+    }
+    out[h * d + t] = acc;
+}
+
+// Greedy sampling (qwen3_moe_runner.cpp:320-333): the first maximum of the
+// logits becomes token position + 1 of the sequence; a non-finite logit sets
+// the status word (the reference throws).
+__global__ void argmax_kernel(const float* __restrict__ logits, uint32_t n, uint32_t* __restrict__ seq,
+                              const uint32_t* __restrict__ pos_p, uint32_t seq_cap, uint32_t* __restrict__ status) {
+    __shared__ float rv[32];
+    __shared__ uint32_t ri[32];
+    float best = -INFINITY;
+    uint32_t bi = 0xffffffffu;
+    int bad = 0;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = logits[i];
+        if (!isfinite(v)) bad = 1;
+        else if (v > best || bi == 0xffffffffu) { best = v; bi = i; }
+    }
+    bad = __syncthreads_or(bad);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi != 0xffffffffu && (bi == 0xffffffffu || ov > best || (ov == best && oi < bi))) { best = ov; bi = oi; }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { rv[warp] = best; ri[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>((blockDim.x + 31) >> 5); ++w)
+            if (ri[w] != 0xffffffffu && (bi == 0xffffffffu || rv[w] > best || (rv[w] == best && ri[w] < bi))) {
+                best = rv[w];
+                bi = ri[w];
+            }
+        if (bad) atomicOr(status, kStatusDecoderNonFinite);
+        const uint32_t p = *pos_p;
+        if (p + 1 < seq_cap) seq[p + 1] = bad || bi == 0xffffffffu ? 0u : bi;
+    }
+}
+
+__global__ void advance_kernel(uint32_t* pos) { *pos += 1u; }
+
+template <uint32_t T>
+cudaError_t launch_embed(const void* table, uint32_t cols, const uint32_t* seq, const uint32_t* pos, float* out,
+                         cudaStream_t s) {
+    embed_kernel<T><<<1, 256, 0, s>>>(static_cast<const uint8_t*>(table), cols, seq, pos, out);
+    return cudaGetLastError();
+}
+
+void set_error(char* destination, size_t capacity, const char* message) noexcept {
+    if (!destination || capacity == 0) return;
+    const size_t n = std::min(capacity - 1, std::strlen(message));
+    std::memcpy(destination, message, n);
+    destination[n] = '\0';
+}
+
+uint64_t align256(uint64_t v) { return (v + 255u) & ~uint64_t(255); }
+
+bool decoder_type(uint32_t t) { return t == kF32 || t == kQ8_0 || t == kQ4_K || t == kQ5_K || t == kQ6_K; }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+class Decoder {
+public:
+    explicit Decoder(const pokit_cuda_decoder_config& c) : cfg_(c) {
+        const size_t d = c.head_dim;
+        if (c.layers == 0 || c.hidden == 0 || c.hidden % 256 || c.vocab == 0 || c.vocab > 0xffffffffu ||
+            c.q_heads == 0 || c.kv_heads == 0 || c.q_heads % c.kv_heads || d == 0 || d % 32 || d > kMaxHeadDim ||
+            c.context == 0 || c.context > (1u << 24) || c.eos_token >= c.vocab || !(c.rope_theta > 0.0f) ||
+            !(c.rms_epsilon > 0.0f) || (c.q_heads * d) % 256)
+            throw std::invalid_argument("invalid decoder configuration");
+        if (!decoder_type(c.attn_type) || c.attn_type == kF32 || !decoder_type(c.embed_type) ||
+            !decoder_type(c.output_type))
+            throw std::invalid_argument("unsupported decoder tensor type");
+        window_ = c.kv_window ? c.kv_window : std::min<size_t>(c.context, 512);
+        if (window_ > c.context || window_ > kMaxWindow) throw std::invalid_argument("invalid KV window");
+        qd_ = c.q_heads * d;
+        kd_ = c.kv_heads * d;
+        pokit_cuda_moe_config mc{};
+        mc.device = c.device;
+        mc.layers = c.layers;
+        mc.hidden = c.hidden;
+        mc.inter = c.expert_inter;
+        mc.experts = c.experts;
+        mc.top_k = c.top_k;
+        mc.flavour = POKIT_CUDA_MOE_QWEN3;
+        mc.normalize_top_k = c.normalize_top_k;
+        mc.expert_weights_scale = 1.0f;
+        mc.rms_epsilon = c.rms_epsilon;
+        mc.gate_type = mc.up_type = mc.down_type = c.expert_type;
+        mc.shared_gate_type = mc.shared_up_type = mc.shared_down_type = kQ8_0;
+        char err[512];
+        const pokit_cuda_status st = pokit_cuda_moe_create(&mc, &moe_, err, sizeof err);
+        if (st == POKIT_CUDA_STATUS_INVALID_ARGUMENT) throw std::invalid_argument(err);
+        if (st != POKIT_CUDA_STATUS_OK) throw std::runtime_error(err);
+        int prev = 0;
+        check(cudaGetDevice(&prev), "cudaGetDevice");
+        check(cudaSetDevice(c.device), "cudaSetDevice");
+        try {
+            allocate();
+        } catch (...) {
+            cudaSetDevice(prev);
+            release();
+            throw;
+        }
+        cudaSetDevice(prev);
+    }
+
+    ~Decoder() { release(); }
+    Decoder(const Decoder&) = delete;
+    Decoder& operator=(const Decoder&) = delete;
+
+    std::mutex& mutex() { return mutex_; }
+    pokit_cuda_moe* moe() { return moe_; }
+
+    uint64_t tensor_bytes(size_t layer, uint32_t t) const {
+        const uint64_t H = cfg_.hidden, d = cfg_.head_dim;
+        switch (t) {
+            case POKIT_CUDA_DEC_TOKEN_EMBD: return cfg_.vocab * row_bytes(cfg_.embed_type, H);
+            case POKIT_CUDA_DEC_OUTPUT_NORM: return H * 4;
+            case POKIT_CUDA_DEC_OUTPUT: return cfg_.vocab * row_bytes(cfg_.output_type, H);
+            default: break;
+        }
+        if (layer >= cfg_.layers) return 0;
+        switch (t) {
+            case POKIT_CUDA_DEC_ATTN_NORM: return H * 4;
+            case POKIT_CUDA_DEC_ATTN_Q: return qd_ * row_bytes(cfg_.attn_type, H);
+            case POKIT_CUDA_DEC_ATTN_Q_NORM: return d * 4;
+            case POKIT_CUDA_DEC_ATTN_K: return kd_ * row_bytes(cfg_.attn_type, H);
+            case POKIT_CUDA_DEC_ATTN_K_NORM: return d * 4;
+            case POKIT_CUDA_DEC_ATTN_V: return kd_ * row_bytes(cfg_.attn_type, H);
+            case POKIT_CUDA_DEC_ATTN_OUTPUT: return H * row_bytes(cfg_.attn_type, qd_);
+            default: return 0;
+        }
+    }
+
+    void upload(size_t layer, uint32_t t, const void* host, size_t bytes) {
+        ensure_ok();
+        uint8_t* dst = tensor_ptr(layer, t);
+        if (!dst) throw std::invalid_argument("tensor does not exist in this configuration");
+        if (!host || bytes != tensor_bytes(layer, t)) throw std::invalid_argument("tensor byte size does not match");
+        Scope scope(cfg_.device);
+        guard(cudaMemcpy(dst, host, bytes, cudaMemcpyHostToDevice), "upload");
+    }
+
+    void synthesize(size_t layer, uint32_t t, uint64_t seed, uint64_t stream_id) {
+        ensure_ok();
+        uint8_t* dst = tensor_ptr(layer, t);
+        const uint32_t type = tensor_type(t);
+        if (!dst || type == kF32) throw std::invalid_argument("only quantised decoder tensors can be synthesised");
+        Scope scope(cfg_.device);
+        guard(launch_synth_blocks(type, seed, stream_id, tensor_bytes(layer, t) / block_bytes(type), dst, stream_),
+              "synthesize");
+        guard(cudaStreamSynchronize(stream_), "synthesize");
+    }
+
+    void reset() {
+        ensure_ok();
+        Scope scope(cfg_.device);
+        guard(cudaMemsetAsync(pos_, 0, 4, stream_), "reset");
+        guard(cudaStreamSynchronize(stream_), "reset");
+        next_position_ = 0;
+    }
+
+    // Qwen3MoeRunner::forward_token: the token at `position` (the next one),
+    // logits out (may be null).
+    void forward_token(uint32_t token, uint64_t position, float* logits) {
+        ensure_ok();
+        if (token >= cfg_.vocab) throw std::out_of_range("token id exceeds model vocabulary");
+        if (position != next_position_ || position >= cfg_.context)
+            throw std::invalid_argument("token position is not the next position in this decode state");
+        Scope scope(cfg_.device);
+        *pinned_ids_ = token;
+        guard(cudaMemcpyAsync(seq_ + position, pinned_ids_, 4, cudaMemcpyHostToDevice, stream_), "token");
+        step(true);
+        ++next_position_;
+        if (logits) guard(cudaMemcpyAsync(logits, logits_, cfg_.vocab * 4, cudaMemcpyDeviceToHost, stream_), "logits");
+        sync_and_check();
+    }
+
+    // Qwen3MoeRunner::generate_tokens with greedy sampling (temperature 0):
+    // resets the state, prefills the prompt (logits for its last token only),
+    // then samples up to max_new tokens, stopping after the end token.
+    void generate(const uint32_t* prompt, size_t n, size_t max_new, uint32_t* out, size_t* n_out,
+                  pokit_cuda_generation_stats* stats) {
+        ensure_ok();
+        if (!prompt || n == 0) throw std::invalid_argument("generation prompt must contain at least one token");
+        if (n > cfg_.context || max_new > cfg_.context - n)
+            throw std::length_error("prompt and generation length exceed model context");
+        if (max_new && (!out || !n_out)) throw std::invalid_argument("output buffers are required");
+        for (size_t i = 0; i < n; ++i)
+            if (prompt[i] >= cfg_.vocab) throw std::out_of_range("token id exceeds model vocabulary");
+        Scope scope(cfg_.device);
+        if (stats) *stats = {};
+        if (n_out) *n_out = 0;
+        const auto t0 = std::chrono::steady_clock::now();
+        guard(cudaMemsetAsync(pos_, 0, 4, stream_), "reset");
+        next_position_ = 0;
+        for (size_t i = 0; i < n;) {
+            const size_t m = std::min(n - i, kPinnedIds);
+            std::memcpy(pinned_ids_, prompt + i, m * 4);
+            guard(cudaMemcpyAsync(seq_ + i, pinned_ids_, m * 4, cudaMemcpyHostToDevice, stream_), "prompt");
+            guard(cudaStreamSynchronize(stream_), "prompt");
+            i += m;
+        }
+        for (size_t i = 0; i < n; ++i) step(i + 1 == n);
+        next_position_ = n;
+        sync_and_check();
+        const auto t1 = std::chrono::steady_clock::now();
+        // Token i (i >= 1) is sampled by the forward of token i - 1; token 0 by
+        // the last prompt step.  The forwards of a chunk run back to back on the
+        // device and the host reads the chunk's tokens once, to find the end
+        // token.  Forwards past the end token are harmless while the KV ring has
+        // not wrapped (they write slots no later position reads before it is
+        // rewritten); after that, one token per round trip.
+        size_t produced = 0, forwarded = 0;
+        bool ended = false;
+        while (produced < max_new && !ended) {
+            const bool wrapped = n + produced + 16 >= window_;
+            const size_t chunk = wrapped ? 1 : std::min<size_t>(max_new - produced, 16);
+            const size_t last = produced + chunk - 1;
+            for (; forwarded < last; ++forwarded) step(true);
+            guard(cudaMemcpyAsync(pinned_ids_, seq_ + n + produced, chunk * 4, cudaMemcpyDeviceToHost, stream_),
+                  "tokens");
+            sync_and_check();
+            for (size_t i = 0; i < chunk && !ended; ++i) {
+                out[produced] = pinned_ids_[i];
+                ++produced;
+                if (pinned_ids_[i] == cfg_.eos_token) ended = true;
+            }
+        }
+        // The reference forwards every generated token but the last one.
+        next_position_ = n + (produced ? produced - 1 : 0);
+        // Forwards past the end token left the device position ahead: align it.
+        *pinned_ids_ = static_cast<uint32_t>(next_position_);
+        guard(cudaMemcpyAsync(pos_, pinned_ids_, 4, cudaMemcpyHostToDevice, stream_), "position");
+        guard(cudaStreamSynchronize(stream_), "position");
+        const auto t2 = std::chrono::steady_clock::now();
+        *n_out = produced;
+        if (stats) {
+            stats->prefill_time_ns = static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count());
+            stats->decode_time_ns = static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(t2 - t1).count());
+            stats->generated_tokens = produced;
+        }
+    }
+
+    // Enqueues `steps` token steps with logits on `s` (device-resident
+    // sequence: each step's token is the previous step's argmax).  For
+    // benchmarks: the caller synchronises.
+    void run_steps(size_t steps, cudaStream_t s) {
+        ensure_ok();
+        if (next_position_ + steps >= cfg_.context) throw std::length_error("steps exceed model context");
+        Scope scope(cfg_.device);
+        for (size_t i = 0; i < steps; ++i) step(true, s ? s : stream_);
+        next_position_ += steps;
+    }
+
+    size_t position() const { return next_position_; }
+    uint64_t launches_per_step() const { return launches_per_step_; }
+
+private:
+    static constexpr size_t kPinnedIds = 4096;
+
+    struct Scope {
+        explicit Scope(int device) {
+            cudaGetDevice(&prev);
+            if (prev != device) cudaSetDevice(device);
+            dev = device;
+        }
+        ~Scope() {
+            if (prev != dev) cudaSetDevice(prev);
+        }
+        int prev = 0, dev = 0;
+    };
+
+    static void check(cudaError_t e, const char* what) {
+        if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+    }
+    void guard(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return;
+        if (e == cudaErrorInvalidValue) throw std::invalid_argument(std::string(what) + ": unsupported shape or argument");
+        failed_ = true;
+        failure_ = std::string(what) + ": " + cudaGetErrorString(e);
+        throw std::runtime_error(failure_);
+    }
+    void ensure_ok() const {
+        if (failed_) throw std::runtime_error("CUDA decoder failed earlier: " + failure_);
+    }
+
+    uint32_t tensor_type(uint32_t t) const {
+        switch (t) {
+            case POKIT_CUDA_DEC_TOKEN_EMBD: return cfg_.embed_type;
+            case POKIT_CUDA_DEC_OUTPUT: return cfg_.output_type;
+            case POKIT_CUDA_DEC_ATTN_Q: case POKIT_CUDA_DEC_ATTN_K: case POKIT_CUDA_DEC_ATTN_V:
+            case POKIT_CUDA_DEC_ATTN_OUTPUT: return cfg_.attn_type;
+            default: return kF32;
+        }
+    }
+
+    uint8_t* tensor_ptr(size_t layer, uint32_t t) const {
+        if (t > POKIT_CUDA_DEC_ATTN_OUTPUT || tensor_bytes(layer, t) == 0) return nullptr;
+        if (t <= POKIT_CUDA_DEC_OUTPUT) return pool_ + global_off_[t];
+        return pool_ + layer_off_[layer] + local_off_[t - POKIT_CUDA_DEC_ATTN_NORM];
+    }
+
+    void allocate() {
+        // Pool: embedding, output norm, LM head, then per layer attn_norm,
+        // q, k, v (contiguous rows: one matvec), o, q_norm, k_norm.
+        uint64_t off = 0;
+        for (uint32_t t = 0; t <= POKIT_CUDA_DEC_OUTPUT; ++t) {
+            global_off_[t] = off;
+            off += align256(tensor_bytes(0, t));
+        }
+        const uint64_t rb = row_bytes(cfg_.attn_type, cfg_.hidden);
+        uint64_t lo = 0;
+        const auto place = [&](uint32_t t, uint64_t bytes, bool pad) {
+            local_off_[t - POKIT_CUDA_DEC_ATTN_NORM] = lo;
+            lo += pad ? align256(bytes) : bytes;
+        };
+        place(POKIT_CUDA_DEC_ATTN_NORM, cfg_.hidden * 4, true);
+        place(POKIT_CUDA_DEC_ATTN_Q, qd_ * rb, false);
+        place(POKIT_CUDA_DEC_ATTN_K, kd_ * rb, false);
+        place(POKIT_CUDA_DEC_ATTN_V, kd_ * rb, true);
+        place(POKIT_CUDA_DEC_ATTN_OUTPUT, cfg_.hidden * row_bytes(cfg_.attn_type, qd_), true);
+        place(POKIT_CUDA_DEC_ATTN_Q_NORM, cfg_.head_dim * 4, true);
+        place(POKIT_CUDA_DEC_ATTN_K_NORM, cfg_.head_dim * 4, true);
+        layer_off_.resize(cfg_.layers);
+        for (size_t l = 0; l < cfg_.layers; ++l) {
+            layer_off_[l] = off;
+            off += lo;
+        }
+        check(cudaMalloc(&pool_, off), "cudaMalloc(decoder pool)");
+        check(cudaMemset(pool_, 0, off), "cudaMemset(decoder pool)");
+        const uint64_t kv = static_cast<uint64_t>(cfg_.layers) * window_ * kd_ * sizeof(__half);
+        check(cudaMalloc(&kcache_, kv), "cudaMalloc(K cache)");
+        check(cudaMalloc(&vcache_, kv), "cudaMalloc(V cache)");
+        const size_t half = cfg_.head_dim / 2;
+        std::vector<float> cs(cfg_.context * half), sn(cfg_.context * half);
+        // The reference's table (qwen3_moe_runner.cpp:141-156), in its float
+        // arithmetic: angle = position * theta^(-pair / half).
+        for (size_t p = 0; p < cfg_.context; ++p)
+            for (size_t i = 0; i < half; ++i) {
+                const float angle = static_cast<float>(p) *
+                    std::pow(cfg_.rope_theta, -static_cast<float>(i) / static_cast<float>(half));
+                cs[p * half + i] = std::cos(angle);
+                sn[p * half + i] = std::sin(angle);
+            }
+        check(cudaMalloc(&rope_, cs.size() * 8), "cudaMalloc(rope)");
+        check(cudaMemcpy(rope_, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope");
+        check(cudaMemcpy(rope_ + cs.size(), sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope");
+        const uint64_t H = cfg_.hidden;
+        const uint64_t fl = align256(H * 4) * 2 + align256((qd_ + 2 * kd_) * 4) + align256(qd_ * 4) * 2 +
+                            align256(cfg_.vocab * 4);
+        check(cudaMalloc(&work_, fl), "cudaMalloc(decoder work)");
+        uint8_t* w = static_cast<uint8_t*>(work_);
+        hidden_ = reinterpret_cast<float*>(w); w += align256(H * 4);
+        xn_ = reinterpret_cast<float*>(w); w += align256(H * 4);
+        qkv_ = reinterpret_cast<float*>(w); w += align256((qd_ + 2 * kd_) * 4);
+        q_ = reinterpret_cast<float*>(w); w += align256(qd_ * 4);
+        att_ = reinterpret_cast<float*>(w); w += align256(qd_ * 4);
+        logits_ = reinterpret_cast<float*>(w);
+        check(cudaMalloc(&seq_, (cfg_.context + 1) * 4 + 512), "cudaMalloc(sequence)");
+        check(cudaMemset(seq_, 0, (cfg_.context + 1) * 4 + 512), "cudaMemset(sequence)");
+        pos_ = seq_ + cfg_.context + 1 + 32;
+        status_ = pos_ + 32;
+        check(cudaMallocHost(&pinned_ids_, kPinnedIds * 4), "cudaMallocHost");
+        check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming), "cudaEventCreate");
+        const size_t attend_smem = window_ * 4;
+        if (attend_smem > 48u * 1024u)
+            check(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(attend_smem)), "attend smem");
+    }
+
+    void release() {
+        for (auto& g : graphs_) if (g) cudaGraphExecDestroy(g);
+        if (join_) cudaEventDestroy(join_);
+        if (capture_stream_) cudaStreamDestroy(capture_stream_);
+        if (stream_) cudaStreamDestroy(stream_);
+        if (pinned_ids_) cudaFreeHost(pinned_ids_);
+        if (seq_) cudaFree(seq_);
+        if (work_) cudaFree(work_);
+        if (rope_) cudaFree(rope_);
+        if (vcache_) cudaFree(vcache_);
+        if (kcache_) cudaFree(kcache_);
+        if (pool_) cudaFree(pool_);
+        if (moe_) pokit_cuda_moe_destroy(moe_);
+        moe_ = nullptr;
+    }
+
+    cudaError_t embed(cudaStream_t s) {
+        const void* t = pool_ + global_off_[POKIT_CUDA_DEC_TOKEN_EMBD];
+        const uint32_t H = static_cast<uint32_t>(cfg_.hidden);
+        switch (cfg_.embed_type) {
+            case kF32: return launch_embed<kF32>(t, H, seq_, pos_, hidden_, s);
+            case kQ8_0: return launch_embed<kQ8_0>(t, H, seq_, pos_, hidden_, s);
+            case kQ4_K: return launch_embed<kQ4_K>(t, H, seq_, pos_, hidden_, s);
+            case kQ5_K: return launch_embed<kQ5_K>(t, H, seq_, pos_, hidden_, s);
+            default: return launch_embed<kQ6_K>(t, H, seq_, pos_, hidden_, s);
+        }
+    }
+
+    // The launches of one token step on `s`.
+    cudaError_t enqueue(bool logits, cudaStream_t s, uint64_t* launches) {
+        const uint32_t H = static_cast<uint32_t>(cfg_.hidden), d = static_cast<uint32_t>(cfg_.head_dim);
+        const uint32_t qh = static_cast<uint32_t>(cfg_.q_heads), kvh = static_cast<uint32_t>(cfg_.kv_heads);
+        const uint32_t win = static_cast<uint32_t>(window_), half = d / 2;
+        const float eps = cfg_.rms_epsilon, scale = 1.0f / std::sqrt(static_cast<float>(d));
+        uint64_t n = 0;
+        cudaError_t e = embed(s);
+        ++n;
+        for (size_t l = 0; l < cfg_.layers && e == cudaSuccess; ++l) {
+            const auto P = [&](uint32_t t) { return tensor_ptr(l, t); };
+            const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
+            rms_norm_kernel<<<1, 1024, 0, s>>>(hidden_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_NORM)), eps,
+                                               xn_, H);
+            e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_Q), static_cast<uint32_t>(qd_ + 2 * kd_), H, xn_,
+                              qkv_, s);
+            if (e != cudaSuccess) break;
+            attn_prep_kernel<<<qh + kvh, d, 0, s>>>(
+                qkv_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_Q_NORM)),
+                reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_K_NORM)), eps, rope_,
+                rope_ + cfg_.context * half, pos_, win, qh, kvh, q_, kcache_ + kv_off, vcache_ + kv_off);
+            attend_kernel<<<qh, d, win * 4, s>>>(q_, kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh, kvh, scale, att_);
+            e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
+                              hidden_, s, false, true);
+            if (e != cudaSuccess) break;
+            char err[256];
+            const pokit_cuda_status st = pokit_cuda_moe_decode_layers(moe_, l, 1, hidden_, s, err, sizeof err);
+            if (st != POKIT_CUDA_STATUS_OK) {
+                moe_error_ = err;
+                return st == POKIT_CUDA_STATUS_INVALID_ARGUMENT ? cudaErrorInvalidValue : cudaErrorUnknown;
+            }
+            n += 6;
+            e = cudaGetLastError();
+        }
+        if (e != cudaSuccess) return e;
+        if (logits) {
+            rms_norm_kernel<<<1, 1024, 0, s>>>(hidden_, reinterpret_cast<const float*>(pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT_NORM]),
+                                               eps, xn_, H);
+            e = launch_linear(cfg_.output_type, pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT], static_cast<uint32_t>(cfg_.vocab), H,
+                              xn_, logits_, s);
+            if (e != cudaSuccess) return e;
+            argmax_kernel<<<1, 1024, 0, s>>>(logits_, static_cast<uint32_t>(cfg_.vocab), seq_, pos_,
+                                             static_cast<uint32_t>(cfg_.context + 1), status_);
+            n += 3;
+        }
+        advance_kernel<<<1, 1, 0, s>>>(pos_);
+        ++n;
+        if (launches) *launches = n;
+        return cudaGetLastError();
+    }
+
+    // One token step: a CUDA graph replay after the variant has run once
+    // eagerly (which also sets every kernel attribute); eager launches if the
+    // capture is refused.
+    void step(bool logits, cudaStream_t s = nullptr) {
+        cudaStream_t st = s ? s : stream_;
+        const int v = logits ? 1 : 0;
+        if (!graphs_[v] && (eager_runs_[v] == 0 || no_graphs_)) {
+            uint64_t n = 0;
+            const cudaError_t e = enqueue(logits, st, &n);
+            if (e != cudaSuccess) fail_enqueue(e);
+            ++eager_runs_[v];
+            launches_per_step_ = n;
+            return;
+        }
+        if (!graphs_[v]) {
+            cudaGraph_t g = nullptr;
+            guard(cudaStreamBeginCapture(capture_stream_, cudaStreamCaptureModeThreadLocal), "capture");
+            uint64_t n = 0;
+            const cudaError_t e = enqueue(logits, capture_stream_, &n);
+            const cudaError_t end = cudaStreamEndCapture(capture_stream_, &g);
+            cudaGraphExec_t exec = nullptr;
+            if (e == cudaSuccess && end == cudaSuccess && cudaGraphInstantiate(&exec, g, 0) == cudaSuccess) {
+                graphs_[v] = exec;
+            } else {
+                no_graphs_ = true;          // capture refused: eager launches from now on
+                cudaGetLastError();
+            }
+            if (g) cudaGraphDestroy(g);
+            if (!graphs_[v]) {
+                const cudaError_t e2 = enqueue(logits, st, &n);
+                if (e2 != cudaSuccess) fail_enqueue(e2);
+                return;
+            }
+        }
+        guard(cudaGraphLaunch(graphs_[v], st), "step graph");
+    }
+
+    void fail_enqueue(cudaError_t e) {
+        if (!moe_error_.empty()) {
+            const std::string m = "MoE block: " + moe_error_;
+            moe_error_.clear();
+            if (e == cudaErrorInvalidValue) throw std::invalid_argument(m);
+            failed_ = true;
+            failure_ = m;
+            throw std::runtime_error(m);
+        }
+        guard(e, "decoder step");
+    }
+
+    void sync_and_check() {
+        guard(cudaStreamSynchronize(stream_), "synchronize");
+        uint32_t st = 0;
+        guard(cudaMemcpyAsync(pinned_ids_ + kPinnedIds - 1, status_, 4, cudaMemcpyDeviceToHost, stream_), "status");
+        guard(cudaStreamSynchronize(stream_), "status");
+        st = pinned_ids_[kPinnedIds - 1];
+        char err[256];
+        if (pokit_cuda_moe_synchronize(moe_, stream_, err, sizeof err) != POKIT_CUDA_STATUS_OK) {
+            next_position_ = 0;
+            cudaMemsetAsync(pos_, 0, 4, stream_);
+            throw std::runtime_error(std::string("MoE block: ") + err);
+        }
+        if (st & kStatusDecoderNonFinite) {
+            cudaMemsetAsync(status_, 0, 4, stream_);
+            cudaMemsetAsync(pos_, 0, 4, stream_);
+            cudaStreamSynchronize(stream_);
+            next_position_ = 0;           // the reference resets its state and rethrows
+            throw std::runtime_error("model produced non-finite logits");
+        }
+    }
+
+    pokit_cuda_decoder_config cfg_;
+    size_t window_ = 0, qd_ = 0, kd_ = 0;
+    pokit_cuda_moe* moe_ = nullptr;
+    uint8_t* pool_ = nullptr;
+    uint64_t global_off_[3] = {};
+    uint64_t local_off_[7] = {};
+    std::vector<uint64_t> layer_off_;
+    __half* kcache_ = nullptr;
+    __half* vcache_ = nullptr;
+    float* rope_ = nullptr;          // [context][half] cos, then [context][half] sin
+    void* work_ = nullptr;
+    float *hidden_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *logits_ = nullptr;
+    uint32_t *seq_ = nullptr, *pos_ = nullptr, *status_ = nullptr;
+    uint32_t* pinned_ids_ = nullptr;
+    cudaStream_t stream_ = nullptr, capture_stream_ = nullptr;
+    cudaEvent_t join_ = nullptr;
+    cudaGraphExec_t graphs_[2] = {nullptr, nullptr};
+    int eager_runs_[2] = {0, 0};
+    bool no_graphs_ = false;
+    uint64_t launches_per_step_ = 0;
+    size_t next_position_ = 0;
+    std::string moe_error_;
+    std::mutex mutex_;
+    bool failed_ = false;
+    std::string failure_;
+};
+
+}  // namespace pokit
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+struct pokit_cuda_decoder {
+    explicit pokit_cuda_decoder(const pokit_cuda_decoder_config& c) : impl(c) {}
+    pokit::Decoder impl;
+};
+
+namespace {
+template <typename F>
+pokit_cuda_status dguarded(char* err, size_t cap, F&& body) noexcept {
+    try {
+        body();
+        pokit::set_error(err, cap, "");
+        return POKIT_CUDA_STATUS_OK;
+    } catch (const std::invalid_argument& e) {
+        pokit::set_error(err, cap, e.what());
+        return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    } catch (const std::out_of_range& e) {
+        pokit::set_error(err, cap, e.what());
+        return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    } catch (const std::length_error& e) {
+        pokit::set_error(err, cap, e.what());
+        return POKIT_CUDA_STATUS_INVALID_ARGUMENT;
+    } catch (const std::exception& e) {
+        pokit::set_error(err, cap, e.what());
+        return POKIT_CUDA_STATUS_RUNTIME_ERROR;
+    } catch (...) {
+        pokit::set_error(err, cap, "unknown decoder failure");
+        return POKIT_CUDA_STATUS_INTERNAL_ERROR;
+    }
+}
+}  // namespace
+
+extern "C" {
+
+pokit_cuda_status pokit_cuda_decoder_create(const pokit_cuda_decoder_config* config, pokit_cuda_decoder** out,
+                                            char* error_buffer, size_t error_capacity) {
+    if (out) *out = nullptr;
+    return dguarded(error_buffer, error_capacity, [&] {
+        if (!config || !out) throw std::invalid_argument("configuration and output handle are required");
+        *out = new pokit_cuda_decoder(*config);
+    });
+}
+
+void pokit_cuda_decoder_destroy(pokit_cuda_decoder* decoder) { delete decoder; }
+
+pokit_cuda_moe* pokit_cuda_decoder_moe(pokit_cuda_decoder* decoder) { return decoder ? decoder->impl.moe() : nullptr; }
+
+size_t pokit_cuda_decoder_tensor_bytes(const pokit_cuda_decoder* decoder, size_t layer, uint32_t tensor) {
+    return decoder ? decoder->impl.tensor_bytes(layer, tensor) : 0;
+}
+
+pokit_cuda_status pokit_cuda_decoder_upload_tensor(pokit_cuda_decoder* decoder, size_t layer, uint32_t tensor,
+                                                   const void* host_bytes, size_t bytes, char* error_buffer,
+                                                   size_t error_capacity) {
+    return dguarded(error_buffer, error_capacity, [&] {
+        if (!decoder) throw std::invalid_argument("decoder handle is required");
+        std::lock_guard<std::mutex> lock(decoder->impl.mutex());
+        decoder->impl.upload(layer, tensor, host_bytes, bytes);
+    });
+}
+
+pokit_cuda_status pokit_cuda_decoder_synthesize_tensor(pokit_cuda_decoder* decoder, size_t layer, uint32_t tensor,
+                                                       uint64_t seed, uint64_t stream_id, char* error_buffer,
+                                                       size_t error_capacity) {
+    return dguarded(error_buffer, error_capacity, [&] {
+        if (!decoder) throw std::invalid_argument("decoder handle is required");
+        std::lock_guard<std::mutex> lock(decoder->impl.mutex());
+        decoder->impl.synthesize(layer, tensor, seed, stream_id);
+    });
+}
+
+pokit_cuda_status pokit_cuda_decoder_forward_token(pokit_cuda_decoder* decoder, uint32_t token, uint64_t position,
+                                                   float* logits_host, char* error_buffer, size_t error_capacity) {
+    return dguarded(error_buffer, error_capacity, [&] {
+        if (!decoder) throw std::invalid_argument("decoder handle is required");
+        std::lock_guard<std::mutex> lock(decoder->impl.mutex());
+        decoder->impl.forward_token(token, position, logits_host);
+    });
+}
+
+pokit_cuda_status pokit_cuda_decoder_generate_tokens(pokit_cuda_decoder* decoder, const uint32_t* prompt,
+                                                     size_t prompt_tokens, size_t max_new_tokens,
+                                                     uint32_t* tokens_out, size_t* generated,
+                                                     pokit_cuda_generation_stats* stats, char* error_buffer,
+                                                     size_t error_capacity) {
+    return dguarded(error_buffer, error_capacity, [&] {
+        if (!decoder) throw std::invalid_argument("decoder handle is required");
+        std::lock_guard<std::mutex> lock(decoder->impl.mutex());
+        decoder->impl.generate(prompt, prompt_tokens, max_new_tokens, tokens_out, generated, stats);
+    });
+}
+
+pokit_cuda_status pokit_cuda_decoder_run_steps(pokit_cuda_decoder* decoder, size_t steps, void* stream,
+                                               char* error_buffer, size_t error_capacity) {
+    return dguarded(error_buffer, error_capacity, [&] {
+        if (!decoder) throw std::invalid_argument("decoder handle is required");
+        std::lock_guard<std::mutex> lock(decoder->impl.mutex());
+        decoder->impl.run_steps(steps, static_cast<cudaStream_t>(stream));
+    });
+}
+
+pokit_cuda_status pokit_cuda_decoder_reset(pokit_cuda_decoder* decoder, char* error_buffer, size_t error_capacity) {
+    return dguarded(error_buffer, error_capacity, [&] {
+        if (!decoder) throw std::invalid_argument("decoder handle is required");
+        std::lock_guard<std::mutex> lock(decoder->impl.mutex());
+        decoder->impl.reset();
+    });
+}
+
+uint64_t pokit_cuda_decoder_launches_per_step(const pokit_cuda_decoder* decoder) {
+    return decoder ? decoder->impl.launches_per_step() : 0;
+}
+
+}  // extern "C"

@@ -10,10 +10,11 @@ namespace pokit {
 
 int device_sm_count();
 
-// y[rows] = W[rows, cols] . x for a GGUF-encoded W (F32, Q8_0, Q4_K, Q5_K, Q6_K).
+// y[rows] = W[rows, cols] . x for a GGUF-encoded W (F32, Q8_0, Q4_K, Q5_K, Q6_K);
+// with accumulate, y[rows] += W . x.
 cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
                           const float* x, float* y, cudaStream_t stream,
-                          bool force_generic = false);
+                          bool force_generic = false, bool accumulate = false);
 
 // out[rows, cols] = decoded weights, bit-identical to the reference decoders.
 cudaError_t launch_dequantize(uint32_t type, const void* w, uint32_t rows, uint32_t cols,

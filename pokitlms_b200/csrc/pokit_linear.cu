@@ -7,6 +7,9 @@
 #include "pokit_kernels.h"
 #include "pokit_quant.cuh"
 
+#include <map>
+#include <mutex>
+
 namespace pokit {
 namespace {
 
@@ -16,7 +19,7 @@ constexpr int kLinearThreads = 256;
 // prepares x once and then streams its rows.
 __global__ void __launch_bounds__(kLinearThreads)
 linear_q4k_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols,
-                  const float* __restrict__ x, float* __restrict__ y) {
+                  const float* __restrict__ x, float* __restrict__ y, int accumulate) {
     extern __shared__ float smem[];
     const int nsb = static_cast<int>(cols >> 8);
     float* xp = smem;                                  // nsb*4*68 floats
@@ -45,14 +48,14 @@ linear_q4k_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols,
         }
         acc += __shfl_xor_sync(0xffffffffu, acc, 1);
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        if (c == 0 && row < rows) y[row] = acc;
+        if (c == 0 && row < rows) y[row] = accumulate ? y[row] + acc : acc;
     }
 }
 
 // F32: one warp per row, 128-bit loads straight from global.
 __global__ void __launch_bounds__(kLinearThreads)
 linear_f32_kernel(const float* __restrict__ w, uint32_t rows, uint32_t cols,
-                  const float* __restrict__ x, float* __restrict__ y) {
+                  const float* __restrict__ x, float* __restrict__ y, int accumulate) {
     const int lane = threadIdx.x & 31;
     const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
     for (uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
@@ -72,7 +75,7 @@ linear_f32_kernel(const float* __restrict__ w, uint32_t rows, uint32_t cols,
             for (uint32_t i = lane; i < cols; i += 32u) acc = fmaf(__ldg(rp + i), x[i], acc);
         }
         acc = warp_sum(acc);
-        if (lane == 0) y[row] = acc;
+        if (lane == 0) y[row] = accumulate ? y[row] + acc : acc;
     }
 }
 
@@ -81,7 +84,7 @@ linear_f32_kernel(const float* __restrict__ w, uint32_t rows, uint32_t cols,
 template <uint32_t T>
 __global__ void __launch_bounds__(kLinearThreads)
 linear_generic_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols,
-                      const float* __restrict__ x, float* __restrict__ y) {
+                      const float* __restrict__ x, float* __restrict__ y, int accumulate) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     float* xs = reinterpret_cast<float*>(smem_raw);
     const uint32_t rbytes = static_cast<uint32_t>(row_bytes(T, cols));
@@ -99,63 +102,8 @@ linear_generic_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t col
         float acc = 0.0f;
         for (int g = lane; g < groups; g += 32) acc += group_dot<T>(my_row, g, xs);
         acc = warp_sum(acc);
-        if (lane == 0) y[row] = acc;
+        if (lane == 0) y[row] = accumulate ? y[row] + acc : acc;
         __syncwarp();
-    }
-}
-
-// Bit-exact decoders (explicit round-to-nearest operations so the compiler
-// cannot contract them into FMAs): same expressions as the reference's
-// decode_q4_k / decode_q5_k / decode_q6_k / Q8_0 scale (quantized_linear.cpp).
-template <uint32_t T>
-__device__ __forceinline__ void group_decode(const uint8_t* __restrict__ row, int g,
-                                             float* __restrict__ out) {
-    if constexpr (T == kF32) {
-        const float* w = reinterpret_cast<const float*>(row) + g * 32;
-        for (int i = 0; i < 32; ++i) out[i] = w[i];
-    } else if constexpr (T == kQ8_0) {
-        const uint8_t* blk = row + g * 34;
-        const float d = half_bits_to_float(sm_u16(blk));
-        const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
-        for (int i = 0; i < 32; ++i) out[i] = __fmul_rn(d, static_cast<float>(q[i]));
-    } else if constexpr (T == kQ4_K || T == kQ5_K) {
-        const int sb = g >> 3, j = g & 7;
-        const uint8_t* blk = row + sb * block_bytes(T);
-        const float d = half_bits_to_float(sm_u16(blk));
-        const float dmin = half_bits_to_float(sm_u16(blk + 2));
-        const uint8_t* packed = blk + 4;
-        uint32_t sc, mn;
-        if (j < 4) {
-            sc = packed[j] & 63u; mn = packed[j + 4] & 63u;
-        } else {
-            sc = (packed[j + 4] & 0x0fu) | ((packed[j - 4] >> 6) << 4);
-            mn = (packed[j + 4] >> 4) | ((packed[j] >> 6) << 4);
-        }
-        const float ds = __fmul_rn(d, static_cast<float>(sc));
-        const float dm = __fmul_rn(dmin, static_cast<float>(mn));
-        const int chunk = j >> 1, part = j & 1;
-        const uint8_t* qs = blk + (T == kQ4_K ? 16 : 48) + chunk * 32;
-        const uint8_t* qh = blk + 16;
-        for (int i = 0; i < 32; ++i) {
-            uint32_t q = part ? (qs[i] >> 4) : (qs[i] & 0x0fu);
-            if constexpr (T == kQ5_K) q += (qh[i] & (1u << (2 * chunk + part))) ? 16u : 0u;
-            out[i] = __fsub_rn(__fmul_rn(ds, static_cast<float>(q)), dm);
-        }
-    } else if constexpr (T == kQ6_K) {
-        const int sb = g >> 3, j = g & 7;
-        const uint8_t* blk = row + sb * 210;
-        const float d = half_bits_to_float(sm_u16(blk + 208));
-        const int half = j >> 2, jj = j & 3;
-        const uint8_t* ql = blk + half * 64 + (jj & 1) * 32;
-        const uint8_t* qh = blk + 128 + half * 32;
-        const int8_t* scales = reinterpret_cast<const int8_t*>(blk + 192 + half * 8);
-        const int shift_lo = (jj >> 1) * 4, shift_hi = jj * 2;
-        for (int l = 0; l < 32; ++l) {
-            const int q = static_cast<int>(((ql[l] >> shift_lo) & 0x0fu) |
-                                           (((qh[l] >> shift_hi) & 0x03u) << 4)) - 32;
-            out[l] = __fmul_rn(__fmul_rn(d, static_cast<float>(scales[l / 16 + 2 * jj])),
-                               static_cast<float>(q));
-        }
     }
 }
 
@@ -190,16 +138,27 @@ int sm_count_cached() {
     return count;
 }
 
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device);
+// the attribute is per device, and later launches skip the call.
 template <typename K>
 cudaError_t set_smem(K kernel, size_t bytes) {
     if (bytes <= 48u * 1024u) return cudaSuccess;
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(bytes));
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> granted;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& have = granted[{reinterpret_cast<const void*>(kernel), dev}];
+    if (bytes <= have) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess) have = bytes;
+    return e;
 }
 
 template <uint32_t T>
 cudaError_t launch_generic(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, bool accumulate) {
     const size_t stage = (row_bytes(T, cols) + 15u) & ~size_t(15);
     const size_t smem = static_cast<size_t>(cols) * 4u + stage * (kLinearThreads / 32);
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;
@@ -210,7 +169,7 @@ cudaError_t launch_generic(const void* w, uint32_t rows, uint32_t cols, const fl
     const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 4u;
     if (grid > cap) grid = cap;
     linear_generic_kernel<T><<<grid, kLinearThreads, smem, stream>>>(
-        static_cast<const uint8_t*>(w), rows, cols, x, y);
+        static_cast<const uint8_t*>(w), rows, cols, x, y, accumulate ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -236,7 +195,7 @@ cudaError_t launch_dequant(const void* w, uint32_t rows, uint32_t cols, float* o
 int device_sm_count() { return sm_count_cached(); }
 
 cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
-                          const float* x, float* y, cudaStream_t stream, bool force_generic) {
+                          const float* x, float* y, cudaStream_t stream, bool force_generic, bool accumulate) {
     if (rows == 0 || cols == 0) return cudaErrorInvalidValue;
     switch (type) {
         case kF32: {
@@ -245,7 +204,7 @@ cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t 
             const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 8u;
             if (grid > cap) grid = cap;
             linear_f32_kernel<<<grid, kLinearThreads, 0, stream>>>(
-                static_cast<const float*>(w), rows, cols, x, y);
+                static_cast<const float*>(w), rows, cols, x, y, accumulate ? 1 : 0);
             return cudaGetLastError();
         }
         case kQ4_K: {
@@ -261,14 +220,14 @@ cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t 
                 const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 2u;
                 if (grid > cap) grid = cap;
                 linear_q4k_kernel<<<grid, kLinearThreads, smem, stream>>>(
-                    static_cast<const uint8_t*>(w), rows, cols, x, y);
+                    static_cast<const uint8_t*>(w), rows, cols, x, y, accumulate ? 1 : 0);
                 return cudaGetLastError();
             }
-            return launch_generic<kQ4_K>(w, rows, cols, x, y, stream);
+            return launch_generic<kQ4_K>(w, rows, cols, x, y, stream, accumulate);
         }
-        case kQ5_K: return launch_generic<kQ5_K>(w, rows, cols, x, y, stream);
-        case kQ6_K: return launch_generic<kQ6_K>(w, rows, cols, x, y, stream);
-        case kQ8_0: return launch_generic<kQ8_0>(w, rows, cols, x, y, stream);
+        case kQ5_K: return launch_generic<kQ5_K>(w, rows, cols, x, y, stream, accumulate);
+        case kQ6_K: return launch_generic<kQ6_K>(w, rows, cols, x, y, stream, accumulate);
+        case kQ8_0: return launch_generic<kQ8_0>(w, rows, cols, x, y, stream, accumulate);
         default: return cudaErrorInvalidValue;
     }
 }

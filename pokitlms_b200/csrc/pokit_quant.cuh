@@ -458,4 +458,60 @@ __device__ __forceinline__ uint32_t warp_stage_span(const uint8_t* __restrict__ 
     return delta;
 }
 
+// Bit-exact decoders (explicit round-to-nearest operations so the compiler
+// cannot contract them into FMAs): same expressions as the reference's
+// decode_q4_k / decode_q5_k / decode_q6_k / Q8_0 scale (quantized_linear.cpp).
+template <uint32_t T>
+__device__ __forceinline__ void group_decode(const uint8_t* __restrict__ row, int g,
+                                             float* __restrict__ out) {
+    if constexpr (T == kF32) {
+        const float* w = reinterpret_cast<const float*>(row) + g * 32;
+        for (int i = 0; i < 32; ++i) out[i] = w[i];
+    } else if constexpr (T == kQ8_0) {
+        const uint8_t* blk = row + g * 34;
+        const float d = half_bits_to_float(sm_u16(blk));
+        const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
+        for (int i = 0; i < 32; ++i) out[i] = __fmul_rn(d, static_cast<float>(q[i]));
+    } else if constexpr (T == kQ4_K || T == kQ5_K) {
+        const int sb = g >> 3, j = g & 7;
+        const uint8_t* blk = row + sb * block_bytes(T);
+        const float d = half_bits_to_float(sm_u16(blk));
+        const float dmin = half_bits_to_float(sm_u16(blk + 2));
+        const uint8_t* packed = blk + 4;
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = packed[j] & 63u; mn = packed[j + 4] & 63u;
+        } else {
+            sc = (packed[j + 4] & 0x0fu) | ((packed[j - 4] >> 6) << 4);
+            mn = (packed[j + 4] >> 4) | ((packed[j] >> 6) << 4);
+        }
+        const float ds = __fmul_rn(d, static_cast<float>(sc));
+        const float dm = __fmul_rn(dmin, static_cast<float>(mn));
+        const int chunk = j >> 1, part = j & 1;
+        const uint8_t* qs = blk + (T == kQ4_K ? 16 : 48) + chunk * 32;
+        const uint8_t* qh = blk + 16;
+        for (int i = 0; i < 32; ++i) {
+            uint32_t q = part ? (qs[i] >> 4) : (qs[i] & 0x0fu);
+            if constexpr (T == kQ5_K) q += (qh[i] & (1u << (2 * chunk + part))) ? 16u : 0u;
+            out[i] = __fsub_rn(__fmul_rn(ds, static_cast<float>(q)), dm);
+        }
+    } else if constexpr (T == kQ6_K) {
+        const int sb = g >> 3, j = g & 7;
+        const uint8_t* blk = row + sb * 210;
+        const float d = half_bits_to_float(sm_u16(blk + 208));
+        const int half = j >> 2, jj = j & 3;
+        const uint8_t* ql = blk + half * 64 + (jj & 1) * 32;
+        const uint8_t* qh = blk + 128 + half * 32;
+        const int8_t* scales = reinterpret_cast<const int8_t*>(blk + 192 + half * 8);
+        const int shift_lo = (jj >> 1) * 4, shift_hi = jj * 2;
+        for (int l = 0; l < 32; ++l) {
+            const int q = static_cast<int>(((ql[l] >> shift_lo) & 0x0fu) |
+                                           (((qh[l] >> shift_hi) & 0x03u) << 4)) - 32;
+            out[l] = __fmul_rn(__fmul_rn(d, static_cast<float>(scales[l / 16 + 2 * jj])),
+                               static_cast<float>(q));
+        }
+    }
+}
+
+
 }  // namespace pokit
