@@ -544,6 +544,7 @@ def measure_decoder(device: int, stream, new_tokens: int = 128, layers: int = 48
     torch.cuda.synchronize()
     step_us = a.elapsed_time(b) * 1e3 / steps
     launches = dec.launches_per_step()
+    graphs, why = dec.step_graphs()
     dec.close()
     peaks = measured_peaks()
     tb = decoder_token_bytes(shape)
@@ -558,6 +559,7 @@ def measure_decoder(device: int, stream, new_tokens: int = 128, layers: int = 48
         "hbm": {"bytes_per_token": tb, "achieved_gbs": gbs, "frac": gbs / peaks["hbm_gbs"],
                 "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]},
         "gpu_launches_per_token": int(launches),
+        "step_graphs": graphs, **({"capture_refused": why} if why else {}),
         "first_ids": [int(i) for i in ids[:8]],
     }
 
@@ -579,10 +581,20 @@ CFG5_WORKLOAD = ("qwen3-235b-a22b-shaped MoE expert path: 94 MoE FFN layers (hid
 
 
 def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_over_ranks,
-                        shape: dict | None = None) -> None:
-    """Expert-parallel decode (module docstring).  Default shape: configuration 2
-    with one token per rank per step; `shape` = CFG5 runs configuration 5
-    (64 tokens per step whatever the rank count)."""
+                        shape: dict | None = None, emit: bool = True, steps: int | None = None,
+                        warmup: int | None = None) -> dict:
+    """Expert-parallel decode.  Default shape: configuration 2 with one token per
+    rank per step (--workload ep-decode); `shape` = CFG5 runs configuration 5
+    (64 tokens per step whatever the rank count), with a parity object (the
+    all-reduced block output of layer 0 on the last step's rows against one
+    whole-pool handle on rank 0, and whether every rank holds the same bits)
+    and, for N > 1, the exchange step timed both ways (NCCL all-reduce of the
+    [64, 4096] partial against the two all-to-alls of the same bytes that a
+    dispatch/combine design would make).  Returns the line; prints it on rank 0
+    when `emit`."""
+    import argparse as _ap
+    args = _ap.Namespace(**{**vars(args), **({"steps": steps} if steps else {}),
+                            **({"warmup": warmup} if warmup else {})})
     import torch
     import torch.distributed as dist
     from pokitlms_b200 import synth
@@ -709,6 +721,57 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
              ["router", "route", "group", "pack_x", "gate_up_gemm", "pack_act", "down_gemm", "combine"])
     st = be.time_batch(0, x, part, logits=route_logits[0] if cfg5 else None, reps=20)
     stage_us = {"layer": 0, **{n_: round(v, 2) for n_, v in zip(names, st)}}
+    parity = None
+    if cfg5:
+        from pokitlms_b200 import backend as B
+        lg0 = route_logits[0]
+        ep.forward_batch(0, x, part, logits=lg0)          # the whole block's output on every rank
+        torch.cuda.synchronize()
+        sig = part.view(torch.int32).to(torch.int64).sum().reshape(1)
+        sigs = [torch.zeros_like(sig) for _ in range(world)]
+        if world > 1:
+            dist.all_gather(sigs, sig)
+        else:
+            sigs = [sig]
+        same = all(int(v) == int(sig) for v in sigs)
+        if rank == 0:
+            full = B.CudaMoeBackend(layers=1, hidden=Hs, inter=Is, experts=E, top_k=K_TOP, rms_epsilon=EPS,
+                                    device=local)
+            full.upload_tensor(0, ROUTER, synth.router_weights(E, Hs, SEED, 0))
+            for t in (GATE, UP, DOWN):
+                full.synthesize_tensor(0, t, SEED, synth.stream_id(0, t))
+            ref = torch.empty_like(part)
+            full.forward_batch(0, x, ref, logits=lg0)
+            full.synchronize()
+            full.close()
+            err = ((part - ref).abs().amax(dim=1) / ref.pow(2).mean(dim=1).sqrt()).max()
+            parity = {"tokens": T, "max_err_over_rms": float(err), "bar": 1e-3, "ranks_bitwise_equal": same,
+                      "reference": "layer 0, the last step's rows and logits: one whole-pool handle on rank 0"}
+        barrier()
+    exchange = None
+    if world > 1:
+        buf = torch.randn(T * Hs, device="cuda")
+        out = torch.empty_like(buf)
+
+        def timed(fn, reps=20):
+            fn()
+            torch.cuda.synchronize()
+            barrier()
+            ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ea.record()
+            for _ in range(reps):
+                fn()
+            eb.record()
+            torch.cuda.synchronize()
+            return max_over_ranks(ea.elapsed_time(eb) * 1e3 / reps)
+
+        def a2a2():
+            dist.all_to_all_single(out, buf)
+            dist.all_to_all_single(buf, out)
+
+        exchange = {"bytes": T * Hs * 4, "all_reduce_us": timed(lambda: dist.all_reduce(buf)),
+                    "all_to_all_x2_us": timed(a2a2),
+                    "how": "NCCL, CUDA events on the rank, max over ranks, 20 back to back"}
     barrier()
     graph_used = graph is not None
     graph = None                      # release the graph (it holds NCCL calls) before the group goes
@@ -722,8 +785,7 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     else:
         per_rank_bytes = K_TOP * expert_bytes
     per_rank_gbs = per_rank_bytes / (ms_per_step / 1e3 / layers) / 1e9
-    if rank == 0:
-        print(json.dumps({
+    line = {
             "metric": METRIC, "value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong" if cfg5 else "weak", "vs_baseline": None,
@@ -749,8 +811,13 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
                     "d2h_bytes_per_step": T * Hs * 4},
             "gpu_launches": int(gpu_launches), "clocks": clocks, "cpu_baseline": None,
             **({"stage_us": stage_us} if stage_us else {}),
-        }))
+            **({"parity": parity} if parity else {}),
+            **({"exchange": exchange} if exchange else {}),
+    }
+    if emit and rank == 0:
+        print(json.dumps(line))
     ep.close()
+    return line
 
 
 def main() -> None:
@@ -762,17 +829,19 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config5", action="store_true", help="skip the configuration-5 object of the line")
     ap.add_argument("--ep-combine", default="nccl", choices=["peer", "nccl"],
                     help="N > 1: sum the shards' outputs in the block's last kernel over NVLink peer memory "
                          "(peer) or with an NCCL all-reduce (nccl)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "chain", "decoder", "grouped", "config3", "config5"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "chain", "decoder", "grouped", "config3", "config5", "ep-decode"],
                     help="decoder: only configuration 2's whole decoder (one GPU; --layers shortens it); "
                          "chain: only the decode chain of the headline (one GPU; --layers shortens it; a small "
                          "process for profiling moe_chain_kernel); "
                          "grouped: only the configuration-4 measurement (one GPU; a small process for "
                          "profiling the grouped kernels); config3: only the configuration-3 chain (one "
                          "GPU; --layers shortens it); config5: configuration 5 (94 layers, hidden "
-                         "4096, batch 64) through the expert-parallel path on 1..N GPUs")
+                         "4096, batch 64) through the expert-parallel path on 1..N GPUs; ep-decode: configuration "
+                         "2 with one token per rank per step through expert parallelism")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -835,10 +904,13 @@ def main() -> None:
         if world > 1:
             dist.destroy_process_group()
         return
-    if world > 1:
+    if args.workload == "ep-decode":
         run_expert_parallel(args, rank, world, local, barrier, max_over_ranks)
-        dist.destroy_process_group()
+        if world > 1:
+            dist.destroy_process_group()
         return
+    # N >= 1: every rank decodes its own sequence on its own copy of the model
+    # (independent replicas: 16.3 GB fits one GPU's HBM), no data-path collective.
     be = B.CudaMoeBackend(layers=layers, hidden=H, inter=I, experts=E, top_k=K_TOP,
                           rms_epsilon=EPS, device=local)
     build_model(be, layers)
@@ -919,11 +991,28 @@ def main() -> None:
     phases["gate_up_gbs"] = GATE_UP_BYTES / (gu * 1e-6) / 1e9
     phases["gate_up_frac"] = phases["gate_up_gbs"] / peaks["hbm_gbs"]
 
+    # Replicas run the same weights: the same input must give the same bits on
+    # every rank (and rank 0's is the single-GPU result).
+    probe = synth.activation(H, SEED, 424_242)
+    probe_out = np.empty(H, dtype=np.float32)
+    be.decode_layers_host(0, layers, probe, probe_out)
+    sig = torch.tensor([int(probe_out.view(np.int32).astype(np.int64).sum())], dtype=torch.int64, device="cuda")
+    sigs = [torch.zeros_like(sig) for _ in range(world)]
+    if world > 1:
+        dist.all_gather(sigs, sig)
+    else:
+        sigs = [sig]
+    parity = {"replicas_bitwise_equal": all(int(v) == int(sig) for v in sigs), "ranks": world,
+              "probe": f"one {layers}-layer chain on a common seeded input, bit signature gathered from every rank",
+              "finite": bool(np.all(np.isfinite(probe_out)))}
+
     chain_only = args.workload == "chain"
-    decoder = None if chain_only else measure_decoder(local, stream)
-    grouped = None if chain_only else measure_grouped(local, stream)
-    config3 = None if chain_only else measure_config3(local, stream, steps=max(args.steps // 10, 20),
-                                                      cpu_seconds=None if (args.no_cpu_baseline or rank != 0) else 6.0)
+    one_gpu = world == 1 and not chain_only
+    decoder = measure_decoder(local, stream) if one_gpu else None
+    grouped = measure_grouped(local, stream) if one_gpu else None
+    config3 = (measure_config3(local, stream, steps=max(args.steps // 10, 20),
+                               cpu_seconds=None if (args.no_cpu_baseline or rank != 0) else 6.0)
+               if one_gpu else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -934,6 +1023,19 @@ def main() -> None:
             grouped["cpu_baseline"] = {"value": v * LAYERS, "unit": "tokens/s", "cores": cores, "kind": kind,
                                        "sample": sample + "; one config-4 token = one of those block evaluations"}
 
+    # Configuration 5 (expert parallel over all ranks, strong scaling): the
+    # replica model is released first (the whole-pool config-5 model is 128 GB
+    # on one GPU).
+    be.close()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    config5 = None
+    if not chain_only and not args.no_config5:
+        config5 = run_expert_parallel(args, rank, world, local, barrier, max_over_ranks, shape=CFG5, emit=False,
+                                      steps=20, warmup=3)
+        for k in ("metric", "n_gpus", "higher_is_better", "vs_baseline", "dtype", "cpu_baseline"):
+            config5.pop(k, None)
+
     if rank == 0:
         print(json.dumps({
             "metric": METRIC, "value": tokens_per_s, "unit": "tokens/s", "n_gpus": world,
@@ -942,7 +1044,10 @@ def main() -> None:
             "data": "synthetic (seed 0): Q4_K experts synthesised in HBM, F32 router N(0,0.02)",
             "config": {"workload": WORKLOAD, "layers": layers, "hidden": H, "experts": E,
                        "top_k": K_TOP, "inter": I, "expert_type": "Q4_K",
-                       "parallelism": "single GPU (N > 1 runs expert parallelism)",
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"{world} independent replicas: each GPU decodes its own sequence on its "
+                                       "own copy of the 16.3 GB model, no data-path collective; expert "
+                                       "parallelism is the config5 object"),
                        "l2": "no flush: each step streams 1.07 GB of distinct weights (> 126 MB L2)"},
             "routed_expert_gbs": routed_gbs,
             "routed_expert_frac_of_peak": routed_gbs / peaks["hbm_gbs"],
@@ -964,8 +1069,9 @@ def main() -> None:
             **({"decoder": decoder} if decoder is not None else {}),
             **({"grouped": grouped} if grouped is not None else {}),
             **({"config3": config3} if config3 is not None else {}),
+            "parity": parity,
+            **({"config5": config5} if config5 is not None else {}),
         }))
-    be.close()
 
 
 if __name__ == "__main__":

@@ -529,6 +529,11 @@ pokit_cuda_status pokit_cuda_decoder_reset(pokit_cuda_decoder* decoder, char* er
 /* Kernels one token step with logits launches (measurement). */
 uint64_t pokit_cuda_decoder_launches_per_step(const pokit_cuda_decoder* decoder);
 
+/* How many of the two token-step variants (with and without logits) replay
+ * as CUDA graphs (measurement); when a capture was refused, reason_buffer (may
+ * be NULL) receives why and the steps run as plain launches. */
+int pokit_cuda_decoder_step_graphs(const pokit_cuda_decoder* decoder, char* reason_buffer, size_t reason_capacity);
+
 /* ------------------------------------------------------------------------ */
 /* One MoE block without any device allocation                              */
 /* ------------------------------------------------------------------------ */

@@ -195,6 +195,7 @@ SIGNATURES = {
     "pokit_cuda_decoder_run_steps": (C.c_int, [_VP, _SZ, _VP, _ERR, _SZ]),
     "pokit_cuda_decoder_reset": (C.c_int, [_VP, _ERR, _SZ]),
     "pokit_cuda_decoder_launches_per_step": (C.c_uint64, [_VP]),
+    "pokit_cuda_decoder_step_graphs": (C.c_int, [_VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_static_scratch": (C.c_int, [C.POINTER(MoeBlockDevice), _VP, _VP, _VP,
                                                         _VP, _VP, _ERR, _SZ]),
 }

@@ -398,6 +398,12 @@ class CudaDecoder:
     def launches_per_step(self) -> int:
         return int(lib().pokit_cuda_decoder_launches_per_step(self._h))
 
+    def step_graphs(self) -> tuple[int, str]:
+        """(token-step variants replayed as CUDA graphs, why a capture was refused)."""
+        buf = C.create_string_buffer(256)
+        n = lib().pokit_cuda_decoder_step_graphs(self._h, buf, 256)
+        return int(n), buf.value.decode()
+
     def close(self) -> None:
         if self._h:
             self.moe._h = None

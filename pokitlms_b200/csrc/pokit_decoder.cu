@@ -38,6 +38,7 @@ namespace {
 constexpr uint32_t kStatusDecoderNonFinite = 1u;   // LM head produced NaN/Inf (the reference throws)
 constexpr uint32_t kMaxHeadDim = 256;
 constexpr uint32_t kMaxWindow = 8192;
+constexpr uint32_t kArgmaxCtas = 148;
 
 template <typename T, typename Op>
 __device__ __forceinline__ T block_reduce_all(T v, T* red, Op op) {
@@ -106,74 +107,153 @@ __global__ void attn_prep_kernel(const float* __restrict__ qkv, const float* __r
 
 // GQA decode attention of one query head over the ring's last min(pos + 1,
 // window) positions, oldest first (KvCache::attend, kv_cache.cpp:185-294):
-// scores = q . k * scale, softmax, out = sum_j (e_j / sum e) v_j.
-__global__ void attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                              const __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, uint32_t window,
-                              uint32_t qh, uint32_t kvh, float scale, float* __restrict__ out) {
+// scores = q . k * scale, softmax, out = sum_j (e_j / sum e) v_j.  Eight warps
+// score four positions each per pass (loads of all four in flight); for the
+// output, threads t and t + d sum the even and odd positions of dimension t
+// (eight loads in flight), added in position-pair order at the end.
+constexpr uint32_t kAttendThreads = 256;
+
+__global__ void __launch_bounds__(kAttendThreads)
+attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
+              const uint32_t* __restrict__ pos_p, uint32_t window, uint32_t qh, uint32_t kvh, uint32_t d, float scale,
+              float* __restrict__ out) {
     extern __shared__ float sc[];
     __shared__ float red[32];
-    const uint32_t d = blockDim.x, t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
+    __shared__ float part[kAttendThreads];
+    const uint32_t t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
     const uint32_t kh = h / (qh / kvh);
     const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
-    const int lane = t & 31, warp = t >> 5, nwarps = (d + 31) >> 5;
-    const float* qv = q + h * d;
-    for (uint32_t j = warp; j < n; j += nwarps) {
-        const __half* k = kc + (static_cast<uint64_t>((first + j) % window) * kvh + kh) * d;
-        float dot = 0.0f;
-        for (uint32_t e = lane; e < d; e += 32) dot = fmaf(qv[e], __half2float(k[e]), dot);
-        dot = warp_sum(dot);
-        if (lane == 0) sc[j] = dot * scale;
+    const int lane = t & 31, warp = t >> 5;
+    constexpr int kWarpsA = kAttendThreads / 32;
+    const uint32_t per = d / 32;                        // dimensions per lane (d <= 256)
+    float qv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qv[e] = e < static_cast<int>(per) ? q[h * d + lane * per + e] : 0.0f;
+    const auto key = [&](uint32_t j) {
+        return kc + (static_cast<uint64_t>((first + j) % window) * kvh + kh) * d + lane * per;
+    };
+    for (uint32_t j0 = warp; j0 < n; j0 += 4 * kWarpsA) {
+        float dots[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t j = j0 + u * kWarpsA;
+            float dot = 0.0f;
+            if (j < n) {
+                const __half* k = key(j);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    if (e < static_cast<int>(per)) dot = fmaf(qv[e], __half2float(k[e]), dot);
+            }
+            dots[u] = dot;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float dsum = warp_sum(dots[u]);
+            const uint32_t j = j0 + u * kWarpsA;
+            if (lane == 0 && j < n) sc[j] = dsum * scale;
+        }
     }
     __syncthreads();
     float m = -INFINITY;
-    for (uint32_t j = t; j < n; j += d) m = fmaxf(m, sc[j]);
+    for (uint32_t j = t; j < n; j += kAttendThreads) m = fmaxf(m, sc[j]);
     m = block_reduce_all(m, red, [](float a, float b) { return fmaxf(a, b); });
     float den = 0.0f;
-    for (uint32_t j = t; j < n; j += d) {
+    for (uint32_t j = t; j < n; j += kAttendThreads) {
         const float e = expf(sc[j] - m);
         sc[j] = e;
         den += e;
     }
     den = block_reduce_all(den, red, [](float a, float b) { return a + b; });
+    const uint32_t dim = t % d, grp = t / d, groups = kAttendThreads / d;
     float acc = 0.0f;
-    for (uint32_t j = 0; j < n; ++j) {
-        const __half* vv = vc + (static_cast<uint64_t>((first + j) % window) * kvh + kh) * d;
-        acc = fmaf(sc[j] / den, __half2float(vv[t]), acc);
+    if (grp < groups) {
+        uint32_t j = grp;
+        for (; j + 7 * groups < n; j += 8 * groups) {
+            float vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                vv[u] = __half2float(vc[(static_cast<uint64_t>((first + j + u * groups) % window) * kvh + kh) * d + dim]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = fmaf(sc[j + u * groups] / den, vv[u], acc);
+        }
+        for (; j < n; j += groups)
+            acc = fmaf(sc[j] / den, __half2float(vc[(static_cast<uint64_t>((first + j) % window) * kvh + kh) * d + dim]), acc);
     }
-    out[h * d + t] = acc;
+    part[t] = acc;
+    __syncthreads();
+    if (grp == 0) {
+        for (uint32_t g = 1; g < groups; ++g) acc += part[g * d + dim];
+        out[h * d + dim] = acc;
+    }
 }
 
 // Greedy sampling (qwen3_moe_runner.cpp:320-333): the first maximum of the
 // logits becomes token position + 1 of the sequence; a non-finite logit sets
-// the status word (the reference throws).
-__global__ void argmax_kernel(const float* __restrict__ logits, uint32_t n, uint32_t* __restrict__ seq,
-                              const uint32_t* __restrict__ pos_p, uint32_t seq_cap, uint32_t* __restrict__ status) {
+// the status word (the reference throws).  Each CTA reduces a slice to its
+// (value, index) pair; the CTA that arrives last combines them, larger value
+// first and the lower index on ties, and leaves the arrival counter at zero.
+__device__ __forceinline__ void better(float& v, uint32_t& i, float ov, uint32_t oi) {
+    if (oi != 0xffffffffu && (i == 0xffffffffu || ov > v || (ov == v && oi < i))) {
+        v = ov;
+        i = oi;
+    }
+}
+
+__device__ void block_best(float& v, uint32_t& i, float* rv, uint32_t* ri) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+        better(v, i, ov, oi);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) { rv[warp] = v; ri[warp] = i; }
+    __syncthreads();
+    v = rv[0];
+    i = ri[0];
+    for (int w = 1; w < static_cast<int>((blockDim.x + 31) >> 5); ++w) better(v, i, rv[w], ri[w]);
+}
+
+__global__ void argmax_kernel(const float* __restrict__ logits, uint32_t n, float* __restrict__ part_v,
+                              uint32_t* __restrict__ part_i, uint32_t* __restrict__ arrivals,
+                              uint32_t* __restrict__ seq, const uint32_t* __restrict__ pos_p, uint32_t seq_cap,
+                              uint32_t* __restrict__ status) {
     __shared__ float rv[32];
     __shared__ uint32_t ri[32];
+    __shared__ uint32_t last;
+    const uint32_t per = (n + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(n, lo + per);
     float best = -INFINITY;
     uint32_t bi = 0xffffffffu;
     int bad = 0;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float v = logits[i];
         if (!isfinite(v)) bad = 1;
-        else if (v > best || bi == 0xffffffffu) { best = v; bi = i; }
+        else if (bi == 0xffffffffu || v > best) { best = v; bi = i; }
     }
     bad = __syncthreads_or(bad);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi != 0xffffffffu && (bi == 0xffffffffu || ov > best || (ov == best && oi < bi))) { best = ov; bi = oi; }
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) { rv[warp] = best; ri[warp] = bi; }
-    __syncthreads();
+    block_best(best, bi, rv, ri);
     if (threadIdx.x == 0) {
-        for (int w = 1; w < static_cast<int>((blockDim.x + 31) >> 5); ++w)
-            if (ri[w] != 0xffffffffu && (bi == 0xffffffffu || rv[w] > best || (rv[w] == best && ri[w] < bi))) {
-                best = rv[w];
-                bi = ri[w];
-            }
+        part_v[blockIdx.x] = best;
+        part_i[blockIdx.x] = bad ? 0xfffffffeu : bi;
+        __threadfence();
+        last = atomicAdd(arrivals, 1u) == gridDim.x - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    best = -INFINITY;
+    bi = 0xffffffffu;
+    bad = 0;
+    for (uint32_t b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
+        const uint32_t oi = __ldcg(part_i + b);
+        if (oi == 0xfffffffeu) bad = 1;
+        else better(best, bi, __ldcg(part_v + b), oi);
+    }
+    bad = __syncthreads_or(bad);
+    block_best(best, bi, rv, ri);
+    if (threadIdx.x == 0) {
+        *arrivals = 0u;
         if (bad) atomicOr(status, kStatusDecoderNonFinite);
         const uint32_t p = *pos_p;
         if (p + 1 < seq_cap) seq[p + 1] = bad || bi == 0xffffffffu ? 0u : bi;
@@ -400,6 +480,8 @@ public:
 
     size_t position() const { return next_position_; }
     uint64_t launches_per_step() const { return launches_per_step_; }
+    int step_graphs() const { return (graphs_[0] ? 1 : 0) + (graphs_[1] ? 1 : 0); }
+    const std::string& capture_error() const { return capture_error_; }
 
 private:
     static constexpr size_t kPinnedIds = 4096;
@@ -502,10 +584,14 @@ private:
         q_ = reinterpret_cast<float*>(w); w += align256(qd_ * 4);
         att_ = reinterpret_cast<float*>(w); w += align256(qd_ * 4);
         logits_ = reinterpret_cast<float*>(w);
-        check(cudaMalloc(&seq_, (cfg_.context + 1) * 4 + 512), "cudaMalloc(sequence)");
-        check(cudaMemset(seq_, 0, (cfg_.context + 1) * 4 + 512), "cudaMemset(sequence)");
+        const size_t seq_words = cfg_.context + 1 + 32 + 32 + 32 + 2 * kArgmaxCtas;
+        check(cudaMalloc(&seq_, seq_words * 4), "cudaMalloc(sequence)");
+        check(cudaMemset(seq_, 0, seq_words * 4), "cudaMemset(sequence)");
         pos_ = seq_ + cfg_.context + 1 + 32;
         status_ = pos_ + 32;
+        arrivals_ = status_ + 32;
+        part_i_ = arrivals_ + 32;
+        part_v_ = reinterpret_cast<float*>(part_i_ + kArgmaxCtas);
         check(cudaMallocHost(&pinned_ids_, kPinnedIds * 4), "cudaMallocHost");
         check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
         check(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -565,7 +651,8 @@ private:
                 qkv_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_Q_NORM)),
                 reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_K_NORM)), eps, rope_,
                 rope_ + cfg_.context * half, pos_, win, qh, kvh, q_, kcache_ + kv_off, vcache_ + kv_off);
-            attend_kernel<<<qh, d, win * 4, s>>>(q_, kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh, kvh, scale, att_);
+            attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(q_, kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh, kvh,
+                                                             d, scale, att_);
             e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
                               hidden_, s, false, true);
             if (e != cudaSuccess) break;
@@ -585,8 +672,9 @@ private:
             e = launch_linear(cfg_.output_type, pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT], static_cast<uint32_t>(cfg_.vocab), H,
                               xn_, logits_, s);
             if (e != cudaSuccess) return e;
-            argmax_kernel<<<1, 1024, 0, s>>>(logits_, static_cast<uint32_t>(cfg_.vocab), seq_, pos_,
-                                             static_cast<uint32_t>(cfg_.context + 1), status_);
+            argmax_kernel<<<kArgmaxCtas, 256, 0, s>>>(logits_, static_cast<uint32_t>(cfg_.vocab), part_v_, part_i_,
+                                                      arrivals_, seq_, pos_, static_cast<uint32_t>(cfg_.context + 1),
+                                                      status_);
             n += 3;
         }
         advance_kernel<<<1, 1, 0, s>>>(pos_);
@@ -616,10 +704,16 @@ private:
             const cudaError_t e = enqueue(logits, capture_stream_, &n);
             const cudaError_t end = cudaStreamEndCapture(capture_stream_, &g);
             cudaGraphExec_t exec = nullptr;
-            if (e == cudaSuccess && end == cudaSuccess && cudaGraphInstantiate(&exec, g, 0) == cudaSuccess) {
+            cudaError_t inst = cudaErrorUnknown;
+            if (e == cudaSuccess && end == cudaSuccess) inst = cudaGraphInstantiate(&exec, g, 0);
+            if (inst == cudaSuccess) {
                 graphs_[v] = exec;
             } else {
-                no_graphs_ = true;          // capture refused: eager launches from now on
+                // Capture refused: eager launches from now on (the reason is kept).
+                no_graphs_ = true;
+                capture_error_ = std::string(cudaGetErrorString(e != cudaSuccess ? e : end != cudaSuccess ? end : inst)) +
+                                 (moe_error_.empty() ? "" : " (MoE block: " + moe_error_ + ")");
+                moe_error_.clear();
                 cudaGetLastError();
             }
             if (g) cudaGraphDestroy(g);
@@ -677,7 +771,8 @@ private:
     float* rope_ = nullptr;          // [context][half] cos, then [context][half] sin
     void* work_ = nullptr;
     float *hidden_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *logits_ = nullptr;
-    uint32_t *seq_ = nullptr, *pos_ = nullptr, *status_ = nullptr;
+    uint32_t *seq_ = nullptr, *pos_ = nullptr, *status_ = nullptr, *arrivals_ = nullptr, *part_i_ = nullptr;
+    float* part_v_ = nullptr;
     uint32_t* pinned_ids_ = nullptr;
     cudaStream_t stream_ = nullptr, capture_stream_ = nullptr;
     cudaEvent_t join_ = nullptr;
@@ -687,6 +782,7 @@ private:
     uint64_t launches_per_step_ = 0;
     size_t next_position_ = 0;
     std::string moe_error_;
+    std::string capture_error_;
     std::mutex mutex_;
     bool failed_ = false;
     std::string failure_;
@@ -807,6 +903,12 @@ pokit_cuda_status pokit_cuda_decoder_reset(pokit_cuda_decoder* decoder, char* er
 
 uint64_t pokit_cuda_decoder_launches_per_step(const pokit_cuda_decoder* decoder) {
     return decoder ? decoder->impl.launches_per_step() : 0;
+}
+
+int pokit_cuda_decoder_step_graphs(const pokit_cuda_decoder* decoder, char* reason_buffer, size_t reason_capacity) {
+    if (!decoder) return 0;
+    pokit::set_error(reason_buffer, reason_capacity, decoder->impl.capture_error().c_str());
+    return decoder->impl.step_graphs();
 }
 
 }  // extern "C"

@@ -15,43 +15,6 @@ namespace {
 
 constexpr int kLinearThreads = 256;
 
-// Q4_K: 8 rows per warp, lane = (row r = lane/4, chunk c = lane%4); the CTA
-// prepares x once and then streams its rows.
-__global__ void __launch_bounds__(kLinearThreads)
-linear_q4k_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols,
-                  const float* __restrict__ x, float* __restrict__ y, int accumulate) {
-    extern __shared__ float smem[];
-    const int nsb = static_cast<int>(cols >> 8);
-    float* xp = smem;                                  // nsb*4*68 floats
-    float* gsum = smem + nsb * 4 * kQ4kChunkStride;    // nsb*8 floats
-    q4k_prepare_x(x, static_cast<int>(cols), xp, gsum);
-    __syncthreads();
-    const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
-    const uint32_t warps_total = gridDim.x * (blockDim.x >> 5);
-    const uint32_t warp_id = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const uint64_t rb = static_cast<uint64_t>(nsb) * 144u;
-    for (uint32_t base = warp_id * 8u; base < rows; base += warps_total * 8u) {
-        const uint32_t row = base + r;
-        float acc = 0.0f;
-        if (row < rows) {
-            const uint8_t* rp = w + row * rb;
-#pragma unroll 2
-            for (int sb = 0; sb < nsb; ++sb) {
-                const uint8_t* blk = rp + sb * 144;
-                const uint4 hdr = ldg_stream128(blk);
-                const uint4 q0 = ldg_stream128(blk + 16 + 32 * c);
-                const uint4 q1 = ldg_stream128(blk + 32 + 32 * c);
-                const int k = sb * 4 + c;
-                acc += q4k_chunk_dot(hdr, q0, q1, c, xp + k * kQ4kChunkStride,
-                                     gsum[sb * 8 + 2 * c], gsum[sb * 8 + 2 * c + 1]);
-            }
-        }
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        if (c == 0 && row < rows) y[row] = accumulate ? y[row] + acc : acc;
-    }
-}
-
 // F32: one warp per row, 128-bit loads straight from global.
 __global__ void __launch_bounds__(kLinearThreads)
 linear_f32_kernel(const float* __restrict__ w, uint32_t rows, uint32_t cols,
@@ -76,6 +39,66 @@ linear_f32_kernel(const float* __restrict__ w, uint32_t rows, uint32_t cols,
         }
         acc = warp_sum(acc);
         if (lane == 0) y[row] = accumulate ? y[row] + acc : acc;
+    }
+}
+
+// Quantised rows of 16-byte multiples (every K-quant row, Q8_0 rows of 128
+// multiples): x in shared memory, one warp per row at a time, the warp's next
+// row loaded into registers (16-byte streaming loads) while the current one,
+// staged in shared memory, is dotted four weights per lane and step
+// (lane_row_dot4: byte-parallel decode, one scale per four weights).  The
+// grid is a few CTAs per SM so x is read once per CTA, not once per row.
+constexpr uint32_t kRowsMaxUnits = 8;          // 16-byte units per lane: rows up to 4 KiB
+
+template <uint32_t T>
+__global__ void __launch_bounds__(kLinearThreads)
+linear_rows_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, const float* __restrict__ x,
+                   float* __restrict__ y, int accumulate) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    float* xs = reinterpret_cast<float*>(smem_raw);
+    const uint32_t rb = static_cast<uint32_t>(row_bytes(T, cols)), units = rb / 16u;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t* buf0 = smem_raw + cols * 4u + warp * 2u * rb;
+    uint8_t* buf1 = buf0 + rb;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        for (uint32_t i = threadIdx.x * 4u; i < cols; i += blockDim.x * 4u)
+            *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
+    } else {
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = x[i];
+    }
+    __syncthreads();
+    const uint32_t nw = gridDim.x * (blockDim.x >> 5);
+    uint32_t row = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (row >= rows) return;
+    uint4 v[kRowsMaxUnits];
+    const auto load = [&](uint32_t r) {
+        const uint4* src = reinterpret_cast<const uint4*>(w + static_cast<uint64_t>(r) * rb);
+#pragma unroll
+        for (uint32_t j = 0; j < kRowsMaxUnits; ++j) {
+            const uint32_t u = lane + 32u * j;
+            if (u < units) v[j] = ldg_stream128(src + u);
+        }
+    };
+    const auto store = [&](uint8_t* dst) {
+#pragma unroll
+        for (uint32_t j = 0; j < kRowsMaxUnits; ++j) {
+            const uint32_t u = lane + 32u * j;
+            if (u < units) reinterpret_cast<uint4*>(dst)[u] = v[j];
+        }
+    };
+    load(row);
+    store(buf0);
+    __syncwarp();
+    bool cur0 = true;
+    for (; row < rows; row += nw) {
+        const uint32_t next = row + nw;
+        if (next < rows) load(next);
+        float acc = lane_row_dot4<T>(cur0 ? buf0 : buf1, cols, xs, lane);
+        acc = warp_sum(acc);
+        if (lane == 0) y[row] = accumulate ? y[row] + acc : acc;
+        if (next < rows) store(cur0 ? buf1 : buf0);
+        __syncwarp();
+        cur0 = !cur0;
     }
 }
 
@@ -173,6 +196,37 @@ cudaError_t launch_generic(const void* w, uint32_t rows, uint32_t cols, const fl
     return cudaGetLastError();
 }
 
+// The row kernel serves the matrix: 16-byte aligned rows of at most 4 KiB.
+template <uint32_t T>
+bool rows_kernel_fits(const void* w, uint32_t cols) {
+    const uint64_t rb = row_bytes(T, cols);
+    if ((reinterpret_cast<uint64_t>(w) & 15u) || (rb & 15u) || rb > 16u * 32u * kRowsMaxUnits) return false;
+    if (T == kQ8_0 && (cols & 127u)) return false;
+    return static_cast<uint64_t>(cols) * 4u + 2u * rb * (kLinearThreads / 32) <= 200u * 1024u;
+}
+
+template <uint32_t T>
+cudaError_t launch_rows(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y, cudaStream_t stream,
+                        bool accumulate) {
+    const size_t smem = static_cast<size_t>(cols) * 4u + 2u * row_bytes(T, cols) * (kLinearThreads / 32);
+    cudaError_t e = set_smem(linear_rows_kernel<T>, smem);
+    if (e != cudaSuccess) return e;
+    const uint32_t warps = kLinearThreads / 32;
+    uint32_t grid = (rows + warps - 1) / warps;
+    const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 4u;
+    if (grid > cap) grid = cap;
+    linear_rows_kernel<T><<<grid, kLinearThreads, smem, stream>>>(static_cast<const uint8_t*>(w), rows, cols, x, y,
+                                                                  accumulate ? 1 : 0);
+    return cudaGetLastError();
+}
+
+template <uint32_t T>
+cudaError_t launch_quant(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y, cudaStream_t stream,
+                         bool force_generic, bool accumulate) {
+    if (!force_generic && rows_kernel_fits<T>(w, cols)) return launch_rows<T>(w, rows, cols, x, y, stream, accumulate);
+    return launch_generic<T>(w, rows, cols, x, y, stream, accumulate);
+}
+
 template <uint32_t T>
 cudaError_t launch_dequant(const void* w, uint32_t rows, uint32_t cols, float* out,
                            cudaStream_t stream) {
@@ -207,27 +261,10 @@ cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t 
                 static_cast<const float*>(w), rows, cols, x, y, accumulate ? 1 : 0);
             return cudaGetLastError();
         }
-        case kQ4_K: {
-            const bool aligned = (reinterpret_cast<uint64_t>(w) & 15u) == 0;
-            if (!force_generic && aligned) {
-                const uint32_t nsb = cols / 256u;
-                const size_t smem = (static_cast<size_t>(nsb) * 4u * kQ4kChunkStride +
-                                     nsb * 8u) * sizeof(float);
-                if (smem > 200u * 1024u) return cudaErrorInvalidValue;
-                cudaError_t e = set_smem(linear_q4k_kernel, smem);
-                if (e != cudaSuccess) return e;
-                uint32_t grid = (rows + 63u) / 64u;   // 8 warps x 8 rows per CTA pass
-                const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 2u;
-                if (grid > cap) grid = cap;
-                linear_q4k_kernel<<<grid, kLinearThreads, smem, stream>>>(
-                    static_cast<const uint8_t*>(w), rows, cols, x, y, accumulate ? 1 : 0);
-                return cudaGetLastError();
-            }
-            return launch_generic<kQ4_K>(w, rows, cols, x, y, stream, accumulate);
-        }
-        case kQ5_K: return launch_generic<kQ5_K>(w, rows, cols, x, y, stream, accumulate);
-        case kQ6_K: return launch_generic<kQ6_K>(w, rows, cols, x, y, stream, accumulate);
-        case kQ8_0: return launch_generic<kQ8_0>(w, rows, cols, x, y, stream, accumulate);
+        case kQ4_K: return launch_quant<kQ4_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
+        case kQ5_K: return launch_quant<kQ5_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
+        case kQ6_K: return launch_quant<kQ6_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
+        case kQ8_0: return launch_quant<kQ8_0>(w, rows, cols, x, y, stream, force_generic, accumulate);
         default: return cudaErrorInvalidValue;
     }
 }
