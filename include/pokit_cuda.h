@@ -535,6 +535,41 @@ uint64_t pokit_cuda_decoder_launches_per_step(const pokit_cuda_decoder* decoder)
 int pokit_cuda_decoder_step_graphs(const pokit_cuda_decoder* decoder, char* reason_buffer, size_t reason_capacity);
 
 /* ------------------------------------------------------------------------ */
+/* Qwen3.5 Gated DeltaNet mixer (configuration 3's linear-attention layers)  */
+/* ------------------------------------------------------------------------ */
+
+typedef struct pokit_cuda_delta_net_shape {
+    size_t key_heads;                 /* ssm.group_count */
+    size_t value_heads;               /* ssm.time_step_rank (a multiple of key_heads) */
+    size_t key_dim;                   /* ssm.state_size: multiple of 32, <= 256 */
+    size_t value_dim;                 /* ssm.inner_size / value_heads: <= 256 */
+    size_t conv_kernel;               /* ssm.conv_kernel */
+    float rms_epsilon;
+} pokit_cuda_delta_net_shape;
+
+/* One token of the mixer between its projections (src/qwen35_runner.cpp:613-656):
+ * the causal conv1d step with SiLU over `projected` (the linear_qkv output,
+ * [2 key_heads key_dim + value_heads value_dim], convolved in place; replaces
+ * causal_depthwise_conv1d_step, src/causal_conv1d.cpp:25-50), the decay and
+ * update gates from the linear_alpha / linear_beta outputs (log_decay = ssm_a *
+ * softplus(alpha + dt_bias), beta = sigmoid(beta); :633-642), the gated
+ * delta-rule step on recurrent_state ([value_heads][value_dim][key_dim] F32,
+ * updated in place; replaces gated_delta_recurrent_step_grouped,
+ * src/gated_delta_net.cpp:28-110) and the gated RMSNorm with the linear_gate
+ * output `gate` and ssm_norm (replaces rms_norm_gated, src/rms_norm.cpp:46-74);
+ * `output` [value_heads value_dim] is the linear_output projection's input.
+ * conv_weights [channels][conv_kernel], conv_state [channels][conv_kernel - 1]
+ * (in place).  All device pointers; asynchronous on `stream`.  An invalid decay
+ * or gate (the reference throws) OR-s 1 into *status (device, may be NULL),
+ * leaves that head's state untouched and writes zeros. */
+pokit_cuda_status pokit_cuda_delta_net_step(const pokit_cuda_delta_net_shape* shape, float* projected,
+                                            const float* gate, const float* alpha, const float* beta,
+                                            const float* conv_weights, float* conv_state, const float* ssm_a,
+                                            const float* dt_bias, const float* ssm_norm, float* recurrent_state,
+                                            float* output, uint32_t* status, void* stream, char* error_buffer,
+                                            size_t error_capacity);
+
+/* ------------------------------------------------------------------------ */
 /* One MoE block without any device allocation                              */
 /* ------------------------------------------------------------------------ */
 

@@ -122,6 +122,10 @@ def port() -> C.CDLL:
             ("po_moe_forward", C.c_int, [C.POINTER(_MoeDesc), V, V, V, V, V, V, V]),
             ("po_rms_norm", None, [V, V, S, C.c_float, V]),
             ("po_half_to_float", C.c_float, [C.c_uint16]),
+            ("po_causal_conv1d_step", None, [V, V, S, S, V, V]),
+            ("po_delta_gates", None, [V, V, V, V, S, V, V]),
+            ("po_gated_delta_step", C.c_int, [V, V, V, V, V, S, S, S, S, V, V]),
+            ("po_rms_norm_gated", None, [V, V, V, S, S, C.c_float, V]),
         ]:
             f = getattr(dll, name)
             f.restype = res
@@ -150,6 +154,9 @@ def ref() -> C.CDLL:
             ("pr_moe_create", C.c_void_p, [C.POINTER(_MoeDesc)]),
             ("pr_moe_destroy", None, [V]),
             ("pr_moe_forward", C.c_int, [V, V, V, V, V]),
+            ("ref_causal_conv1d_step", C.c_int, [V, V, S, S, V, V]),
+            ("ref_gated_delta_step", C.c_int, [V, V, V, V, V, S, S, S, S, V, V]),
+            ("ref_rms_norm_gated", C.c_int, [V, V, V, S, S, C.c_float, V]),
         ]:
             f = getattr(dll, name)
             f.restype = res
@@ -312,3 +319,33 @@ class RefMoe:
             self.close()
         except Exception:
             pass
+
+
+# --- Qwen3.5 Gated DeltaNet mixer (src/qwen35_runner.cpp:613-656) ----------------
+
+def delta_net_step(shape: dict, projected, gate, alpha, beta_raw, conv_w, conv_state, a, dt_bias, norm, state,
+                   fn_prefix: str = "po"):
+    """One token of the DeltaNet mixer between its projections, in place on
+    conv_state and state: conv1d + SiLU of the projected q|k|v, the gates,
+    the gated delta-rule step and the gated RMSNorm.  Returns (out, conv
+    output) F32.  fn_prefix "ref" runs the reference's own conv1d, delta step
+    and gated norm (oracle/_ref) instead of the restatement."""
+    kh, vh, dk, dv, K = (shape[k] for k in ("key_heads", "value_heads", "key_dim", "value_dim", "conv_kernel"))
+    eps = shape["rms_epsilon"]
+    P, R = port(), (ref() if fn_prefix == "ref" else None)
+    xq = np.array(projected, dtype=np.float32, copy=True)
+    conv = (R.ref_causal_conv1d_step if R else P.po_causal_conv1d_step)
+    conv(_fptr(xq), _fptr(conv_w), xq.size, K, _fptr(conv_state), _fptr(xq))
+    qk = kh * dk
+    q, k, v = xq[:qk].copy(), xq[qk:2 * qk].copy(), xq[2 * qk:].copy()
+    log_decay = np.empty(vh, np.float32)
+    beta = np.empty(vh, np.float32)
+    P.po_delta_gates(_fptr(a), _fptr(dt_bias), _fptr(alpha), _fptr(beta_raw), vh, _fptr(log_decay), _fptr(beta))
+    out = np.empty(vh * dv, np.float32)
+    step = R.ref_gated_delta_step if R else P.po_gated_delta_step
+    if step(_fptr(q), _fptr(k), _fptr(v), _fptr(log_decay), _fptr(beta), kh, vh, dk, dv, _fptr(state), _fptr(out)):
+        raise ValueError("invalid gated-delta decay or update gate")
+    y = np.empty_like(out)
+    g = np.ascontiguousarray(gate, dtype=np.float32)
+    (R.ref_rms_norm_gated if R else P.po_rms_norm_gated)(_fptr(out), _fptr(norm), _fptr(g), vh, dv, eps, _fptr(y))
+    return y, xq

@@ -23,6 +23,7 @@
 #include <math.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define PO_OK 0
@@ -446,4 +447,123 @@ void po_rms_norm(const float* x, const float* w, size_t n, float eps, float* y) 
     for (size_t i = 0; i < n; ++i) sum += x[i] * x[i];
     const float scale = 1.0f / sqrtf(sum / (float)n + eps);
     for (size_t i = 0; i < n; ++i) y[i] = x[i] * scale * w[i];
+}
+
+/* ---------------------------------------------------------------------------
+ * Qwen3.5 Gated DeltaNet mixer, one token (the pieces between its
+ * projections, src/qwen35_runner.cpp:613-656).
+ * ------------------------------------------------------------------------- */
+
+/* softplus of the runner, src/qwen35_runner.cpp:117-121. */
+float po_softplus(float v) {
+    if (v > 20.0f) return v;
+    if (v < -20.0f) return expf(v);
+    return log1pf(expf(v));
+}
+
+/* Depthwise causal convolution step with SiLU, restating
+ * causal_depthwise_conv1d_step, src/causal_conv1d.cpp:25-50: input and
+ * output may alias; state holds the last kernel - 1 inputs per channel. */
+void po_causal_conv1d_step(const float* input, const float* weights, size_t channels, size_t kernel,
+                           float* state, float* output) {
+    const size_t sl = kernel - 1;
+    for (size_t c = 0; c < channels; ++c) {
+        const size_t wo = c * kernel, so = c * sl;
+        float sum = input[c] * weights[wo + sl];
+        for (size_t t = 0; t < sl; ++t) sum += state[so + t] * weights[wo + t];
+        if (sl) {
+            for (size_t t = 0; t + 1 < sl; ++t) state[so + t] = state[so + t + 1];
+            state[so + sl - 1] = input[c];
+        }
+        /* silu with the sign branch, src/causal_conv1d.cpp:17-21 */
+        float s;
+        if (sum >= 0.0f) s = sum / (1.0f + expf(-sum));
+        else {
+            const float e = expf(sum);
+            s = sum * e / (1.0f + e);
+        }
+        output[c] = s;
+    }
+}
+
+/* The per-head decay and update gate of the mixer, src/qwen35_runner.cpp:633-642:
+ * log_decay = a * softplus(alpha + dt_bias), beta = sigmoid(beta_raw). */
+void po_delta_gates(const float* a, const float* dt_bias, const float* alpha, const float* beta_raw,
+                    size_t heads, float* log_decay, float* beta) {
+    for (size_t h = 0; h < heads; ++h) {
+        log_decay[h] = a[h] * po_softplus(alpha[h] + dt_bias[h]);
+        beta[h] = po_sigmoid(beta_raw[h]);
+    }
+}
+
+/* Restates gated_delta_recurrent_step_grouped, src/gated_delta_net.cpp:28-110:
+ * L2-normalised q (times 1/sqrt(dk)) and k per key head, value head h uses key
+ * head h % key_heads; state[h][v][k] decays, then delta = (v - state.k) * beta,
+ * state += k delta, out = state.q.  Returns 1 (nothing changed) for an invalid
+ * decay or gate, where the reference throws. */
+int po_gated_delta_step(const float* query, const float* key, const float* value, const float* log_decay,
+                        const float* beta, size_t key_heads, size_t value_heads, size_t dk, size_t dv,
+                        float* state, float* output) {
+    for (size_t h = 0; h < value_heads; ++h)
+        if (!isfinite(log_decay[h]) || log_decay[h] > 0.0f || !isfinite(beta[h]) || beta[h] < 0.0f ||
+            beta[h] > 1.0f)
+            return 1;
+    float* nq = (float*)malloc(key_heads * dk * sizeof(float));
+    float* nk = (float*)malloc(key_heads * dk * sizeof(float));
+    float* delta = (float*)malloc(dv * sizeof(float));
+    if (!nq || !nk || !delta) {
+        free(nq); free(nk); free(delta);
+        return 2;
+    }
+    const float qs = 1.0f / sqrtf((float)dk);
+    for (size_t h = 0; h < key_heads; ++h) {
+        float sq = 0.0f, sk = 0.0f;
+        for (size_t i = 0; i < dk; ++i) {
+            sq += query[h * dk + i] * query[h * dk + i];
+            sk += key[h * dk + i] * key[h * dk + i];
+        }
+        const float iq = 1.0f / sqrtf(sq + 1.0e-6f), ik = 1.0f / sqrtf(sk + 1.0e-6f);
+        for (size_t i = 0; i < dk; ++i) {
+            nq[h * dk + i] = query[h * dk + i] * iq * qs;
+            nk[h * dk + i] = key[h * dk + i] * ik;
+        }
+    }
+    for (size_t h = 0; h < value_heads; ++h) {
+        const float* q = nq + (h % key_heads) * dk;
+        const float* k = nk + (h % key_heads) * dk;
+        float* S = state + h * dv * dk;
+        const float decay = expf(log_decay[h]);
+        for (size_t i = 0; i < dv * dk; ++i) S[i] *= decay;
+        for (size_t v = 0; v < dv; ++v) {
+            float mem = 0.0f;
+            for (size_t i = 0; i < dk; ++i) mem += S[v * dk + i] * k[i];
+            delta[v] = (value[h * dv + v] - mem) * beta[h];
+            output[h * dv + v] = 0.0f;
+        }
+        for (size_t v = 0; v < dv; ++v)
+            for (size_t i = 0; i < dk; ++i) {
+                float* cell = &S[v * dk + i];
+                *cell += k[i] * delta[v];
+                output[h * dv + v] += *cell * q[i];
+            }
+    }
+    free(nq); free(nk); free(delta);
+    return 0;
+}
+
+/* Restates rms_norm_gated, src/rms_norm.cpp:46-74: per row of `width`,
+ * y = x * (1 / sqrt(mean(x^2) + eps)) * w * (g * sigmoid(g)). */
+void po_rms_norm_gated(const float* x, const float* w, const float* gate, size_t rows, size_t width, float eps,
+                       float* y) {
+    for (size_t r = 0; r < rows; ++r) {
+        const float* xr = x + r * width;
+        float sum = 0.0f;
+        for (size_t i = 0; i < width; ++i) sum += xr[i] * xr[i];
+        const float scale = 1.0f / sqrtf(sum / (float)width + eps);
+        for (size_t i = 0; i < width; ++i) {
+            const float g = gate[r * width + i];
+            const float sg = g >= 0.0f ? 1.0f / (1.0f + expf(-g)) : expf(g) / (1.0f + expf(g));
+            y[r * width + i] = xr[i] * scale * w[i] * (g * sg);
+        }
+    }
 }

@@ -19,6 +19,8 @@
 #include "pokitlms/ops/linear.hpp"
 #include "pokitlms/ops/quantized_linear.hpp"
 #include "pokitlms/ops/rms_norm.hpp"
+#include "pokitlms/ops/causal_conv1d.hpp"
+#include "pokitlms/ops/gated_delta_net.hpp"
 
 #include <cmath>
 #include <cstdint>
@@ -266,3 +268,40 @@ int pr_moe_forward(void* handle, const float* x, float* out, uint32_t* ids, floa
 }
 
 }  // extern "C"
+
+// The reference's own Gated DeltaNet pieces (src/causal_conv1d.cpp,
+// src/gated_delta_net.cpp, src/rms_norm.cpp), for pinning the restatement.
+extern "C" int ref_causal_conv1d_step(const float* input, const float* weights, size_t channels, size_t kernel,
+                                      float* state, float* output) {
+    try {
+        pokitlms::causal_depthwise_conv1d_step(input, weights, channels, kernel, state, output);
+        return 0;
+    } catch (...) {
+        return 1;
+    }
+}
+
+extern "C" int ref_gated_delta_step(const float* query, const float* key, const float* value,
+                                    const float* log_decay, const float* beta, size_t key_heads,
+                                    size_t value_heads, size_t dk, size_t dv, float* state, float* output) {
+    try {
+        pokitlms::GatedDeltaNetScratch scratch;
+        pokitlms::gated_delta_recurrent_step_grouped(query, key, value, log_decay, beta, key_heads, value_heads,
+                                                     dk, dv, state, output, scratch);
+        return 0;
+    } catch (...) {
+        return 1;
+    }
+}
+
+extern "C" int ref_rms_norm_gated(const float* x, const float* w, const float* gate, size_t rows, size_t width,
+                                  float eps, float* y) {
+    try {
+        pokitlms::rms_norm_gated(std::span<const float>(x, rows * width), std::span<const float>(w, width),
+                                 std::span<const float>(gate, rows * width), std::span<float>(y, rows * width),
+                                 rows, eps);
+        return 0;
+    } catch (...) {
+        return 1;
+    }
+}

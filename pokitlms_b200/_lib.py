@@ -130,6 +130,11 @@ class GenerationStats(C.Structure):
 DEC_TOKEN_EMBD, DEC_OUTPUT_NORM, DEC_OUTPUT = 0, 1, 2
 DEC_ATTN_NORM, DEC_ATTN_Q, DEC_ATTN_Q_NORM, DEC_ATTN_K, DEC_ATTN_K_NORM, DEC_ATTN_V, DEC_ATTN_OUTPUT = range(3, 10)
 
+class DeltaNetShape(C.Structure):
+    _fields_ = [("key_heads", C.c_size_t), ("value_heads", C.c_size_t), ("key_dim", C.c_size_t),
+                ("value_dim", C.c_size_t), ("conv_kernel", C.c_size_t), ("rms_epsilon", C.c_float)]
+
+
 STATIC_SCRATCH_BYTES = 256 * 1024
 
 _ERR = C.c_char_p
@@ -196,6 +201,8 @@ SIGNATURES = {
     "pokit_cuda_decoder_reset": (C.c_int, [_VP, _ERR, _SZ]),
     "pokit_cuda_decoder_launches_per_step": (C.c_uint64, [_VP]),
     "pokit_cuda_decoder_step_graphs": (C.c_int, [_VP, _ERR, _SZ]),
+    "pokit_cuda_delta_net_step": (C.c_int, [C.POINTER(DeltaNetShape), _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
+                                            _VP, _VP, _VP, _VP, _VP, _ERR, _SZ]),
     "pokit_cuda_moe_forward_static_scratch": (C.c_int, [C.POINTER(MoeBlockDevice), _VP, _VP, _VP,
                                                         _VP, _VP, _ERR, _SZ]),
 }

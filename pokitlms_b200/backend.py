@@ -77,6 +77,18 @@ def synthesize_blocks(ggml_type: int, seed: int, stream_id: int, nblocks: int, d
          _stream(stream))
 
 
+def delta_net_step(shape: dict, projected, gate, alpha, beta, conv_weights, conv_state, ssm_a, dt_bias, ssm_norm,
+                   recurrent_state, output, status=None, stream=None) -> None:
+    """One token of the Gated DeltaNet mixer on device tensors (see
+    pokit_cuda_delta_net_step); projected, conv_state and recurrent_state are
+    updated in place."""
+    s = _lib.DeltaNetShape(shape["key_heads"], shape["value_heads"], shape["key_dim"], shape["value_dim"],
+                           shape["conv_kernel"], shape["rms_epsilon"])
+    call("pokit_cuda_delta_net_step", C.byref(s), _ptr(projected), _ptr(gate), _ptr(alpha), _ptr(beta),
+         _ptr(conv_weights), _ptr(conv_state), _ptr(ssm_a), _ptr(dt_bias), _ptr(ssm_norm), _ptr(recurrent_state),
+         _ptr(output), _ptr(status), _stream(stream))
+
+
 class CudaLinearBackend:
     """TensorLinearBackend with host spans; payloads are streamed per call, or
     cached in HBM under a caller-chosen key (try_linear(..., key=...))."""

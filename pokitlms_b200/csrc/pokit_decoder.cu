@@ -107,11 +107,13 @@ __global__ void attn_prep_kernel(const float* __restrict__ qkv, const float* __r
 
 // GQA decode attention of one query head over the ring's last min(pos + 1,
 // window) positions, oldest first (KvCache::attend, kv_cache.cpp:185-294):
-// scores = q . k * scale, softmax, out = sum_j (e_j / sum e) v_j.  Eight warps
-// score four positions each per pass (loads of all four in flight); for the
-// output, threads t and t + d sum the even and odd positions of dimension t
-// (eight loads in flight), added in position-pair order at the end.
+// scores = q . k * scale, softmax, out = sum_j (e_j / sum e) v_j.
+// Scores: each lane takes a whole position (its key row as 16-byte loads, all
+// in flight at once), 256 positions per pass.  Output: warp w sums positions
+// w, w + 8, ... for four dimensions per lane, eight positions' loads in flight
+// per round; the eight warps' partial sums are added in warp order.
 constexpr uint32_t kAttendThreads = 256;
+constexpr uint32_t kAttendMaxDim = 128;
 
 __global__ void __launch_bounds__(kAttendThreads)
 attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
@@ -119,38 +121,39 @@ attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const 
               float* __restrict__ out) {
     extern __shared__ float sc[];
     __shared__ float red[32];
-    __shared__ float part[kAttendThreads];
+    __shared__ __align__(16) float qs[kAttendMaxDim];
+    __shared__ __align__(16) float part[kAttendThreads / 32][kAttendMaxDim];
     const uint32_t t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
     const uint32_t kh = h / (qh / kvh);
     const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
     const int lane = t & 31, warp = t >> 5;
-    constexpr int kWarpsA = kAttendThreads / 32;
-    const uint32_t per = d / 32;                        // dimensions per lane (d <= 256)
-    float qv[8];
+    constexpr int kW = kAttendThreads / 32;
+    const uint64_t row_stride = static_cast<uint64_t>(kvh) * d;
+    if (t < d) qs[t] = q[h * d + t];
+    __syncthreads();
+    const uint32_t units = d / 8;                         // 16-byte units of a key row
+    for (uint32_t j0 = 0; j0 < n; j0 += kAttendThreads) {
+        const uint32_t j = j0 + t;
+        if (j < n) {
+            const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + j) % window) * row_stride + kh * d);
+            uint4 kv[kAttendMaxDim / 8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) qv[e] = e < static_cast<int>(per) ? q[h * d + lane * per + e] : 0.0f;
-    const auto key = [&](uint32_t j) {
-        return kc + (static_cast<uint64_t>((first + j) % window) * kvh + kh) * d + lane * per;
-    };
-    for (uint32_t j0 = warp; j0 < n; j0 += 4 * kWarpsA) {
-        float dots[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint32_t j = j0 + u * kWarpsA;
+            for (uint32_t u = 0; u < kAttendMaxDim / 8; ++u)
+                if (u < units) kv[u] = __ldg(k + u);
             float dot = 0.0f;
-            if (j < n) {
-                const __half* k = key(j);
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    if (e < static_cast<int>(per)) dot = fmaf(qv[e], __half2float(k[e]), dot);
+            for (uint32_t u = 0; u < kAttendMaxDim / 8; ++u) {
+                if (u < units) {
+                    const __half2* hp = reinterpret_cast<const __half2*>(&kv[u]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(hp[e]);
+                        dot = fmaf(qs[u * 8 + 2 * e], f.x, dot);
+                        dot = fmaf(qs[u * 8 + 2 * e + 1], f.y, dot);
+                    }
+                }
             }
-            dots[u] = dot;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const float dsum = warp_sum(dots[u]);
-            const uint32_t j = j0 + u * kWarpsA;
-            if (lane == 0 && j < n) sc[j] = dsum * scale;
+            sc[j] = dot * scale;
         }
     }
     __syncthreads();
@@ -164,26 +167,37 @@ attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const 
         den += e;
     }
     den = block_reduce_all(den, red, [](float a, float b) { return a + b; });
-    const uint32_t dim = t % d, grp = t / d, groups = kAttendThreads / d;
-    float acc = 0.0f;
-    if (grp < groups) {
-        uint32_t j = grp;
-        for (; j + 7 * groups < n; j += 8 * groups) {
-            float vv[8];
+    // Output: lane covers dimensions 4 lane .. 4 lane + 3 (d / 4 lanes active).
+    const bool active = static_cast<uint32_t>(lane) * 4u < d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t j0 = warp; j0 < n; j0 += 8u * kW) {
+        uint2 vv[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                vv[u] = __half2float(vc[(static_cast<uint64_t>((first + j + u * groups) % window) * kvh + kh) * d + dim]);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) acc = fmaf(sc[j + u * groups] / den, vv[u], acc);
+        for (int u = 0; u < 8; ++u) {
+            const uint32_t j = j0 + u * kW;
+            if (active && j < n)
+                vv[u] = __ldg(reinterpret_cast<const uint2*>(vc + ((first + j) % window) * row_stride + kh * d) + lane);
         }
-        for (; j < n; j += groups)
-            acc = fmaf(sc[j] / den, __half2float(vc[(static_cast<uint64_t>((first + j) % window) * kvh + kh) * d + dim]), acc);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint32_t j = j0 + u * kW;
+            if (active && j < n) {
+                const float p = sc[j] / den;
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].y));
+                acc.x = fmaf(p, a.x, acc.x);
+                acc.y = fmaf(p, a.y, acc.y);
+                acc.z = fmaf(p, b.x, acc.z);
+                acc.w = fmaf(p, b.y, acc.w);
+            }
+        }
     }
-    part[t] = acc;
+    if (active) *reinterpret_cast<float4*>(&part[warp][lane * 4]) = acc;
     __syncthreads();
-    if (grp == 0) {
-        for (uint32_t g = 1; g < groups; ++g) acc += part[g * d + dim];
-        out[h * d + dim] = acc;
+    if (t < d) {
+        float o = part[0][t];
+        for (int w = 1; w < kW; ++w) o += part[w][t];
+        out[h * d + t] = o;
     }
 }
 
@@ -288,7 +302,7 @@ public:
     explicit Decoder(const pokit_cuda_decoder_config& c) : cfg_(c) {
         const size_t d = c.head_dim;
         if (c.layers == 0 || c.hidden == 0 || c.hidden % 256 || c.vocab == 0 || c.vocab > 0xffffffffu ||
-            c.q_heads == 0 || c.kv_heads == 0 || c.q_heads % c.kv_heads || d == 0 || d % 32 || d > kMaxHeadDim ||
+            c.q_heads == 0 || c.kv_heads == 0 || c.q_heads % c.kv_heads || d == 0 || d % 32 || d > kAttendMaxDim ||
             c.context == 0 || c.context > (1u << 24) || c.eos_token >= c.vocab || !(c.rope_theta > 0.0f) ||
             !(c.rms_epsilon > 0.0f) || (c.q_heads * d) % 256)
             throw std::invalid_argument("invalid decoder configuration");

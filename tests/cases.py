@@ -226,3 +226,23 @@ class MoeShape:
         self.flavour, self.shared_inter = flavour, shared_inter
         self.gate_type, self.up_type, self.down_type = gate_type, up_type, down_type
         self.normalize, self.expert_weights_scale = normalize, expert_weights_scale
+
+
+# Benchmark configuration 3's Gated DeltaNet mixer: 16 key heads, 32 value
+# heads, head_dim 128, causal conv1d kernel 4, F32 recurrent state.
+DELTA_NET_CFG3 = dict(key_heads=16, value_heads=32, key_dim=128, value_dim=128, conv_kernel=4, rms_epsilon=1e-6)
+
+
+def delta_net_inputs(shape: dict, seed: int, steps: int):
+    """Seeded synthetic inputs of the DeltaNet mixer: per step the projected
+    q|k|v ~N(0,1) (x4), gate z ~N(0,1), alpha ~N(0,1), beta ~N(0,1); tensors
+    conv1d weights ~N(0,0.5), ssm_a = -exp(N(0,0.5)) (the GGUF stores -exp(A_log)),
+    dt_bias ~N(0,0.5), ssm_norm ~U(0.5,1.5)."""
+    rng = np.random.default_rng([seed, 0x646e])
+    kh, vh, dk, dv, K = (shape[k] for k in ("key_heads", "value_heads", "key_dim", "value_dim", "conv_kernel"))
+    C = 2 * kh * dk + vh * dv
+    f = lambda *s_, scale=1.0: (rng.standard_normal(s_, dtype=np.float32) * np.float32(scale))  # noqa: E731
+    tensors = dict(conv_w=f(C, K, scale=0.5), a=-np.exp(f(vh, scale=0.5)).astype(np.float32),
+                   dt_bias=f(vh, scale=0.5), norm=rng.uniform(0.5, 1.5, dv).astype(np.float32))
+    steps_in = [dict(projected=f(C, scale=4.0), gate=f(vh * dv), alpha=f(vh), beta=f(vh)) for _ in range(steps)]
+    return tensors, steps_in
