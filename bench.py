@@ -725,6 +725,9 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
     if cfg5:
         from pokitlms_b200 import backend as B
         lg0 = route_logits[0]
+        # Seeded rows (normalised N(0, 1)), not the synthetic model's late hidden state.
+        xp = torch.from_numpy(np.stack([synth.activation(Hs, SEED + 7, 90_000 + t) for t in range(T)])).cuda()
+        x.copy_(torch.nn.functional.rms_norm(xp, (Hs,), eps=EPS))
         ep.forward_batch(0, x, part, logits=lg0)          # the whole block's output on every rank
         torch.cuda.synchronize()
         sig = part.view(torch.int32).to(torch.int64).sum().reshape(1)
@@ -746,7 +749,9 @@ def run_expert_parallel(args, rank: int, world: int, local: int, barrier, max_ov
             full.close()
             err = ((part - ref).abs().amax(dim=1) / ref.pow(2).mean(dim=1).sqrt()).max()
             parity = {"tokens": T, "max_err_over_rms": float(err), "bar": 1e-3, "ranks_bitwise_equal": same,
-                      "reference": "layer 0, the last step's rows and logits: one whole-pool handle on rank 0"}
+                      "finite": bool(torch.isfinite(part).all().item() and torch.isfinite(ref).all().item()),
+                      "reference": ("layer 0 on 64 seeded normalised rows with the step's logits: the expert-"
+                                    "parallel sum against one whole-pool handle on rank 0")}
         barrier()
     exchange = None
     if world > 1:

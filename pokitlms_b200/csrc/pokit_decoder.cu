@@ -73,38 +73,6 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
 }
 
-// One CTA per query head and per KV head, one thread per dimension: per-head
-// RMSNorm (q_norm / k_norm), rotate-half RoPE (qwen3_moe_runner.cpp:141-172:
-// first = a cos - b sin, second = b cos + a sin), then the query to q_out or
-// the key and value to the FP16 ring at slot position % window.
-__global__ void attn_prep_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm,
-                                 const float* __restrict__ k_norm, float eps, const float* __restrict__ rope_cos,
-                                 const float* __restrict__ rope_sin, const uint32_t* __restrict__ pos_p,
-                                 uint32_t window, uint32_t qh, uint32_t kvh, float* __restrict__ q_out,
-                                 __half* __restrict__ kc, __half* __restrict__ vc) {
-    __shared__ float v[kMaxHeadDim];
-    __shared__ float red[32];
-    const uint32_t d = blockDim.x, half = d / 2, t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
-    const bool is_q = h < qh;
-    const uint32_t kh = h - qh;
-    const float x = is_q ? qkv[h * d + t] : qkv[(qh + kh) * d + t];
-    const float total = block_reduce_all(x * x, red, [](float a, float b) { return a + b; });
-    const float scale = 1.0f / sqrtf(total / static_cast<float>(d) + eps);
-    v[t] = __fmul_rn(__fmul_rn(x, scale), is_q ? q_norm[t] : k_norm[t]);
-    __syncthreads();
-    const uint32_t j = t < half ? t : t - half;
-    const float c = rope_cos[static_cast<uint64_t>(pos) * half + j], s = rope_sin[static_cast<uint64_t>(pos) * half + j];
-    const float a = v[j], b = v[j + half];
-    const float r = t < half ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)) : __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
-    if (is_q) {
-        q_out[h * d + t] = r;
-    } else {
-        const uint64_t at = (static_cast<uint64_t>(pos % window) * kvh + kh) * d + t;
-        kc[at] = __float2half_rn(r);
-        vc[at] = __float2half_rn(qkv[(qh + kvh + kh) * d + t]);
-    }
-}
-
 // GQA decode attention of one query head over the ring's last min(pos + 1,
 // window) positions, oldest first (KvCache::attend, kv_cache.cpp:185-294):
 // scores = q . k * scale, softmax, out = sum_j (e_j / sum e) v_j.
@@ -115,26 +83,83 @@ __global__ void attn_prep_kernel(const float* __restrict__ qkv, const float* __r
 constexpr uint32_t kAttendThreads = 256;
 constexpr uint32_t kAttendMaxDim = 128;
 
+// The CTA first forms its own query and its KV head's new key and value from
+// the projected q|k|v (per-head RMSNorm with q_norm / k_norm, rotate-half
+// RoPE, qwen3_moe_runner.cpp:141-172, 614-636; key and value rounded to FP16
+// as the ring stores them, kv_cache.cpp:20-44); the group's first CTA writes
+// them to the ring at slot position % window, and every CTA uses its own copy
+// for the newest position (no CTA reads the slot being written).
+__device__ __forceinline__ float head_rms_scale(float x, uint32_t d, float eps, float* red) {
+    float v = x * x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float total = 0.0f;
+    for (uint32_t w = 0; w < (d + 31) / 32; ++w) total += red[w];
+    return 1.0f / sqrtf(total / static_cast<float>(d) + eps);
+}
+
 __global__ void __launch_bounds__(kAttendThreads)
-attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const __half* __restrict__ vc,
-              const uint32_t* __restrict__ pos_p, uint32_t window, uint32_t qh, uint32_t kvh, uint32_t d, float scale,
-              float* __restrict__ out) {
+attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+              float eps, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
+              __half* __restrict__ kc, __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, uint32_t window,
+              uint32_t qh, uint32_t kvh, uint32_t d, float scale, float* __restrict__ out) {
     extern __shared__ float sc[];
     __shared__ float red[32];
     __shared__ __align__(16) float qs[kAttendMaxDim];
+    __shared__ __align__(16) float kn[kAttendMaxDim];
+    __shared__ __align__(16) float knew[kAttendMaxDim];
+    __shared__ __align__(16) float vnew[kAttendMaxDim];
     __shared__ __align__(16) float part[kAttendThreads / 32][kAttendMaxDim];
     const uint32_t t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
-    const uint32_t kh = h / (qh / kvh);
+    const uint32_t group = qh / kvh, kh = h / group;
     const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
     const int lane = t & 31, warp = t >> 5;
     constexpr int kW = kAttendThreads / 32;
     const uint64_t row_stride = static_cast<uint64_t>(kvh) * d;
-    if (t < d) qs[t] = q[h * d + t];
+    const bool dim = t < d;
+    const float xq = dim ? qkv[h * d + t] : 0.0f;
+    const float xk = dim ? qkv[(qh + kh) * d + t] : 0.0f;
+    const float sq = head_rms_scale(xq, d, eps, red);
+    const float sk = head_rms_scale(xk, d, eps, red);
+    if (dim) {
+        qs[t] = __fmul_rn(__fmul_rn(xq, sq), q_norm[t]);
+        kn[t] = __fmul_rn(__fmul_rn(xk, sk), k_norm[t]);
+    }
+    __syncthreads();
+    float rq = 0.0f, rk = 0.0f;
+    if (dim) {
+        const uint32_t half = d / 2, j = t < half ? t : t - half;
+        const float c = rope_cos[static_cast<uint64_t>(pos) * half + j], s = rope_sin[static_cast<uint64_t>(pos) * half + j];
+        const float aq = qs[j], bq = qs[j + half], ak = kn[j], bk = kn[j + half];
+        rq = t < half ? __fsub_rn(__fmul_rn(aq, c), __fmul_rn(bq, s)) : __fadd_rn(__fmul_rn(bq, c), __fmul_rn(aq, s));
+        rk = t < half ? __fsub_rn(__fmul_rn(ak, c), __fmul_rn(bk, s)) : __fadd_rn(__fmul_rn(bk, c), __fmul_rn(ak, s));
+    }
+    __syncthreads();
+    if (dim) {
+        qs[t] = rq;
+        const __half hk = __float2half_rn(rk);
+        const __half hv = __float2half_rn(qkv[(qh + kvh + kh) * d + t]);
+        knew[t] = __half2float(hk);
+        vnew[t] = __half2float(hv);
+        if (h % group == 0) {
+            const uint64_t at = static_cast<uint64_t>(pos % window) * row_stride + kh * d + t;
+            kc[at] = hk;
+            vc[at] = hv;
+        }
+    }
     __syncthreads();
     const uint32_t units = d / 8;                         // 16-byte units of a key row
     for (uint32_t j0 = 0; j0 < n; j0 += kAttendThreads) {
         const uint32_t j = j0 + t;
-        if (j < n) {
+        if (j + 1 == n) {
+            float dot = 0.0f;
+            for (uint32_t e = 0; e < d; ++e) dot = fmaf(qs[e], knew[e], dot);
+            sc[j] = dot * scale;
+        } else if (j < n) {
             const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + j) % window) * row_stride + kh * d);
             uint4 kv[kAttendMaxDim / 8];
 #pragma unroll
@@ -175,7 +200,7 @@ attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const 
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             const uint32_t j = j0 + u * kW;
-            if (active && j < n)
+            if (active && j + 1 < n)
                 vv[u] = __ldg(reinterpret_cast<const uint2*>(vc + ((first + j) % window) * row_stride + kh * d) + lane);
         }
 #pragma unroll
@@ -183,8 +208,14 @@ attend_kernel(const float* __restrict__ q, const __half* __restrict__ kc, const 
             const uint32_t j = j0 + u * kW;
             if (active && j < n) {
                 const float p = sc[j] / den;
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].x));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].y));
+                float2 a, b;
+                if (j + 1 == n) {
+                    a = make_float2(vnew[lane * 4], vnew[lane * 4 + 1]);
+                    b = make_float2(vnew[lane * 4 + 2], vnew[lane * 4 + 3]);
+                } else {
+                    a = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].x));
+                    b = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].y));
+                }
                 acc.x = fmaf(p, a.x, acc.x);
                 acc.y = fmaf(p, a.y, acc.y);
                 acc.z = fmaf(p, b.x, acc.z);
@@ -656,17 +687,13 @@ private:
         for (size_t l = 0; l < cfg_.layers && e == cudaSuccess; ++l) {
             const auto P = [&](uint32_t t) { return tensor_ptr(l, t); };
             const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
-            rms_norm_kernel<<<1, 1024, 0, s>>>(hidden_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_NORM)), eps,
-                                               xn_, H);
-            e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_Q), static_cast<uint32_t>(qd_ + 2 * kd_), H, xn_,
-                              qkv_, s);
+            e = launch_linear_normed(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_Q), static_cast<uint32_t>(qd_ + 2 * kd_), H,
+                                     hidden_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_NORM)), eps, qkv_, s);
             if (e != cudaSuccess) break;
-            attn_prep_kernel<<<qh + kvh, d, 0, s>>>(
+            attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(
                 qkv_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_Q_NORM)),
-                reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_K_NORM)), eps, rope_,
-                rope_ + cfg_.context * half, pos_, win, qh, kvh, q_, kcache_ + kv_off, vcache_ + kv_off);
-            attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(q_, kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh, kvh,
-                                                             d, scale, att_);
+                reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_K_NORM)), eps, rope_, rope_ + cfg_.context * half,
+                kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh, kvh, d, scale, att_);
             e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
                               hidden_, s, false, true);
             if (e != cudaSuccess) break;
@@ -676,20 +703,24 @@ private:
                 moe_error_ = err;
                 return st == POKIT_CUDA_STATUS_INVALID_ARGUMENT ? cudaErrorInvalidValue : cudaErrorUnknown;
             }
-            n += 6;
+            n += 4;
             e = cudaGetLastError();
         }
         if (e != cudaSuccess) return e;
         if (logits) {
-            rms_norm_kernel<<<1, 1024, 0, s>>>(hidden_, reinterpret_cast<const float*>(pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT_NORM]),
-                                               eps, xn_, H);
-            e = launch_linear(cfg_.output_type, pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT], static_cast<uint32_t>(cfg_.vocab), H,
-                              xn_, logits_, s);
+            const float* onorm = reinterpret_cast<const float*>(pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT_NORM]);
+            const void* ow = pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT];
+            e = launch_linear_normed(cfg_.output_type, ow, static_cast<uint32_t>(cfg_.vocab), H, hidden_, onorm, eps,
+                                     logits_, s);
+            if (e == cudaErrorInvalidValue) {        // an F32 or unaligned LM head: norm, then the plain matvec
+                rms_norm_kernel<<<1, 1024, 0, s>>>(hidden_, onorm, eps, xn_, H);
+                e = launch_linear(cfg_.output_type, ow, static_cast<uint32_t>(cfg_.vocab), H, xn_, logits_, s);
+            }
             if (e != cudaSuccess) return e;
             argmax_kernel<<<kArgmaxCtas, 256, 0, s>>>(logits_, static_cast<uint32_t>(cfg_.vocab), part_v_, part_i_,
                                                       arrivals_, seq_, pos_, static_cast<uint32_t>(cfg_.context + 1),
                                                       status_);
-            n += 3;
+            n += 2;
         }
         advance_kernel<<<1, 1, 0, s>>>(pos_);
         ++n;

@@ -16,6 +16,11 @@ cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t 
                           const float* x, float* y, cudaStream_t stream,
                           bool force_generic = false, bool accumulate = false);
 
+// y[rows] = W . rms_norm(x, norm_w) (every CTA normalises x as it stages it);
+// quantised W with 16-byte aligned rows of at most 4 KiB, else cudaErrorInvalidValue.
+cudaError_t launch_linear_normed(uint32_t type, const void* w, uint32_t rows, uint32_t cols, const float* x,
+                                 const float* norm_w, float eps, float* y, cudaStream_t stream);
+
 // out[rows, cols] = decoded weights, bit-identical to the reference decoders.
 cudaError_t launch_dequantize(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
                               float* out, cudaStream_t stream);

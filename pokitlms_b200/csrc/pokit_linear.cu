@@ -53,7 +53,7 @@ constexpr uint32_t kRowsMaxUnits = 8;          // 16-byte units per lane: rows u
 template <uint32_t T>
 __global__ void __launch_bounds__(kLinearThreads)
 linear_rows_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, const float* __restrict__ x,
-                   float* __restrict__ y, int accumulate) {
+                   float* __restrict__ y, int accumulate, const float* __restrict__ norm_w, float norm_eps) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     float* xs = reinterpret_cast<float*>(smem_raw);
     const uint32_t rb = static_cast<uint32_t>(row_bytes(T, cols)), units = rb / 16u;
@@ -67,6 +67,21 @@ linear_rows_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, 
         for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = x[i];
     }
     __syncthreads();
+    if (norm_w) {
+        // x = rms_norm(x, norm_w) first (src/rms_norm.cpp:9-27), in every CTA.
+        __shared__ float red[kLinearThreads / 32];
+        float ss = 0.0f;
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) ss = fmaf(xs[i], xs[i], ss);
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float total = 0.0f;
+        for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) total += red[i];
+        const float scale = 1.0f / sqrtf(total / static_cast<float>(cols) + norm_eps);
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], scale), norm_w[i]);
+        __syncthreads();
+    }
     const uint32_t nw = gridDim.x * (blockDim.x >> 5);
     uint32_t row = blockIdx.x * (blockDim.x >> 5) + warp;
     if (row >= rows) return;
@@ -207,7 +222,7 @@ bool rows_kernel_fits(const void* w, uint32_t cols) {
 
 template <uint32_t T>
 cudaError_t launch_rows(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y, cudaStream_t stream,
-                        bool accumulate) {
+                        bool accumulate, const float* norm_w = nullptr, float norm_eps = 0.0f) {
     const size_t smem = static_cast<size_t>(cols) * 4u + 2u * row_bytes(T, cols) * (kLinearThreads / 32);
     cudaError_t e = set_smem(linear_rows_kernel<T>, smem);
     if (e != cudaSuccess) return e;
@@ -216,7 +231,7 @@ cudaError_t launch_rows(const void* w, uint32_t rows, uint32_t cols, const float
     const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 4u;
     if (grid > cap) grid = cap;
     linear_rows_kernel<T><<<grid, kLinearThreads, smem, stream>>>(static_cast<const uint8_t*>(w), rows, cols, x, y,
-                                                                  accumulate ? 1 : 0);
+                                                                  accumulate ? 1 : 0, norm_w, norm_eps);
     return cudaGetLastError();
 }
 
@@ -265,6 +280,26 @@ cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t 
         case kQ5_K: return launch_quant<kQ5_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
         case kQ6_K: return launch_quant<kQ6_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
         case kQ8_0: return launch_quant<kQ8_0>(w, rows, cols, x, y, stream, force_generic, accumulate);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_linear_normed(uint32_t type, const void* w, uint32_t rows, uint32_t cols, const float* x,
+                                 const float* norm_w, float eps, float* y, cudaStream_t stream) {
+    if (rows == 0 || cols == 0 || !norm_w) return cudaErrorInvalidValue;
+    switch (type) {
+        case kQ4_K:
+            if (!rows_kernel_fits<kQ4_K>(w, cols)) return cudaErrorInvalidValue;
+            return launch_rows<kQ4_K>(w, rows, cols, x, y, stream, false, norm_w, eps);
+        case kQ5_K:
+            if (!rows_kernel_fits<kQ5_K>(w, cols)) return cudaErrorInvalidValue;
+            return launch_rows<kQ5_K>(w, rows, cols, x, y, stream, false, norm_w, eps);
+        case kQ6_K:
+            if (!rows_kernel_fits<kQ6_K>(w, cols)) return cudaErrorInvalidValue;
+            return launch_rows<kQ6_K>(w, rows, cols, x, y, stream, false, norm_w, eps);
+        case kQ8_0:
+            if (!rows_kernel_fits<kQ8_0>(w, cols)) return cudaErrorInvalidValue;
+            return launch_rows<kQ8_0>(w, rows, cols, x, y, stream, false, norm_w, eps);
         default: return cudaErrorInvalidValue;
     }
 }
