@@ -35,11 +35,19 @@ and router bytes, far above the 126 MB L2.
           (pokit_cuda_moe_forward_batch); L2 flushed (256 MiB write) between
           timed batches; per-kernel times from pokit_cuda_moe_time_batch.
 
-With N > 1 (torchrun) the ranks run expert parallelism: every step decodes N
-tokens (one per rank, the batch replicated on all ranks) through the 48
-layers; each rank holds 128 / N experts of every layer and runs the batched
-block on them, and the partial outputs are summed by an NCCL all-reduce
-(pokitlms_b200.ep).  value = N tokens per step / the slowest rank's step time.
+With N > 1 (torchrun) every rank decodes its own sequence on its own copy of the
+model (independent replicas: the 16.3 GB pool fits one GPU; no data-path
+collective); value = N tokens per step / the slowest rank's step time, and
+`parity` checks that every rank gives the same bits on a common input.
+
+  decoder (N = 1) benchmark configuration 2 end to end: the whole 48-layer
+          decoder (attention, MoE, Q6_K LM head) greedy-decoding 128 tokens
+          after a 32-token prompt (pokit_cuda_decoder_*).
+  config5 (every N) benchmark configuration 5 through expert parallelism over
+          all ranks (128 / N experts per GPU, NCCL all-reduce of the partial
+          outputs inside the step's CUDA graph), strong scaling, with a parity
+          object and the exchange step timed as an all-reduce and as two
+          all-to-alls.
 
 --impl reference times the PokitLMs reference's own CPU kernels and row
 executor (oracle/_ref) on the host cores, same metric and unit.
