@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
@@ -114,12 +115,26 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     __shared__ __align__(16) float knew[kAttendMaxDim];
     __shared__ __align__(16) float vnew[kAttendMaxDim];
     __shared__ __align__(16) float part[kAttendThreads / 32][kAttendMaxDim];
+    // The position counter changes only at the end of a token step, so it and
+    // the cached keys and values of earlier positions are read before waiting
+    // for the Q/K/V projection: the first CTA of each query group pulls its
+    // head's cached rows towards L2 while the projection finishes.
     const uint32_t t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
     const uint32_t group = qh / kvh, kh = h / group;
     const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
     const int lane = t & 31, warp = t >> 5;
     constexpr int kW = kAttendThreads / 32;
     const uint64_t row_stride = static_cast<uint64_t>(kvh) * d;
+    if (h % group == 0) {
+        const uint32_t lines = (d * 2u + 127u) / 128u;
+        for (uint32_t i = t; i + lines < n * lines; i += kAttendThreads) {
+            const uint64_t at = ((first + i / lines) % window) * row_stride + kh * d + (i % lines) * 64u;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(kc + at));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(vc + at));
+        }
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const bool dim = t < d;
     const float xq = dim ? qkv[h * d + t] : 0.0f;
     const float xk = dim ? qkv[(qh + kh) * d + t] : 0.0f;
@@ -267,6 +282,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, uint32_t n, floa
     __shared__ float rv[32];
     __shared__ uint32_t ri[32];
     __shared__ uint32_t last;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t per = (n + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(n, lo + per);
     float best = -INFINITY;
     uint32_t bi = 0xffffffffu;
@@ -306,6 +322,25 @@ __global__ void argmax_kernel(const float* __restrict__ logits, uint32_t n, floa
 }
 
 __global__ void advance_kernel(uint32_t* pos) { *pos += 1u; }
+
+// A launch that may start while the previous kernel in the stream finishes
+// (programmatic dependent launch); the kernel waits for it with
+// griddepcontrol.wait before reading its results.
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(Params...), uint32_t grid, uint32_t block, size_t smem, cudaStream_t s,
+                             Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
 
 template <uint32_t T>
 cudaError_t launch_embed(const void* table, uint32_t cols, const uint32_t* seq, const uint32_t* pos, float* out,
@@ -688,14 +723,23 @@ private:
             const auto P = [&](uint32_t t) { return tensor_ptr(l, t); };
             const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
             e = launch_linear_normed(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_Q), static_cast<uint32_t>(qd_ + 2 * kd_), H,
-                                     hidden_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_NORM)), eps, qkv_, s);
+                                     hidden_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_NORM)), eps, qkv_, s,
+                                     pdl_);
             if (e != cudaSuccess) break;
-            attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(
-                qkv_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_Q_NORM)),
-                reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_K_NORM)), eps, rope_, rope_ + cfg_.context * half,
-                kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh, kvh, d, scale, att_);
+            const float* qn = reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_Q_NORM));
+            const float* kn = reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_K_NORM));
+            if (pdl_) {
+                e = launch_dependent(attend_kernel, qh, kAttendThreads, win * 4, s, qkv_, qn, kn, eps, rope_,
+                                     rope_ + cfg_.context * half, kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh,
+                                     kvh, d, scale, att_);
+                if (e != cudaSuccess) break;
+            } else {
+                attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(qkv_, qn, kn, eps, rope_, rope_ + cfg_.context * half,
+                                                                  kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh,
+                                                                  kvh, d, scale, att_);
+            }
             e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
-                              hidden_, s, false, true);
+                              hidden_, s, false, true, pdl_);
             if (e != cudaSuccess) break;
             char err[256];
             const pokit_cuda_status st = pokit_cuda_moe_decode_layers(moe_, l, 1, hidden_, s, err, sizeof err);
@@ -711,15 +755,22 @@ private:
             const float* onorm = reinterpret_cast<const float*>(pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT_NORM]);
             const void* ow = pool_ + global_off_[POKIT_CUDA_DEC_OUTPUT];
             e = launch_linear_normed(cfg_.output_type, ow, static_cast<uint32_t>(cfg_.vocab), H, hidden_, onorm, eps,
-                                     logits_, s);
+                                     logits_, s, pdl_);
             if (e == cudaErrorInvalidValue) {        // an F32 or unaligned LM head: norm, then the plain matvec
                 rms_norm_kernel<<<1, 1024, 0, s>>>(hidden_, onorm, eps, xn_, H);
                 e = launch_linear(cfg_.output_type, ow, static_cast<uint32_t>(cfg_.vocab), H, xn_, logits_, s);
             }
             if (e != cudaSuccess) return e;
-            argmax_kernel<<<kArgmaxCtas, 256, 0, s>>>(logits_, static_cast<uint32_t>(cfg_.vocab), part_v_, part_i_,
-                                                      arrivals_, seq_, pos_, static_cast<uint32_t>(cfg_.context + 1),
-                                                      status_);
+            if (pdl_) {
+                e = launch_dependent(argmax_kernel, kArgmaxCtas, 256, 0, s, logits_,
+                                     static_cast<uint32_t>(cfg_.vocab), part_v_, part_i_, arrivals_, seq_, pos_,
+                                     static_cast<uint32_t>(cfg_.context + 1), status_);
+                if (e != cudaSuccess) return e;
+            } else {
+                argmax_kernel<<<kArgmaxCtas, 256, 0, s>>>(logits_, static_cast<uint32_t>(cfg_.vocab), part_v_, part_i_,
+                                                          arrivals_, seq_, pos_,
+                                                          static_cast<uint32_t>(cfg_.context + 1), status_);
+            }
             n += 2;
         }
         advance_kernel<<<1, 1, 0, s>>>(pos_);
@@ -824,6 +875,12 @@ private:
     cudaGraphExec_t graphs_[2] = {nullptr, nullptr};
     int eager_runs_[2] = {0, 0};
     bool no_graphs_ = false;
+    // Programmatic dependent launches between the attention-side kernels
+    // (POKIT_CUDA_PDL=0 turns them off).
+    bool pdl_ = [] {
+        const char* v = std::getenv("POKIT_CUDA_PDL");
+        return !(v && v[0] == '0');
+    }();
     uint64_t launches_per_step_ = 0;
     size_t next_position_ = 0;
     std::string moe_error_;

@@ -11,15 +11,17 @@ namespace pokit {
 int device_sm_count();
 
 // y[rows] = W[rows, cols] . x for a GGUF-encoded W (F32, Q8_0, Q4_K, Q5_K, Q6_K);
-// with accumulate, y[rows] += W . x.
+// with accumulate, y[rows] += W . x.  pdl: launched as a programmatic
+// dependent of the previous kernel in the stream (the quantised row kernel
+// requests its first weight rows before waiting for it).
 cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
                           const float* x, float* y, cudaStream_t stream,
-                          bool force_generic = false, bool accumulate = false);
+                          bool force_generic = false, bool accumulate = false, bool pdl = false);
 
 // y[rows] = W . rms_norm(x, norm_w) (every CTA normalises x as it stages it);
 // quantised W with 16-byte aligned rows of at most 4 KiB, else cudaErrorInvalidValue.
 cudaError_t launch_linear_normed(uint32_t type, const void* w, uint32_t rows, uint32_t cols, const float* x,
-                                 const float* norm_w, float eps, float* y, cudaStream_t stream);
+                                 const float* norm_w, float eps, float* y, cudaStream_t stream, bool pdl = false);
 
 // out[rows, cols] = decoded weights, bit-identical to the reference decoders.
 cudaError_t launch_dequantize(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
@@ -196,15 +198,18 @@ cudaError_t launch_moe_batch(const MoeLayerDev& L, const MoeBatchScratch& S, con
 // ---------------------------------------------------------------------------
 constexpr uint32_t kChainCounterStride = 64;   // uint32 words between the counters (256 B)
 struct ChainScratch {
-    unsigned long long* racc = nullptr;   // [2 parities][experts][8 limbs] router accumulators
-    float* rsq = nullptr;                 // [2][hidden / 16] per-chunk sums of squares
-    uint32_t* rbad = nullptr;             // [2] non-finite partial flags
+    unsigned long long* racc = nullptr;   // [layer % 3][experts][8 limbs] router accumulators
+    float* rsq = nullptr;                 // [layer % 2][hidden / 16] per-chunk sums of squares
+    uint32_t* rbad = nullptr;             // [layer % 3] non-finite partial flags
     float* xrep = nullptr;                // [kChainXReplicas][hidden] x' = ffn_norm * hidden of the next layer
-    uint32_t* counters = nullptr;         // route, act, exit counters, kChainCounterStride apart
+    unsigned long long* act = nullptr;    // [kChainXReplicas][top_k][inter] (layer tag << 32 | activation bits)
+    uint32_t* counters = nullptr;         // route, (unused), exit counters and the layer sequence
+                                          // number, kChainCounterStride apart
 };
 constexpr uint32_t kChainXReplicas = 8;
 // Bytes of the chain scratch (must be zero before the first launch; every
-// launch leaves it at zero).
+// launch leaves the accumulators and counters at zero and advances the
+// sequence number by its layer count).
 uint64_t moe_chain_scratch_bytes(const MoeLayerDev& shape);
 ChainScratch moe_chain_scratch_carve(const MoeLayerDev& shape, void* base);
 

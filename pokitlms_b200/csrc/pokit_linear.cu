@@ -60,6 +60,23 @@ linear_rows_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint8_t* buf0 = smem_raw + cols * 4u + warp * 2u * rb;
     uint8_t* buf1 = buf0 + rb;
+    const uint32_t nw = gridDim.x * (blockDim.x >> 5);
+    uint32_t row = blockIdx.x * (blockDim.x >> 5) + warp;
+    uint4 v[kRowsMaxUnits];
+    const auto load = [&](uint32_t r) {
+        const uint4* src = reinterpret_cast<const uint4*>(w + static_cast<uint64_t>(r) * rb);
+#pragma unroll
+        for (uint32_t j = 0; j < kRowsMaxUnits; ++j) {
+            const uint32_t u = lane + 32u * j;
+            if (u < units) v[j] = ldg_stream128(src + u);
+        }
+    };
+    // The weights do not depend on the previous kernel: the warp's first row
+    // is requested before waiting for it (a programmatic dependent launch
+    // starts this grid while its predecessor finishes; a no-op otherwise).
+    if (row < rows) load(row);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
         for (uint32_t i = threadIdx.x * 4u; i < cols; i += blockDim.x * 4u)
             *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(x + i);
@@ -82,18 +99,7 @@ linear_rows_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, 
         for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], scale), norm_w[i]);
         __syncthreads();
     }
-    const uint32_t nw = gridDim.x * (blockDim.x >> 5);
-    uint32_t row = blockIdx.x * (blockDim.x >> 5) + warp;
     if (row >= rows) return;
-    uint4 v[kRowsMaxUnits];
-    const auto load = [&](uint32_t r) {
-        const uint4* src = reinterpret_cast<const uint4*>(w + static_cast<uint64_t>(r) * rb);
-#pragma unroll
-        for (uint32_t j = 0; j < kRowsMaxUnits; ++j) {
-            const uint32_t u = lane + 32u * j;
-            if (u < units) v[j] = ldg_stream128(src + u);
-        }
-    };
     const auto store = [&](uint8_t* dst) {
 #pragma unroll
         for (uint32_t j = 0; j < kRowsMaxUnits; ++j) {
@@ -101,7 +107,6 @@ linear_rows_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, 
             if (u < units) reinterpret_cast<uint4*>(dst)[u] = v[j];
         }
     };
-    load(row);
     store(buf0);
     __syncwarp();
     bool cur0 = true;
@@ -222,7 +227,7 @@ bool rows_kernel_fits(const void* w, uint32_t cols) {
 
 template <uint32_t T>
 cudaError_t launch_rows(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y, cudaStream_t stream,
-                        bool accumulate, const float* norm_w = nullptr, float norm_eps = 0.0f) {
+                        bool accumulate, const float* norm_w = nullptr, float norm_eps = 0.0f, bool pdl = false) {
     const size_t smem = static_cast<size_t>(cols) * 4u + 2u * row_bytes(T, cols) * (kLinearThreads / 32);
     cudaError_t e = set_smem(linear_rows_kernel<T>, smem);
     if (e != cudaSuccess) return e;
@@ -230,15 +235,25 @@ cudaError_t launch_rows(const void* w, uint32_t rows, uint32_t cols, const float
     uint32_t grid = (rows + warps - 1) / warps;
     const uint32_t cap = static_cast<uint32_t>(sm_count_cached()) * 4u;
     if (grid > cap) grid = cap;
-    linear_rows_kernel<T><<<grid, kLinearThreads, smem, stream>>>(static_cast<const uint8_t*>(w), rows, cols, x, y,
-                                                                  accumulate ? 1 : 0, norm_w, norm_eps);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kLinearThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_rows_kernel<T>, static_cast<const uint8_t*>(w), rows, cols, x, y,
+                              accumulate ? 1 : 0, norm_w, norm_eps);
 }
 
 template <uint32_t T>
 cudaError_t launch_quant(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y, cudaStream_t stream,
-                         bool force_generic, bool accumulate) {
-    if (!force_generic && rows_kernel_fits<T>(w, cols)) return launch_rows<T>(w, rows, cols, x, y, stream, accumulate);
+                         bool force_generic, bool accumulate, bool pdl) {
+    if (!force_generic && rows_kernel_fits<T>(w, cols))
+        return launch_rows<T>(w, rows, cols, x, y, stream, accumulate, nullptr, 0.0f, pdl);
     return launch_generic<T>(w, rows, cols, x, y, stream, accumulate);
 }
 
@@ -264,7 +279,8 @@ cudaError_t launch_dequant(const void* w, uint32_t rows, uint32_t cols, float* o
 int device_sm_count() { return sm_count_cached(); }
 
 cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t cols,
-                          const float* x, float* y, cudaStream_t stream, bool force_generic, bool accumulate) {
+                          const float* x, float* y, cudaStream_t stream, bool force_generic, bool accumulate,
+                          bool pdl) {
     if (rows == 0 || cols == 0) return cudaErrorInvalidValue;
     switch (type) {
         case kF32: {
@@ -276,30 +292,30 @@ cudaError_t launch_linear(uint32_t type, const void* w, uint32_t rows, uint32_t 
                 static_cast<const float*>(w), rows, cols, x, y, accumulate ? 1 : 0);
             return cudaGetLastError();
         }
-        case kQ4_K: return launch_quant<kQ4_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
-        case kQ5_K: return launch_quant<kQ5_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
-        case kQ6_K: return launch_quant<kQ6_K>(w, rows, cols, x, y, stream, force_generic, accumulate);
-        case kQ8_0: return launch_quant<kQ8_0>(w, rows, cols, x, y, stream, force_generic, accumulate);
+        case kQ4_K: return launch_quant<kQ4_K>(w, rows, cols, x, y, stream, force_generic, accumulate, pdl);
+        case kQ5_K: return launch_quant<kQ5_K>(w, rows, cols, x, y, stream, force_generic, accumulate, pdl);
+        case kQ6_K: return launch_quant<kQ6_K>(w, rows, cols, x, y, stream, force_generic, accumulate, pdl);
+        case kQ8_0: return launch_quant<kQ8_0>(w, rows, cols, x, y, stream, force_generic, accumulate, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
 
 cudaError_t launch_linear_normed(uint32_t type, const void* w, uint32_t rows, uint32_t cols, const float* x,
-                                 const float* norm_w, float eps, float* y, cudaStream_t stream) {
+                                 const float* norm_w, float eps, float* y, cudaStream_t stream, bool pdl) {
     if (rows == 0 || cols == 0 || !norm_w) return cudaErrorInvalidValue;
     switch (type) {
         case kQ4_K:
             if (!rows_kernel_fits<kQ4_K>(w, cols)) return cudaErrorInvalidValue;
-            return launch_rows<kQ4_K>(w, rows, cols, x, y, stream, false, norm_w, eps);
+            return launch_rows<kQ4_K>(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
         case kQ5_K:
             if (!rows_kernel_fits<kQ5_K>(w, cols)) return cudaErrorInvalidValue;
-            return launch_rows<kQ5_K>(w, rows, cols, x, y, stream, false, norm_w, eps);
+            return launch_rows<kQ5_K>(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
         case kQ6_K:
             if (!rows_kernel_fits<kQ6_K>(w, cols)) return cudaErrorInvalidValue;
-            return launch_rows<kQ6_K>(w, rows, cols, x, y, stream, false, norm_w, eps);
+            return launch_rows<kQ6_K>(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
         case kQ8_0:
             if (!rows_kernel_fits<kQ8_0>(w, cols)) return cudaErrorInvalidValue;
-            return launch_rows<kQ8_0>(w, rows, cols, x, y, stream, false, norm_w, eps);
+            return launch_rows<kQ8_0>(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -218,6 +218,14 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 __device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 // Grid-wide barrier for a co-resident (cooperative) grid.  `counter` only
 // grows; barrier number `index` (1-based within this launch) completes when
@@ -1683,23 +1691,29 @@ __global__ void __maxnreg__(88) moe_down_mma_kernel(const __grid_constant__ MmaA
 //          halves); its TMA boxes go out right after the selection, together
 //          with its D unit's down boxes (all k slots x I/256 superblocks of
 //          its 16 output rows) and the next layer's router slice (registers).
-//          act = silu(s g) * (s u) to global (rep replicas), then the CTA
-//          arrives on the act counter.
-//   D      CTA c < H/16 owns hidden rows [16c, 16c + 16): it waits for the
-//          act counter (every CTA's G done), builds the activation records,
-//          multiplies its already-landed down boxes, combines the slots in
-//          route order into the residual, and adds the next layer's router
-//          partials for its 16 rows into the other parity's accumulators
-//          before arriving on the route counter.
+//          act = silu(s g) * (s u) goes to global memory as 8-byte words
+//          (the layer's sequence number << 32 | the float's bits): no fence
+//          or counter between producer and consumer.
+//   D      CTA c < H/16 owns hidden rows [16c, 16c + 16): it reads the k x I
+//          activation words until every tag is this layer's (every CTA's G
+//          done), builds the activation records, multiplies its already-
+//          landed down boxes, combines the slots in route order into the
+//          residual, and adds the next layer's router partials for its 16
+//          rows into the other parity's accumulators before arriving on the
+//          route counter.
 //
-// Buffer reuse is ordered by the counters: a CTA zeroes its share of the
-// previous layer's accumulators (every CTA has read them: passing this
-// layer's route wait implies every CTA passed the previous layer's act
-// wait) before its act arrival, and D units add into them only after the
-// act wait.  The last CTA to leave zeroes the accumulators read last and
-// resets the counters, so the next launch finds them at zero.  Every wait
-// is bounded (~2 s): a timeout sets kStatusWaitTimeout (a sticky failure on
-// the host), the CTA drains its in-flight copies and returns.
+// Buffer reuse: layer l's router accumulators sit in parity l % 3.  The D
+// units zero parity (l - 1) % 3 during layer l (every CTA has read it:
+// passing layer l's route wait implies every D unit saw every CTA's layer
+// l - 1 activation words, written after that CTA's routing reads); their
+// layer l route arrivals (fence, release) publish the zeros before any CTA
+// adds into that parity again, in layer l + 1's D.  Each activation word is
+// rewritten every layer, and a CTA writes layer l + 1's only after every D
+// unit finished reading layer l's.  The last CTA to leave zeroes the
+// accumulators read last, resets the counters and advances the sequence
+// number, so the next launch finds them ready.  Every wait is bounded (~2 s):
+// a timeout sets kStatusWaitTimeout (a sticky failure on the host), the CTA
+// drains its in-flight copies and returns.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kChainGroupsPerCta = kWarps / 4;
 constexpr uint32_t kChainStamps = 8;
@@ -1847,8 +1861,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
     uint8_t* gtiles = smem + c.gtiles;
     uint8_t* dtiles = smem + c.dtiles;
     uint32_t* ctr_route = a.C.counters;
-    uint32_t* ctr_act = a.C.counters + kChainCounterStride;
     uint32_t* ctr_exit = a.C.counters + 2u * kChainCounterStride;
+    uint32_t* ctr_seq = a.C.counters + 3u * kChainCounterStride;
     uint32_t* status = a.S.status;
     const uint64_t racc_span = static_cast<uint64_t>(E) * kRaccLimbs;
     // x' = ffn_norm * hidden of the layer being routed, in kChainXReplicas
@@ -1904,21 +1918,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
         RouterSlice rs{};
         if (static_cast<uint32_t>(tid) < E) rs = router_slice(router_of(a.first), H, tid, cta);
         const uint32_t p = a.first & 1u;
-        chain_partials(router_of(a.first), E, rs, hrow, a.C.racc + p * racc_span, a.C.rbad + p, a.C.rsq + p * units,
+        const uint32_t r0 = a.first % 3u;
+        chain_partials(router_of(a.first), E, rs, hrow, a.C.racc + r0 * racc_span, a.C.rbad + r0, a.C.rsq + p * units,
                        cta, H);
         chain_arrive(ctr_route);
     }
 
     uint32_t phase = 0;
     bool ok = true;
+    // Activation words carry the sequence number of the layer that wrote
+    // them (launches advance it by their layer count; zero-filled memory
+    // never matches).
+    const uint32_t seq0 = __ldcg(ctr_seq);
     for (uint32_t l = 0; l < a.count && ok; ++l, phase ^= 1u) {
-        const uint32_t layer = a.first + l, p = layer & 1u;
+        const uint32_t layer = a.first + l, p = layer & 1u, pr = layer % 3u, tag = seq0 + l + 1u;
         const bool has_next = l + 1 < a.count;
         const uint32_t nlayer = has_next ? layer + 1 : layer;
         // ---- route ----
         if (!chain_wait(ctr_route, units * (l + 1u), status, &abort_sh)) { ok = false; break; }
         stamp(l, 0);
-        const unsigned long long* racc = a.C.racc + p * racc_span;
+        const unsigned long long* racc = a.C.racc + pr * racc_span;
         if (warp < static_cast<int>(kTailLogitWarps)) {
             if (warp == 0) {
                 float sq = 0.0f;
@@ -1928,7 +1947,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                 if (lane == 0) {
                     // rms_norm scale (src/rms_norm.cpp:20-26).
                     scale_sh = 1.0f / sqrtf(sq / static_cast<float>(H) + Ls.rms_eps);
-                    bad_sh = __ldcg(a.C.rbad + p);
+                    bad_sh = __ldcg(a.C.rbad + pr);
                 }
             }
             for (uint32_t e0 = warp * 32u; e0 < E; e0 += kTailLogitWarps * 32u) {
@@ -1987,11 +2006,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                            static_cast<int>(layer), &mybars[i]);
             }
         }
-        // The previous layer's accumulators and flag: every CTA has read them.
-        if (l > 0) {
-            for (uint32_t i = cta * kThreads + tid; i < racc_span; i += G * kThreads)
-                a.C.racc[(p ^ 1u) * racc_span + i] = 0ull;
-            if (cta == 0 && tid == 0) a.C.rbad[p ^ 1u] = 0u;
+        // The previous layer's accumulators and flag (every CTA has read
+        // them), zeroed by the D units: their route arrivals publish the
+        // zeros before anyone adds into this parity again (the layer after next).
+        if (has_unit) {
+            const uint32_t pz = (layer + 2u) % 3u;
+            for (uint32_t i = cta * kThreads + tid; i < racc_span; i += units * kThreads)
+                a.C.racc[pz * racc_span + i] = 0ull;
+            if (cta == 0 && tid == 0) a.C.rbad[pz] = 0u;
         }
         // The next layer's router slice and ffn_norm, this unit's residual rows.
         RouterSlice rs{};
@@ -2044,33 +2066,54 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                 const float uv = part[(gl * 4 + 2) * 16 + r] + part[(gl * 4 + 3) * 16 + r];
                 const uint32_t slot = rgx / per_slot, row = (rgx % per_slot) * 16u + r;
                 const float av = silu_mul(gv * scale, uv * scale, Ls.flavour);
-                for (uint32_t cp = 0; cp < a.S.rep; ++cp)
-                    a.S.actr[static_cast<uint64_t>(cp) * k * I + slot * I + row] = av;
+                const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(av);
+                for (uint32_t r = 0; r < kChainXReplicas; ++r)
+                    st_relaxed_gpu_u64(a.C.act + (static_cast<uint64_t>(r) * k + slot) * I + row, w);
             }
         }
-        chain_arrive(ctr_act);
         stamp(l, 3);
         if (!has_unit) continue;
         // ---- D ----
-        if (!chain_wait(ctr_act, G * (l + 1u), status, &abort_sh)) {
-            if (static_cast<uint32_t>(warp) < k && lane == 0)
-                for (uint32_t j = 0; j < dpairs; ++j) mbar_wait(&dbars[warp * dpairs + j], phase);
-            ok = false;
-            break;
-        }
-        stamp(l, 4);
         {
-            const float* act = a.S.actr + static_cast<uint64_t>(cta % a.S.rep) * k * I;
+            // Every activation word of this layer, read as it arrives: a word
+            // is current once its tag is this layer's sequence number (each
+            // word is one 8-byte store, so tag and value arrive together).
             const uint32_t nrec = k * nsd;
             // Two records per warp per pass, all of their loads in flight together.
             for (uint32_t q0 = warp; q0 < nrec; q0 += 2 * kWarps) {
-                float v[2][8];
+                unsigned long long v[2][8];
+                const auto word = [&](int i, int j) {
+                    return a.C.act + static_cast<uint64_t>(cta % kChainXReplicas) * k * I +
+                           static_cast<uint64_t>(q0 + i * kWarps) * 256u + 32 * j + lane;
+                };
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const uint32_t q = q0 + i * kWarps;
+                for (int i = 0; i < 2; ++i)
 #pragma unroll
                     for (int j = 0; j < 8; ++j)
-                        v[i][j] = q < nrec ? __ldcg(act + static_cast<uint64_t>(q) * 256u + 32 * j + lane) : 0.0f;
+                        v[i][j] = q0 + i * kWarps < nrec ? ld_relaxed_gpu_u64(word(i, j))
+                                                         : static_cast<unsigned long long>(tag) << 32;
+                long long t0 = 0;
+                for (uint32_t polls = 0;; ++polls) {
+                    bool ready = true;
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) ready = ready && static_cast<uint32_t>(v[i][j] >> 32) == tag;
+                    if (__all_sync(0xffffffffu, ready)) break;
+                    if (polls == 0) t0 = clock64();
+                    if ((polls & 63u) == 63u &&
+                        ((ld_acquire_gpu(status) & kStatusWaitTimeout) || clock64() - t0 > kBarrierTimeoutCycles)) {
+                        if (lane == 0) {
+                            atomicOr(status, kStatusWaitTimeout);
+                            abort_sh = 1u;
+                        }
+                        break;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (static_cast<uint32_t>(v[i][j] >> 32) != tag) v[i][j] = ld_relaxed_gpu_u64(word(i, j));
                 }
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -2078,7 +2121,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                     if (q < nrec) {
                         float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = v[i][j];
+                        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = __uint_as_float(static_cast<uint32_t>(v[i][j]));
                     }
                 }
                 __syncwarp();
@@ -2089,7 +2132,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                         q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords, lane);
                 }
             }
+            stamp(l, 4);
             __syncthreads();
+            if (abort_sh) {
+                if (static_cast<uint32_t>(warp) < k && lane == 0)
+                    for (uint32_t j = 0; j < dpairs; ++j) mbar_wait(&dbars[warp * dpairs + j], phase);
+                ok = false;
+                break;
+            }
             stamp(l, 5);
             for (uint32_t u = warp; u < nrec; u += 2 * kWarps) {
                 const uint32_t v2 = u + kWarps;
@@ -2145,7 +2195,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
             }
             if (has_next) {
                 __syncthreads();
-                chain_partials(router_of(nlayer), E, rs, hrow, a.C.racc + (p ^ 1u) * racc_span, a.C.rbad + (p ^ 1u),
+                const uint32_t pn = (layer + 1u) % 3u;
+                chain_partials(router_of(nlayer), E, rs, hrow, a.C.racc + pn * racc_span, a.C.rbad + pn,
                                a.C.rsq + (p ^ 1u) * units, cta, H);
             }
         }
@@ -2162,14 +2213,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
     __syncthreads();
     if (!last_sh) return;
     __threadfence();
-    const uint32_t plast = (a.first + a.count - 1u) & 1u;
+    const uint32_t plast = (a.first + a.count - 1u) % 3u;
     for (uint32_t i = tid; i < racc_span; i += kThreads) a.C.racc[plast * racc_span + i] = 0ull;
     __syncthreads();
     if (tid == 0) {
         a.C.rbad[plast] = 0u;
         *ctr_route = 0u;
-        *ctr_act = 0u;
         *ctr_exit = 0u;
+        *ctr_seq = seq0 + a.count;
         __threadfence();
     }
 }
@@ -2544,18 +2595,20 @@ cudaError_t time_moe_kernel(const MoeLayerDev* layers, uint32_t count, const Moe
 }
 
 uint64_t moe_chain_scratch_bytes(const MoeLayerDev& L) {
-    return align256(2ull * L.experts * kRaccLimbs * 8u) + align256(2ull * (L.hidden / kPartRows) * 4u) +
-           align256(2u * 4u) + align256(static_cast<uint64_t>(kChainXReplicas) * L.hidden * 4u) +
-           3u * kChainCounterStride * 4u;
+    return align256(3ull * L.experts * kRaccLimbs * 8u) + align256(2ull * (L.hidden / kPartRows) * 4u) +
+           align256(3u * 4u) + align256(static_cast<uint64_t>(kChainXReplicas) * L.hidden * 4u) +
+           align256(static_cast<uint64_t>(kChainXReplicas) * L.top_k * L.inter * 8u) + 4u * kChainCounterStride * 4u;
 }
 
 ChainScratch moe_chain_scratch_carve(const MoeLayerDev& L, void* base) {
     uint8_t* p = static_cast<uint8_t*>(base);
     ChainScratch c;
-    c.racc = reinterpret_cast<unsigned long long*>(p); p += align256(2ull * L.experts * kRaccLimbs * 8u);
+    c.racc = reinterpret_cast<unsigned long long*>(p); p += align256(3ull * L.experts * kRaccLimbs * 8u);
     c.rsq = reinterpret_cast<float*>(p); p += align256(2ull * (L.hidden / kPartRows) * 4u);
-    c.rbad = reinterpret_cast<uint32_t*>(p); p += align256(2u * 4u);
+    c.rbad = reinterpret_cast<uint32_t*>(p); p += align256(3u * 4u);
     c.xrep = reinterpret_cast<float*>(p); p += align256(static_cast<uint64_t>(kChainXReplicas) * L.hidden * 4u);
+    c.act = reinterpret_cast<unsigned long long*>(p);
+    p += align256(static_cast<uint64_t>(kChainXReplicas) * L.top_k * L.inter * 8u);
     c.counters = reinterpret_cast<uint32_t*>(p);
     return c;
 }
@@ -2603,7 +2656,9 @@ bool moe_chain_plan(const MoeLayerDev* layers, uint32_t n, ChainPlan* plan) {
     const uint32_t sms = static_cast<uint32_t>(device_sm_count());
     const uint32_t units = L0.hidden / kPartRows, groups = L0.top_k * (L0.inter / 16u);
     const ChainLayout c = chain_layout(L0);
-    if (units > sms || groups > kChainGroupsPerCta * sms || L0.experts > kThreads ||
+    // Every CTA owns at least one gate/up row group (its activation words
+    // order its routing reads before the D units' next writes).
+    if (units > sms || groups > kChainGroupsPerCta * sms || groups < sms || L0.experts > kThreads ||
         c.total > 227u * 1024u || (L0.hidden >> 8) > 64u)
         return false;
     if (ensure_smem(moe_chain_kernel, c.total) != cudaSuccess) return false;
