@@ -435,8 +435,22 @@ size_t pokit_cuda_moe_tensor_bytes(const pokit_cuda_moe* moe, size_t layer, uint
  * final RMSNorm, the LM head and the argmax (src/qwen3_moe_runner.cpp:580-704,
  * 751-821).  Every weight is resident in HBM; the MoE tensors (router,
  * ffn_norm, experts) live in the handle returned by pokit_cuda_decoder_moe and
- * are uploaded or synthesised with the pokit_cuda_moe_* calls. */
+ * are uploaded or synthesised with the pokit_cuda_moe_* calls.
+ *
+ * With arch = POKIT_CUDA_ARCH_QWEN35MOE the same handle replaces Qwen35Runner
+ * (include/pokitlms/model/qwen35_runner.hpp:56-100) for the Qwen3.5-MoE hybrid
+ * (src/qwen35_runner.cpp:538-777): layer l is full attention when
+ * (l + 1) % full_attention_interval == 0 (gated query: sigmoid(gate) times the
+ * attention output, partial MRoPE over rotary_dim dimensions), otherwise a
+ * Gated DeltaNet layer (attn_qkv / attn_gate / ssm_alpha / ssm_beta
+ * projections, causal conv1d, the gated delta rule, gated RMSNorm, ssm_out);
+ * the MoE blocks carry the sigmoid-gated shared expert. */
 typedef struct pokit_cuda_decoder pokit_cuda_decoder;
+
+typedef enum pokit_cuda_decoder_arch {
+    POKIT_CUDA_ARCH_QWEN3MOE = 0,     /* general.architecture "qwen3moe" */
+    POKIT_CUDA_ARCH_QWEN35MOE = 1     /* general.architecture "qwen35moe" */
+} pokit_cuda_decoder_arch;
 
 typedef struct pokit_cuda_decoder_config {
     int device;
@@ -456,6 +470,20 @@ typedef struct pokit_cuda_decoder_config {
     uint32_t expert_type;             /* GGML type of the routed experts */
     uint32_t embed_type;              /* GGML type of token_embd */
     uint32_t output_type;             /* GGML type of output (the LM head) */
+    /* Qwen3.5-MoE hybrid (arch = POKIT_CUDA_ARCH_QWEN35MOE); zero for qwen3moe. */
+    uint32_t arch;                    /* pokit_cuda_decoder_arch */
+    size_t rotary_dim;                /* rope.dimension_count: even, <= head_dim */
+    uint32_t rope_sections[4];        /* rope.dimension_sections (text positions) */
+    size_t full_attention_interval;   /* full_attention_interval */
+    size_t ssm_conv_kernel;           /* ssm.conv_kernel */
+    size_t ssm_state_size;            /* ssm.state_size: linear key head dimension */
+    size_t ssm_group_count;           /* ssm.group_count: linear key heads */
+    size_t ssm_time_step_rank;        /* ssm.time_step_rank: linear value heads */
+    size_t ssm_inner_size;            /* ssm.inner_size: value heads x value head dimension */
+    float expert_weights_scale;       /* expert_weights_scale */
+    size_t shared_inter;              /* expert_shared_feed_forward_length */
+    uint32_t shared_type;             /* GGML type of the shared expert tensors */
+    const uint32_t* layer_down_types; /* optional [layers] routed down types (NULL: expert_type) */
 } pokit_cuda_decoder_config;
 
 /* Decoder tensors outside the MoE blocks (GGUF names in comments). */
@@ -469,7 +497,18 @@ typedef enum pokit_cuda_decoder_tensor {
     POKIT_CUDA_DEC_ATTN_K = 6,        /* blk.L.attn_k.weight      [hidden, kv_heads * head_dim] */
     POKIT_CUDA_DEC_ATTN_K_NORM = 7,   /* blk.L.attn_k_norm.weight F32 [head_dim] */
     POKIT_CUDA_DEC_ATTN_V = 8,        /* blk.L.attn_v.weight      [hidden, kv_heads * head_dim] */
-    POKIT_CUDA_DEC_ATTN_OUTPUT = 9    /* blk.L.attn_output.weight [q_heads * head_dim, hidden] */
+    POKIT_CUDA_DEC_ATTN_OUTPUT = 9,   /* blk.L.attn_output.weight [q_heads * head_dim, hidden] */
+    /* Qwen3.5: attn_q is [hidden, q_heads * head_dim * 2] (per head: query,
+     * then gate); the tensors below exist on Gated DeltaNet layers only. */
+    POKIT_CUDA_DEC_SSM_QKV = 10,      /* blk.L.attn_qkv.weight  [hidden, 2 * key width + ssm_inner_size] */
+    POKIT_CUDA_DEC_SSM_GATE = 11,     /* blk.L.attn_gate.weight [hidden, ssm_inner_size] */
+    POKIT_CUDA_DEC_SSM_ALPHA = 12,    /* blk.L.ssm_alpha.weight [hidden, ssm_time_step_rank] */
+    POKIT_CUDA_DEC_SSM_BETA = 13,     /* blk.L.ssm_beta.weight  [hidden, ssm_time_step_rank] */
+    POKIT_CUDA_DEC_SSM_CONV1D = 14,   /* blk.L.ssm_conv1d.weight F32 [conv_kernel, channels] */
+    POKIT_CUDA_DEC_SSM_A = 15,        /* blk.L.ssm_a             F32 [ssm_time_step_rank] */
+    POKIT_CUDA_DEC_SSM_DT_BIAS = 16,  /* blk.L.ssm_dt.bias       F32 [ssm_time_step_rank] */
+    POKIT_CUDA_DEC_SSM_NORM = 17,     /* blk.L.ssm_norm.weight   F32 [value head dimension] */
+    POKIT_CUDA_DEC_SSM_OUT = 18       /* blk.L.ssm_out.weight    [ssm_inner_size, hidden] */
 } pokit_cuda_decoder_tensor;
 
 /* Mirrors GenerationStats (qwen3_moe_runner.hpp:33-37). */
@@ -523,7 +562,8 @@ pokit_cuda_status pokit_cuda_decoder_generate_tokens(pokit_cuda_decoder* decoder
 pokit_cuda_status pokit_cuda_decoder_run_steps(pokit_cuda_decoder* decoder, size_t steps, void* stream,
                                                char* error_buffer, size_t error_capacity);
 
-/* Clears the decode state (position 0, empty KV cache). */
+/* Clears the decode state (position 0, empty KV cache, zero convolution and
+ * recurrent states). */
 pokit_cuda_status pokit_cuda_decoder_reset(pokit_cuda_decoder* decoder, char* error_buffer, size_t error_capacity);
 
 /* Kernels one token step with logits launches (measurement). */

@@ -119,7 +119,16 @@ class DecoderConfig(C.Structure):
         ("rope_theta", C.c_float), ("normalize_top_k", C.c_int), ("eos_token", C.c_uint32),
         ("attn_type", C.c_uint32), ("expert_type", C.c_uint32), ("embed_type", C.c_uint32),
         ("output_type", C.c_uint32),
+        # Qwen3.5-MoE hybrid (arch ARCH_QWEN35MOE); zero for qwen3moe.
+        ("arch", C.c_uint32), ("rotary_dim", C.c_size_t), ("rope_sections", C.c_uint32 * 4),
+        ("full_attention_interval", C.c_size_t), ("ssm_conv_kernel", C.c_size_t),
+        ("ssm_state_size", C.c_size_t), ("ssm_group_count", C.c_size_t), ("ssm_time_step_rank", C.c_size_t),
+        ("ssm_inner_size", C.c_size_t), ("expert_weights_scale", C.c_float), ("shared_inter", C.c_size_t),
+        ("shared_type", C.c_uint32), ("layer_down_types", C.POINTER(C.c_uint32)),
     ]
+
+
+ARCH_QWEN3MOE, ARCH_QWEN35MOE = 0, 1
 
 
 class GenerationStats(C.Structure):
@@ -129,6 +138,8 @@ class GenerationStats(C.Structure):
 
 DEC_TOKEN_EMBD, DEC_OUTPUT_NORM, DEC_OUTPUT = 0, 1, 2
 DEC_ATTN_NORM, DEC_ATTN_Q, DEC_ATTN_Q_NORM, DEC_ATTN_K, DEC_ATTN_K_NORM, DEC_ATTN_V, DEC_ATTN_OUTPUT = range(3, 10)
+(DEC_SSM_QKV, DEC_SSM_GATE, DEC_SSM_ALPHA, DEC_SSM_BETA, DEC_SSM_CONV1D, DEC_SSM_A, DEC_SSM_DT_BIAS, DEC_SSM_NORM,
+ DEC_SSM_OUT) = range(10, 19)
 
 class DeltaNetShape(C.Structure):
     _fields_ = [("key_heads", C.c_size_t), ("value_heads", C.c_size_t), ("key_dim", C.c_size_t),

@@ -330,15 +330,36 @@ __all__ = ["CudaLinearBackend", "CudaMoeBackend", "linear", "dequantize_rows", "
 
 
 class CudaDecoder:
-    """The whole Qwen3-MoE decoder of one sequence on the GPU (the reference's
-    Qwen3MoeRunner: forward_token, generate_tokens with greedy sampling)."""
+    """The whole decoder of one sequence on the GPU: the reference's
+    Qwen3MoeRunner for a gguf.Qwen3MoeShape, or its Qwen35Runner (the
+    Qwen3.5-MoE hybrid of Gated DeltaNet and gated full-attention layers) for
+    a gguf.Qwen35MoeShape; forward_token, generate_tokens with greedy sampling."""
 
     def __init__(self, shape, *, device: int = 0, kv_window: int = 0):
-        """`shape`: a pokitlms_b200.gguf.Qwen3MoeShape (the model's hyper-parameters and tensor types)."""
+        """`shape`: a pokitlms_b200.gguf.Qwen3MoeShape or Qwen35MoeShape (the
+        model's hyper-parameters and tensor types)."""
+        from . import gguf
+        self.hybrid = isinstance(shape, gguf.Qwen35MoeShape)
         cfg = _lib.DecoderConfig(device, shape.layers, shape.hidden, shape.vocab, shape.q_heads, shape.kv_heads,
                                  shape.head_dim, shape.experts, shape.top_k, shape.expert_inter, shape.context,
                                  kv_window, shape.rms_epsilon, shape.rope_theta, 1, shape.eos, shape.attn_type,
                                  shape.expert_type, shape.embed_type, shape.output_type)
+        self._ldt = None
+        if self.hybrid:
+            self._ldt = (C.c_uint32 * shape.layers)(*[shape.down_type(l) for l in range(shape.layers)])
+            cfg.arch = _lib.ARCH_QWEN35MOE
+            cfg.rotary_dim = shape.rotary_dim
+            cfg.rope_sections[:] = list(shape.rope_sections)
+            cfg.full_attention_interval = shape.full_attention_interval
+            cfg.ssm_conv_kernel = shape.ssm_conv_kernel
+            cfg.ssm_state_size = shape.ssm_state_size
+            cfg.ssm_group_count = shape.ssm_group_count
+            cfg.ssm_time_step_rank = shape.ssm_time_step_rank
+            cfg.ssm_inner_size = shape.ssm_inner_size
+            cfg.expert_weights_scale = shape.expert_weights_scale
+            cfg.shared_inter = shape.shared_inter
+            cfg.shared_type = shape.shared_type
+            cfg.layer_down_types = C.cast(self._ldt, C.POINTER(C.c_uint32))
         h = C.c_void_p()
         call("pokit_cuda_decoder_create", C.byref(cfg), C.byref(h))
         self._h = h
@@ -348,8 +369,10 @@ class CudaDecoder:
         moe._borrowed = True
         moe._ldt = None
         moe.layers, moe.hidden, moe.inter = shape.layers, shape.hidden, shape.expert_inter
-        moe.experts, moe.top_k, moe.flavour = shape.experts, shape.top_k, QWEN3
-        moe.shared_inter, moe.expert_first, moe.expert_count = 0, 0, shape.experts
+        moe.experts, moe.top_k = shape.experts, shape.top_k
+        moe.flavour = QWEN35 if self.hybrid else QWEN3
+        moe.shared_inter = shape.shared_inter if self.hybrid else 0
+        moe.expert_first, moe.expert_count = 0, shape.experts
         self.moe = moe
 
     def tensor_bytes(self, layer: int, tensor: int) -> int:
@@ -364,10 +387,11 @@ class CudaDecoder:
 
     def synthesize_model(self) -> None:
         """Every tensor of the synthetic model that pokitlms_b200.gguf writes
-        for this shape, generated in HBM from the same seeds (F32 routers and
-        norms uploaded from the host)."""
+        for this shape, generated in HBM from the same seeds (F32 routers,
+        norms and DeltaNet parameters uploaded from the host)."""
         from . import gguf, synth
-        from ._lib import DOWN as MD, FFN_NORM, GATE as MG, ROUTER, UP as MU
+        from ._lib import (DOWN as MD, FFN_NORM, GATE as MG, ROUTER, SHARED_DOWN, SHARED_GATE, SHARED_ROUTER,
+                           SHARED_UP, UP as MU)
         s = self.shape
         seed = s.seed
         H, d = s.hidden, s.head_dim
@@ -376,15 +400,30 @@ class CudaDecoder:
         self.upload_tensor(0, _lib.DEC_OUTPUT_NORM, np.ones(H, np.float32))
         for l in range(s.layers):
             self.upload_tensor(l, _lib.DEC_ATTN_NORM, np.ones(H, np.float32))
-            self.upload_tensor(l, _lib.DEC_ATTN_Q_NORM, np.ones(d, np.float32))
-            self.upload_tensor(l, _lib.DEC_ATTN_K_NORM, np.ones(d, np.float32))
-            for t, sid in ((_lib.DEC_ATTN_Q, gguf.ATTN_Q), (_lib.DEC_ATTN_K, gguf.ATTN_K),
-                           (_lib.DEC_ATTN_V, gguf.ATTN_V), (_lib.DEC_ATTN_OUTPUT, gguf.ATTN_OUTPUT)):
-                self.synthesize_tensor(l, t, seed, synth.stream_id(l, sid))
+            if not self.hybrid or s.attention_layer(l):
+                self.upload_tensor(l, _lib.DEC_ATTN_Q_NORM, np.ones(d, np.float32))
+                self.upload_tensor(l, _lib.DEC_ATTN_K_NORM, np.ones(d, np.float32))
+                for t, sid in ((_lib.DEC_ATTN_Q, gguf.ATTN_Q), (_lib.DEC_ATTN_K, gguf.ATTN_K),
+                               (_lib.DEC_ATTN_V, gguf.ATTN_V), (_lib.DEC_ATTN_OUTPUT, gguf.ATTN_OUTPUT)):
+                    self.synthesize_tensor(l, t, seed, synth.stream_id(l, sid))
+            else:
+                for t, sid in ((_lib.DEC_SSM_QKV, gguf.SSM_QKV), (_lib.DEC_SSM_GATE, gguf.SSM_GATE),
+                               (_lib.DEC_SSM_ALPHA, gguf.SSM_ALPHA), (_lib.DEC_SSM_BETA, gguf.SSM_BETA),
+                               (_lib.DEC_SSM_OUT, gguf.SSM_OUT)):
+                    self.synthesize_tensor(l, t, seed, synth.stream_id(l, sid))
+                f = gguf.ssm_f32_tensors(s, l)
+                self.upload_tensor(l, _lib.DEC_SSM_CONV1D, f["conv1d"])
+                self.upload_tensor(l, _lib.DEC_SSM_A, f["a"])
+                self.upload_tensor(l, _lib.DEC_SSM_DT_BIAS, f["dt_bias"])
+                self.upload_tensor(l, _lib.DEC_SSM_NORM, f["norm"])
             self.moe.upload_tensor(l, ROUTER, synth.router_weights(s.experts, H, seed, l))
             self.moe.upload_tensor(l, FFN_NORM, np.ones(H, np.float32))
             for t in (MG, MU, MD):
                 self.moe.synthesize_tensor(l, t, seed, synth.stream_id(l, t))
+            if self.hybrid and s.shared_inter:
+                self.moe.upload_tensor(l, SHARED_ROUTER, gguf.shared_router(s, l))
+                for t in (SHARED_GATE, SHARED_UP, SHARED_DOWN):
+                    self.moe.synthesize_tensor(l, t, seed, synth.stream_id(l, t))
 
     def forward_token(self, token: int, position: int, logits: bool = True) -> np.ndarray | None:
         out = np.empty(self.shape.vocab, np.float32) if logits else None

@@ -460,6 +460,25 @@ public:
             kernel_launches_ += 1;
             return;
         }
+        // Inside the caller's stream capture (a decoder's token-step graph)
+        // the blocks' kernels join that capture directly: a graph launch
+        // cannot be captured.
+        cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+        guard(cudaStreamIsCapturing(st, &capturing), "capture status");
+        if (capturing == cudaStreamCaptureStatusActive) {
+            uint32_t launches = 0;
+            for (size_t l = first; l < first + count; ++l) {
+                const MoeLayerDev* prev = l > first ? &devs_[l - 1] : nullptr;
+                const MoeLayerDev* next = l + 1 < first + count ? &devs_[l + 1] : nullptr;
+                uint32_t n = 0;
+                guard(launch_moe_block(devs_[l], S_, nullptr, hidden, nullptr, prev, next, st, &n), "block launch");
+                launches += n;
+            }
+            forward_calls_ += count;
+            hits_ += count * cfg_.top_k;
+            kernel_launches_ += launches;
+            return;
+        }
         const auto key = std::make_tuple(first, count, hidden);
         auto it = graphs_.find(key);
         if (it == graphs_.end()) {

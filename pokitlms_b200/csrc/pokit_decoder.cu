@@ -14,6 +14,14 @@
 //             router, top-k, experts, combine, residual)
 //   logits    rms_norm(output_norm) -> LM head -> greedy argmax (first maximum,
 //             :320-333) written as the next token of the sequence
+// The Qwen3.5-MoE hybrid (Qwen35Runner::Impl::forward_into,
+// src/qwen35_runner.cpp:538-777) runs in the same frame: its full-attention
+// layers project a gated query (per head: query, then gate), rotate the first
+// rotary_dim dimensions with the text-position MRoPE table and multiply the
+// attention output by sigmoid(gate); its Gated DeltaNet layers project
+// [qkv | gate | alpha | beta] in one matvec, run the conv1d + delta-rule step
+// (pokit_cuda_delta_net_step) on per-layer states and add ssm_out's product;
+// the MoE blocks add the sigmoid-gated shared expert.
 // The token and position live in device memory, so a step is position-free
 // and runs as one CUDA graph replay (captured on first use).
 #include "../../include/pokit_cuda.h"
@@ -37,7 +45,6 @@ namespace pokit {
 namespace {
 
 constexpr uint32_t kStatusDecoderNonFinite = 1u;   // LM head produced NaN/Inf (the reference throws)
-constexpr uint32_t kMaxHeadDim = 256;
 constexpr uint32_t kMaxWindow = 8192;
 constexpr uint32_t kArgmaxCtas = 148;
 
@@ -82,7 +89,7 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
 // w, w + 8, ... for four dimensions per lane, eight positions' loads in flight
 // per round; the eight warps' partial sums are added in warp order.
 constexpr uint32_t kAttendThreads = 256;
-constexpr uint32_t kAttendMaxDim = 128;
+constexpr uint32_t kAttendMaxDim = 256;
 
 // The CTA first forms its own query and its KV head's new key and value from
 // the projected q|k|v (per-head RMSNorm with q_norm / k_norm, rotate-half
@@ -103,11 +110,27 @@ __device__ __forceinline__ float head_rms_scale(float x, uint32_t d, float eps, 
     return 1.0f / sqrtf(total / static_cast<float>(d) + eps);
 }
 
+// Geometry of one attention layer's projected [q (| gate) per head | k | v].
+struct AttendShape {
+    uint32_t qh, kvh, d;       // query heads, KV heads, head dimension (<= kAttendMaxDim)
+    uint32_t q_stride;         // floats per query head in the projection: d, or 2 d with a gate
+    uint32_t gated;            // Qwen3.5: out *= sigmoid(gate), gate = the head's second d floats
+    uint32_t rh;               // rotary half: dimensions [0, 2 rh) rotate (rh = d / 2: all)
+    uint32_t window;
+    float eps, scale;
+};
+
+__device__ __forceinline__ float sigmoid_signed(float v) {
+    if (v >= 0.0f) return 1.0f / (1.0f + expf(-v));
+    const float e = expf(v);
+    return e / (1.0f + e);
+}
+
 __global__ void __launch_bounds__(kAttendThreads)
 attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
-              float eps, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
-              __half* __restrict__ kc, __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, uint32_t window,
-              uint32_t qh, uint32_t kvh, uint32_t d, float scale, float* __restrict__ out) {
+              const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, __half* __restrict__ kc,
+              __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, const AttendShape sh,
+              float* __restrict__ out) {
     extern __shared__ float sc[];
     __shared__ float red[32];
     __shared__ __align__(16) float qs[kAttendMaxDim];
@@ -115,6 +138,7 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     __shared__ __align__(16) float knew[kAttendMaxDim];
     __shared__ __align__(16) float vnew[kAttendMaxDim];
     __shared__ __align__(16) float part[kAttendThreads / 32][kAttendMaxDim];
+    const uint32_t d = sh.d, window = sh.window, qh = sh.qh, kvh = sh.kvh, rh = sh.rh;
     // The position counter changes only at the end of a token step, so it and
     // the cached keys and values of earlier positions are read before waiting
     // for the Q/K/V projection: the first CTA of each query group pulls its
@@ -135,11 +159,12 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     }
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t kbase = qh * sh.q_stride, vbase = kbase + kvh * d;
     const bool dim = t < d;
-    const float xq = dim ? qkv[h * d + t] : 0.0f;
-    const float xk = dim ? qkv[(qh + kh) * d + t] : 0.0f;
-    const float sq = head_rms_scale(xq, d, eps, red);
-    const float sk = head_rms_scale(xk, d, eps, red);
+    const float xq = dim ? qkv[h * sh.q_stride + t] : 0.0f;
+    const float xk = dim ? qkv[kbase + kh * d + t] : 0.0f;
+    const float sq = head_rms_scale(xq, d, sh.eps, red);
+    const float sk = head_rms_scale(xk, d, sh.eps, red);
     if (dim) {
         qs[t] = __fmul_rn(__fmul_rn(xq, sq), q_norm[t]);
         kn[t] = __fmul_rn(__fmul_rn(xk, sk), k_norm[t]);
@@ -147,17 +172,22 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     __syncthreads();
     float rq = 0.0f, rk = 0.0f;
     if (dim) {
-        const uint32_t half = d / 2, j = t < half ? t : t - half;
-        const float c = rope_cos[static_cast<uint64_t>(pos) * half + j], s = rope_sin[static_cast<uint64_t>(pos) * half + j];
-        const float aq = qs[j], bq = qs[j + half], ak = kn[j], bk = kn[j + half];
-        rq = t < half ? __fsub_rn(__fmul_rn(aq, c), __fmul_rn(bq, s)) : __fadd_rn(__fmul_rn(bq, c), __fmul_rn(aq, s));
-        rk = t < half ? __fsub_rn(__fmul_rn(ak, c), __fmul_rn(bk, s)) : __fadd_rn(__fmul_rn(bk, c), __fmul_rn(ak, s));
+        if (t < 2u * rh) {
+            const uint32_t j = t < rh ? t : t - rh;
+            const float c = rope_cos[static_cast<uint64_t>(pos) * rh + j], s = rope_sin[static_cast<uint64_t>(pos) * rh + j];
+            const float aq = qs[j], bq = qs[j + rh], ak = kn[j], bk = kn[j + rh];
+            rq = t < rh ? __fsub_rn(__fmul_rn(aq, c), __fmul_rn(bq, s)) : __fadd_rn(__fmul_rn(bq, c), __fmul_rn(aq, s));
+            rk = t < rh ? __fsub_rn(__fmul_rn(ak, c), __fmul_rn(bk, s)) : __fadd_rn(__fmul_rn(bk, c), __fmul_rn(ak, s));
+        } else {
+            rq = qs[t];
+            rk = kn[t];
+        }
     }
     __syncthreads();
     if (dim) {
         qs[t] = rq;
         const __half hk = __float2half_rn(rk);
-        const __half hv = __float2half_rn(qkv[(qh + kvh + kh) * d + t]);
+        const __half hv = __float2half_rn(qkv[vbase + kh * d + t]);
         knew[t] = __half2float(hk);
         vnew[t] = __half2float(hv);
         if (h % group == 0) {
@@ -168,32 +198,35 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     }
     __syncthreads();
     const uint32_t units = d / 8;                         // 16-byte units of a key row
+    constexpr uint32_t kChunk = 16;                       // units loaded at once (128 dimensions)
     for (uint32_t j0 = 0; j0 < n; j0 += kAttendThreads) {
         const uint32_t j = j0 + t;
         if (j + 1 == n) {
             float dot = 0.0f;
             for (uint32_t e = 0; e < d; ++e) dot = fmaf(qs[e], knew[e], dot);
-            sc[j] = dot * scale;
+            sc[j] = dot * sh.scale;
         } else if (j < n) {
             const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + j) % window) * row_stride + kh * d);
-            uint4 kv[kAttendMaxDim / 8];
-#pragma unroll
-            for (uint32_t u = 0; u < kAttendMaxDim / 8; ++u)
-                if (u < units) kv[u] = __ldg(k + u);
             float dot = 0.0f;
+            for (uint32_t c0 = 0; c0 < units; c0 += kChunk) {
+                uint4 kv[kChunk];
 #pragma unroll
-            for (uint32_t u = 0; u < kAttendMaxDim / 8; ++u) {
-                if (u < units) {
-                    const __half2* hp = reinterpret_cast<const __half2*>(&kv[u]);
+                for (uint32_t u = 0; u < kChunk; ++u)
+                    if (c0 + u < units) kv[u] = __ldg(k + c0 + u);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = __half22float2(hp[e]);
-                        dot = fmaf(qs[u * 8 + 2 * e], f.x, dot);
-                        dot = fmaf(qs[u * 8 + 2 * e + 1], f.y, dot);
+                for (uint32_t u = 0; u < kChunk; ++u) {
+                    if (c0 + u < units) {
+                        const __half2* hp = reinterpret_cast<const __half2*>(&kv[u]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = __half22float2(hp[e]);
+                            dot = fmaf(qs[(c0 + u) * 8 + 2 * e], f.x, dot);
+                            dot = fmaf(qs[(c0 + u) * 8 + 2 * e + 1], f.y, dot);
+                        }
                     }
                 }
             }
-            sc[j] = dot * scale;
+            sc[j] = dot * sh.scale;
         }
     }
     __syncthreads();
@@ -207,42 +240,48 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
         den += e;
     }
     den = block_reduce_all(den, red, [](float a, float b) { return a + b; });
-    // Output: lane covers dimensions 4 lane .. 4 lane + 3 (d / 4 lanes active).
-    const bool active = static_cast<uint32_t>(lane) * 4u < d;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (uint32_t j0 = warp; j0 < n; j0 += 8u * kW) {
-        uint2 vv[8];
+    // Output: in segment g (dimensions 128 g .. 128 g + 127) lane covers
+    // dimensions 128 g + 4 lane .. + 3.
+    for (uint32_t g0 = 0; g0 < d; g0 += 128u) {
+        const bool active = g0 + static_cast<uint32_t>(lane) * 4u < d;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t j0 = warp; j0 < n; j0 += 8u * kW) {
+            uint2 vv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint32_t j = j0 + u * kW;
-            if (active && j + 1 < n)
-                vv[u] = __ldg(reinterpret_cast<const uint2*>(vc + ((first + j) % window) * row_stride + kh * d) + lane);
-        }
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t j = j0 + u * kW;
+                if (active && j + 1 < n)
+                    vv[u] = __ldg(reinterpret_cast<const uint2*>(vc + ((first + j) % window) * row_stride + kh * d + g0) +
+                                  lane);
+            }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint32_t j = j0 + u * kW;
-            if (active && j < n) {
-                const float p = sc[j] / den;
-                float2 a, b;
-                if (j + 1 == n) {
-                    a = make_float2(vnew[lane * 4], vnew[lane * 4 + 1]);
-                    b = make_float2(vnew[lane * 4 + 2], vnew[lane * 4 + 3]);
-                } else {
-                    a = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].x));
-                    b = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].y));
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t j = j0 + u * kW;
+                if (active && j < n) {
+                    const float p = sc[j] / den;
+                    float2 a, b;
+                    if (j + 1 == n) {
+                        a = make_float2(vnew[g0 + lane * 4], vnew[g0 + lane * 4 + 1]);
+                        b = make_float2(vnew[g0 + lane * 4 + 2], vnew[g0 + lane * 4 + 3]);
+                    } else {
+                        a = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].x));
+                        b = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].y));
+                    }
+                    acc.x = fmaf(p, a.x, acc.x);
+                    acc.y = fmaf(p, a.y, acc.y);
+                    acc.z = fmaf(p, b.x, acc.z);
+                    acc.w = fmaf(p, b.y, acc.w);
                 }
-                acc.x = fmaf(p, a.x, acc.x);
-                acc.y = fmaf(p, a.y, acc.y);
-                acc.z = fmaf(p, b.x, acc.z);
-                acc.w = fmaf(p, b.y, acc.w);
             }
         }
+        if (active) *reinterpret_cast<float4*>(&part[warp][g0 + lane * 4]) = acc;
     }
-    if (active) *reinterpret_cast<float4*>(&part[warp][lane * 4]) = acc;
     __syncthreads();
     if (t < d) {
         float o = part[0][t];
         for (int w = 1; w < kW; ++w) o += part[w][t];
+        // qwen35_runner.cpp:577-580: the gated output attended * sigmoid(gate).
+        if (sh.gated) o = __fmul_rn(o, sigmoid_signed(qkv[h * sh.q_stride + d + t]));
         out[h * d + t] = o;
     }
 }
@@ -367,18 +406,41 @@ class Decoder {
 public:
     explicit Decoder(const pokit_cuda_decoder_config& c) : cfg_(c) {
         const size_t d = c.head_dim;
-        if (c.layers == 0 || c.hidden == 0 || c.hidden % 256 || c.vocab == 0 || c.vocab > 0xffffffffu ||
-            c.q_heads == 0 || c.kv_heads == 0 || c.q_heads % c.kv_heads || d == 0 || d % 32 || d > kAttendMaxDim ||
-            c.context == 0 || c.context > (1u << 24) || c.eos_token >= c.vocab || !(c.rope_theta > 0.0f) ||
-            !(c.rms_epsilon > 0.0f) || (c.q_heads * d) % 256)
+        hybrid_ = c.arch == POKIT_CUDA_ARCH_QWEN35MOE;
+        if (c.arch > POKIT_CUDA_ARCH_QWEN35MOE || c.layers == 0 || c.hidden == 0 || c.hidden % 256 || c.vocab == 0 ||
+            c.vocab > 0xffffffffu || c.q_heads == 0 || c.kv_heads == 0 || c.q_heads % c.kv_heads || d == 0 ||
+            d % 32 || d > kAttendMaxDim || c.context == 0 || c.context > (1u << 24) || c.eos_token >= c.vocab ||
+            !(c.rope_theta > 0.0f) || !(c.rms_epsilon > 0.0f) || (c.q_heads * d) % 256)
             throw std::invalid_argument("invalid decoder configuration");
         if (!decoder_type(c.attn_type) || c.attn_type == kF32 || !decoder_type(c.embed_type) ||
             !decoder_type(c.output_type))
             throw std::invalid_argument("unsupported decoder tensor type");
+        rh_ = d / 2;
+        if (hybrid_) {
+            // Qwen35Index::load_config and Qwen35Runner::Impl checks
+            // (src/qwen35_index.cpp:205-220, src/qwen35_runner.cpp:425-434).
+            uint64_t sections = 0;
+            for (uint32_t v : c.rope_sections) sections += v;
+            if (c.rotary_dim == 0 || c.rotary_dim % 2 || c.rotary_dim > d || sections == 0 ||
+                sections > c.rotary_dim / 2 || c.full_attention_interval == 0 ||
+                c.full_attention_interval > c.layers || c.ssm_conv_kernel == 0 || c.ssm_conv_kernel > 64 ||
+                c.ssm_state_size == 0 || c.ssm_state_size % 32 || c.ssm_state_size > 256 || c.ssm_group_count == 0 ||
+                c.ssm_time_step_rank == 0 || c.ssm_time_step_rank % c.ssm_group_count ||
+                c.ssm_inner_size % c.ssm_time_step_rank || c.ssm_inner_size % 256 ||
+                c.ssm_inner_size / c.ssm_time_step_rank > 256 || !(c.expert_weights_scale >= 0.0f) ||
+                (c.shared_inter && !decoder_type(c.shared_type)))
+                throw std::invalid_argument("invalid Qwen3.5 hybrid configuration");
+            rh_ = c.rotary_dim / 2;
+            kw_ = c.ssm_group_count * c.ssm_state_size;
+            vw_ = c.ssm_inner_size;
+            hv_ = c.ssm_time_step_rank;
+            conv_ch_ = 2 * kw_ + vw_;
+        }
         window_ = c.kv_window ? c.kv_window : std::min<size_t>(c.context, 512);
         if (window_ > c.context || window_ > kMaxWindow) throw std::invalid_argument("invalid KV window");
         qd_ = c.q_heads * d;
         kd_ = c.kv_heads * d;
+        qrows_ = hybrid_ ? 2 * qd_ : qd_;
         pokit_cuda_moe_config mc{};
         mc.device = c.device;
         mc.layers = c.layers;
@@ -386,12 +448,14 @@ public:
         mc.inter = c.expert_inter;
         mc.experts = c.experts;
         mc.top_k = c.top_k;
-        mc.flavour = POKIT_CUDA_MOE_QWEN3;
+        mc.flavour = hybrid_ ? POKIT_CUDA_MOE_QWEN35 : POKIT_CUDA_MOE_QWEN3;
         mc.normalize_top_k = c.normalize_top_k;
-        mc.expert_weights_scale = 1.0f;
+        mc.expert_weights_scale = hybrid_ ? c.expert_weights_scale : 1.0f;
         mc.rms_epsilon = c.rms_epsilon;
         mc.gate_type = mc.up_type = mc.down_type = c.expert_type;
-        mc.shared_gate_type = mc.shared_up_type = mc.shared_down_type = kQ8_0;
+        mc.layer_down_types = hybrid_ ? c.layer_down_types : nullptr;
+        mc.shared_inter = hybrid_ ? c.shared_inter : 0;
+        mc.shared_gate_type = mc.shared_up_type = mc.shared_down_type = hybrid_ && c.shared_inter ? c.shared_type : kQ8_0;
         char err[512];
         const pokit_cuda_status st = pokit_cuda_moe_create(&mc, &moe_, err, sizeof err);
         if (st == POKIT_CUDA_STATUS_INVALID_ARGUMENT) throw std::invalid_argument(err);
@@ -416,6 +480,10 @@ public:
     std::mutex& mutex() { return mutex_; }
     pokit_cuda_moe* moe() { return moe_; }
 
+    // Layer l is full attention (Qwen3.5Config::is_full_attention_layer,
+    // src/qwen35_index.cpp:230-233); every Qwen3-MoE layer is.
+    bool attention_layer(size_t l) const { return !hybrid_ || (l + 1) % cfg_.full_attention_interval == 0; }
+
     uint64_t tensor_bytes(size_t layer, uint32_t t) const {
         const uint64_t H = cfg_.hidden, d = cfg_.head_dim;
         switch (t) {
@@ -425,14 +493,27 @@ public:
             default: break;
         }
         if (layer >= cfg_.layers) return 0;
+        if (t == POKIT_CUDA_DEC_ATTN_NORM) return H * 4;
+        const uint64_t rb = row_bytes(cfg_.attn_type, H);
+        if (attention_layer(layer)) {
+            switch (t) {
+                case POKIT_CUDA_DEC_ATTN_Q: return qrows_ * rb;
+                case POKIT_CUDA_DEC_ATTN_Q_NORM: return d * 4;
+                case POKIT_CUDA_DEC_ATTN_K: return kd_ * rb;
+                case POKIT_CUDA_DEC_ATTN_K_NORM: return d * 4;
+                case POKIT_CUDA_DEC_ATTN_V: return kd_ * rb;
+                case POKIT_CUDA_DEC_ATTN_OUTPUT: return H * row_bytes(cfg_.attn_type, qd_);
+                default: return 0;
+            }
+        }
         switch (t) {
-            case POKIT_CUDA_DEC_ATTN_NORM: return H * 4;
-            case POKIT_CUDA_DEC_ATTN_Q: return qd_ * row_bytes(cfg_.attn_type, H);
-            case POKIT_CUDA_DEC_ATTN_Q_NORM: return d * 4;
-            case POKIT_CUDA_DEC_ATTN_K: return kd_ * row_bytes(cfg_.attn_type, H);
-            case POKIT_CUDA_DEC_ATTN_K_NORM: return d * 4;
-            case POKIT_CUDA_DEC_ATTN_V: return kd_ * row_bytes(cfg_.attn_type, H);
-            case POKIT_CUDA_DEC_ATTN_OUTPUT: return H * row_bytes(cfg_.attn_type, qd_);
+            case POKIT_CUDA_DEC_SSM_QKV: return conv_ch_ * rb;
+            case POKIT_CUDA_DEC_SSM_GATE: return vw_ * rb;
+            case POKIT_CUDA_DEC_SSM_ALPHA: case POKIT_CUDA_DEC_SSM_BETA: return hv_ * rb;
+            case POKIT_CUDA_DEC_SSM_CONV1D: return conv_ch_ * cfg_.ssm_conv_kernel * 4;
+            case POKIT_CUDA_DEC_SSM_A: case POKIT_CUDA_DEC_SSM_DT_BIAS: return hv_ * 4;
+            case POKIT_CUDA_DEC_SSM_NORM: return (vw_ / hv_) * 4;
+            case POKIT_CUDA_DEC_SSM_OUT: return H * row_bytes(cfg_.attn_type, vw_);
             default: return 0;
         }
     }
@@ -460,7 +541,7 @@ public:
     void reset() {
         ensure_ok();
         Scope scope(cfg_.device);
-        guard(cudaMemsetAsync(pos_, 0, 4, stream_), "reset");
+        clear_state();
         guard(cudaStreamSynchronize(stream_), "reset");
         next_position_ = 0;
     }
@@ -497,7 +578,7 @@ public:
         if (stats) *stats = {};
         if (n_out) *n_out = 0;
         const auto t0 = std::chrono::steady_clock::now();
-        guard(cudaMemsetAsync(pos_, 0, 4, stream_), "reset");
+        clear_state();
         next_position_ = 0;
         for (size_t i = 0; i < n;) {
             const size_t m = std::min(n - i, kPinnedIds);
@@ -515,11 +596,14 @@ public:
         // device and the host reads the chunk's tokens once, to find the end
         // token.  Forwards past the end token are harmless while the KV ring has
         // not wrapped (they write slots no later position reads before it is
-        // rewritten); after that, one token per round trip.
+        // rewritten) and no layer is recurrent; otherwise one token per round
+        // trip.
         size_t produced = 0, forwarded = 0;
         bool ended = false;
         while (produced < max_new && !ended) {
-            const bool wrapped = n + produced + 16 >= window_;
+            // A recurrent (DeltaNet) state would absorb forwards past the end
+            // token: the hybrid forwards exactly the reference's tokens.
+            const bool wrapped = hybrid_ || n + produced + 16 >= window_;
             const size_t chunk = wrapped ? 1 : std::min<size_t>(max_new - produced, 16);
             const size_t last = produced + chunk - 1;
             for (; forwarded < last; ++forwarded) step(true);
@@ -597,56 +681,95 @@ private:
             case POKIT_CUDA_DEC_TOKEN_EMBD: return cfg_.embed_type;
             case POKIT_CUDA_DEC_OUTPUT: return cfg_.output_type;
             case POKIT_CUDA_DEC_ATTN_Q: case POKIT_CUDA_DEC_ATTN_K: case POKIT_CUDA_DEC_ATTN_V:
-            case POKIT_CUDA_DEC_ATTN_OUTPUT: return cfg_.attn_type;
+            case POKIT_CUDA_DEC_ATTN_OUTPUT: case POKIT_CUDA_DEC_SSM_QKV: case POKIT_CUDA_DEC_SSM_GATE:
+            case POKIT_CUDA_DEC_SSM_ALPHA: case POKIT_CUDA_DEC_SSM_BETA: case POKIT_CUDA_DEC_SSM_OUT:
+                return cfg_.attn_type;
             default: return kF32;
         }
     }
 
     uint8_t* tensor_ptr(size_t layer, uint32_t t) const {
-        if (t > POKIT_CUDA_DEC_ATTN_OUTPUT || tensor_bytes(layer, t) == 0) return nullptr;
+        if (t >= kTensors || tensor_bytes(layer, t) == 0) return nullptr;
         if (t <= POKIT_CUDA_DEC_OUTPUT) return pool_ + global_off_[t];
-        return pool_ + layer_off_[layer] + local_off_[t - POKIT_CUDA_DEC_ATTN_NORM];
+        return pool_ + off_[layer * kTensors + t];
     }
 
     void allocate() {
-        // Pool: embedding, output norm, LM head, then per layer attn_norm,
-        // q, k, v (contiguous rows: one matvec), o, q_norm, k_norm.
+        // Pool: embedding, output norm, LM head, then per layer attn_norm and
+        // the projections of one normed input as contiguous rows (one
+        // matvec): attention layers [q | k | v], o, q_norm, k_norm; DeltaNet
+        // layers [qkv | gate | alpha | beta], ssm_out, conv1d, ssm_a, dt_bias,
+        // ssm_norm.
         uint64_t off = 0;
         for (uint32_t t = 0; t <= POKIT_CUDA_DEC_OUTPUT; ++t) {
             global_off_[t] = off;
             off += align256(tensor_bytes(0, t));
         }
-        const uint64_t rb = row_bytes(cfg_.attn_type, cfg_.hidden);
-        uint64_t lo = 0;
-        const auto place = [&](uint32_t t, uint64_t bytes, bool pad) {
-            local_off_[t - POKIT_CUDA_DEC_ATTN_NORM] = lo;
-            lo += pad ? align256(bytes) : bytes;
-        };
-        place(POKIT_CUDA_DEC_ATTN_NORM, cfg_.hidden * 4, true);
-        place(POKIT_CUDA_DEC_ATTN_Q, qd_ * rb, false);
-        place(POKIT_CUDA_DEC_ATTN_K, kd_ * rb, false);
-        place(POKIT_CUDA_DEC_ATTN_V, kd_ * rb, true);
-        place(POKIT_CUDA_DEC_ATTN_OUTPUT, cfg_.hidden * row_bytes(cfg_.attn_type, qd_), true);
-        place(POKIT_CUDA_DEC_ATTN_Q_NORM, cfg_.head_dim * 4, true);
-        place(POKIT_CUDA_DEC_ATTN_K_NORM, cfg_.head_dim * 4, true);
-        layer_off_.resize(cfg_.layers);
+        off_.assign(cfg_.layers * kTensors, 0);
         for (size_t l = 0; l < cfg_.layers; ++l) {
-            layer_off_[l] = off;
-            off += lo;
+            const auto place = [&](uint32_t t, bool pad) {
+                off_[l * kTensors + t] = off;
+                off += pad ? align256(tensor_bytes(l, t)) : tensor_bytes(l, t);
+            };
+            place(POKIT_CUDA_DEC_ATTN_NORM, true);
+            if (attention_layer(l)) {
+                place(POKIT_CUDA_DEC_ATTN_Q, false);
+                place(POKIT_CUDA_DEC_ATTN_K, false);
+                place(POKIT_CUDA_DEC_ATTN_V, true);
+                place(POKIT_CUDA_DEC_ATTN_OUTPUT, true);
+                place(POKIT_CUDA_DEC_ATTN_Q_NORM, true);
+                place(POKIT_CUDA_DEC_ATTN_K_NORM, true);
+            } else {
+                place(POKIT_CUDA_DEC_SSM_QKV, false);
+                place(POKIT_CUDA_DEC_SSM_GATE, false);
+                place(POKIT_CUDA_DEC_SSM_ALPHA, false);
+                place(POKIT_CUDA_DEC_SSM_BETA, true);
+                place(POKIT_CUDA_DEC_SSM_OUT, true);
+                place(POKIT_CUDA_DEC_SSM_CONV1D, true);
+                place(POKIT_CUDA_DEC_SSM_A, true);
+                place(POKIT_CUDA_DEC_SSM_DT_BIAS, true);
+                place(POKIT_CUDA_DEC_SSM_NORM, true);
+            }
         }
         check(cudaMalloc(&pool_, off), "cudaMalloc(decoder pool)");
         check(cudaMemset(pool_, 0, off), "cudaMemset(decoder pool)");
         const uint64_t kv = static_cast<uint64_t>(cfg_.layers) * window_ * kd_ * sizeof(__half);
         check(cudaMalloc(&kcache_, kv), "cudaMalloc(K cache)");
         check(cudaMalloc(&vcache_, kv), "cudaMalloc(V cache)");
-        const size_t half = cfg_.head_dim / 2;
+        // Convolution and recurrent states of the DeltaNet layers.
+        if (hybrid_) {
+            const uint64_t conv = align256(conv_ch_ * (cfg_.ssm_conv_kernel - 1) * 4);
+            const uint64_t rec = align256(hv_ * cfg_.ssm_state_size * (vw_ / hv_) * 4);
+            ssm_off_.assign(cfg_.layers, 0);
+            uint64_t so = 0;
+            for (size_t l = 0; l < cfg_.layers; ++l)
+                if (!attention_layer(l)) {
+                    ssm_off_[l] = so;
+                    so += conv + rec;
+                }
+            ssm_conv_bytes_ = conv;
+            ssm_bytes_ = so;
+            if (so) {
+                check(cudaMalloc(&ssm_, so), "cudaMalloc(DeltaNet states)");
+                check(cudaMemset(ssm_, 0, so), "cudaMemset(DeltaNet states)");
+            }
+        }
+        // RoPE tables [context][rotary half], the reference's float arithmetic:
+        // angle = position * theta^(-pair / half) (qwen3_moe_runner.cpp:141-156);
+        // Qwen3.5 text positions leave the pairs of the fourth MRoPE section at
+        // position 0 (prepare_rope, qwen35_runner.cpp:69-92).
+        const size_t half = rh_;
+        uint64_t section_total = 0, three = 0;
+        if (hybrid_) {
+            for (uint32_t v : cfg_.rope_sections) section_total += v;
+            three = uint64_t(cfg_.rope_sections[0]) + cfg_.rope_sections[1] + cfg_.rope_sections[2];
+        }
         std::vector<float> cs(cfg_.context * half), sn(cfg_.context * half);
-        // The reference's table (qwen3_moe_runner.cpp:141-156), in its float
-        // arithmetic: angle = position * theta^(-pair / half).
         for (size_t p = 0; p < cfg_.context; ++p)
             for (size_t i = 0; i < half; ++i) {
-                const float angle = static_cast<float>(p) *
-                    std::pow(cfg_.rope_theta, -static_cast<float>(i) / static_cast<float>(half));
+                const bool extra = hybrid_ && (i % section_total) >= three;
+                const float at = extra ? 0.0f : static_cast<float>(p);
+                const float angle = at * std::pow(cfg_.rope_theta, -static_cast<float>(i) / static_cast<float>(half));
                 cs[p * half + i] = std::cos(angle);
                 sn[p * half + i] = std::sin(angle);
             }
@@ -654,15 +777,15 @@ private:
         check(cudaMemcpy(rope_, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope");
         check(cudaMemcpy(rope_ + cs.size(), sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope");
         const uint64_t H = cfg_.hidden;
-        const uint64_t fl = align256(H * 4) * 2 + align256((qd_ + 2 * kd_) * 4) + align256(qd_ * 4) * 2 +
-                            align256(cfg_.vocab * 4);
+        const uint64_t proj = std::max<uint64_t>(qrows_ + 2 * kd_, hybrid_ ? conv_ch_ + vw_ + 2 * hv_ : 0);
+        const uint64_t mix = std::max<uint64_t>(qd_, vw_);
+        const uint64_t fl = align256(H * 4) * 2 + align256(proj * 4) + align256(mix * 4) + align256(cfg_.vocab * 4);
         check(cudaMalloc(&work_, fl), "cudaMalloc(decoder work)");
         uint8_t* w = static_cast<uint8_t*>(work_);
         hidden_ = reinterpret_cast<float*>(w); w += align256(H * 4);
         xn_ = reinterpret_cast<float*>(w); w += align256(H * 4);
-        qkv_ = reinterpret_cast<float*>(w); w += align256((qd_ + 2 * kd_) * 4);
-        q_ = reinterpret_cast<float*>(w); w += align256(qd_ * 4);
-        att_ = reinterpret_cast<float*>(w); w += align256(qd_ * 4);
+        qkv_ = reinterpret_cast<float*>(w); w += align256(proj * 4);
+        att_ = reinterpret_cast<float*>(w); w += align256(mix * 4);
         logits_ = reinterpret_cast<float*>(w);
         const size_t seq_words = cfg_.context + 1 + 32 + 32 + 32 + 2 * kArgmaxCtas;
         check(cudaMalloc(&seq_, seq_words * 4), "cudaMalloc(sequence)");
@@ -676,10 +799,15 @@ private:
         check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
         check(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
         check(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming), "cudaEventCreate");
-        const size_t attend_smem = window_ * 4;
-        if (attend_smem > 48u * 1024u)
-            check(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(attend_smem)), "attend smem");
+        check(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(window_ * 4)), "attend smem");
+    }
+
+    // Position 0 and zero DeltaNet states (the KV ring needs no clearing:
+    // attention reads only positions written since).
+    void clear_state() {
+        guard(cudaMemsetAsync(pos_, 0, 4, stream_), "reset");
+        if (ssm_) guard(cudaMemsetAsync(ssm_, 0, ssm_bytes_, stream_), "reset");
     }
 
     void release() {
@@ -693,6 +821,7 @@ private:
         if (rope_) cudaFree(rope_);
         if (vcache_) cudaFree(vcache_);
         if (kcache_) cudaFree(kcache_);
+        if (ssm_) cudaFree(ssm_);
         if (pool_) cudaFree(pool_);
         if (moe_) pokit_cuda_moe_destroy(moe_);
         moe_ = nullptr;
@@ -714,40 +843,84 @@ private:
     cudaError_t enqueue(bool logits, cudaStream_t s, uint64_t* launches) {
         const uint32_t H = static_cast<uint32_t>(cfg_.hidden), d = static_cast<uint32_t>(cfg_.head_dim);
         const uint32_t qh = static_cast<uint32_t>(cfg_.q_heads), kvh = static_cast<uint32_t>(cfg_.kv_heads);
-        const uint32_t win = static_cast<uint32_t>(window_), half = d / 2;
+        const uint32_t win = static_cast<uint32_t>(window_);
         const float eps = cfg_.rms_epsilon, scale = 1.0f / std::sqrt(static_cast<float>(d));
+        AttendShape ash{};
+        ash.qh = qh;
+        ash.kvh = kvh;
+        ash.d = d;
+        ash.q_stride = hybrid_ ? 2u * d : d;
+        ash.gated = hybrid_ ? 1u : 0u;
+        ash.rh = static_cast<uint32_t>(rh_);
+        ash.window = win;
+        ash.eps = eps;
+        ash.scale = scale;
+        pokit_cuda_delta_net_shape dsh{};
+        dsh.key_heads = cfg_.ssm_group_count;
+        dsh.value_heads = hv_;
+        dsh.key_dim = cfg_.ssm_state_size;
+        dsh.value_dim = hv_ ? vw_ / hv_ : 0;
+        dsh.conv_kernel = cfg_.ssm_conv_kernel;
+        dsh.rms_epsilon = eps;
         uint64_t n = 0;
         cudaError_t e = embed(s);
         ++n;
         for (size_t l = 0; l < cfg_.layers && e == cudaSuccess; ++l) {
             const auto P = [&](uint32_t t) { return tensor_ptr(l, t); };
-            const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
-            e = launch_linear_normed(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_Q), static_cast<uint32_t>(qd_ + 2 * kd_), H,
-                                     hidden_, reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_NORM)), eps, qkv_, s,
-                                     pdl_);
-            if (e != cudaSuccess) break;
-            const float* qn = reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_Q_NORM));
-            const float* kn = reinterpret_cast<const float*>(P(POKIT_CUDA_DEC_ATTN_K_NORM));
-            if (pdl_) {
-                e = launch_dependent(attend_kernel, qh, kAttendThreads, win * 4, s, qkv_, qn, kn, eps, rope_,
-                                     rope_ + cfg_.context * half, kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh,
-                                     kvh, d, scale, att_);
+            const auto F = [&](uint32_t t) { return reinterpret_cast<const float*>(tensor_ptr(l, t)); };
+            if (attention_layer(l)) {
+                const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
+                e = launch_linear_normed(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_Q), static_cast<uint32_t>(qrows_ + 2 * kd_),
+                                         H, hidden_, F(POKIT_CUDA_DEC_ATTN_NORM), eps, qkv_, s, pdl_);
                 if (e != cudaSuccess) break;
+                const float* qn = F(POKIT_CUDA_DEC_ATTN_Q_NORM);
+                const float* kn = F(POKIT_CUDA_DEC_ATTN_K_NORM);
+                const float* rc = rope_;
+                const float* rs = rope_ + cfg_.context * rh_;
+                if (pdl_) {
+                    e = launch_dependent(attend_kernel, qh, kAttendThreads, win * 4, s, qkv_, qn, kn, rc, rs,
+                                         kcache_ + kv_off, vcache_ + kv_off, pos_, ash, att_);
+                    if (e != cudaSuccess) break;
+                } else {
+                    attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(qkv_, qn, kn, rc, rs, kcache_ + kv_off,
+                                                                      vcache_ + kv_off, pos_, ash, att_);
+                }
+                e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
+                                  hidden_, s, false, true, pdl_);
+                n += 3;
             } else {
-                attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(qkv_, qn, kn, eps, rope_, rope_ + cfg_.context * half,
-                                                                  kcache_ + kv_off, vcache_ + kv_off, pos_, win, qh,
-                                                                  kvh, d, scale, att_);
+                // Gated DeltaNet (qwen35_runner.cpp:582-627): one matvec over
+                // [qkv | gate | alpha | beta], the conv1d + delta-rule step, ssm_out.
+                e = launch_linear_normed(cfg_.attn_type, P(POKIT_CUDA_DEC_SSM_QKV),
+                                         static_cast<uint32_t>(conv_ch_ + vw_ + 2 * hv_), H, hidden_,
+                                         F(POKIT_CUDA_DEC_ATTN_NORM), eps, qkv_, s, pdl_);
+                if (e != cudaSuccess) break;
+                uint8_t* st = ssm_ + ssm_off_[l];
+                float* gate = qkv_ + conv_ch_;
+                float* alpha = gate + vw_;
+                float* beta = alpha + hv_;
+                char derr[256];
+                const pokit_cuda_status ds = pokit_cuda_delta_net_step(
+                    &dsh, qkv_, gate, alpha, beta, F(POKIT_CUDA_DEC_SSM_CONV1D), reinterpret_cast<float*>(st),
+                    F(POKIT_CUDA_DEC_SSM_A), F(POKIT_CUDA_DEC_SSM_DT_BIAS), F(POKIT_CUDA_DEC_SSM_NORM),
+                    reinterpret_cast<float*>(st + ssm_conv_bytes_), att_, status_ + 1, s, derr, sizeof derr);
+                if (ds != POKIT_CUDA_STATUS_OK) return ds == POKIT_CUDA_STATUS_INVALID_ARGUMENT ? cudaErrorInvalidValue
+                                                                                                : cudaErrorUnknown;
+                e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_SSM_OUT), H, static_cast<uint32_t>(vw_), att_,
+                                  hidden_, s, false, true, false);
+                n += 4;
             }
-            e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
-                              hidden_, s, false, true, pdl_);
             if (e != cudaSuccess) break;
             char err[256];
+            pokit_cuda_moe_stats before{}, after{};
+            pokit_cuda_moe_get_stats(moe_, &before);
             const pokit_cuda_status st = pokit_cuda_moe_decode_layers(moe_, l, 1, hidden_, s, err, sizeof err);
             if (st != POKIT_CUDA_STATUS_OK) {
                 moe_error_ = err;
                 return st == POKIT_CUDA_STATUS_INVALID_ARGUMENT ? cudaErrorInvalidValue : cudaErrorUnknown;
             }
-            n += 4;
+            pokit_cuda_moe_get_stats(moe_, &after);
+            n += after.kernel_launches - before.kernel_launches;
             e = cudaGetLastError();
         }
         if (e != cudaSuccess) return e;
@@ -836,37 +1009,43 @@ private:
 
     void sync_and_check() {
         guard(cudaStreamSynchronize(stream_), "synchronize");
-        uint32_t st = 0;
-        guard(cudaMemcpyAsync(pinned_ids_ + kPinnedIds - 1, status_, 4, cudaMemcpyDeviceToHost, stream_), "status");
+        guard(cudaMemcpyAsync(pinned_ids_ + kPinnedIds - 2, status_, 8, cudaMemcpyDeviceToHost, stream_), "status");
         guard(cudaStreamSynchronize(stream_), "status");
-        st = pinned_ids_[kPinnedIds - 1];
+        const uint32_t st = pinned_ids_[kPinnedIds - 2], gates = pinned_ids_[kPinnedIds - 1];
         char err[256];
         if (pokit_cuda_moe_synchronize(moe_, stream_, err, sizeof err) != POKIT_CUDA_STATUS_OK) {
             next_position_ = 0;
             cudaMemsetAsync(pos_, 0, 4, stream_);
             throw std::runtime_error(std::string("MoE block: ") + err);
         }
-        if (st & kStatusDecoderNonFinite) {
-            cudaMemsetAsync(status_, 0, 4, stream_);
+        if ((st & kStatusDecoderNonFinite) || gates) {
+            cudaMemsetAsync(status_, 0, 8, stream_);
             cudaMemsetAsync(pos_, 0, 4, stream_);
+            if (ssm_) cudaMemsetAsync(ssm_, 0, ssm_bytes_, stream_);
             cudaStreamSynchronize(stream_);
             next_position_ = 0;           // the reference resets its state and rethrows
-            throw std::runtime_error("model produced non-finite logits");
+            throw std::runtime_error(gates ? "invalid Gated DeltaNet decay or beta (gated_delta_net.cpp)"
+                                           : "model produced non-finite logits");
         }
     }
 
+    static constexpr uint32_t kTensors = POKIT_CUDA_DEC_SSM_OUT + 1;
     pokit_cuda_decoder_config cfg_;
-    size_t window_ = 0, qd_ = 0, kd_ = 0;
+    bool hybrid_ = false;
+    size_t window_ = 0, qd_ = 0, kd_ = 0, qrows_ = 0, rh_ = 0;
+    size_t kw_ = 0, vw_ = 0, hv_ = 0, conv_ch_ = 0;   // DeltaNet key width, value width, value heads, channels
     pokit_cuda_moe* moe_ = nullptr;
     uint8_t* pool_ = nullptr;
     uint64_t global_off_[3] = {};
-    uint64_t local_off_[7] = {};
-    std::vector<uint64_t> layer_off_;
+    std::vector<uint64_t> off_;      // [layer][tensor] pool offsets
+    uint8_t* ssm_ = nullptr;         // per DeltaNet layer: conv state, then recurrent state
+    std::vector<uint64_t> ssm_off_;
+    uint64_t ssm_conv_bytes_ = 0, ssm_bytes_ = 0;
     __half* kcache_ = nullptr;
     __half* vcache_ = nullptr;
     float* rope_ = nullptr;          // [context][half] cos, then [context][half] sin
     void* work_ = nullptr;
-    float *hidden_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *q_ = nullptr, *att_ = nullptr, *logits_ = nullptr;
+    float *hidden_ = nullptr, *xn_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *logits_ = nullptr;
     uint32_t *seq_ = nullptr, *pos_ = nullptr, *status_ = nullptr, *arrivals_ = nullptr, *part_i_ = nullptr;
     float* part_v_ = nullptr;
     uint32_t* pinned_ids_ = nullptr;

@@ -1,5 +1,5 @@
-"""Golden greedy-decode targets of benchmark configuration 2 from the
-reference's own decoder (test infrastructure; run in a container that has the
+"""Golden greedy-decode targets of benchmark configurations 2 and 3 from the
+reference's own decoders (test infrastructure; run in a container that has the
 PokitLMs checkout).
 
 Writes a reduced-layer synthetic Qwen3-30B-A3B-shaped GGUF (pokitlms_b200.gguf:
@@ -14,7 +14,12 @@ RMS of all of them) in tests/golden/decoder_cfg2_L{layers}.npz.  The GPU test
 synthesises the same weights in HBM from the same seeds, so the 1.2 GB model
 file is never committed or shipped.
 
-    python tests/golden/make_decoder_golden.py [--layers 2] [--keep PATH]
+With --arch qwen35 the model is configuration 3's Qwen3.5-MoE hybrid
+(pokitlms_b200.gguf.Qwen35MoeShape: layer 3 full attention, the others Gated
+DeltaNet; 512 experts top-10 with the Q8_0 shared expert, Q5_K/Q6_K down),
+decoded by Qwen35Runner::generate_tokens, stored as decoder_cfg3_L{layers}.npz.
+
+    python tests/golden/make_decoder_golden.py [--arch qwen3moe|qwen35] [--layers N] [--keep PATH]
 """
 from __future__ import annotations
 
@@ -46,30 +51,34 @@ def logit_sample_positions(vocab: int) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--arch", default="qwen3moe", choices=["qwen3moe", "qwen35"])
+    ap.add_argument("--layers", type=int, default=None, help="default 2 (qwen3moe) or 4 (qwen35)")
     ap.add_argument("--keep", type=Path, default=None, help="keep the GGUF at this path")
     a = ap.parse_args()
+    q35 = a.arch == "qwen35"
+    layers = a.layers or (4 if q35 else 2)
     runner = ROOT / "oracle" / "_ref" / "ref_runner"
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "runner"], check=True)
-    shape = gguf.Qwen3MoeShape(layers=a.layers)
+    shape = gguf.Qwen35MoeShape(layers=layers) if q35 else gguf.Qwen3MoeShape(layers=layers)
     with tempfile.TemporaryDirectory() as tmp:
         model = a.keep or Path(tmp) / "model.gguf"
-        gguf.write_qwen3moe(model, shape)
+        (gguf.write_qwen35moe if q35 else gguf.write_qwen3moe)(model, shape)
         prompt = prompt_ids(shape.vocab)
         (Path(tmp) / "prompt.txt").write_text(" ".join(str(int(t)) for t in prompt))
         logits_file = Path(tmp) / "logits.bin"
-        res = subprocess.run([str(runner), str(model), str(Path(tmp) / "prompt.txt"), str(NEW_TOKENS),
-                              str(logits_file)], capture_output=True, text=True, check=True)
+        res = subprocess.run([str(runner)] + (["--qwen35"] if q35 else []) +
+                             [str(model), str(Path(tmp) / "prompt.txt"), str(NEW_TOKENS), str(logits_file)],
+                             capture_output=True, text=True, check=True)
         out = json.loads(res.stdout.strip().splitlines()[-1])
         logits = np.fromfile(logits_file, dtype=np.float32)
     ids = np.asarray(out["ids"], dtype=np.int64)
     top = np.argsort(-logits.astype(np.float64), kind="stable")[:64]
     pos = logit_sample_positions(shape.vocab)
-    dest = ROOT / "tests" / "golden" / f"decoder_cfg2_L{a.layers}.npz"
+    dest = ROOT / "tests" / "golden" / f"decoder_cfg{3 if q35 else 2}_L{layers}.npz"
     np.savez_compressed(dest, prompt=prompt, ids=ids, top_ids=top, top_logits=logits[top],
                         sample_pos=pos, sample_logits=logits[pos],
                         logits_rms=np.float64(np.sqrt(np.mean(logits.astype(np.float64) ** 2))),
-                        layers=a.layers, decode_ns=out["decode_ns"], generated=out["generated"])
+                        layers=layers, decode_ns=out["decode_ns"], generated=out["generated"])
     print(f"{dest}: {len(ids)} ids, first 16 {ids[:16].tolist()}, distinct {len(set(ids.tolist()))}, "
           f"reference decode {out['generated'] / (out['decode_ns'] * 1e-9):.2f} tokens/s")
 

@@ -94,3 +94,46 @@ def test_reference_runner_loads_the_model(tmp_path):
     assert r.returncode == 0, r.stderr
     out = json.loads(r.stdout.strip().splitlines()[-1])
     assert 1 <= len(out["ids"]) <= 6 and all(0 <= i < TINY.vocab for i in out["ids"])
+
+
+TINY35 = gguf.Qwen35MoeShape(layers=4, hidden=256, q_heads=2, kv_heads=1, head_dim=128, rotary_dim=32,
+                             rope_sections=(6, 5, 5, 0), ssm_state_size=32, ssm_group_count=2,
+                             ssm_time_step_rank=4, ssm_inner_size=256, experts=8, top_k=2, expert_inter=256,
+                             shared_inter=256, vocab=512, context=64)
+
+
+def test_qwen35_writer_layout(tmp_path):
+    path = gguf.write_qwen35moe(tmp_path / "m35.gguf", TINY35)
+    version, meta, tensors, data, raw = _read(path)
+    a = "qwen35moe."
+    assert version == 3 and meta["general.architecture"] == "qwen35moe"
+    assert meta[a + "full_attention_interval"] == 4 and list(meta[a + "rope.dimension_sections"]) == [6, 5, 5, 0]
+    assert meta[a + "ssm.inner_size"] == 256 and meta[a + "expert_shared_feed_forward_length"] == 256
+    names = {t[0]: t for t in tensors}
+    # Layer 3 is full attention (gated query: twice the query rows), 0..2 Gated DeltaNet.
+    assert tuple(names["blk.3.attn_q.weight"][1]) == (256, 2 * 2 * 128) and "blk.3.attn_qkv.weight" not in names
+    assert tuple(names["blk.0.attn_qkv.weight"][1]) == (256, 2 * 2 * 32 + 256) and "blk.0.attn_q.weight" not in names
+    assert tuple(names["blk.0.ssm_conv1d.weight"][1]) == (4, TINY35.conv_channels)
+    assert names["blk.0.ffn_down_exps.weight"][2] == TINY35.down_type(0)
+    assert names["blk.1.ffn_down_exps.weight"][2] == TINY35.down_type(1)
+    for name, dims, t, o in tensors:
+        elems, bb = BLOCK[t]
+        rows = int(np.prod(dims[1:])) if len(dims) > 1 else 1
+        assert data + o + rows * dims[0] // elems * bb <= len(raw)
+    name, dims, t, o = names["blk.2.ssm_out.weight"]
+    want = synth.synth_matrix(t, dims[1], dims[0], TINY35.seed, synth.stream_id(2, gguf.SSM_OUT))
+    assert np.array_equal(np.frombuffer(raw, np.uint8, want.size, data + o), want)
+    name, dims, t, o = names["blk.1.ssm_a"]
+    assert np.array_equal(np.frombuffer(raw, np.float32, dims[0], data + o), gguf.ssm_f32_tensors(TINY35, 1)["a"])
+
+
+@pytest.mark.skipif(not (ROOT / "oracle" / "_ref" / "ref_runner").exists(),
+                    reason="the reference's runner is not built on this machine")
+def test_reference_qwen35_runner_loads_the_model(tmp_path):
+    path = gguf.write_qwen35moe(tmp_path / "m35.gguf", TINY35)
+    (tmp_path / "p.txt").write_text("1 2 3 4 5")
+    r = subprocess.run([str(ROOT / "oracle" / "_ref" / "ref_runner"), "--qwen35", str(path), str(tmp_path / "p.txt"),
+                        "6"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert 1 <= len(out["ids"]) <= 6 and all(0 <= i < TINY35.vocab for i in out["ids"])
