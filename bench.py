@@ -525,17 +525,41 @@ def decoder_token_bytes(shape) -> int:
     return L * (attn + experts + router) + q6(shape.vocab, H) + q6(1, H)
 
 
-def measure_decoder(device: int, stream, new_tokens: int = 128, layers: int = 48) -> dict:
+def decoder35_token_bytes(shape) -> int:
+    """Bytes one Qwen3.5-MoE hybrid token step reads (weights, the DeltaNet
+    states read and written, routed experts as 10 distinct slices)."""
+    from pokitlms_b200._lib import BLOCK
+    H = shape.hidden
+    qd, kd = shape.q_heads * shape.head_dim, shape.kv_heads * shape.head_dim
+    mat = lambda t, rows, cols: rows * (cols // BLOCK[t][0]) * BLOCK[t][1]   # noqa: E731
+    a = shape.attn_type
+    hv, vw, ch = shape.ssm_time_step_rank, shape.ssm_inner_size, shape.conv_channels
+    state = hv * shape.ssm_state_size * (vw // hv) * 4
+    total = mat(shape.output_type, shape.vocab, H) + mat(shape.embed_type, 1, H)
+    for l in range(shape.layers):
+        if shape.attention_layer(l):
+            total += mat(a, 2 * qd + 2 * kd, H) + mat(a, H, qd)
+        else:
+            total += mat(a, ch + vw + 2 * hv, H) + mat(a, H, vw) + ch * shape.ssm_conv_kernel * 4 + 2 * state
+        I, Is = shape.expert_inter, shape.shared_inter
+        total += shape.experts * H * 4 + H * 4
+        total += shape.top_k * (2 * mat(shape.expert_type, I, H) + mat(shape.down_type(l), H, I))
+        total += 2 * mat(shape.shared_type, Is, H) + mat(shape.shared_type, H, Is)
+    return total
+
+
+def measure_decoder(device: int, stream, new_tokens: int = 128, layers: int = 48, hybrid: bool = False) -> dict:
     """Benchmark configuration 2 end to end: the whole synthetic Qwen3-30B-A3B-shaped
     decoder (48 layers, GQA 32/4 x 128, RoPE theta 1e6, FP16 KV ring, MoE 128 experts
     top-8, Q4_K experts and attention, Q6_K embedding and LM head, vocabulary 151,936),
     weights synthesised in HBM from seed 0, greedy decoding of `new_tokens` tokens after a
     32-token uniform-random prompt through pokit_cuda_decoder_generate_tokens (the
-    reference's metric: generated tokens / decode time, host wall clock)."""
+    reference's metric: generated tokens / decode time, host wall clock).  With `hybrid`,
+    configuration 3's Qwen3.5-MoE hybrid (gguf.Qwen35MoeShape) the same way."""
     import torch
     from pokitlms_b200 import backend as B
     from pokitlms_b200 import gguf
-    shape = gguf.Qwen3MoeShape(layers=layers)
+    shape = gguf.Qwen35MoeShape(layers=layers) if hybrid else gguf.Qwen3MoeShape(layers=layers)
     dec = B.CudaDecoder(shape, device=device)
     dec.synthesize_model()
     prompt = np.random.default_rng([0, 0x7072]).integers(0, shape.vocab, 32)
@@ -555,11 +579,15 @@ def measure_decoder(device: int, stream, new_tokens: int = 128, layers: int = 48
     graphs, why = dec.step_graphs()
     dec.close()
     peaks = measured_peaks()
-    tb = decoder_token_bytes(shape)
+    tb = decoder35_token_bytes(shape) if hybrid else decoder_token_bytes(shape)
     gbs = tb / (step_us * 1e-6) / 1e9
+    what = ("benchmark configuration 3 end to end: {n}-layer synthetic Qwen3.5-MoE hybrid (Gated DeltaNet and "
+            "gated full attention 3:1, MoE 512 experts top-10 + Q8_0 shared expert, Q6_K LM head over vocabulary "
+            "151,936), 32-token prompt, greedy decode" if hybrid else
+            "benchmark configuration 2 end to end: {n}-layer synthetic Qwen3-30B-A3B-shaped decoder "
+            "(attention + MoE + Q6_K LM head over vocabulary 151,936), 32-token prompt, greedy decode")
     return {
-        "workload": (f"benchmark configuration 2 end to end: {layers}-layer synthetic Qwen3-30B-A3B-shaped decoder "
-                     "(attention + MoE + Q6_K LM head over vocabulary 151,936), 32-token prompt, greedy decode"),
+        "workload": what.format(n=layers),
         "value": 1e6 / step_us, "unit": "tokens/s", "us_per_token": step_us,
         "e2e": {"value": e2e, "unit": "tokens/s", "generated": int(st["generated_tokens"]),
                 "how": "pokit_cuda_decoder_generate_tokens: generated tokens / decode time (host clock), "
@@ -846,8 +874,10 @@ def main() -> None:
     ap.add_argument("--ep-combine", default="nccl", choices=["peer", "nccl"],
                     help="N > 1: sum the shards' outputs in the block's last kernel over NVLink peer memory "
                          "(peer) or with an NCCL all-reduce (nccl)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "chain", "decoder", "grouped", "config3", "config5", "ep-decode"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "chain", "decoder", "decoder3", "grouped", "config3", "config5",
+                             "ep-decode"],
                     help="decoder: only configuration 2's whole decoder (one GPU; --layers shortens it); "
+                         "decoder3: only configuration 3's whole hybrid decoder (one GPU; --layers shortens it); "
                          "chain: only the decode chain of the headline (one GPU; --layers shortens it; a small "
                          "process for profiling moe_chain_kernel); "
                          "grouped: only the configuration-4 measurement (one GPU; a small process for "
@@ -894,11 +924,12 @@ def main() -> None:
         if world > 1:
             dist.destroy_process_group()
         return
-    if args.workload == "decoder":
+    if args.workload in ("decoder", "decoder3"):
         if rank == 0:
-            print(json.dumps({"metric": "configuration-2 decoder tokens/s", "n_gpus": 1,
+            hybrid = args.workload == "decoder3"
+            print(json.dumps({"metric": f"configuration-{3 if hybrid else 2} decoder tokens/s", "n_gpus": 1,
                               **measure_decoder(local, torch.cuda.current_stream(),
-                                                layers=args.layers)}))
+                                                layers=args.layers, hybrid=hybrid)}))
         if world > 1:
             dist.destroy_process_group()
         return
@@ -1022,6 +1053,7 @@ def main() -> None:
     chain_only = args.workload == "chain"
     one_gpu = world == 1 and not chain_only
     decoder = measure_decoder(local, stream) if one_gpu else None
+    decoder3 = measure_decoder(local, stream, hybrid=True) if one_gpu else None
     grouped = measure_grouped(local, stream) if one_gpu else None
     config3 = (measure_config3(local, stream, steps=max(args.steps // 10, 20),
                                cpu_seconds=None if (args.no_cpu_baseline or rank != 0) else 6.0)
@@ -1080,6 +1112,7 @@ def main() -> None:
             "clocks": clocks,
             "cpu_baseline": cpu,
             **({"decoder": decoder} if decoder is not None else {}),
+            **({"config3_decoder": decoder3} if decoder3 is not None else {}),
             **({"grouped": grouped} if grouped is not None else {}),
             **({"config3": config3} if config3 is not None else {}),
             "parity": parity,
