@@ -106,7 +106,10 @@ def chain_phases(be, layers: int, work, stream) -> dict:
     (pokit_cuda_moe_trace_decode; globaltimer stamps of every CTA): medians
     over the inner layers.  gate_up_us: first CTA's routes ready -> last CTA's
     gate/up products done (the window in which the layer's 14.2 MB of gate/up
-    weights stream in)."""
+    weights stream in); act_exchange_down_us: last CTA's activation words
+    stored -> last D unit's down products combined (the tagged-word exchange
+    plus the down MMA); partials_us: -> last D unit's next-layer router
+    partials added and its route arrival."""
     import torch
     grid = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     st = torch.zeros(layers * grid * 16, dtype=torch.int64, device="cuda")
@@ -120,9 +123,10 @@ def chain_phases(be, layers: int, work, stream) -> dict:
         "layer_us": med([ns[l, :units, 7].max() - ns[l - 1, :units, 7].max() for l in inner if l > 0]) if layers > 1 else None,
         "route_us": med([ns[l, :, 1].max() - ns[l, :, 0].min() for l in inner]),
         "gate_up_us": med([ns[l, :, 2].max() - ns[l, :, 1].min() for l in inner]),
-        "act_publish_us": med([ns[l, :, 3].max() - ns[l, :, 2].max() for l in inner]),
-        "down_us": med([ns[l, :units, 7].max() - ns[l, :units, 4].min() for l in inner]),
-        "how": "pokit_cuda_moe_trace_decode: globaltimer stamps per CTA and phase, medians over layers",
+        "act_exchange_down_us": med([ns[l, :units, 5].max() - ns[l, :, 3].max() for l in inner]),
+        "partials_us": med([ns[l, :units, 7].max() - ns[l, :units, 5].max() for l in inner]),
+        "how": "pokit_cuda_moe_trace_decode: globaltimer stamps per CTA and phase, medians over layers "
+               "(globaltimer ticks are coarse: sub-microsecond phases are approximate)",
     }
 
 

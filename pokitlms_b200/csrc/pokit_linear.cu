@@ -5,6 +5,7 @@
 // with W in its GGUF block encoding, FP32 x and FP32 accumulation, plus the
 // row decoder behind dequantize_quantized_row (quantized_linear.hpp:11-13).
 #include "pokit_kernels.h"
+#include "pokit_mma.cuh"
 #include "pokit_quant.cuh"
 
 #include <map>
@@ -249,9 +250,141 @@ cudaError_t launch_rows(const void* w, uint32_t rows, uint32_t cols, const float
                               accumulate ? 1 : 0, norm_w, norm_eps);
 }
 
+// ---------------------------------------------------------------------------
+// Q4_K matvec on the integer tensor path (mma.sync m16n8k32, u8 weights x
+// int8 pieces of x, q4k_mma_superblock): CTA c owns rows [16c, 16c + 16) and
+// its warp w the superblocks w, w + 8, ... of those rows.  Each warp copies
+// its 16-row x 144-byte superblock tiles with bulk copies (lanes 0..15, one
+// row each) before waiting on the previous kernel (the weights do not depend
+// on it), builds the x records of its own superblocks (after the fused RMS
+// norm, when given), multiplies, and the CTA adds the eight warps' partial
+// rows in warp order.  Rows past `rows` in the last block are neither copied
+// nor written.
+constexpr uint32_t kMmaLinWarps = 8;
+constexpr uint32_t kMmaLinMaxPer = 4;           // superblocks per warp: cols <= 8192
+
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kMmaLinWarps * 32)
+linear_q4k_mma_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, const float* __restrict__ x,
+                      float* __restrict__ y, int accumulate, const float* __restrict__ norm_w, float norm_eps) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bar[kMmaLinWarps];
+    __shared__ float red[kMmaLinWarps];
+    __shared__ float part[kMmaLinWarps][16];
+    const uint32_t nsb = cols / 256u, per = (nsb + kMmaLinWarps - 1) / kMmaLinWarps;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2;
+    const uint32_t row0 = blockIdx.x * 16u, nrows = min(16u, rows - row0);
+    const uint64_t rb = static_cast<uint64_t>(nsb) * 144u;
+    const uint32_t mine = static_cast<uint32_t>(warp) < nsb ? (nsb - warp + kMmaLinWarps - 1) / kMmaLinWarps : 0u;
+    uint8_t* tiles = smem + static_cast<uint32_t>(warp) * per * kBoxBytes;
+    uint32_t* recs = reinterpret_cast<uint32_t*>(smem + kMmaLinWarps * per * kBoxBytes) + warp * per * kFragWords;
+    if (lane == 0) {
+        mbar_init(&bar[warp], 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    if (mine) {
+        if (lane == 0) mbar_expect_tx(&bar[warp], mine * nrows * 144u);
+        __syncwarp();
+        if (static_cast<uint32_t>(lane) < nrows)
+            for (uint32_t i = 0; i < mine; ++i)
+                bulk_copy_g2s(tiles + i * kBoxBytes + lane * 144u,
+                              w + static_cast<uint64_t>(row0 + lane) * rb + (warp + kMmaLinWarps * i) * 144u, 144u,
+                              &bar[warp]);
+    }
+    grid_dep_launch();
+    grid_dep_wait();
+    float scale = 1.0f;
+    if (norm_w) {
+        // x = rms_norm(x, norm_w) first (src/rms_norm.cpp:9-27).
+        float ss = 0.0f;
+        for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float total = 0.0f;
+        for (uint32_t i = 0; i < kMmaLinWarps; ++i) total += red[i];
+        scale = 1.0f / sqrtf(total / static_cast<float>(cols) + norm_eps);
+    }
+    for (uint32_t i = 0; i < mine; ++i) {
+        const uint32_t sb = warp + kMmaLinWarps * i;
+        float* stage = reinterpret_cast<float*>(recs + i * kFragWords);
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t c = sb * 256u + 32u * j + lane;
+            v[j] = norm_w ? __fmul_rn(__fmul_rn(x[c], scale), norm_w[c]) : x[c];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = v[j];
+        __syncwarp();
+        q4k_frag_superblock(stage, recs + i * kFragWords, lane);
+        __syncwarp();
+    }
+    float acc0 = 0.0f, acc1 = 0.0f;
+    if (mine) {
+        // The copies land well within the bound; if not, wait once more:
+        // shared memory a copy may still write is never given up.
+        if (!mbar_wait(&bar[warp], 0)) {
+            mbar_wait(&bar[warp], 0);
+            acc0 = acc1 = __int_as_float(0x7fc00000);
+        }
+        for (uint32_t i = 0; i < mine; ++i) {
+            const uint8_t* t = tiles + i * kBoxBytes;
+            q4k_mma_superblock(t + g * 144u, t + (g + 8) * 144u, recs + i * kFragWords, acc0, acc1);
+        }
+    }
+    acc0 = quad_sum(acc0);
+    acc1 = quad_sum(acc1);
+    if ((lane & 3) == 0) {
+        part[warp][g] = acc0;
+        part[warp][g + 8] = acc1;
+    }
+    __syncthreads();
+    if (threadIdx.x < nrows) {
+        float v = part[0][threadIdx.x];
+        for (uint32_t i = 1; i < kMmaLinWarps; ++i) v += part[i][threadIdx.x];
+        const uint32_t r = row0 + threadIdx.x;
+        y[r] = accumulate ? y[r] + v : v;
+    }
+}
+
+bool mma_linear_fits(const void* w, uint32_t cols) {
+    return (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && cols % 256u == 0 &&
+           (cols / 256u + kMmaLinWarps - 1) / kMmaLinWarps <= kMmaLinMaxPer;
+}
+
+cudaError_t launch_q4k_mma(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y,
+                           cudaStream_t stream, bool accumulate, const float* norm_w, float norm_eps, bool pdl) {
+    const uint32_t per = (cols / 256u + kMmaLinWarps - 1) / kMmaLinWarps;
+    const size_t smem = static_cast<size_t>(kMmaLinWarps) * per * (kBoxBytes + kFragWords * 4u);
+    cudaError_t e = set_smem(linear_q4k_mma_kernel, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((rows + 15u) / 16u);
+    cfg.blockDim = dim3(kMmaLinWarps * 32u);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_q4k_mma_kernel, static_cast<const uint8_t*>(w), rows, cols, x, y,
+                              accumulate ? 1 : 0, norm_w, norm_eps);
+}
+
 template <uint32_t T>
 cudaError_t launch_quant(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y, cudaStream_t stream,
                          bool force_generic, bool accumulate, bool pdl) {
+    if constexpr (T == kQ4_K)
+        if (!force_generic && mma_linear_fits(w, cols))
+            return launch_q4k_mma(w, rows, cols, x, y, stream, accumulate, nullptr, 0.0f, pdl);
     if (!force_generic && rows_kernel_fits<T>(w, cols))
         return launch_rows<T>(w, rows, cols, x, y, stream, accumulate, nullptr, 0.0f, pdl);
     return launch_generic<T>(w, rows, cols, x, y, stream, accumulate);
@@ -305,6 +438,7 @@ cudaError_t launch_linear_normed(uint32_t type, const void* w, uint32_t rows, ui
     if (rows == 0 || cols == 0 || !norm_w) return cudaErrorInvalidValue;
     switch (type) {
         case kQ4_K:
+            if (mma_linear_fits(w, cols)) return launch_q4k_mma(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
             if (!rows_kernel_fits<kQ4_K>(w, cols)) return cudaErrorInvalidValue;
             return launch_rows<kQ4_K>(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
         case kQ5_K:

@@ -1725,7 +1725,7 @@ constexpr uint32_t kChainStamps = 8;
 constexpr uint32_t kPairRowBytes = 288u, kPairBytes = 16u * kPairRowBytes;
 
 struct ChainLayout {
-    uint32_t gbars, dbars, recs, lg, sel_id, sel_w, part, comb, hrow, gtiles, dtiles, total;
+    uint32_t gbars, dbars, recs, lg, sel_id, sel_w, part, dpart, comb, hrow, gtiles, dtiles, total;
     uint32_t nsb, half_sb, nsd, gpairs, dpairs;
 };
 
@@ -1744,7 +1744,8 @@ __host__ __device__ inline ChainLayout chain_layout(const MoeLayerDev& L) {
     c.lg = off; off += al16(L.experts * 4u);
     c.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
     c.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
-    c.part = off; off += al16(umax(kWarps * 16u, k * nsd * 16u) * 4u);
+    c.part = off; off += al16(kWarps * 16u * 4u);
+    c.dpart = off; off += al16(k * nsd * 16u * 4u);
     c.comb = off; off += al16(k * 16u * 4u);
     c.hrow = off; off += al16(2u * kPartRows * 4u);
     off = al128(off);
@@ -1856,6 +1857,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
     uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + c.sel_id);
     float* sel_w = reinterpret_cast<float*>(smem + c.sel_w);
     float* part = reinterpret_cast<float*>(smem + c.part);
+    float* dpart = reinterpret_cast<float*>(smem + c.dpart);
     float* comb = reinterpret_cast<float*>(smem + c.comb);
     float* hrow = reinterpret_cast<float*>(smem + c.hrow);
     uint8_t* gtiles = smem + c.gtiles;
@@ -1939,6 +1941,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
         stamp(l, 0);
         const unsigned long long* racc = a.C.racc + pr * racc_span;
         if (warp < static_cast<int>(kTailLogitWarps)) {
+            // The first expert's limbs, then (warp 0) the per-chunk sums of
+            // squares: both loads in flight before either is used.
+            const uint32_t e_first = warp * 32u + lane;
+            ulonglong2 limbs[kRaccLimbs / 2];
+            if (e_first < E) {
+                const ulonglong2* q = reinterpret_cast<const ulonglong2*>(racc + static_cast<uint64_t>(e_first) * kRaccLimbs);
+#pragma unroll
+                for (int h2 = 0; h2 < kRaccLimbs / 2; ++h2) limbs[h2] = __ldcg(q + h2);
+            }
             if (warp == 0) {
                 float sq = 0.0f;
                 for (uint32_t u = lane; u < units; u += 32) sq += __ldcg(a.C.rsq + p * units + u);
@@ -1950,10 +1961,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                     bad_sh = __ldcg(a.C.rbad + pr);
                 }
             }
-            for (uint32_t e0 = warp * 32u; e0 < E; e0 += kTailLogitWarps * 32u) {
+            if (e_first < E) lg[e_first] = racc_value(limbs);
+            for (uint32_t e0 = warp * 32u + kTailLogitWarps * 32u; e0 < E; e0 += kTailLogitWarps * 32u) {
                 const uint32_t e = e0 + lane;
                 if (e < E) {
-                    ulonglong2 limbs[kRaccLimbs / 2];
                     const ulonglong2* q = reinterpret_cast<const ulonglong2*>(racc + static_cast<uint64_t>(e) * kRaccLimbs);
 #pragma unroll
                     for (int h2 = 0; h2 < kRaccLimbs / 2; ++h2) limbs[h2] = __ldcg(q + h2);
@@ -2131,20 +2142,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                     if (q < nrec)
                         q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords, lane);
                 }
-            }
-            stamp(l, 4);
-            __syncthreads();
-            if (abort_sh) {
-                if (static_cast<uint32_t>(warp) < k && lane == 0)
-                    for (uint32_t j = 0; j < dpairs; ++j) mbar_wait(&dbars[warp * dpairs + j], phase);
-                ok = false;
-                break;
-            }
-            stamp(l, 5);
-            for (uint32_t u = warp; u < nrec; u += 2 * kWarps) {
-                const uint32_t v2 = u + kWarps;
+                __syncwarp();
+                // The warp multiplies the records it just built (no wait for
+                // the CTA's other warps): unit (slot, sb) lives in pair box
+                // slot * dpairs + sb / 2.
+                const uint32_t u = q0, v2 = q0 + kWarps;
                 float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
-                // Unit (slot, sb) lives in pair box slot * dpairs + sb / 2.
                 const auto unit_box = [&](uint32_t q) {
                     const uint32_t sl = q / nsd, sb = q % nsd, bi = sl * dpairs + (sb >> 1);
                     wait_bar(&dbars[bi]);
@@ -2162,20 +2165,28 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                 b0 = quad_sum(b0);
                 b1 = quad_sum(b1);
                 if ((lane & 3) == 0) {
-                    part[u * 16 + g] = a0;
-                    part[u * 16 + g + 8] = a1;
+                    dpart[u * 16 + g] = a0;
+                    dpart[u * 16 + g + 8] = a1;
                     if (v2 < nrec) {
-                        part[v2 * 16 + g] = b0;
-                        part[v2 * 16 + g + 8] = b1;
+                        dpart[v2 * 16 + g] = b0;
+                        dpart[v2 * 16 + g + 8] = b1;
                     }
                 }
             }
+            stamp(l, 4);
             __syncthreads();
+            if (abort_sh) {
+                if (static_cast<uint32_t>(warp) < k && lane == 0)
+                    for (uint32_t j = 0; j < dpairs; ++j) mbar_wait(&dbars[warp * dpairs + j], phase);
+                ok = false;
+                break;
+            }
+            stamp(l, 5);
             // Weighted slot rows, then the sum over slots in route order.
             for (uint32_t t = tid; t < 16u * k; t += kThreads) {
                 const uint32_t row = t & 15u, sl = t >> 4;
                 float y = 0.0f;
-                for (uint32_t sb = 0; sb < nsd; ++sb) y += part[(sl * nsd + sb) * 16 + row];
+                for (uint32_t sb = 0; sb < nsd; ++sb) y += dpart[(sl * nsd + sb) * 16 + row];
                 comb[sl * 16 + row] = sel_w[sl] * y;
             }
             __syncthreads();
