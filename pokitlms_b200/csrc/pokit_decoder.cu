@@ -26,6 +26,7 @@
 // and runs as one CUDA graph replay (captured on first use).
 #include "../../include/pokit_cuda.h"
 #include "pokit_kernels.h"
+#include "pokit_mma.cuh"
 #include "pokit_quant.cuh"
 
 #include <cuda_fp16.h>
@@ -126,12 +127,17 @@ __device__ __forceinline__ float sigmoid_signed(float v) {
     return e / (1.0f + e);
 }
 
-__global__ void __launch_bounds__(kAttendThreads)
-attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
-              const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, __half* __restrict__ kc,
-              __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, const AttendShape sh,
-              float* __restrict__ out) {
-    extern __shared__ float sc[];
+// One query head of the layer: q_in / k_in / v_in are the head's projected
+// query, its KV head's new key and value (d floats each, global or shared
+// memory), gate_in the head's gate (Qwen3.5) or null, rope_cos / rope_sin the
+// rotary half's table rows of this position; writes the head's d outputs to
+// out.  sc: window floats of dynamic shared memory.  Every thread of the CTA
+// calls it.
+__device__ void attend_head(const float* q_in, const float* k_in, const float* v_in, const float* gate_in,
+                            const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+                            const float* rope_cos, const float* rope_sin,
+                            __half* __restrict__ kc, __half* __restrict__ vc, uint32_t pos, const AttendShape& sh,
+                            uint32_t h, float* sc, float* out) {
     __shared__ float red[32];
     __shared__ __align__(16) float qs[kAttendMaxDim];
     __shared__ __align__(16) float kn[kAttendMaxDim];
@@ -139,30 +145,15 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     __shared__ __align__(16) float vnew[kAttendMaxDim];
     __shared__ __align__(16) float part[kAttendThreads / 32][kAttendMaxDim];
     const uint32_t d = sh.d, window = sh.window, qh = sh.qh, kvh = sh.kvh, rh = sh.rh;
-    // The position counter changes only at the end of a token step, so it and
-    // the cached keys and values of earlier positions are read before waiting
-    // for the Q/K/V projection: the first CTA of each query group pulls its
-    // head's cached rows towards L2 while the projection finishes.
-    const uint32_t t = threadIdx.x, h = blockIdx.x, pos = *pos_p;
+    const uint32_t t = threadIdx.x;
     const uint32_t group = qh / kvh, kh = h / group;
     const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
     const int lane = t & 31, warp = t >> 5;
     constexpr int kW = kAttendThreads / 32;
     const uint64_t row_stride = static_cast<uint64_t>(kvh) * d;
-    if (h % group == 0) {
-        const uint32_t lines = (d * 2u + 127u) / 128u;
-        for (uint32_t i = t; i + lines < n * lines; i += kAttendThreads) {
-            const uint64_t at = ((first + i / lines) % window) * row_stride + kh * d + (i % lines) * 64u;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(kc + at));
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(vc + at));
-        }
-    }
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const uint32_t kbase = qh * sh.q_stride, vbase = kbase + kvh * d;
     const bool dim = t < d;
-    const float xq = dim ? qkv[h * sh.q_stride + t] : 0.0f;
-    const float xk = dim ? qkv[kbase + kh * d + t] : 0.0f;
+    const float xq = dim ? q_in[t] : 0.0f;
+    const float xk = dim ? k_in[t] : 0.0f;
     const float sq = head_rms_scale(xq, d, sh.eps, red);
     const float sk = head_rms_scale(xk, d, sh.eps, red);
     if (dim) {
@@ -174,7 +165,7 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     if (dim) {
         if (t < 2u * rh) {
             const uint32_t j = t < rh ? t : t - rh;
-            const float c = rope_cos[static_cast<uint64_t>(pos) * rh + j], s = rope_sin[static_cast<uint64_t>(pos) * rh + j];
+            const float c = rope_cos[j], s = rope_sin[j];
             const float aq = qs[j], bq = qs[j + rh], ak = kn[j], bk = kn[j + rh];
             rq = t < rh ? __fsub_rn(__fmul_rn(aq, c), __fmul_rn(bq, s)) : __fadd_rn(__fmul_rn(bq, c), __fmul_rn(aq, s));
             rk = t < rh ? __fsub_rn(__fmul_rn(ak, c), __fmul_rn(bk, s)) : __fadd_rn(__fmul_rn(bk, c), __fmul_rn(ak, s));
@@ -187,7 +178,7 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     if (dim) {
         qs[t] = rq;
         const __half hk = __float2half_rn(rk);
-        const __half hv = __float2half_rn(qkv[vbase + kh * d + t]);
+        const __half hv = __float2half_rn(v_in[t]);
         knew[t] = __half2float(hk);
         vnew[t] = __half2float(hv);
         if (h % group == 0) {
@@ -281,8 +272,362 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
         float o = part[0][t];
         for (int w = 1; w < kW; ++w) o += part[w][t];
         // qwen35_runner.cpp:577-580: the gated output attended * sigmoid(gate).
-        if (sh.gated) o = __fmul_rn(o, sigmoid_signed(qkv[h * sh.q_stride + d + t]));
-        out[h * d + t] = o;
+        if (gate_in) o = __fmul_rn(o, sigmoid_signed(gate_in[t]));
+        out[t] = o;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kAttendThreads)
+attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+              const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, __half* __restrict__ kc,
+              __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, const AttendShape sh,
+              float* __restrict__ out) {
+    extern __shared__ float sc[];
+    // The position counter changes only at the end of a token step, so it and
+    // the cached keys and values of earlier positions are read before waiting
+    // for the Q/K/V projection: the first CTA of each query group pulls its
+    // head's cached rows towards L2 while the projection finishes.
+    const uint32_t t = threadIdx.x, h = blockIdx.x, pos = *pos_p, d = sh.d, window = sh.window;
+    const uint32_t group = sh.qh / sh.kvh, kh = h / group;
+    const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
+    const uint64_t row_stride = static_cast<uint64_t>(sh.kvh) * d;
+    if (h % group == 0) {
+        const uint32_t lines = (d * 2u + 127u) / 128u;
+        for (uint32_t i = t; i + lines < n * lines; i += kAttendThreads) {
+            const uint64_t at = ((first + i / lines) % window) * row_stride + kh * d + (i % lines) * 64u;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(kc + at));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(vc + at));
+        }
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t kbase = sh.qh * sh.q_stride, vbase = kbase + sh.kvh * d;
+    attend_head(qkv + h * sh.q_stride, qkv + kbase + kh * d, qkv + vbase + kh * d,
+                sh.gated ? qkv + h * sh.q_stride + d : nullptr, q_norm, k_norm,
+                rope_cos + static_cast<uint64_t>(pos) * sh.rh, rope_sin + static_cast<uint64_t>(pos) * sh.rh, kc, vc,
+                pos, sh, h, sc, out + h * d);
+}
+
+// ---------------------------------------------------------------------------
+// The attention block of one layer in one cooperative launch (Q4_K
+// projections): rms_norm(attn_norm) -> the [q (| gate) | k | v] matvec ->
+// attention per query head -> the output projection added into the residual.
+// Steps and who runs them (G CTAs of 256 threads, one per SM):
+//   entry   every CTA bulk-copies its Q/K/V row blocks (16 rows each: blocks
+//           c, c + G, ...) and, for c < H/16, its 16 rows of attn_output into
+//           shared memory (rows padded by 16 bytes so the fragment reads
+//           spread over the banks); query-head CTAs load this position's RoPE
+//           rows and pull their KV head's cached rows towards L2
+//   qkv     every CTA stages h once, forms x' = attn_norm * h / rms(h)
+//           records, multiplies its blocks on the integer tensor path
+//           (q4k_mma_superblock), adds each row's superblock partials in
+//           order and publishes the rows as 8-byte words (tag << 32 | bits)
+//   attend  CTA h < q_heads reads its query (and gate) and its KV head's key
+//           and value words as they arrive and runs attend_head (norms,
+//           RoPE, FP16 ring append, softmax, values); publishes its d outputs
+//   o       CTA c < H/16 reads all output words of its records at once as
+//           they arrive, multiplies its attn_output rows and writes hidden
+//           rows [16c, 16c + 16) = their staged residual + the product
+// Order: every CTA publishes Q/K/V words only after reading all of hidden,
+// and attention needs words from the CTAs owning every row, so no CTA writes
+// hidden before all have read it.  The tag is position * layers + layer + 1
+// (unique within a sequence; the words are cleared with the decode state), so
+// words of another layer or step never match.  Waits are bounded (~2 s); a
+// timeout sets the status word and the CTA drains its copies and leaves.
+struct AttnBlockArgs {
+    const uint8_t* wqkv;             // Q4_K [rows][hidden]: q (| gate), k, v
+    const uint8_t* wo;               // Q4_K [hidden][q_heads * d]
+    const float* attn_norm;
+    const float* q_norm;
+    const float* k_norm;
+    const float* rope_cos;           // [context][rotary half]
+    const float* rope_sin;
+    __half* kc;                      // this layer's rings
+    __half* vc;
+    const uint32_t* pos_p;
+    AttendShape sh;
+    float* hidden;
+    unsigned long long* qkv_ll;      // [rows] words
+    unsigned long long* att_ll;      // [q_heads * d] words
+    uint32_t* status;                // timeout flag
+    uint32_t H, rows, qd, layer, layers;
+    float eps;
+};
+
+constexpr uint32_t kAttnBlockThreads = 256, kAttnBlockWarps = 8;
+constexpr uint32_t kAttnStatusTimeout = 1u;
+constexpr uint32_t kAttnMaxOutPerWarp = 2;          // output superblocks per warp: q_heads * d <= 4096
+
+struct AttnBlockLayout {
+    uint32_t nsb_in, nsb_o, pitch_in, pitch_o, blocks_max;
+    uint32_t qtiles, otiles, xrec, arec, qpart, opart, stage, rope, sc, total;
+};
+
+__host__ __device__ inline AttnBlockLayout attn_block_layout(uint32_t H, uint32_t rows, uint32_t qd, uint32_t d,
+                                                             uint32_t rh, uint32_t window, uint32_t grid) {
+    AttnBlockLayout c{};
+    c.nsb_in = H / 256u;
+    c.nsb_o = qd / 256u;
+    c.pitch_in = c.nsb_in * 144u + 16u;
+    c.pitch_o = c.nsb_o * 144u + 16u;
+    c.blocks_max = (rows / 16u + grid - 1u) / grid;
+    uint32_t off = 0;
+    c.qtiles = off; off += c.blocks_max * 16u * c.pitch_in;
+    off = (off + 127u) & ~127u;
+    c.otiles = off; off += 16u * c.pitch_o;
+    off = (off + 127u) & ~127u;
+    c.xrec = off; off += c.nsb_in * kFragWords * 4u;
+    c.arec = off; off += c.nsb_o * kFragWords * 4u;
+    c.qpart = off; off += c.blocks_max * c.nsb_in * 16u * 4u;
+    c.opart = off; off += c.nsb_o * 16u * 4u;
+    c.stage = off; off += 5u * d * 4u;                   // query, gate, key, value, output of one head
+    c.rope = off; off += 2u * rh * 4u;                   // this position's cos and sin rows
+    c.sc = off; off += window * 4u;
+    c.total = (off + 127u) & ~127u;
+    return c;
+}
+
+// Polls the words src[i] (where use[i]) until every tag is `tag`; false on a
+// timeout (or another CTA's).
+template <int N>
+__device__ __forceinline__ bool await_words(const unsigned long long* const (&src)[N], unsigned long long (&v)[N],
+                                            const bool (&use)[N], uint32_t tag, uint32_t* status) {
+    long long t0 = 0;
+    for (uint32_t polls = 0;; ++polls) {
+        bool ready = true;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            if (use[i] && static_cast<uint32_t>(v[i] >> 32) != tag) {
+                ready = false;
+                unsigned long long w;
+                asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(src[i]) : "memory");
+                v[i] = w;
+            }
+        }
+        if (ready) return true;
+        if (polls == 0) t0 = clock64();
+        if ((polls & 63u) == 63u) {
+            uint32_t st;
+            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(st) : "l"(status) : "memory");
+            if (st || clock64() - t0 > 4000000000LL) {
+                atomicOr(status, kAttnStatusTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void put_word(unsigned long long* p, uint32_t tag, float v) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__global__ void __launch_bounds__(kAttnBlockThreads, 1) attn_block_kernel(const __grid_constant__ AttnBlockArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bars[2];
+    __shared__ float red[kAttnBlockWarps];
+    __shared__ uint32_t abort_sh;
+    const AttendShape& sh = a.sh;
+    const uint32_t G = gridDim.x, cta = blockIdx.x, tid = threadIdx.x, d = sh.d;
+    const int lane = tid & 31, warp = tid >> 5, g = lane >> 2;
+    const AttnBlockLayout c = attn_block_layout(a.H, a.rows, a.qd, d, sh.rh, sh.window, G);
+    const uint32_t nblk = a.rows / 16u, units = a.H / 16u;
+    const uint32_t mine = cta < nblk ? (nblk - cta + G - 1u) / G : 0u;
+    const bool o_unit = cta < units, head = cta < sh.qh;
+    const uint64_t rb_in = c.nsb_in * 144u, rb_o = c.nsb_o * 144u;
+    uint8_t* qtiles = smem + c.qtiles;
+    uint8_t* otiles = smem + c.otiles;
+    uint32_t* xrec = reinterpret_cast<uint32_t*>(smem + c.xrec);
+    uint32_t* arec = reinterpret_cast<uint32_t*>(smem + c.arec);
+    float* qpart = reinterpret_cast<float*>(smem + c.qpart);
+    float* opart = reinterpret_cast<float*>(smem + c.opart);
+    float* stage = reinterpret_cast<float*>(smem + c.stage);
+    float* rope = reinterpret_cast<float*>(smem + c.rope);
+    float* sc = reinterpret_cast<float*>(smem + c.sc);
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        mbar_fence_init();
+        abort_sh = 0u;
+    }
+    __syncthreads();
+    // ---- entry: copies, RoPE rows, KV rows towards L2 ----
+    if (warp == 0 && mine) {
+        if (lane == 0) mbar_expect_tx(&bars[0], mine * 16u * static_cast<uint32_t>(rb_in));
+        __syncwarp();
+        if (lane < 16)
+            for (uint32_t i = 0; i < mine; ++i)
+                bulk_copy_g2s(qtiles + (i * 16u + lane) * c.pitch_in,
+                              a.wqkv + static_cast<uint64_t>((cta + G * i) * 16u + lane) * rb_in,
+                              static_cast<uint32_t>(rb_in), &bars[0]);
+    } else if (warp == 1 && o_unit) {
+        if (lane == 0) mbar_expect_tx(&bars[1], 16u * static_cast<uint32_t>(rb_o));
+        __syncwarp();
+        if (lane < 16)
+            bulk_copy_g2s(otiles + lane * c.pitch_o, a.wo + static_cast<uint64_t>(cta * 16u + lane) * rb_o,
+                          static_cast<uint32_t>(rb_o), &bars[1]);
+    }
+    const uint32_t pos = *a.pos_p, tag = pos * a.layers + a.layer + 1u;
+    if (head) {
+        for (uint32_t j = tid; j < sh.rh; j += kAttnBlockThreads) {
+            rope[j] = a.rope_cos[static_cast<uint64_t>(pos) * sh.rh + j];
+            rope[sh.rh + j] = a.rope_sin[static_cast<uint64_t>(pos) * sh.rh + j];
+        }
+        const uint32_t group = sh.qh / sh.kvh, kh = cta / group;
+        if (cta % group == 0) {
+            const uint32_t n = pos + 1 < sh.window ? pos + 1 : sh.window, first = pos + 1 - n;
+            const uint32_t lines = (d * 2u + 127u) / 128u;
+            const uint64_t row_stride = static_cast<uint64_t>(sh.kvh) * d;
+            for (uint32_t i = tid; i + lines < n * lines; i += kAttnBlockThreads) {
+                const uint64_t at = ((first + i / lines) % sh.window) * row_stride + kh * d + (i % lines) * 64u;
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(a.kc + at));
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(a.vc + at));
+            }
+        }
+    }
+    // ---- qkv: h staged once, x' records ----
+    const float resid = o_unit && tid < 16 ? __ldcg(a.hidden + cta * 16u + tid) : 0.0f;
+    {
+        float ss = 0.0f;
+        for (uint32_t sb = warp; sb < c.nsb_in; sb += kAttnBlockWarps) {
+            float* st = reinterpret_cast<float*>(xrec + sb * kFragWords);
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldcg(a.hidden + sb * 256u + 32u * j + lane);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                ss = fmaf(v[j], v[j], ss);
+                st[32 * j + lane] = v[j];
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float total = 0.0f;
+        for (uint32_t i = 0; i < kAttnBlockWarps; ++i) total += red[i];
+        const float scale = 1.0f / sqrtf(total / static_cast<float>(a.H) + a.eps);
+        for (uint32_t sb = warp; sb < c.nsb_in; sb += kAttnBlockWarps) {
+            float* st = reinterpret_cast<float*>(xrec + sb * kFragWords);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t col = sb * 256u + 32u * j + lane;
+                st[32 * j + lane] = __fmul_rn(__fmul_rn(st[32 * j + lane], scale), a.attn_norm[col]);
+            }
+            __syncwarp();
+            q4k_frag_superblock(st, xrec + sb * kFragWords, lane);
+        }
+    }
+    __syncthreads();
+    // ---- qkv: multiply, publish ----
+    if (mine) {
+        if (!mbar_wait(&bars[0], 0)) {
+            if (lane == 0) { atomicOr(a.status, kAttnStatusTimeout); abort_sh = 1u; }
+            mbar_wait(&bars[0], 0);
+        }
+        for (uint32_t task = warp; task < mine * c.nsb_in; task += kAttnBlockWarps) {
+            const uint32_t i = task / c.nsb_in, sb = task % c.nsb_in;
+            const uint8_t* t0 = qtiles + (i * 16u) * c.pitch_in + sb * 144u;
+            float a0 = 0.0f, a1 = 0.0f;
+            q4k_mma_superblock(t0 + g * c.pitch_in, t0 + (g + 8) * c.pitch_in, xrec + sb * kFragWords, a0, a1);
+            a0 = quad_sum(a0);
+            a1 = quad_sum(a1);
+            if ((lane & 3) == 0) {
+                qpart[(i * c.nsb_in + sb) * 16u + g] = a0;
+                qpart[(i * c.nsb_in + sb) * 16u + g + 8] = a1;
+            }
+        }
+        __syncthreads();
+        for (uint32_t t = tid; t < mine * 16u; t += kAttnBlockThreads) {
+            const uint32_t i = t / 16u, r = t % 16u;
+            float v = qpart[(i * c.nsb_in) * 16u + r];
+            for (uint32_t sb = 1; sb < c.nsb_in; ++sb) v += qpart[(i * c.nsb_in + sb) * 16u + r];
+            put_word(a.qkv_ll + (cta + G * i) * 16u + r, tag, v);
+        }
+    }
+    // ---- attend ----
+    if (head) {
+        const uint32_t h = cta, kh = h / (sh.qh / sh.kvh);
+        const uint32_t kbase = sh.qh * sh.q_stride, vbase = kbase + sh.kvh * d;
+        float* qin = stage;
+        float* gin = stage + d;
+        float* kin = stage + 2 * d;
+        float* vin = stage + 3 * d;
+        float* aout = stage + 4 * d;
+        if (tid < d) {
+            const unsigned long long* src[4] = {a.qkv_ll + h * sh.q_stride + tid, a.qkv_ll + h * sh.q_stride + d + tid,
+                                                a.qkv_ll + kbase + kh * d + tid, a.qkv_ll + vbase + kh * d + tid};
+            unsigned long long v[4] = {0ull, 0ull, 0ull, 0ull};
+            const bool use[4] = {true, sh.gated != 0u, true, true};
+            if (!await_words<4>(src, v, use, tag, a.status)) abort_sh = 1u;
+            qin[tid] = __uint_as_float(static_cast<uint32_t>(v[0]));
+            gin[tid] = __uint_as_float(static_cast<uint32_t>(v[1]));
+            kin[tid] = __uint_as_float(static_cast<uint32_t>(v[2]));
+            vin[tid] = __uint_as_float(static_cast<uint32_t>(v[3]));
+        }
+        __syncthreads();
+        if (!abort_sh) {
+            attend_head(qin, kin, vin, sh.gated ? gin : nullptr, a.q_norm, a.k_norm, rope, rope + sh.rh, a.kc, a.vc,
+                        pos, sh, h, sc, aout);
+            if (tid < d) put_word(a.att_ll + h * d + tid, tag, aout[tid]);
+        }
+    }
+    // ---- o ----
+    if (o_unit) {
+        // All of the warp's output words in flight at once, then its records.
+        const uint32_t first_sb = warp, nmine = first_sb < c.nsb_o ? (c.nsb_o - first_sb + kAttnBlockWarps - 1) /
+                                                                     kAttnBlockWarps : 0u;
+        if (nmine && !abort_sh) {
+            const unsigned long long* src[8 * kAttnMaxOutPerWarp];
+            unsigned long long v[8 * kAttnMaxOutPerWarp];
+            bool use[8 * kAttnMaxOutPerWarp];
+#pragma unroll
+            for (uint32_t i = 0; i < kAttnMaxOutPerWarp; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t sb = first_sb + i * kAttnBlockWarps;
+                    use[i * 8 + j] = i < nmine;
+                    src[i * 8 + j] = a.att_ll + (i < nmine ? sb : first_sb) * 256u + 32u * j + lane;
+                    v[i * 8 + j] = 0ull;
+                }
+            if (!await_words<8 * kAttnMaxOutPerWarp>(src, v, use, tag, a.status)) abort_sh = 1u;
+#pragma unroll
+            for (uint32_t i = 0; i < kAttnMaxOutPerWarp; ++i) {
+                if (i < nmine) {
+                    const uint32_t sb = first_sb + i * kAttnBlockWarps;
+                    float* st = reinterpret_cast<float*>(arec + sb * kFragWords);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) st[32 * j + lane] = __uint_as_float(static_cast<uint32_t>(v[i * 8 + j]));
+                    __syncwarp();
+                    q4k_frag_superblock(st, arec + sb * kFragWords, lane);
+                }
+            }
+        }
+        __syncthreads();
+        if (!mbar_wait(&bars[1], 0)) {
+            if (lane == 0) { atomicOr(a.status, kAttnStatusTimeout); abort_sh = 1u; }
+            mbar_wait(&bars[1], 0);
+        }
+        __syncthreads();
+        if (!abort_sh) {
+            for (uint32_t sb = warp; sb < c.nsb_o; sb += kAttnBlockWarps) {
+                float a0 = 0.0f, a1 = 0.0f;
+                const uint8_t* t0 = otiles + sb * 144u;
+                q4k_mma_superblock(t0 + g * c.pitch_o, t0 + (g + 8) * c.pitch_o, arec + sb * kFragWords, a0, a1);
+                a0 = quad_sum(a0);
+                a1 = quad_sum(a1);
+                if ((lane & 3) == 0) {
+                    opart[sb * 16u + g] = a0;
+                    opart[sb * 16u + g + 8] = a1;
+                }
+            }
+            __syncthreads();
+            if (tid < 16) {
+                float v = opart[tid];
+                for (uint32_t sb = 1; sb < c.nsb_o; ++sb) v += opart[sb * 16u + tid];
+                a.hidden[cta * 16u + tid] = resid + v;
+            }
+        }
     }
 }
 
@@ -618,9 +963,11 @@ public:
         }
         // The reference forwards every generated token but the last one.
         next_position_ = n + (produced ? produced - 1 : 0);
-        // Forwards past the end token left the device position ahead: align it.
+        // Forwards past the end token left the device position ahead: align it
+        // (and drop their attention words, whose tags the next forwards reuse).
         *pinned_ids_ = static_cast<uint32_t>(next_position_);
         guard(cudaMemcpyAsync(pos_, pinned_ids_, 4, cudaMemcpyHostToDevice, stream_), "position");
+        if (attn_ll_) guard(cudaMemsetAsync(attn_ll_, 0, attn_words_ * 8, stream_), "position");
         guard(cudaStreamSynchronize(stream_), "position");
         const auto t2 = std::chrono::steady_clock::now();
         *n_out = produced;
@@ -801,13 +1148,91 @@ private:
         check(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming), "cudaEventCreate");
         check(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(window_ * 4)), "attend smem");
+        plan_attn_block();
     }
 
-    // Position 0 and zero DeltaNet states (the KV ring needs no clearing:
-    // attention reads only positions written since).
+    // The fused attention block serves Q4_K projections when every CTA owns
+    // a Q/K/V row block, the output-projection units and query heads fit the
+    // grid, and one CTA per SM fits (POKIT_CUDA_FUSED_ATTN=0 turns it off).
+    void plan_attn_block() {
+        const char* env = std::getenv("POKIT_CUDA_FUSED_ATTN");
+        if (env && env[0] == '0') return;
+        int sms = 0;
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg_.device), "SM count");
+        const uint32_t rows = static_cast<uint32_t>(qrows_ + 2 * kd_), H = static_cast<uint32_t>(cfg_.hidden);
+        const uint32_t grid = static_cast<uint32_t>(sms);
+        if (cfg_.attn_type != kQ4_K || rows % 16 || qd_ % 256 || rows / 16 < grid || H / 16 > grid ||
+            cfg_.q_heads > grid)
+            return;
+        if (qd_ / 256 > kAttnBlockWarps * kAttnMaxOutPerWarp || cfg_.layers > 255) return;
+        const AttnBlockLayout c = attn_block_layout(H, rows, static_cast<uint32_t>(qd_),
+                                                    static_cast<uint32_t>(cfg_.head_dim), static_cast<uint32_t>(rh_),
+                                                    static_cast<uint32_t>(window_), grid);
+        if (c.total > 200u * 1024u) return;
+        if (cudaFuncSetAttribute(attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(c.total)) != cudaSuccess) {
+            cudaGetLastError();
+            return;
+        }
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_block_kernel, kAttnBlockThreads, c.total) !=
+                cudaSuccess || per_sm < 1) {
+            cudaGetLastError();
+            return;
+        }
+        attn_words_ = rows + qd_;
+        check(cudaMalloc(&attn_ll_, attn_words_ * 8), "cudaMalloc(attention words)");
+        check(cudaMemset(attn_ll_, 0, attn_words_ * 8), "cudaMemset(attention words)");
+        attn_grid_ = grid;
+        attn_smem_ = c.total;
+    }
+
+    cudaError_t launch_attn_block(size_t l, cudaStream_t s) {
+        AttnBlockArgs a{};
+        const auto F = [&](uint32_t t) { return reinterpret_cast<const float*>(tensor_ptr(l, t)); };
+        const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
+        const uint32_t rows = static_cast<uint32_t>(qrows_ + 2 * kd_);
+        a.wqkv = tensor_ptr(l, POKIT_CUDA_DEC_ATTN_Q);
+        a.wo = tensor_ptr(l, POKIT_CUDA_DEC_ATTN_OUTPUT);
+        a.attn_norm = F(POKIT_CUDA_DEC_ATTN_NORM);
+        a.q_norm = F(POKIT_CUDA_DEC_ATTN_Q_NORM);
+        a.k_norm = F(POKIT_CUDA_DEC_ATTN_K_NORM);
+        a.rope_cos = rope_;
+        a.rope_sin = rope_ + cfg_.context * rh_;
+        a.kc = kcache_ + kv_off;
+        a.vc = vcache_ + kv_off;
+        a.pos_p = pos_;
+        a.sh = ash_;
+        a.hidden = hidden_;
+        a.qkv_ll = attn_ll_;
+        a.att_ll = attn_ll_ + rows;
+        a.status = status_ + 2;
+        a.H = static_cast<uint32_t>(cfg_.hidden);
+        a.rows = rows;
+        a.qd = static_cast<uint32_t>(qd_);
+        a.layer = static_cast<uint32_t>(l);
+        a.layers = static_cast<uint32_t>(cfg_.layers);
+        a.eps = cfg_.rms_epsilon;
+        cudaLaunchConfig_t lc{};
+        lc.gridDim = dim3(attn_grid_);
+        lc.blockDim = dim3(kAttnBlockThreads);
+        lc.dynamicSmemBytes = attn_smem_;
+        lc.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        return cudaLaunchKernelEx(&lc, attn_block_kernel, a);
+    }
+
+    // Position 0, zero DeltaNet states and attention words (the KV ring
+    // needs no clearing: attention reads only positions written since).
     void clear_state() {
         guard(cudaMemsetAsync(pos_, 0, 4, stream_), "reset");
         if (ssm_) guard(cudaMemsetAsync(ssm_, 0, ssm_bytes_, stream_), "reset");
+        // The attention words' tags repeat with the positions of a new sequence.
+        if (attn_ll_) guard(cudaMemsetAsync(attn_ll_, 0, attn_words_ * 8, stream_), "reset");
     }
 
     void release() {
@@ -822,6 +1247,7 @@ private:
         if (vcache_) cudaFree(vcache_);
         if (kcache_) cudaFree(kcache_);
         if (ssm_) cudaFree(ssm_);
+        if (attn_ll_) cudaFree(attn_ll_);
         if (pool_) cudaFree(pool_);
         if (moe_) pokit_cuda_moe_destroy(moe_);
         moe_ = nullptr;
@@ -855,6 +1281,7 @@ private:
         ash.window = win;
         ash.eps = eps;
         ash.scale = scale;
+        ash_ = ash;
         pokit_cuda_delta_net_shape dsh{};
         dsh.key_heads = cfg_.ssm_group_count;
         dsh.value_heads = hv_;
@@ -868,7 +1295,10 @@ private:
         for (size_t l = 0; l < cfg_.layers && e == cudaSuccess; ++l) {
             const auto P = [&](uint32_t t) { return tensor_ptr(l, t); };
             const auto F = [&](uint32_t t) { return reinterpret_cast<const float*>(tensor_ptr(l, t)); };
-            if (attention_layer(l)) {
+            if (attention_layer(l) && attn_grid_) {
+                e = launch_attn_block(l, s);
+                ++n;
+            } else if (attention_layer(l)) {
                 const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
                 e = launch_linear_normed(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_Q), static_cast<uint32_t>(qrows_ + 2 * kd_),
                                          H, hidden_, F(POKIT_CUDA_DEC_ATTN_NORM), eps, qkv_, s, pdl_);
@@ -1009,9 +1439,16 @@ private:
 
     void sync_and_check() {
         guard(cudaStreamSynchronize(stream_), "synchronize");
-        guard(cudaMemcpyAsync(pinned_ids_ + kPinnedIds - 2, status_, 8, cudaMemcpyDeviceToHost, stream_), "status");
+        guard(cudaMemcpyAsync(pinned_ids_ + kPinnedIds - 3, status_, 12, cudaMemcpyDeviceToHost, stream_), "status");
         guard(cudaStreamSynchronize(stream_), "status");
-        const uint32_t st = pinned_ids_[kPinnedIds - 2], gates = pinned_ids_[kPinnedIds - 1];
+        const uint32_t st = pinned_ids_[kPinnedIds - 3], gates = pinned_ids_[kPinnedIds - 2];
+        if (pinned_ids_[kPinnedIds - 1]) {
+            // A bounded wait of the attention block gave up: its counters no
+            // longer match (sticky, like a CUDA error).
+            failed_ = true;
+            failure_ = "the attention block abandoned its work after a bounded device-side wait timed out";
+            throw std::runtime_error(failure_);
+        }
         char err[256];
         if (pokit_cuda_moe_synchronize(moe_, stream_, err, sizeof err) != POKIT_CUDA_STATUS_OK) {
             next_position_ = 0;
@@ -1022,6 +1459,7 @@ private:
             cudaMemsetAsync(status_, 0, 8, stream_);
             cudaMemsetAsync(pos_, 0, 4, stream_);
             if (ssm_) cudaMemsetAsync(ssm_, 0, ssm_bytes_, stream_);
+            if (attn_ll_) cudaMemsetAsync(attn_ll_, 0, attn_words_ * 8, stream_);
             cudaStreamSynchronize(stream_);
             next_position_ = 0;           // the reference resets its state and rethrows
             throw std::runtime_error(gates ? "invalid Gated DeltaNet decay or beta (gated_delta_net.cpp)"
@@ -1060,6 +1498,11 @@ private:
         const char* v = std::getenv("POKIT_CUDA_PDL");
         return !(v && v[0] == '0');
     }();
+    unsigned long long* attn_ll_ = nullptr;   // fused attention block: Q/K/V words, then output words
+    uint64_t attn_words_ = 0;
+    uint32_t attn_grid_ = 0;                   // 0: the three-kernel attention path
+    size_t attn_smem_ = 0;
+    AttendShape ash_{};
     uint64_t launches_per_step_ = 0;
     size_t next_position_ = 0;
     std::string moe_error_;

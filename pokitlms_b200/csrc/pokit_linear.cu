@@ -263,12 +263,6 @@ cudaError_t launch_rows(const void* w, uint32_t rows, uint32_t cols, const float
 constexpr uint32_t kMmaLinWarps = 8;
 constexpr uint32_t kMmaLinMaxPer = 4;           // superblocks per warp: cols <= 8192
 
-__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
-                 : "memory");
-}
-
 __global__ void __launch_bounds__(kMmaLinWarps * 32)
 linear_q4k_mma_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, const float* __restrict__ x,
                       float* __restrict__ y, int accumulate, const float* __restrict__ norm_w, float norm_eps) {

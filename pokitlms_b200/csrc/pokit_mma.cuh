@@ -106,6 +106,13 @@ __device__ __forceinline__ void tma_box_3d(void* dst, const CUtensorMap* map, in
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
+// Contiguous global -> shared bulk copy (no multicast) completing on `bar`;
+// both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
 // 16-byte asynchronous global -> shared copy through L2 (no L1 allocation);
 // completion by cp_async_wait_all.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
