@@ -152,6 +152,17 @@ __device__ void attend_head(const float* q_in, const float* k_in, const float* v
     constexpr int kW = kAttendThreads / 32;
     const uint64_t row_stride = static_cast<uint64_t>(kvh) * d;
     const bool dim = t < d;
+    const uint32_t units = d / 8;                         // 16-byte units of a key row
+    constexpr uint32_t kChunk = 16;                       // units loaded at once (128 dimensions)
+    // The first chunk of this thread's cached key (position t of the window,
+    // first pass) is requested before the norms: it does not depend on them.
+    uint4 k0[kChunk];
+    if (t + 1 < n) {
+        const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + t) % window) * row_stride + kh * d);
+#pragma unroll
+        for (uint32_t u = 0; u < kChunk; ++u)
+            if (u < units) k0[u] = __ldg(k + u);
+    }
     const float xq = dim ? q_in[t] : 0.0f;
     const float xk = dim ? k_in[t] : 0.0f;
     const float sq = head_rms_scale(xq, d, sh.eps, red);
@@ -188,8 +199,6 @@ __device__ void attend_head(const float* q_in, const float* k_in, const float* v
         }
     }
     __syncthreads();
-    const uint32_t units = d / 8;                         // 16-byte units of a key row
-    constexpr uint32_t kChunk = 16;                       // units loaded at once (128 dimensions)
     for (uint32_t j0 = 0; j0 < n; j0 += kAttendThreads) {
         const uint32_t j = j0 + t;
         if (j + 1 == n) {
@@ -201,9 +210,14 @@ __device__ void attend_head(const float* q_in, const float* k_in, const float* v
             float dot = 0.0f;
             for (uint32_t c0 = 0; c0 < units; c0 += kChunk) {
                 uint4 kv[kChunk];
+                if (j0 == 0 && c0 == 0) {
 #pragma unroll
-                for (uint32_t u = 0; u < kChunk; ++u)
-                    if (c0 + u < units) kv[u] = __ldg(k + c0 + u);
+                    for (uint32_t u = 0; u < kChunk; ++u) kv[u] = k0[u];
+                } else {
+#pragma unroll
+                    for (uint32_t u = 0; u < kChunk; ++u)
+                        if (c0 + u < units) kv[u] = __ldg(k + c0 + u);
+                }
 #pragma unroll
                 for (uint32_t u = 0; u < kChunk; ++u) {
                     if (c0 + u < units) {
@@ -231,25 +245,30 @@ __device__ void attend_head(const float* q_in, const float* k_in, const float* v
         den += e;
     }
     den = block_reduce_all(den, red, [](float a, float b) { return a + b; });
+    // Each position's probability once: the reference's score / sum.
+    for (uint32_t j = t; j < n; j += kAttendThreads) sc[j] = sc[j] / den;
+    __syncthreads();
     // Output: in segment g (dimensions 128 g .. 128 g + 127) lane covers
-    // dimensions 128 g + 4 lane .. + 3.
+    // dimensions 128 g + 4 lane .. + 3; sixteen positions' loads in flight
+    // per warp and round.
+    constexpr int kVals = 16;
     for (uint32_t g0 = 0; g0 < d; g0 += 128u) {
         const bool active = g0 + static_cast<uint32_t>(lane) * 4u < d;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t j0 = warp; j0 < n; j0 += 8u * kW) {
-            uint2 vv[8];
+        for (uint32_t j0 = warp; j0 < n; j0 += kVals * kW) {
+            uint2 vv[kVals];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < kVals; ++u) {
                 const uint32_t j = j0 + u * kW;
                 if (active && j + 1 < n)
                     vv[u] = __ldg(reinterpret_cast<const uint2*>(vc + ((first + j) % window) * row_stride + kh * d + g0) +
                                   lane);
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < kVals; ++u) {
                 const uint32_t j = j0 + u * kW;
                 if (active && j < n) {
-                    const float p = sc[j] / den;
+                    const float p = sc[j];
                     float2 a, b;
                     if (j + 1 == n) {
                         a = make_float2(vnew[g0 + lane * 4], vnew[g0 + lane * 4 + 1]);
@@ -278,7 +297,7 @@ __device__ void attend_head(const float* q_in, const float* k_in, const float* v
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(kAttendThreads)
+__global__ void __launch_bounds__(kAttendThreads, 1)
 attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
               const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, __half* __restrict__ kc,
               __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, const AttendShape sh,
@@ -452,7 +471,7 @@ __global__ void __launch_bounds__(kAttnBlockThreads, 1) attn_block_kernel(const 
         abort_sh = 0u;
     }
     __syncthreads();
-    // ---- entry: copies, RoPE rows, KV rows towards L2 ----
+    // ---- entry: copies ----
     if (warp == 0 && mine) {
         if (lane == 0) mbar_expect_tx(&bars[0], mine * 16u * static_cast<uint32_t>(rb_in));
         __syncwarp();
@@ -468,37 +487,48 @@ __global__ void __launch_bounds__(kAttnBlockThreads, 1) attn_block_kernel(const 
             bulk_copy_g2s(otiles + lane * c.pitch_o, a.wo + static_cast<uint64_t>(cta * 16u + lane) * rb_o,
                           static_cast<uint32_t>(rb_o), &bars[1]);
     }
-    const uint32_t pos = *a.pos_p, tag = pos * a.layers + a.layer + 1u;
-    if (head) {
-        for (uint32_t j = tid; j < sh.rh; j += kAttnBlockThreads) {
-            rope[j] = a.rope_cos[static_cast<uint64_t>(pos) * sh.rh + j];
-            rope[sh.rh + j] = a.rope_sin[static_cast<uint64_t>(pos) * sh.rh + j];
-        }
-        const uint32_t group = sh.qh / sh.kvh, kh = cta / group;
-        if (cta % group == 0) {
-            const uint32_t n = pos + 1 < sh.window ? pos + 1 : sh.window, first = pos + 1 - n;
-            const uint32_t lines = (d * 2u + 127u) / 128u;
-            const uint64_t row_stride = static_cast<uint64_t>(sh.kvh) * d;
-            for (uint32_t i = tid; i + lines < n * lines; i += kAttnBlockThreads) {
-                const uint64_t at = ((first + i / lines) % sh.window) * row_stride + kh * d + (i % lines) * 64u;
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(a.kc + at));
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(a.vc + at));
-            }
-        }
-    }
     // ---- qkv: h staged once, x' records ----
+    const uint32_t pos = *a.pos_p, tag = pos * a.layers + a.layer + 1u;
     const float resid = o_unit && tid < 16 ? __ldcg(a.hidden + cta * 16u + tid) : 0.0f;
     {
+        // The warp's superblocks of h (hidden <= 4096: two per warp) into
+        // registers, then this position's RoPE rows and the KV head's cached
+        // rows towards L2 (query-head CTAs) while they are in flight.
+        float v[2][8];
+#pragma unroll
+        for (uint32_t i = 0; i < 2; ++i) {
+            const uint32_t sb = warp + kAttnBlockWarps * i;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = sb < c.nsb_in ? __ldcg(a.hidden + sb * 256u + 32u * j + lane) : 0.0f;
+        }
+        if (head) {
+            for (uint32_t j = tid; j < sh.rh; j += kAttnBlockThreads) {
+                rope[j] = a.rope_cos[static_cast<uint64_t>(pos) * sh.rh + j];
+                rope[sh.rh + j] = a.rope_sin[static_cast<uint64_t>(pos) * sh.rh + j];
+            }
+            const uint32_t group = sh.qh / sh.kvh, kh = cta / group;
+            if (cta % group == 0) {
+                const uint32_t n = pos + 1 < sh.window ? pos + 1 : sh.window, first = pos + 1 - n;
+                const uint32_t lines = (d * 2u + 127u) / 128u;
+                const uint64_t row_stride = static_cast<uint64_t>(sh.kvh) * d;
+                for (uint32_t i = tid; i + lines < n * lines; i += kAttnBlockThreads) {
+                    const uint64_t at = ((first + i / lines) % sh.window) * row_stride + kh * d + (i % lines) * 64u;
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a.kc + at));
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a.vc + at));
+                }
+            }
+        }
         float ss = 0.0f;
-        for (uint32_t sb = warp; sb < c.nsb_in; sb += kAttnBlockWarps) {
-            float* st = reinterpret_cast<float*>(xrec + sb * kFragWords);
-            float v[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __ldcg(a.hidden + sb * 256u + 32u * j + lane);
+        for (uint32_t i = 0; i < 2; ++i) {
+            const uint32_t sb = warp + kAttnBlockWarps * i;
+            if (sb < c.nsb_in) {
+                float* st = reinterpret_cast<float*>(xrec + sb * kFragWords);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                ss = fmaf(v[j], v[j], ss);
-                st[32 * j + lane] = v[j];
+                for (int j = 0; j < 8; ++j) {
+                    ss = fmaf(v[i][j], v[i][j], ss);
+                    st[32 * j + lane] = v[i][j];
+                }
             }
         }
         ss = warp_sum(ss);
@@ -1164,7 +1194,8 @@ private:
         if (cfg_.attn_type != kQ4_K || rows % 16 || qd_ % 256 || rows / 16 < grid || H / 16 > grid ||
             cfg_.q_heads > grid)
             return;
-        if (qd_ / 256 > kAttnBlockWarps * kAttnMaxOutPerWarp || cfg_.layers > 255) return;
+        if (qd_ / 256 > kAttnBlockWarps * kAttnMaxOutPerWarp || H / 256 > 2 * kAttnBlockWarps || cfg_.layers > 255)
+            return;
         const AttnBlockLayout c = attn_block_layout(H, rows, static_cast<uint32_t>(qd_),
                                                     static_cast<uint32_t>(cfg_.head_dim), static_cast<uint32_t>(rh_),
                                                     static_cast<uint32_t>(window_), grid);
