@@ -526,6 +526,29 @@ public:
         return chain_plan_.grid;
     }
 
+    // A decoder's layer loop: its attention blocks and these MoE blocks in
+    // one chain launch (false when the layers do not take the chain kernel or
+    // the attention phase does not fit it).
+    bool attention_chain_fits(const ChainAttnDesc& att) const {
+        return chain_ok_ && !failed_ && chain_attention_smem(chain_plan_, att) <=
+                                             chain_plan_.smem - chain_tile_offset(chain_plan_);
+    }
+    void decode_layers_attention(size_t first, size_t count, float* hidden, const ChainAttnDesc& att,
+                                 cudaStream_t s) {
+        ensure_ok();
+        if (!chain_ok_) throw std::invalid_argument("the layers do not run the persistent chain kernel");
+        if (count == 0 || first >= cfg_.layers || count > cfg_.layers - first || !hidden)
+            throw std::invalid_argument("layer range and hidden state are required");
+        for (size_t l = first; l < first + count; ++l)
+            if (!resident_complete(l)) throw std::invalid_argument("layer weights were not uploaded");
+        DeviceScope scope(device_);
+        guard(launch_moe_chain(chain_plan_, devs_dev_, static_cast<uint32_t>(first), static_cast<uint32_t>(count), S_,
+                               C_, hidden, s ? s : stream_, nullptr, &att), "decode chain kernel with attention");
+        forward_calls_ += count;
+        hits_ += count * cfg_.top_k;
+        kernel_launches_ += 1;
+    }
+
     void decode_layers_host(size_t first, size_t count, const float* in, float* out) {
         ensure_ok();
         if (!in || !out) throw std::invalid_argument("hidden buffers are required");
@@ -982,6 +1005,29 @@ struct pokit_cuda_moe {
     explicit pokit_cuda_moe(const pokit_cuda_moe_config& c) : impl(c) {}
     pokit::MoeBackend impl;
 };
+
+namespace pokit {
+
+bool moe_attention_chain_fits(const pokit_cuda_moe* moe, const ChainAttnDesc& att) {
+    return moe && moe->impl.attention_chain_fits(att);
+}
+
+cudaError_t moe_decode_layers_attention(pokit_cuda_moe* moe, size_t first, size_t count, float* hidden,
+                                        const ChainAttnDesc& att, cudaStream_t stream, std::string* error) {
+    if (!moe) return cudaErrorInvalidValue;
+    try {
+        moe->impl.decode_layers_attention(first, count, hidden, att, stream);
+        return cudaSuccess;
+    } catch (const std::invalid_argument& e) {
+        if (error) *error = e.what();
+        return cudaErrorInvalidValue;
+    } catch (const std::exception& e) {
+        if (error) *error = e.what();
+        return cudaErrorUnknown;
+    }
+}
+
+}  // namespace pokit
 
 struct pokit_cuda_linear_backend {
     explicit pokit_cuda_linear_backend(int device) : impl(device) {}

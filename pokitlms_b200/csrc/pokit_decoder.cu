@@ -25,6 +25,7 @@
 // The token and position live in device memory, so a step is position-free
 // and runs as one CUDA graph replay (captured on first use).
 #include "../../include/pokit_cuda.h"
+#include "pokit_attention.cuh"
 #include "pokit_kernels.h"
 #include "pokit_mma.cuh"
 #include "pokit_quant.cuh"
@@ -49,19 +50,6 @@ constexpr uint32_t kStatusDecoderNonFinite = 1u;   // LM head produced NaN/Inf (
 constexpr uint32_t kMaxWindow = 8192;
 constexpr uint32_t kArgmaxCtas = 148;
 
-template <typename T, typename Op>
-__device__ __forceinline__ T block_reduce_all(T v, T* red, Op op) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    T r = red[0];
-    for (int w = 1; w < nw; ++w) r = op(r, red[w]);
-    return r;
-}
-
 // The token's embedding row, decoded exactly as dequantize_quantized_row.
 template <uint32_t T>
 __global__ void embed_kernel(const uint8_t* __restrict__ table, uint32_t cols, const uint32_t* __restrict__ seq,
@@ -82,227 +70,14 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, const float* __rest
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
 }
 
-// GQA decode attention of one query head over the ring's last min(pos + 1,
-// window) positions, oldest first (KvCache::attend, kv_cache.cpp:185-294):
-// scores = q . k * scale, softmax, out = sum_j (e_j / sum e) v_j.
-// Scores: each lane takes a whole position (its key row as 16-byte loads, all
-// in flight at once), 256 positions per pass.  Output: warp w sums positions
-// w, w + 8, ... for four dimensions per lane, eight positions' loads in flight
-// per round; the eight warps' partial sums are added in warp order.
-constexpr uint32_t kAttendThreads = 256;
-constexpr uint32_t kAttendMaxDim = 256;
-
-// The CTA first forms its own query and its KV head's new key and value from
-// the projected q|k|v (per-head RMSNorm with q_norm / k_norm, rotate-half
-// RoPE, qwen3_moe_runner.cpp:141-172, 614-636; key and value rounded to FP16
-// as the ring stores them, kv_cache.cpp:20-44); the group's first CTA writes
-// them to the ring at slot position % window, and every CTA uses its own copy
-// for the newest position (no CTA reads the slot being written).
-__device__ __forceinline__ float head_rms_scale(float x, uint32_t d, float eps, float* red) {
-    float v = x * x;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float total = 0.0f;
-    for (uint32_t w = 0; w < (d + 31) / 32; ++w) total += red[w];
-    return 1.0f / sqrtf(total / static_cast<float>(d) + eps);
-}
-
-// Geometry of one attention layer's projected [q (| gate) per head | k | v].
-struct AttendShape {
-    uint32_t qh, kvh, d;       // query heads, KV heads, head dimension (<= kAttendMaxDim)
-    uint32_t q_stride;         // floats per query head in the projection: d, or 2 d with a gate
-    uint32_t gated;            // Qwen3.5: out *= sigmoid(gate), gate = the head's second d floats
-    uint32_t rh;               // rotary half: dimensions [0, 2 rh) rotate (rh = d / 2: all)
-    uint32_t window;
-    float eps, scale;
-};
-
-__device__ __forceinline__ float sigmoid_signed(float v) {
-    if (v >= 0.0f) return 1.0f / (1.0f + expf(-v));
-    const float e = expf(v);
-    return e / (1.0f + e);
-}
-
-// One query head of the layer: q_in / k_in / v_in are the head's projected
-// query, its KV head's new key and value (d floats each, global or shared
-// memory), gate_in the head's gate (Qwen3.5) or null, rope_cos / rope_sin the
-// rotary half's table rows of this position; writes the head's d outputs to
-// out.  sc: window floats of dynamic shared memory.  Every thread of the CTA
-// calls it.
-__device__ void attend_head(const float* q_in, const float* k_in, const float* v_in, const float* gate_in,
-                            const float* __restrict__ q_norm, const float* __restrict__ k_norm,
-                            const float* rope_cos, const float* rope_sin,
-                            __half* __restrict__ kc, __half* __restrict__ vc, uint32_t pos, const AttendShape& sh,
-                            uint32_t h, float* sc, float* out) {
-    __shared__ float red[32];
-    __shared__ __align__(16) float qs[kAttendMaxDim];
-    __shared__ __align__(16) float kn[kAttendMaxDim];
-    __shared__ __align__(16) float knew[kAttendMaxDim];
-    __shared__ __align__(16) float vnew[kAttendMaxDim];
-    __shared__ __align__(16) float part[kAttendThreads / 32][kAttendMaxDim];
-    const uint32_t d = sh.d, window = sh.window, qh = sh.qh, kvh = sh.kvh, rh = sh.rh;
-    const uint32_t t = threadIdx.x;
-    const uint32_t group = qh / kvh, kh = h / group;
-    const uint32_t n = pos + 1 < window ? pos + 1 : window, first = pos + 1 - n;
-    const int lane = t & 31, warp = t >> 5;
-    constexpr int kW = kAttendThreads / 32;
-    const uint64_t row_stride = static_cast<uint64_t>(kvh) * d;
-    const bool dim = t < d;
-    const uint32_t units = d / 8;                         // 16-byte units of a key row
-    constexpr uint32_t kChunk = 16;                       // units loaded at once (128 dimensions)
-    // The first chunk of this thread's cached key (position t of the window,
-    // first pass) is requested before the norms: it does not depend on them.
-    uint4 k0[kChunk];
-    if (t + 1 < n) {
-        const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + t) % window) * row_stride + kh * d);
-#pragma unroll
-        for (uint32_t u = 0; u < kChunk; ++u)
-            if (u < units) k0[u] = __ldg(k + u);
-    }
-    const float xq = dim ? q_in[t] : 0.0f;
-    const float xk = dim ? k_in[t] : 0.0f;
-    const float sq = head_rms_scale(xq, d, sh.eps, red);
-    const float sk = head_rms_scale(xk, d, sh.eps, red);
-    if (dim) {
-        qs[t] = __fmul_rn(__fmul_rn(xq, sq), q_norm[t]);
-        kn[t] = __fmul_rn(__fmul_rn(xk, sk), k_norm[t]);
-    }
-    __syncthreads();
-    float rq = 0.0f, rk = 0.0f;
-    if (dim) {
-        if (t < 2u * rh) {
-            const uint32_t j = t < rh ? t : t - rh;
-            const float c = rope_cos[j], s = rope_sin[j];
-            const float aq = qs[j], bq = qs[j + rh], ak = kn[j], bk = kn[j + rh];
-            rq = t < rh ? __fsub_rn(__fmul_rn(aq, c), __fmul_rn(bq, s)) : __fadd_rn(__fmul_rn(bq, c), __fmul_rn(aq, s));
-            rk = t < rh ? __fsub_rn(__fmul_rn(ak, c), __fmul_rn(bk, s)) : __fadd_rn(__fmul_rn(bk, c), __fmul_rn(ak, s));
-        } else {
-            rq = qs[t];
-            rk = kn[t];
-        }
-    }
-    __syncthreads();
-    if (dim) {
-        qs[t] = rq;
-        const __half hk = __float2half_rn(rk);
-        const __half hv = __float2half_rn(v_in[t]);
-        knew[t] = __half2float(hk);
-        vnew[t] = __half2float(hv);
-        if (h % group == 0) {
-            const uint64_t at = static_cast<uint64_t>(pos % window) * row_stride + kh * d + t;
-            kc[at] = hk;
-            vc[at] = hv;
-        }
-    }
-    __syncthreads();
-    for (uint32_t j0 = 0; j0 < n; j0 += kAttendThreads) {
-        const uint32_t j = j0 + t;
-        if (j + 1 == n) {
-            float dot = 0.0f;
-            for (uint32_t e = 0; e < d; ++e) dot = fmaf(qs[e], knew[e], dot);
-            sc[j] = dot * sh.scale;
-        } else if (j < n) {
-            const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + j) % window) * row_stride + kh * d);
-            float dot = 0.0f;
-            for (uint32_t c0 = 0; c0 < units; c0 += kChunk) {
-                uint4 kv[kChunk];
-                if (j0 == 0 && c0 == 0) {
-#pragma unroll
-                    for (uint32_t u = 0; u < kChunk; ++u) kv[u] = k0[u];
-                } else {
-#pragma unroll
-                    for (uint32_t u = 0; u < kChunk; ++u)
-                        if (c0 + u < units) kv[u] = __ldg(k + c0 + u);
-                }
-#pragma unroll
-                for (uint32_t u = 0; u < kChunk; ++u) {
-                    if (c0 + u < units) {
-                        const __half2* hp = reinterpret_cast<const __half2*>(&kv[u]);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 f = __half22float2(hp[e]);
-                            dot = fmaf(qs[(c0 + u) * 8 + 2 * e], f.x, dot);
-                            dot = fmaf(qs[(c0 + u) * 8 + 2 * e + 1], f.y, dot);
-                        }
-                    }
-                }
-            }
-            sc[j] = dot * sh.scale;
-        }
-    }
-    __syncthreads();
-    float m = -INFINITY;
-    for (uint32_t j = t; j < n; j += kAttendThreads) m = fmaxf(m, sc[j]);
-    m = block_reduce_all(m, red, [](float a, float b) { return fmaxf(a, b); });
-    float den = 0.0f;
-    for (uint32_t j = t; j < n; j += kAttendThreads) {
-        const float e = expf(sc[j] - m);
-        sc[j] = e;
-        den += e;
-    }
-    den = block_reduce_all(den, red, [](float a, float b) { return a + b; });
-    // Each position's probability once: the reference's score / sum.
-    for (uint32_t j = t; j < n; j += kAttendThreads) sc[j] = sc[j] / den;
-    __syncthreads();
-    // Output: in segment g (dimensions 128 g .. 128 g + 127) lane covers
-    // dimensions 128 g + 4 lane .. + 3; sixteen positions' loads in flight
-    // per warp and round.
-    constexpr int kVals = 16;
-    for (uint32_t g0 = 0; g0 < d; g0 += 128u) {
-        const bool active = g0 + static_cast<uint32_t>(lane) * 4u < d;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (uint32_t j0 = warp; j0 < n; j0 += kVals * kW) {
-            uint2 vv[kVals];
-#pragma unroll
-            for (int u = 0; u < kVals; ++u) {
-                const uint32_t j = j0 + u * kW;
-                if (active && j + 1 < n)
-                    vv[u] = __ldg(reinterpret_cast<const uint2*>(vc + ((first + j) % window) * row_stride + kh * d + g0) +
-                                  lane);
-            }
-#pragma unroll
-            for (int u = 0; u < kVals; ++u) {
-                const uint32_t j = j0 + u * kW;
-                if (active && j < n) {
-                    const float p = sc[j];
-                    float2 a, b;
-                    if (j + 1 == n) {
-                        a = make_float2(vnew[g0 + lane * 4], vnew[g0 + lane * 4 + 1]);
-                        b = make_float2(vnew[g0 + lane * 4 + 2], vnew[g0 + lane * 4 + 3]);
-                    } else {
-                        a = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].x));
-                        b = __half22float2(*reinterpret_cast<const __half2*>(&vv[u].y));
-                    }
-                    acc.x = fmaf(p, a.x, acc.x);
-                    acc.y = fmaf(p, a.y, acc.y);
-                    acc.z = fmaf(p, b.x, acc.z);
-                    acc.w = fmaf(p, b.y, acc.w);
-                }
-            }
-        }
-        if (active) *reinterpret_cast<float4*>(&part[warp][g0 + lane * 4]) = acc;
-    }
-    __syncthreads();
-    if (t < d) {
-        float o = part[0][t];
-        for (int w = 1; w < kW; ++w) o += part[w][t];
-        // qwen35_runner.cpp:577-580: the gated output attended * sigmoid(gate).
-        if (gate_in) o = __fmul_rn(o, sigmoid_signed(gate_in[t]));
-        out[t] = o;
-    }
-    __syncthreads();
-}
-
 __global__ void __launch_bounds__(kAttendThreads, 1)
 attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, const float* __restrict__ k_norm,
               const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, __half* __restrict__ kc,
               __half* __restrict__ vc, const uint32_t* __restrict__ pos_p, const AttendShape sh,
               float* __restrict__ out) {
-    extern __shared__ float sc[];
+    extern __shared__ __align__(16) float dyn[];
+    float* scratch = dyn;
+    float* sc = dyn + attend_scratch_floats(sh.d, kAttendThreads / 32);
     // The position counter changes only at the end of a token step, so it and
     // the cached keys and values of earlier positions are read before waiting
     // for the Q/K/V projection: the first CTA of each query group pulls its
@@ -325,14 +100,14 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
     attend_head(qkv + h * sh.q_stride, qkv + kbase + kh * d, qkv + vbase + kh * d,
                 sh.gated ? qkv + h * sh.q_stride + d : nullptr, q_norm, k_norm,
                 rope_cos + static_cast<uint64_t>(pos) * sh.rh, rope_sin + static_cast<uint64_t>(pos) * sh.rh, kc, vc,
-                pos, sh, h, sc, out + h * d);
+                pos, sh, h, sc, scratch, out + h * d);
 }
 
 // ---------------------------------------------------------------------------
 // The attention block of one layer in one cooperative launch (Q4_K
 // projections): rms_norm(attn_norm) -> the [q (| gate) | k | v] matvec ->
 // attention per query head -> the output projection added into the residual.
-// Steps and who runs them (G CTAs of 256 threads, one per SM):
+// Steps and who runs them (G CTAs, one per SM):
 //   entry   every CTA bulk-copies its Q/K/V row blocks (16 rows each: blocks
 //           c, c + G, ...) and, for c < H/16, its 16 rows of attn_output into
 //           shared memory (rows padded by 16 bytes so the fragment reads
@@ -354,311 +129,20 @@ attend_kernel(const float* __restrict__ qkv, const float* __restrict__ q_norm, c
 // (unique within a sequence; the words are cleared with the decode state), so
 // words of another layer or step never match.  Waits are bounded (~2 s); a
 // timeout sets the status word and the CTA drains its copies and leaves.
-struct AttnBlockArgs {
-    const uint8_t* wqkv;             // Q4_K [rows][hidden]: q (| gate), k, v
-    const uint8_t* wo;               // Q4_K [hidden][q_heads * d]
-    const float* attn_norm;
-    const float* q_norm;
-    const float* k_norm;
-    const float* rope_cos;           // [context][rotary half]
-    const float* rope_sin;
-    __half* kc;                      // this layer's rings
-    __half* vc;
-    const uint32_t* pos_p;
-    AttendShape sh;
-    float* hidden;
-    unsigned long long* qkv_ll;      // [rows] words
-    unsigned long long* att_ll;      // [q_heads * d] words
-    uint32_t* status;                // timeout flag
-    uint32_t H, rows, qd, layer, layers;
-    float eps;
-};
-
-constexpr uint32_t kAttnBlockThreads = 256, kAttnBlockWarps = 8;
-constexpr uint32_t kAttnStatusTimeout = 1u;
-constexpr uint32_t kAttnMaxOutPerWarp = 2;          // output superblocks per warp: q_heads * d <= 4096
-
-struct AttnBlockLayout {
-    uint32_t nsb_in, nsb_o, pitch_in, pitch_o, blocks_max;
-    uint32_t qtiles, otiles, xrec, arec, qpart, opart, stage, rope, sc, total;
-};
-
-__host__ __device__ inline AttnBlockLayout attn_block_layout(uint32_t H, uint32_t rows, uint32_t qd, uint32_t d,
-                                                             uint32_t rh, uint32_t window, uint32_t grid) {
-    AttnBlockLayout c{};
-    c.nsb_in = H / 256u;
-    c.nsb_o = qd / 256u;
-    c.pitch_in = c.nsb_in * 144u + 16u;
-    c.pitch_o = c.nsb_o * 144u + 16u;
-    c.blocks_max = (rows / 16u + grid - 1u) / grid;
-    uint32_t off = 0;
-    c.qtiles = off; off += c.blocks_max * 16u * c.pitch_in;
-    off = (off + 127u) & ~127u;
-    c.otiles = off; off += 16u * c.pitch_o;
-    off = (off + 127u) & ~127u;
-    c.xrec = off; off += c.nsb_in * kFragWords * 4u;
-    c.arec = off; off += c.nsb_o * kFragWords * 4u;
-    c.qpart = off; off += c.blocks_max * c.nsb_in * 16u * 4u;
-    c.opart = off; off += c.nsb_o * 16u * 4u;
-    c.stage = off; off += 5u * d * 4u;                   // query, gate, key, value, output of one head
-    c.rope = off; off += 2u * rh * 4u;                   // this position's cos and sin rows
-    c.sc = off; off += window * 4u;
-    c.total = (off + 127u) & ~127u;
-    return c;
-}
-
-// Polls the words src[i] (where use[i]) until every tag is `tag`; false on a
-// timeout (or another CTA's).
-template <int N>
-__device__ __forceinline__ bool await_words(const unsigned long long* const (&src)[N], unsigned long long (&v)[N],
-                                            const bool (&use)[N], uint32_t tag, uint32_t* status) {
-    long long t0 = 0;
-    for (uint32_t polls = 0;; ++polls) {
-        bool ready = true;
-#pragma unroll
-        for (int i = 0; i < N; ++i) {
-            if (use[i] && static_cast<uint32_t>(v[i] >> 32) != tag) {
-                ready = false;
-                unsigned long long w;
-                asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(src[i]) : "memory");
-                v[i] = w;
-            }
-        }
-        if (ready) return true;
-        if (polls == 0) t0 = clock64();
-        if ((polls & 63u) == 63u) {
-            uint32_t st;
-            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(st) : "l"(status) : "memory");
-            if (st || clock64() - t0 > 4000000000LL) {
-                atomicOr(status, kAttnStatusTimeout);
-                return false;
-            }
-        }
-    }
-}
-
-__device__ __forceinline__ void put_word(unsigned long long* p, uint32_t tag, float v) {
-    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-
 __global__ void __launch_bounds__(kAttnBlockThreads, 1) attn_block_kernel(const __grid_constant__ AttnBlockArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bars[2];
     __shared__ float red[kAttnBlockWarps];
     __shared__ uint32_t abort_sh;
-    const AttendShape& sh = a.sh;
-    const uint32_t G = gridDim.x, cta = blockIdx.x, tid = threadIdx.x, d = sh.d;
-    const int lane = tid & 31, warp = tid >> 5, g = lane >> 2;
-    const AttnBlockLayout c = attn_block_layout(a.H, a.rows, a.qd, d, sh.rh, sh.window, G);
-    const uint32_t nblk = a.rows / 16u, units = a.H / 16u;
-    const uint32_t mine = cta < nblk ? (nblk - cta + G - 1u) / G : 0u;
-    const bool o_unit = cta < units, head = cta < sh.qh;
-    const uint64_t rb_in = c.nsb_in * 144u, rb_o = c.nsb_o * 144u;
-    uint8_t* qtiles = smem + c.qtiles;
-    uint8_t* otiles = smem + c.otiles;
-    uint32_t* xrec = reinterpret_cast<uint32_t*>(smem + c.xrec);
-    uint32_t* arec = reinterpret_cast<uint32_t*>(smem + c.arec);
-    float* qpart = reinterpret_cast<float*>(smem + c.qpart);
-    float* opart = reinterpret_cast<float*>(smem + c.opart);
-    float* stage = reinterpret_cast<float*>(smem + c.stage);
-    float* rope = reinterpret_cast<float*>(smem + c.rope);
-    float* sc = reinterpret_cast<float*>(smem + c.sc);
-    if (tid == 0) {
+    if (threadIdx.x == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
         mbar_fence_init();
         abort_sh = 0u;
     }
     __syncthreads();
-    // ---- entry: copies ----
-    if (warp == 0 && mine) {
-        if (lane == 0) mbar_expect_tx(&bars[0], mine * 16u * static_cast<uint32_t>(rb_in));
-        __syncwarp();
-        if (lane < 16)
-            for (uint32_t i = 0; i < mine; ++i)
-                bulk_copy_g2s(qtiles + (i * 16u + lane) * c.pitch_in,
-                              a.wqkv + static_cast<uint64_t>((cta + G * i) * 16u + lane) * rb_in,
-                              static_cast<uint32_t>(rb_in), &bars[0]);
-    } else if (warp == 1 && o_unit) {
-        if (lane == 0) mbar_expect_tx(&bars[1], 16u * static_cast<uint32_t>(rb_o));
-        __syncwarp();
-        if (lane < 16)
-            bulk_copy_g2s(otiles + lane * c.pitch_o, a.wo + static_cast<uint64_t>(cta * 16u + lane) * rb_o,
-                          static_cast<uint32_t>(rb_o), &bars[1]);
-    }
-    // ---- qkv: h staged once, x' records ----
-    const uint32_t pos = *a.pos_p, tag = pos * a.layers + a.layer + 1u;
-    const float resid = o_unit && tid < 16 ? __ldcg(a.hidden + cta * 16u + tid) : 0.0f;
-    {
-        // The warp's superblocks of h (hidden <= 4096: two per warp) into
-        // registers, then this position's RoPE rows and the KV head's cached
-        // rows towards L2 (query-head CTAs) while they are in flight.
-        float v[2][8];
-#pragma unroll
-        for (uint32_t i = 0; i < 2; ++i) {
-            const uint32_t sb = warp + kAttnBlockWarps * i;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[i][j] = sb < c.nsb_in ? __ldcg(a.hidden + sb * 256u + 32u * j + lane) : 0.0f;
-        }
-        if (head) {
-            for (uint32_t j = tid; j < sh.rh; j += kAttnBlockThreads) {
-                rope[j] = a.rope_cos[static_cast<uint64_t>(pos) * sh.rh + j];
-                rope[sh.rh + j] = a.rope_sin[static_cast<uint64_t>(pos) * sh.rh + j];
-            }
-            const uint32_t group = sh.qh / sh.kvh, kh = cta / group;
-            if (cta % group == 0) {
-                const uint32_t n = pos + 1 < sh.window ? pos + 1 : sh.window, first = pos + 1 - n;
-                const uint32_t lines = (d * 2u + 127u) / 128u;
-                const uint64_t row_stride = static_cast<uint64_t>(sh.kvh) * d;
-                for (uint32_t i = tid; i + lines < n * lines; i += kAttnBlockThreads) {
-                    const uint64_t at = ((first + i / lines) % sh.window) * row_stride + kh * d + (i % lines) * 64u;
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a.kc + at));
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a.vc + at));
-                }
-            }
-        }
-        float ss = 0.0f;
-#pragma unroll
-        for (uint32_t i = 0; i < 2; ++i) {
-            const uint32_t sb = warp + kAttnBlockWarps * i;
-            if (sb < c.nsb_in) {
-                float* st = reinterpret_cast<float*>(xrec + sb * kFragWords);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    ss = fmaf(v[i][j], v[i][j], ss);
-                    st[32 * j + lane] = v[i][j];
-                }
-            }
-        }
-        ss = warp_sum(ss);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        float total = 0.0f;
-        for (uint32_t i = 0; i < kAttnBlockWarps; ++i) total += red[i];
-        const float scale = 1.0f / sqrtf(total / static_cast<float>(a.H) + a.eps);
-        for (uint32_t sb = warp; sb < c.nsb_in; sb += kAttnBlockWarps) {
-            float* st = reinterpret_cast<float*>(xrec + sb * kFragWords);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const uint32_t col = sb * 256u + 32u * j + lane;
-                st[32 * j + lane] = __fmul_rn(__fmul_rn(st[32 * j + lane], scale), a.attn_norm[col]);
-            }
-            __syncwarp();
-            q4k_frag_superblock(st, xrec + sb * kFragWords, lane);
-        }
-    }
-    __syncthreads();
-    // ---- qkv: multiply, publish ----
-    if (mine) {
-        if (!mbar_wait(&bars[0], 0)) {
-            if (lane == 0) { atomicOr(a.status, kAttnStatusTimeout); abort_sh = 1u; }
-            mbar_wait(&bars[0], 0);
-        }
-        for (uint32_t task = warp; task < mine * c.nsb_in; task += kAttnBlockWarps) {
-            const uint32_t i = task / c.nsb_in, sb = task % c.nsb_in;
-            const uint8_t* t0 = qtiles + (i * 16u) * c.pitch_in + sb * 144u;
-            float a0 = 0.0f, a1 = 0.0f;
-            q4k_mma_superblock(t0 + g * c.pitch_in, t0 + (g + 8) * c.pitch_in, xrec + sb * kFragWords, a0, a1);
-            a0 = quad_sum(a0);
-            a1 = quad_sum(a1);
-            if ((lane & 3) == 0) {
-                qpart[(i * c.nsb_in + sb) * 16u + g] = a0;
-                qpart[(i * c.nsb_in + sb) * 16u + g + 8] = a1;
-            }
-        }
-        __syncthreads();
-        for (uint32_t t = tid; t < mine * 16u; t += kAttnBlockThreads) {
-            const uint32_t i = t / 16u, r = t % 16u;
-            float v = qpart[(i * c.nsb_in) * 16u + r];
-            for (uint32_t sb = 1; sb < c.nsb_in; ++sb) v += qpart[(i * c.nsb_in + sb) * 16u + r];
-            put_word(a.qkv_ll + (cta + G * i) * 16u + r, tag, v);
-        }
-    }
-    // ---- attend ----
-    if (head) {
-        const uint32_t h = cta, kh = h / (sh.qh / sh.kvh);
-        const uint32_t kbase = sh.qh * sh.q_stride, vbase = kbase + sh.kvh * d;
-        float* qin = stage;
-        float* gin = stage + d;
-        float* kin = stage + 2 * d;
-        float* vin = stage + 3 * d;
-        float* aout = stage + 4 * d;
-        if (tid < d) {
-            const unsigned long long* src[4] = {a.qkv_ll + h * sh.q_stride + tid, a.qkv_ll + h * sh.q_stride + d + tid,
-                                                a.qkv_ll + kbase + kh * d + tid, a.qkv_ll + vbase + kh * d + tid};
-            unsigned long long v[4] = {0ull, 0ull, 0ull, 0ull};
-            const bool use[4] = {true, sh.gated != 0u, true, true};
-            if (!await_words<4>(src, v, use, tag, a.status)) abort_sh = 1u;
-            qin[tid] = __uint_as_float(static_cast<uint32_t>(v[0]));
-            gin[tid] = __uint_as_float(static_cast<uint32_t>(v[1]));
-            kin[tid] = __uint_as_float(static_cast<uint32_t>(v[2]));
-            vin[tid] = __uint_as_float(static_cast<uint32_t>(v[3]));
-        }
-        __syncthreads();
-        if (!abort_sh) {
-            attend_head(qin, kin, vin, sh.gated ? gin : nullptr, a.q_norm, a.k_norm, rope, rope + sh.rh, a.kc, a.vc,
-                        pos, sh, h, sc, aout);
-            if (tid < d) put_word(a.att_ll + h * d + tid, tag, aout[tid]);
-        }
-    }
-    // ---- o ----
-    if (o_unit) {
-        // All of the warp's output words in flight at once, then its records.
-        const uint32_t first_sb = warp, nmine = first_sb < c.nsb_o ? (c.nsb_o - first_sb + kAttnBlockWarps - 1) /
-                                                                     kAttnBlockWarps : 0u;
-        if (nmine && !abort_sh) {
-            const unsigned long long* src[8 * kAttnMaxOutPerWarp];
-            unsigned long long v[8 * kAttnMaxOutPerWarp];
-            bool use[8 * kAttnMaxOutPerWarp];
-#pragma unroll
-            for (uint32_t i = 0; i < kAttnMaxOutPerWarp; ++i)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t sb = first_sb + i * kAttnBlockWarps;
-                    use[i * 8 + j] = i < nmine;
-                    src[i * 8 + j] = a.att_ll + (i < nmine ? sb : first_sb) * 256u + 32u * j + lane;
-                    v[i * 8 + j] = 0ull;
-                }
-            if (!await_words<8 * kAttnMaxOutPerWarp>(src, v, use, tag, a.status)) abort_sh = 1u;
-#pragma unroll
-            for (uint32_t i = 0; i < kAttnMaxOutPerWarp; ++i) {
-                if (i < nmine) {
-                    const uint32_t sb = first_sb + i * kAttnBlockWarps;
-                    float* st = reinterpret_cast<float*>(arec + sb * kFragWords);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) st[32 * j + lane] = __uint_as_float(static_cast<uint32_t>(v[i * 8 + j]));
-                    __syncwarp();
-                    q4k_frag_superblock(st, arec + sb * kFragWords, lane);
-                }
-            }
-        }
-        __syncthreads();
-        if (!mbar_wait(&bars[1], 0)) {
-            if (lane == 0) { atomicOr(a.status, kAttnStatusTimeout); abort_sh = 1u; }
-            mbar_wait(&bars[1], 0);
-        }
-        __syncthreads();
-        if (!abort_sh) {
-            for (uint32_t sb = warp; sb < c.nsb_o; sb += kAttnBlockWarps) {
-                float a0 = 0.0f, a1 = 0.0f;
-                const uint8_t* t0 = otiles + sb * 144u;
-                q4k_mma_superblock(t0 + g * c.pitch_o, t0 + (g + 8) * c.pitch_o, arec + sb * kFragWords, a0, a1);
-                a0 = quad_sum(a0);
-                a1 = quad_sum(a1);
-                if ((lane & 3) == 0) {
-                    opart[sb * 16u + g] = a0;
-                    opart[sb * 16u + g + 8] = a1;
-                }
-            }
-            __syncthreads();
-            if (tid < 16) {
-                float v = opart[tid];
-                for (uint32_t sb = 1; sb < c.nsb_o; ++sb) v += opart[sb * 16u + tid];
-                a.hidden[cta * 16u + tid] = resid + v;
-            }
-        }
-    }
+    const AttnPhaseCtx x{smem, bars, 0u, &abort_sh, red};
+    attention_phase(a, x, nullptr, 0u);
 }
 
 // Greedy sampling (qwen3_moe_runner.cpp:320-333): the first maximum of the
@@ -1177,8 +661,12 @@ private:
         check(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
         check(cudaEventCreateWithFlags(&join_, cudaEventDisableTiming), "cudaEventCreate");
         check(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   static_cast<int>(window_ * 4)), "attend smem");
+                                   static_cast<int>(attend_smem_bytes())), "attend smem");
         plan_attn_block();
+    }
+
+    size_t attend_smem_bytes() const {
+        return (attend_scratch_floats(static_cast<uint32_t>(cfg_.head_dim), kAttendThreads / 32) + window_) * 4;
     }
 
     // The fused attention block serves Q4_K projections when every CTA owns
@@ -1198,7 +686,7 @@ private:
             return;
         const AttnBlockLayout c = attn_block_layout(H, rows, static_cast<uint32_t>(qd_),
                                                     static_cast<uint32_t>(cfg_.head_dim), static_cast<uint32_t>(rh_),
-                                                    static_cast<uint32_t>(window_), grid);
+                                                    static_cast<uint32_t>(window_), grid, kAttnBlockWarps);
         if (c.total > 200u * 1024u) return;
         if (cudaFuncSetAttribute(attn_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(c.total)) != cudaSuccess) {
@@ -1211,11 +699,58 @@ private:
             cudaGetLastError();
             return;
         }
-        attn_words_ = rows + qd_;
+        attn_words_ = rows + qd_ + cfg_.hidden;
         check(cudaMalloc(&attn_ll_, attn_words_ * 8), "cudaMalloc(attention words)");
         check(cudaMemset(attn_ll_, 0, attn_words_ * 8), "cudaMemset(attention words)");
         attn_grid_ = grid;
         attn_smem_ = c.total;
+        plan_layer_chain();
+    }
+
+    // The whole layer loop as one chain launch (attention phase + MoE block
+    // per layer) when every layer is a full-attention layer whose tensors sit
+    // at one stride and the MoE handle's layers take the chain kernel
+    // (POKIT_CUDA_FUSED_LAYERS=0 turns it off).
+    void plan_layer_chain() {
+        const char* env = std::getenv("POKIT_CUDA_FUSED_LAYERS");
+        if ((env && env[0] == '0') || hybrid_) return;
+        ChainAttnDesc d{};
+        const uint32_t ts[5] = {POKIT_CUDA_DEC_ATTN_Q, POKIT_CUDA_DEC_ATTN_OUTPUT, POKIT_CUDA_DEC_ATTN_NORM,
+                                POKIT_CUDA_DEC_ATTN_Q_NORM, POKIT_CUDA_DEC_ATTN_K_NORM};
+        const uint64_t stride = cfg_.layers > 1 ? off_[kTensors + ts[0]] - off_[ts[0]] : 0;
+        for (size_t l = 0; l < cfg_.layers; ++l)
+            for (uint32_t t : ts)
+                if (off_[l * kTensors + t] != off_[t] + l * stride) return;
+        d.wqkv = tensor_ptr(0, POKIT_CUDA_DEC_ATTN_Q);
+        d.wo = tensor_ptr(0, POKIT_CUDA_DEC_ATTN_OUTPUT);
+        d.attn_norm = reinterpret_cast<const float*>(tensor_ptr(0, POKIT_CUDA_DEC_ATTN_NORM));
+        d.q_norm = reinterpret_cast<const float*>(tensor_ptr(0, POKIT_CUDA_DEC_ATTN_Q_NORM));
+        d.k_norm = reinterpret_cast<const float*>(tensor_ptr(0, POKIT_CUDA_DEC_ATTN_K_NORM));
+        d.w_stride = stride;
+        d.rope_cos = rope_;
+        d.rope_sin = rope_ + cfg_.context * rh_;
+        d.kc = kcache_;
+        d.vc = vcache_;
+        d.kv_stride = static_cast<uint64_t>(window_) * kd_;
+        d.pos = pos_;
+        d.q_heads = static_cast<uint32_t>(cfg_.q_heads);
+        d.kv_heads = static_cast<uint32_t>(cfg_.kv_heads);
+        d.head_dim = static_cast<uint32_t>(cfg_.head_dim);
+        d.q_stride = d.head_dim;
+        d.gated = 0;
+        d.rotary_half = static_cast<uint32_t>(rh_);
+        d.window = static_cast<uint32_t>(window_);
+        d.eps = cfg_.rms_epsilon;
+        d.scale = 1.0f / std::sqrt(static_cast<float>(cfg_.head_dim));
+        d.rows = static_cast<uint32_t>(qrows_ + 2 * kd_);
+        d.qkv_words = attn_ll_;
+        d.att_words = attn_ll_ + d.rows;
+        d.hidden_words = attn_ll_ + d.rows + qd_;
+        d.status = status_ + 2;
+        d.layers_total = static_cast<uint32_t>(cfg_.layers);
+        if (!moe_attention_chain_fits(moe_, d)) return;
+        layer_chain_ = d;
+        fused_layers_ = true;
     }
 
     cudaError_t launch_attn_block(size_t l, cudaStream_t s) {
@@ -1323,7 +858,19 @@ private:
         uint64_t n = 0;
         cudaError_t e = embed(s);
         ++n;
-        for (size_t l = 0; l < cfg_.layers && e == cudaSuccess; ++l) {
+        if (fused_layers_ && e == cudaSuccess) {
+            std::string err;
+            pokit_cuda_moe_stats before{}, after{};
+            pokit_cuda_moe_get_stats(moe_, &before);
+            e = moe_decode_layers_attention(moe_, 0, cfg_.layers, hidden_, layer_chain_, s, &err);
+            if (e != cudaSuccess) {
+                moe_error_ = err;
+                return e;
+            }
+            pokit_cuda_moe_get_stats(moe_, &after);
+            n += after.kernel_launches - before.kernel_launches;
+        }
+        for (size_t l = 0; l < cfg_.layers && e == cudaSuccess && !fused_layers_; ++l) {
             const auto P = [&](uint32_t t) { return tensor_ptr(l, t); };
             const auto F = [&](uint32_t t) { return reinterpret_cast<const float*>(tensor_ptr(l, t)); };
             if (attention_layer(l) && attn_grid_) {
@@ -1339,11 +886,11 @@ private:
                 const float* rc = rope_;
                 const float* rs = rope_ + cfg_.context * rh_;
                 if (pdl_) {
-                    e = launch_dependent(attend_kernel, qh, kAttendThreads, win * 4, s, qkv_, qn, kn, rc, rs,
+                    e = launch_dependent(attend_kernel, qh, kAttendThreads, attend_smem_bytes(), s, qkv_, qn, kn, rc, rs,
                                          kcache_ + kv_off, vcache_ + kv_off, pos_, ash, att_);
                     if (e != cudaSuccess) break;
                 } else {
-                    attend_kernel<<<qh, kAttendThreads, win * 4, s>>>(qkv_, qn, kn, rc, rs, kcache_ + kv_off,
+                    attend_kernel<<<qh, kAttendThreads, attend_smem_bytes(), s>>>(qkv_, qn, kn, rc, rs, kcache_ + kv_off,
                                                                       vcache_ + kv_off, pos_, ash, att_);
                 }
                 e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
@@ -1529,8 +1076,10 @@ private:
         const char* v = std::getenv("POKIT_CUDA_PDL");
         return !(v && v[0] == '0');
     }();
-    unsigned long long* attn_ll_ = nullptr;   // fused attention block: Q/K/V words, then output words
+    unsigned long long* attn_ll_ = nullptr;   // fused attention: Q/K/V words, output words, hidden words
     uint64_t attn_words_ = 0;
+    bool fused_layers_ = false;               // the layer loop as one chain launch
+    ChainAttnDesc layer_chain_{};
     uint32_t attn_grid_ = 0;                   // 0: the three-kernel attention path
     size_t attn_smem_ = 0;
     AttendShape ash_{};

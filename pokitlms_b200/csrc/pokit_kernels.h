@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace pokit {
 
 int device_sm_count();
@@ -234,9 +236,48 @@ bool moe_chain_plan(const MoeLayerDev* layers, uint32_t n, ChainPlan* plan);
 // published, act wait done, down records built, down products combined,
 // router partials published.
 constexpr uint32_t kChainTraceStamps = 16;
+// A decoder's attention blocks run inside the chain: before layer l's MoE
+// block, rms_norm(attn_norm_l) -> the Q4_K [q (| gate) | k | v] matvec ->
+// attention over layer l's FP16 ring -> the Q4_K output projection into the
+// residual (the attention phase of pokit_attention.cuh), with every per-layer
+// tensor `w_stride` bytes after the previous layer's and the rings
+// `kv_stride` halves apart.  Words exchange hidden rows, Q/K/V rows and the
+// attention output between CTAs (tags from the device position).
+struct ChainAttnDesc {
+    const uint8_t* wqkv = nullptr;        // layer 0's tensors
+    const uint8_t* wo = nullptr;
+    const float* attn_norm = nullptr;
+    const float* q_norm = nullptr;
+    const float* k_norm = nullptr;
+    uint64_t w_stride = 0;
+    const float* rope_cos = nullptr;      // [context][rotary half]
+    const float* rope_sin = nullptr;
+    void* kc = nullptr;                   // layer 0's rings (__half)
+    void* vc = nullptr;
+    uint64_t kv_stride = 0;
+    const uint32_t* pos = nullptr;        // the decoder's device position
+    uint32_t q_heads = 0, kv_heads = 0, head_dim = 0, q_stride = 0, gated = 0, rotary_half = 0, window = 0;
+    float eps = 0.0f, scale = 0.0f;
+    unsigned long long* qkv_words = nullptr;   // [rows]
+    unsigned long long* att_words = nullptr;   // [q_heads * head_dim]
+    unsigned long long* hidden_words = nullptr;  // [hidden]
+    uint32_t* status = nullptr;           // attention timeout flag
+    uint32_t rows = 0, layers_total = 0;
+};
+// Bytes of shared memory the attention phase needs, and where the chain's
+// tile region (which it runs in) starts.
+uint32_t chain_attention_smem(const ChainPlan& plan, const ChainAttnDesc& att);
+uint32_t chain_tile_offset(const ChainPlan& plan);
 cudaError_t launch_moe_chain(const ChainPlan& plan, const MoeLayerDev* layers_dev, uint32_t first, uint32_t count,
                              const MoeScratch& S, const ChainScratch& C, float* hidden, cudaStream_t stream,
-                             unsigned long long* trace = nullptr);
+                             unsigned long long* trace = nullptr, const ChainAttnDesc* attention = nullptr);
+}  // namespace pokit
+struct pokit_cuda_moe;
+namespace pokit {
+// A MoE handle's decode chain with a decoder's attention blocks (pokit_backend.cpp).
+bool moe_attention_chain_fits(const pokit_cuda_moe* moe, const ChainAttnDesc& att);
+cudaError_t moe_decode_layers_attention(pokit_cuda_moe* moe, size_t first, size_t count, float* hidden,
+                                        const ChainAttnDesc& att, cudaStream_t stream, std::string* error);
 
 // Grid-wide barriers one layer of launch_moe_decode performs.
 uint32_t moe_barriers_per_layer();

@@ -23,6 +23,7 @@
 // Data written by other CTAs of the same kernel (h, partials, act) is read with
 // ld.global.cg so a stale L1 line can never be observed.  Weights are read-only
 // for the kernel's lifetime and use the non-coherent path.
+#include "pokit_attention.cuh"
 #include "pokit_kernels.h"
 #include "pokit_mma.cuh"
 #include "pokit_quant.cuh"
@@ -1725,7 +1726,7 @@ constexpr uint32_t kChainStamps = 8;
 constexpr uint32_t kPairRowBytes = 288u, kPairBytes = 16u * kPairRowBytes;
 
 struct ChainLayout {
-    uint32_t gbars, dbars, recs, lg, sel_id, sel_w, part, dpart, comb, hrow, gtiles, dtiles, total;
+    uint32_t gbars, dbars, abars, recs, lg, sel_id, sel_w, part, dpart, comb, hrow, gtiles, dtiles, total;
     uint32_t nsb, half_sb, nsd, gpairs, dpairs;
 };
 
@@ -1740,6 +1741,7 @@ __host__ __device__ inline ChainLayout chain_layout(const MoeLayerDev& L) {
     uint32_t off = 0;
     c.gbars = off; off += al16(kWarps * c.gpairs * 8u);
     c.dbars = off; off += al16(k * c.dpairs * 8u);
+    c.abars = off; off += 16u;
     c.recs = off; off += al16(umax(nsb, k * nsd) * kFragWords * 4u);
     c.lg = off; off += al16(L.experts * 4u);
     c.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
@@ -1772,6 +1774,9 @@ struct ChainArgs {
     // globaltimer readings (ns) and then kChainStamps clock64 readings per
     // layer at [(l * grid + cta) * 2 * kChainStamps + i].
     unsigned long long* trace;
+    // A decoder's attention blocks before each MoE block (with_att != 0).
+    ChainAttnDesc att;
+    uint32_t with_att;
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -1837,10 +1842,14 @@ __device__ __forceinline__ void chain_partials(const float* router, uint32_t E, 
     }
 }
 
+// kAtt: a decoder's attention blocks before each MoE block (a separate
+// instantiation, so the MoE-only chain keeps its registers).
+template <bool kAtt>
 __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_constant__ ChainArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t abort_sh, bad_sh, last_sh;
     __shared__ float scale_sh;
+    __shared__ float attn_red[kWarps];
     const ChainLayout& c = a.c;
     const MoeLayerDev& Ls = a.shape;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1852,6 +1861,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
     const uint32_t j0 = cta * kPartRows;
     uint64_t* gbars = reinterpret_cast<uint64_t*>(smem + c.gbars);
     uint64_t* dbars = reinterpret_cast<uint64_t*>(smem + c.dbars);
+    uint64_t* abars = reinterpret_cast<uint64_t*>(smem + c.abars);
     uint32_t* recs = reinterpret_cast<uint32_t*>(smem + c.recs);
     float* lg = reinterpret_cast<float*>(smem + c.lg);
     uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + c.sel_id);
@@ -1889,8 +1899,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
     const uint32_t gpairs = c.gpairs, dpairs = c.dpairs;
     if (lane == 0) {
         for (uint32_t i = 0; i < gpairs; ++i) mbar_init(&gbars[warp * gpairs + i], 1);
-        if (warp == 0)
+        if (warp == 0) {
             for (uint32_t u = 0; u < k * dpairs; ++u) mbar_init(&dbars[u], 1);
+            mbar_init(&abars[0], 1);
+            mbar_init(&abars[1], 1);
+        }
         mbar_fence_init();
     }
     // This CTA's gate/up row group and superblock half per warp (the same
@@ -1907,8 +1920,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
     (void)half;
 
     // Prologue: the first layer's router partials and x' rows from the input
-    // hidden state.
-    if (has_unit) {
+    // hidden state (with attention blocks, the first attention phase adds them).
+    if (has_unit && !kAtt) {
         if (tid < 16) {
             const float h = __ldcg(a.hidden + j0 + tid);
             const float xn = __ldg(norm_of(a.first) + j0 + tid) * h;
@@ -1932,10 +1945,62 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
     // them (launches advance it by their layer count; zero-filled memory
     // never matches).
     const uint32_t seq0 = __ldcg(ctr_seq);
+    // With attention blocks: the decoder's position (hidden-row word tags) and
+    // the router slice of the layer whose partials the next attention phase adds.
+    const uint32_t att_pos = kAtt ? *a.att.pos : 0u;
+    RouterSlice rs_att{};
+    if (kAtt && has_unit && static_cast<uint32_t>(tid) < E) rs_att = router_slice(router_of(a.first), H, tid, cta);
     for (uint32_t l = 0; l < a.count && ok; ++l, phase ^= 1u) {
         const uint32_t layer = a.first + l, p = layer & 1u, pr = layer % 3u, tag = seq0 + l + 1u;
         const bool has_next = l + 1 < a.count;
         const uint32_t nlayer = has_next ? layer + 1 : layer;
+        // ---- attention (decoder layer loop) ----
+        if constexpr (kAtt) {
+            const ChainAttnDesc& d = a.att;
+            const uint64_t wo = static_cast<uint64_t>(layer) * d.w_stride;
+            AttnBlockArgs aa{};
+            aa.wqkv = d.wqkv + wo;
+            aa.wo = d.wo + wo;
+            aa.attn_norm = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(d.attn_norm) + wo);
+            aa.q_norm = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(d.q_norm) + wo);
+            aa.k_norm = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(d.k_norm) + wo);
+            aa.rope_cos = d.rope_cos;
+            aa.rope_sin = d.rope_sin;
+            aa.kc = static_cast<__half*>(d.kc) + static_cast<uint64_t>(layer) * d.kv_stride;
+            aa.vc = static_cast<__half*>(d.vc) + static_cast<uint64_t>(layer) * d.kv_stride;
+            aa.pos_p = d.pos;
+            aa.sh = AttendShape{d.q_heads, d.kv_heads, d.head_dim, d.q_stride, d.gated, d.rotary_half, d.window,
+                                d.eps, d.scale};
+            aa.hidden = a.hidden;
+            aa.qkv_ll = d.qkv_words;
+            aa.att_ll = d.att_words;
+            aa.status = d.status;
+            aa.H = H;
+            aa.rows = d.rows;
+            aa.qd = d.q_heads * d.head_dim;
+            aa.layer = layer;
+            aa.layers = d.layers_total;
+            aa.eps = d.eps;
+            const AttnPhaseCtx x{smem + c.gtiles, abars, phase, &abort_sh, attn_red};
+            // Smaller load batches keep the attention inside the chain's
+            // register budget (384 threads).
+            const float hn = attention_phase<8, 8>(aa, x, l > 0 ? d.hidden_words : nullptr,
+                                                   att_pos * d.layers_total + layer + 1u);
+            if (abort_sh) { ok = false; break; }
+            // This layer's router partials from the D unit's new rows.
+            if (has_unit) {
+                if (tid < 16) {
+                    const float xn = __ldg(norm_of(layer) + j0 + tid) * hn;
+                    hrow[tid] = xn;
+                    hrow[kPartRows + tid] = hn * hn;
+                    for (uint32_t r = 0; r < kChainXReplicas; ++r) a.C.xrep[static_cast<uint64_t>(r) * H + j0 + tid] = xn;
+                }
+                __syncthreads();
+                chain_partials(router_of(layer), E, rs_att, hrow, a.C.racc + pr * racc_span, a.C.rbad + pr,
+                               a.C.rsq + p * units, cta, H);
+                chain_arrive(ctr_route);
+            }
+        }
         // ---- route ----
         if (!chain_wait(ctr_route, units * (l + 1u), status, &abort_sh)) { ok = false; break; }
         stamp(l, 0);
@@ -2029,6 +2094,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
         // The next layer's router slice and ffn_norm, this unit's residual rows.
         RouterSlice rs{};
         if (has_unit && has_next && static_cast<uint32_t>(tid) < E) rs = router_slice(router_of(nlayer), H, tid, cta);
+        if (kAtt) rs_att = rs;
         const float resid = (has_unit && tid < 16) ? __ldcg(a.hidden + j0 + tid) : 0.0f;
         const float nnorm = (has_unit && has_next && tid < 16) ? __ldg(norm_of(nlayer) + j0 + tid) : 0.0f;
         // ---- G: multiply the boxes as they land ----
@@ -2196,7 +2262,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                 for (uint32_t sl = 0; sl < k; ++sl) acc += comb[sl * 16 + tid];
                 const float h = resid + acc;
                 a.hidden[j0 + tid] = h;
-                if (has_next) {
+                if (has_next && kAtt) {
+                    // The next attention phase stages every row from these words.
+                    put_word(a.att.hidden_words + j0 + tid, att_pos * a.att.layers_total + nlayer + 1u, h);
+                } else if (has_next) {
                     const float xn = nnorm * h;
                     hrow[tid] = xn;
                     hrow[kPartRows + tid] = h * h;
@@ -2204,14 +2273,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                         a.C.xrep[static_cast<uint64_t>(r) * H + j0 + tid] = xn;
                 }
             }
-            if (has_next) {
+            if (has_next && !kAtt) {
                 __syncthreads();
                 const uint32_t pn = (layer + 1u) % 3u;
                 chain_partials(router_of(nlayer), E, rs, hrow, a.C.racc + pn * racc_span, a.C.rbad + pn,
                                a.C.rsq + (p ^ 1u) * units, cta, H);
             }
         }
-        chain_arrive(ctr_route);
+        // With attention blocks the next layer's attention phase arrives.
+        if (!kAtt) chain_arrive(ctr_route);
+        else __syncthreads();
         stamp(l, 7);
     }
     if (!ok) return;
@@ -2672,9 +2743,11 @@ bool moe_chain_plan(const MoeLayerDev* layers, uint32_t n, ChainPlan* plan) {
     if (units > sms || groups > kChainGroupsPerCta * sms || groups < sms || L0.experts > kThreads ||
         c.total > 227u * 1024u || (L0.hidden >> 8) > 64u)
         return false;
-    if (ensure_smem(moe_chain_kernel, c.total) != cudaSuccess) return false;
+    if (ensure_smem(moe_chain_kernel<false>, c.total) != cudaSuccess ||
+        ensure_smem(moe_chain_kernel<true>, c.total) != cudaSuccess)
+        return false;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_chain_kernel, kThreads, c.total) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_chain_kernel<false>, kThreads, c.total) != cudaSuccess ||
         per_sm < 1)
         return false;
     const uint64_t rb_in = static_cast<uint64_t>(L0.hidden >> 8) * 144u;
@@ -2691,12 +2764,34 @@ bool moe_chain_plan(const MoeLayerDev* layers, uint32_t n, ChainPlan* plan) {
     return true;
 }
 
+uint32_t chain_tile_offset(const ChainPlan& plan) { return chain_layout(plan.shape).gtiles; }
+
+uint32_t chain_attention_smem(const ChainPlan& plan, const ChainAttnDesc& att) {
+    return attn_block_layout(plan.shape.hidden, att.rows, att.q_heads * att.head_dim, att.head_dim, att.rotary_half,
+                             att.window, plan.grid, kWarps)
+        .total;
+}
+
 cudaError_t launch_moe_chain(const ChainPlan& plan, const MoeLayerDev* layers_dev, uint32_t first, uint32_t count,
                              const MoeScratch& S, const ChainScratch& C, float* hidden, cudaStream_t stream,
-                             unsigned long long* trace) {
+                             unsigned long long* trace, const ChainAttnDesc* attention) {
     (void)layers_dev;
     if (!hidden || count == 0 || first >= plan.layers || count > plan.layers - first || plan.grid == 0)
         return cudaErrorInvalidValue;
+    if (attention) {
+        // The attention phase runs in the tile region (gate/up and down tiles
+        // are not live then); every CTA owns a Q/K/V row block, the output
+        // units are the chain's D units and the query heads fit the grid.
+        const ChainAttnDesc& t = *attention;
+        const ChainLayout cl = chain_layout(plan.shape);
+        const uint32_t qd = t.q_heads * t.head_dim;
+        if (!t.wqkv || !t.wo || !t.pos || !t.qkv_words || !t.att_words || !t.hidden_words || !t.status ||
+            t.rows % 16u || t.rows / 16u < plan.grid || plan.shape.hidden / 16u > plan.grid || t.q_heads > plan.grid ||
+            t.head_dim == 0 || t.head_dim > kAttendMaxDim || t.head_dim > kThreads || qd % 256u ||
+            qd / 256u > kWarps * kAttnMaxOutPerWarp || plan.shape.hidden / 256u > 2u * kWarps ||
+            chain_attention_smem(plan, t) > plan.smem - cl.gtiles)
+            return cudaErrorInvalidValue;
+    }
     ChainArgs a{};
     a.tm_gate = plan.tm_gate;
     a.tm_up = plan.tm_up;
@@ -2712,6 +2807,10 @@ cudaError_t launch_moe_chain(const ChainPlan& plan, const MoeLayerDev* layers_de
     a.hidden = hidden;
     a.c = chain_layout(plan.shape);
     a.trace = trace;
+    if (attention) {
+        a.att = *attention;
+        a.with_att = 1u;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.grid);
     cfg.blockDim = dim3(kThreads);
@@ -2722,7 +2821,8 @@ cudaError_t launch_moe_chain(const ChainPlan& plan, const MoeLayerDev* layers_de
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_chain_kernel, a);
+    return attention ? cudaLaunchKernelEx(&cfg, moe_chain_kernel<true>, a)
+                     : cudaLaunchKernelEx(&cfg, moe_chain_kernel<false>, a);
 }
 
 cudaError_t prepare_moe_block(const MoeLayerDev& L) {
