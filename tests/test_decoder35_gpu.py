@@ -22,10 +22,21 @@ pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden" / "decoder_cfg3_L4.npz"
 
 
-@pytest.fixture(scope="module")
-def decoder(cuda):
+# The full-attention layers as the fused attention block (the default) and
+# as three kernels.
+MODES = {"attention_block": {}, "three_kernels": {"POKIT_CUDA_FUSED_ATTN": "0"}}
+
+
+@pytest.fixture(scope="module", params=list(MODES))
+def decoder(cuda, request):
     g = np.load(GOLDEN)
-    dec = B.CudaDecoder(gguf.Qwen35MoeShape(layers=int(g["layers"])))
+    mp = pytest.MonkeyPatch()
+    for k, v in MODES[request.param].items():
+        mp.setenv(k, v)                      # read when the decoder is created
+    try:
+        dec = B.CudaDecoder(gguf.Qwen35MoeShape(layers=int(g["layers"])))
+    finally:
+        mp.undo()
     dec.synthesize_model()
     yield dec, g
     dec.close()

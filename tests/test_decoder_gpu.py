@@ -6,7 +6,9 @@ forward_token on a synthetic GGUF; the weights are synthesised here in HBM
 from the same seeds).
 
 Bar (north star): greedy token ids identical for the first 64 generated
-tokens; the logits after the prompt within 1e-3 x their RMS.
+tokens; the logits after the prompt within 1e-3 x their RMS.  Every form of
+the layer loop is checked (one chain launch for the whole loop, the fused
+attention block beside the MoE chain, three attention kernels per layer).
 """
 from pathlib import Path
 
@@ -20,10 +22,23 @@ pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden" / "decoder_cfg2_L2.npz"
 
 
-@pytest.fixture(scope="module")
-def decoder(cuda):
+# The decoder's layer loop forms: the whole loop in one chain launch (the
+# default), the fused attention block and the MoE chain as two launches per
+# layer, and three attention kernels per layer.
+MODES = {"layer_chain": {}, "attention_block": {"POKIT_CUDA_FUSED_LAYERS": "0"},
+         "three_kernels": {"POKIT_CUDA_FUSED_LAYERS": "0", "POKIT_CUDA_FUSED_ATTN": "0"}}
+
+
+@pytest.fixture(scope="module", params=list(MODES))
+def decoder(cuda, request):
     g = np.load(GOLDEN)
-    dec = B.CudaDecoder(gguf.Qwen3MoeShape(layers=int(g["layers"])))
+    mp = pytest.MonkeyPatch()
+    for k, v in MODES[request.param].items():
+        mp.setenv(k, v)                      # read when the decoder is created
+    try:
+        dec = B.CudaDecoder(gguf.Qwen3MoeShape(layers=int(g["layers"])))
+    finally:
+        mp.undo()
     dec.synthesize_model()
     yield dec, g
     dec.close()
