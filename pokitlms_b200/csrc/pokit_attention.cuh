@@ -45,6 +45,31 @@ constexpr uint32_t kAttendMaxDim = 256;
 // as the ring stores them, kv_cache.cpp:20-44); the group's first CTA writes
 // them to the ring at slot position % window, and every CTA uses its own copy
 // for the newest position (no CTA reads the slot being written).
+// The query's and the key's scales in one reduction (red: 2 floats per warp).
+__device__ __forceinline__ void head_rms_scale2(float xq, float xk, uint32_t d, float eps, float* red, float& sq,
+                                                float& sk) {
+    float vq = xq * xq, vk = xk * xk;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        vq += __shfl_xor_sync(0xffffffffu, vq, o);
+        vk += __shfl_xor_sync(0xffffffffu, vk, o);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) {
+        red[2 * warp] = vq;
+        red[2 * warp + 1] = vk;
+    }
+    __syncthreads();
+    float tq = 0.0f, tk = 0.0f;
+    for (uint32_t w = 0; w < (d + 31) / 32; ++w) {
+        tq += red[2 * w];
+        tk += red[2 * w + 1];
+    }
+    sq = 1.0f / sqrtf(tq / static_cast<float>(d) + eps);
+    sk = 1.0f / sqrtf(tk / static_cast<float>(d) + eps);
+}
+
 __device__ __forceinline__ float head_rms_scale(float x, uint32_t d, float eps, float* red) {
     float v = x * x;
 #pragma unroll
@@ -113,8 +138,8 @@ __device__ void attend_head(const float* q_in, const float* k_in, const float* v
     const uint32_t units = d / 8;                         // 16-byte units of a key row
     const float xq = dim ? q_in[t] : 0.0f;
     const float xk = dim ? k_in[t] : 0.0f;
-    const float sq = head_rms_scale(xq, d, sh.eps, red);
-    const float sk = head_rms_scale(xk, d, sh.eps, red);
+    float sq, sk;
+    head_rms_scale2(xq, xk, d, sh.eps, red, sq, sk);
     if (dim) {
         qs[t] = __fmul_rn(__fmul_rn(xq, sq), q_norm[t]);
         kn[t] = __fmul_rn(__fmul_rn(xk, sk), k_norm[t]);
@@ -147,35 +172,39 @@ __device__ void attend_head(const float* q_in, const float* k_in, const float* v
         }
     }
     __syncthreads();
-    for (uint32_t j0 = 0; j0 < n; j0 += nthreads) {
-        const uint32_t j = j0 + t;
+    // Two threads per position (adjacent lanes), each dotting half the key
+    // row; the halves are added at the end.
+    const uint32_t half_units = units / 2, hsel = t & 1u;
+    for (uint32_t j0 = 0; j0 < n; j0 += nthreads / 2) {
+        const uint32_t j = j0 + t / 2;
+        float dot = 0.0f;
         if (j + 1 == n) {
-            float dot = 0.0f;
-            for (uint32_t e = 0; e < d; ++e) dot = fmaf(qs[e], knew[e], dot);
-            sc[j] = dot * sh.scale;
+            for (uint32_t e = hsel * (d / 2); e < (hsel + 1) * (d / 2); ++e) dot = fmaf(qs[e], knew[e], dot);
         } else if (j < n) {
-            const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + j) % window) * row_stride + kh * d);
-            float dot = 0.0f;
-            for (uint32_t c0 = 0; c0 < units; c0 += kChunk) {
+            const uint4* k = reinterpret_cast<const uint4*>(kc + ((first + j) % window) * row_stride + kh * d) +
+                             hsel * half_units;
+            const float* qh_ = qs + hsel * (d / 2);
+            for (uint32_t c0 = 0; c0 < half_units; c0 += kChunk) {
                 uint4 kv[kChunk];
 #pragma unroll
                 for (uint32_t u = 0; u < kChunk; ++u)
-                    if (c0 + u < units) kv[u] = __ldg(k + c0 + u);
+                    if (c0 + u < half_units) kv[u] = __ldg(k + c0 + u);
 #pragma unroll
                 for (uint32_t u = 0; u < kChunk; ++u) {
-                    if (c0 + u < units) {
+                    if (c0 + u < half_units) {
                         const __half2* hp = reinterpret_cast<const __half2*>(&kv[u]);
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const float2 f = __half22float2(hp[e]);
-                            dot = fmaf(qs[(c0 + u) * 8 + 2 * e], f.x, dot);
-                            dot = fmaf(qs[(c0 + u) * 8 + 2 * e + 1], f.y, dot);
+                            dot = fmaf(qh_[(c0 + u) * 8 + 2 * e], f.x, dot);
+                            dot = fmaf(qh_[(c0 + u) * 8 + 2 * e + 1], f.y, dot);
                         }
                     }
                 }
             }
-            sc[j] = dot * sh.scale;
         }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        if (j < n && hsel == 0) sc[j] = dot * sh.scale;
     }
     __syncthreads();
     float m = -INFINITY;
