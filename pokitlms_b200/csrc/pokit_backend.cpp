@@ -154,6 +154,7 @@ public:
         const std::string want = mode ? mode : "";
         const bool want_persistent = want == "persistent";
         decode_grid_ = want_persistent ? moe_decode_grid(devs_[0]) : 0u;
+        std::vector<Chain35Maps> chain35_maps;
         if (!sharded() && !want_persistent && want != "graph" &&
             moe_chain_plan(devs_.data(), static_cast<uint32_t>(c.layers), &chain_plan_)) {
             const uint64_t cb = moe_chain_scratch_bytes(devs_[0]);
@@ -161,6 +162,18 @@ public:
             check(cudaMemset(chain_scratch_, 0, cb), "cudaMemset(chain scratch)");
             C_ = moe_chain_scratch_carve(devs_[0], chain_scratch_);
             chain_ok_ = true;
+        } else if (!sharded() && !want_persistent && want != "graph" &&
+                   moe_chain35_plan(devs_.data(), static_cast<uint32_t>(c.layers), &chain35_plan_, &chain35_maps)) {
+            // Qwen3.5-MoE blocks (shared expert, per-layer down types): their chain kernel.
+            check(cudaMalloc(&chain35_maps_, sizeof(Chain35Maps) * chain35_maps.size()), "cudaMalloc(tensor maps)");
+            check(cudaMemcpy(chain35_maps_, chain35_maps.data(), sizeof(Chain35Maps) * chain35_maps.size(),
+                             cudaMemcpyHostToDevice),
+                  "cudaMemcpy(tensor maps)");
+            const uint64_t cb = moe_chain_scratch_bytes(devs_[0]);
+            check(cudaMalloc(&chain_scratch_, cb), "cudaMalloc(chain scratch)");
+            check(cudaMemset(chain_scratch_, 0, cb), "cudaMemset(chain scratch)");
+            C_ = moe_chain_scratch_carve(devs_[0], chain_scratch_);
+            chain35_ok_ = true;
         }
         check(cudaMalloc(&io_, align256(c.hidden * 4) * 2), "cudaMalloc(io)");
         check(cudaMallocHost(&pinned_, align256(c.hidden * 4) * 2 + 4096), "cudaMallocHost");
@@ -179,6 +192,7 @@ public:
         if (scratch_) cudaFree(scratch_);
         if (chain_scratch_) cudaFree(chain_scratch_);
         if (devs_dev_) cudaFree(devs_dev_);
+        if (chain35_maps_) cudaFree(chain35_maps_);
         if (pool_) cudaFree(pool_);
         if (capture_stream_) cudaStreamDestroy(capture_stream_);
         if (stream_) cudaStreamDestroy(stream_);
@@ -452,6 +466,15 @@ public:
             kernel_launches_ += 1;
             return;
         }
+        if (chain35_ok_) {
+            guard(launch_moe_chain35(chain35_plan_, devs_dev_, chain35_maps_, static_cast<uint32_t>(first),
+                                     static_cast<uint32_t>(count), S_, C_, hidden, st),
+                  "decode chain kernel");
+            forward_calls_ += count;
+            hits_ += count * cfg_.top_k;
+            kernel_launches_ += 1;
+            return;
+        }
         if (chain_ok_) {
             guard(launch_moe_chain(chain_plan_, devs_dev_, static_cast<uint32_t>(first), static_cast<uint32_t>(count),
                                    S_, C_, hidden, st), "decode chain kernel");
@@ -513,17 +536,22 @@ public:
     uint32_t trace_decode(size_t first, size_t count, float* hidden, unsigned long long* stamps, size_t capacity,
                           cudaStream_t s) {
         ensure_ok();
-        if (!chain_ok_) throw std::invalid_argument("the layers do not run the persistent chain kernel");
+        if (!chain_ok_ && !chain35_ok_) throw std::invalid_argument("the layers do not run a persistent chain kernel");
         if (count == 0 || first >= cfg_.layers || count > cfg_.layers - first || !hidden || !stamps)
             throw std::invalid_argument("layer range, hidden state and stamp buffer are required");
-        if (capacity < count * chain_plan_.grid * kChainTraceStamps)
+        const uint32_t grid = chain_ok_ ? chain_plan_.grid : chain35_plan_.grid;
+        if (capacity < count * grid * kChainTraceStamps)
             throw std::invalid_argument("stamp buffer too small (count x grid x 16 words)");
         DeviceScope scope(device_);
         cudaStream_t st = s ? s : stream_;
-        guard(launch_moe_chain(chain_plan_, devs_dev_, static_cast<uint32_t>(first), static_cast<uint32_t>(count), S_,
-                               C_, hidden, st, stamps), "decode chain kernel");
+        if (chain_ok_)
+            guard(launch_moe_chain(chain_plan_, devs_dev_, static_cast<uint32_t>(first), static_cast<uint32_t>(count),
+                                   S_, C_, hidden, st, stamps), "decode chain kernel");
+        else
+            guard(launch_moe_chain35(chain35_plan_, devs_dev_, chain35_maps_, static_cast<uint32_t>(first),
+                                     static_cast<uint32_t>(count), S_, C_, hidden, st, stamps), "decode chain kernel");
         kernel_launches_ += 1;
-        return chain_plan_.grid;
+        return grid;
     }
 
     // A decoder's layer loop: its attention blocks and these MoE blocks in
@@ -773,6 +801,9 @@ private:
     uint32_t barrier_count_ = 0;
     bool chain_ok_ = false;              // decode_layers runs moe_chain_kernel
     ChainPlan chain_plan_{};
+    bool chain35_ok_ = false;            // decode_layers runs moe_chain35_kernel (Qwen3.5-MoE blocks)
+    Chain35Plan chain35_plan_{};
+    Chain35Maps* chain35_maps_ = nullptr;   // device table of the chain's per-layer tensor maps
     void* chain_scratch_ = nullptr;
     ChainScratch C_;
     uint64_t scratch_bytes_ = 0;

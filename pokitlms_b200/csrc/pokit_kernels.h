@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 namespace pokit {
 
@@ -264,6 +265,26 @@ struct ChainAttnDesc {
     uint32_t* status = nullptr;           // attention timeout flag
     uint32_t rows = 0, layers_total = 0;
 };
+// The decode chain for Qwen3.5-MoE blocks (Q4_K gate/up, any K-quant or Q8_0
+// down per layer, the Q8_0 shared expert with its sigmoid gate), per-layer
+// pointers read from the device table.
+struct Chain35Plan {
+    MoeLayerDev shape;
+    uint32_t layers = 0, grid = 0, smem = 0, rb_down_max = 0;
+};
+// A layer's tensor maps for the chain's gate/up boxes: (8-byte column, row,
+// expert) views of the routed Q4_K gate and up, boxes of 16 rows by two
+// superblocks; (8-byte column, row) views of the shared expert's Q8_0 gate
+// and up, boxes of 8 rows by half a row.  Kept in device memory, a table per
+// layer.
+struct Chain35Maps {
+    CUtensorMap gate, up, shared_gate, shared_up;
+};
+// Plans the chain for `n` layers and encodes each layer's maps into `maps`.
+bool moe_chain35_plan(const MoeLayerDev* layers, uint32_t n, Chain35Plan* plan, std::vector<Chain35Maps>* maps);
+cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layers_dev, const Chain35Maps* maps_dev,
+                               uint32_t first, uint32_t count, const MoeScratch& S, const ChainScratch& C,
+                               float* hidden, cudaStream_t stream, unsigned long long* trace = nullptr);
 // Bytes of shared memory the attention phase needs, and where the chain's
 // tile region (which it runs in) starts.
 uint32_t chain_attention_smem(const ChainPlan& plan, const ChainAttnDesc& att);

@@ -106,6 +106,16 @@ __device__ __forceinline__ void tma_box_3d(void* dst, const CUtensorMap* map, in
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
+// One box of a 2-D tensor map (x = column in the map's element units, y =
+// row) into shared memory, completing on `bar`.  x * element size must be a
+// multiple of 16 bytes.
+__device__ __forceinline__ void tma_box_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
 // Contiguous global -> shared bulk copy (no multicast) completing on `bar`;
 // both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -318,6 +328,157 @@ __device__ __forceinline__ void q4k_mma_superblock(const uint8_t* __restrict__ b
     const float dd1 = half_bits_to_float(h1.x), dm1 = half_bits_to_float(h1.x >> 16) * me;
     acc0 = fmaf(dd0, y0, fmaf(dm0, d2[0] + d2[1], acc0));
     acc1 = fmaf(dd1, y1, fmaf(dm1, d2[2] + d2[3], acc1));
+}
+
+__device__ __forceinline__ void imma16832_ss(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                             uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// q4k_mma_superblock for Q5_K superblocks (176 bytes: d, dmin, the twelve
+// scale bytes, qh[32], qs[128]).  Element l of sub-block j carries bit j of
+// qh[l] as its fifth bit (the reference's Q5_K decoder, quantized_linear.cpp
+// :286-328), so each A byte is the nibble with that bit at 16; the scales,
+// mins and the min term are Q4_K's.
+__device__ __forceinline__ void q5k_mma_superblock(const uint8_t* __restrict__ b0p, const uint8_t* __restrict__ b1p,
+                                                   const uint32_t* __restrict__ rec, float& acc0, float& acc1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const bool bact = g < 4;
+    const uint4 h0 = *reinterpret_cast<const uint4*>(b0p);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(b1p);
+    const uint2 e0 = *reinterpret_cast<const uint2*>(b0p + 16 + 8 * t);
+    const uint2 e1 = *reinterpret_cast<const uint2*>(b1p + 16 + 8 * t);
+    uint2 q0[4], q1[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        q0[c] = *reinterpret_cast<const uint2*>(b0p + 48 + 32 * c + 8 * t);
+        q1[c] = *reinterpret_cast<const uint2*>(b1p + 48 + 32 * c + 8 * t);
+    }
+    const uint32_t sA0 = h0.y & 0x3F3F3F3Fu, sB0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+    const uint32_t sA1 = h1.y & 0x3F3F3F3Fu, sB1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+    const uint32_t mA0 = h0.z & 0x3F3F3F3Fu, mB0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+    const uint32_t mA1 = h1.z & 0x3F3F3F3Fu, mB1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+    const uint8_t* rb = reinterpret_cast<const uint8_t*>(rec) + g * 32 + 8 * t;
+    const auto fifth = [](uint32_t e, int bit) { return ((e >> bit) & 0x01010101u) << 4; };
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t sw0 = c < 2 ? sA0 : sB0, sw1 = c < 2 ? sA1 : sB1;
+        const uint32_t bl = (2 * c) & 3, bh = (2 * c + 1) & 3;
+        const int sl0 = static_cast<int>(__byte_perm(sw0, 0u, 0x4440u | bl));
+        const int sl1 = static_cast<int>(__byte_perm(sw1, 0u, 0x4440u | bl));
+        const int sh0 = static_cast<int>(__byte_perm(sw0, 0u, 0x4440u | bh));
+        const int sh1 = static_cast<int>(__byte_perm(sw1, 0u, 0x4440u | bh));
+        const uint2 xl = bact ? *reinterpret_cast<const uint2*>(rb + (2 * c) * 128) : make_uint2(0u, 0u);
+        const uint2 xh = bact ? *reinterpret_cast<const uint2*>(rb + (2 * c + 1) * 128) : make_uint2(0u, 0u);
+        int dl[4], dh[4];
+        imma16832(dl, (q0[c].x & 0x0F0F0F0Fu) | fifth(e0.x, 2 * c), (q1[c].x & 0x0F0F0F0Fu) | fifth(e1.x, 2 * c),
+                  (q0[c].y & 0x0F0F0F0Fu) | fifth(e0.y, 2 * c), (q1[c].y & 0x0F0F0F0Fu) | fifth(e1.y, 2 * c), xl.x,
+                  xl.y);
+        imma16832(dh, ((q0[c].x >> 4) & 0x0F0F0F0Fu) | fifth(e0.x, 2 * c + 1),
+                  ((q1[c].x >> 4) & 0x0F0F0F0Fu) | fifth(e1.x, 2 * c + 1),
+                  ((q0[c].y >> 4) & 0x0F0F0F0Fu) | fifth(e0.y, 2 * c + 1),
+                  ((q1[c].y >> 4) & 0x0F0F0F0Fu) | fifth(e1.y, 2 * c + 1), xh.x, xh.y);
+        acc[0] += dl[0] * sl0 + dh[0] * sh0;
+        acc[1] += dl[1] * sl0 + dh[1] * sh0;
+        acc[2] += dl[2] * sl1 + dh[2] * sh1;
+        acc[3] += dl[3] * sl1 + dh[3] * sh1;
+    }
+    const uint32_t mw0 = t < 2 ? mA0 : mB0, mw1 = t < 2 ? mA1 : mB1;
+    const uint32_t ja = (2 * t) & 3;
+    const uint32_t M0 = hsub2u(__byte_perm(mw0, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
+    const uint32_t M1 = hsub2u(__byte_perm(mw1, 0x64u, 0x4040u | ((ja + 1) << 8) | ja), kHalfMagic);
+    const uint32_t bm = g < 2 ? rec[256 + t * 2 + (g & 1)] : 0u;
+    float d2[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816(d2, M0, M1, 0u, 0u, bm, 0u);
+    const float s0 = __uint_as_float(rec[265]);
+    const float ca = t == 0 ? s0 : (t == 1 ? s0 * (1.0f / 16384.0f) : 0.0f);
+    const float cb = t == 0 ? s0 * (1.0f / 128.0f) : (t == 1 ? s0 * (1.0f / 2097152.0f) : 0.0f);
+    const float y0 = ca * static_cast<float>(acc[0]) + cb * static_cast<float>(acc[1]);
+    const float y1 = ca * static_cast<float>(acc[2]) + cb * static_cast<float>(acc[3]);
+    const float me = __uint_as_float(rec[264]);
+    const float dd0 = half_bits_to_float(h0.x), dm0 = half_bits_to_float(h0.x >> 16) * me;
+    const float dd1 = half_bits_to_float(h1.x), dm1 = half_bits_to_float(h1.x >> 16) * me;
+    acc0 = fmaf(dd0, y0, fmaf(dm0, d2[0] + d2[1], acc0));
+    acc1 = fmaf(dd1, y1, fmaf(dm1, d2[2] + d2[3], acc1));
+}
+
+// Eight bytes at a 2-byte-aligned shared-memory address: `odd` says p sits 2
+// bytes past a word boundary (Q6_K superblocks are 210 bytes, so alternate
+// superblocks of a row are).  Reads up to 2 bytes past p + 7.
+__device__ __forceinline__ uint2 lds_u64_a2(const uint8_t* p, bool odd) {
+    if (!odd) return make_uint2(*reinterpret_cast<const uint32_t*>(p), *reinterpret_cast<const uint32_t*>(p + 4));
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(p - 2);
+    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+    return make_uint2(__funnelshift_r(w0, w1, 16), __funnelshift_r(w1, w2, 16));
+}
+
+// Four 6-bit quants (bytes 0..63) as the signed bytes q - 32.
+__device__ __forceinline__ uint32_t q6_centered(uint32_t v) {
+    const uint32_t r = v ^ 0x20202020u;               // q - 32 for q >= 32; q | 32 otherwise
+    const uint32_t m = r & 0x20202020u;                // set where q < 32: extend the sign
+    return r | (m << 1) | (m << 2);
+}
+
+// One Q6_K superblock of 16 rows (210 bytes each: ql[128], qh[64], sc[16],
+// d; the reference's decoder, quantized_linear.cpp:330-358) dotted with the
+// activation record `rec`, as q4k_mma_superblock: sub-block j = 4 * half +
+// quarter holds elements 128 half + 32 quarter + l, whose 6-bit value is
+// nibble (quarter / 2) of ql[64 half + 32 (quarter % 2) + l] with bits
+// 2 quarter of qh[32 half + l] above it, and whose scale is sc[2 j + l / 16].
+// The A bytes are q - 32 (signed), so there is no min term; the two scales of
+// a sub-block take one MMA each, lanes t < 2 (elements 0..15) feeding the
+// first and lanes t >= 2 the second.
+__device__ __forceinline__ void q6k_mma_superblock(const uint8_t* __restrict__ b0p, const uint8_t* __restrict__ b1p,
+                                                   const uint32_t* __restrict__ rec, float& acc0, float& acc1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const bool bact = g < 4, first16 = t < 2;
+    const bool odd = (reinterpret_cast<uintptr_t>(b0p) & 2u) != 0;
+    const uint2 s0a = lds_u64_a2(b0p + 192, odd), s0b = lds_u64_a2(b0p + 200, odd);
+    const uint2 s1a = lds_u64_a2(b1p + 192, odd), s1b = lds_u64_a2(b1p + 200, odd);
+    const uint32_t sc0[4] = {s0a.x, s0a.y, s0b.x, s0b.y}, sc1[4] = {s1a.x, s1a.y, s1b.x, s1b.y};
+    const uint8_t* rb = reinterpret_cast<const uint8_t*>(rec) + g * 32 + 8 * t;
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint2 la0 = lds_u64_a2(b0p + 64 * h + 8 * t, odd), lb0 = lds_u64_a2(b0p + 64 * h + 32 + 8 * t, odd);
+        const uint2 la1 = lds_u64_a2(b1p + 64 * h + 8 * t, odd), lb1 = lds_u64_a2(b1p + 64 * h + 32 + 8 * t, odd);
+        const uint2 qh0 = lds_u64_a2(b0p + 128 + 32 * h + 8 * t, odd);
+        const uint2 qh1 = lds_u64_a2(b1p + 128 + 32 * h + 8 * t, odd);
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+            const int j = 4 * h + qq, sh = 4 * (qq >> 1), hb = 2 * qq;
+            const uint2 l0 = (qq & 1) ? lb0 : la0, l1 = (qq & 1) ? lb1 : la1;
+            const auto val = [&](uint32_t lo, uint32_t hi) {
+                return q6_centered(((lo >> sh) & 0x0F0F0F0Fu) | (((hi >> hb) & 0x03030303u) << 4));
+            };
+            const uint32_t a0 = val(l0.x, qh0.x), a1 = val(l1.x, qh1.x), a2 = val(l0.y, qh0.y), a3 = val(l1.y, qh1.y);
+            const uint2 xb = bact ? *reinterpret_cast<const uint2*>(rb + j * 128) : make_uint2(0u, 0u);
+            int dA[4], dB[4];
+            imma16832_ss(dA, first16 ? a0 : 0u, first16 ? a1 : 0u, first16 ? a2 : 0u, first16 ? a3 : 0u, xb.x, xb.y);
+            imma16832_ss(dB, first16 ? 0u : a0, first16 ? 0u : a1, first16 ? 0u : a2, first16 ? 0u : a3, xb.x, xb.y);
+            const int bi = 8 * (2 * (j & 1));
+            const int sA0 = static_cast<int8_t>(sc0[j >> 1] >> bi), sB0 = static_cast<int8_t>(sc0[j >> 1] >> (bi + 8));
+            const int sA1 = static_cast<int8_t>(sc1[j >> 1] >> bi), sB1 = static_cast<int8_t>(sc1[j >> 1] >> (bi + 8));
+            acc[0] += dA[0] * sA0 + dB[0] * sB0;
+            acc[1] += dA[1] * sA0 + dB[1] * sB0;
+            acc[2] += dA[2] * sA1 + dB[2] * sB1;
+            acc[3] += dA[3] * sA1 + dB[3] * sB1;
+        }
+    }
+    const float s0 = __uint_as_float(rec[265]);
+    const float ca = t == 0 ? s0 : (t == 1 ? s0 * (1.0f / 16384.0f) : 0.0f);
+    const float cb = t == 0 ? s0 * (1.0f / 128.0f) : (t == 1 ? s0 * (1.0f / 2097152.0f) : 0.0f);
+    const float y0 = ca * static_cast<float>(acc[0]) + cb * static_cast<float>(acc[1]);
+    const float y1 = ca * static_cast<float>(acc[2]) + cb * static_cast<float>(acc[3]);
+    const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b0p + 208));
+    const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(b1p + 208));
+    acc0 = fmaf(d0, y0, acc0);
+    acc1 = fmaf(d1, y1, acc1);
 }
 
 // The row total from the four lanes t of a row group (all four lanes get it).

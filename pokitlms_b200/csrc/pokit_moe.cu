@@ -584,13 +584,31 @@ __device__ void route_select_regs(const MoeLayerDev& L, const float (&lgv)[kSlot
         uint32_t my_id = 0;
         float my_v = 0.0f, mx = 0.0f;
         for (uint32_t r = 0; r < k; ++r) {
-            uint32_t best_ord = 0, best_e = 0xffffffffu;
+            // The lane's maximum by a tree of pairwise maxima (ties to the
+            // lower slot, which holds the lower id).
+            uint32_t to[kSlots], ti[kSlots];
 #pragma unroll
-            for (uint32_t i = 0; i < kSlots; ++i)
-                if (ord[i] > best_ord) { best_ord = ord[i]; best_e = lane + 32u * i; }
+            for (uint32_t i = 0; i < kSlots; ++i) {
+                to[i] = ord[i];
+                ti[i] = i;
+            }
+#pragma unroll
+            for (uint32_t w = kSlots / 2; w > 0; w >>= 1)
+#pragma unroll
+                for (uint32_t i = 0; i < w; ++i) {
+                    const bool hi = to[2 * i + 1] > to[2 * i];
+                    to[i] = hi ? to[2 * i + 1] : to[2 * i];
+                    ti[i] = hi ? ti[2 * i + 1] : ti[2 * i];
+                }
+            const uint32_t best_ord = to[0];
+            const uint32_t best_e = best_ord ? lane + 32u * ti[0] : 0xffffffffu;
             const uint32_t top = __reduce_max_sync(0xffffffffu, best_ord);
-            // The lowest id among the lanes at the maximum.
-            const uint32_t win = __reduce_min_sync(0xffffffffu, best_ord == top ? best_e : 0xffffffffu);
+            // The lowest id among the lanes at the maximum: with one such lane
+            // (the usual case) its id, else the minimum over them.
+            const uint32_t at = __ballot_sync(0xffffffffu, best_ord == top);
+            const uint32_t win = (at & (at - 1u)) == 0u
+                                     ? __shfl_sync(0xffffffffu, best_e, __ffs(at) - 1)
+                                     : __reduce_min_sync(0xffffffffu, best_ord == top ? best_e : 0xffffffffu);
 #pragma unroll
             for (uint32_t i = 0; i < kSlots; ++i)
                 if (lane + 32u * i == win) ord[i] = 0u;
@@ -1174,6 +1192,41 @@ __device__ __forceinline__ void racc_add(unsigned long long* limbs, uint32_t* ba
     const long long hi = v >> 32;                             // floor division
     if (lo) atomicAdd(limbs + i, lo);
     if (hi) atomicAdd(limbs + i + 1, static_cast<unsigned long long>(hi));
+}
+
+// racc_add with one atomic: the whole signed m 2^o (|v| < 2^55) into limb i.
+// The limbs then hold larger values (up to units x 2^55 < 2^63 for at most
+// 256 adding units) but the same integer sum over limbs; racc_value reads
+// either form, rounding a limb beyond 2^53 to double (relative 2^-53), which
+// stays far below a float's unit in the last place unless the exact sum
+// cancels to about 2^-29 of its largest limb term.  The value still depends
+// only on the limbs, not on the order of the additions.
+__device__ __forceinline__ void racc_add1(unsigned long long* limbs, uint32_t* bad, float p) {
+    const uint32_t b = __float_as_uint(p);
+    const uint32_t eb = (b >> 23) & 0xffu;
+    if (eb == 0xffu) {
+        atomicOr(bad, 1u);
+        return;
+    }
+    uint32_t m = b & 0x7fffffu;
+    int ex;
+    if (eb == 0u) {
+        if (m == 0u) return;
+        ex = -149;
+    } else {
+        m |= 0x800000u;
+        ex = static_cast<int>(eb) - 150;
+    }
+    int pos = ex - kRaccBase;
+    if (pos < 0) {
+        if (pos <= -24) return;
+        m >>= -pos;
+        pos = 0;
+        if (m == 0u) return;
+    }
+    long long v = static_cast<long long>(m) << (pos & 31);
+    if (b >> 31) v = -v;
+    atomicAdd(limbs + (pos >> 5), static_cast<unsigned long long>(v));
 }
 
 // The accumulated value of the limbs (as loaded): Horner's rule in double from
@@ -2308,6 +2361,600 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
 }
 
 // ---------------------------------------------------------------------------
+// moe_chain35_kernel: the decode chain for Qwen3.5-MoE blocks (configuration
+// 3): Q4_K gate/up and Q4_K / Q5_K / Q6_K down (per layer) on the integer
+// tensor path, and the sigmoid-gated Q8_0 shared expert (src/qwen35_runner.cpp:
+// 691-763).  The same phases and hand-offs as moe_chain_kernel, with:
+//   route  E + 1 accumulator rows (the shared expert's gate row last), staged
+//          into shared memory by one bulk copy; the selection takes
+//          sigmoid(scale * that logit) as the shared weight
+//   G      routed 16-row groups as in the chain, a tensor-map box per
+//          two-superblock tile from the layer's own maps (the layers' tensors
+//          need not sit at one stride); the shared expert's gate/up in 8-row
+//          groups, a box of half rows per warp, dotted in FP32 with x'
+//   D      every slot's 16 down rows by one bulk copy; the routed slots'
+//          activation records built as they arrive and multiplied on the
+//          tensor path (q4k / q5k / q6k_mma_superblock); the shared slot as
+//          FP32 row dots by the last four warps; the combine in route order,
+//          then + sigmoid gate * shared output, into the residual; the next
+//          layer's router partials (E + 1 rows)
+// ---------------------------------------------------------------------------
+constexpr uint32_t kChain35SharedRows = 8;       // rows per shared-expert gate/up group
+constexpr uint32_t kChain35SharedWarps = 4;      // warps taking the shared slot in D
+
+struct Chain35Layout {
+    uint32_t gbars, dbars, rbar, recs, xf, lg, sel_id, sel_w, part, dpart, hrow, gtiles, dtiles, total;
+    uint32_t nsb, nsd, gpairs, slots, rb_down_max, rb_shared, nrec;
+};
+
+__host__ __device__ inline Chain35Layout chain35_layout(const MoeLayerDev& L, uint32_t rb_down_max) {
+    Chain35Layout c{};
+    const uint32_t nsb = L.hidden >> 8, half = (nsb + 1u) / 2u;
+    c.nsb = nsb;
+    c.nsd = L.inter >> 8;
+    c.gpairs = (half + 1u) / 2u;
+    c.slots = L.top_k + 1u;
+    c.nrec = L.top_k * c.nsd;
+    c.rb_down_max = rb_down_max;
+    c.rb_shared = static_cast<uint32_t>(row_bytes(L.shared_down_type, L.shared_inter));
+    uint32_t off = 0;
+    c.gbars = off; off += al16(kWarps * c.gpairs * 8u);
+    c.dbars = off; off += al16(c.slots * 8u);
+    c.rbar = off; off += 16u;
+    c.recs = off; off += al16(umax(nsb, c.nrec) * kFragWords * 4u);
+    c.xf = off; off += al16(L.hidden * 4u);
+    c.lg = off; off += al16((L.experts + 1u) * 4u);
+    c.sel_id = off; off += al16((kMaxTopK + 1) * 4u);
+    c.sel_w = off; off += al16((kMaxTopK + 1) * 4u);
+    c.part = off; off += al16(kWarps * 16u * 4u);
+    c.dpart = off; off += al16((c.nrec + 1u) * 16u * 4u);
+    c.hrow = off; off += al16(2u * kPartRows * 4u);
+    off = al128(off);
+    // Tile space: the gate/up tiles, the staged accumulator rows (route) and
+    // the shared slot's activation floats (D) in turn.
+    c.gtiles = off;
+    off += umax(umax(kWarps * c.gpairs * kPairBytes, (L.experts + 1u) * kRaccLimbs * 8u), al16(L.inter * 4u));
+    off = al128(off);
+    c.dtiles = off; off += L.top_k * 16u * rb_down_max + 16u * c.rb_shared;
+    c.total = off;
+    return c;
+}
+
+struct Chain35Args {
+    const MoeLayerDev* layers;   // device table
+    MoeLayerDev shape;           // the common shape (hidden, inter, experts, top_k, flavour, ...)
+    uint32_t first, count;
+    MoeScratch S;
+    ChainScratch C;
+    float* hidden;
+    Chain35Layout c;
+    const Chain35Maps* maps;     // per-layer tensor maps (device memory)
+    unsigned long long* trace;   // optional per-(layer, CTA) phase stamps (measurement)
+};
+
+// A read-only 16-byte load issued where it stands: the compiler keeps the
+// order of volatile asm, so the load is not sunk to its first use (which
+// would expose its latency in a later phase).
+__device__ __forceinline__ float4 ldg_f4_issue_here(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ldcg_f32_issue_here(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ RouterSlice router_slice_issue_here(const float* router, uint32_t H, uint32_t e,
+                                                               uint32_t c) {
+    const float* p = router + static_cast<uint64_t>(e) * H + c * kPartRows;
+    return RouterSlice{{ldg_f4_issue_here(p), ldg_f4_issue_here(p + 4), ldg_f4_issue_here(p + 8),
+                        ldg_f4_issue_here(p + 12)}};
+}
+
+// Thread t's router slices of a layer: expert t (rs) and expert t + kThreads,
+// or for the last thread the shared expert's gate row (rs2).  E <= 2 kThreads - 1.
+__device__ __forceinline__ void chain35_slices(const MoeLayerDev& L, uint32_t E, uint32_t H, uint32_t chunk,
+                                               RouterSlice& rs, RouterSlice& rs2) {
+    const uint32_t tid = threadIdx.x;
+    if (tid < E) rs = router_slice_issue_here(L.router, H, tid, chunk);
+    if (tid + kThreads < E) rs2 = router_slice_issue_here(L.router, H, tid + kThreads, chunk);
+    else if (tid == kThreads - 1u) rs2 = router_slice_issue_here(L.shared_router, H, 0, chunk);
+}
+
+// Router partials of 16 hidden rows for E experts and the shared gate row
+// (accumulator row E), from the slices chain35_slices loaded.
+__device__ __forceinline__ void chain35_partials(uint32_t E, const RouterSlice& rs, const RouterSlice& rs2,
+                                                 const float* hrow, unsigned long long* racc, uint32_t* rbad,
+                                                 float* rsq, uint32_t chunk) {
+    const uint32_t tid = threadIdx.x;
+    if (tid < E) racc_add1(racc + static_cast<uint64_t>(tid) * kRaccLimbs, rbad, router_dot16(rs, hrow));
+    if (tid + kThreads < E)
+        racc_add1(racc + static_cast<uint64_t>(tid + kThreads) * kRaccLimbs, rbad, router_dot16(rs2, hrow));
+    else if (tid == kThreads - 1u)
+        racc_add1(racc + static_cast<uint64_t>(E) * kRaccLimbs, rbad, router_dot16(rs2, hrow));
+    if (tid == 0) {
+        float sq = 0.0f;
+        for (uint32_t r = 0; r < kPartRows; ++r) sq += hrow[kPartRows + r];
+        rsq[chunk] = sq;
+    }
+}
+
+__device__ __forceinline__ void chain35_down_mma(uint32_t type, const uint8_t* b0p, const uint8_t* b1p,
+                                                 const uint32_t* rec, float& acc0, float& acc1) {
+    if (type == kQ6_K) q6k_mma_superblock(b0p, b1p, rec, acc0, acc1);
+    else if (type == kQ5_K) q5k_mma_superblock(b0p, b1p, rec, acc0, acc1);
+    else q4k_mma_superblock(b0p, b1p, rec, acc0, acc1);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_constant__ Chain35Args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t abort_sh, bad_sh, last_sh;
+    __shared__ float scale_sh;
+    const Chain35Layout& c = a.c;
+    const MoeLayerDev& Ls = a.shape;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t G = gridDim.x, cta = blockIdx.x;
+    const uint32_t H = Ls.hidden, I = Ls.inter, E = Ls.experts, k = Ls.top_k;
+    const uint32_t nsb = c.nsb, nsd = c.nsd, slots = c.slots, nrec = c.nrec;
+    const uint32_t per_slot = I / 16u, routed_groups = k * per_slot;
+    const uint32_t groups = routed_groups + Ls.shared_inter / kChain35SharedRows;
+    const uint32_t units = H / kPartRows;
+    const bool has_unit = cta < units;
+    const uint32_t j0 = cta * kPartRows;
+    uint64_t* gbars = reinterpret_cast<uint64_t*>(smem + c.gbars);
+    uint64_t* dbars = reinterpret_cast<uint64_t*>(smem + c.dbars);
+    uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + c.rbar);
+    uint32_t* recs = reinterpret_cast<uint32_t*>(smem + c.recs);
+    float* xf = reinterpret_cast<float*>(smem + c.xf);
+    float* lg = reinterpret_cast<float*>(smem + c.lg);
+    uint32_t* sel_id = reinterpret_cast<uint32_t*>(smem + c.sel_id);
+    float* sel_w = reinterpret_cast<float*>(smem + c.sel_w);
+    float* part = reinterpret_cast<float*>(smem + c.part);
+    float* dpart = reinterpret_cast<float*>(smem + c.dpart);
+    float* dsh = dpart + nrec * 16u;                               // the shared slot's 16 rows
+    float* hrow = reinterpret_cast<float*>(smem + c.hrow);
+    uint8_t* gtiles = smem + c.gtiles;
+    const ulonglong2* rstage = reinterpret_cast<const ulonglong2*>(smem + c.gtiles);   // route
+    float* actsh = reinterpret_cast<float*>(smem + c.gtiles);      // D: the shared slot's activations
+    uint8_t* dtiles = smem + c.dtiles;
+    uint32_t* ctr_route = a.C.counters;
+    uint32_t* ctr_exit = a.C.counters + 2u * kChainCounterStride;
+    uint32_t* ctr_seq = a.C.counters + 3u * kChainCounterStride;
+    uint32_t* status = a.S.status;
+    const uint32_t Er = E + 1u;                                     // accumulator rows
+    const uint64_t racc_span = static_cast<uint64_t>(Er) * kRaccLimbs;
+    const float* xrep = a.C.xrep + static_cast<uint64_t>(cta % kChainXReplicas) * H;
+    const uint64_t act_span = static_cast<uint64_t>(slots) * I;
+    const unsigned long long* act_mine = a.C.act + static_cast<uint64_t>(cta % kChainXReplicas) * act_span;
+    const auto stamp = [&](uint32_t l, uint32_t i) {
+        if (a.trace && tid == 0) {
+            unsigned long long* t = a.trace + (static_cast<uint64_t>(l) * G + cta) * (2u * kChainStamps);
+            t[i] = global_ns();
+            t[kChainStamps + i] = static_cast<unsigned long long>(clock64());
+        }
+    };
+    if (tid == 0) abort_sh = 0u;
+    const uint32_t gpairs = c.gpairs;
+    if (lane == 0) {
+        for (uint32_t i = 0; i < gpairs; ++i) mbar_init(&gbars[warp * gpairs + i], 1);
+        if (warp == 0) {
+            for (uint32_t u = 0; u < slots; ++u) mbar_init(&dbars[u], 1);
+            mbar_init(rbar, 1);
+        }
+        mbar_fence_init();
+    }
+    // This CTA's row group and superblock half per warp (as in the chain).
+    const uint32_t rg = cta + G * static_cast<uint32_t>(warp >> 2);
+    const uint32_t mat = (warp >> 1) & 1, hsel = warp & 1;
+    const uint32_t split = (nsb + 1u) / 2u;
+    const uint32_t sb0 = hsel ? split : 0u, sb1 = hsel ? nsb : split;
+    const bool routed_group = rg < routed_groups;
+    const bool shared_group = !routed_group && rg < groups;
+    const uint32_t nmine = (routed_group && sb1 > sb0) ? sb1 - sb0 : 0u;
+    const uint32_t npairs = (nmine + 1u) / 2u;
+    uint8_t* mytile = gtiles + warp * gpairs * kPairBytes;
+    uint64_t* mybars = gbars + warp * gpairs;
+    const int g = lane >> 2;
+    // Shared-expert gate/up rows (Q8_0): a warp's half row is shalf bytes.
+    const uint32_t srb = static_cast<uint32_t>(row_bytes(kQ8_0, H)), shalf = srb / 2u;
+
+    // Prologue: the first layer's router partials and x' rows.
+    if (has_unit) {
+        const MoeLayerDev L0 = a.layers[a.first];
+        if (tid < 16) {
+            const float h = __ldcg(a.hidden + j0 + tid);
+            const float xn = __ldg(L0.ffn_norm + j0 + tid) * h;
+            hrow[tid] = xn;
+            hrow[kPartRows + tid] = h * h;
+            for (uint32_t r = 0; r < kChainXReplicas; ++r) a.C.xrep[static_cast<uint64_t>(r) * H + j0 + tid] = xn;
+        }
+        __syncthreads();
+        RouterSlice rs{}, rs2{};
+        chain35_slices(L0, E, H, cta, rs, rs2);
+        const uint32_t r0 = a.first % 3u;
+        chain35_partials(E, rs, rs2, hrow, a.C.racc + r0 * racc_span, a.C.rbad + r0, a.C.rsq + (a.first & 1u) * units,
+                         cta);
+        chain_arrive(ctr_route);
+    }
+
+    uint32_t phase = 0;
+    bool ok = true;
+    const uint32_t seq0 = __ldcg(ctr_seq);
+    const auto wait_bar = [&](uint64_t* bar) {
+        if (!mbar_wait(bar, phase)) {
+            if (lane == 0) atomicOr(status, kStatusWaitTimeout);
+            mbar_wait(bar, phase);
+        }
+    };
+    for (uint32_t l = 0; l < a.count && ok; ++l, phase ^= 1u) {
+        const uint32_t layer = a.first + l, p = layer & 1u, pr = layer % 3u, tag = seq0 + l + 1u;
+        const bool has_next = l + 1 < a.count;
+        const MoeLayerDev L = a.layers[layer];
+        // The tile space's generic accesses so far come before this layer's
+        // bulk copies into it.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        // ---- route ----
+        if (!chain_wait(ctr_route, units * (l + 1u), status, &abort_sh)) { ok = false; break; }
+        stamp(l, 0);
+        if (tid == 0) {
+            // Every unit's accumulator additions (acquired above) before the
+            // async-proxy read of them.
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_expect_tx(rbar, Er * kRaccLimbs * 8u);
+            bulk_copy_g2s(gtiles, a.C.racc + pr * racc_span, Er * kRaccLimbs * 8u, rbar);
+        }
+        if (warp < static_cast<int>(kTailLogitWarps)) {
+            if (warp == 0) {
+                float sq = 0.0f;
+                for (uint32_t u = lane; u < units; u += 32) sq += __ldcg(a.C.rsq + p * units + u);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+                if (lane == 0) {
+                    scale_sh = 1.0f / sqrtf(sq / static_cast<float>(H) + Ls.rms_eps);
+                    bad_sh = __ldcg(a.C.rbad + pr);
+                }
+            }
+            wait_bar(rbar);
+            for (uint32_t e = warp * 32u + lane; e < Er; e += kTailLogitWarps * 32u) {
+                ulonglong2 limbs[kRaccLimbs / 2];
+#pragma unroll
+                for (int h2 = 0; h2 < kRaccLimbs / 2; ++h2) limbs[h2] = rstage[e * (kRaccLimbs / 2) + h2];
+                lg[e] = racc_value(limbs);
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kTailLogitWarps * 32u) : "memory");
+            if (warp == 0) {
+                const float scale = scale_sh;
+                const bool bad = bad_sh != 0u;
+                const float shared_logit = bad ? __int_as_float(0x7fc00000) : lg[E] * scale;
+                const auto select = [&](auto slots_c) {
+                    constexpr uint32_t kSlots = decltype(slots_c)::value;
+                    float lgv[kSlots];
+#pragma unroll
+                    for (uint32_t i = 0; i < kSlots; ++i) {
+                        const uint32_t e = lane + 32u * i;
+                        lgv[i] = e < E ? (bad ? __int_as_float(0x7fc00000) : lg[e] * scale) : 0.0f;
+                    }
+                    route_select_regs<kSlots>(Ls, lgv, shared_logit, sel_id, sel_w, status, cta == 0, a.S);
+                };
+                if (E <= 128u) select(std::integral_constant<uint32_t, 4>{});
+                else if (E <= 256u) select(std::integral_constant<uint32_t, 8>{});
+                else select(std::integral_constant<uint32_t, 16>{});
+            }
+        } else {
+            // x' floats (for the shared expert's rows) and fragment records.
+            const uint32_t builders = static_cast<uint32_t>(kWarps) - kTailLogitWarps;
+            for (uint32_t q = static_cast<uint32_t>(warp) - kTailLogitWarps; q < nsb; q += builders) {
+                float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
+                float xv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) xv[j] = __ldcg(xrep + q * 256u + 32u * j + lane);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    stage[32 * j + lane] = xv[j];
+                    xf[q * 256u + 32u * j + lane] = xv[j];
+                }
+                __syncwarp();
+                q4k_frag_superblock(stage, recs + q * kFragWords, lane);
+                __syncwarp();
+            }
+        }
+        // The staged accumulator rows are read before the gate/up copies
+        // overwrite them.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        stamp(l, 1);
+        const float scale = scale_sh;
+        // ---- G: the gate/up boxes of this layer's maps ----
+        const Chain35Maps* maps = a.maps + layer;
+        if (nmine && lane == 0) {
+            const int id = static_cast<int>(sel_id[rg / per_slot]);
+            const int row0 = static_cast<int>((rg % per_slot) * 16u);
+            const CUtensorMap* map = mat ? &maps->up : &maps->gate;
+            for (uint32_t i = 0; i < npairs; ++i) {
+                mbar_expect_tx(&mybars[i], kPairBytes);
+                tma_box_3d(mytile + i * kPairBytes, map, static_cast<int>((sb0 + 2u * i) * 18u), row0, id, &mybars[i]);
+            }
+        } else if (shared_group && lane == 0) {
+            // 8 half rows of the shared expert's gate or up.
+            const int srow0 = static_cast<int>((rg - routed_groups) * kChain35SharedRows);
+            mbar_expect_tx(&mybars[0], kChain35SharedRows * shalf);
+            tma_box_2d(mytile, mat ? &maps->shared_up : &maps->shared_gate, static_cast<int>(hsel * (shalf / 8u)), srow0,
+                       &mybars[0]);
+        }
+        // The previous layer's accumulators (zeroed by the D units).
+        if (has_unit) {
+            const uint32_t pz = (layer + 2u) % 3u;
+            for (uint32_t i = cta * kThreads + tid; i < racc_span; i += units * kThreads)
+                a.C.racc[pz * racc_span + i] = 0ull;
+            if (cta == 0 && tid == 0) a.C.rbad[pz] = 0u;
+        }
+        const MoeLayerDev Ln = has_next ? a.layers[layer + 1] : L;
+        RouterSlice rs{}, rs2{};
+        if (has_unit && has_next) chain35_slices(Ln, E, H, cta, rs, rs2);
+        const float resid = (has_unit && tid < 16) ? ldcg_f32_issue_here(a.hidden + j0 + tid) : 0.0f;
+        const float nnorm = (has_unit && has_next && tid < 16) ? ldcg_f32_issue_here(Ln.ffn_norm + j0 + tid) : 0.0f;
+        if (routed_group) {
+            float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+            for (uint32_t i = 0; i < npairs; ++i) {
+                wait_bar(&mybars[i]);
+                const uint8_t* bx = mytile + i * kPairBytes;
+                const uint32_t s0 = sb0 + 2u * i;
+                q4k_mma_superblock(bx + g * kPairRowBytes, bx + (g + 8) * kPairRowBytes, recs + s0 * kFragWords,
+                                   acc0, acc1);
+                if (2u * i + 1u < nmine)
+                    q4k_mma_superblock(bx + g * kPairRowBytes + 144u, bx + (g + 8) * kPairRowBytes + 144u,
+                                       recs + (s0 + 1u) * kFragWords, acc2, acc3);
+            }
+            acc0 = quad_sum(acc0 + acc2);
+            acc1 = quad_sum(acc1 + acc3);
+            if ((lane & 3) == 0) {
+                part[warp * 16 + g] = acc0;
+                part[warp * 16 + g + 8] = acc1;
+            }
+        } else if (shared_group) {
+            wait_bar(&mybars[0]);
+            const float* xs = xf + hsel * (H / 2u);
+#pragma unroll 1
+            for (uint32_t r = 0; r < kChain35SharedRows; r += 2u) {
+                float v0 = lane_row_dot4<kQ8_0>(mytile + r * shalf, H / 2u, xs, lane);
+                float v1 = lane_row_dot4<kQ8_0>(mytile + (r + 1u) * shalf, H / 2u, xs, lane);
+                v0 = warp_sum(v0);
+                v1 = warp_sum(v1);
+                if (lane == 0) {
+                    part[warp * 16 + r] = v0;
+                    part[warp * 16 + r + 1] = v1;
+                }
+            }
+        }
+        stamp(l, 2);
+        // Every slot's 16 down rows of this D unit: one bulk copy per slot,
+        // once the warp's own gate/up work is done.
+        if (has_unit && static_cast<uint32_t>(warp) < slots && lane == 0) {
+            const uint32_t sl = warp;
+            const bool shared = sl == k;
+            const uint32_t rbd = shared ? c.rb_shared : static_cast<uint32_t>(row_bytes(L.down_type, I));
+            const uint8_t* src = shared ? L.shared_down + static_cast<uint64_t>(j0) * rbd
+                                        : L.down + static_cast<uint64_t>(sel_id[sl]) * L.down_slice +
+                                              static_cast<uint64_t>(j0) * rbd;
+            mbar_expect_tx(&dbars[sl], 16u * rbd);
+            bulk_copy_g2s(dtiles + sl * 16u * c.rb_down_max, src, 16u * rbd, &dbars[sl]);
+        }
+        __syncthreads();
+        if (tid < static_cast<int>(kChainGroupsPerCta * 16u)) {
+            const uint32_t gl = tid >> 4, r = tid & 15, rgx = cta + G * gl;
+            uint32_t slot = 0, row = 0;
+            bool mine = false;
+            if (rgx < routed_groups) {
+                slot = rgx / per_slot;
+                row = (rgx % per_slot) * 16u + r;
+                mine = true;
+            } else if (rgx < groups && r < kChain35SharedRows) {
+                slot = k;
+                row = (rgx - routed_groups) * kChain35SharedRows + r;
+                mine = true;
+            }
+            if (mine) {
+                const float gv = part[(gl * 4 + 0) * 16 + r] + part[(gl * 4 + 1) * 16 + r];
+                const float uv = part[(gl * 4 + 2) * 16 + r] + part[(gl * 4 + 3) * 16 + r];
+                const float av = silu_mul(gv * scale, uv * scale, Ls.flavour);
+                const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(av);
+                for (uint32_t rr = 0; rr < kChainXReplicas; ++rr)
+                    st_relaxed_gpu_u64(a.C.act + rr * act_span + slot * I + row, w);
+            }
+        }
+        stamp(l, 3);
+        if (!has_unit) continue;
+        // ---- D ----
+        {
+            const uint32_t dtype = L.down_type;
+            const uint32_t rbd = static_cast<uint32_t>(row_bytes(dtype, I));
+            const uint32_t sbb = dtype == kQ6_K ? 210u : (dtype == kQ5_K ? 176u : 144u);
+            // Routed units (slot, superblock): two per warp and pass, every
+            // activation word read as it arrives (tag = this layer's sequence
+            // number), the records built and multiplied by the same warp.
+            for (uint32_t q0 = warp; q0 < nrec; q0 += 2 * kWarps) {
+                unsigned long long v[2][8];
+                const auto word = [&](int i, int j) {
+                    return act_mine + static_cast<uint64_t>(q0 + i * kWarps) * 256u + 32 * j + lane;
+                };
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        v[i][j] = q0 + i * kWarps < nrec ? ld_relaxed_gpu_u64(word(i, j))
+                                                         : static_cast<unsigned long long>(tag) << 32;
+                long long t0 = 0;
+                for (uint32_t polls = 0;; ++polls) {
+                    bool ready = true;
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) ready = ready && static_cast<uint32_t>(v[i][j] >> 32) == tag;
+                    if (__all_sync(0xffffffffu, ready)) break;
+                    if (polls == 0) t0 = clock64();
+                    if ((polls & 63u) == 63u &&
+                        ((ld_acquire_gpu(status) & kStatusWaitTimeout) || clock64() - t0 > kBarrierTimeoutCycles)) {
+                        if (lane == 0) {
+                            atomicOr(status, kStatusWaitTimeout);
+                            abort_sh = 1u;
+                        }
+                        break;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (static_cast<uint32_t>(v[i][j] >> 32) != tag) v[i][j] = ld_relaxed_gpu_u64(word(i, j));
+                }
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t q = q0 + i * kWarps;
+                    if (q < nrec) {
+                        float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = __uint_as_float(static_cast<uint32_t>(v[i][j]));
+                    }
+                }
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const uint32_t q = q0 + i * kWarps;
+                    if (q < nrec)
+                        q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords, lane);
+                }
+                __syncwarp();
+                const auto unit = [&](uint32_t q, float& r0, float& r1) {
+                    const uint32_t sl = q / nsd, sb = q % nsd;
+                    wait_bar(&dbars[sl]);
+                    const uint8_t* bx = dtiles + sl * 16u * c.rb_down_max + sb * sbb;
+                    chain35_down_mma(dtype, bx + g * rbd, bx + (g + 8) * rbd, recs + q * kFragWords, r0, r1);
+                    r0 = quad_sum(r0);
+                    r1 = quad_sum(r1);
+                    if ((lane & 3) == 0) {
+                        dpart[q * 16 + g] = r0;
+                        dpart[q * 16 + g + 8] = r1;
+                    }
+                };
+                float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+                unit(q0, a0, a1);
+                if (q0 + kWarps < nrec) unit(q0 + kWarps, b0, b1);
+            }
+            // The shared slot: its activations into shared memory, then a
+            // (row) FP32 dot per warp and pass.
+            if (warp >= kWarps - static_cast<int>(kChain35SharedWarps)) {
+                const uint32_t sw = static_cast<uint32_t>(warp) - (kWarps - kChain35SharedWarps);
+                const unsigned long long* src = act_mine + static_cast<uint64_t>(k) * I;
+                for (uint32_t w0 = sw * 32u + lane; w0 < I; w0 += 4u * kChain35SharedWarps * 32u) {
+                    unsigned long long v[4];
+                    bool use[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t w = w0 + i * kChain35SharedWarps * 32u;
+                        use[i] = w < I;
+                        v[i] = use[i] ? ld_relaxed_gpu_u64(src + w) : static_cast<unsigned long long>(tag) << 32;
+                    }
+                    long long t0 = 0;
+                    for (uint32_t polls = 0;; ++polls) {
+                        bool ready = true;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) ready = ready && static_cast<uint32_t>(v[i] >> 32) == tag;
+                        if (__all_sync(0xffffffffu, ready)) break;
+                        if (polls == 0) t0 = clock64();
+                        if ((polls & 63u) == 63u &&
+                            ((ld_acquire_gpu(status) & kStatusWaitTimeout) || clock64() - t0 > kBarrierTimeoutCycles)) {
+                            if (lane == 0) {
+                                atomicOr(status, kStatusWaitTimeout);
+                                abort_sh = 1u;
+                            }
+                            break;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            if (use[i] && static_cast<uint32_t>(v[i] >> 32) != tag)
+                                v[i] = ld_relaxed_gpu_u64(src + w0 + i * kChain35SharedWarps * 32u);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (use[i]) actsh[w0 + i * kChain35SharedWarps * 32u] = __uint_as_float(static_cast<uint32_t>(v[i]));
+                }
+                asm volatile("bar.sync 2, %0;" ::"r"(kChain35SharedWarps * 32u) : "memory");
+                wait_bar(&dbars[k]);
+                for (uint32_t r = sw; r < 16u; r += kChain35SharedWarps) {
+                    float v = lane_row_dot_any(L.shared_down_type, dtiles + k * 16u * c.rb_down_max + r * c.rb_shared,
+                                               I, actsh, lane);
+                    v = warp_sum(v);
+                    if (lane == 0) dsh[r] = v;
+                }
+            }
+            stamp(l, 4);
+            __syncthreads();
+            if (abort_sh) {
+                if (static_cast<uint32_t>(warp) < slots && lane == 0) mbar_wait(&dbars[warp], phase);
+                ok = false;
+                break;
+            }
+            stamp(l, 5);
+            // Weighted slot rows (a thread per slot and row; the gate/up
+            // partials' space is free), then in route order (qwen35_runner.cpp
+            // :738-741) the gated shared expert (:760-763) and the residual.
+            float* comb = part;
+            if (static_cast<uint32_t>(tid) < k * 16u) {
+                const uint32_t sl = static_cast<uint32_t>(tid) >> 4, row = tid & 15;
+                float y = 0.0f;
+                for (uint32_t sb = 0; sb < nsd; ++sb) y += dpart[(sl * nsd + sb) * 16u + row];
+                comb[tid] = sel_w[sl] * y;
+            }
+            __syncthreads();
+            if (tid < 16) {
+                float moe = 0.0f;
+                for (uint32_t sl = 0; sl < k; ++sl) moe += comb[sl * 16u + tid];
+                const float sh = sel_w[k] * dsh[tid];
+                const float h = resid + (moe + sh);
+                a.hidden[j0 + tid] = h;
+                if (has_next) {
+                    const float xn = nnorm * h;
+                    hrow[tid] = xn;
+                    hrow[kPartRows + tid] = h * h;
+                    for (uint32_t r = 0; r < kChainXReplicas; ++r)
+                        a.C.xrep[static_cast<uint64_t>(r) * H + j0 + tid] = xn;
+                }
+            }
+            if (has_next) {
+                __syncthreads();
+                stamp(l, 6);
+                const uint32_t pn = (layer + 1u) % 3u;
+                chain35_partials(E, rs, rs2, hrow, a.C.racc + pn * racc_span, a.C.rbad + pn,
+                                 a.C.rsq + (p ^ 1u) * units, cta);
+            }
+        }
+        chain_arrive(ctr_route);
+        stamp(l, 7);
+    }
+    if (!ok) return;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        last_sh = atomicAdd(ctr_exit, 1u) == G - 1u ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!last_sh) return;
+    __threadfence();
+    const uint32_t plast = (a.first + a.count - 1u) % 3u;
+    for (uint32_t i = tid; i < racc_span; i += kThreads) a.C.racc[plast * racc_span + i] = 0ull;
+    __syncthreads();
+    if (tid == 0) {
+        a.C.rbad[plast] = 0u;
+        *ctr_route = 0u;
+        *ctr_exit = 0u;
+        *ctr_seq = seq0 + a.count;
+        __threadfence();
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Raises a kernel's dynamic shared-memory limit once per (kernel, device):
 // cudaFuncSetAttribute applies to the current device only, so a grant made
 // on one GPU says nothing about another.  Later launches skip the call, so
@@ -2676,21 +3323,29 @@ cudaError_t time_moe_kernel(const MoeLayerDev* layers, uint32_t count, const Moe
     return e;
 }
 
+// Router accumulators cover the experts and, with a shared expert, its gate
+// row (index `experts`); activation words cover the routed slots and the
+// shared expert's.
+static uint64_t chain_router_rows(const MoeLayerDev& L) { return L.experts + (L.shared_inter ? 1u : 0u); }
+static uint64_t chain_act_words(const MoeLayerDev& L) {
+    return static_cast<uint64_t>(L.top_k + (L.shared_inter ? 1u : 0u)) * umax(L.inter, L.shared_inter);
+}
+
 uint64_t moe_chain_scratch_bytes(const MoeLayerDev& L) {
-    return align256(3ull * L.experts * kRaccLimbs * 8u) + align256(2ull * (L.hidden / kPartRows) * 4u) +
+    return align256(3ull * chain_router_rows(L) * kRaccLimbs * 8u) + align256(2ull * (L.hidden / kPartRows) * 4u) +
            align256(3u * 4u) + align256(static_cast<uint64_t>(kChainXReplicas) * L.hidden * 4u) +
-           align256(static_cast<uint64_t>(kChainXReplicas) * L.top_k * L.inter * 8u) + 4u * kChainCounterStride * 4u;
+           align256(static_cast<uint64_t>(kChainXReplicas) * chain_act_words(L) * 8u) + 4u * kChainCounterStride * 4u;
 }
 
 ChainScratch moe_chain_scratch_carve(const MoeLayerDev& L, void* base) {
     uint8_t* p = static_cast<uint8_t*>(base);
     ChainScratch c;
-    c.racc = reinterpret_cast<unsigned long long*>(p); p += align256(3ull * L.experts * kRaccLimbs * 8u);
+    c.racc = reinterpret_cast<unsigned long long*>(p); p += align256(3ull * chain_router_rows(L) * kRaccLimbs * 8u);
     c.rsq = reinterpret_cast<float*>(p); p += align256(2ull * (L.hidden / kPartRows) * 4u);
     c.rbad = reinterpret_cast<uint32_t*>(p); p += align256(3u * 4u);
     c.xrep = reinterpret_cast<float*>(p); p += align256(static_cast<uint64_t>(kChainXReplicas) * L.hidden * 4u);
     c.act = reinterpret_cast<unsigned long long*>(p);
-    p += align256(static_cast<uint64_t>(kChainXReplicas) * L.top_k * L.inter * 8u);
+    p += align256(static_cast<uint64_t>(kChainXReplicas) * chain_act_words(L) * 8u);
     c.counters = reinterpret_cast<uint32_t*>(p);
     return c;
 }
@@ -2762,6 +3417,125 @@ bool moe_chain_plan(const MoeLayerDev* layers, uint32_t n, ChainPlan* plan) {
     plan->grid = sms;
     plan->smem = c.total;
     return true;
+}
+
+// (8-byte column, row) view of a shared expert's Q8_0 gate or up: boxes of
+// kChain35SharedRows rows by half a row.
+static bool encode_shared_half_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows) {
+    const auto encode = tensor_map_encoder();
+    if (!encode || (reinterpret_cast<uintptr_t>(base) & 15u) || (row_bytes % 16u) || ((row_bytes / 2u) % 16u) ||
+        row_bytes / 16u > 256u || rows < kChain35SharedRows)
+        return false;
+    const cuuint64_t dims[2] = {row_bytes / 8u, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(row_bytes / 16u), kChain35SharedRows};
+    const cuuint32_t elem[2] = {1u, 1u};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// (8-byte column, row, expert) view of a layer's routed Q4_K gate or up:
+// boxes of two superblocks (288 bytes) by 16 rows.
+static bool encode_pair_map(CUtensorMap* map, const uint8_t* base, uint64_t row_bytes, uint64_t rows,
+                            uint64_t experts, uint64_t slice) {
+    const auto encode = tensor_map_encoder();
+    if (!encode || (reinterpret_cast<uintptr_t>(base) & 15u) || (row_bytes & 15u) || (slice & 15u)) return false;
+    const cuuint64_t dims[3] = {row_bytes / 8u, rows, experts};
+    const cuuint64_t strides[2] = {row_bytes, slice};
+    const cuuint32_t box[3] = {kPairRowBytes / 8u, kBoxRows, 1u};
+    const cuuint32_t elem[3] = {1u, 1u, 1u};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<uint8_t*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool moe_chain35_plan(const MoeLayerDev* layers, uint32_t n, Chain35Plan* plan, std::vector<Chain35Maps>* maps) {
+    if (!layers || n == 0 || !plan || !maps) return false;
+    const MoeLayerDev& L0 = layers[0];
+    const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const auto down_ok = [](uint32_t t) { return t == kQ4_K || t == kQ5_K || t == kQ6_K; };
+    if (!layer_valid(L0) || L0.flavour != 1u || L0.shared_inter == 0 || L0.shared_inter != L0.inter ||
+        (L0.expert_local != 0 && L0.expert_local != L0.experts) || L0.experts > 512u ||
+        L0.top_k + 1u > static_cast<uint32_t>(kWarps) || L0.top_k > static_cast<uint32_t>(kMaxTopK) ||
+        L0.hidden % 512u || (L0.hidden >> 8) > 64u || L0.inter % 256u)
+        return false;
+    uint32_t rb_max = 0;
+    for (uint32_t l = 0; l < n; ++l) {
+        const MoeLayerDev& L = layers[l];
+        if (L.hidden != L0.hidden || L.inter != L0.inter || L.experts != L0.experts || L.top_k != L0.top_k ||
+            L.flavour != L0.flavour || L.normalize != L0.normalize ||
+            L.expert_weights_scale != L0.expert_weights_scale || L.rms_eps != L0.rms_eps ||
+            L.shared_inter != L0.shared_inter || L.gate_type != kQ4_K || L.up_type != kQ4_K ||
+            !down_ok(L.down_type) || L.shared_gate_type != kQ8_0 || L.shared_up_type != kQ8_0 ||
+            L.shared_down_type != kQ8_0 || !L.router || !L.ffn_norm || !L.shared_router || !L.gate || !L.up ||
+            !L.down || !L.shared_gate || !L.shared_up || !L.shared_down || !a16(L.gate) || !a16(L.up) ||
+            !a16(L.down) || !a16(L.shared_down) || !a16(L.router) || !a16(L.shared_router) || !a16(L.shared_gate) ||
+            !a16(L.shared_up) || L.gate_slice % 16u || L.up_slice % 16u || L.down_slice % 16u)
+            return false;
+        rb_max = umax(rb_max, static_cast<uint32_t>(row_bytes(L.down_type, L.inter)));
+    }
+    const uint32_t sms = static_cast<uint32_t>(device_sm_count());
+    const uint32_t units = L0.hidden / kPartRows;
+    const uint32_t groups = L0.top_k * (L0.inter / 16u) + L0.shared_inter / kChain35SharedRows;
+    const Chain35Layout c = chain35_layout(L0, rb_max);
+    // A shared-expert group's half rows fill at most one warp's tile space.
+    const uint64_t shared_tile = kChain35SharedRows * (row_bytes(kQ8_0, L0.hidden) / 2u);
+    if (units > sms || groups > kChainGroupsPerCta * sms || groups < sms || c.total > 227u * 1024u ||
+        shared_tile > static_cast<uint64_t>(c.gpairs) * kPairBytes || (row_bytes(kQ8_0, L0.hidden) / 2u) % 16u)
+        return false;
+    if (ensure_smem(moe_chain35_kernel, c.total) != cudaSuccess) return false;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_chain35_kernel, kThreads, c.total) != cudaSuccess ||
+        per_sm < 1)
+        return false;
+    std::vector<Chain35Maps> m(n);
+    const uint64_t rb_in = row_bytes(kQ4_K, L0.hidden), rb_shared = row_bytes(kQ8_0, L0.hidden);
+    for (uint32_t l = 0; l < n; ++l) {
+        const MoeLayerDev& L = layers[l];
+        if (!encode_pair_map(&m[l].gate, L.gate, rb_in, L.inter, L.experts, L.gate_slice) ||
+            !encode_pair_map(&m[l].up, L.up, rb_in, L.inter, L.experts, L.up_slice) ||
+            !encode_shared_half_map(&m[l].shared_gate, L.shared_gate, rb_shared, L.shared_inter) ||
+            !encode_shared_half_map(&m[l].shared_up, L.shared_up, rb_shared, L.shared_inter))
+            return false;
+    }
+    plan->shape = L0;
+    plan->layers = n;
+    plan->grid = sms;
+    plan->smem = c.total;
+    plan->rb_down_max = rb_max;
+    *maps = std::move(m);
+    return true;
+}
+
+cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layers_dev, const Chain35Maps* maps_dev,
+                               uint32_t first, uint32_t count, const MoeScratch& S, const ChainScratch& C,
+                               float* hidden, cudaStream_t stream, unsigned long long* trace) {
+    if (!hidden || !layers_dev || !maps_dev || count == 0 || first >= plan.layers || count > plan.layers - first ||
+        plan.grid == 0)
+        return cudaErrorInvalidValue;
+    Chain35Args a{};
+    a.layers = layers_dev;
+    a.shape = plan.shape;
+    a.first = first;
+    a.count = count;
+    a.S = S;
+    a.C = C;
+    a.hidden = hidden;
+    a.c = chain35_layout(plan.shape, plan.rb_down_max);
+    a.maps = maps_dev;
+    a.trace = trace;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, moe_chain35_kernel, a);
 }
 
 uint32_t chain_tile_offset(const ChainPlan& plan) { return chain_layout(plan.shape).gtiles; }

@@ -149,6 +149,39 @@ def test_config3_shape_layer(cuda):
     be.close()
 
 
+@pytest.mark.parametrize("experts,top_k,downs", [
+    (512, 10, ("Q5_K", "Q6_K", "Q5_K", "Q6_K")),      # configuration 3
+    (128, 8, ("Q4_K", "Q6_K", "Q5_K", "Q4_K")),
+])
+def test_config3_decode_chain(cuda, experts, top_k, downs):
+    """Qwen3.5-MoE blocks in their decode chain (moe_chain35_kernel): Q4_K
+    gate/up, the down type per layer, the Q8_0 shared expert and its sigmoid
+    gate, ffn_norm per layer (configuration 3: 512 experts top-10, inter 512,
+    Q5_K / Q6_K down alternating)."""
+    downs = [getattr(cases, d) for d in downs]
+    layers = [cases.moe_layer(hidden=2048, inter=512, experts=experts, top_k=top_k, seed=6, layer=l, flavour=1,
+                              down_type=downs[l], shared_inter=512, with_norm=True) for l in range(4)]
+    be = make_backend(layers[0], layers=4, rms_epsilon=1e-6, layer_down_types=downs)
+    for l, L in enumerate(layers):
+        upload(be, l, L)
+    h0 = synth.activation(2048, 6, 0)
+    k0 = be.stats()["kernel_launches"]
+    out = be.decode_layers_host(0, 4, h0)
+    assert be.stats()["kernel_launches"] - k0 == 1          # one chain launch for the four blocks
+    ref = O.decode_layers(layers, h0, 1e-6)
+    assert_moe_close(out - h0, ref.astype(np.float64) - h0)
+    again = be.decode_layers_host(0, 4, h0)
+    assert np.array_equal(out, again)
+    mid = be.decode_layers_host(1, 3, h0)                   # odd first layer
+    assert_moe_close(mid - h0, O.decode_layers(layers[1:], h0, 1e-6).astype(np.float64) - h0)
+    h = torch.from_numpy(h0).cuda()
+    be.decode_layers(0, 2, h)
+    be.decode_layers(2, 2, h)
+    torch.cuda.synchronize()
+    assert np.array_equal(h.cpu().numpy(), out)
+    be.close()
+
+
 def test_decode_chain_matches_golden(cuda):
     layers = [cases.moe_layer(hidden=2048, inter=768, experts=32, top_k=8, seed=3, layer=l,
                               with_norm=True) for l in range(4)]
