@@ -584,31 +584,13 @@ __device__ void route_select_regs(const MoeLayerDev& L, const float (&lgv)[kSlot
         uint32_t my_id = 0;
         float my_v = 0.0f, mx = 0.0f;
         for (uint32_t r = 0; r < k; ++r) {
-            // The lane's maximum by a tree of pairwise maxima (ties to the
-            // lower slot, which holds the lower id).
-            uint32_t to[kSlots], ti[kSlots];
+            uint32_t best_ord = 0, best_e = 0xffffffffu;
 #pragma unroll
-            for (uint32_t i = 0; i < kSlots; ++i) {
-                to[i] = ord[i];
-                ti[i] = i;
-            }
-#pragma unroll
-            for (uint32_t w = kSlots / 2; w > 0; w >>= 1)
-#pragma unroll
-                for (uint32_t i = 0; i < w; ++i) {
-                    const bool hi = to[2 * i + 1] > to[2 * i];
-                    to[i] = hi ? to[2 * i + 1] : to[2 * i];
-                    ti[i] = hi ? ti[2 * i + 1] : ti[2 * i];
-                }
-            const uint32_t best_ord = to[0];
-            const uint32_t best_e = best_ord ? lane + 32u * ti[0] : 0xffffffffu;
+            for (uint32_t i = 0; i < kSlots; ++i)
+                if (ord[i] > best_ord) { best_ord = ord[i]; best_e = lane + 32u * i; }
             const uint32_t top = __reduce_max_sync(0xffffffffu, best_ord);
-            // The lowest id among the lanes at the maximum: with one such lane
-            // (the usual case) its id, else the minimum over them.
-            const uint32_t at = __ballot_sync(0xffffffffu, best_ord == top);
-            const uint32_t win = (at & (at - 1u)) == 0u
-                                     ? __shfl_sync(0xffffffffu, best_e, __ffs(at) - 1)
-                                     : __reduce_min_sync(0xffffffffu, best_ord == top ? best_e : 0xffffffffu);
+            // The lowest id among the lanes at the maximum.
+            const uint32_t win = __reduce_min_sync(0xffffffffu, best_ord == top ? best_e : 0xffffffffu);
 #pragma unroll
             for (uint32_t i = 0; i < kSlots; ++i)
                 if (lane + 32u * i == win) ord[i] = 0u;
