@@ -907,13 +907,12 @@ private:
                 float* gate = qkv_ + conv_ch_;
                 float* alpha = gate + vw_;
                 float* beta = alpha + hv_;
-                char derr[256];
-                const pokit_cuda_status ds = pokit_cuda_delta_net_step(
-                    &dsh, qkv_, gate, alpha, beta, F(POKIT_CUDA_DEC_SSM_CONV1D), reinterpret_cast<float*>(st),
-                    F(POKIT_CUDA_DEC_SSM_A), F(POKIT_CUDA_DEC_SSM_DT_BIAS), F(POKIT_CUDA_DEC_SSM_NORM),
-                    reinterpret_cast<float*>(st + ssm_conv_bytes_), att_, status_ + 1, s, derr, sizeof derr);
-                if (ds != POKIT_CUDA_STATUS_OK) return ds == POKIT_CUDA_STATUS_INVALID_ARGUMENT ? cudaErrorInvalidValue
-                                                                                                : cudaErrorUnknown;
+                if (!delta_net_shape_valid(dsh)) return cudaErrorInvalidValue;
+                e = launch_delta_net_step(dsh, qkv_, gate, alpha, beta, F(POKIT_CUDA_DEC_SSM_CONV1D),
+                                          reinterpret_cast<float*>(st), F(POKIT_CUDA_DEC_SSM_A),
+                                          F(POKIT_CUDA_DEC_SSM_DT_BIAS), F(POKIT_CUDA_DEC_SSM_NORM),
+                                          reinterpret_cast<float*>(st + ssm_conv_bytes_), att_, status_ + 1, s, pdl_);
+                if (e != cudaSuccess) break;
                 e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_SSM_OUT), H, static_cast<uint32_t>(vw_), att_,
                                   hidden_, s, false, true, false);
                 n += 4;

@@ -9,6 +9,8 @@
 #include <string>
 #include <vector>
 
+struct pokit_cuda_delta_net_shape;   // include/pokit_cuda.h
+
 namespace pokit {
 
 int device_sm_count();
@@ -268,6 +270,16 @@ struct ChainAttnDesc {
 // The decode chain for Qwen3.5-MoE blocks (Q4_K gate/up, any K-quant or Q8_0
 // down per layer, the Q8_0 shared expert with its sigmoid gate), per-layer
 // pointers read from the device table.
+// The Gated DeltaNet mixer step (conv1d, gates, delta rule, gated norm) of
+// pokit_cuda_delta_net_step, its two kernels launched as programmatic
+// dependents when `pdl` (each waits for its predecessor before reading its
+// outputs, and loads only its own states before that).
+bool delta_net_shape_valid(const pokit_cuda_delta_net_shape& s);
+cudaError_t launch_delta_net_step(const pokit_cuda_delta_net_shape& s, float* projected, const float* gate,
+                                  const float* alpha, const float* beta, const float* conv_weights, float* conv_state,
+                                  const float* ssm_a, const float* dt_bias, const float* ssm_norm,
+                                  float* recurrent_state, float* output, uint32_t* status, cudaStream_t st, bool pdl);
+
 struct Chain35Plan {
     MoeLayerDev shape;
     uint32_t layers = 0, grid = 0, smem = 0, rb_down_max = 0;

@@ -21,8 +21,10 @@ def _rms(a):
 
 
 @pytest.mark.parametrize("shape", [cases.DELTA_NET_CFG3, dict(key_heads=2, value_heads=6, key_dim=64, value_dim=96,
-                                                             conv_kernel=4, rms_epsilon=1e-6)],
-                         ids=["config3", "odd"])
+                                                             conv_kernel=4, rms_epsilon=1e-6),
+                                   dict(key_heads=1, value_heads=2, key_dim=256, value_dim=160, conv_kernel=4,
+                                        rms_epsilon=1e-6)],
+                         ids=["config3", "odd", "wide"])   # wide: heads beyond 128 (the streamed-row kernel)
 def test_delta_net_steps_match_the_oracle(cuda, shape):
     t, steps = cases.delta_net_inputs(shape, seed=7, steps=6)
     C, K = t["conv_w"].shape
