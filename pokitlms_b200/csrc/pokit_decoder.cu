@@ -663,6 +663,32 @@ private:
         check(cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(attend_smem_bytes())), "attend smem");
         plan_attn_block();
+        plan_delta_block();
+    }
+
+    // DeltaNet layers run as one cooperative launch each (pokit_deltablock.cu)
+    // when the projections are Q4_K and the heads 128 wide
+    // (POKIT_CUDA_FUSED_DELTANET=0 keeps the four-kernel path).
+    void plan_delta_block() {
+        const char* env = std::getenv("POKIT_CUDA_FUSED_DELTANET");
+        if (!hybrid_ || (env && env[0] == '0') || cfg_.attn_type != kQ4_K || hv_ == 0) return;
+        DeltaBlockShape d{};
+        d.hidden = static_cast<uint32_t>(cfg_.hidden);
+        d.rows_in = static_cast<uint32_t>(conv_ch_ + vw_ + 2 * hv_);
+        d.key_heads = static_cast<uint32_t>(cfg_.ssm_group_count);
+        d.value_heads = static_cast<uint32_t>(hv_);
+        d.key_dim = static_cast<uint32_t>(cfg_.ssm_state_size);
+        d.value_dim = static_cast<uint32_t>(vw_ / hv_);
+        d.conv_kernel = static_cast<uint32_t>(cfg_.ssm_conv_kernel);
+        d.norm_eps = cfg_.rms_epsilon;
+        d.eps = cfg_.rms_epsilon;
+        if (2 * cfg_.ssm_group_count * cfg_.ssm_state_size + vw_ != conv_ch_ || vw_ % hv_) return;
+        uint32_t grid = 0, smem = 0;
+        if (!delta_block_plan(d, &grid, &smem)) return;
+        check(cudaMalloc(&delta_scratch_, sizeof(float) * 4 * hv_), "cudaMalloc(DeltaNet scratch)");
+        delta_shape_ = d;
+        delta_grid_ = grid;
+        delta_smem_ = smem;
     }
 
     size_t attend_smem_bytes() const {
@@ -808,6 +834,7 @@ private:
         if (stream_) cudaStreamDestroy(stream_);
         if (pinned_ids_) cudaFreeHost(pinned_ids_);
         if (seq_) cudaFree(seq_);
+        if (delta_scratch_) cudaFree(delta_scratch_);
         if (work_) cudaFree(work_);
         if (rope_) cudaFree(rope_);
         if (vcache_) cudaFree(vcache_);
@@ -896,6 +923,28 @@ private:
                 e = launch_linear(cfg_.attn_type, P(POKIT_CUDA_DEC_ATTN_OUTPUT), H, static_cast<uint32_t>(qd_), att_,
                                   hidden_, s, false, true, pdl_);
                 n += 3;
+            } else if (delta_grid_) {
+                // Gated DeltaNet (qwen35_runner.cpp:582-656) in one launch.
+                uint8_t* st = ssm_ + ssm_off_[l];
+                DeltaBlockTensors t{};
+                t.w_in = P(POKIT_CUDA_DEC_SSM_QKV);
+                t.w_out = P(POKIT_CUDA_DEC_SSM_OUT);
+                t.attn_norm = F(POKIT_CUDA_DEC_ATTN_NORM);
+                t.conv_w = F(POKIT_CUDA_DEC_SSM_CONV1D);
+                t.conv_state = reinterpret_cast<float*>(st);
+                t.ssm_a = F(POKIT_CUDA_DEC_SSM_A);
+                t.dt_bias = F(POKIT_CUDA_DEC_SSM_DT_BIAS);
+                t.ssm_norm = F(POKIT_CUDA_DEC_SSM_NORM);
+                t.state = reinterpret_cast<float*>(st + ssm_conv_bytes_);
+                t.hidden = hidden_;
+                t.proj = qkv_;
+                t.att = att_;
+                t.ms_part = delta_scratch_;
+                t.counters = status_ + 16;
+                t.timeout = status_ + 2;
+                t.gates_bad = status_ + 1;
+                e = launch_delta_block(delta_shape_, t, delta_grid_, delta_smem_, s);
+                n += 1;
             } else {
                 // Gated DeltaNet (qwen35_runner.cpp:582-627): one matvec over
                 // [qkv | gate | alpha | beta], the conv1d + delta-rule step, ssm_out.
@@ -1020,10 +1069,11 @@ private:
         guard(cudaStreamSynchronize(stream_), "status");
         const uint32_t st = pinned_ids_[kPinnedIds - 3], gates = pinned_ids_[kPinnedIds - 2];
         if (pinned_ids_[kPinnedIds - 1]) {
-            // A bounded wait of the attention block gave up: its counters no
-            // longer match (sticky, like a CUDA error).
+            // A bounded wait of the attention or DeltaNet block gave up: its
+            // counters no longer match (sticky, like a CUDA error).
             failed_ = true;
-            failure_ = "the attention block abandoned its work after a bounded device-side wait timed out";
+            failure_ = "a fused attention or DeltaNet block abandoned its work after a bounded device-side wait "
+                       "timed out";
             throw std::runtime_error(failure_);
         }
         char err[256];
@@ -1075,6 +1125,9 @@ private:
         const char* v = std::getenv("POKIT_CUDA_PDL");
         return !(v && v[0] == '0');
     }();
+    DeltaBlockShape delta_shape_{};           // the one-launch DeltaNet layer (delta_grid_ > 0)
+    uint32_t delta_grid_ = 0, delta_smem_ = 0;
+    float* delta_scratch_ = nullptr;
     unsigned long long* attn_ll_ = nullptr;   // fused attention: Q/K/V words, output words, hidden words
     uint64_t attn_words_ = 0;
     bool fused_layers_ = false;               // the layer loop as one chain launch

@@ -280,6 +280,35 @@ cudaError_t launch_delta_net_step(const pokit_cuda_delta_net_shape& s, float* pr
                                   const float* ssm_a, const float* dt_bias, const float* ssm_norm,
                                   float* recurrent_state, float* output, uint32_t* status, cudaStream_t st, bool pdl);
 
+// A Gated DeltaNet layer's mixer, from the attention norm to ssm_out's
+// residual add, in one cooperative launch (pokit_deltablock.cu): Q4_K
+// in-projection [q|k|v|z|alpha|beta] and ssm_out, 128-wide key and value heads.
+struct DeltaBlockShape {
+    uint32_t hidden = 0, rows_in = 0, key_heads = 0, value_heads = 0, key_dim = 0, value_dim = 0, conv_kernel = 0;
+    float norm_eps = 0.0f, eps = 0.0f;
+};
+struct DeltaBlockTensors {
+    const void* w_in = nullptr;        // Q4_K [rows_in][hidden]
+    const void* w_out = nullptr;       // Q4_K [hidden][value_heads * value_dim]
+    const float* attn_norm = nullptr;
+    const float* conv_w = nullptr;
+    float* conv_state = nullptr;
+    const float* ssm_a = nullptr;
+    const float* dt_bias = nullptr;
+    const float* ssm_norm = nullptr;
+    float* state = nullptr;            // [value_heads][value_dim][key_dim]
+    float* hidden = nullptr;           // the residual, in and out
+    float* proj = nullptr;             // [rows_in] scratch
+    float* att = nullptr;              // [value_heads * value_dim] scratch
+    float* ms_part = nullptr;          // [value_heads * 4] scratch
+    uint32_t* counters = nullptr;      // [2], zero between launches
+    uint32_t* timeout = nullptr;       // set when a bounded device-side wait gave up
+    uint32_t* gates_bad = nullptr;     // bit 0: an invalid decay or beta
+};
+bool delta_block_plan(const DeltaBlockShape& s, uint32_t* grid, uint32_t* smem);
+cudaError_t launch_delta_block(const DeltaBlockShape& s, const DeltaBlockTensors& t, uint32_t grid, uint32_t smem,
+                               cudaStream_t stream);
+
 struct Chain35Plan {
     MoeLayerDev shape;
     uint32_t layers = 0, grid = 0, smem = 0, rb_down_max = 0;
