@@ -1321,6 +1321,29 @@ __device__ __forceinline__ float router_dot16(const RouterSlice& r, const float*
     return p;
 }
 
+// A read-only 16-byte load issued where it stands: the compiler keeps the
+// order of volatile asm, so the load is not sunk to its first use (which
+// would expose its latency in a later phase).
+__device__ __forceinline__ float4 ldg_f4_issue_here(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ldcg_f32_issue_here(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ RouterSlice router_slice_issue_here(const float* router, uint32_t H, uint32_t e,
+                                                               uint32_t c) {
+    const float* p = router + static_cast<uint64_t>(e) * H + c * kPartRows;
+    return RouterSlice{{ldg_f4_issue_here(p), ldg_f4_issue_here(p + 4), ldg_f4_issue_here(p + 8),
+                        ldg_f4_issue_here(p + 12)}};
+}
+
+
 // The routing tail's selection in warp 0 (lane l owns experts l, l + 32, ...):
 // the rms scale from the per-chunk sums of squares (hidden_mode), the exact
 // logits from the accumulators (left zero), then route_select_regs.  The
@@ -1866,10 +1889,10 @@ __device__ __forceinline__ void chain_partials(const float* router, uint32_t E, 
                                                const float* hrow, unsigned long long* racc, uint32_t* rbad, float* rsq,
                                                uint32_t chunk, uint32_t H) {
     const uint32_t tid = threadIdx.x;
-    if (tid < E) racc_add(racc + static_cast<uint64_t>(tid) * kRaccLimbs, rbad, router_dot16(rs, hrow));
+    if (tid < E) racc_add1(racc + static_cast<uint64_t>(tid) * kRaccLimbs, rbad, router_dot16(rs, hrow));
     for (uint32_t e = tid + kThreads; e < E; e += kThreads)
-        racc_add(racc + static_cast<uint64_t>(e) * kRaccLimbs, rbad,
-                 router_dot16(router_slice(router, H, e, chunk), hrow));
+        racc_add1(racc + static_cast<uint64_t>(e) * kRaccLimbs, rbad,
+                  router_dot16(router_slice(router, H, e, chunk), hrow));
     if (tid == 0) {
         float sq = 0.0f;
         for (uint32_t r = 0; r < kPartRows; ++r) sq += hrow[kPartRows + r];
@@ -2128,7 +2151,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
         }
         // The next layer's router slice and ffn_norm, this unit's residual rows.
         RouterSlice rs{};
-        if (has_unit && has_next && static_cast<uint32_t>(tid) < E) rs = router_slice(router_of(nlayer), H, tid, cta);
+        if (has_unit && has_next && static_cast<uint32_t>(tid) < E)
+            rs = router_slice_issue_here(router_of(nlayer), H, tid, cta);
         if (kAtt) rs_att = rs;
         const float resid = (has_unit && tid < 16) ? __ldcg(a.hidden + j0 + tid) : 0.0f;
         const float nnorm = (has_unit && has_next && tid < 16) ? __ldg(norm_of(nlayer) + j0 + tid) : 0.0f;
@@ -2413,28 +2437,6 @@ struct Chain35Args {
     const Chain35Maps* maps;     // per-layer tensor maps (device memory)
     unsigned long long* trace;   // optional per-(layer, CTA) phase stamps (measurement)
 };
-
-// A read-only 16-byte load issued where it stands: the compiler keeps the
-// order of volatile asm, so the load is not sunk to its first use (which
-// would expose its latency in a later phase).
-__device__ __forceinline__ float4 ldg_f4_issue_here(const float* p) {
-    float4 v;
-    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ float ldcg_f32_issue_here(const float* p) {
-    float v;
-    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ RouterSlice router_slice_issue_here(const float* router, uint32_t H, uint32_t e,
-                                                               uint32_t c) {
-    const float* p = router + static_cast<uint64_t>(e) * H + c * kPartRows;
-    return RouterSlice{{ldg_f4_issue_here(p), ldg_f4_issue_here(p + 4), ldg_f4_issue_here(p + 8),
-                        ldg_f4_issue_here(p + 12)}};
-}
 
 // Thread t's router slices of a layer: expert t (rs) and expert t + kThreads,
 // or for the last thread the shared expert's gate row (rs2).  E <= 2 kThreads - 1.
