@@ -411,7 +411,7 @@ def cfg3_layer_bytes(down_type: int) -> int:
 
 
 def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None, layers: int | None = None) -> dict:
-    """Configuration 3's MoE path: a 48-layer decode chain of Qwen3.5-MoE blocks (generic path),
+    """Configuration 3's MoE path: a 48-layer decode chain of Qwen3.5-MoE blocks (moe_chain35_kernel),
     weights synthesised in HBM from seed 0; tokens/s device-resident and end to end.  `layers`
     shortens the chain (a small process for profiling its kernels)."""
     import torch
@@ -471,7 +471,9 @@ def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None, 
                 "peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"]},
         "e2e": {"value": 1.0 / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": c["hidden"] * 4,
                 "d2h_bytes_per_step": c["hidden"] * 4},
-        "path": "generic (FP32 dequant-dot; the tensor-core decode kernels serve all-Q4_K blocks without a shared expert)",
+        "path": ("moe_chain35_kernel: one cooperative launch for the 48 blocks; Q4_K gate/up and Q5_K/Q6_K down on "
+                 "integer mma.sync (u8/s8 x int8 activation pieces), the Q8_0 shared expert as FP32 dots of "
+                 "tensor-map boxes"),
     }
     if cpu_seconds:
         res["cpu_baseline"] = cpu_config3_rate(cpu_seconds)
