@@ -26,7 +26,7 @@ LIB = PKG / "libpokit_cuda.so"
 SOURCES = ["pokit_linear.cu", "pokit_moe.cu", "pokit_grouped.cu", "pokit_synth.cu", "pokit_backend.cpp",
            "pokit_static_scratch.cu", "pokit_decoder.cu", "pokit_deltanet.cu",
            "pokit_deltablock.cu"]
-HEADERS = ["pokit_common.cuh", "pokit_quant.cuh", "pokit_mma.cuh", "pokit_tc.cuh", "pokit_attention.cuh", "pokit_kernels.h",
+HEADERS = ["pokit_common.cuh", "pokit_quant.cuh", "pokit_mma.cuh", "pokit_tc.cuh", "pokit_attention.cuh", "pokit_deltablock.cuh", "pokit_kernels.h",
            "pokit_types.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

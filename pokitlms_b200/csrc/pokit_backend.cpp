@@ -554,6 +554,26 @@ public:
         return grid;
     }
 
+    // A decoder's Gated DeltaNet layer and this MoE block in one chain launch.
+    bool delta_layer_fits(const DeltaBlockShape& d) const {
+        return chain35_ok_ && !failed_ && moe_chain35_delta_fits(chain35_plan_, d);
+    }
+    void decode_layer_delta(size_t layer, float* hidden, const DeltaBlockShape& d, const DeltaBlockTensors& t,
+                            cudaStream_t s) {
+        ensure_ok();
+        if (!chain35_ok_) throw std::invalid_argument("the layers do not run the Qwen3.5-MoE chain kernel");
+        if (layer >= cfg_.layers || !hidden) throw std::invalid_argument("layer and hidden state are required");
+        if (!resident_complete(layer)) throw std::invalid_argument("layer weights were not uploaded");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        guard(launch_moe_chain35(chain35_plan_, devs_dev_, chain35_maps_, static_cast<uint32_t>(layer), 1u, S_, C_,
+                                 hidden, st, nullptr, &d, &t),
+              "decode chain kernel");
+        forward_calls_ += 1;
+        hits_ += cfg_.top_k;
+        kernel_launches_ += 1;
+    }
+
     // A decoder's layer loop: its attention blocks and these MoE blocks in
     // one chain launch (false when the layers do not take the chain kernel or
     // the attention phase does not fit it).
@@ -1038,6 +1058,25 @@ struct pokit_cuda_moe {
 };
 
 namespace pokit {
+
+bool moe_delta_layer_fits(const pokit_cuda_moe* moe, const DeltaBlockShape& d) {
+    return moe && moe->impl.delta_layer_fits(d);
+}
+
+cudaError_t moe_decode_layer_delta(pokit_cuda_moe* moe, size_t layer, float* hidden, const DeltaBlockShape& d,
+                                   const DeltaBlockTensors& t, cudaStream_t stream, std::string* error) {
+    if (!moe) return cudaErrorInvalidValue;
+    try {
+        moe->impl.decode_layer_delta(layer, hidden, d, t, stream);
+        return cudaSuccess;
+    } catch (const std::invalid_argument& e) {
+        if (error) *error = e.what();
+        return cudaErrorInvalidValue;
+    } catch (const std::exception& e) {
+        if (error) *error = e.what();
+        return cudaErrorUnknown;
+    }
+}
 
 bool moe_attention_chain_fits(const pokit_cuda_moe* moe, const ChainAttnDesc& att) {
     return moe && moe->impl.attention_chain_fits(att);

@@ -689,6 +689,11 @@ private:
         delta_shape_ = d;
         delta_grid_ = grid;
         delta_smem_ = smem;
+        // The DeltaNet layer and its MoE block as one launch when the MoE
+        // blocks take the Qwen3.5 chain kernel (POKIT_CUDA_FUSED_DELTA_MOE=0
+        // keeps two launches per layer).
+        const char* both = std::getenv("POKIT_CUDA_FUSED_DELTA_MOE");
+        delta_moe_ = !(both && both[0] == '0') && moe_delta_layer_fits(moe_, d);
     }
 
     size_t attend_smem_bytes() const {
@@ -943,6 +948,16 @@ private:
                 t.counters = status_ + 16;
                 t.timeout = status_ + 2;
                 t.gates_bad = status_ + 1;
+                if (delta_moe_) {
+                    std::string err;
+                    e = moe_decode_layer_delta(moe_, l, hidden_, delta_shape_, t, s, &err);
+                    if (e != cudaSuccess) {
+                        moe_error_ = err;
+                        return e;
+                    }
+                    n += 1;
+                    continue;                          // the MoE block ran in the same launch
+                }
                 e = launch_delta_block(delta_shape_, t, delta_grid_, delta_smem_, s);
                 n += 1;
             } else {
@@ -1127,6 +1142,7 @@ private:
     }();
     DeltaBlockShape delta_shape_{};           // the one-launch DeltaNet layer (delta_grid_ > 0)
     uint32_t delta_grid_ = 0, delta_smem_ = 0;
+    bool delta_moe_ = false;                  // a DeltaNet layer and its MoE block in one launch
     float* delta_scratch_ = nullptr;
     unsigned long long* attn_ll_ = nullptr;   // fused attention: Q/K/V words, output words, hidden words
     uint64_t attn_words_ = 0;

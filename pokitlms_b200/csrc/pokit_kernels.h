@@ -323,9 +323,14 @@ struct Chain35Maps {
 };
 // Plans the chain for `n` layers and encodes each layer's maps into `maps`.
 bool moe_chain35_plan(const MoeLayerDev* layers, uint32_t n, Chain35Plan* plan, std::vector<Chain35Maps>* maps);
+// With `delta` (count 1): the layer's Gated DeltaNet mixer (delta_block's
+// phases) runs first in the same launch, leaving each D unit's residual rows
+// in its own CTA.
 cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layers_dev, const Chain35Maps* maps_dev,
                                uint32_t first, uint32_t count, const MoeScratch& S, const ChainScratch& C,
-                               float* hidden, cudaStream_t stream, unsigned long long* trace = nullptr);
+                               float* hidden, cudaStream_t stream, unsigned long long* trace = nullptr,
+                               const DeltaBlockShape* delta_shape = nullptr, const DeltaBlockTensors* delta = nullptr);
+bool moe_chain35_delta_fits(const Chain35Plan& plan, const DeltaBlockShape& d);
 // Bytes of shared memory the attention phase needs, and where the chain's
 // tile region (which it runs in) starts.
 uint32_t chain_attention_smem(const ChainPlan& plan, const ChainAttnDesc& att);
@@ -338,6 +343,11 @@ struct pokit_cuda_moe;
 namespace pokit {
 // A MoE handle's decode chain with a decoder's attention blocks (pokit_backend.cpp).
 bool moe_attention_chain_fits(const pokit_cuda_moe* moe, const ChainAttnDesc& att);
+// A Qwen3.5 decoder's DeltaNet layer `layer` and the handle's MoE block of
+// that layer in one launch (moe_chain35_kernel with the mixer ahead).
+bool moe_delta_layer_fits(const pokit_cuda_moe* moe, const DeltaBlockShape& d);
+cudaError_t moe_decode_layer_delta(pokit_cuda_moe* moe, size_t layer, float* hidden, const DeltaBlockShape& d,
+                                   const DeltaBlockTensors& t, cudaStream_t stream, std::string* error);
 cudaError_t moe_decode_layers_attention(pokit_cuda_moe* moe, size_t first, size_t count, float* hidden,
                                         const ChainAttnDesc& att, cudaStream_t stream, std::string* error);
 

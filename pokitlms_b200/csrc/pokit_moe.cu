@@ -24,6 +24,7 @@
 // ld.global.cg so a stale L1 line can never be observed.  Weights are read-only
 // for the kernel's lifetime and use the non-coherent path.
 #include "pokit_attention.cuh"
+#include "pokit_deltablock.cuh"
 #include "pokit_kernels.h"
 #include "pokit_mma.cuh"
 #include "pokit_quant.cuh"
@@ -2436,6 +2437,8 @@ struct Chain35Args {
     Chain35Layout c;
     const Chain35Maps* maps;     // per-layer tensor maps (device memory)
     unsigned long long* trace;   // optional per-(layer, CTA) phase stamps (measurement)
+    DeltaBlockArgs delta;        // with_delta: the layer's Gated DeltaNet mixer runs first
+    uint32_t with_delta;
 };
 
 // Thread t's router slices of a layer: expert t (rs) and expert t + kThreads,
@@ -2520,6 +2523,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
             t[kChainStamps + i] = static_cast<unsigned long long>(clock64());
         }
     };
+    // A decoder's DeltaNet layer ahead of its MoE block (one launch, count 1):
+    // its phase 3 leaves this CTA's D-unit rows of the residual, read by the
+    // prologue below after a CTA barrier.  The mixer runs in the tile space.
+    if (a.with_delta) {
+        if (!delta_layer_run(a.delta, smem + c.gtiles)) return;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+    }
     if (tid == 0) abort_sh = 0u;
     const uint32_t gpairs = c.gpairs;
     if (lane == 0) {
@@ -2934,6 +2945,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
         *ctr_route = 0u;
         *ctr_exit = 0u;
         *ctr_seq = seq0 + a.count;
+        if (a.with_delta) {
+            a.delta.counters[0] = 0u;
+            a.delta.counters[1] = 0u;
+        }
         __threadfence();
     }
 }
@@ -3492,12 +3507,27 @@ bool moe_chain35_plan(const MoeLayerDev* layers, uint32_t n, Chain35Plan* plan, 
     return true;
 }
 
+bool moe_chain35_delta_fits(const Chain35Plan& plan, const DeltaBlockShape& d) {
+    const Chain35Layout c = chain35_layout(plan.shape, plan.rb_down_max);
+    return plan.grid != 0 && d.hidden == plan.shape.hidden &&
+           db_layout(d.hidden, d.value_heads * kDbHeadDim).total <= c.total - c.gtiles;
+}
+
 cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layers_dev, const Chain35Maps* maps_dev,
                                uint32_t first, uint32_t count, const MoeScratch& S, const ChainScratch& C,
-                               float* hidden, cudaStream_t stream, unsigned long long* trace) {
+                               float* hidden, cudaStream_t stream, unsigned long long* trace,
+                               const DeltaBlockShape* delta_shape, const DeltaBlockTensors* delta) {
     if (!hidden || !layers_dev || !maps_dev || count == 0 || first >= plan.layers || count > plan.layers - first ||
         plan.grid == 0)
         return cudaErrorInvalidValue;
+    if (delta_shape || delta) {
+        const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+        if (!delta_shape || !delta || count != 1 || !moe_chain35_delta_fits(plan, *delta_shape) ||
+            delta->hidden != hidden || !a16(delta->w_in) || !a16(delta->w_out) || !a16(delta->state) ||
+            !delta->counters || !delta->timeout || !delta->gates_bad || !delta->proj || !delta->att ||
+            !delta->ms_part)
+            return cudaErrorInvalidValue;
+    }
     Chain35Args a{};
     a.layers = layers_dev;
     a.shape = plan.shape;
@@ -3509,6 +3539,10 @@ cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layer
     a.c = chain35_layout(plan.shape, plan.rb_down_max);
     a.maps = maps_dev;
     a.trace = trace;
+    if (delta) {
+        a.delta = make_delta_args(*delta_shape, *delta);
+        a.with_delta = 1u;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.grid);
     cfg.blockDim = dim3(kThreads);

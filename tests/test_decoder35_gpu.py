@@ -23,9 +23,11 @@ GOLDEN = Path(__file__).resolve().parent / "golden" / "decoder_cfg3_L4.npz"
 
 
 # The full-attention layers as the fused attention block (the default) and
-# as three kernels; the DeltaNet layers as one launch each (the default) and
-# as the in-projection, conv1d, delta-step and ssm_out kernels.
+# as three kernels; a DeltaNet layer and its MoE block in one launch (the
+# default), as two launches, and the DeltaNet layer as the in-projection,
+# conv1d, delta-step and ssm_out kernels.
 MODES = {"attention_block": {}, "three_kernels": {"POKIT_CUDA_FUSED_ATTN": "0"},
+         "delta_block": {"POKIT_CUDA_FUSED_DELTA_MOE": "0"},
          "delta_kernels": {"POKIT_CUDA_FUSED_DELTANET": "0"}}
 
 
