@@ -348,6 +348,148 @@ linear_q4k_mma_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t col
     }
 }
 
+// Q6_K y = W x on the integer tensor path (q6k_mma_superblock): a persistent
+// grid.  CTA c builds the x records once (after the fused RMS norm, when
+// given; warp w the superblocks w, w + 8, ...) and then takes the 16-row tiles
+// c, c + grid, ...: a tile's rows are bulk-copied (one copy per row; a row of
+// 2048k columns is a multiple of 16 bytes) into one of two buffers at a row
+// pitch of row bytes + 16, the next tile's copies in flight while the current
+// one is multiplied; warp w multiplies superblocks w, w + 8, ... of the 16
+// rows and the CTA adds the warps' partial rows in warp order.
+constexpr uint32_t kQ6MmaWarps = 8;
+constexpr uint32_t kQ6MmaMaxSb = 32;            // cols <= 8192
+
+__host__ __device__ inline uint32_t q6mma_pitch(uint32_t cols) { return (cols / 256u) * 210u + 16u; }
+__host__ __device__ inline uint32_t q6mma_smem(uint32_t cols) {
+    return 2u * 16u * q6mma_pitch(cols) + (cols / 256u) * kFragWords * 4u;
+}
+
+__global__ void __launch_bounds__(kQ6MmaWarps * 32)
+linear_q6k_mma_kernel(const uint8_t* __restrict__ w, uint32_t rows, uint32_t cols, const float* x, float* y,
+                      int accumulate, const float* __restrict__ norm_w, float norm_eps) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bar[2];
+    __shared__ float red[kQ6MmaWarps];
+    __shared__ float part[kQ6MmaWarps][16];
+    const uint32_t nsb = cols / 256u, rb = nsb * 210u, pitch = q6mma_pitch(cols);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2;
+    const uint32_t ntiles = (rows + 15u) / 16u, G = gridDim.x;
+    uint8_t* const buf0 = smem;
+    uint8_t* const buf1 = smem + 16u * pitch;
+    uint32_t* recs = reinterpret_cast<uint32_t*>(smem + 32u * pitch);
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    const auto issue = [&](uint32_t t, uint32_t b) {
+        const uint32_t row0 = t * 16u, nr = min(16u, rows - row0);
+        if (warp == 0) {
+            if (lane == 0) mbar_expect_tx(&bar[b], nr * rb);
+            __syncwarp();
+            if (static_cast<uint32_t>(lane) < nr)
+                bulk_copy_g2s((b ? buf1 : buf0) + lane * pitch, w + static_cast<uint64_t>(row0 + lane) * rb, rb,
+                              &bar[b]);
+        }
+    };
+    // The weights do not depend on the previous kernel: the first tile is
+    // requested before waiting for it (programmatic dependent launch).
+    if (blockIdx.x < ntiles) issue(blockIdx.x, 0);
+    grid_dep_launch();
+    grid_dep_wait();
+    float scale = 1.0f;
+    if (norm_w) {
+        // x = rms_norm(x, norm_w) first (src/rms_norm.cpp:9-27).
+        float ss = 0.0f;
+        for (uint32_t i = tid; i < cols; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float total = 0.0f;
+        for (uint32_t i = 0; i < kQ6MmaWarps; ++i) total += red[i];
+        scale = 1.0f / sqrtf(total / static_cast<float>(cols) + norm_eps);
+    }
+    for (uint32_t q = warp; q < nsb; q += kQ6MmaWarps) {
+        float* stage = reinterpret_cast<float*>(recs + q * kFragWords);
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t c = q * 256u + 32u * j + lane;
+            v[j] = norm_w ? __fmul_rn(__fmul_rn(x[c], scale), norm_w[c]) : x[c];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) stage[32 * j + lane] = v[j];
+        __syncwarp();
+        q4k_frag_superblock(stage, recs + q * kFragWords, lane);
+        __syncwarp();
+    }
+    __syncthreads();
+    uint32_t it = 0;
+    for (uint32_t t = blockIdx.x; t < ntiles; t += G, ++it) {
+        const uint32_t b = it & 1u, ph = (it >> 1) & 1u;
+        if (t + G < ntiles) issue(t + G, b ^ 1u);
+        float acc0 = 0.0f, acc1 = 0.0f;
+        // The copies land well within the bound; if not, wait once more:
+        // shared memory a copy may still write is never given up.
+        if (!mbar_wait(&bar[b], ph)) {
+            mbar_wait(&bar[b], ph);
+            acc0 = acc1 = __int_as_float(0x7fc00000);
+        }
+        const uint8_t* tile = b ? buf1 : buf0;
+        for (uint32_t q = warp; q < nsb; q += kQ6MmaWarps)
+            q6k_mma_superblock(tile + g * pitch + q * 210u, tile + (g + 8) * pitch + q * 210u, recs + q * kFragWords,
+                               acc0, acc1);
+        acc0 = quad_sum(acc0);
+        acc1 = quad_sum(acc1);
+        if ((lane & 3) == 0) {
+            part[warp][g] = acc0;
+            part[warp][g + 8] = acc1;
+        }
+        __syncthreads();
+        const uint32_t row0 = t * 16u, nr = min(16u, rows - row0);
+        if (static_cast<uint32_t>(tid) < nr) {
+            float v = part[0][tid];
+            for (uint32_t i = 1; i < kQ6MmaWarps; ++i) v += part[i][tid];
+            const uint32_t r = row0 + tid;
+            y[r] = accumulate ? y[r] + v : v;
+        }
+        // This buffer's generic reads come before its next bulk copies.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+    }
+}
+
+bool q6k_mma_linear_fits(const void* w, uint32_t cols) {
+    return (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && cols % 2048u == 0 && cols / 256u <= kQ6MmaMaxSb &&
+           q6mma_smem(cols) <= 200u * 1024u;
+}
+
+cudaError_t launch_q6k_mma(const void* w, uint32_t rows, uint32_t cols, const float* x, float* y,
+                           cudaStream_t stream, bool accumulate, const float* norm_w, float norm_eps, bool pdl) {
+    const size_t smem = q6mma_smem(cols);
+    cudaError_t e = set_smem(linear_q6k_mma_kernel, smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, linear_q6k_mma_kernel, kQ6MmaWarps * 32, smem);
+    if (e != cudaSuccess) return e;
+    const uint32_t ntiles = (rows + 15u) / 16u;
+    uint32_t grid = static_cast<uint32_t>(sm_count_cached()) * static_cast<uint32_t>(per_sm < 1 ? 1 : per_sm);
+    if (grid > ntiles) grid = ntiles;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kQ6MmaWarps * 32u);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_q6k_mma_kernel, static_cast<const uint8_t*>(w), rows, cols, x, y,
+                              accumulate ? 1 : 0, norm_w, norm_eps);
+}
+
 bool mma_linear_fits(const void* w, uint32_t cols) {
     return (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && cols % 256u == 0 &&
            (cols / 256u + kMmaLinWarps - 1) / kMmaLinWarps <= kMmaLinMaxPer;
@@ -379,6 +521,9 @@ cudaError_t launch_quant(const void* w, uint32_t rows, uint32_t cols, const floa
     if constexpr (T == kQ4_K)
         if (!force_generic && mma_linear_fits(w, cols))
             return launch_q4k_mma(w, rows, cols, x, y, stream, accumulate, nullptr, 0.0f, pdl);
+    if constexpr (T == kQ6_K)
+        if (!force_generic && q6k_mma_linear_fits(w, cols))
+            return launch_q6k_mma(w, rows, cols, x, y, stream, accumulate, nullptr, 0.0f, pdl);
     if (!force_generic && rows_kernel_fits<T>(w, cols))
         return launch_rows<T>(w, rows, cols, x, y, stream, accumulate, nullptr, 0.0f, pdl);
     return launch_generic<T>(w, rows, cols, x, y, stream, accumulate);
@@ -439,6 +584,7 @@ cudaError_t launch_linear_normed(uint32_t type, const void* w, uint32_t rows, ui
             if (!rows_kernel_fits<kQ5_K>(w, cols)) return cudaErrorInvalidValue;
             return launch_rows<kQ5_K>(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
         case kQ6_K:
+            if (q6k_mma_linear_fits(w, cols)) return launch_q6k_mma(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
             if (!rows_kernel_fits<kQ6_K>(w, cols)) return cudaErrorInvalidValue;
             return launch_rows<kQ6_K>(w, rows, cols, x, y, stream, false, norm_w, eps, pdl);
         case kQ8_0:

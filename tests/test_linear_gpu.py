@@ -43,7 +43,8 @@ def assert_close_rms(got, ref, rel=1e-4):
 SHAPES = [(cases.Q4_K, 768, 2048), (cases.Q4_K, 2048, 768), (cases.Q4_K, 1536, 4096),
           (cases.Q4_K, 4096, 1536), (cases.Q4_K, 1, 256), (cases.Q4_K, 13, 512),
           (cases.Q5_K, 2048, 512), (cases.Q5_K, 37, 768), (cases.Q6_K, 2048, 512),
-          (cases.Q6_K, 37, 768), (cases.Q6_K, 5, 2048), (cases.Q8_0, 512, 2048),
+          (cases.Q6_K, 37, 768), (cases.Q6_K, 5, 2048), (cases.Q6_K, 16003, 2048),
+          (cases.Q6_K, 300, 4096), (cases.Q8_0, 512, 2048),
           (cases.Q8_0, 2048, 512), (cases.Q8_0, 3, 32), (cases.F32, 128, 2048),
           (cases.F32, 1, 2048), (cases.F32, 37, 257)]
 
@@ -70,6 +71,18 @@ def test_q4k_fast_and_generic_paths_agree(cuda, rows, cols):
     generic = run_linear(cases.Q4_K, w, rows, cols, x, offset=2)
     assert_close_rms(fast, ref)
     assert_close_rms(generic, ref)
+
+
+@pytest.mark.parametrize("rows,cols", [(777, 2048), (3001, 4096)])
+def test_q6k_tensor_and_row_paths_agree(cuda, rows, cols):
+    """A 16-byte-aligned Q6_K matrix of 2048k columns takes the integer
+    tensor-core kernel (persistent, several 16-row tiles per CTA); the same
+    bytes at a 2-byte offset take the FP32 path."""
+    w = synth.synth_matrix(cases.Q6_K, rows, cols, 9, 2)
+    x = synth.activation(cols, 9)
+    ref = O.linear(cases.Q6_K, x, w, rows)
+    assert_close_rms(run_linear(cases.Q6_K, w, rows, cols, x), ref)
+    assert_close_rms(run_linear(cases.Q6_K, w, rows, cols, x, offset=2), ref)
 
 
 def test_reference_parity_cases(cuda):
