@@ -251,6 +251,100 @@ __device__ __forceinline__ void q4k_frag_superblock(const float* v, uint32_t* re
     }
 }
 
+// q4k_frag_superblock for N superblocks at once, their steps interleaved
+// (the shuffles of one record overlap the other's): each record is built
+// exactly as q4k_frag_superblock builds it.
+template <int N>
+__device__ __forceinline__ void q4k_frag_superblocks(const float* const (&vp)[N], uint32_t* const (&recp)[N], int lane) {
+    float x[N][8], m[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        m[n] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            x[n][j] = vp[n][32 * j + lane];
+            m[n] = fmaxf(m[n], fabsf(x[n][j]));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int n = 0; n < N; ++n) m[n] = fmaxf(m[n], __shfl_xor_sync(0xffffffffu, m[n], o));
+    int e0[N], e[N];
+    int8_t q[N][8][4];
+    float xh[N][8];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        const uint32_t mb = __float_as_uint(m[n] * (1.0f / 127.0f));
+        e0[n] = max(static_cast<int>(mb >> 23) - 126, -100);
+        const float upN = pow2f(21 - e0[n]), unitN = pow2f(e0[n] - 21);
+        e[n] = m[n] > 1024.0f ? static_cast<int>(__float_as_uint(m[n]) >> 23) - 127 - 9 : 0;
+        const float inv = pow2f(-e[n]) * unitN;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            int v = __float2int_rn(x[n][j] * upN);
+            xh[n][j] = static_cast<float>(v) * inv;
+            const int d3 = ((v + 64) & 127) - 64;
+            v = (v - d3) >> 7;
+            const int d2 = ((v + 64) & 127) - 64;
+            v = (v - d2) >> 7;
+            const int d1 = ((v + 64) & 127) - 64;
+            v = (v - d1) >> 7;
+            q[n][j][0] = static_cast<int8_t>(max(-127, min(127, v)));
+            q[n][j][1] = static_cast<int8_t>(d1);
+            q[n][j][2] = static_cast<int8_t>(d2);
+            q[n][j][3] = static_cast<int8_t>(d3);
+        }
+    }
+    const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+    float y[N][4], z[N][2], w[N], gA[N], gB[N];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            const float keep = b4 ? xh[n][4 + i] : xh[n][i], send = b4 ? xh[n][i] : xh[n][4 + i];
+            y[n][i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            const float keep = b3 ? y[n][2 + i] : y[n][i], send = b3 ? y[n][i] : y[n][2 + i];
+            z[n][i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+#pragma unroll
+    for (int n = 0; n < N; ++n) w[n] = (b2 ? z[n][1] : z[n][0]) + __shfl_xor_sync(0xffffffffu, b2 ? z[n][0] : z[n][1], 4);
+#pragma unroll
+    for (int n = 0; n < N; ++n) w[n] += __shfl_xor_sync(0xffffffffu, w[n], 2);
+#pragma unroll
+    for (int n = 0; n < N; ++n) w[n] += __shfl_xor_sync(0xffffffffu, w[n], 1);
+    const int tq = (lane >> 1) & 3;
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        gA[n] = __shfl_sync(0xffffffffu, w[n], (2 * tq) << 2);
+        gB[n] = __shfl_sync(0xffffffffu, w[n], (2 * tq + 1) << 2);
+    }
+    __syncwarp();                                   // all reads of the inputs are done
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+        int8_t* bytes = reinterpret_cast<int8_t*>(recp[n]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int p = 0; p < 4; ++p) bytes[(j * 4 + p) * 32 + lane] = q[n][j][p];
+        if (lane < 8) {
+            const int half = lane & 1;
+            const float g0 = -gA[n], g1 = -gB[n];
+            recp[n][256 + lane] = half == 0 ? pack_half2(g0, g1)
+                                            : pack_half2(g0 - half_round(g0), g1 - half_round(g1));
+        }
+        if (lane == 0) {
+            recp[n][264] = __float_as_uint(pow2f(e[n]));
+            recp[n][265] = __float_as_uint(pow2f(e0[n]));
+        }
+    }
+}
+
 __device__ __forceinline__ void imma16832(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1) {
     asm volatile(

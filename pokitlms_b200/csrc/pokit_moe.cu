@@ -2262,11 +2262,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                     }
                 }
                 __syncwarp();
+                if (!kAtt && q0 + kWarps < nrec) {
+                    // Both records' steps interleaved (the attention instantiation
+                    // keeps one at a time: it is at its register cap).
+                    const float* const vp[2] = {reinterpret_cast<const float*>(recs + q0 * kFragWords),
+                                                reinterpret_cast<const float*>(recs + (q0 + kWarps) * kFragWords)};
+                    uint32_t* const rp[2] = {recs + q0 * kFragWords, recs + (q0 + kWarps) * kFragWords};
+                    q4k_frag_superblocks<2>(vp, rp, lane);
+                } else {
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const uint32_t q = q0 + i * kWarps;
-                    if (q < nrec)
-                        q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords, lane);
+                    for (int i = 0; i < 2; ++i) {
+                        const uint32_t q = q0 + i * kWarps;
+                        if (q < nrec)
+                            q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords,
+                                                lane);
+                    }
                 }
                 __syncwarp();
                 // The warp multiplies the records it just built (no wait for
@@ -2814,11 +2824,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
                     }
                 }
                 __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const uint32_t q = q0 + i * kWarps;
-                    if (q < nrec)
-                        q4k_frag_superblock(reinterpret_cast<float*>(recs + q * kFragWords), recs + q * kFragWords, lane);
+                if (q0 + kWarps < nrec) {
+                    const float* const vp[2] = {reinterpret_cast<const float*>(recs + q0 * kFragWords),
+                                                reinterpret_cast<const float*>(recs + (q0 + kWarps) * kFragWords)};
+                    uint32_t* const rp[2] = {recs + q0 * kFragWords, recs + (q0 + kWarps) * kFragWords};
+                    q4k_frag_superblocks<2>(vp, rp, lane);       // both records' steps interleaved
+                } else {
+                    q4k_frag_superblock(reinterpret_cast<float*>(recs + q0 * kFragWords), recs + q0 * kFragWords, lane);
                 }
                 __syncwarp();
                 const auto unit = [&](uint32_t q, float& r0, float& r1) {
