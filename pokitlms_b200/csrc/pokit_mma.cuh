@@ -514,8 +514,7 @@ __device__ __forceinline__ uint2 lds_u64_a2(const uint8_t* p, bool odd) {
 // Four 6-bit quants (bytes 0..63) as the signed bytes q - 32.
 __device__ __forceinline__ uint32_t q6_centered(uint32_t v) {
     const uint32_t r = v ^ 0x20202020u;               // q - 32 for q >= 32; q | 32 otherwise
-    const uint32_t m = r & 0x20202020u;                // set where q < 32: extend the sign
-    return r | (m << 1) | (m << 2);
+    return r + (r & 0x20202020u) * 6u;                 // where q < 32, bits 6 and 7 too (no carries)
 }
 
 // One Q6_K superblock of 16 rows (210 bytes each: ql[128], qh[64], sc[16],
@@ -525,8 +524,8 @@ __device__ __forceinline__ uint32_t q6_centered(uint32_t v) {
 // nibble (quarter / 2) of ql[64 half + 32 (quarter % 2) + l] with bits
 // 2 quarter of qh[32 half + l] above it, and whose scale is sc[2 j + l / 16].
 // The A bytes are q - 32 (signed), so there is no min term; the two scales of
-// a sub-block take one MMA each, lanes t < 2 (elements 0..15) feeding the
-// first and lanes t >= 2 the second.
+// a sub-block take one MMA each, the activation pieces of lanes t < 2
+// (elements 0..15) feeding the first and those of lanes t >= 2 the second.
 __device__ __forceinline__ void q6k_mma_superblock(const uint8_t* __restrict__ b0p, const uint8_t* __restrict__ b1p,
                                                    const uint32_t* __restrict__ rec, float& acc0, float& acc1) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -552,9 +551,12 @@ __device__ __forceinline__ void q6k_mma_superblock(const uint8_t* __restrict__ b
             };
             const uint32_t a0 = val(l0.x, qh0.x), a1 = val(l1.x, qh1.x), a2 = val(l0.y, qh0.y), a3 = val(l1.y, qh1.y);
             const uint2 xb = bact ? *reinterpret_cast<const uint2*>(rb + j * 128) : make_uint2(0u, 0u);
+            // The two scale groups through B: lanes t < 2 hold the k positions
+            // of elements 0..15 in both operands, lanes t >= 2 those of 16..31.
+            const uint32_t bl0 = first16 ? xb.x : 0u, bl1 = first16 ? xb.y : 0u;
             int dA[4], dB[4];
-            imma16832_ss(dA, first16 ? a0 : 0u, first16 ? a1 : 0u, first16 ? a2 : 0u, first16 ? a3 : 0u, xb.x, xb.y);
-            imma16832_ss(dB, first16 ? 0u : a0, first16 ? 0u : a1, first16 ? 0u : a2, first16 ? 0u : a3, xb.x, xb.y);
+            imma16832_ss(dA, a0, a1, a2, a3, bl0, bl1);
+            imma16832_ss(dB, a0, a1, a2, a3, xb.x ^ bl0, xb.y ^ bl1);
             const int bi = 8 * (2 * (j & 1));
             const int sA0 = static_cast<int8_t>(sc0[j >> 1] >> bi), sB0 = static_cast<int8_t>(sc0[j >> 1] >> (bi + 8));
             const int sA1 = static_cast<int8_t>(sc1[j >> 1] >> bi), sB1 = static_cast<int8_t>(sc1[j >> 1] >> (bi + 8));
