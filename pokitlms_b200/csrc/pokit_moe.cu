@@ -2382,9 +2382,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
 // 3): Q4_K gate/up and Q4_K / Q5_K / Q6_K down (per layer) on the integer
 // tensor path, and the sigmoid-gated Q8_0 shared expert (src/qwen35_runner.cpp:
 // 691-763).  The same phases and hand-offs as moe_chain_kernel, with:
-//   route  E + 1 accumulator rows (the shared expert's gate row last), staged
-//          into shared memory by one bulk copy; the selection takes
-//          sigmoid(scale * that logit) as the shared weight
+//   route  E + 1 accumulator rows (the shared expert's gate row last), at
+//          most two per thread with all loads in flight; one warp selects, the
+//          selection taking sigmoid(scale * that logit) as the shared weight,
+//          while eight build the x' records
 //   G      routed 16-row groups as in the chain, a tensor-map box per
 //          two-superblock tile from the layer's own maps (the layers' tensors
 //          need not sit at one stride); the shared expert's gate/up in 8-row
@@ -2400,7 +2401,7 @@ constexpr uint32_t kChain35SharedRows = 8;       // rows per shared-expert gate/
 constexpr uint32_t kChain35SharedWarps = 4;      // warps taking the shared slot in D
 
 struct Chain35Layout {
-    uint32_t gbars, dbars, rbar, recs, xf, lg, sel_id, sel_w, part, dpart, hrow, gtiles, dtiles, total;
+    uint32_t gbars, dbars, recs, xf, lg, sel_id, sel_w, part, dpart, hrow, gtiles, dtiles, total;
     uint32_t nsb, nsd, gpairs, slots, rb_down_max, rb_shared, nrec;
 };
 
@@ -2417,7 +2418,6 @@ __host__ __device__ inline Chain35Layout chain35_layout(const MoeLayerDev& L, ui
     uint32_t off = 0;
     c.gbars = off; off += al16(kWarps * c.gpairs * 8u);
     c.dbars = off; off += al16(c.slots * 8u);
-    c.rbar = off; off += 16u;
     c.recs = off; off += al16(umax(nsb, c.nrec) * kFragWords * 4u);
     c.xf = off; off += al16(L.hidden * 4u);
     c.lg = off; off += al16((L.experts + 1u) * 4u);
@@ -2427,10 +2427,10 @@ __host__ __device__ inline Chain35Layout chain35_layout(const MoeLayerDev& L, ui
     c.dpart = off; off += al16((c.nrec + 1u) * 16u * 4u);
     c.hrow = off; off += al16(2u * kPartRows * 4u);
     off = al128(off);
-    // Tile space: the gate/up tiles, the staged accumulator rows (route) and
-    // the shared slot's activation floats (D) in turn.
+    // Tile space: the gate/up tiles and the shared slot's activation floats
+    // (D) in turn.
     c.gtiles = off;
-    off += umax(umax(kWarps * c.gpairs * kPairBytes, (L.experts + 1u) * kRaccLimbs * 8u), al16(L.inter * 4u));
+    off += umax(kWarps * c.gpairs * kPairBytes, al16(L.inter * 4u));
     off = al128(off);
     c.dtiles = off; off += L.top_k * 16u * rb_down_max + 16u * c.rb_shared;
     c.total = off;
@@ -2503,7 +2503,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
     const uint32_t j0 = cta * kPartRows;
     uint64_t* gbars = reinterpret_cast<uint64_t*>(smem + c.gbars);
     uint64_t* dbars = reinterpret_cast<uint64_t*>(smem + c.dbars);
-    uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + c.rbar);
     uint32_t* recs = reinterpret_cast<uint32_t*>(smem + c.recs);
     float* xf = reinterpret_cast<float*>(smem + c.xf);
     float* lg = reinterpret_cast<float*>(smem + c.lg);
@@ -2514,7 +2513,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
     float* dsh = dpart + nrec * 16u;                               // the shared slot's 16 rows
     float* hrow = reinterpret_cast<float*>(smem + c.hrow);
     uint8_t* gtiles = smem + c.gtiles;
-    const ulonglong2* rstage = reinterpret_cast<const ulonglong2*>(smem + c.gtiles);   // route
     float* actsh = reinterpret_cast<float*>(smem + c.gtiles);      // D: the shared slot's activations
     uint8_t* dtiles = smem + c.dtiles;
     uint32_t* ctr_route = a.C.counters;
@@ -2545,10 +2543,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
     const uint32_t gpairs = c.gpairs;
     if (lane == 0) {
         for (uint32_t i = 0; i < gpairs; ++i) mbar_init(&gbars[warp * gpairs + i], 1);
-        if (warp == 0) {
+        if (warp == 0)
             for (uint32_t u = 0; u < slots; ++u) mbar_init(&dbars[u], 1);
-            mbar_init(rbar, 1);
-        }
         mbar_fence_init();
     }
     // This CTA's row group and superblock half per warp (as in the chain).
@@ -2604,14 +2600,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
         // ---- route ----
         if (!chain_wait(ctr_route, units * (l + 1u), status, &abort_sh)) { ok = false; break; }
         stamp(l, 0);
-        if (tid == 0) {
-            // Every unit's accumulator additions (acquired above) before the
-            // async-proxy read of them.
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-            mbar_expect_tx(rbar, Er * kRaccLimbs * 8u);
-            bulk_copy_g2s(gtiles, a.C.racc + pr * racc_span, Er * kRaccLimbs * 8u, rbar);
-        }
-        if (warp < static_cast<int>(kTailLogitWarps)) {
+        {
+            // Every thread turns at most two accumulator rows into logits, all
+            // of their loads in flight together (E + 1 <= 2 x kThreads rows).
+            const unsigned long long* racc = a.C.racc + pr * racc_span;
+            ulonglong2 limbs[2][kRaccLimbs / 2];
+#pragma unroll
+            for (uint32_t i = 0; i < 2; ++i) {
+                const uint32_t e = static_cast<uint32_t>(tid) + i * kThreads;
+                if (e < Er) {
+                    const ulonglong2* q = reinterpret_cast<const ulonglong2*>(racc + static_cast<uint64_t>(e) * kRaccLimbs);
+#pragma unroll
+                    for (int h2 = 0; h2 < kRaccLimbs / 2; ++h2) limbs[i][h2] = __ldcg(q + h2);
+                }
+            }
             if (warp == 0) {
                 float sq = 0.0f;
                 for (uint32_t u = lane; u < units; u += 32) sq += __ldcg(a.C.rsq + p * units + u);
@@ -2622,14 +2624,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
                     bad_sh = __ldcg(a.C.rbad + pr);
                 }
             }
-            wait_bar(rbar);
-            for (uint32_t e = warp * 32u + lane; e < Er; e += kTailLogitWarps * 32u) {
-                ulonglong2 limbs[kRaccLimbs / 2];
 #pragma unroll
-                for (int h2 = 0; h2 < kRaccLimbs / 2; ++h2) limbs[h2] = rstage[e * (kRaccLimbs / 2) + h2];
-                lg[e] = racc_value(limbs);
+            for (uint32_t i = 0; i < 2; ++i) {
+                const uint32_t e = static_cast<uint32_t>(tid) + i * kThreads;
+                if (e < Er) lg[e] = racc_value(limbs[i]);
             }
-            asm volatile("bar.sync 1, %0;" ::"r"(kTailLogitWarps * 32u) : "memory");
+        }
+        __syncthreads();
+        if (warp < static_cast<int>(kTailLogitWarps)) {
             if (warp == 0) {
                 const float scale = scale_sh;
                 const bool bad = bad_sh != 0u;
