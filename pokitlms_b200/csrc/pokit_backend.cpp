@@ -435,12 +435,14 @@ public:
         float* dy = reinterpret_cast<float*>(static_cast<uint8_t*>(io_) + align256(cfg_.hidden * 4));
         float* h_out = static_cast<float*>(pinned_);
         uint8_t* h_tail = static_cast<uint8_t*>(pinned_) + align256(cfg_.hidden * 4) * 2;
-        guard(cudaMemcpyAsync(dx, x, cfg_.hidden * 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        float* h_in = reinterpret_cast<float*>(static_cast<uint8_t*>(pinned_) + align256(cfg_.hidden * 4));
+        std::memcpy(h_in, x, cfg_.hidden * 4);
+        guard(cudaMemcpyAsync(dx, h_in, cfg_.hidden * 4, cudaMemcpyHostToDevice, stream_), "h2d");
         forward(layer, dx, dy, nullptr, nullptr, stream_);
         guard(cudaMemcpyAsync(h_out, dy, cfg_.hidden * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
         guard(cudaMemcpyAsync(h_tail, S_.ids, cfg_.top_k * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
         guard(cudaMemcpyAsync(h_tail + 1024, S_.weights, cfg_.top_k * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
-        synchronize(stream_);
+        synchronize_host_call();
         std::memcpy(out, h_out, cfg_.hidden * 4);
         if (ids) std::memcpy(ids, h_tail, cfg_.top_k * 4);
         if (w) std::memcpy(w, h_tail + 1024, cfg_.top_k * 4);
@@ -602,11 +604,15 @@ public:
         if (!in || !out) throw std::invalid_argument("hidden buffers are required");
         DeviceScope scope(device_);
         float* dh = static_cast<float*>(io_);
-        guard(cudaMemcpyAsync(dh, in, cfg_.hidden * 4, cudaMemcpyHostToDevice, stream_), "h2d");
-        decode_layers(first, count, dh, stream_);
         float* h_out = static_cast<float*>(pinned_);
+        // The input through pinned memory: an asynchronous copy instead of a
+        // staged pageable one.
+        float* h_in = reinterpret_cast<float*>(static_cast<uint8_t*>(pinned_) + align256(cfg_.hidden * 4));
+        std::memcpy(h_in, in, cfg_.hidden * 4);
+        guard(cudaMemcpyAsync(dh, h_in, cfg_.hidden * 4, cudaMemcpyHostToDevice, stream_), "h2d");
+        decode_layers(first, count, dh, stream_);
         guard(cudaMemcpyAsync(h_out, dh, cfg_.hidden * 4, cudaMemcpyDeviceToHost, stream_), "d2h");
-        synchronize(stream_);
+        synchronize_host_call();
         std::memcpy(out, h_out, cfg_.hidden * 4);
     }
 
@@ -616,6 +622,20 @@ public:
         guard(cudaStreamSynchronize(s ? s : stream_), "synchronize");
         uint32_t status = 0;
         guard(cudaMemcpy(&status, S_.status, 4, cudaMemcpyDeviceToHost), "status");
+        raise_status(status);
+    }
+
+    // The host-buffer entries: the status word rides the same stream as the
+    // results, into pinned memory, so a call waits on its stream once.
+    void synchronize_host_call() {
+        uint32_t* h_status = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(pinned_) +
+                                                         align256(cfg_.hidden * 4) * 2 + 2048);
+        guard(cudaMemcpyAsync(h_status, S_.status, 4, cudaMemcpyDeviceToHost, stream_), "status");
+        guard(cudaStreamSynchronize(stream_), "synchronize");
+        raise_status(*h_status);
+    }
+
+    void raise_status(uint32_t status) {
         if (status & kStatusWaitTimeout) {
             // A grid barrier gave up: the launch was abandoned and the barrier
             // counter no longer matches the host's count.  Sticky, like a CUDA error.
