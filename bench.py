@@ -1124,6 +1124,14 @@ def main() -> None:
             "parity": parity,
             **({"config5": config5} if config5 is not None else {}),
         }))
+    if world > 1:
+        # Every graph that held NCCL calls is gone with its frame; collect any
+        # cycle still holding one before the communicators go.
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
+        barrier()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
