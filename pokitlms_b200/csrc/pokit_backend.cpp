@@ -576,6 +576,24 @@ public:
         kernel_launches_ += 1;
     }
 
+    bool attention_layer_fits(const void* args, size_t bytes) const {
+        return chain35_ok_ && !failed_ && moe_chain35_attention_fits(chain35_plan_, args, bytes);
+    }
+    void decode_layer_attention(size_t layer, float* hidden, const void* args, size_t bytes, cudaStream_t s) {
+        ensure_ok();
+        if (!chain35_ok_) throw std::invalid_argument("the layers do not run the Qwen3.5-MoE chain kernel");
+        if (layer >= cfg_.layers || !hidden) throw std::invalid_argument("layer and hidden state are required");
+        if (!resident_complete(layer)) throw std::invalid_argument("layer weights were not uploaded");
+        DeviceScope scope(device_);
+        cudaStream_t st = s ? s : stream_;
+        guard(launch_moe_chain35(chain35_plan_, devs_dev_, chain35_maps_, static_cast<uint32_t>(layer), 1u, S_, C_,
+                                 hidden, st, nullptr, nullptr, nullptr, args, bytes),
+              "decode chain kernel");
+        forward_calls_ += 1;
+        hits_ += cfg_.top_k;
+        kernel_launches_ += 1;
+    }
+
     // A decoder's layer loop: its attention blocks and these MoE blocks in
     // one chain launch (false when the layers do not take the chain kernel or
     // the attention phase does not fit it).
@@ -1078,6 +1096,25 @@ struct pokit_cuda_moe {
 };
 
 namespace pokit {
+
+bool moe_attention_layer_fits(const pokit_cuda_moe* moe, const void* args, size_t bytes) {
+    return moe && moe->impl.attention_layer_fits(args, bytes);
+}
+
+cudaError_t moe_decode_layer_attention(pokit_cuda_moe* moe, size_t layer, float* hidden, const void* args,
+                                       size_t bytes, cudaStream_t stream, std::string* error) {
+    if (!moe) return cudaErrorInvalidValue;
+    try {
+        moe->impl.decode_layer_attention(layer, hidden, args, bytes, stream);
+        return cudaSuccess;
+    } catch (const std::invalid_argument& e) {
+        if (error) *error = e.what();
+        return cudaErrorInvalidValue;
+    } catch (const std::exception& e) {
+        if (error) *error = e.what();
+        return cudaErrorUnknown;
+    }
+}
 
 bool moe_delta_layer_fits(const pokit_cuda_moe* moe, const DeltaBlockShape& d) {
     return moe && moe->impl.delta_layer_fits(d);

@@ -735,6 +735,11 @@ private:
         check(cudaMemset(attn_ll_, 0, attn_words_ * 8), "cudaMemset(attention words)");
         attn_grid_ = grid;
         attn_smem_ = c.total;
+        // A hybrid decoder's attention layer and its MoE block run as one
+        // launch when the Qwen3.5 chain kernel fits the attention phase
+        // (POKIT_CUDA_FUSED_ATTN_MOE=0 keeps two launches per layer).
+        const char* both = std::getenv("POKIT_CUDA_FUSED_ATTN_MOE");
+        attn_moe_ = !(both && both[0] == '0');
         plan_layer_chain();
     }
 
@@ -784,7 +789,8 @@ private:
         fused_layers_ = true;
     }
 
-    cudaError_t launch_attn_block(size_t l, cudaStream_t s) {
+    // The attention block's arguments for layer l (ash_ holds this step's shape).
+    AttnBlockArgs attn_args(size_t l) const {
         AttnBlockArgs a{};
         const auto F = [&](uint32_t t) { return reinterpret_cast<const float*>(tensor_ptr(l, t)); };
         const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
@@ -810,6 +816,10 @@ private:
         a.layer = static_cast<uint32_t>(l);
         a.layers = static_cast<uint32_t>(cfg_.layers);
         a.eps = cfg_.rms_epsilon;
+        return a;
+    }
+
+    cudaError_t launch_attn_block(const AttnBlockArgs& a, cudaStream_t s) {
         cudaLaunchConfig_t lc{};
         lc.gridDim = dim3(attn_grid_);
         lc.blockDim = dim3(kAttnBlockThreads);
@@ -906,7 +916,19 @@ private:
             const auto P = [&](uint32_t t) { return tensor_ptr(l, t); };
             const auto F = [&](uint32_t t) { return reinterpret_cast<const float*>(tensor_ptr(l, t)); };
             if (attention_layer(l) && attn_grid_) {
-                e = launch_attn_block(l, s);
+                const AttnBlockArgs a = attn_args(l);
+                if (attn_moe_ && moe_attention_layer_fits(moe_, &a, sizeof a)) {
+                    // The attention block and the layer's MoE block in one launch.
+                    std::string err;
+                    e = moe_decode_layer_attention(moe_, l, hidden_, &a, sizeof a, s, &err);
+                    if (e != cudaSuccess) {
+                        moe_error_ = err;
+                        return e;
+                    }
+                    n += 1;
+                    continue;
+                }
+                e = launch_attn_block(a, s);
                 ++n;
             } else if (attention_layer(l)) {
                 const uint64_t kv_off = static_cast<uint64_t>(l) * window_ * kd_;
@@ -1143,6 +1165,7 @@ private:
     DeltaBlockShape delta_shape_{};           // the one-launch DeltaNet layer (delta_grid_ > 0)
     uint32_t delta_grid_ = 0, delta_smem_ = 0;
     bool delta_moe_ = false;                  // a DeltaNet layer and its MoE block in one launch
+    bool attn_moe_ = false;                   // an attention layer and its MoE block in one launch
     float* delta_scratch_ = nullptr;
     unsigned long long* attn_ll_ = nullptr;   // fused attention: Q/K/V words, output words, hidden words
     uint64_t attn_words_ = 0;

@@ -326,11 +326,15 @@ bool moe_chain35_plan(const MoeLayerDev* layers, uint32_t n, Chain35Plan* plan, 
 // With `delta` (count 1): the layer's Gated DeltaNet mixer (delta_block's
 // phases) runs first in the same launch, leaving each D unit's residual rows
 // in its own CTA.
+// With `att_args` (an AttnBlockArgs of pokit_attention.cuh, `att_bytes` its
+// size; count 1): the layer's attention block runs first instead.
 cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layers_dev, const Chain35Maps* maps_dev,
                                uint32_t first, uint32_t count, const MoeScratch& S, const ChainScratch& C,
                                float* hidden, cudaStream_t stream, unsigned long long* trace = nullptr,
-                               const DeltaBlockShape* delta_shape = nullptr, const DeltaBlockTensors* delta = nullptr);
+                               const DeltaBlockShape* delta_shape = nullptr, const DeltaBlockTensors* delta = nullptr,
+                               const void* att_args = nullptr, size_t att_bytes = 0);
 bool moe_chain35_delta_fits(const Chain35Plan& plan, const DeltaBlockShape& d);
+bool moe_chain35_attention_fits(const Chain35Plan& plan, const void* att_args, size_t bytes);
 // Bytes of shared memory the attention phase needs, and where the chain's
 // tile region (which it runs in) starts.
 uint32_t chain_attention_smem(const ChainPlan& plan, const ChainAttnDesc& att);
@@ -346,6 +350,10 @@ bool moe_attention_chain_fits(const pokit_cuda_moe* moe, const ChainAttnDesc& at
 // A Qwen3.5 decoder's DeltaNet layer `layer` and the handle's MoE block of
 // that layer in one launch (moe_chain35_kernel with the mixer ahead).
 bool moe_delta_layer_fits(const pokit_cuda_moe* moe, const DeltaBlockShape& d);
+// The same for an attention layer (`args`: an AttnBlockArgs, `bytes` its size).
+bool moe_attention_layer_fits(const pokit_cuda_moe* moe, const void* args, size_t bytes);
+cudaError_t moe_decode_layer_attention(pokit_cuda_moe* moe, size_t layer, float* hidden, const void* args,
+                                       size_t bytes, cudaStream_t stream, std::string* error);
 cudaError_t moe_decode_layer_delta(pokit_cuda_moe* moe, size_t layer, float* hidden, const DeltaBlockShape& d,
                                    const DeltaBlockTensors& t, cudaStream_t stream, std::string* error);
 cudaError_t moe_decode_layers_attention(pokit_cuda_moe* moe, size_t first, size_t count, float* hidden,

@@ -33,6 +33,7 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -2449,6 +2450,8 @@ struct Chain35Args {
     unsigned long long* trace;   // optional per-(layer, CTA) phase stamps (measurement)
     DeltaBlockArgs delta;        // with_delta: the layer's Gated DeltaNet mixer runs first
     uint32_t with_delta;
+    AttnBlockArgs att;           // with_att: the layer's attention block runs first
+    uint32_t with_att;
 };
 
 // Thread t's router slices of a layer: expert t (rs) and expert t + kThreads,
@@ -2531,6 +2534,28 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
             t[kChainStamps + i] = static_cast<unsigned long long>(clock64());
         }
     };
+    if (a.with_att) {
+        // A decoder's attention layer ahead of its MoE block (count 1): its
+        // output units leave this CTA's D-unit rows of the residual (rows
+        // [16c, 16c + 16), the prologue's), and every CTA has read all of
+        // hidden before any CTA reaches the route below.  It runs in the
+        // tile space.
+        __shared__ uint64_t att_bars[2];
+        __shared__ float att_red[kWarps];
+        __shared__ uint32_t att_abort;
+        if (tid == 0) {
+            mbar_init(&att_bars[0], 1);
+            mbar_init(&att_bars[1], 1);
+            mbar_fence_init();
+            att_abort = 0u;
+        }
+        __syncthreads();
+        const AttnPhaseCtx x{smem + c.gtiles, att_bars, 0u, &att_abort, att_red};
+        attention_phase<8, 8>(a.att, x, nullptr, 0u);
+        if (att_abort) return;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+    }
     // A decoder's DeltaNet layer ahead of its MoE block (one launch, count 1):
     // its phase 3 leaves this CTA's D-unit rows of the residual, read by the
     // prologue below after a CTA barrier.  The mixer runs in the tile space.
@@ -3527,10 +3552,28 @@ bool moe_chain35_delta_fits(const Chain35Plan& plan, const DeltaBlockShape& d) {
            db_layout(d.hidden, d.value_heads * kDbHeadDim).total <= c.total - c.gtiles;
 }
 
+bool moe_chain35_attention_fits(const Chain35Plan& plan, const void* att_args, size_t bytes) {
+    if (!att_args || bytes != sizeof(AttnBlockArgs) || plan.grid == 0) return false;
+    AttnBlockArgs at;
+    std::memcpy(&at, att_args, sizeof at);
+    const Chain35Layout c = chain35_layout(plan.shape, plan.rb_down_max);
+    // The attention phase's own limits (as the standalone block's planner
+    // sets them): a Q/K/V row block per CTA, an output unit and query head
+    // per CTA at most, two output superblocks per warp.
+    const uint32_t G = plan.grid;
+    if (at.rows % 16u || at.qd % 256u || at.H % 256u || at.rows / 16u < G || at.H / 16u > G || at.sh.qh > G ||
+        at.qd / 256u > 8u * kAttnMaxOutPerWarp || at.H / 256u > 2u * kWarps || at.layers > 255u)
+        return false;
+    return at.H == plan.shape.hidden && at.sh.d <= static_cast<uint32_t>(kThreads) &&
+           attn_block_layout(at.H, at.rows, at.qd, at.sh.d, at.sh.rh, at.sh.window, plan.grid, kWarps).total <=
+               c.total - c.gtiles;
+}
+
 cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layers_dev, const Chain35Maps* maps_dev,
                                uint32_t first, uint32_t count, const MoeScratch& S, const ChainScratch& C,
                                float* hidden, cudaStream_t stream, unsigned long long* trace,
-                               const DeltaBlockShape* delta_shape, const DeltaBlockTensors* delta) {
+                               const DeltaBlockShape* delta_shape, const DeltaBlockTensors* delta,
+                               const void* att_args, size_t att_bytes) {
     if (!hidden || !layers_dev || !maps_dev || count == 0 || first >= plan.layers || count > plan.layers - first ||
         plan.grid == 0)
         return cudaErrorInvalidValue;
@@ -3556,6 +3599,13 @@ cudaError_t launch_moe_chain35(const Chain35Plan& plan, const MoeLayerDev* layer
     if (delta) {
         a.delta = make_delta_args(*delta_shape, *delta);
         a.with_delta = 1u;
+    }
+    if (att_args) {
+        if (delta || count != 1 || !moe_chain35_attention_fits(plan, att_args, att_bytes))
+            return cudaErrorInvalidValue;
+        std::memcpy(&a.att, att_args, sizeof a.att);
+        if (a.att.hidden != hidden) return cudaErrorInvalidValue;
+        a.with_att = 1u;
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(plan.grid);

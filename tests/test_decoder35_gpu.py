@@ -22,11 +22,13 @@ pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden" / "decoder_cfg3_L4.npz"
 
 
-# The full-attention layers as the fused attention block (the default) and
-# as three kernels; a DeltaNet layer and its MoE block in one launch (the
-# default), as two launches, and the DeltaNet layer as the in-projection,
+# Every layer (attention or DeltaNet) and its MoE block in one launch (the
+# default); the full-attention layers as the fused attention block ahead of
+# a separate MoE launch, and as three kernels; a DeltaNet layer and its MoE
+# block as two launches, and the DeltaNet layer as the in-projection,
 # conv1d, delta-step and ssm_out kernels.
 MODES = {"attention_block": {}, "three_kernels": {"POKIT_CUDA_FUSED_ATTN": "0"},
+         "attention_block_split": {"POKIT_CUDA_FUSED_ATTN_MOE": "0"},
          "delta_block": {"POKIT_CUDA_FUSED_DELTA_MOE": "0"},
          "delta_kernels": {"POKIT_CUDA_FUSED_DELTANET": "0"}}
 
@@ -80,3 +82,15 @@ def test_greedy_tokens_match_the_reference(decoder):
     again, _ = dec.generate_tokens(g["prompt"], 16)          # generate resets the state
     assert np.array_equal(again, g["ids"][:16])
     assert dec.step_graphs()[0] == 2
+
+
+def test_each_layer_is_one_launch_by_default(decoder, request):
+    """The default step: the embedding, one launch per layer (its mixer and
+    its MoE block), the LM head and argmax when logits are wanted, and the
+    position advance."""
+    if request.node.callspec.params["decoder"] != "attention_block":
+        pytest.skip("launch count of the default mode")
+    dec, g = decoder
+    layers = int(g["layers"])
+    dec.generate_tokens(g["prompt"], 2)
+    assert dec.launches_per_step() in (layers + 2, layers + 4)
