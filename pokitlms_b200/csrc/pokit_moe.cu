@@ -2142,6 +2142,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                            static_cast<int>(layer), &mybars[i]);
             }
         }
+        // The down boxes (needed after the act wait).  MoE-only chain: right
+        // behind the gate/up boxes -- its gate/up phase is latency-bound, so
+        // they do not slow it, and they land before the activations do.  With
+        // attention: once the warp's gate/up work is done (measured no gain).
+        const auto issue_down = [&]() {
+            if (!(has_unit && static_cast<uint32_t>(warp) < k && lane == 0)) return;
+            const int id = static_cast<int>(sel_id[warp]);
+            for (uint32_t j = 0; j < dpairs; ++j) {
+                const uint32_t u = warp * dpairs + j;
+                mbar_expect_tx(&dbars[u], kPairBytes);
+                tma_box_4d(dtiles + u * kPairBytes, &a.tm_down, static_cast<int>(j * 36u), static_cast<int>(j0), id,
+                           static_cast<int>(layer), &dbars[u]);
+            }
+        };
+        if (!kAtt) issue_down();
         // The previous layer's accumulators and flag (every CTA has read
         // them), zeroed by the D units: their route arrivals publish the
         // zeros before anyone adds into this parity again (the layer after next).
@@ -2184,17 +2199,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain_kernel(const __grid_con
                 part[warp * 16 + g + 8] = acc1;
             }
         }
-        // The down boxes go out once this warp's gate/up boxes are in, so they
-        // do not compete with them for DRAM bandwidth (needed after the act wait).
-        if (has_unit && static_cast<uint32_t>(warp) < k && lane == 0) {
-            const int id = static_cast<int>(sel_id[warp]);
-            for (uint32_t j = 0; j < dpairs; ++j) {
-                const uint32_t u = warp * dpairs + j;
-                mbar_expect_tx(&dbars[u], kPairBytes);
-                tma_box_4d(dtiles + u * kPairBytes, &a.tm_down, static_cast<int>(j * 36u), static_cast<int>(j0), id,
-                           static_cast<int>(layer), &dbars[u]);
-            }
-        }
+        if (kAtt) issue_down();
         __syncthreads();
         stamp(l, 2);
         if (tid < static_cast<int>(kChainGroupsPerCta * 16u)) {
@@ -2763,7 +2768,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_chain35_kernel(const __grid_c
         }
         stamp(l, 2);
         // Every slot's 16 down rows of this D unit: one bulk copy per slot,
-        // once the warp's own gate/up work is done.
+        // once the warp's own gate/up work is done (issued with the gate/up
+        // copies they slow this kernel's bandwidth-sensitive gate/up phase).
         if (has_unit && static_cast<uint32_t>(warp) < slots && lane == 0) {
             const uint32_t sl = warp;
             const bool shared = sl == k;
