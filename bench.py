@@ -458,6 +458,8 @@ def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None, 
     for i in range(e2e_steps):
         be.decode_layers_host(0, c["layers"], hin[i % 4], hout)
     e2e_s = (time.perf_counter() - t0) / e2e_steps
+    work.copy_(inputs[0], non_blocking=True)
+    phases = chain_phases(be, c["layers"], work, stream)
     be.close()
     tok_bytes = sum(cfg3_layer_bytes(d) for d in downs)
     peaks = measured_peaks()
@@ -474,6 +476,7 @@ def measure_config3(device: int, stream, steps: int, cpu_seconds: float | None, 
         "path": ("moe_chain35_kernel: one cooperative launch for the 48 blocks; Q4_K gate/up and Q5_K/Q6_K down on "
                  "integer mma.sync (u8/s8 x int8 activation pieces), the Q8_0 shared expert as FP32 dots of "
                  "tensor-map boxes"),
+        "chain_phases": phases,
     }
     if cpu_seconds:
         res["cpu_baseline"] = cpu_config3_rate(cpu_seconds)
